@@ -1,0 +1,431 @@
+#!/usr/bin/env python
+"""Leaf-operator replay benchmark on B200.
+
+Workload (one step): 4096 independent leaves x 2048 rows, 768-d SQ8 codes
+(per-row symmetric int8 as the reference quantizes them), all-pairs distances
+with a bounded top-32 list per row -- the SQ8 leaf hot path of SHEAR's TESSA
+replay (``tessa_operator_replay`` A2/A3 leaf stage).  Synthetic rows ~N(0,1),
+L2-normalised, seed 0 (the Wiki/LAION datasets are not available here).
+
+Arms:
+  ours (default)   libtessa_sm100.so (tcgen05 leaf kernel) through its C ABI.
+                   value = rows/s with inputs resident in HBM (device API);
+                   e2e   = the same through the host-buffer API with pinned host
+                           inputs/outputs copied inside the timed region.
+  reference        the reference's leaf algorithm restated on the CPU
+                   (oracle/, OpenMP over leaves, all host threads), bounded
+                   sample per step.  The reference itself is Rust and cannot be
+                   built in this image.
+
+Multi-GPU (torchrun): every rank runs the full per-GPU workload on its own
+device (weak scaling, leaves are independent; no collective on the data path).
+Timing is device time between barriers, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+NOMINAL_INT8_TOPS = 4500.0  # B200 dense int8, nominal
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--leaves", type=int, default=4096)
+    ap.add_argument("--leaf-rows", type=int, default=2048)
+    ap.add_argument("--dim", type=int, default=768)
+    ap.add_argument("--k", type=int, default=32)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def workload_desc(a):
+    return {
+        "workload": f"leaf-operator replay (BASELINE config 2): {a.leaves} leaves x {a.leaf_rows} rows, "
+                    f"{a.dim}-d SQ8, top-{a.k} per row",
+        "leaves": a.leaves, "leaf_rows": a.leaf_rows, "dim": a.dim, "k": a.k,
+        "sq8": "per-row symmetric int8 (reference scheme, dco_sq_int8.rs:1431-1466)",
+        "l2": "inputs larger than L2 (codes %.1f GB per GPU); no flush" % (a.leaves * a.leaf_rows * a.dim / 1e9),
+    }
+
+
+# ----------------------------------------------------------------- workload
+
+def make_workload(torch, dev, a, seed):
+    """Synthetic SQ8 leaf batch generated and quantized on the device."""
+    from shear_b200 import ops
+
+    rows = a.leaves * a.leaf_rows
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    pd = ops.padded_dim(a.dim, 16)
+    codes = torch.empty((rows, pd), dtype=torch.int8, device=dev)
+    scales = torch.empty(rows, dtype=torch.float32, device=dev)
+    norms = torch.empty(rows, dtype=torch.float32, device=dev)
+    chunk = 1 << 20
+    for r0 in range(0, rows, chunk):
+        r1 = min(rows, r0 + chunk)
+        x = torch.randn((r1 - r0, a.dim), generator=g, device=dev, dtype=torch.float32)
+        x /= torch.linalg.vector_norm(x, dim=1, keepdim=True)
+        c, s, n = ops.quantize_sq8(x)
+        codes[r0:r1].copy_(c)
+        scales[r0:r1].copy_(s)
+        norms[r0:r1].copy_(n)
+        del x, c, s, n
+    gids = torch.randperm(rows, generator=g, device=dev).to(torch.int32)
+    members = torch.arange(rows, dtype=torch.int32, device=dev)
+    starts = np.arange(a.leaves, dtype=np.uint64) * np.uint64(a.leaf_rows)
+    sizes = np.full(a.leaves, a.leaf_rows, dtype=np.uint64)
+    torch.cuda.synchronize(dev)
+    return dict(codes=codes, scales=scales, norms=norms, gids=gids, members=members, starts=starts, sizes=sizes)
+
+
+# ----------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.dev = device_index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not getattr(self, "out", ""):
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        loaded = [v for v in sm if v > 0.5 * max(sm)] or sm
+        return {"sm_mhz": float(np.median(loaded)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- peaks
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def int8_peak_tops(torch, dev):
+    """Burst int8 GEMM rate of cuBLAS (torch._int_mm, 8192^3) on this GPU, TOP/s."""
+    try:
+        n = 8192
+        a = torch.randint(-127, 127, (n, n), dtype=torch.int8, device=dev)
+        b = torch.randint(-127, 127, (n, n), dtype=torch.int8, device=dev).t().contiguous().t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = None
+        for _ in range(10):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch._int_mm(a, b)
+            e.record()
+            e.synchronize()
+            t = s.elapsed_time(e) / 1e3
+            best = t if best is None else min(best, t)
+        return 2.0 * n ** 3 / best / 1e12
+    except Exception:
+        return None
+
+
+def ncu_traffic_per_launch():
+    """DRAM bytes per leaf-kernel launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "leaf_topk_sq8_config2.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+# ----------------------------------------------------------------- CPU legs
+
+def cpu_leaf_sample(oracle_mod, host, a, seconds, max_leaves):
+    """Time the CPU restatement on whole leaves until `seconds` pass; rows/s."""
+    threads = oracle_mod.num_threads()
+    n = a.leaf_rows
+    done_rows, t0, leaves = 0, time.perf_counter(), 0
+    batch = max(1, threads)
+    while leaves < max_leaves:
+        cnt = min(batch, max_leaves - leaves)
+        lo, hi = leaves * n, (leaves + cnt) * n
+        members = np.arange(hi - lo, dtype=np.uint32)
+        starts = np.arange(cnt, dtype=np.uint64) * np.uint64(n)
+        sizes = np.full(cnt, n, np.uint64)
+        oracle_mod.leaf_topk_sq8(host["codes"][lo:hi], host["scales"][lo:hi], host["norms"][lo:hi],
+                                 host["gids"][lo:hi], members, starts, sizes, a.k)
+        done_rows += hi - lo
+        leaves += cnt
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return done_rows / dt, threads, leaves, dt
+
+
+def host_sample(torch, w, leaves, a):
+    rows = leaves * a.leaf_rows
+    return dict(codes=w["codes"][:rows].cpu().numpy(), scales=w["scales"][:rows].cpu().numpy(),
+                norms=w["norms"][:rows].cpu().numpy(), gids=w["gids"][:rows].cpu().numpy().view(np.uint32))
+
+
+def run_reference(a):
+    """CPU restatement of the reference leaf operator (oracle port), rank 0 only."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    threads = O.num_threads()
+    rng = np.random.default_rng(0)
+    per_step = max(threads, 1)
+    rows = per_step * a.leaf_rows
+    x = rng.standard_normal((rows, a.dim)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    codes, scales, norms = O.quantize_sq8(x)
+    gids = rng.permutation(rows).astype(np.uint32)
+    members = np.arange(rows, dtype=np.uint32)
+    starts = np.arange(per_step, dtype=np.uint64) * np.uint64(a.leaf_rows)
+    sizes = np.full(per_step, a.leaf_rows, np.uint64)
+    times = []
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        O.leaf_topk_sq8(codes, scales, norms, gids, members, starts, sizes, a.k)
+        dt = time.perf_counter() - t0
+        if i >= a.warmup:
+            times.append(dt)
+    mean = float(np.mean(times))
+    value = rows / mean
+    sample = f"{per_step} leaves x {a.leaf_rows} rows per step ({per_step / a.leaves:.4%} of the workload)"
+    line = {
+        "impl": "reference", "metric": "build vectors/sec", "value": value, "unit": "vectors/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": mean * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: N(0,1) rows, L2-normalised, SQ8 per-row int8 (seed 0)",
+        "config": workload_desc(a),
+        "cpu_baseline": {"value": value, "unit": "vectors/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference is Rust+NVRTC (no cargo in this image); timed leg is its leaf algorithm "
+                "restated in C (oracle/tessa_oracle.c) on all host threads",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------- our arm
+
+def run_ours(a):
+    import torch
+
+    from shear_b200 import ops
+
+    world, rank, local = dist_env()
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = ops.context(dev.index)
+    w = make_workload(torch, dev, a, seed=1234 + rank)
+    rows = a.leaves * a.leaf_rows
+    ids = torch.empty(rows * a.k, dtype=torch.int32, device=dev)
+    dists = torch.empty(rows * a.k, dtype=torch.float32, device=dev)
+
+    def step():
+        ops.leaf_topk_sq8(w["codes"], w["scales"], w["norms"], w["gids"], w["members"], w["starts"],
+                          w["sizes"], a.k, leaf_ordered_codes=w["codes"], out=(ids, dists), ctx=ctx)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(a.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    with ClockSampler(dev.index) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for s, e in evs:
+            s.record(stream)
+            step()
+            e.record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    total_s = t_start.elapsed_time(t_end) / 1e3
+    kern_s = float(np.mean([s.elapsed_time(e) for s, e in evs])) / 1e3
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([total_s, kern_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_s, kern_s = float(tt[0]), float(tt[1])
+    per_step = total_s / a.steps
+    value = world * rows / per_step
+    pairs = a.leaves * a.leaf_rows * (a.leaf_rows - 1)
+    ops_per_step = 2.0 * a.dim * a.leaf_rows * a.leaf_rows * a.leaves  # int8 MAC*2 incl. the diagonal tile
+
+    # ------------------------------------------------------------- e2e
+    e2e = None
+    if not a.no_e2e and a.e2e_steps > 0:
+        pin = lambda t: t.cpu().pin_memory()
+        hc, hs, hn, hg = pin(w["codes"]), pin(w["scales"]), pin(w["norms"]), pin(w["gids"])
+        hm = pin(w["members"])
+        oi = torch.empty(rows * a.k, dtype=torch.int32).pin_memory()
+        od = torch.empty(rows * a.k, dtype=torch.float32).pin_memory()
+        nv = lambda t: t.numpy()
+        args = (nv(hc), nv(hs), nv(hn), nv(hg).view(np.uint32), nv(hm).view(np.uint32), w["starts"],
+                w["sizes"], a.k)
+        ops.leaf_topk_sq8_host(*args, device=dev.index, out=(nv(oi).view(np.uint32), nv(od)))
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(a.e2e_steps):
+            ops.leaf_topk_sq8_host(*args, device=dev.index, out=(nv(oi).view(np.uint32), nv(od)))
+        e2e_s = (time.perf_counter() - t0) / a.e2e_steps
+        if world > 1:
+            import torch.distributed as dist
+            tt = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_s = float(tt[0])
+        h2d = hc.numel() + 4 * (hs.numel() + hn.numel() + hg.numel() + hm.numel())
+        d2h = 8 * rows * a.k
+        e2e = {"value": world * rows / e2e_s, "unit": "vectors/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3,
+               "timing": "wall clock around the synchronous host-buffer C-ABI call, pinned host memory"}
+        del hc, hs, hn, hg, hm, oi, od
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    peaks = measured_peaks()
+    int8_peak = int8_peak_tops(torch, dev)
+    achieved_tops = ops_per_step / kern_s / 1e12
+    peak, src = (int8_peak, "measured in-run: cuBLAS int8 burst (torch._int_mm 8192^3)") if int8_peak else \
+        (NOMINAL_INT8_TOPS, "nominal B200 dense int8 4.5 POPS (no measured int8 peak)")
+    traffic = ncu_traffic_per_launch()
+    roofline = {"bound": "tensor", "achieved": achieved_tops, "peak": peak, "unit": "TOP/s",
+                "frac": achieved_tops / peak, "traffic": traffic, "peak_source": src,
+                "frac_of_nominal_4500": achieved_tops / NOMINAL_INT8_TOPS,
+                "kernel": "tessa::leaf::leaf_topk_sq8_kernel<32>",
+                "algorithmic_ops_per_launch": ops_per_step,
+                "hbm_bytes_algorithmic": rows * (a.dim + 16) + rows * a.k * 8,
+                "hbm_peak_gbs": peaks.get("hbm_gbs")}
+
+    cpu = None
+    if not a.no_cpu_baseline and world == 1:
+        from oracle import oracle as O
+        max_leaves = max(O.num_threads(), 1) * 4
+        host = host_sample(torch, w, min(a.leaves, max_leaves), a)
+        v, thr, nl, dt = cpu_leaf_sample(O, host, a, a.cpu_seconds, min(a.leaves, max_leaves))
+        cpu = {"value": v, "unit": "vectors/s", "cores": thr, "kind": "port",
+               "sample": f"{nl} of {a.leaves} leaves ({nl * a.leaf_rows} rows) in {dt:.1f} s, "
+                         f"oracle/tessa_oracle.c OpenMP"}
+
+    line = {
+        "metric": "build vectors/sec", "value": value, "unit": "vectors/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: N(0,1) rows, L2-normalised, SQ8 per-row int8 (seed 1234+rank)",
+        "config": dict(workload_desc(a), parallelism=f"leaf-sharded x{world} (independent, no collective)"),
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": a.steps,
+        "clocks": clk.summary(),
+        "leaf_kernel_ms": kern_s * 1e3, "pairs_per_sec": world * pairs / per_step,
+        "int8_tops": achieved_tops,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    a = parse_args()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_ours(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

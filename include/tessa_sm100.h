@@ -1,0 +1,254 @@
+/*
+ * tessa_sm100.h -- C ABI of the B200 (sm_100a) TESSA hot-path library
+ * (libtessa_sm100.so).
+ *
+ * The library replaces the NVRTC/cudarc leaf and assignment kernel bindings of
+ * SHEAR (wbh1765091327/SHEAR).  Reference paths below are relative to that
+ * project's root; CB = shear-core/src/algorithm/pipnn/compute_backend.rs,
+ * P = shear-core/src/algorithm/pipnn/.
+ *
+ * Conventions
+ *  - Every function returns TESSA_OK (0) or a negative TESSA_ERR_* code; nothing
+ *    aborts or unwinds across the ABI.  tessa_strerror() names a code and
+ *    tessa_last_error_message() gives the detail of the calling thread's last
+ *    failure.
+ *  - "device pointer" arguments point to CUDA device memory on the context's
+ *    device; "host pointer" arguments point to ordinary (pageable or pinned)
+ *    host memory owned by the caller.  The library owns every buffer it
+ *    allocates (device scratch, pinned staging) and frees it in the matching
+ *    destroy call.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - A context is bound to one device and is not thread-safe: use one context
+ *    per GPU per host thread (the reference serialises its CUDA engine behind a
+ *    mutex, CB:34666).
+ *  - Distances follow the reference bit for bit: SQ8 leaf distances are
+ *    rn(rn(n_i+n_j) + rn(-2*rn(rn(s_i*s_j)*dot))) clamped at 0 (CB:8987-9002);
+ *    leaf lists use the stable eps/id order of CB:7229-7259.
+ */
+#ifndef TESSA_SM100_H
+#define TESSA_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TESSA_API __attribute__((visibility("default")))
+#else
+#define TESSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TESSA_ABI_VERSION 1
+
+#define TESSA_OK 0
+#define TESSA_ERR_INVALID_ARG (-1)  /* malformed sizes, null pointers, k out of range */
+#define TESSA_ERR_CUDA (-2)         /* a CUDA runtime/driver call failed */
+#define TESSA_ERR_OOM (-3)          /* device or pinned allocation failed */
+#define TESSA_ERR_TIMEOUT (-4)      /* a bounded device wait expired (kernel gave up) */
+#define TESSA_ERR_BAD_ROW (-5)      /* a member/leader id is outside the resident rows */
+#define TESSA_ERR_UNSUPPORTED (-6)  /* shape or mode this build does not implement */
+#define TESSA_ERR_NONFINITE (-7)    /* non-finite input to the SQ8 quantizer */
+#define TESSA_ERR_NO_DEVICE (-8)    /* no sm_100 device / extension not usable */
+#define TESSA_ERR_BAD_TASK (-9)     /* malformed task descriptor seen on the device */
+
+/* Largest leaf k (CB:4890 GPU_PERSISTENT_LEAF_DCO_MAX_SURVIVORS). */
+#define TESSA_MAX_LEAF_K 32
+/* Largest assignment fan-out r_h (CB:15784-15786). */
+#define TESSA_MAX_RH 4
+/* Largest padded SQ8 dimension the leaf kernel accepts (shared-memory bound). */
+#define TESSA_MAX_PADDED_DIM 1024
+
+typedef struct tessa_ctx tessa_ctx;
+typedef struct tessa_replay_session tessa_replay_session;
+
+/* ---------------------------------------------------------------- misc --- */
+
+TESSA_API int tessa_abi_version(void);
+TESSA_API const char* tessa_strerror(int code);
+/* Detail of the last failure on the calling thread ("" if none). */
+TESSA_API const char* tessa_last_error_message(void);
+
+/* Replaces CudaComputeBackend::new / validate_gpu_subtree_hardware
+ * (CB:3693-3884 trait, CB:34654-34662 SM check): binds device `device`,
+ * verifies it is sm_100 and prepares library state. */
+TESSA_API int tessa_create(int device, tessa_ctx** out);
+TESSA_API void tessa_destroy(tessa_ctx* ctx);
+TESSA_API int tessa_ctx_device(const tessa_ctx* ctx);
+
+/* ------------------------------------------------------- SQ8 quantizer --- */
+
+/* Per-row symmetric int8 quantization, bit-exact with the reference CPU
+ * quantizer quantize_sq_int8_matrix_with_bits (P/dco_sq_int8.rs:1331-1375,
+ * 1431-1466), which the reference replay uses (P/tessa_replay.rs:1291-1296):
+ *   norm  = sequential f32 sum of x*x; scale = max|x| / (2^(bits-1)-1) (1 if 0);
+ *   code  = clamp(round_half_away(x/scale)), zero-padded to padded_dim =
+ *           ceil(dim/k_align)*k_align.
+ * Replaces sq8_quantize_rows_kernel (CB:17955-18014), whose tree-reduced norm
+ * does not match the CPU bits.  Device pointers; codes is rows x padded_dim. */
+TESSA_API int tessa_quantize_sq8(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t dim,
+                       uint32_t k_align, uint32_t bits, int8_t* codes, float* scales, float* norms,
+                       void* stream);
+
+/* Host-buffer variant (copies in and out inside the call). */
+TESSA_API int tessa_quantize_sq8_host(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t dim,
+                            uint32_t k_align, uint32_t bits, int8_t* codes, float* scales,
+                            float* norms);
+
+/* ------------------------------------------------------- SQ8 leaf top-k --- */
+
+/* A batch of leaves, laid out as the reference replay lays them out
+ * (TessaLeafLayout, P/tessa_replay.rs:1045-1050; leaf descriptors CB:35189-35230):
+ * leaf l owns leaf_members[leaf_starts[l] .. leaf_starts[l] + leaf_sizes[l]),
+ * each entry a local resident row id; output row r of leaf l is written at
+ * (leaf_starts[l] + r) * k in topk_ids / topk_dists. */
+typedef struct tessa_leaf_args {
+  /* resident rows, indexed by local id (device pointers) */
+  const int8_t* codes;          /* resident_rows x padded_dim, zero padded */
+  const float* scales;          /* SQ8 scales */
+  const float* norms;           /* SQ8 norms (CB:35094-35098 passes sq8_norms) */
+  const uint32_t* global_ids;   /* output id of each resident row */
+  uint64_t resident_rows;
+  uint32_t padded_dim;          /* multiple of 16, <= TESSA_MAX_PADDED_DIM */
+  uint32_t k;                   /* 1 .. TESSA_MAX_LEAF_K */
+  /* leaf layout */
+  const uint32_t* leaf_members; /* device pointer, leaf_rows entries */
+  const uint64_t* leaf_starts;  /* HOST pointer, leaf_count entries */
+  const uint64_t* leaf_sizes;   /* HOST pointer, leaf_count entries */
+  uint64_t leaf_count;
+  uint64_t leaf_rows;           /* total member entries */
+  /* outputs (device pointers, leaf_rows * k entries each) */
+  uint32_t* topk_ids;
+  float* topk_dists;
+  /* Optional (may be NULL): codes already in leaf order, row p = codes row
+   * leaf_members[p], leaf_rows x padded_dim.  When NULL the library gathers
+   * them into its own device scratch (leaf_rows * padded_dim bytes). */
+  const int8_t* leaf_ordered_codes;
+} tessa_leaf_args;
+
+/* All-pairs SQ8 leaf evaluation with per-row bounded top-k: int8 tcgen05 GEMM
+ * with int32 accumulation in TMEM fed by TMA, fused with the reference's
+ * per-row sorted insertion (ascending member order, self skipped by local id,
+ * CB:9569-9650), so no distance matrix reaches HBM.  Replaces
+ * gpu_persistent_subtree_topk_only's SQ8 executors (CB:16146, CB:9364,
+ * CB:10389) as launched by TessaCudaReplaySession::launch_leaf
+ * (CB:35026-35152).  Rows without k candidates keep (FLT_MAX, 0xffffffff)
+ * in their tail slots. */
+TESSA_API int tessa_leaf_topk_sq8(tessa_ctx* ctx, const tessa_leaf_args* args, void* stream);
+
+/* Host-buffer variant: every pointer of `args` (including leaf_members and the
+ * outputs) is a HOST pointer; the call uploads, runs and downloads.  This is
+ * the form the compute-backend trait method
+ * process_quantized_subtree_l2_compact_topk (CB:3693-3884) binds. */
+TESSA_API int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* args);
+
+/* ------------------------------------------------------------ assignment --- */
+
+/* Frozen assignment tasks in the replay layout (TessaAssignmentLayout,
+ * P/tessa_replay.rs:1036-1043; kernel arguments CB:15729-15758). */
+typedef struct tessa_assign_args {
+  const float* x;              /* resident_rows x dim raw vectors (FP32 modes) */
+  const float* raw_norms;      /* FP32-mode norms */
+  const int8_t* codes;         /* resident_rows x padded_dim (SQ8 modes) */
+  const float* scales;
+  const float* sq8_norms;
+  const uint32_t* global_ids;
+  uint64_t resident_rows;
+  uint32_t dim;
+  uint32_t padded_dim;
+  const uint32_t* members;
+  const uint32_t* leaders;
+  const uint32_t* task_member_offsets;
+  const uint32_t* task_member_counts;
+  const uint32_t* task_leader_offsets;
+  const uint32_t* task_leader_counts;
+  const uint32_t* task_rh;
+  const uint64_t* task_output_offsets;
+  uint32_t task_count;
+  uint64_t member_rows;        /* total member entries over all tasks */
+  uint32_t* out_ids;           /* output_len entries */
+  float* out_dists;
+} tessa_assign_args;
+
+/* Distance source of an assignment call. */
+#define TESSA_ASSIGN_FP32 0u  /* A0: sequential FP32 dot, CB:13646-13896 / CB:6436-6444 */
+#define TESSA_ASSIGN_SQ8 2u   /* SQ8 int8 dot, n_p+n_l-2*s_p*s_l*dot, CB:14676-14678 */
+
+/* Per-row best r_h <= 4 leaders (local fan-out 4, CB:15808) with the
+ * reference's splitmix64 tie keys (CB:6510-6578); output id =
+ * global_ids[leader].  All pointers are device pointers except the task
+ * arrays, which are HOST pointers (the library uploads them). */
+TESSA_API int tessa_assign(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* args, void* stream);
+
+/* ------------------------------------------------------- replay session --- */
+
+/* TessaPreparedReplay (P/tessa_replay.rs:1052-1074) as host arrays. */
+typedef struct tessa_prepared_replay {
+  uint32_t dim;
+  uint32_t padded_dim;
+  uint64_t resident_rows;        /* = len(global_ids) */
+  const uint32_t* global_ids;
+  const float* vectors;          /* resident_rows x dim */
+  const float* raw_norms;
+  const int8_t* sq8_codes;       /* resident_rows x padded_dim */
+  const float* sq8_scales;
+  const float* sq8_norms;
+  const uint32_t* assignment_members;
+  uint64_t assignment_member_rows;
+  const uint32_t* assignment_leaders;
+  uint64_t assignment_leader_rows;
+  const uint32_t* task_member_offsets;
+  const uint32_t* task_member_counts;
+  const uint32_t* task_leader_offsets;
+  const uint32_t* task_leader_counts;
+  const uint32_t* task_rh;
+  const uint64_t* task_output_offsets;
+  uint32_t task_count;
+  uint64_t assignment_output_len;
+  const uint32_t* leaf_members;
+  uint64_t leaf_rows;
+  const uint64_t* leaf_starts;
+  const uint64_t* leaf_sizes;
+  uint64_t leaf_count;
+  uint32_t leaf_k;
+} tessa_prepared_replay;
+
+/* TessaReplayMode (P/tessa_replay.rs:18-86), same order and codes. */
+#define TESSA_MODE_A0_FP32_SIMT 0u
+#define TESSA_MODE_A1_TF32_WMMA 1u
+#define TESSA_MODE_A2_SQ8_DP4A_BATCH1 2u
+#define TESSA_MODE_A3_SQ8_WMMA_BATCH8 3u
+#define TESSA_MODE_SQ8_DP4A_BATCH8 4u
+#define TESSA_MODE_SQ8_WMMA_BATCH1 5u
+
+/* TessaCudaModeResult (P/tessa_replay.rs:190-200); caller-owned host buffers
+ * of assignment_output_len and leaf_rows*leaf_k entries.  leaf_* may be NULL
+ * for modes that replay no leaf tasks. */
+typedef struct tessa_mode_result {
+  double assignment_event_ms;
+  double leaf_event_ms;          /* < 0 when the mode replays no leaf tasks */
+  double total_event_ms;
+  uint32_t* assignment_ids;
+  float* assignment_dists;
+  uint32_t* leaf_ids;
+  float* leaf_dists;
+  uint64_t device_error_bits;    /* OR of kernel error words (0 = clean) */
+} tessa_mode_result;
+
+/* TessaCudaReplaySession::new (CB:34649-34839): uploads the prepared replay
+ * once. */
+TESSA_API int tessa_replay_session_create(int device, const tessa_prepared_replay* prepared,
+                                tessa_replay_session** out);
+/* TessaCudaReplaySession::run_mode (CB:34841-34969): clears outputs, runs the
+ * assignment and (for modes A0-A3) leaf operators between CUDA events,
+ * downloads the results and applies the safety gate. */
+TESSA_API int tessa_replay_run_mode(tessa_replay_session* session, uint32_t mode, tessa_mode_result* result);
+TESSA_API void tessa_replay_session_destroy(tessa_replay_session* session);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TESSA_SM100_H */

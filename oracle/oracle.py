@@ -1,0 +1,167 @@
+"""ctypes front end of the CPU checker library (``oracle/tessa_oracle.c``).
+
+Test infrastructure only: tests/, ``__graft_entry__.smoke()`` and bench.py's
+CPU-baseline leg import this module to check or time the CUDA path.  The
+shipped package never imports it.
+
+Each wrapper restates one reference function; the C file cites the
+reference file:line for each.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libtessa_oracle.so")
+_lib = None
+
+EMPTY_ID = 0xFFFFFFFF
+EMPTY_DIST = np.float32(3.402823466e38)
+
+
+def build() -> str:
+    """Compile the checker library with the committed Makefile."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        _lib = ctypes.CDLL(_LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def _p(dtype):
+    return np.ctypeslib.ndpointer(dtype=dtype, flags="C_CONTIGUOUS")
+
+
+def _declare(L):
+    u32, u64, i64, f32 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int64, ctypes.c_float
+    L.oracle_padded_dim.restype = u32
+    L.oracle_padded_dim.argtypes = [u32, u32]
+    L.oracle_quantize_sq8.restype = i64
+    L.oracle_quantize_sq8.argtypes = [_p(np.float32), u64, u32, u32, u32, _p(np.int8),
+                                      _p(np.float32), _p(np.float32)]
+    L.oracle_raw_norms.restype = None
+    L.oracle_raw_norms.argtypes = [_p(np.float32), u64, u32, _p(np.float32)]
+    L.oracle_sq8_dot.restype = ctypes.c_int32
+    L.oracle_sq8_dot.argtypes = [_p(np.int8), _p(np.int8), u32]
+    L.oracle_sq8_l2_from_dot.restype = f32
+    L.oracle_sq8_l2_from_dot.argtypes = [ctypes.c_int32, f32, f32, f32, f32]
+    L.oracle_leaf_topk_sq8.restype = ctypes.c_int
+    L.oracle_leaf_topk_sq8.argtypes = [_p(np.int8), _p(np.float32), _p(np.float32), _p(np.uint32),
+                                       u64, u32, _p(np.uint32), _p(np.uint64), _p(np.uint64), u64,
+                                       u32, u32, u32, _p(np.uint32), _p(np.float32)]
+    L.oracle_hash64.restype = u64
+    L.oracle_hash64.argtypes = [u64]
+    L.oracle_assignment_tie_key.restype = u64
+    L.oracle_assignment_tie_key.argtypes = [u32, u32]
+    L.oracle_assign.restype = ctypes.c_int
+    L.oracle_assign.argtypes = [u32, _p(np.float32), _p(np.float32), _p(np.int8), _p(np.float32),
+                                _p(np.uint32), u64, u32, u32, _p(np.uint32), _p(np.uint32),
+                                _p(np.uint32), _p(np.uint32), _p(np.uint32), _p(np.uint32),
+                                _p(np.uint32), _p(np.uint64), u32, _p(np.uint32), _p(np.float32)]
+    L.oracle_num_threads.restype = ctypes.c_int
+    L.oracle_set_num_threads.argtypes = [ctypes.c_int]
+
+
+def padded_dim(dim: int, k_align: int = 16) -> int:
+    return int(lib().oracle_padded_dim(dim, k_align))
+
+
+def quantize_sq8(x: np.ndarray, k_align: int = 16, bits: int = 8):
+    """P/dco_sq_int8.rs:1331-1375 -> (codes [rows, padded_dim] i8, scales, norms)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, dim = x.shape
+    pd = padded_dim(dim, k_align)
+    codes = np.zeros((rows, pd), dtype=np.int8)
+    scales = np.zeros(rows, dtype=np.float32)
+    norms = np.zeros(rows, dtype=np.float32)
+    rc = lib().oracle_quantize_sq8(x.reshape(-1), rows, dim, k_align, bits, codes.reshape(-1),
+                                   scales, norms)
+    if rc < 0:
+        raise ValueError(f"SQ-int8 quantization failed (code {rc})")
+    return codes, scales, norms
+
+
+def raw_norms(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(x.shape[0], dtype=np.float32)
+    lib().oracle_raw_norms(x.reshape(-1), x.shape[0], x.shape[1], out)
+    return out
+
+
+def sq8_dot(a: np.ndarray, b: np.ndarray) -> int:
+    a = np.ascontiguousarray(a, dtype=np.int8)
+    b = np.ascontiguousarray(b, dtype=np.int8)
+    return int(lib().oracle_sq8_dot(a, b, a.shape[0]))
+
+
+def sq8_l2_from_dot(dot, rs, rn, cs, cn) -> np.float32:
+    return np.float32(lib().oracle_sq8_l2_from_dot(int(dot), float(rs), float(rn), float(cs),
+                                                   float(cn)))
+
+
+def leaf_topk_sq8(codes, scales, norms, global_ids, leaf_members, leaf_offsets, leaf_counts, k,
+                  col_task_width: int = 0, staged_min_rows: int = 512):
+    """Leaf top-k over a batch of leaves; returns (ids, dists) of len(leaf_members)*k."""
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    leaf_members = np.ascontiguousarray(leaf_members, dtype=np.uint32)
+    offs = np.ascontiguousarray(leaf_offsets, dtype=np.uint64)
+    cnts = np.ascontiguousarray(leaf_counts, dtype=np.uint64)
+    n_out = int(leaf_members.shape[0]) * k
+    ids = np.full(n_out, EMPTY_ID, dtype=np.uint32)
+    dists = np.full(n_out, EMPTY_DIST, dtype=np.float32)
+    rc = lib().oracle_leaf_topk_sq8(codes.reshape(-1), np.ascontiguousarray(scales, np.float32),
+                                    np.ascontiguousarray(norms, np.float32),
+                                    np.ascontiguousarray(global_ids, np.uint32), codes.shape[0],
+                                    codes.shape[1], leaf_members, offs, cnts, offs.shape[0], k,
+                                    col_task_width, staged_min_rows, ids, dists)
+    if rc != 0:
+        raise ValueError(f"oracle leaf top-k failed (code {rc})")
+    return ids, dists
+
+
+def assign(mode, x, norms, codes, scales, global_ids, members, leaders, task_member_offsets,
+           task_member_counts, task_leader_offsets, task_leader_counts, task_rh,
+           task_output_offsets, output_len):
+    """Assignment replay semantics (CB:15729-15943); mode 0 FP32, 2 SQ8 plain, 3 SQ8 fused."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    ids = np.full(output_len, EMPTY_ID, dtype=np.uint32)
+    dists = np.full(output_len, EMPTY_DIST, dtype=np.float32)
+    u32 = lambda a: np.ascontiguousarray(a, dtype=np.uint32)
+    rc = lib().oracle_assign(mode, x.reshape(-1), np.ascontiguousarray(norms, np.float32),
+                             codes.reshape(-1), np.ascontiguousarray(scales, np.float32),
+                             u32(global_ids), x.shape[0], x.shape[1], codes.shape[1], u32(members),
+                             u32(leaders), u32(task_member_offsets), u32(task_member_counts),
+                             u32(task_leader_offsets), u32(task_leader_counts), u32(task_rh),
+                             np.ascontiguousarray(task_output_offsets, np.uint64),
+                             len(task_rh), ids, dists)
+    if rc != 0:
+        raise ValueError(f"oracle assignment failed (code {rc})")
+    return ids, dists
+
+
+def hash64(v: int) -> int:
+    return int(lib().oracle_hash64(v))
+
+
+def tie_key(point: int, leader: int) -> int:
+    return int(lib().oracle_assignment_tie_key(point, leader))
+
+
+def num_threads() -> int:
+    return int(lib().oracle_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    lib().oracle_set_num_threads(int(n))

@@ -1,0 +1,138 @@
+"""ctypes binding of libtessa_sm100.so (declarations mirror include/tessa_sm100.h).
+
+The shared library is the product; this module only loads it and declares the
+entry points.  Loading fails loudly: there is no CPU fallback anywhere in this
+package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtessa_sm100.so")
+
+TESSA_OK = 0
+ERRORS = {
+    -1: "TESSA_ERR_INVALID_ARG",
+    -2: "TESSA_ERR_CUDA",
+    -3: "TESSA_ERR_OOM",
+    -4: "TESSA_ERR_TIMEOUT",
+    -5: "TESSA_ERR_BAD_ROW",
+    -6: "TESSA_ERR_UNSUPPORTED",
+    -7: "TESSA_ERR_NONFINITE",
+    -8: "TESSA_ERR_NO_DEVICE",
+    -9: "TESSA_ERR_BAD_TASK",
+}
+MAX_LEAF_K = 32
+MAX_RH = 4
+MAX_PADDED_DIM = 1024
+ASSIGN_FP32 = 0
+ASSIGN_SQ8 = 2
+
+c_u32p = ctypes.POINTER(ctypes.c_uint32)
+c_u64p = ctypes.POINTER(ctypes.c_uint64)
+c_f32p = ctypes.POINTER(ctypes.c_float)
+c_i8p = ctypes.POINTER(ctypes.c_int8)
+c_vp = ctypes.c_void_p
+
+
+class TessaError(RuntimeError):
+    """A TESSA_ERR_* code returned across the C ABI."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {message}")
+        self.code = code
+
+
+class LeafArgs(ctypes.Structure):
+    _fields_ = [
+        ("codes", c_vp), ("scales", c_vp), ("norms", c_vp), ("global_ids", c_vp),
+        ("resident_rows", ctypes.c_uint64), ("padded_dim", ctypes.c_uint32), ("k", ctypes.c_uint32),
+        ("leaf_members", c_vp), ("leaf_starts", c_vp), ("leaf_sizes", c_vp),
+        ("leaf_count", ctypes.c_uint64), ("leaf_rows", ctypes.c_uint64),
+        ("topk_ids", c_vp), ("topk_dists", c_vp), ("leaf_ordered_codes", c_vp),
+    ]
+
+
+class AssignArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_vp), ("raw_norms", c_vp), ("codes", c_vp), ("scales", c_vp), ("sq8_norms", c_vp),
+        ("global_ids", c_vp), ("resident_rows", ctypes.c_uint64), ("dim", ctypes.c_uint32),
+        ("padded_dim", ctypes.c_uint32), ("members", c_vp), ("leaders", c_vp),
+        ("task_member_offsets", c_vp), ("task_member_counts", c_vp), ("task_leader_offsets", c_vp),
+        ("task_leader_counts", c_vp), ("task_rh", c_vp), ("task_output_offsets", c_vp),
+        ("task_count", ctypes.c_uint32), ("member_rows", ctypes.c_uint64), ("out_ids", c_vp),
+        ("out_dists", c_vp),
+    ]
+
+
+class PreparedReplay(ctypes.Structure):
+    _fields_ = [
+        ("dim", ctypes.c_uint32), ("padded_dim", ctypes.c_uint32), ("resident_rows", ctypes.c_uint64),
+        ("global_ids", c_vp), ("vectors", c_vp), ("raw_norms", c_vp), ("sq8_codes", c_vp),
+        ("sq8_scales", c_vp), ("sq8_norms", c_vp), ("assignment_members", c_vp),
+        ("assignment_member_rows", ctypes.c_uint64), ("assignment_leaders", c_vp),
+        ("assignment_leader_rows", ctypes.c_uint64), ("task_member_offsets", c_vp),
+        ("task_member_counts", c_vp), ("task_leader_offsets", c_vp), ("task_leader_counts", c_vp),
+        ("task_rh", c_vp), ("task_output_offsets", c_vp), ("task_count", ctypes.c_uint32),
+        ("assignment_output_len", ctypes.c_uint64), ("leaf_members", c_vp),
+        ("leaf_rows", ctypes.c_uint64), ("leaf_starts", c_vp), ("leaf_sizes", c_vp),
+        ("leaf_count", ctypes.c_uint64), ("leaf_k", ctypes.c_uint32),
+    ]
+
+
+class ModeResult(ctypes.Structure):
+    _fields_ = [
+        ("assignment_event_ms", ctypes.c_double), ("leaf_event_ms", ctypes.c_double),
+        ("total_event_ms", ctypes.c_double), ("assignment_ids", c_vp), ("assignment_dists", c_vp),
+        ("leaf_ids", c_vp), ("leaf_dists", c_vp), ("device_error_bits", ctypes.c_uint64),
+    ]
+
+
+# (name, restype, argtypes) for every entry point of include/tessa_sm100.h
+SIGNATURES = [
+    ("tessa_abi_version", ctypes.c_int, []),
+    ("tessa_strerror", ctypes.c_char_p, [ctypes.c_int]),
+    ("tessa_last_error_message", ctypes.c_char_p, []),
+    ("tessa_create", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(c_vp)]),
+    ("tessa_destroy", None, [c_vp]),
+    ("tessa_ctx_device", ctypes.c_int, [c_vp]),
+    ("tessa_quantize_sq8", ctypes.c_int,
+     [c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp,
+      c_vp]),
+    ("tessa_quantize_sq8_host", ctypes.c_int,
+     [c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp]),
+    ("tessa_leaf_topk_sq8", ctypes.c_int, [c_vp, ctypes.POINTER(LeafArgs), c_vp]),
+    ("tessa_leaf_topk_sq8_host", ctypes.c_int, [c_vp, ctypes.POINTER(LeafArgs)]),
+    ("tessa_assign", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(AssignArgs), c_vp]),
+    ("tessa_replay_session_create", ctypes.c_int,
+     [ctypes.c_int, ctypes.POINTER(PreparedReplay), ctypes.POINTER(c_vp)]),
+    ("tessa_replay_run_mode", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(ModeResult)]),
+    ("tessa_replay_session_destroy", None, [c_vp]),
+]
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the library (raises if it is missing: there is no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(
+            f"{path} is missing; build it with `python -m shear_b200.build` (nvcc, sm_100a)")
+    lib = ctypes.CDLL(path)
+    for name, res, args in SIGNATURES:
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(code: int) -> None:
+    if code != TESSA_OK:
+        msg = load().tessa_last_error_message()
+        raise TessaError(code, msg.decode() if msg else "")

@@ -1,0 +1,236 @@
+// TESSA leader assignment replay on sm_100a: for every member row of a frozen
+// assignment task, the best four leader slots (local fan-out 4) under the
+// reference's hash-keyed tie rule, then the first r_h of them as
+// (global id, distance).
+//
+// Reference (wbh1765091327/SHEAR, CB = shear-core/src/algorithm/pipnn/
+// compute_backend.rs): gpu_tessa_assignment_replay CB:15729-15943; leaders are
+// visited in ascending slot order (CB:13614-13634, CB:14782-14908) and each
+// distance goes through gpu_persistent_assignment_insert_candidate
+// (CB:6524-6578) with tie key splitmix64((point<<32) ^ leader ^ golden)
+// (CB:5983-5989, 6510-6520) over LOCAL resident ids.
+//
+// Distances:
+//   FP32 (A0): dot = sequential rn(rn(x*y) + acc) over axes (the tiled FP32
+//              executor's order, CB:13829-13842, equal to CB:6077-6087), then
+//              rn(rn(n_p + n_l) + rn(-2*dot)) clamped at 0 (CB:13621-13624) --
+//              bit-exact with the reference's FP32 SIMT executor.
+//   SQ8:       n_p + n_l - 2*s_p*s_l*dot (CB:14676-14678).  The reference
+//              leaves contraction to the compiler; `fused` selects the single
+//              FFMA form nvcc's default --fmad=true produces, otherwise one
+//              rounding per operation.
+//
+// Layout: one CTA = 128 member rows of one task, one thread per row; leaders
+// are streamed through shared memory in groups of 32 leaders x one K tile, and
+// each thread keeps 32 independent partial dots in registers (axis order per
+// dot is preserved, so the FP32 sums stay bit-exact).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tessa {
+namespace assign {
+
+constexpr uint32_t kRows = 128;     // member rows per CTA
+constexpr uint32_t kLeaders = 32;   // leaders per register group
+constexpr uint32_t kAxF = 32;       // FP32 axes per K tile
+constexpr uint32_t kAxQ = 64;       // SQ8 bytes per K tile
+
+
+__device__ __forceinline__ uint64_t hash64(uint64_t v) {
+  v ^= v >> 30;
+  v *= 0xbf58476d1ce4e5b9ull;
+  v ^= v >> 27;
+  v *= 0x94d049bb133111ebull;
+  return v ^ (v >> 31);
+}
+
+__device__ __forceinline__ uint64_t tie_key(uint32_t point, uint32_t leader) {
+  return hash64((((uint64_t)point) << 32) ^ (uint64_t)leader ^ 0x9e3779b97f4a7c15ull);
+}
+
+// CB:6524-6578 with slots = 4.
+__device__ __forceinline__ void insert4(float d, uint32_t point, uint32_t leader, uint32_t slot, float (&bd)[4],
+                                        uint32_t (&bs)[4], uint32_t (&bl)[4]) {
+  bool better = d < bd[3];
+  uint64_t ck = 0;
+  bool ck_ready = false;
+  if (fabsf(__fsub_rn(d, bd[3])) <= 2.0e-5f) {
+    ck = tie_key(point, leader);
+    ck_ready = true;
+    uint64_t fk = tie_key(point, bl[3]);
+    better = ck < fk || (ck == fk && leader < bl[3]);
+  }
+  if (!better) return;
+  int pos = 3;
+#pragma unroll
+  for (int j = 3; j >= 1; --j) {
+    if (pos != j) break;
+    bool before = d < bd[j - 1];
+    if (fabsf(__fsub_rn(d, bd[j - 1])) <= 2.0e-5f) {
+      if (!ck_ready) {
+        ck = tie_key(point, leader);
+        ck_ready = true;
+      }
+      uint64_t pk = tie_key(point, bl[j - 1]);
+      before = ck < pk || (ck == pk && leader < bl[j - 1]);
+    }
+    if (!before) break;
+    bd[j] = bd[j - 1];
+    bs[j] = bs[j - 1];
+    bl[j] = bl[j - 1];
+    pos = j - 1;
+  }
+  // pos is where the candidate lands; write with compile-time indices.
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (j == pos) {
+      bd[j] = d;
+      bs[j] = slot;
+      bl[j] = leader;
+    }
+}
+
+template <bool SQ8>
+__global__ void __launch_bounds__(kRows) assign_kernel(const Params p) {
+  __shared__ __align__(16) float lt_f[kLeaders][kAxF];
+  __shared__ __align__(16) int lt_q[kLeaders][kAxQ / 4];
+  __shared__ uint32_t l_ids[kLeaders];
+  __shared__ float l_norm[kLeaders];
+  __shared__ float l_scale[kLeaders];
+
+  if (blockIdx.x >= p.num_work) return;
+  uint2 w = p.work[blockIdx.x];
+  uint32_t task = w.x;
+  uint32_t moff = p.t_moff[task], mcnt = p.t_mcnt[task];
+  uint32_t loff = p.t_loff[task], nl = p.t_lcnt[task], rh = p.t_rh[task];
+  uint32_t r = w.y + threadIdx.x;
+  bool valid = r < mcnt;
+  uint32_t point = valid ? p.members[moff + r] : 0u;
+  if (valid && point >= p.resident_rows) {
+    atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+    valid = false;
+  }
+  const float* norms = SQ8 ? p.sq8_norms : p.raw_norms;
+  float n_p = valid ? norms[point] : 0.f;
+  float s_p = (SQ8 && valid) ? p.scales[point] : 0.f;
+
+  float bd[4];
+  uint32_t bs[4], bl[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    bd[j] = 3.402823466e+38F;
+    bs[j] = 0xffffffffu;
+    bl[j] = 0xffffffffu;
+  }
+
+  for (uint32_t lg = 0; lg < nl; lg += kLeaders) {
+    uint32_t gl = nl - lg < kLeaders ? nl - lg : kLeaders;
+    __syncthreads();
+    if (threadIdx.x < kLeaders) {
+      uint32_t lid = 0xffffffffu;
+      float ln = 0.f, ls = 0.f;
+      if (threadIdx.x < gl) {
+        lid = p.leaders[loff + lg + threadIdx.x];
+        if (lid >= p.resident_rows) {
+          atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+          lid = 0xffffffffu;
+        } else {
+          ln = norms[lid];
+          ls = SQ8 ? p.scales[lid] : 0.f;
+        }
+      }
+      l_ids[threadIdx.x] = lid;
+      l_norm[threadIdx.x] = ln;
+      l_scale[threadIdx.x] = ls;
+    }
+    float accf[kLeaders];
+    int acci[kLeaders];
+#pragma unroll
+    for (int l = 0; l < (int)kLeaders; ++l) {
+      accf[l] = 0.0f;
+      acci[l] = 0;
+    }
+    if (!SQ8) {
+      for (uint32_t a0 = 0; a0 < p.dim; a0 += kAxF) {
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < kLeaders * kAxF; i += kRows) {
+          uint32_t l = i / kAxF, a = i % kAxF;
+          uint32_t lid = l_ids[l];
+          lt_f[l][a] = (lid != 0xffffffffu && a0 + a < p.dim) ? p.x[(uint64_t)lid * p.dim + a0 + a] : 0.0f;
+        }
+        __syncthreads();
+        uint32_t na = p.dim - a0 < kAxF ? p.dim - a0 : kAxF;
+        const float* xr = p.x + (uint64_t)point * p.dim + a0;
+        for (uint32_t a = 0; a < na; ++a) {
+          float xv = valid ? __ldg(xr + a) : 0.0f;
+#pragma unroll
+          for (int l = 0; l < (int)kLeaders; ++l) accf[l] = __fadd_rn(accf[l], __fmul_rn(xv, lt_f[l][a]));
+        }
+      }
+    } else {
+      for (uint32_t a0 = 0; a0 < p.padded_dim; a0 += kAxQ) {
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < kLeaders * (kAxQ / 4); i += kRows) {
+          uint32_t l = i / (kAxQ / 4), q = i % (kAxQ / 4);
+          uint32_t lid = l_ids[l];
+          int v = 0;
+          if (lid != 0xffffffffu && a0 + q * 4 < p.padded_dim)
+            v = *reinterpret_cast<const int*>(p.codes + (uint64_t)lid * p.padded_dim + a0 + q * 4);
+          lt_q[l][q] = v;
+        }
+        __syncthreads();
+        uint32_t nq = (p.padded_dim - a0 < kAxQ ? p.padded_dim - a0 : kAxQ) / 4;
+        const int* cr = reinterpret_cast<const int*>(p.codes + (uint64_t)point * p.padded_dim + a0);
+        for (uint32_t q = 0; q < nq; ++q) {
+          int cv = valid ? __ldg(cr + q) : 0;
+#pragma unroll
+          for (int l = 0; l < (int)kLeaders; ++l) acci[l] = __dp4a(cv, lt_q[l][q], acci[l]);
+        }
+      }
+    }
+    if (valid) {
+      for (uint32_t l = 0; l < gl; ++l) {
+        uint32_t lid = l_ids[l];
+        if (lid == 0xffffffffu) continue;
+        float d;
+        if (!SQ8) {
+          d = __fadd_rn(__fadd_rn(n_p, l_norm[l]), __fmul_rn(-2.0f, accf[l]));
+        } else {
+          float nn = __fadd_rn(n_p, l_norm[l]);
+          float t = __fmul_rn(__fmul_rn(2.0f, s_p), l_scale[l]);
+          float df = __int2float_rn(acci[l]);
+          d = p.fused ? __fmaf_rn(-t, df, nn) : __fsub_rn(nn, __fmul_rn(t, df));
+        }
+        if (d <= 0.0f) d = 0.0f;
+        insert4(d, point, lid, lg + l, bd, bs, bl);
+      }
+    }
+  }
+
+  if (!valid) return;
+  uint64_t out = p.t_out[task] + (uint64_t)r * rh;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if ((uint32_t)j >= rh) break;
+    if (bs[j] >= nl) {
+      atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
+      continue;
+    }
+    p.out_ids[out + j] = p.global_ids[bl[j]];
+    p.out_dists[out + j] = bd[j];
+  }
+}
+
+}  // namespace assign
+
+
+int launch_assign(const assign::Params& prm, bool sq8, cudaStream_t stream) {
+  if (prm.num_work == 0) return TESSA_OK;
+  if (sq8)
+    assign::assign_kernel<true><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+  else
+    assign::assign_kernel<false><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+}  // namespace tessa

@@ -1,0 +1,708 @@
+// C ABI of libtessa_sm100.so: contexts, argument validation, host-side
+// planning (tile tables), device scratch, the host-buffer entry points and the
+// replay session that mirrors TessaCudaReplaySession (reference
+// CB:34597-35305).  No exception or abort crosses the ABI: every entry point
+// returns TESSA_OK or a negative TESSA_ERR_* code and records a message for
+// tessa_last_error_message().
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+#include "kernels.h"
+
+using namespace tessa;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                        \
+  do {                                                                                        \
+    cudaError_t _e = (expr);                                                                  \
+    if (_e != cudaSuccess)                                                                    \
+      return fail(_e == cudaErrorMemoryAllocation ? TESSA_ERR_OOM : TESSA_ERR_CUDA, "%s: %s (%s:%d)", #expr, \
+                  cudaGetErrorString(_e), __FILE__, __LINE__);                                 \
+  } while (0)
+
+#define TRY(expr)              \
+  do {                         \
+    int _r = (expr);           \
+    if (_r != TESSA_OK) return _r; \
+  } while (0)
+
+constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // bounded device waits: 2 s
+
+// Grow-only device buffer.
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int ensure(size_t need) {
+    if (need <= bytes) return TESSA_OK;
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+    if (need == 0) return TESSA_OK;
+    cudaError_t e = cudaMalloc(&ptr, need);
+    if (e != cudaSuccess) {
+      ptr = nullptr;
+      return fail(e == cudaErrorMemoryAllocation ? TESSA_ERR_OOM : TESSA_ERR_CUDA, "cudaMalloc(%zu): %s", need,
+                  cudaGetErrorString(e));
+    }
+    bytes = need;
+    return TESSA_OK;
+  }
+  void release() {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+  }
+  template <class T>
+  T* as() const {
+    return reinterpret_cast<T*>(ptr);
+  }
+};
+
+int map_device_error(uint32_t bits) {
+  if (bits == 0) return TESSA_OK;
+  if (bits & TESSA_DEVERR_TIMEOUT) return fail(TESSA_ERR_TIMEOUT, "device wait timed out (error bits 0x%x)", bits);
+  if (bits & TESSA_DEVERR_BAD_ROW) return fail(TESSA_ERR_BAD_ROW, "row id outside resident rows (0x%x)", bits);
+  if (bits & TESSA_DEVERR_NONFINITE) return fail(TESSA_ERR_NONFINITE, "non-finite quantizer input (0x%x)", bits);
+  return fail(TESSA_ERR_BAD_TASK, "malformed task descriptor on device (0x%x)", bits);
+}
+
+// Host-side leaf plan: (leaf, first row) per 128-row tile plus device copies
+// of the leaf layout.  Cached by content so repeated calls on the same layout
+// upload nothing.
+struct LeafPlan {
+  std::vector<uint64_t> starts;
+  std::vector<uint64_t> sizes;
+  uint64_t leaf_rows = 0;
+  uint32_t num_tiles = 0;
+  DevBuf d_starts, d_sizes, d_tiles;
+  bool valid = false;
+
+  int build(const uint64_t* h_starts, const uint64_t* h_sizes, uint64_t leaf_count, uint64_t rows, cudaStream_t st) {
+    if (valid && leaf_count == starts.size() && rows == leaf_rows &&
+        (leaf_count == 0 || (memcmp(h_starts, starts.data(), leaf_count * 8) == 0 &&
+                             memcmp(h_sizes, sizes.data(), leaf_count * 8) == 0)))
+      return TESSA_OK;
+    valid = false;
+    std::vector<uint32_t> sz32(leaf_count);
+    std::vector<uint2> tiles;
+    for (uint64_t l = 0; l < leaf_count; ++l) {
+      if (h_sizes[l] > 0x7fffffffull || h_starts[l] > rows || h_sizes[l] > rows - h_starts[l])
+        return fail(TESSA_ERR_INVALID_ARG, "leaf %llu [start %llu, size %llu] outside %llu member rows",
+                    (unsigned long long)l, (unsigned long long)h_starts[l], (unsigned long long)h_sizes[l],
+                    (unsigned long long)rows);
+      if (h_starts[l] + h_sizes[l] > 0x7fffffffull)
+        return fail(TESSA_ERR_UNSUPPORTED, "leaf member rows beyond 2^31 are not supported");
+      sz32[l] = (uint32_t)h_sizes[l];
+      for (uint64_t r0 = 0; r0 < h_sizes[l]; r0 += 128) tiles.push_back(make_uint2((uint32_t)l, (uint32_t)r0));
+    }
+    if (tiles.size() > 0xffffffffull) return fail(TESSA_ERR_UNSUPPORTED, "too many leaf tiles");
+    TRY(d_starts.ensure(leaf_count * 8 + 8));
+    TRY(d_sizes.ensure(leaf_count * 4 + 4));
+    TRY(d_tiles.ensure(tiles.size() * 8 + 8));
+    if (leaf_count) {
+      CUDA_TRY(cudaMemcpyAsync(d_starts.ptr, h_starts, leaf_count * 8, cudaMemcpyHostToDevice, st));
+      CUDA_TRY(cudaMemcpyAsync(d_sizes.ptr, sz32.data(), leaf_count * 4, cudaMemcpyHostToDevice, st));
+    }
+    if (!tiles.empty())
+      CUDA_TRY(cudaMemcpyAsync(d_tiles.ptr, tiles.data(), tiles.size() * 8, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    starts.assign(h_starts, h_starts + leaf_count);
+    sizes.assign(h_sizes, h_sizes + leaf_count);
+    leaf_rows = rows;
+    num_tiles = (uint32_t)tiles.size();
+    valid = true;
+    return TESSA_OK;
+  }
+  void release() {
+    d_starts.release();
+    d_sizes.release();
+    d_tiles.release();
+    valid = false;
+  }
+};
+
+// Host-side assignment plan: (task, first row) per 128-row work item plus
+// device copies of the task arrays.
+struct AssignPlan {
+  DevBuf d_moff, d_mcnt, d_loff, d_lcnt, d_rh, d_out, d_work;
+  uint32_t num_work = 0;
+  uint32_t task_count = 0;
+
+  int build(const tessa_assign_args& a, uint64_t* output_len, cudaStream_t st) {
+    std::vector<uint2> work;
+    uint64_t out_len = 0;
+    for (uint32_t t = 0; t < a.task_count; ++t) {
+      if (a.task_rh[t] == 0 || a.task_rh[t] > TESSA_MAX_RH || a.task_leader_counts[t] < a.task_rh[t])
+        return fail(TESSA_ERR_INVALID_ARG, "assignment task %u has invalid r_h=%u for %u leaders", t, a.task_rh[t],
+                    a.task_leader_counts[t]);
+      if ((uint64_t)a.task_member_offsets[t] + a.task_member_counts[t] > a.member_rows)
+        return fail(TESSA_ERR_INVALID_ARG, "assignment task %u members outside the member array", t);
+      for (uint32_t r0 = 0; r0 < a.task_member_counts[t]; r0 += 128) work.push_back(make_uint2(t, r0));
+      uint64_t end = a.task_output_offsets[t] + (uint64_t)a.task_member_counts[t] * a.task_rh[t];
+      if (end > out_len) out_len = end;
+    }
+    *output_len = out_len;
+    size_t n = a.task_count;
+    TRY(d_moff.ensure(n * 4 + 4));
+    TRY(d_mcnt.ensure(n * 4 + 4));
+    TRY(d_loff.ensure(n * 4 + 4));
+    TRY(d_lcnt.ensure(n * 4 + 4));
+    TRY(d_rh.ensure(n * 4 + 4));
+    TRY(d_out.ensure(n * 8 + 8));
+    TRY(d_work.ensure(work.size() * 8 + 8));
+    if (n) {
+      CUDA_TRY(cudaMemcpyAsync(d_moff.ptr, a.task_member_offsets, n * 4, cudaMemcpyHostToDevice, st));
+      CUDA_TRY(cudaMemcpyAsync(d_mcnt.ptr, a.task_member_counts, n * 4, cudaMemcpyHostToDevice, st));
+      CUDA_TRY(cudaMemcpyAsync(d_loff.ptr, a.task_leader_offsets, n * 4, cudaMemcpyHostToDevice, st));
+      CUDA_TRY(cudaMemcpyAsync(d_lcnt.ptr, a.task_leader_counts, n * 4, cudaMemcpyHostToDevice, st));
+      CUDA_TRY(cudaMemcpyAsync(d_rh.ptr, a.task_rh, n * 4, cudaMemcpyHostToDevice, st));
+      CUDA_TRY(cudaMemcpyAsync(d_out.ptr, a.task_output_offsets, n * 8, cudaMemcpyHostToDevice, st));
+    }
+    if (!work.empty())
+      CUDA_TRY(cudaMemcpyAsync(d_work.ptr, work.data(), work.size() * 8, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    num_work = (uint32_t)work.size();
+    task_count = a.task_count;
+    return TESSA_OK;
+  }
+  void release() {
+    d_moff.release();
+    d_mcnt.release();
+    d_loff.release();
+    d_lcnt.release();
+    d_rh.release();
+    d_out.release();
+    d_work.release();
+  }
+};
+
+}  // namespace
+
+struct tessa_ctx {
+  int device = -1;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  DevBuf d_err;         // one uint32 error word
+  DevBuf gather;        // leaf-ordered codes scratch
+  LeafPlan leaf_plan;
+  AssignPlan assign_plan;
+  // staging for host-buffer entry points
+  DevBuf h_codes, h_scales, h_norms, h_gids, h_members, h_ids, h_dists, h_x;
+  uint64_t timeout_ns = kDefaultTimeoutNs;
+};
+
+namespace {
+
+int bind(tessa_ctx* ctx) {
+  if (!ctx) return fail(TESSA_ERR_INVALID_ARG, "null context");
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  return TESSA_OK;
+}
+
+int read_err(tessa_ctx* ctx, cudaStream_t st, uint32_t* bits) {
+  CUDA_TRY(cudaMemcpyAsync(bits, ctx->d_err.ptr, 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return TESSA_OK;
+}
+
+int clear_err(tessa_ctx* ctx, cudaStream_t st) {
+  CUDA_TRY(cudaMemsetAsync(ctx->d_err.ptr, 0, 4, st));
+  return TESSA_OK;
+}
+
+bool members_identity(const uint32_t* m, uint64_t n) {
+  for (uint64_t i = 0; i < n; ++i)
+    if (m[i] != (uint32_t)i) return false;
+  return true;
+}
+
+int validate_leaf(const tessa_leaf_args* a) {
+  if (!a) return fail(TESSA_ERR_INVALID_ARG, "null leaf args");
+  if (a->k == 0 || a->k > TESSA_MAX_LEAF_K) return fail(TESSA_ERR_INVALID_ARG, "leaf k=%u outside 1..%d", a->k, TESSA_MAX_LEAF_K);
+  if (a->padded_dim == 0 || a->padded_dim % 16 != 0)
+    return fail(TESSA_ERR_INVALID_ARG, "padded_dim=%u must be a positive multiple of 16", a->padded_dim);
+  if (a->padded_dim > TESSA_MAX_PADDED_DIM || leaf_num_bstages(a->padded_dim) == 0)
+    return fail(TESSA_ERR_UNSUPPORTED, "padded_dim=%u above the supported %d", a->padded_dim, TESSA_MAX_PADDED_DIM);
+  if (a->resident_rows > 0xffffffffull) return fail(TESSA_ERR_UNSUPPORTED, "more than 2^32 resident rows");
+  if (a->leaf_count && (!a->leaf_starts || !a->leaf_sizes))
+    return fail(TESSA_ERR_INVALID_ARG, "null leaf layout");
+  if (a->leaf_rows && (!a->leaf_members || !a->codes || !a->scales || !a->norms || !a->global_ids || !a->topk_ids ||
+                       !a->topk_dists))
+    return fail(TESSA_ERR_INVALID_ARG, "null leaf data pointer");
+  return TESSA_OK;
+}
+
+// Leaf op on device pointers (layout arrays on the host).
+int leaf_device(tessa_ctx* ctx, const tessa_leaf_args* a, cudaStream_t st) {
+  TRY(ctx->leaf_plan.build(a->leaf_starts, a->leaf_sizes, a->leaf_count, a->leaf_rows, st));
+  if (ctx->leaf_plan.num_tiles == 0) return TESSA_OK;
+  const int8_t* lc = a->leaf_ordered_codes;
+  if (!lc) {
+    TRY(ctx->gather.ensure((size_t)a->leaf_rows * a->padded_dim));
+    TRY(launch_gather_rows(a->codes, a->leaf_members, a->leaf_rows, a->padded_dim, ctx->gather.as<int8_t>(),
+                           ctx->sm_count, st));
+    lc = ctx->gather.as<int8_t>();
+  }
+  TRY(clear_err(ctx, st));
+  LeafLaunch L;
+  L.leaf_codes = lc;
+  L.leaf_rows = a->leaf_rows;
+  L.padded_dim = a->padded_dim;
+  L.scales = a->scales;
+  L.norms = a->norms;
+  L.global_ids = a->global_ids;
+  L.members = a->leaf_members;
+  L.d_leaf_starts = ctx->leaf_plan.d_starts.as<uint64_t>();
+  L.d_leaf_sizes = ctx->leaf_plan.d_sizes.as<uint32_t>();
+  L.d_tiles = ctx->leaf_plan.d_tiles.as<uint2>();
+  L.num_tiles = ctx->leaf_plan.num_tiles;
+  L.k = a->k;
+  L.out_ids = a->topk_ids;
+  L.out_dists = a->topk_dists;
+  L.d_err = ctx->d_err.as<uint32_t>();
+  L.timeout_ns = ctx->timeout_ns;
+  L.sm_count = ctx->sm_count;
+  int r = launch_leaf_topk_sq8(L, st);
+  if (r != TESSA_OK) return fail(r, "leaf kernel launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  return map_device_error(bits);
+}
+
+int assign_device(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* a, cudaStream_t st) {
+  if (!a) return fail(TESSA_ERR_INVALID_ARG, "null assignment args");
+  if (source != TESSA_ASSIGN_FP32 && source != TESSA_ASSIGN_SQ8)
+    return fail(TESSA_ERR_INVALID_ARG, "unknown assignment source %u", source);
+  if (source == TESSA_ASSIGN_SQ8 && (a->padded_dim == 0 || a->padded_dim % 16 != 0))
+    return fail(TESSA_ERR_INVALID_ARG, "padded_dim=%u must be a positive multiple of 16", a->padded_dim);
+  if (a->task_count && (!a->task_member_offsets || !a->task_member_counts || !a->task_leader_offsets ||
+                        !a->task_leader_counts || !a->task_rh || !a->task_output_offsets))
+    return fail(TESSA_ERR_INVALID_ARG, "null task array");
+  uint64_t out_len = 0;
+  TRY(ctx->assign_plan.build(*a, &out_len, st));
+  if (ctx->assign_plan.num_work == 0) return TESSA_OK;
+  TRY(clear_err(ctx, st));
+  assign::Params p;
+  p.x = a->x;
+  p.raw_norms = a->raw_norms;
+  p.codes = a->codes;
+  p.scales = a->scales;
+  p.sq8_norms = a->sq8_norms;
+  p.global_ids = a->global_ids;
+  p.resident_rows = a->resident_rows;
+  p.dim = a->dim;
+  p.padded_dim = a->padded_dim;
+  p.members = a->members;
+  p.leaders = a->leaders;
+  p.t_moff = ctx->assign_plan.d_moff.as<uint32_t>();
+  p.t_mcnt = ctx->assign_plan.d_mcnt.as<uint32_t>();
+  p.t_loff = ctx->assign_plan.d_loff.as<uint32_t>();
+  p.t_lcnt = ctx->assign_plan.d_lcnt.as<uint32_t>();
+  p.t_rh = ctx->assign_plan.d_rh.as<uint32_t>();
+  p.t_out = ctx->assign_plan.d_out.as<uint64_t>();
+  p.work = ctx->assign_plan.d_work.as<uint2>();
+  p.num_work = ctx->assign_plan.num_work;
+  p.fused = 1u;
+  p.out_ids = a->out_ids;
+  p.out_dists = a->out_dists;
+  p.err_word = ctx->d_err.as<uint32_t>();
+  TRY(launch_assign(p, source == TESSA_ASSIGN_SQ8, st));
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  return map_device_error(bits);
+}
+
+}  // namespace
+
+extern "C" {
+
+int tessa_abi_version(void) { return TESSA_ABI_VERSION; }
+
+const char* tessa_strerror(int code) {
+  switch (code) {
+    case TESSA_OK: return "ok";
+    case TESSA_ERR_INVALID_ARG: return "invalid argument";
+    case TESSA_ERR_CUDA: return "CUDA error";
+    case TESSA_ERR_OOM: return "out of memory";
+    case TESSA_ERR_TIMEOUT: return "device wait timed out";
+    case TESSA_ERR_BAD_ROW: return "row id outside resident rows";
+    case TESSA_ERR_UNSUPPORTED: return "unsupported shape or mode";
+    case TESSA_ERR_NONFINITE: return "non-finite input";
+    case TESSA_ERR_NO_DEVICE: return "no usable sm_100 device";
+    case TESSA_ERR_BAD_TASK: return "malformed task descriptor";
+    default: return "unknown error";
+  }
+}
+
+const char* tessa_last_error_message(void) { return g_last_error.c_str(); }
+
+int tessa_create(int device, tessa_ctx** out) {
+  if (!out) return fail(TESSA_ERR_INVALID_ARG, "null output pointer");
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(TESSA_ERR_NO_DEVICE, "no CUDA device");
+  if (device < 0 || device >= n) return fail(TESSA_ERR_INVALID_ARG, "device %d outside 0..%d", device, n - 1);
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(TESSA_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", device, prop.major,
+                prop.minor);
+  tessa_ctx* ctx = new (std::nothrow) tessa_ctx();
+  if (!ctx) return fail(TESSA_ERR_OOM, "context allocation failed");
+  ctx->device = device;
+  ctx->sm_count = prop.multiProcessorCount;
+  int r = bind(ctx);
+  if (r == TESSA_OK) {
+    if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) r = fail(TESSA_ERR_CUDA, "stream create failed");
+  }
+  if (r == TESSA_OK) r = ctx->d_err.ensure(4);
+  if (r != TESSA_OK) {
+    tessa_destroy(ctx);
+    return r;
+  }
+  *out = ctx;
+  return TESSA_OK;
+}
+
+void tessa_destroy(tessa_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  ctx->d_err.release();
+  ctx->gather.release();
+  ctx->leaf_plan.release();
+  ctx->assign_plan.release();
+  DevBuf* bufs[] = {&ctx->h_codes, &ctx->h_scales, &ctx->h_norms, &ctx->h_gids, &ctx->h_members,
+                    &ctx->h_ids, &ctx->h_dists, &ctx->h_x};
+  for (DevBuf* b : bufs) b->release();
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+int tessa_ctx_device(const tessa_ctx* ctx) { return ctx ? ctx->device : -1; }
+
+int tessa_quantize_sq8(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t dim, uint32_t k_align, uint32_t bits,
+                       int8_t* codes, float* scales, float* norms, void* stream) {
+  TRY(bind(ctx));
+  if (bits < 2 || bits > 8) return fail(TESSA_ERR_INVALID_ARG, "SQ-int8 bits=%u outside 2..8", bits);
+  if (dim == 0) return fail(TESSA_ERR_INVALID_ARG, "SQ-int8 quantization requires dim > 0");
+  if (k_align == 0) k_align = 1;
+  uint64_t padded = ((uint64_t)dim + k_align - 1) / k_align * k_align;
+  if (padded % 16 != 0 || padded > 0xffffffffull)
+    return fail(TESSA_ERR_UNSUPPORTED, "padded_dim=%llu must be a multiple of 16", (unsigned long long)padded);
+  if (rows && (!x || !codes || !scales || !norms)) return fail(TESSA_ERR_INVALID_ARG, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  TRY(clear_err(ctx, st));
+  TRY(launch_quantize_sq8(x, rows, dim, (uint32_t)padded, bits, codes, scales, norms, ctx->d_err.as<uint32_t>(), st));
+  uint32_t b = 0;
+  TRY(read_err(ctx, st, &b));
+  return map_device_error(b);
+}
+
+int tessa_quantize_sq8_host(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t dim, uint32_t k_align,
+                            uint32_t bits, int8_t* codes, float* scales, float* norms) {
+  TRY(bind(ctx));
+  if (dim == 0) return fail(TESSA_ERR_INVALID_ARG, "SQ-int8 quantization requires dim > 0");
+  uint32_t ka = k_align ? k_align : 1;
+  uint64_t padded = ((uint64_t)dim + ka - 1) / ka * ka;
+  cudaStream_t st = ctx->stream;
+  TRY(ctx->h_x.ensure(rows * dim * 4 + 4));
+  TRY(ctx->h_codes.ensure(rows * padded + 16));
+  TRY(ctx->h_scales.ensure(rows * 4 + 4));
+  TRY(ctx->h_norms.ensure(rows * 4 + 4));
+  if (rows) CUDA_TRY(cudaMemcpyAsync(ctx->h_x.ptr, x, rows * dim * 4, cudaMemcpyHostToDevice, st));
+  TRY(tessa_quantize_sq8(ctx, ctx->h_x.as<float>(), rows, dim, k_align, bits, ctx->h_codes.as<int8_t>(),
+                         ctx->h_scales.as<float>(), ctx->h_norms.as<float>(), st));
+  if (rows) {
+    CUDA_TRY(cudaMemcpyAsync(codes, ctx->h_codes.ptr, rows * padded, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(scales, ctx->h_scales.ptr, rows * 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(norms, ctx->h_norms.ptr, rows * 4, cudaMemcpyDeviceToHost, st));
+  }
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return TESSA_OK;
+}
+
+int tessa_leaf_topk_sq8(tessa_ctx* ctx, const tessa_leaf_args* args, void* stream) {
+  TRY(bind(ctx));
+  TRY(validate_leaf(args));
+  return leaf_device(ctx, args, (cudaStream_t)stream);
+}
+
+int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* a) {
+  TRY(bind(ctx));
+  TRY(validate_leaf(a));
+  for (uint64_t i = 0; i < a->leaf_rows; ++i)
+    if (a->leaf_members[i] >= a->resident_rows)
+      return fail(TESSA_ERR_BAD_ROW, "leaf member %llu = %u outside %llu resident rows", (unsigned long long)i,
+                  a->leaf_members[i], (unsigned long long)a->resident_rows);
+  cudaStream_t st = ctx->stream;
+  const uint64_t R = a->resident_rows, M = a->leaf_rows, P = a->padded_dim;
+  bool ident = (M <= R) && members_identity(a->leaf_members, M);
+  TRY(ctx->h_codes.ensure(R * P + 16));
+  TRY(ctx->h_scales.ensure(R * 4 + 4));
+  TRY(ctx->h_norms.ensure(R * 4 + 4));
+  TRY(ctx->h_gids.ensure(R * 4 + 4));
+  TRY(ctx->h_members.ensure(M * 4 + 4));
+  TRY(ctx->h_ids.ensure(M * a->k * 4 + 4));
+  TRY(ctx->h_dists.ensure(M * a->k * 4 + 4));
+  if (R) {
+    CUDA_TRY(cudaMemcpyAsync(ctx->h_codes.ptr, a->codes, R * P, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(ctx->h_scales.ptr, a->scales, R * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(ctx->h_norms.ptr, a->norms, R * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(ctx->h_gids.ptr, a->global_ids, R * 4, cudaMemcpyHostToDevice, st));
+  }
+  if (M) CUDA_TRY(cudaMemcpyAsync(ctx->h_members.ptr, a->leaf_members, M * 4, cudaMemcpyHostToDevice, st));
+  tessa_leaf_args d = *a;
+  d.codes = ctx->h_codes.as<int8_t>();
+  d.scales = ctx->h_scales.as<float>();
+  d.norms = ctx->h_norms.as<float>();
+  d.global_ids = ctx->h_gids.as<uint32_t>();
+  d.leaf_members = ctx->h_members.as<uint32_t>();
+  d.topk_ids = ctx->h_ids.as<uint32_t>();
+  d.topk_dists = ctx->h_dists.as<float>();
+  d.leaf_ordered_codes = ident ? d.codes : nullptr;
+  TRY(leaf_device(ctx, &d, st));
+  if (M) {
+    CUDA_TRY(cudaMemcpyAsync(a->topk_ids, ctx->h_ids.ptr, M * a->k * 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(a->topk_dists, ctx->h_dists.ptr, M * a->k * 4, cudaMemcpyDeviceToHost, st));
+  }
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return TESSA_OK;
+}
+
+int tessa_assign(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* args, void* stream) {
+  TRY(bind(ctx));
+  return assign_device(ctx, source, args, (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ replay session
+
+struct tessa_replay_session {
+  tessa_ctx* ctx = nullptr;
+  uint32_t dim = 0, padded_dim = 0, leaf_k = 0;
+  uint64_t resident_rows = 0, leaf_rows = 0, assign_out_len = 0;
+  DevBuf gids, x, raw_norms, codes, scales, sq8_norms, amembers, aleaders, lmembers, aids, adists, lids, ldists;
+  bool leaf_identity = false;
+  std::vector<uint32_t> t_moff, t_mcnt, t_loff, t_lcnt, t_rh;
+  std::vector<uint64_t> t_out, leaf_starts, leaf_sizes;
+  uint64_t amember_rows = 0;
+  cudaEvent_t ev[6] = {};
+};
+
+namespace {
+
+template <class T>
+int upload(DevBuf& b, const T* h, uint64_t n, cudaStream_t st) {
+  TRY(b.ensure(n * sizeof(T) + 16));
+  if (n) CUDA_TRY(cudaMemcpyAsync(b.ptr, h, n * sizeof(T), cudaMemcpyHostToDevice, st));
+  return TESSA_OK;
+}
+
+bool mode_uses_sq8(uint32_t m) { return m >= TESSA_MODE_A2_SQ8_DP4A_BATCH1; }
+bool mode_replays_leaf(uint32_t m) { return m <= TESSA_MODE_A3_SQ8_WMMA_BATCH8; }
+
+}  // namespace
+
+extern "C" {
+
+int tessa_replay_session_create(int device, const tessa_prepared_replay* p, tessa_replay_session** out) {
+  if (!out || !p) return fail(TESSA_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (p->resident_rows == 0 || p->task_count == 0 || p->leaf_count == 0)
+    return fail(TESSA_ERR_INVALID_ARG, "prepared replay tasks must be non-empty");
+  tessa_ctx* ctx = nullptr;
+  TRY(tessa_create(device, &ctx));
+  tessa_replay_session* s = new (std::nothrow) tessa_replay_session();
+  if (!s) {
+    tessa_destroy(ctx);
+    return fail(TESSA_ERR_OOM, "session allocation failed");
+  }
+  s->ctx = ctx;
+  auto cleanup = [&](int r) {
+    tessa_replay_session_destroy(s);
+    return r;
+  };
+  cudaStream_t st = ctx->stream;
+  s->dim = p->dim;
+  s->padded_dim = p->padded_dim;
+  s->leaf_k = p->leaf_k;
+  s->resident_rows = p->resident_rows;
+  s->leaf_rows = p->leaf_rows;
+  s->assign_out_len = p->assignment_output_len;
+  s->amember_rows = p->assignment_member_rows;
+  int r;
+  if ((r = upload(s->gids, p->global_ids, p->resident_rows, st)) ||
+      (r = upload(s->x, p->vectors, p->resident_rows * p->dim, st)) ||
+      (r = upload(s->raw_norms, p->raw_norms, p->resident_rows, st)) ||
+      (r = upload(s->codes, p->sq8_codes, p->resident_rows * p->padded_dim, st)) ||
+      (r = upload(s->scales, p->sq8_scales, p->resident_rows, st)) ||
+      (r = upload(s->sq8_norms, p->sq8_norms, p->resident_rows, st)) ||
+      (r = upload(s->amembers, p->assignment_members, p->assignment_member_rows, st)) ||
+      (r = upload(s->aleaders, p->assignment_leaders, p->assignment_leader_rows, st)) ||
+      (r = upload(s->lmembers, p->leaf_members, p->leaf_rows, st)))
+    return cleanup(r);
+  if ((r = s->aids.ensure(p->assignment_output_len * 4 + 4)) || (r = s->adists.ensure(p->assignment_output_len * 4 + 4)) ||
+      (r = s->lids.ensure(p->leaf_rows * p->leaf_k * 4 + 4)) || (r = s->ldists.ensure(p->leaf_rows * p->leaf_k * 4 + 4)))
+    return cleanup(r);
+  for (uint64_t i = 0; i < p->leaf_rows; ++i)
+    if (p->leaf_members[i] >= p->resident_rows) return cleanup(fail(TESSA_ERR_BAD_ROW, "leaf member outside resident rows"));
+  for (uint64_t i = 0; i < p->assignment_member_rows; ++i)
+    if (p->assignment_members[i] >= p->resident_rows) return cleanup(fail(TESSA_ERR_BAD_ROW, "assignment member outside resident rows"));
+  for (uint64_t i = 0; i < p->assignment_leader_rows; ++i)
+    if (p->assignment_leaders[i] >= p->resident_rows) return cleanup(fail(TESSA_ERR_BAD_ROW, "assignment leader outside resident rows"));
+  s->leaf_identity = p->leaf_rows <= p->resident_rows && members_identity(p->leaf_members, p->leaf_rows);
+  s->t_moff.assign(p->task_member_offsets, p->task_member_offsets + p->task_count);
+  s->t_mcnt.assign(p->task_member_counts, p->task_member_counts + p->task_count);
+  s->t_loff.assign(p->task_leader_offsets, p->task_leader_offsets + p->task_count);
+  s->t_lcnt.assign(p->task_leader_counts, p->task_leader_counts + p->task_count);
+  s->t_rh.assign(p->task_rh, p->task_rh + p->task_count);
+  s->t_out.assign(p->task_output_offsets, p->task_output_offsets + p->task_count);
+  s->leaf_starts.assign(p->leaf_starts, p->leaf_starts + p->leaf_count);
+  s->leaf_sizes.assign(p->leaf_sizes, p->leaf_sizes + p->leaf_count);
+  for (auto& e : s->ev)
+    if (cudaEventCreate(&e) != cudaSuccess) return cleanup(fail(TESSA_ERR_CUDA, "event create failed"));
+  if (cudaStreamSynchronize(st) != cudaSuccess) return cleanup(fail(TESSA_ERR_CUDA, "upload failed"));
+  *out = s;
+  return TESSA_OK;
+}
+
+int tessa_replay_run_mode(tessa_replay_session* s, uint32_t mode, tessa_mode_result* res) {
+  if (!s || !res) return fail(TESSA_ERR_INVALID_ARG, "null argument");
+  if (mode > TESSA_MODE_SQ8_WMMA_BATCH1) return fail(TESSA_ERR_INVALID_ARG, "unknown replay mode %u", mode);
+  if (mode_replays_leaf(mode) && !mode_uses_sq8(mode))
+    return fail(TESSA_ERR_UNSUPPORTED,
+                "mode %u replays raw FP32/TF32 leaf tasks; only the SQ8 leaf operator is built (use modes 2-5)", mode);
+  tessa_ctx* ctx = s->ctx;
+  TRY(bind(ctx));
+  cudaStream_t st = ctx->stream;
+  // clear outputs as run_mode does (CB:34849-34889): ids 0xffffffff, dists FLT_MAX
+  std::vector<uint32_t> fill_id(1, 0xffffffffu);
+  CUDA_TRY(cudaMemsetAsync(s->aids.ptr, 0xff, s->assign_out_len * 4, st));
+  {
+    std::vector<float> fmax(s->assign_out_len, 3.402823466e+38F);
+    if (!fmax.empty()) CUDA_TRY(cudaMemcpyAsync(s->adists.ptr, fmax.data(), fmax.size() * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+  }
+  bool leaf = mode_replays_leaf(mode);
+  if (leaf) {
+    CUDA_TRY(cudaMemsetAsync(s->lids.ptr, 0xff, s->leaf_rows * s->leaf_k * 4, st));
+    std::vector<float> fmax(s->leaf_rows * s->leaf_k, 3.402823466e+38F);
+    if (!fmax.empty()) CUDA_TRY(cudaMemcpyAsync(s->ldists.ptr, fmax.data(), fmax.size() * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+  }
+  tessa_assign_args aa;
+  memset(&aa, 0, sizeof(aa));
+  aa.x = s->x.as<float>();
+  aa.raw_norms = s->raw_norms.as<float>();
+  aa.codes = s->codes.as<int8_t>();
+  aa.scales = s->scales.as<float>();
+  aa.sq8_norms = s->sq8_norms.as<float>();
+  aa.global_ids = s->gids.as<uint32_t>();
+  aa.resident_rows = s->resident_rows;
+  aa.dim = s->dim;
+  aa.padded_dim = s->padded_dim;
+  aa.members = s->amembers.as<uint32_t>();
+  aa.leaders = s->aleaders.as<uint32_t>();
+  aa.task_member_offsets = s->t_moff.data();
+  aa.task_member_counts = s->t_mcnt.data();
+  aa.task_leader_offsets = s->t_loff.data();
+  aa.task_leader_counts = s->t_lcnt.data();
+  aa.task_rh = s->t_rh.data();
+  aa.task_output_offsets = s->t_out.data();
+  aa.task_count = (uint32_t)s->t_moff.size();
+  aa.member_rows = s->amember_rows;
+  aa.out_ids = s->aids.as<uint32_t>();
+  aa.out_dists = s->adists.as<float>();
+  uint64_t err_bits = 0;
+  CUDA_TRY(cudaEventRecord(s->ev[0], st));
+  CUDA_TRY(cudaEventRecord(s->ev[1], st));
+  int r = assign_device(ctx, mode_uses_sq8(mode) ? TESSA_ASSIGN_SQ8 : TESSA_ASSIGN_FP32, &aa, st);
+  if (r == TESSA_ERR_TIMEOUT || r == TESSA_ERR_BAD_ROW || r == TESSA_ERR_BAD_TASK) err_bits |= 1;
+  TRY(r);
+  CUDA_TRY(cudaEventRecord(s->ev[2], st));
+  if (leaf) {
+    CUDA_TRY(cudaEventRecord(s->ev[3], st));
+    tessa_leaf_args la;
+    memset(&la, 0, sizeof(la));
+    la.codes = s->codes.as<int8_t>();
+    la.scales = s->scales.as<float>();
+    la.norms = s->sq8_norms.as<float>();
+    la.global_ids = s->gids.as<uint32_t>();
+    la.resident_rows = s->resident_rows;
+    la.padded_dim = s->padded_dim;
+    la.k = s->leaf_k;
+    la.leaf_members = s->lmembers.as<uint32_t>();
+    la.leaf_starts = s->leaf_starts.data();
+    la.leaf_sizes = s->leaf_sizes.data();
+    la.leaf_count = s->leaf_starts.size();
+    la.leaf_rows = s->leaf_rows;
+    la.topk_ids = s->lids.as<uint32_t>();
+    la.topk_dists = s->ldists.as<float>();
+    la.leaf_ordered_codes = s->leaf_identity ? la.codes : nullptr;
+    TRY(validate_leaf(&la));
+    TRY(leaf_device(ctx, &la, st));
+    CUDA_TRY(cudaEventRecord(s->ev[4], st));
+  }
+  CUDA_TRY(cudaEventRecord(s->ev[5], st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  float ms = 0;
+  CUDA_TRY(cudaEventElapsedTime(&ms, s->ev[1], s->ev[2]));
+  res->assignment_event_ms = ms;
+  if (leaf) {
+    CUDA_TRY(cudaEventElapsedTime(&ms, s->ev[3], s->ev[4]));
+    res->leaf_event_ms = ms;
+  } else {
+    res->leaf_event_ms = -1.0;
+  }
+  CUDA_TRY(cudaEventElapsedTime(&ms, s->ev[0], s->ev[5]));
+  res->total_event_ms = ms;
+  res->device_error_bits = err_bits;
+  if (res->assignment_ids && s->assign_out_len)
+    CUDA_TRY(cudaMemcpyAsync(res->assignment_ids, s->aids.ptr, s->assign_out_len * 4, cudaMemcpyDeviceToHost, st));
+  if (res->assignment_dists && s->assign_out_len)
+    CUDA_TRY(cudaMemcpyAsync(res->assignment_dists, s->adists.ptr, s->assign_out_len * 4, cudaMemcpyDeviceToHost, st));
+  if (leaf && res->leaf_ids)
+    CUDA_TRY(cudaMemcpyAsync(res->leaf_ids, s->lids.ptr, s->leaf_rows * s->leaf_k * 4, cudaMemcpyDeviceToHost, st));
+  if (leaf && res->leaf_dists)
+    CUDA_TRY(cudaMemcpyAsync(res->leaf_dists, s->ldists.ptr, s->leaf_rows * s->leaf_k * 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return TESSA_OK;
+}
+
+void tessa_replay_session_destroy(tessa_replay_session* s) {
+  if (!s) return;
+  if (s->ctx) {
+    cudaSetDevice(s->ctx->device);
+    cudaStreamSynchronize(s->ctx->stream);
+  }
+  for (auto& e : s->ev)
+    if (e) cudaEventDestroy(e);
+  DevBuf* bufs[] = {&s->gids, &s->x, &s->raw_norms, &s->codes, &s->scales, &s->sq8_norms, &s->amembers,
+                    &s->aleaders, &s->lmembers, &s->aids, &s->adists, &s->lids, &s->ldists};
+  for (DevBuf* b : bufs) b->release();
+  tessa_destroy(s->ctx);
+  delete s;
+}
+
+}  // extern "C"

@@ -1,0 +1,66 @@
+// Host-visible launch descriptors and launchers of the TESSA sm_100a kernels
+// (defined in leaf_sq8.cu, quantize_sq8.cu and assign.cu, called by capi.cu).
+#pragma once
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+namespace tessa {
+
+struct LeafLaunch {
+  const int8_t* leaf_codes;   // leaf-ordered codes (row p = member p)
+  uint64_t leaf_rows;
+  uint32_t padded_dim;
+  const float* scales;        // by local id
+  const float* norms;
+  const uint32_t* global_ids;
+  const uint32_t* members;    // leaf-ordered local ids
+  const uint64_t* d_leaf_starts;
+  const uint32_t* d_leaf_sizes;
+  const uint2* d_tiles;       // (leaf, first row) per 128-row tile
+  uint32_t num_tiles;
+  uint32_t k;
+  uint32_t* out_ids;
+  float* out_dists;
+  uint32_t* d_err;
+  uint64_t timeout_ns;
+  int sm_count;
+};
+
+int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream);
+int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes, int8_t* dst,
+                       int sm_count, cudaStream_t stream);
+int leaf_num_bstages(uint32_t padded_dim);
+int launch_quantize_sq8(const float* x, uint64_t rows, uint32_t dim, uint32_t padded, uint32_t bits, int8_t* codes,
+                        float* scales, float* norms, uint32_t* d_err, cudaStream_t stream);
+
+namespace assign {
+struct Params {
+  const float* x;
+  const float* raw_norms;
+  const int8_t* codes;
+  const float* scales;
+  const float* sq8_norms;
+  const uint32_t* global_ids;
+  uint64_t resident_rows;
+  uint32_t dim;
+  uint32_t padded_dim;
+  const uint32_t* members;
+  const uint32_t* leaders;
+  const uint32_t* t_moff;
+  const uint32_t* t_mcnt;
+  const uint32_t* t_loff;
+  const uint32_t* t_lcnt;
+  const uint32_t* t_rh;
+  const uint64_t* t_out;
+  const uint2* work;          // (task, first row) per 128-row work item
+  uint32_t num_work;
+  uint32_t fused;             // SQ8 distance as one FFMA (1) or one rounding per op (0)
+  uint32_t* out_ids;
+  float* out_dists;
+  uint32_t* err_word;
+};
+}  // namespace assign
+
+int launch_assign(const assign::Params& prm, bool sq8, cudaStream_t stream);
+
+}  // namespace tessa

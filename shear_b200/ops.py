@@ -1,0 +1,223 @@
+"""Device-tensor and host-buffer entry points over the C ABI.
+
+Device forms take CUDA tensors (torch is used only for device memory and
+streams) and run on the tensors' current stream.  Host forms take numpy arrays
+and are the reference-facing calls: they copy in, run and copy out inside the
+call, like the compute-backend trait method they replace
+(``PiPNNComputeBackend::process_quantized_subtree_l2_compact_topk``,
+shear-core/src/algorithm/pipnn/compute_backend.rs:3693-3884).
+
+uint32 data (ids) travel in torch as int32 tensors with the same bit pattern;
+``as_u32`` turns them back into numpy uint32.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import numpy as np
+
+from . import _capi as C
+
+_tls = threading.local()
+
+
+class Context:
+    """One library context (one device, one host thread)."""
+
+    def __init__(self, device: int = 0):
+        lib = C.load()
+        h = ctypes.c_void_p()
+        C.check(lib.tessa_create(int(device), ctypes.byref(h)))
+        self.handle = h
+        self.device = int(device)
+
+    def close(self) -> None:
+        if self.handle:
+            C.load().tessa_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def context(device: int = 0) -> Context:
+    cache = getattr(_tls, "ctx", None)
+    if cache is None:
+        cache = _tls.ctx = {}
+    if device not in cache:
+        cache[device] = Context(device)
+    return cache[device]
+
+
+def _stream_ptr(torch, device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p()
+
+
+def _np_ptr(a):
+    return ctypes.c_void_p(a.ctypes.data) if a is not None else ctypes.c_void_p()
+
+
+def as_u32(t) -> np.ndarray:
+    """int32 torch tensor (or numpy) holding uint32 bits -> numpy uint32."""
+    a = t.detach().cpu().numpy() if hasattr(t, "detach") else np.asarray(t)
+    return a.view(np.uint32)
+
+
+def padded_dim(dim: int, k_align: int = 16) -> int:
+    """P/dco_sq_int8.rs:1216-1224 sq_int8_padded_dim."""
+    if dim <= 0:
+        raise ValueError("SQ-int8 quantization requires dim > 0")
+    k_align = max(1, int(k_align))
+    return (dim + k_align - 1) // k_align * k_align
+
+
+# ----------------------------------------------------------------- SQ8 quant
+
+def quantize_sq8(x, k_align: int = 16, bits: int = 8, ctx: Context | None = None):
+    """GPU quantize_sq_int8_matrix_with_bits (P/dco_sq_int8.rs:1331-1375).
+
+    x: CUDA float32 tensor [rows, dim].  Returns (codes int8 [rows, padded],
+    scales f32 [rows], norms f32 [rows]) on the same device, bit-exact with the
+    reference CPU quantizer.
+    """
+    import torch
+
+    if not x.is_cuda or x.dtype != torch.float32 or x.dim() != 2:
+        raise ValueError("x must be a 2-D float32 CUDA tensor")
+    x = x.contiguous()
+    rows, dim = x.shape
+    dev = x.device.index
+    ctx = ctx or context(dev)
+    pd = padded_dim(dim, k_align)
+    codes = torch.empty((rows, pd), dtype=torch.int8, device=x.device)
+    scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+    norms = torch.empty(rows, dtype=torch.float32, device=x.device)
+    C.check(C.load().tessa_quantize_sq8(ctx.handle, _ptr(x), rows, dim, k_align, bits, _ptr(codes),
+                                        _ptr(scales), _ptr(norms), _stream_ptr(torch, dev)))
+    return codes, scales, norms
+
+
+def quantize_sq8_host(x: np.ndarray, k_align: int = 16, bits: int = 8, device: int = 0):
+    """Host-buffer form of :func:`quantize_sq8` (numpy in, numpy out)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, dim = x.shape
+    pd = padded_dim(dim, k_align)
+    codes = np.zeros((rows, pd), dtype=np.int8)
+    scales = np.zeros(rows, dtype=np.float32)
+    norms = np.zeros(rows, dtype=np.float32)
+    C.check(C.load().tessa_quantize_sq8_host(context(device).handle, _np_ptr(x), rows, dim, k_align, bits,
+                                             _np_ptr(codes), _np_ptr(scales), _np_ptr(norms)))
+    return codes, scales, norms
+
+
+# -------------------------------------------------------------- leaf top-k
+
+def _layout(leaf_starts, leaf_sizes):
+    starts = np.ascontiguousarray(leaf_starts, dtype=np.uint64)
+    sizes = np.ascontiguousarray(leaf_sizes, dtype=np.uint64)
+    if starts.shape != sizes.shape or starts.ndim != 1:
+        raise ValueError("leaf_starts and leaf_sizes must be 1-D and of equal length")
+    return starts, sizes
+
+
+def leaf_topk_sq8(codes, scales, norms, global_ids, leaf_members, leaf_starts, leaf_sizes, k: int,
+                  leaf_ordered_codes=None, out=None, ctx: Context | None = None):
+    """Fused SQ8 leaf top-k on device tensors (see tessa_leaf_topk_sq8).
+
+    codes int8 [resident_rows, padded_dim]; scales / norms f32 and global_ids
+    int32(uint32 bits) [resident_rows]; leaf_members int32(uint32) [leaf_rows];
+    leaf_starts / leaf_sizes host sequences.  Returns (ids int32-bits,
+    dists f32), each [leaf_rows * k].
+    """
+    import torch
+
+    starts, sizes = _layout(leaf_starts, leaf_sizes)
+    dev = codes.device.index
+    ctx = ctx or context(dev)
+    leaf_rows = int(leaf_members.numel())
+    if out is None:
+        ids = torch.empty(leaf_rows * k, dtype=torch.int32, device=codes.device)
+        dists = torch.empty(leaf_rows * k, dtype=torch.float32, device=codes.device)
+    else:
+        ids, dists = out
+    a = C.LeafArgs(codes=codes.data_ptr(), scales=scales.data_ptr(), norms=norms.data_ptr(),
+                   global_ids=global_ids.data_ptr(), resident_rows=codes.shape[0],
+                   padded_dim=codes.shape[1], k=k, leaf_members=leaf_members.data_ptr(),
+                   leaf_starts=starts.ctypes.data, leaf_sizes=sizes.ctypes.data,
+                   leaf_count=starts.shape[0], leaf_rows=leaf_rows, topk_ids=ids.data_ptr(),
+                   topk_dists=dists.data_ptr(),
+                   leaf_ordered_codes=leaf_ordered_codes.data_ptr() if leaf_ordered_codes is not None else None)
+    C.check(C.load().tessa_leaf_topk_sq8(ctx.handle, ctypes.byref(a), _stream_ptr(torch, dev)))
+    return ids, dists
+
+
+def leaf_topk_sq8_host(codes, scales, norms, global_ids, leaf_members, leaf_starts, leaf_sizes, k: int,
+                       device: int = 0, out=None):
+    """Host-buffer form: numpy arrays in, numpy (ids uint32, dists f32) out.
+
+    Pinned host arrays (e.g. ``torch.empty(..., pin_memory=True).numpy()``)
+    make the copies inside the call run at full link speed.
+    """
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    scales = np.ascontiguousarray(scales, dtype=np.float32)
+    norms = np.ascontiguousarray(norms, dtype=np.float32)
+    gids = np.ascontiguousarray(global_ids, dtype=np.uint32)
+    members = np.ascontiguousarray(leaf_members, dtype=np.uint32)
+    starts, sizes = _layout(leaf_starts, leaf_sizes)
+    n = members.shape[0] * k
+    if out is None:
+        ids = np.empty(n, dtype=np.uint32)
+        dists = np.empty(n, dtype=np.float32)
+    else:
+        ids, dists = out
+    a = C.LeafArgs(codes=codes.ctypes.data, scales=scales.ctypes.data, norms=norms.ctypes.data,
+                   global_ids=gids.ctypes.data, resident_rows=codes.shape[0], padded_dim=codes.shape[1],
+                   k=k, leaf_members=members.ctypes.data, leaf_starts=starts.ctypes.data,
+                   leaf_sizes=sizes.ctypes.data, leaf_count=starts.shape[0], leaf_rows=members.shape[0],
+                   topk_ids=ids.ctypes.data, topk_dists=dists.ctypes.data, leaf_ordered_codes=None)
+    C.check(C.load().tessa_leaf_topk_sq8_host(context(device).handle, ctypes.byref(a)))
+    return ids, dists
+
+
+# -------------------------------------------------------------- assignment
+
+def assign(source: int, *, x=None, raw_norms=None, codes=None, scales=None, sq8_norms=None, global_ids,
+           members, leaders, task_member_offsets, task_member_counts, task_leader_offsets,
+           task_leader_counts, task_rh, task_output_offsets, output_len: int, ctx: Context | None = None):
+    """Assignment replay (tessa_assign) on device tensors; task arrays are host sequences.
+
+    source: ``ASSIGN_FP32`` (x, raw_norms) or ``ASSIGN_SQ8`` (codes, scales,
+    sq8_norms).  Returns (ids int32-bits, dists f32) of output_len entries.
+    """
+    import torch
+
+    dev = global_ids.device.index
+    ctx = ctx or context(dev)
+    u32 = lambda v: np.ascontiguousarray(v, dtype=np.uint32)
+    moff, mcnt, loff, lcnt, rh = (u32(task_member_offsets), u32(task_member_counts),
+                                  u32(task_leader_offsets), u32(task_leader_counts), u32(task_rh))
+    outoff = np.ascontiguousarray(task_output_offsets, dtype=np.uint64)
+    ids = torch.full((output_len,), -1, dtype=torch.int32, device=global_ids.device)
+    dists = torch.full((output_len,), 3.402823466e38, dtype=torch.float32, device=global_ids.device)
+    ref = x if x is not None else codes
+    a = C.AssignArgs(x=_ptr(x).value, raw_norms=_ptr(raw_norms).value, codes=_ptr(codes).value,
+                     scales=_ptr(scales).value, sq8_norms=_ptr(sq8_norms).value,
+                     global_ids=global_ids.data_ptr(), resident_rows=ref.shape[0],
+                     dim=x.shape[1] if x is not None else 0,
+                     padded_dim=codes.shape[1] if codes is not None else 0,
+                     members=members.data_ptr(), leaders=leaders.data_ptr(),
+                     task_member_offsets=moff.ctypes.data, task_member_counts=mcnt.ctypes.data,
+                     task_leader_offsets=loff.ctypes.data, task_leader_counts=lcnt.ctypes.data,
+                     task_rh=rh.ctypes.data, task_output_offsets=outoff.ctypes.data,
+                     task_count=moff.shape[0], member_rows=int(members.numel()),
+                     out_ids=ids.data_ptr(), out_dists=dists.data_ptr())
+    C.check(C.load().tessa_assign(ctx.handle, int(source), ctypes.byref(a), _stream_ptr(torch, dev)))
+    return ids, dists

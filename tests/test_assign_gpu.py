@@ -1,0 +1,59 @@
+"""TESSA assignment replay on the B200 vs the oracle.
+
+FP32: bit-exact with the reference's FP32 SIMT executor order.  SQ8: bit-exact
+with the contracted (single FFMA) form of CB:14676-14678; ids equal to the
+uncontracted form except where two leaders are within the 2e-5 tie window.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _tasks(rng, rows, ntasks):
+    moff, mcnt, loff, lcnt, rh, out = [], [], [], [], [], []
+    members, leaders = [], []
+    o = 0
+    for t in range(ntasks):
+        m = int(rng.integers(1, 300))
+        l = int(rng.integers(1, 100))
+        r = int(rng.integers(1, min(4, l) + 1))
+        moff.append(len(members)); mcnt.append(m)
+        loff.append(len(leaders)); lcnt.append(l)
+        rh.append(r); out.append(o)
+        members += rng.integers(0, rows, m).tolist()
+        leaders += rng.choice(rows, l, replace=False).tolist()
+        o += m * r
+    return (np.array(members, np.uint32), np.array(leaders, np.uint32), moff, mcnt, loff, lcnt, rh,
+            np.array(out, np.uint64), o)
+
+
+@pytest.mark.parametrize("dim", [20, 128, 768])
+def test_assignment_fp32_and_sq8_match_oracle(oracle, dim):
+    import torch
+    from shear_b200 import ops
+    from shear_b200._capi import ASSIGN_FP32, ASSIGN_SQ8
+    rng = np.random.default_rng(dim)
+    rows = 2000
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    x[7] = x[6]
+    raw = oracle.raw_norms(x)
+    codes, scales, qn = oracle.quantize_sq8(x)
+    gids = rng.permutation(10 * rows)[:rows].astype(np.uint32)
+    members, leaders, moff, mcnt, loff, lcnt, rh, out, n = _tasks(rng, rows, 6)
+    dv = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    common = dict(global_ids=dv(gids.view(np.int32)), members=dv(members.view(np.int32)),
+                  leaders=dv(leaders.view(np.int32)), task_member_offsets=moff, task_member_counts=mcnt,
+                  task_leader_offsets=loff, task_leader_counts=lcnt, task_rh=rh, task_output_offsets=out,
+                  output_len=n)
+    ids, d = ops.assign(ASSIGN_FP32, x=dv(x), raw_norms=dv(raw), **common)
+    wi, wd = oracle.assign(0, x, raw, codes, scales, gids, members, leaders, moff, mcnt, loff, lcnt, rh, out, n)
+    assert np.array_equal(ops.as_u32(ids), wi)
+    assert np.array_equal(d.cpu().numpy().view(np.uint32), wd.view(np.uint32))
+    ids, d = ops.assign(ASSIGN_SQ8, codes=dv(codes), scales=dv(scales), sq8_norms=dv(qn), **common)
+    wi, wd = oracle.assign(3, x, qn, codes, scales, gids, members, leaders, moff, mcnt, loff, lcnt, rh, out, n)
+    assert np.array_equal(ops.as_u32(ids), wi)
+    assert np.array_equal(d.cpu().numpy().view(np.uint32), wd.view(np.uint32))
+    ui, ud = oracle.assign(2, x, qn, codes, scales, gids, members, leaders, moff, mcnt, loff, lcnt, rh, out, n)
+    # the uncontracted form differs by at most a few ulp
+    assert np.allclose(d.cpu().numpy(), ud, rtol=1e-6, atol=1e-6)

@@ -1,0 +1,130 @@
+"""SQ8 leaf top-k on the B200 (tcgen05 kernel through the C ABI) vs the oracle.
+
+Bit-exact: ids equal and distance bits equal for every output slot.
+"""
+import numpy as np
+import pytest
+
+from leafcases import make_leaf_batch, oracle_leaf
+
+pytestmark = pytest.mark.gpu
+
+
+def _device_run(c, k, leaf_ordered=False):
+    import torch
+    from shear_b200 import ops
+    dev = torch.device("cuda:0")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    codes = t(c["codes"])
+    lo = None
+    if leaf_ordered:
+        lo = t(c["codes"][c["members"].astype(np.int64)])
+    ids, dists = ops.leaf_topk_sq8(codes, t(c["scales"]), t(c["norms"]), t(c["gids"].view(np.int32)),
+                                   t(c["members"].view(np.int32)), c["starts"], c["sizes"], k,
+                                   leaf_ordered_codes=lo)
+    torch.cuda.synchronize()
+    return ops.as_u32(ids), dists.cpu().numpy()
+
+
+def _assert_same(got, want):
+    gi, gd = got
+    wi, wd = want
+    bad = np.nonzero((gi != wi) | (gd.view(np.uint32) != wd.view(np.uint32)))[0]
+    assert bad.size == 0, f"{bad.size} mismatching slots, first at {bad[:5]}: got {gi[bad[:5]]} " \
+                          f"{gd[bad[:5]]} want {wi[bad[:5]]} {wd[bad[:5]]}"
+
+
+CASES = [
+    # (sizes, dim, k, dup, permute)
+    ([2], 16, 1, False, False),
+    ([3, 5], 16, 4, False, False),
+    ([33], 128, 2, True, False),
+    ([128], 128, 32, False, False),
+    ([129], 768, 8, True, True),
+    ([255, 256, 257], 768, 16, False, True),
+    ([1, 300, 2], 100, 4, False, True),
+    ([740, 728, 641], 1024, 2, False, False),
+    ([2048], 768, 32, True, False),
+    ([512, 513], 512, 7, False, True),
+]
+
+
+@pytest.mark.parametrize("sizes,dim,k,dup,permute", CASES)
+def test_leaf_matches_oracle(oracle, sizes, dim, k, dup, permute):
+    c = make_leaf_batch(oracle, sizes, dim, seed=sum(sizes) + dim + k, dup=dup, permute=permute)
+    _assert_same(_device_run(c, k), oracle_leaf(oracle, c, k))
+
+
+def test_leaf_ordered_codes_path_matches_gather_path(oracle):
+    c = make_leaf_batch(oracle, [300, 200], 256, seed=11, permute=True)
+    a = _device_run(c, 8)
+    b = _device_run(c, 8, leaf_ordered=True)
+    _assert_same(a, b)
+    _assert_same(a, oracle_leaf(oracle, c, 8))
+
+
+def test_leaf_host_api_matches_oracle(oracle):
+    from shear_b200 import ops
+    c = make_leaf_batch(oracle, [700, 300], 768, seed=5, dup=True, permute=True)
+    got = ops.leaf_topk_sq8_host(c["codes"], c["scales"], c["norms"], c["gids"], c["members"], c["starts"],
+                                 c["sizes"], 32)
+    _assert_same(got, oracle_leaf(oracle, c, 32))
+
+
+def test_leaf_duplicate_local_ids_are_all_skipped(oracle):
+    # CB:9569-9650 skips every column whose local id equals the row's
+    c = make_leaf_batch(oracle, [40], 64, seed=9)
+    c["members"] = np.array(list(range(20)) + list(range(20)), np.uint32)
+    _assert_same(_device_run(c, 4), oracle_leaf(oracle, c, 4))
+
+
+def test_reference_replay_fixture_607x1024_duplicate_rows(oracle):
+    # P/tessa_replay.rs:1794-1894 input: row 7 duplicates row 6, k = 2
+    def formula(rows, dim):
+        r = np.arange(rows)[:, None]
+        a = np.arange(dim)[None, :]
+        src = np.where(r == 7, 6, r)
+        return (((src * 17 + a * 13) % 97).astype(np.float32) * np.float32(0.03125) - np.float32(1.0))
+    c = make_leaf_batch(oracle, [607], 1024, seed=0, formula=formula)
+    c["gids"] = np.arange(607, dtype=np.uint32)
+    _assert_same(_device_run(c, 2), oracle_leaf(oracle, c, 2))
+
+
+def test_reference_staged_fixture_740_728_641(oracle):
+    # P/tessa_replay.rs:1898-1999 input (staged multi-leaf offsets), k = 2
+    def formula(rows, dim):
+        r = np.arange(rows)[:, None]
+        a = np.arange(dim)[None, :]
+        return (((r * 131 + a * 17 + r * a * 3) % 251).astype(np.float32) * np.float32(0.0078125)
+                - np.float32(0.75))
+    c = make_leaf_batch(oracle, [740, 728, 641], 1024, seed=0, formula=formula)
+    c["gids"] = np.arange(740 + 728 + 641, dtype=np.uint32)
+    want = oracle_leaf(oracle, c, 2)
+    _assert_same(_device_run(c, 2), want)
+    # The staged merge order of the reference gives the same lists here.
+    staged = oracle.leaf_topk_sq8(c["codes"], c["scales"], c["norms"], c["gids"], c["members"], c["starts"],
+                                  c["sizes"], 2, 128)
+    _assert_same(want, staged)
+
+
+def test_leaf_config2_shape_sample(oracle):
+    # 16 leaves of the 4096 x 2048 x 768 k=32 benchmark workload
+    c = make_leaf_batch(oracle, [2048] * 16, 768, seed=2026)
+    _assert_same(_device_run(c, 32), oracle_leaf(oracle, c, 32))
+
+
+def test_leaf_rejects_bad_arguments(oracle):
+    from shear_b200 import ops, TessaError
+    c = make_leaf_batch(oracle, [10], 32, seed=1)
+    for k in (0, 33):
+        with pytest.raises(TessaError, match="INVALID_ARG"):
+            _device_run(c, k)
+    bad = dict(c)
+    bad["members"] = c["members"].copy()
+    bad["members"][3] = 10**6
+    with pytest.raises(TessaError, match="BAD_ROW"):
+        ops.leaf_topk_sq8_host(bad["codes"], bad["scales"], bad["norms"], bad["gids"], bad["members"],
+                               bad["starts"], bad["sizes"], 2)
+    big = make_leaf_batch(oracle, [4], 2048, seed=1)
+    with pytest.raises(TessaError, match="UNSUPPORTED"):
+        _device_run(big, 2)
