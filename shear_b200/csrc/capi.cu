@@ -407,8 +407,7 @@ int tessa_quantize_sq8(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t d
   if (dim == 0) return fail(TESSA_ERR_INVALID_ARG, "SQ-int8 quantization requires dim > 0");
   if (k_align == 0) k_align = 1;
   uint64_t padded = ((uint64_t)dim + k_align - 1) / k_align * k_align;
-  if (padded % 16 != 0 || padded > 0xffffffffull)
-    return fail(TESSA_ERR_UNSUPPORTED, "padded_dim=%llu must be a multiple of 16", (unsigned long long)padded);
+  if (padded > 0xffffffffull) return fail(TESSA_ERR_UNSUPPORTED, "padded_dim=%llu too large", (unsigned long long)padded);
   if (rows && (!x || !codes || !scales || !norms)) return fail(TESSA_ERR_INVALID_ARG, "null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   TRY(clear_err(ctx, st));

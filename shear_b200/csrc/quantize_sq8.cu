@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(kThreads)
   float scale = 1.0f;
   bool zero = (max_abs == 0.0f);
   if (!zero) scale = __fdiv_rn(max_abs, max_code);
-  uint4* out = reinterpret_cast<uint4*>(codes + row * padded);
+  int8_t* orow = codes + row * padded;
   for (uint32_t base = 0; base < padded; base += 16) {
     uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
@@ -48,7 +48,13 @@ __global__ void __launch_bounds__(kThreads)
       }
       w[i >> 2] |= ((uint32_t)(c & 0xff)) << ((i & 3u) * 8u);
     }
-    out[base / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+    if ((padded & 15u) == 0u) {
+      reinterpret_cast<uint4*>(orow)[base / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      // padded_dim need not be a multiple of 16 (any k_align is accepted).
+      for (uint32_t i = 0; i < 16 && base + i < padded; ++i)
+        orow[base + i] = (int8_t)((w[i >> 2] >> ((i & 3u) * 8u)) & 0xffu);
+    }
   }
   scales[row] = scale;
   norms[row] = norm;
