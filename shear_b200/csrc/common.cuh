@@ -77,7 +77,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0u) {
+    // Back off so a waiting thread does not take issue slots from the warps
+    // sharing its scheduler.
+    __nanosleep(spins < 64 ? 32 : 128);
+    if ((++spins & 63u) == 0u) {
       if (*abort_flag) return false;
       if (global_timer_ns() - start > timeout_ns) {
         atomicOr(err_word, TESSA_DEVERR_TIMEOUT);

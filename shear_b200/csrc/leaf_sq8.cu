@@ -130,10 +130,14 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t num_slabs, uint32_t
 template <int KMAX>
 __device__ __forceinline__ void insert_exact(float d, uint32_t id, float (&bd)[KMAX], uint32_t (&bi)[KMAX]) {
   if (!stable_better(d, id, bd[KMAX - 1], bi[KMAX - 1])) return;
+  // Branch-free shift: `run` stays true while the candidate is still moving up.
   bool run = true;
 #pragma unroll
   for (int j = KMAX - 1; j >= 1; --j) {
-    bool b = run && stable_better(d, id, bd[j - 1], bi[j - 1]);
+    float delta = __fsub_rn(d, bd[j - 1]);
+    bool tie = fabsf(delta) <= 2.0e-5f;
+    bool better = (tie & (id < bi[j - 1])) | ((!tie) & (d < bd[j - 1]));
+    bool b = run & better;
     float nd = b ? bd[j - 1] : (run ? d : bd[j]);
     uint32_t ni = b ? bi[j - 1] : (run ? id : bi[j]);
     bd[j] = nd;
@@ -330,6 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0u;
         if (ok) {
           tc_fence_after();
+#pragma unroll 1
           for (uint32_t g = 0; g < kBN / kGroup; ++g) {
             uint32_t v[32];
             tmem_ld_32x32b_x32(tmem_base + ((quad * 32u) << 16) + buf * kBN + g * kGroup, v);
@@ -347,6 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++n_st;
               }
             }
+#pragma unroll 1
             for (uint32_t e = 0; e < n_st; ++e) {
               float d = stash_d[e * 32 + lane];
               uint32_t col = stash_c[e * 32 + lane];
