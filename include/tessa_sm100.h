@@ -144,6 +144,25 @@ TESSA_API int tessa_leaf_topk_sq8(tessa_ctx* ctx, const tessa_leaf_args* args, v
  * process_quantized_subtree_l2_compact_topk (CB:3693-3884) binds. */
 TESSA_API int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* args);
 
+/* Size of the static device scratch of tessa_leaf_topk_sq8_noalloc (64 MiB). */
+#define TESSA_NOALLOC_SCRATCH_BYTES (64u << 20)
+
+/* Allocation-free form of tessa_leaf_topk_sq8 (this entry point has no
+ * counterpart in the reference).  For callers that must not allocate device
+ * memory: hosts whose allocator owns the whole device, latency-critical
+ * threads where cudaMalloc/cudaFree (which can synchronise the device) are not
+ * allowed, embedders that fix their footprint at load time.  Same arguments
+ * and results as tessa_leaf_topk_sq8 (device pointers, HOST leaf layout), on
+ * the current device, but no context: its scratch (tile table, error word and,
+ * when leaf_ordered_codes is NULL, the leaf-ordered copy of the codes) lives in
+ * one static device array of TESSA_NOALLOC_SCRATCH_BYTES that every GPU loading
+ * the library holds until exit.  Batches needing more scratch are rejected
+ * with TESSA_ERR_UNSUPPORTED.  The first call on a device resolves the array's
+ * address (make it before any stream capture).  All calls share the array and
+ * leave their contents in it; calls whose GPU work overlaps race and must be
+ * serialised by the caller.  Returns after the work has completed. */
+TESSA_API int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* args, void* stream);
+
 /* ------------------------------------------------------------ assignment --- */
 
 /* Frozen assignment tasks in the replay layout (TessaAssignmentLayout,

@@ -27,6 +27,7 @@ ERRORS = {
 MAX_LEAF_K = 32
 MAX_RH = 4
 MAX_PADDED_DIM = 1024
+NOALLOC_SCRATCH_BYTES = 64 << 20
 ASSIGN_FP32 = 0
 ASSIGN_SQ8 = 2
 
@@ -105,6 +106,7 @@ SIGNATURES = [
      [c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp]),
     ("tessa_leaf_topk_sq8", ctypes.c_int, [c_vp, ctypes.POINTER(LeafArgs), c_vp]),
     ("tessa_leaf_topk_sq8_host", ctypes.c_int, [c_vp, ctypes.POINTER(LeafArgs)]),
+    ("tessa_leaf_topk_sq8_noalloc", ctypes.c_int, [ctypes.POINTER(LeafArgs), c_vp]),
     ("tessa_assign", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(AssignArgs), c_vp]),
     ("tessa_replay_session_create", ctypes.c_int,
      [ctypes.c_int, ctypes.POINTER(PreparedReplay), ctypes.POINTER(c_vp)]),

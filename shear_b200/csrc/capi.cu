@@ -197,6 +197,8 @@ struct AssignPlan {
 
 }  // namespace
 
+int tessa::set_last_error(int code, const char* message) { return fail(code, "%s", message); }
+
 struct tessa_ctx {
   int device = -1;
   int sm_count = 0;

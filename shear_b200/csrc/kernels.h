@@ -63,4 +63,8 @@ struct Params {
 
 int launch_assign(const assign::Params& prm, bool sq8, cudaStream_t stream);
 
+// Records `code` and `message` as the calling thread's last error (returned by
+// tessa_last_error_message); returns `code`.
+int set_last_error(int code, const char* message);
+
 }  // namespace tessa

@@ -1,0 +1,80 @@
+"""The allocation-free leaf entry point (tessa_leaf_topk_sq8_noalloc).
+
+It serves callers that must not allocate device memory -- hosts whose
+allocator already owns the device, latency-critical threads that cannot afford
+cudaMalloc's possible device synchronisation, embedders with a fixed footprint
+-- by keeping its scratch in a static 64 MiB device array.  These tests call it
+through the C ABI and check it against the allocating entry point
+(tessa_leaf_topk_sq8), bit for bit, on two different batches in a row (the
+second call must not see the first call's leftovers).  The file is named so
+that pytest collects it last.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from leafcases import make_leaf_batch
+
+pytestmark = pytest.mark.gpu
+
+
+def _tensors(c):
+    import torch
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return dict(codes=t(c["codes"]), scales=t(c["scales"]), norms=t(c["norms"]),
+                gids=t(c["gids"].view(np.int32)), members=t(c["members"].view(np.int32)))
+
+
+def _noalloc(c, d, k):
+    import torch
+    from shear_b200 import _capi
+    rows = int(c["members"].shape[0])
+    ids = torch.full((rows * k,), -7, dtype=torch.int32, device="cuda")
+    dists = torch.full((rows * k,), -7.0, dtype=torch.float32, device="cuda")
+    starts = np.ascontiguousarray(c["starts"], np.uint64)
+    sizes = np.ascontiguousarray(c["sizes"], np.uint64)
+    a = _capi.LeafArgs(codes=d["codes"].data_ptr(), scales=d["scales"].data_ptr(), norms=d["norms"].data_ptr(),
+                       global_ids=d["gids"].data_ptr(), resident_rows=c["codes"].shape[0],
+                       padded_dim=c["codes"].shape[1], k=k, leaf_members=d["members"].data_ptr(),
+                       leaf_starts=starts.ctypes.data, leaf_sizes=sizes.ctypes.data, leaf_count=starts.shape[0],
+                       leaf_rows=rows, topk_ids=ids.data_ptr(), topk_dists=dists.data_ptr(),
+                       leaf_ordered_codes=None)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _capi.check(_capi.load().tessa_leaf_topk_sq8_noalloc(ctypes.byref(a), stream))
+    return ids.cpu().numpy().view(np.uint32), dists.cpu().numpy()
+
+
+def _allocating(c, d, k):
+    import torch
+    from shear_b200 import ops
+    ids, dists = ops.leaf_topk_sq8(d["codes"], d["scales"], d["norms"], d["gids"], d["members"], c["starts"],
+                                   c["sizes"], k)
+    torch.cuda.synchronize()
+    return ops.as_u32(ids), dists.cpu().numpy()
+
+
+def test_noalloc_matches_allocating_entry_point_on_two_calls(oracle):
+    # Permuted members force the gather of leaf-ordered codes into the static
+    # scratch; the two batches differ in shape, data and k.
+    for sizes, dim, k, seed in (([300, 257, 129], 768, 32, 41), ([640, 100], 256, 4, 42)):
+        c = make_leaf_batch(oracle, sizes, dim, seed=seed, dup=True, permute=True)
+        d = _tensors(c)
+        want_ids, want_d = _allocating(c, d, k)
+        got_ids, got_d = _noalloc(c, d, k)
+        assert np.array_equal(got_ids, want_ids)
+        assert np.array_equal(got_d.view(np.uint32), want_d.view(np.uint32))
+
+
+def test_noalloc_rejects_batches_beyond_the_static_scratch(oracle):
+    from shear_b200 import _capi
+    c = make_leaf_batch(oracle, [64], 768, seed=3, permute=True)
+    d = _tensors(c)
+    # Claim 100,000 member rows: the gather would need 76.8 MB > 64 MiB.  The
+    # size check runs before any device access.
+    c_big = dict(c)
+    c_big["starts"] = np.array([0], np.uint64)
+    c_big["sizes"] = np.array([100000], np.uint64)
+    c_big["members"] = np.zeros(100000, np.uint32)
+    with pytest.raises(_capi.TessaError, match="UNSUPPORTED.*static"):
+        _noalloc(c_big, d, 4)
