@@ -60,6 +60,8 @@ extern "C" {
 #define TESSA_MAX_RH 4
 /* Largest padded SQ8 dimension the leaf kernel accepts (shared-memory bound). */
 #define TESSA_MAX_PADDED_DIM 1024
+/* Largest leaf (member rows) the leaf kernel accepts. */
+#define TESSA_MAX_LEAF_ROWS 65535
 
 typedef struct tessa_ctx tessa_ctx;
 typedef struct tessa_replay_session tessa_replay_session;
@@ -144,6 +146,12 @@ TESSA_API int tessa_leaf_topk_sq8(tessa_ctx* ctx, const tessa_leaf_args* args, v
  * process_quantized_subtree_l2_compact_topk (CB:3693-3884) binds. */
 TESSA_API int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* args);
 
+/* Rows of the context's last leaf call whose lists depended on insertion order
+ * (eps-tie chains) and were recomputed with the exact sequential rule -- the
+ * counterpart of the reference's leaf_exact_fallback_rows counter
+ * (P/tessa_replay.rs:155-188; here it is a diagnostic, not an error). */
+TESSA_API int tessa_leaf_last_fallback_rows(const tessa_ctx* ctx, uint64_t* rows);
+
 /* Size of the static device scratch of tessa_leaf_topk_sq8_noalloc (64 MiB). */
 #define TESSA_NOALLOC_SCRATCH_BYTES (64u << 20)
 
@@ -153,8 +161,9 @@ TESSA_API int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* ar
  * threads where cudaMalloc/cudaFree (which can synchronise the device) are not
  * allowed, embedders that fix their footprint at load time.  Same arguments
  * and results as tessa_leaf_topk_sq8 (device pointers, HOST leaf layout), on
- * the current device, but no context: its scratch (tile table, error word and,
- * when leaf_ordered_codes is NULL, the leaf-ordered copy of the codes) lives in
+ * the current device, but no context: its scratch (tile table, error word,
+ * exact-fallback row list and, when leaf_ordered_codes is NULL, the
+ * leaf-ordered copy of the codes) lives in
  * one static device array of TESSA_NOALLOC_SCRATCH_BYTES that every GPU loading
  * the library holds until exit.  Batches needing more scratch are rejected
  * with TESSA_ERR_UNSUPPORTED.  The first call on a device resolves the array's

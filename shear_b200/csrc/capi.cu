@@ -111,6 +111,9 @@ struct LeafPlan {
                     (unsigned long long)rows);
       if (h_starts[l] + h_sizes[l] > 0x7fffffffull)
         return fail(TESSA_ERR_UNSUPPORTED, "leaf member rows beyond 2^31 are not supported");
+      if (h_sizes[l] > kMaxLeafRows)
+        return fail(TESSA_ERR_UNSUPPORTED, "leaf %llu has %llu rows; at most %llu are supported", (unsigned long long)l,
+                    (unsigned long long)h_sizes[l], (unsigned long long)kMaxLeafRows);
       sz32[l] = (uint32_t)h_sizes[l];
       for (uint64_t r0 = 0; r0 < h_sizes[l]; r0 += 128) tiles.push_back(make_uint2((uint32_t)l, (uint32_t)r0));
     }
@@ -205,11 +208,13 @@ struct tessa_ctx {
   cudaStream_t stream = nullptr;
   DevBuf d_err;         // one uint32 error word
   DevBuf gather;        // leaf-ordered codes scratch
+  DevBuf fallback;      // exact-fallback row list: count + (leaf, row) entries
   LeafPlan leaf_plan;
   AssignPlan assign_plan;
   // staging for host-buffer entry points
   DevBuf h_codes, h_scales, h_norms, h_gids, h_members, h_ids, h_dists, h_x;
   uint64_t timeout_ns = kDefaultTimeoutNs;
+  uint64_t last_fallback_rows = 0;  // rows of the last leaf call recomputed by the exact fallback
 };
 
 namespace {
@@ -281,12 +286,20 @@ int leaf_device(tessa_ctx* ctx, const tessa_leaf_args* a, cudaStream_t st) {
   L.out_ids = a->topk_ids;
   L.out_dists = a->topk_dists;
   L.d_err = ctx->d_err.as<uint32_t>();
+  TRY(ctx->fallback.ensure(16 + (size_t)a->leaf_rows * 8));
+  L.d_fb_count = ctx->fallback.as<uint32_t>();
+  L.d_fb_list = reinterpret_cast<uint2*>(ctx->fallback.as<uint8_t>() + 16);
+  L.fb_capacity = (uint32_t)a->leaf_rows;
+  L.resident_rows = a->resident_rows;
   L.timeout_ns = ctx->timeout_ns;
   L.sm_count = ctx->sm_count;
   int r = launch_leaf_topk_sq8(L, st);
   if (r != TESSA_OK) return fail(r, "leaf kernel launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  uint32_t fb = 0;
+  CUDA_TRY(cudaMemcpyAsync(&fb, L.d_fb_count, 4, cudaMemcpyDeviceToHost, st));
   uint32_t bits = 0;
   TRY(read_err(ctx, st, &bits));
+  ctx->last_fallback_rows = fb;
   return map_device_error(bits);
 }
 
@@ -391,6 +404,7 @@ void tessa_destroy(tessa_ctx* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   ctx->d_err.release();
   ctx->gather.release();
+  ctx->fallback.release();
   ctx->leaf_plan.release();
   ctx->assign_plan.release();
   DevBuf* bufs[] = {&ctx->h_codes, &ctx->h_scales, &ctx->h_norms, &ctx->h_gids, &ctx->h_members,
@@ -401,6 +415,12 @@ void tessa_destroy(tessa_ctx* ctx) {
 }
 
 int tessa_ctx_device(const tessa_ctx* ctx) { return ctx ? ctx->device : -1; }
+
+int tessa_leaf_last_fallback_rows(const tessa_ctx* ctx, uint64_t* rows) {
+  if (!ctx || !rows) return fail(TESSA_ERR_INVALID_ARG, "null argument");
+  *rows = ctx->last_fallback_rows;
+  return TESSA_OK;
+}
 
 int tessa_quantize_sq8(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t dim, uint32_t k_align, uint32_t bits,
                        int8_t* codes, float* scales, float* norms, void* stream) {

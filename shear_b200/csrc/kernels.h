@@ -22,9 +22,16 @@ struct LeafLaunch {
   uint32_t* out_ids;
   float* out_dists;
   uint32_t* d_err;
+  uint32_t* d_fb_count;       // scratch: number of rows handed to the exact fallback
+  uint2* d_fb_list;           // scratch: (leaf, row) of those rows, fb_capacity entries
+  uint32_t fb_capacity;
+  uint64_t resident_rows;     // bound for member ids
   uint64_t timeout_ns;
   int sm_count;
 };
+
+// Largest leaf the leaf kernel accepts (member positions are kept in 16 bits).
+constexpr uint64_t kMaxLeafRows = 65535;
 
 int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream);
 int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes, int8_t* dst,

@@ -7,7 +7,7 @@
 // the device -- are not allowed, and embedders that must fix their memory
 // footprint when the library is loaded.  tessa_leaf_topk_sq8 cannot serve them:
 // it needs a context and grows device scratch on demand (the leaf-ordered copy
-// of the codes, the tile table, the error word).
+// of the codes, the tile table, the exact-fallback row list, the error word).
 //
 // This entry point keeps that scratch in one file-scope __device__ array of
 // TESSA_NOALLOC_SCRATCH_BYTES (64 MiB) instead.  Every GPU that loads the
@@ -99,6 +99,9 @@ extern "C" int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* a, void* strea
   uint64_t num_tiles = 0;
   for (uint64_t l = 0; l < a->leaf_count; ++l) {
     uint64_t st = a->leaf_starts[l], sz = a->leaf_sizes[l];
+    if (sz > kMaxLeafRows)
+      return err(TESSA_ERR_UNSUPPORTED, "leaf %llu has %llu rows; at most %llu are supported", (unsigned long long)l,
+                 (unsigned long long)sz, (unsigned long long)kMaxLeafRows);
     if (st > a->leaf_rows || sz > a->leaf_rows - st)
       return err(TESSA_ERR_INVALID_ARG, "leaf %llu [start %llu, size %llu] outside %llu member rows",
                  (unsigned long long)l, (unsigned long long)st, (unsigned long long)sz,
@@ -112,7 +115,8 @@ extern "C" int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* a, void* strea
   size_t off_starts = round_up(off_err + 4);
   size_t off_sizes = round_up(off_starts + a->leaf_count * 8);
   size_t off_tiles = round_up(off_sizes + a->leaf_count * 4);
-  size_t off_codes = round_up(off_tiles + num_tiles * 8);
+  size_t off_fb = round_up(off_tiles + num_tiles * 8);
+  size_t off_codes = round_up(off_fb + 16 + (size_t)a->leaf_rows * 8);
   size_t need = gather ? off_codes + (size_t)a->leaf_rows * a->padded_dim : off_codes;
   if (need > kScratchBytes)
     return err(TESSA_ERR_UNSUPPORTED,
@@ -189,6 +193,10 @@ extern "C" int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* a, void* strea
   L.out_ids = a->topk_ids;
   L.out_dists = a->topk_dists;
   L.d_err = reinterpret_cast<uint32_t*>(s + off_err);
+  L.d_fb_count = reinterpret_cast<uint32_t*>(s + off_fb);
+  L.d_fb_list = reinterpret_cast<uint2*>(s + off_fb + 16);
+  L.fb_capacity = (uint32_t)a->leaf_rows;
+  L.resident_rows = a->resident_rows;
   L.timeout_ns = kTimeoutNs;
   L.sm_count = sms;
   r = launch_leaf_topk_sq8(L, st);

@@ -187,6 +187,14 @@ def leaf_topk_sq8_host(codes, scales, norms, global_ids, leaf_members, leaf_star
     return ids, dists
 
 
+def leaf_last_fallback_rows(ctx: Context | None = None, device: int = 0) -> int:
+    """Rows of the last leaf call on `ctx` recomputed by the exact sequential fallback."""
+    ctx = ctx or context(device)
+    n = ctypes.c_uint64()
+    C.check(C.load().tessa_leaf_last_fallback_rows(ctx.handle, ctypes.byref(n)))
+    return int(n.value)
+
+
 # -------------------------------------------------------------- assignment
 
 def assign(source: int, *, x=None, raw_norms=None, codes=None, scales=None, sq8_norms=None, global_ids,

@@ -107,6 +107,22 @@ def test_reference_staged_fixture_740_728_641(oracle):
     _assert_same(want, staged)
 
 
+def test_leaf_tie_chains_go_through_exact_fallback(oracle):
+    # Nearly identical rows: SQ8 distances cluster within the 2e-5 tie window,
+    # so many rows have non-transitive tie chains and need the sequential rule.
+    from shear_b200 import ops
+    rng = np.random.default_rng(77)
+    def formula(rows, dim):
+        base = rng.standard_normal(dim).astype(np.float32)
+        x = base[None, :] + rng.standard_normal((rows, dim)).astype(np.float32) * np.float32(2e-3)
+        return x / np.linalg.norm(x, axis=1, keepdims=True)
+    for k in (4, 32):
+        c = make_leaf_batch(oracle, [700, 300], 128, seed=k, formula=formula)
+        got = _device_run(c, k)
+        _assert_same(got, oracle_leaf(oracle, c, k))
+        assert ops.leaf_last_fallback_rows() > 0
+
+
 def test_leaf_config2_shape_sample(oracle):
     # 16 leaves of the 4096 x 2048 x 768 k=32 benchmark workload
     c = make_leaf_batch(oracle, [2048] * 16, 768, seed=2026)

@@ -70,11 +70,11 @@ def test_noalloc_rejects_batches_beyond_the_static_scratch(oracle):
     from shear_b200 import _capi
     c = make_leaf_batch(oracle, [64], 768, seed=3, permute=True)
     d = _tensors(c)
-    # Claim 100,000 member rows: the gather would need 76.8 MB > 64 MiB.  The
-    # size check runs before any device access.
+    # Claim two leaves of 50,000 member rows: the gather alone would need
+    # 76.8 MB > 64 MiB.  The size check runs before any device access.
     c_big = dict(c)
-    c_big["starts"] = np.array([0], np.uint64)
-    c_big["sizes"] = np.array([100000], np.uint64)
+    c_big["starts"] = np.array([0, 50000], np.uint64)
+    c_big["sizes"] = np.array([50000, 50000], np.uint64)
     c_big["members"] = np.zeros(100000, np.uint32)
     with pytest.raises(_capi.TessaError, match="UNSUPPORTED.*static"):
         _noalloc(c_big, d, 4)
