@@ -18,17 +18,27 @@
 // exactly L sorted by "<": an L-candidate always passes the list's tail (which
 // holds only non-L candidates or empty slots), is never pushed out (only a
 // full list of L-candidates could do it), and stops exactly at its rank
-// because "<" is transitive on L.  The epilogue therefore selects, per row and
-// in any order, the H = k+4 candidates that are smallest by distance, sorts
-// them by (distance, member position), splits them into runs of neighbours
-// closer than the tie eps, and checks (a) and (b): every run up to the one
-// holding rank k must be a transitive tournament under "<" (always true for
-// runs of one or two), and that run must end inside the H (or the H must hold
-// every candidate).  Rows that pass are written directly; the rest (~4e-4 of
-// rows on random data) are listed and recomputed by leaf_fallback_kernel with
-// the reference's exact sequential insertion.
+// because "<" is transitive on L.  Per row the kernel therefore finds, in any
+// column order, every candidate whose distance is within a margin M = 4 eps
+// of the k-th smallest distance (the "zone"), sorts the zone by distance,
+// splits it into runs of neighbours closer than eps and checks (a) and (b):
+// every run up to the one holding rank k must be a transitive tournament
+// under "<" (always true for runs of one), and that run must end inside the
+// zone (a gap > eps to the next zone entry, or more than eps below the zone's
+// upper edge).  Rows that pass are written directly; the rest (a few in 10^4
+// on random data) are listed and recomputed by leaf_fallback_kernel with the
+// reference's exact sequential insertion.
 //
-// B200 design (one persistent CTA per SM, 192 threads):
+// Per-row selection state (thread = row):
+//   * a sorted array of the k smallest distances seen so far, in registers
+//     (KS >= k FP32 slots; candidates go in two at a time, 2 min + 1
+//     three-input max per slot, branch-free); its maximum theta bounds the
+//     k-th smallest distance of the row from above;
+//   * a shared-memory log of (distance, global id) for every candidate that
+//     was within theta + M when it arrived, compacted against the current
+//     bound whenever it fills.  The log always holds the final zone.
+//
+// B200 design (one persistent CTA per SM, 224 threads):
 //   warp 0      TMA producer: A = 128 leaf rows x padded_dim, resident for the
 //               tile; B = 128-column chunks streamed in 128-byte K slabs
 //               through a ring of shared-memory stages (SWIZZLE_128B).
@@ -36,11 +46,13 @@
 //               M=128, N=128, K=32, int32 accumulators) into four 128-column
 //               TMEM buffers, so MMAs run up to three chunks ahead.
 //   warps 2..5  epilogue: thread t owns TMEM lane (leaf row) t; per 32
-//               columns it computes the exact reference distances, marks the
-//               ones below its set's current maximum in a bit mask, stashes the
-//               distances in shared memory and then inserts the marked ones
-//               into an unsorted H-slot set (six blocks of six slots, block
-//               maxima in registers).
+//               columns it computes the exact reference distances, builds a
+//               bit mask of the ones below the row's bound (one funnel shift
+//               per column), stashes the distances in shared memory and then
+//               pops the marked columns into the log and the sorted array.
+//   warp 6      column metadata (scale, norm, global id) of each chunk into a
+//               4-slot shared-memory ring, so the epilogue warps never wait
+//               on each other.
 // The distance matrix never leaves the SM.
 #include "common.cuh"
 #include "kernels.h"
@@ -52,8 +64,10 @@ constexpr uint32_t kBM = 128;          // rows per tile (TMEM lanes)
 constexpr uint32_t kBN = 128;          // columns per chunk (MMA N)
 constexpr uint32_t kSlab = 128;        // K bytes per TMA box (one 128B swizzle atom)
 constexpr uint32_t kMmaK = 32;         // K per tcgen05.mma kind::i8
-constexpr uint32_t kThreads = 192;
-constexpr uint32_t kEpiThreads = 128;
+constexpr uint32_t kThreads = 224;     // TMA, MMA, 4 epilogue warps, metadata warp
+constexpr uint32_t kEpiWarps = 4;
+constexpr uint32_t kMetaWarp = 6;
+constexpr uint32_t kMetaSlots = 4;      // chunk metadata ring
 constexpr uint32_t kAccBufs = 4;
 constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 512
 constexpr uint32_t kASlabBytes = kBM * kSlab;   // 16 KiB
@@ -61,17 +75,16 @@ constexpr uint32_t kBStageBytes = kBN * kSlab;  // 16 KiB
 constexpr uint32_t kGroup = 32;                 // columns per tcgen05.ld
 constexpr uint32_t kGroups = kBN / kGroup;
 constexpr uint32_t kMaxBStages = 8;
-constexpr uint32_t kSetSlots = 36;              // H <= k + 4 <= 36
-constexpr uint32_t kBlk = 6;                    // slots per block
-constexpr uint32_t kNBlk = kSetSlots / kBlk;    // blocks
-constexpr uint32_t kExtra = 4;                  // H = k + kExtra
-constexpr uint32_t kMetaBytes = 2u * kBN * 16u;           // 2 chunk buffers of (s, n, lid, -)
-constexpr uint32_t kStashBytes = 4u * kGroup * 32u * 4u;  // per epilogue warp: 32 x 32 floats
-constexpr uint32_t kSetDBytes = kSetSlots * kBM * 4u;
-constexpr uint32_t kSetJBytes = kSetSlots * kBM * 2u;
+constexpr uint32_t kStashStride = 36;           // floats per lane (16B aligned, conflict-free STS.128)
+constexpr uint32_t kMetaBytes = kMetaSlots * kBN * 12u;  // ring of (scale, norm) + global id
+constexpr uint32_t kStashBytes = 4u * 32u * kStashStride * 4u;
+constexpr uint32_t kLogEntryBytes = 8u;         // (distance bits, global id)
+constexpr uint32_t kMaxLogCap = 64;             // entries per row; ranks fit a 64-bit occupancy mask
 constexpr uint32_t kBarBytes = 512u;
 constexpr uint32_t kSmemLimit = 232448u;  // 227 KiB opt-in per block
 constexpr float kTieEps = 2.0e-5f;
+constexpr float kMargin = 4.0f * kTieEps;  // zone = [0, theta + kMargin]
+constexpr uint32_t kMaxRun = 8;            // longest eps-run checked by tournament
 
 struct Params {
   const float* scales;
@@ -85,7 +98,7 @@ struct Params {
   uint32_t num_slabs;
   uint32_t num_bstages;
   uint32_t k;
-  uint32_t h;                   // set size H = min(k + 4, 36)
+  uint32_t log_cap;             // log entries per row (<= kMaxLogCap)
   uint64_t resident_rows;
   uint32_t* out_ids;
   float* out_dists;
@@ -99,28 +112,29 @@ struct Params {
 struct Smem {
   uint8_t* a;
   uint8_t* b;
-  uint4* meta;
-  float* stash;
-  float* set_d;     // [slot][row]
-  uint16_t* set_j;  // [slot][row]
+  float2* meta_sn;  // [kMetaSlots][kBN] (scale, norm) of a chunk's columns
+  uint32_t* meta_g; // [kMetaSlots][kBN] global id
+  float* stash;     // [4 warps][32 lanes][kStashStride]
+  uint2* log;       // [log_cap][kBM] (distance bits, global id)
   uint64_t* a_full;
   uint64_t* a_empty;
   uint64_t* b_full;
   uint64_t* b_empty;
   uint64_t* t_full;
   uint64_t* t_empty;
+  uint64_t* m_full;
+  uint64_t* m_empty;
   uint64_t* mma_done;
   uint32_t* tmem_slot;
   uint32_t* abort_flag;
-  volatile uint32_t* epi_stop;
 };
 
-__host__ __device__ inline uint32_t smem_bytes(uint32_t num_slabs, uint32_t num_bstages) {
-  return 1024u + num_slabs * kASlabBytes + num_bstages * kBStageBytes + kMetaBytes + kStashBytes + kSetDBytes +
-         kSetJBytes + kBarBytes;
+__host__ __device__ inline uint32_t smem_bytes(uint32_t num_slabs, uint32_t num_bstages, uint32_t log_cap) {
+  return 1024u + num_slabs * kASlabBytes + num_bstages * kBStageBytes + kMetaBytes + kStashBytes +
+         log_cap * kBM * kLogEntryBytes + kBarBytes;
 }
 
-__device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t num_slabs, uint32_t num_bstages) {
+__device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t num_slabs, uint32_t num_bstages, uint32_t log_cap) {
   uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 1023u) & ~uintptr_t(1023u);
   uint8_t* p = reinterpret_cast<uint8_t*>(base);
   Smem s;
@@ -128,174 +142,159 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t num_slabs, uint32_t
   p += num_slabs * kASlabBytes;
   s.b = p;
   p += num_bstages * kBStageBytes;
-  s.meta = reinterpret_cast<uint4*>(p);
-  p += kMetaBytes;
+  s.meta_sn = reinterpret_cast<float2*>(p);
+  p += kMetaSlots * kBN * 8u;
+  s.meta_g = reinterpret_cast<uint32_t*>(p);
+  p += kMetaSlots * kBN * 4u;
   s.stash = reinterpret_cast<float*>(p);
   p += kStashBytes;
-  s.set_d = reinterpret_cast<float*>(p);
-  p += kSetDBytes;
-  s.set_j = reinterpret_cast<uint16_t*>(p);
-  p += kSetJBytes;
+  s.log = reinterpret_cast<uint2*>(p);
+  p += log_cap * kBM * kLogEntryBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(p);
   s.a_full = bars + 0;
   s.a_empty = bars + 1;
   s.b_full = bars + 2;
-  s.b_empty = bars + 2 + kMaxBStages;
-  s.t_full = bars + 2 + 2 * kMaxBStages;
+  s.b_empty = s.b_full + kMaxBStages;
+  s.t_full = s.b_empty + kMaxBStages;
   s.t_empty = s.t_full + kAccBufs;
-  s.mma_done = s.t_empty + kAccBufs;
+  s.m_full = s.t_empty + kAccBufs;
+  s.m_empty = s.m_full + kMetaSlots;
+  s.mma_done = s.m_empty + kMetaSlots;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.mma_done + 1);
   s.abort_flag = s.tmem_slot + 1;
-  s.epi_stop = s.tmem_slot + 2;
   return s;
 }
 
-// Column metadata for the epilogue: (scale, norm, local id, 0).  Columns past
-// the leaf get norm = +inf so their distance is +inf and never selected.
-__device__ __forceinline__ uint4 load_meta(const Params& p, uint64_t start, uint32_t cnt, uint32_t col) {
-  if (col >= cnt) return make_uint4(0u, 0x7f800000u, 0xffffffffu, 0u);
-  uint32_t lid = __ldg(p.members + start + col);
-  if (lid >= p.resident_rows) {
-    atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
-    return make_uint4(0u, 0x7f800000u, 0xffffffffu, 0u);
-  }
-  return make_uint4(__float_as_uint(__ldg(p.scales + lid)), __float_as_uint(__ldg(p.norms + lid)), lid, 0u);
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
-// Selection set of one row: H unsorted slots in shared memory (slot-major so a
-// warp's accesses are conflict-free), six blocks of six slots, block maxima
-// (distance, slot) in registers; theta = max over the set.
-struct RowSet {
-  float bmax[kNBlk];
-  uint32_t bslot[kNBlk];
-  float theta;
-  uint32_t gb;
-  uint32_t fill;
-};
+// Sorted array (descending, s[0] = maximum) of the KS smallest values seen.
+// Inserting the pair x <= y keeps the KS smallest of s, x and y:
+//   new[t] = max(s[t+2], min(s[t+1], y), min(s[t], x))
+// (the t-th largest of the merged sequence; s[KS] = s[KS+1] = -inf).  With
+// y = +inf it is the single insertion max(s[t+1], min(s[t], x)); values at or
+// above s[0] leave s unchanged.  Slots [k, KS) hold -inf sentinels that never
+// move, so s[0] is the k-th smallest.  Branch-free: 2 min + 1 three-input max
+// per slot.
+template <int KS>
+__device__ __forceinline__ void topk_insert2(float (&s)[KS], float x, float y) {
+  float n[KS];
+#pragma unroll
+  for (int t = 0; t < KS; ++t) {
+    float s1 = (t + 1 < KS) ? s[t + 1] : -INFINITY;
+    float s2 = (t + 2 < KS) ? s[t + 2] : -INFINITY;
+    n[t] = fmax3(s2, fminf(s1, y), fminf(s[t], x));
+  }
+#pragma unroll
+  for (int t = 0; t < KS; ++t) s[t] = n[t];
+}
 
-__device__ __forceinline__ void set_rebuild(RowSet& rs, const float* sd, uint32_t row) {
+// Keep the log entries of `row` with distance <= thr, in place.  Entries are
+// read eight at a time (all loads before any store of the batch: the write
+// index never passes the read index, so the batch is intact).
+__device__ __forceinline__ uint32_t log_compact(uint2* log, uint32_t row, uint32_t cnt, float thr) {
+  uint32_t j = 0;
+  for (uint32_t e0 = 0; e0 < cnt; e0 += 8) {
+    uint2 v[8];
 #pragma unroll
-  for (uint32_t b = 0; b < kNBlk; ++b) {
-    float m = -INFINITY;
-    uint32_t ms = b * kBlk;
+    for (uint32_t u = 0; u < 8; ++u) v[u] = (e0 + u < cnt) ? log[(e0 + u) * kBM + row] : make_uint2(0x7f800000u, 0u);
 #pragma unroll
-    for (uint32_t t = 0; t < kBlk; ++t) {
-      uint32_t sl = b * kBlk + t;
-      float x = sd[sl * kBM + row];
-      bool gt = x > m;
-      m = gt ? x : m;
-      ms = gt ? sl : ms;
+    for (uint32_t u = 0; u < 8; ++u) {
+      if (e0 + u < cnt && __uint_as_float(v[u].x) <= thr) {
+        log[j * kBM + row] = v[u];
+        ++j;
+      }
     }
-    rs.bmax[b] = m;
-    rs.bslot[b] = ms;
   }
-  rs.theta = rs.bmax[0];
-  rs.gb = 0;
-#pragma unroll
-  for (uint32_t b = 1; b < kNBlk; ++b) {
-    bool gt = rs.bmax[b] > rs.theta;
-    rs.theta = gt ? rs.bmax[b] : rs.theta;
-    rs.gb = gt ? b : rs.gb;
-  }
+  return j;
 }
 
-// Insert (d, j) given d < theta (set full): overwrite the maximum, refresh
-// its block and the global maximum.
-__device__ __forceinline__ void set_replace_max(RowSet& rs, float* sd, uint16_t* sj, uint32_t row, float d,
-                                                uint32_t j) {
-  uint32_t slot = rs.bslot[0];
-#pragma unroll
-  for (uint32_t b = 1; b < kNBlk; ++b) slot = (rs.gb == b) ? rs.bslot[b] : slot;
-  sd[slot * kBM + row] = d;
-  sj[slot * kBM + row] = (uint16_t)j;
-  uint32_t base = rs.gb * kBlk;
-  float m = -INFINITY;
-  uint32_t ms = base;
-#pragma unroll
-  for (uint32_t t = 0; t < kBlk; ++t) {
-    float x = sd[(base + t) * kBM + row];
-    bool gt = x > m;
-    m = gt ? x : m;
-    ms = gt ? base + t : ms;
-  }
-#pragma unroll
-  for (uint32_t b = 0; b < kNBlk; ++b) {
-    bool me = rs.gb == b;
-    rs.bmax[b] = me ? m : rs.bmax[b];
-    rs.bslot[b] = me ? ms : rs.bslot[b];
-  }
-  rs.theta = rs.bmax[0];
-  rs.gb = 0;
-#pragma unroll
-  for (uint32_t b = 1; b < kNBlk; ++b) {
-    bool gt = rs.bmax[b] > rs.theta;
-    rs.theta = gt ? rs.bmax[b] : rs.theta;
-    rs.gb = gt ? b : rs.gb;
-  }
-}
-
-__device__ __forceinline__ uint32_t gid_of(const Params& p, uint64_t start, uint32_t j) {
-  return __ldg(p.global_ids + __ldg(p.members + start + j));
-}
-
-// Finish one row: sort the set, verify order independence, write k results.
+// Finish one row: sort the zone, verify order independence, write k results.
 // Returns false if the row must be recomputed by the exact fallback.
-__device__ bool finish_row(const Params& p, float* sd, uint16_t* sj, uint32_t row, uint32_t fill, bool complete,
-                           uint64_t start, uint64_t out) {
-  // Rank-sort the fill entries by (distance, position) back into the slots.
-  float d[kSetSlots];
-  uint32_t j[kSetSlots];
-#pragma unroll
-  for (uint32_t a = 0; a < kSetSlots; ++a) {
-    bool live = a < fill;
-    d[a] = live ? sd[a * kBM + row] : INFINITY;
-    j[a] = live ? (uint32_t)sj[a * kBM + row] : 0x10000u + a;
-  }
-#pragma unroll
-  for (uint32_t a = 0; a < kSetSlots; ++a) {
-    uint32_t r = 0;
-#pragma unroll
-    for (uint32_t b = 0; b < kSetSlots; ++b) {
-      bool lt = (d[b] < d[a]) | ((d[b] == d[a]) & (j[b] < j[a]));
-      r += lt ? 1u : 0u;
-    }
-    if (a < fill) {
-      sd[r * kBM + row] = d[a];
-      sj[r * kBM + row] = (uint16_t)j[a];
-    }
-  }
-  const uint32_t V = fill;
+template <int KS>
+__device__ bool finish_row(const Params& p, uint2* log, uint8_t* perm, uint32_t row, uint32_t E,
+                           const float (&s)[KS], float thr, uint32_t gid_i, uint64_t out) {
   const uint32_t k = p.k;
+  const float theta = s[0];
+  const bool complete = !(theta < INFINITY);
+  // Rank of each zone entry.  Entries with d <= theta: the number of smaller
+  // distances among the k smallest (the sorted array); equal distances take
+  // consecutive ranks in log order.  Entries above theta (the margin) follow
+  // all of those, ordered by distance.  A zone entry with the row's own
+  // global id (a repeated member) sends the row to the exact fallback.
+  uint32_t n_inner = 0;
+  bool dup = false;
+  for (uint32_t e = 0; e < E; ++e) {
+    uint2 v = log[e * kBM + row];
+    n_inner += (__uint_as_float(v.x) <= theta) ? 1u : 0u;
+    dup |= v.y == gid_i;
+  }
+  if (dup) return false;
+  uint64_t occ = 0;
+  for (uint32_t e = 0; e < E; ++e) {
+    float d = __uint_as_float(log[e * kBM + row].x);
+    uint32_t r;
+    if (d <= theta) {
+      uint32_t r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+#pragma unroll
+      for (int t = 0; t < KS; t += 4) {
+        r0 += (s[t] < d) ? 1u : 0u;
+        if (t + 1 < KS) r1 += (s[t + 1] < d) ? 1u : 0u;
+        if (t + 2 < KS) r2 += (s[t + 2] < d) ? 1u : 0u;
+        if (t + 3 < KS) r3 += (s[t + 3] < d) ? 1u : 0u;
+      }
+      r = (r0 + r1) + (r2 + r3) - ((uint32_t)KS - k);  // minus the -inf sentinels
+    } else {
+      r = n_inner;
+      for (uint32_t f = 0; f < E; ++f) {
+        float df = __uint_as_float(log[f * kBM + row].x);
+        r += (df > theta && (df < d || (df == d && f < e))) ? 1u : 0u;
+      }
+    }
+    while (r < 63u && ((occ >> r) & 1ull)) ++r;
+    occ |= 1ull << r;
+    perm[r] = (uint8_t)e;
+  }
+  if (occ != (E >= 64u ? ~0ull : ((1ull << E) - 1ull))) return false;  // not a permutation: give up safely
+
   uint32_t q = 0;  // output slots written
   uint32_t i = 0;
-  while (q < k && i < V) {
-    float di = sd[i * kBM + row];
+  uint2 vi = E > 0 ? log[perm[0] * kBM + row] : make_uint2(0u, 0u);
+  while (q < k && i < E) {
+    float di = __uint_as_float(vi.x);
     uint32_t e = i + 1;
     float prev = di;
-    while (e < V) {
-      float de = sd[e * kBM + row];
+    uint2 ve = make_uint2(0u, 0u);
+    while (e < E) {
+      ve = log[perm[e] * kBM + row];
+      float de = __uint_as_float(ve.x);
       if (!(fabsf(__fsub_rn(de, prev)) <= kTieEps)) break;
       prev = de;
       ++e;
     }
     uint32_t len = e - i;
-    // The run holding rank k must end inside the set.
-    if (q + len >= k && e == V && !complete) return false;
+    // The run holding rank k must end inside the zone: every candidate
+    // outside the zone lies above thr, hence more than eps above the run.
+    if (q + len >= k && e == E && !complete && !(__fsub_rn(thr, prev) > kTieEps)) return false;
     if (len == 1) {
-      p.out_ids[out + q] = gid_of(p, start, sj[i * kBM + row]);
+      p.out_ids[out + q] = vi.y;
       p.out_dists[out + q] = di;
       ++q;
     } else {
       // Tournament of the run under the eps/id rule: transitive iff the win
       // counts are 0..len-1 (then "<" orders the run by wins).
-      if (len > 8) return false;
-      float rd[8];
-      uint32_t rg[8];
+      if (len > kMaxRun) return false;
+      float rd[kMaxRun];
+      uint32_t rg[kMaxRun];
       for (uint32_t t = 0; t < len; ++t) {
-        rd[t] = sd[(i + t) * kBM + row];
-        rg[t] = gid_of(p, start, sj[(i + t) * kBM + row]);
+        uint2 v = log[perm[i + t] * kBM + row];
+        rd[t] = __uint_as_float(v.x);
+        rg[t] = v.y;
       }
-      uint32_t wins[8];
+      uint32_t wins[kMaxRun];
       uint32_t seen = 0;
       for (uint32_t t = 0; t < len; ++t) {
         uint32_t w = 0;
@@ -316,6 +315,7 @@ __device__ bool finish_row(const Params& p, float* sd, uint16_t* sj, uint32_t ro
       }
     }
     i = e;
+    vi = ve;
   }
   for (; q < k; ++q) {
     p.out_ids[out + q] = 0xffffffffu;
@@ -324,11 +324,12 @@ __device__ bool finish_row(const Params& p, float* sd, uint16_t* sj, uint32_t ro
   return true;
 }
 
+template <int KS>
 __global__ void __launch_bounds__(kThreads, 1)
     leaf_topk_sq8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          const Params p) {
   extern __shared__ uint8_t smem_raw[];
-  Smem s = carve(smem_raw, p.num_slabs, p.num_bstages);
+  Smem s = carve(smem_raw, p.num_slabs, p.num_bstages, p.log_cap);
   const uint32_t warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
   volatile uint32_t* abort_flag = s.abort_flag;
@@ -342,11 +343,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (uint32_t i = 0; i < kAccBufs; ++i) {
       mbar_init(&s.t_full[i], 1);
-      mbar_init(&s.t_empty[i], kEpiThreads / 32);
+      mbar_init(&s.t_empty[i], kEpiWarps);
+    }
+    for (uint32_t i = 0; i < kMetaSlots; ++i) {
+      mbar_init(&s.m_full[i], 32);
+      mbar_init(&s.m_empty[i], kEpiWarps);
     }
     mbar_init(s.mma_done, 1);
     *s.abort_flag = 0u;
-    *s.epi_stop = 0u;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -446,14 +450,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t dummy_abort = 0u;
       mbar_wait(s.mma_done, 0u, &dummy_abort, p.err_word, p.timeout_ns);
     }
+  } else if (warp == kMetaWarp) {
+    // ------------------------------------------------------ column metadata
+    // (scale, norm, global id) of each chunk's columns into a ring of
+    // kMetaSlots slots; the epilogue warps release a slot when done with it.
+    uint32_t seq = 0;
+    bool ok = true;
+    for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      uint2 t = p.tiles[tile];
+      uint64_t start = p.leaf_starts[t.x];
+      uint32_t cnt = p.leaf_sizes[t.x];
+      uint32_t nchunks = (cnt + kBN - 1) / kBN;
+      for (uint32_t c = 0; c < nchunks; ++c, ++seq) {
+        uint32_t slot = seq % kMetaSlots, use = seq / kMetaSlots;
+        bool w = true;
+        if (lane == 0) w = mbar_wait(&s.m_empty[slot], (use & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns);
+        if (__shfl_sync(0xffffffffu, w ? 1u : 0u, 0) == 0u) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kBN / 32; ++u) {
+          uint32_t col = c * kBN + u * 32 + lane;
+          float2 sn = make_float2(0.f, INFINITY);  // past the leaf: distance +inf
+          uint32_t g = 0xffffffffu;
+          if (col < cnt) {
+            uint32_t lid = __ldg(p.members + start + col);
+            if (lid < p.resident_rows) {
+              sn = make_float2(__ldg(p.scales + lid), __ldg(p.norms + lid));
+              g = __ldg(p.global_ids + lid);
+            } else {
+              atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+            }
+          }
+          s.meta_sn[slot * kBN + u * 32 + lane] = sn;
+          s.meta_g[slot * kBN + u * 32 + lane] = g;
+        }
+        mbar_arrive(&s.m_full[slot]);
+      }
+    }
   } else {
     // ------------------------------------------------------ epilogue
     const uint32_t ew = warp - 2;          // epilogue warp 0..3
     const uint32_t quad = warp & 3u;       // TMEM lane quadrant this warp may access
-    const uint32_t et = threadIdx.x - 64;  // 0..127
     const uint32_t row_in_tile = quad * 32 + lane;
-    float* stash = s.stash + ew * (kGroup * 32);
-    uint32_t acc = 0;
+    float* stash = s.stash + (ew * 32u + lane) * kStashStride;
+    const uint32_t cap = p.log_cap;
+    uint32_t acc = 0, seq = 0;
     bool stop = false;
     for (uint32_t tile = blockIdx.x; tile < p.num_tiles && !stop; tile += gridDim.x) {
       uint2 t = p.tiles[tile];
@@ -461,101 +504,118 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t cnt = p.leaf_sizes[t.x];
       uint32_t row = t.y + row_in_tile;
       bool valid = row < cnt;
-      uint32_t lid_i = 0xfffffffeu;
+      uint32_t gid_i = 0xfffffffeu;
       float s_i = 0.f, n_i = 0.f;
       if (valid) {
-        lid_i = __ldg(p.members + start + row);
+        uint32_t lid_i = __ldg(p.members + start + row);
         if (lid_i >= p.resident_rows) {
           atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
           valid = false;
-          lid_i = 0xfffffffeu;
         } else {
           s_i = __ldg(p.scales + lid_i);
           n_i = __ldg(p.norms + lid_i);
+          gid_i = __ldg(p.global_ids + lid_i);
         }
       }
-      // Sentinel slots beyond H never become the maximum.
-      for (uint32_t sl = p.h; sl < kSetSlots; ++sl) s.set_d[sl * kBM + row_in_tile] = -INFINITY;
-      RowSet rs;
+      float sk[KS];
 #pragma unroll
-      for (uint32_t b = 0; b < kNBlk; ++b) {
-        rs.bmax[b] = -INFINITY;
-        rs.bslot[b] = b * kBlk;
-      }
-      rs.theta = valid ? INFINITY : -INFINITY;
-      rs.gb = 0;
-      rs.fill = 0;
-      uint32_t offered = 0;  // candidates that went through the filter
-      uint32_t nchunks = (cnt + kBN - 1) / kBN;
-      s.meta[et] = load_meta(p, start, cnt, et);
-      __syncwarp();
-      named_bar_sync(1, kEpiThreads);
-      for (uint32_t c = 0; c < nchunks; ++c, ++acc) {
-        const uint4* meta = s.meta + (c & 1u) * kBN;
-        uint4 nm = make_uint4(0, 0, 0, 0);
-        if (c + 1 < nchunks) nm = load_meta(p, start, cnt, (c + 1) * kBN + et);
+      for (int q = 0; q < KS; ++q) sk[q] = (uint32_t)q < p.k ? INFINITY : -INFINITY;
+      float thr = valid ? INFINITY : -INFINITY;  // theta + margin
+      uint32_t nlog = 0;
+      bool ovf = false;
+      const uint32_t nchunks = (cnt + kBN - 1) / kBN;
+      const uint32_t c_self = t.y / kBN;  // the row's own column: chunk c_self, group quad, lane `lane`
+      for (uint32_t c = 0; c < nchunks; ++c, ++acc, ++seq) {
+        const uint32_t mslot = seq % kMetaSlots;
+        const float4* msn = reinterpret_cast<const float4*>(s.meta_sn + mslot * kBN);
+        const uint32_t* mg = s.meta_g + mslot * kBN;
         uint32_t buf = acc % kAccBufs, use = acc / kAccBufs;
         bool ok = true;
-        if (lane == 0) ok = mbar_wait(&s.t_full[buf], use & 1u, abort_flag, p.err_word, p.timeout_ns);
-        ok = __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0u;
-        if (ok) {
-          tc_fence_after();
-#pragma unroll 1
-          for (uint32_t g = 0; g < kGroups; ++g) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem_base + ((quad * 32u) << 16) + buf * kBN + g * kGroup, v);
-            tmem_ld_wait();
-            uint32_t mask = 0, real = 0;
-            const float theta = rs.theta;
-#pragma unroll
-            for (uint32_t cc = 0; cc < kGroup; ++cc) {
-              uint4 m = meta[g * kGroup + cc];
-              float d = sq8_l2_from_dot((int)v[cc], s_i, n_i, __uint_as_float(m.x), __uint_as_float(m.y));
-              bool cand = (m.z != lid_i) & (m.z != 0xffffffffu);
-              real += cand ? 1u : 0u;
-              bool pass = (d < theta) & cand;
-              mask |= pass ? (1u << cc) : 0u;
-              stash[cc * 32 + lane] = d;
-            }
-            offered += real;
-            const uint32_t colbase = c * kBN + g * kGroup;
-#pragma unroll 1
-            while (mask) {
-              uint32_t cc = __ffs(mask) - 1u;
-              mask &= mask - 1u;
-              float d = stash[cc * 32 + lane];
-              if (d < rs.theta) {
-                uint32_t j = colbase + cc;
-                if (rs.fill < p.h) {
-                  s.set_d[rs.fill * kBM + row_in_tile] = d;
-                  s.set_j[rs.fill * kBM + row_in_tile] = (uint16_t)j;
-                  ++rs.fill;
-                  if (rs.fill == p.h) set_rebuild(rs, s.set_d, row_in_tile);
-                } else {
-                  set_replace_max(rs, s.set_d, s.set_j, row_in_tile, d, j);
-                }
-              }
-            }
-            __syncwarp();
-          }
-          tc_fence_before();
+        if (lane == 0) {
+          ok = mbar_wait(&s.m_full[mslot], (seq / kMetaSlots) & 1u, abort_flag, p.err_word, p.timeout_ns) &&
+               mbar_wait(&s.t_full[buf], use & 1u, abort_flag, p.err_word, p.timeout_ns);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s.t_empty[buf]);
-        if (c + 1 < nchunks) s.meta[((c + 1) & 1u) * kBN + et] = nm;
-        __syncwarp();
-        named_bar_sync(1, kEpiThreads);
-        if (et == 0) *s.epi_stop = *abort_flag;
-        named_bar_sync(1, kEpiThreads);
-        if (*s.epi_stop) {
+        if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0u) {
           stop = true;
           break;
         }
+        tc_fence_after();
+#pragma unroll 1
+        for (uint32_t g = 0; g < kGroups; ++g) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem_base + ((quad * 32u) << 16) + buf * kBN + g * kGroup, v);
+          tmem_ld_wait();
+          // Exact reference distances; bit (31 - cc) of mask = column cc is
+          // below the bound (the sign of d - thr, shifted in).
+          float dc[32];
+          uint32_t mask = 0;
+#pragma unroll
+          for (uint32_t cc = 0; cc < kGroup; cc += 2) {
+            float4 m = msn[(g * kGroup + cc) >> 1];
+            float t0 = __fmul_rn(s_i, m.x);
+            float t1 = __fmul_rn(s_i, m.z);
+            float u0 = __fmul_rn(t0, __int2float_rn((int)v[cc]));
+            float u1 = __fmul_rn(t1, __int2float_rn((int)v[cc + 1]));
+            float nn0 = __fadd_rn(n_i, m.y);
+            float nn1 = __fadd_rn(n_i, m.w);
+            // rn(nn + rn(-2*u)) == fma(-2, u, nn): -2*u is exact.
+            float d0 = __fmaf_rn(-2.0f, u0, nn0);
+            float d1 = __fmaf_rn(-2.0f, u1, nn1);
+            dc[cc] = d0;
+            dc[cc + 1] = d1;
+            mask = __funnelshift_l(__float_as_uint(__fsub_rn(d0, thr)), mask, 1);
+            mask = __funnelshift_l(__float_as_uint(__fsub_rn(d1, thr)), mask, 1);
+          }
+          float4* st = reinterpret_cast<float4*>(stash);
+#pragma unroll
+          for (uint32_t q = 0; q < kGroup / 4; ++q)
+            st[q] = make_float4(dc[4 * q], dc[4 * q + 1], dc[4 * q + 2], dc[4 * q + 3]);
+          if (c == c_self && g == quad) mask &= ~(0x80000000u >> lane);  // the row itself
+          if (__any_sync(0xffffffffu, nlog + __popc(mask) > cap)) nlog = log_compact(s.log, row_in_tile, nlog, thr);
+          const uint32_t* gg = mg + g * kGroup;
+          // Two candidates per step.  Both are logged if within the bound;
+          // the pair insertion is a no-op for values above the k-th smallest.
+#pragma unroll 1
+          while (mask) {
+            uint32_t c0 = __clz(mask);
+            mask ^= 0x80000000u >> c0;
+            uint32_t c1 = mask ? __clz(mask) : c0;
+            mask ^= mask ? (0x80000000u >> c1) : 0u;
+            float d0 = stash[c0], d1 = stash[c1];
+            uint32_t g0 = gg[c0], g1 = gg[c1];
+            d0 = d0 > 0.0f ? d0 : 0.0f;  // reference clamp (CB:8999-9001)
+            const bool two = c1 != c0;
+            d1 = two ? (d1 > 0.0f ? d1 : 0.0f) : INFINITY;
+            bool ok0 = d0 <= thr, ok1 = two && d1 <= thr;
+            if (nlog + 2u > cap) {  // rare: make room, or give the row to the fallback
+              nlog = log_compact(s.log, row_in_tile, nlog, thr);
+              if (nlog + 2u > cap) {
+                ovf = true;
+                ok0 = ok1 = false;
+              }
+            }
+            if (ok0) s.log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(d0), g0);
+            nlog += ok0 ? 1u : 0u;
+            if (ok1) s.log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(d1), g1);
+            nlog += ok1 ? 1u : 0u;
+            topk_insert2<KS>(sk, fminf(d0, d1), fmaxf(d0, d1));
+            thr = __fadd_rn(sk[0], kMargin);
+          }
+          __syncwarp();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&s.t_empty[buf]);
+          mbar_arrive(&s.m_empty[mslot]);
+        }
       }
       if (!stop && valid) {
-        uint64_t out = (start + row) * (uint64_t)p.k;
-        bool complete = offered <= rs.fill;  // the set holds every candidate of the row
-        if (!finish_row(p, s.set_d, s.set_j, row_in_tile, rs.fill, complete, start, out)) {
+        const uint32_t E = log_compact(s.log, row_in_tile, nlog, thr);
+        const uint64_t out = (start + row) * (uint64_t)p.k;
+        bool okr = !ovf && finish_row<KS>(p, s.log, reinterpret_cast<uint8_t*>(stash), row_in_tile, E, sk, thr,
+                                          gid_i, out);
+        if (!okr) {
           uint32_t slot = atomicAdd(p.fb_count, 1u);
           if (slot < p.fb_capacity)
             p.fb_list[slot] = make_uint2(t.x, row);
@@ -563,6 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
         }
       }
+      __syncwarp();
     }
   }
 
@@ -575,19 +636,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Exact fallback: recompute one listed row per warp with the reference's
-// sequential insertion (ascending member position, CB:7229-7259).  Lane s holds
-// list slot s; each candidate's rank is found with one ballot.
-__global__ void __launch_bounds__(256) leaf_fallback_kernel(const int8_t* __restrict__ leaf_codes,
-                                                             uint32_t padded_dim, const Params p) {
+// Exact fallback: recompute each listed row with the reference's sequential
+// insertion (ascending member position, CB:7229-7259).  One CTA per row: all
+// threads compute a block of the row's distances into shared memory, then
+// warp 0 walks the block in column order.  Lane s holds list slot s; a ballot
+// pre-filter (distance <= worst + 33 eps, the largest upward creep of the
+// last slot over 32 insertions) skips candidates the reference rejects, and
+// each survivor's rank comes from one ballot of the exact rule.
+constexpr uint32_t kFbThreads = 256;
+constexpr uint32_t kFbBlock = 2048;  // columns per shared-memory block
+
+__global__ void __launch_bounds__(kFbThreads) leaf_fallback_kernel(const int8_t* __restrict__ leaf_codes,
+                                                                    uint32_t padded_dim, const Params p) {
   extern __shared__ int4 fb_smem[];
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t words = padded_dim / 16u;  // int4 words per code row
-  int4* rowbuf = fb_smem + warp * words;
+  int4* rowbuf = fb_smem;
+  float* bd_s = reinterpret_cast<float*>(rowbuf + words);
+  uint32_t* bg_s = reinterpret_cast<uint32_t*>(bd_s + kFbBlock);
+  uint32_t* bl_s = bg_s + kFbBlock;
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   const uint32_t total = *p.fb_count;
   const uint32_t n = total < p.fb_capacity ? total : p.fb_capacity;
   const uint32_t k = p.k;
-  for (uint32_t item = blockIdx.x * (blockDim.x >> 5) + warp; item < n; item += gridDim.x * (blockDim.x >> 5)) {
+  for (uint32_t item = blockIdx.x; item < n; item += gridDim.x) {
     uint2 e = p.fb_list[item];
     uint64_t start = p.leaf_starts[e.x];
     uint32_t cnt = p.leaf_sizes[e.x];
@@ -595,18 +666,18 @@ __global__ void __launch_bounds__(256) leaf_fallback_kernel(const int8_t* __rest
     uint32_t lid_i = p.members[start + row];
     float s_i = p.scales[lid_i], n_i = p.norms[lid_i];
     const int4* rc = reinterpret_cast<const int4*>(leaf_codes + (start + row) * padded_dim);
-    for (uint32_t w = lane; w < words; w += 32) rowbuf[w] = rc[w];
-    __syncwarp();
-    float bd = 3.402823466e+38F;
+    for (uint32_t w = threadIdx.x; w < words; w += kFbThreads) rowbuf[w] = rc[w];
+    float bd = 3.402823466e+38F;  // warp 0: slot `lane` of the list
     uint32_t bi = 0xffffffffu;
-    for (uint32_t c0 = 0; c0 < cnt; c0 += 32) {
-      uint32_t jc = c0 + lane;
-      float dj = INFINITY;
-      uint32_t gj = 0xffffffffu, lj = 0xffffffffu;
-      if (jc < cnt) {
-        lj = p.members[start + jc];
+    for (uint32_t b0 = 0; b0 < cnt; b0 += kFbBlock) {
+      uint32_t bn = cnt - b0 < kFbBlock ? cnt - b0 : kFbBlock;
+      __syncthreads();
+      for (uint32_t c = threadIdx.x; c < bn; c += kFbThreads) {
+        uint32_t lj = p.members[start + b0 + c];
+        float dj = INFINITY;
+        uint32_t gj = 0xffffffffu;
         if (lj < p.resident_rows) {
-          const int4* cc = reinterpret_cast<const int4*>(leaf_codes + (start + jc) * padded_dim);
+          const int4* cc = reinterpret_cast<const int4*>(leaf_codes + (start + b0 + c) * padded_dim);
           int dot = 0;
           for (uint32_t w = 0; w < words; ++w) {
             int4 x = rowbuf[w], y = cc[w];
@@ -618,40 +689,52 @@ __global__ void __launch_bounds__(256) leaf_fallback_kernel(const int8_t* __rest
           dj = sq8_l2_from_dot(dot, s_i, n_i, p.scales[lj], p.norms[lj]);
           gj = p.global_ids[lj];
         } else {
-          lj = lid_i;  // out-of-range ids were flagged by the main kernel; skip
+          lj = lid_i;  // flagged by the main kernel; never a candidate
         }
+        bd_s[c] = dj;
+        bg_s[c] = gj;
+        bl_s[c] = lj;
       }
-      uint32_t lim = cnt - c0 < 32 ? cnt - c0 : 32;
-      for (uint32_t t = 0; t < lim; ++t) {
-        float d = __shfl_sync(0xffffffffu, dj, t);
-        uint32_t g = __shfl_sync(0xffffffffu, gj, t);
-        uint32_t l = __shfl_sync(0xffffffffu, lj, t);
-        if (l == lid_i) continue;
-        bool b = (lane < k) && stable_better(d, g, bd, bi);
-        uint32_t m = __ballot_sync(0xffffffffu, b);
-        if (!((m >> (k - 1)) & 1u)) continue;
-        uint32_t live = k == 32 ? 0xffffffffu : ((1u << k) - 1u);
-        uint32_t inv = ~m & live;
-        uint32_t pos = inv ? (32u - __clz(inv)) : 0u;
-        float ud = __shfl_up_sync(0xffffffffu, bd, 1);
-        uint32_t ui = __shfl_up_sync(0xffffffffu, bi, 1);
-        if (lane < k) {
-          if (lane > pos) {
-            bd = ud;
-            bi = ui;
-          } else if (lane == pos) {
-            bd = d;
-            bi = g;
+      __syncthreads();
+      if (warp == 0) {
+        for (uint32_t c0 = 0; c0 < bn; c0 += 32) {
+          uint32_t c = c0 + lane;
+          float dj = c < bn ? bd_s[c] : INFINITY;
+          uint32_t lj = c < bn ? bl_s[c] : lid_i;
+          float worst = __shfl_sync(0xffffffffu, bd, k - 1);
+          float thr = __fadd_rn(worst, 33.0f * 2.0e-5f);
+          uint32_t cand = __ballot_sync(0xffffffffu, (lj != lid_i) && (dj <= thr));
+          while (cand) {
+            uint32_t t = __ffs(cand) - 1u;
+            cand &= cand - 1u;
+            float d = __shfl_sync(0xffffffffu, dj, t);
+            uint32_t g = bg_s[c0 + t];
+            bool b = (lane < k) && stable_better(d, g, bd, bi);
+            uint32_t m = __ballot_sync(0xffffffffu, b);
+            if (!((m >> (k - 1)) & 1u)) continue;
+            uint32_t live = k == 32 ? 0xffffffffu : ((1u << k) - 1u);
+            uint32_t inv = ~m & live;
+            uint32_t pos = inv ? (32u - __clz(inv)) : 0u;
+            float ud = __shfl_up_sync(0xffffffffu, bd, 1);
+            uint32_t ui = __shfl_up_sync(0xffffffffu, bi, 1);
+            if (lane < k) {
+              if (lane > pos) {
+                bd = ud;
+                bi = ui;
+              } else if (lane == pos) {
+                bd = d;
+                bi = g;
+              }
+            }
           }
         }
       }
     }
-    if (lane < k) {
+    if (warp == 0 && lane < k) {
       uint64_t out = (start + row) * (uint64_t)k + lane;
       p.out_ids[out] = bi;
       p.out_dists[out] = bd;
     }
-    __syncwarp();
   }
 }
 
@@ -703,20 +786,57 @@ int make_code_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint32_t r
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-int leaf_num_bstages(uint32_t padded_dim) {
+// Shared-memory plan for a launch: B-operand stages and log entries per row.
+// Prefers >= 3 stages with a log of k + 24 entries; falls back to 2 stages
+// with at least k + 8.  Returns false if neither fits.
+static bool leaf_plan(uint32_t padded_dim, uint32_t k, uint32_t* stages, uint32_t* log_cap) {
   uint32_t slabs = (padded_dim + leaf::kSlab - 1) / leaf::kSlab;
-  uint32_t fixed = leaf::smem_bytes(slabs, 0);
-  if (fixed >= leaf::kSmemLimit) return 0;
-  uint32_t st = (leaf::kSmemLimit - fixed) / leaf::kBStageBytes;
-  if (st > leaf::kMaxBStages) st = leaf::kMaxBStages;
-  return st >= 2 ? (int)st : 0;
+  uint32_t fixed = leaf::smem_bytes(slabs, 0, 0);
+  auto cap_for = [&](uint32_t st) -> uint32_t {
+    uint32_t used = fixed + st * leaf::kBStageBytes;
+    if (used >= leaf::kSmemLimit) return 0;
+    uint32_t c = (leaf::kSmemLimit - used) / (leaf::kBM * leaf::kLogEntryBytes);
+    return c < leaf::kMaxLogCap ? c : leaf::kMaxLogCap;
+  };
+  uint32_t want = k + 24 < leaf::kMaxLogCap ? k + 24 : leaf::kMaxLogCap;
+  for (uint32_t st = 6; st >= 3; --st) {
+    uint32_t c = cap_for(st);
+    if (c >= want) {
+      *stages = st;
+      *log_cap = c;
+      return true;
+    }
+  }
+  uint32_t c = cap_for(2);
+  if (c >= k + 8) {
+    *stages = 2;
+    *log_cap = c;
+    return true;
+  }
+  return false;
+}
+
+int leaf_num_bstages(uint32_t padded_dim) {
+  uint32_t st = 0, cap = 0;
+  return leaf_plan(padded_dim, 32, &st, &cap) ? (int)st : 0;
+}
+
+template <int KS>
+static int launch_main(const CUtensorMap& ta, const CUtensorMap& tb, const leaf::Params& prm, uint32_t smem,
+                       uint32_t grid, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(leaf::leaf_topk_sq8_kernel<KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return TESSA_ERR_CUDA;
+  leaf::leaf_topk_sq8_kernel<KS><<<grid, leaf::kThreads, smem, stream>>>(ta, tb, prm);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 
 // Returns 0, or a TESSA_ERR_* code.
 int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
   if (L.num_tiles == 0) return TESSA_OK;
-  int nst = leaf_num_bstages(L.padded_dim);
-  if (nst == 0) return TESSA_ERR_UNSUPPORTED;
+  if (L.k == 0 || L.k > 32) return TESSA_ERR_INVALID_ARG;
+  uint32_t nst = 0, log_cap = 0;
+  if (!leaf_plan(L.padded_dim, L.k, &nst, &log_cap)) return TESSA_ERR_UNSUPPORTED;
   uint32_t slabs = (L.padded_dim + leaf::kSlab - 1) / leaf::kSlab;
   CUtensorMap ta, tb;
   if (make_code_tmap(&ta, L.leaf_codes, L.leaf_rows, L.padded_dim, leaf::kBM) != 0) return TESSA_ERR_CUDA;
@@ -731,9 +851,9 @@ int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
   prm.tiles = L.d_tiles;
   prm.num_tiles = L.num_tiles;
   prm.num_slabs = slabs;
-  prm.num_bstages = (uint32_t)nst;
+  prm.num_bstages = nst;
   prm.k = L.k;
-  prm.h = L.k + leaf::kExtra < leaf::kSetSlots ? L.k + leaf::kExtra : leaf::kSetSlots;
+  prm.log_cap = log_cap;
   prm.resident_rows = L.resident_rows;
   prm.out_ids = L.out_ids;
   prm.out_dists = L.out_dists;
@@ -742,18 +862,25 @@ int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
   prm.fb_list = L.d_fb_list;
   prm.fb_capacity = L.fb_capacity;
   prm.timeout_ns = L.timeout_ns;
-  uint32_t smem = leaf::smem_bytes(slabs, (uint32_t)nst);
-  cudaError_t e = cudaFuncSetAttribute(leaf::leaf_topk_sq8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return TESSA_ERR_CUDA;
-  e = cudaMemsetAsync(L.d_fb_count, 0, 4, stream);
-  if (e != cudaSuccess) return TESSA_ERR_CUDA;
+  uint32_t smem = leaf::smem_bytes(slabs, nst, log_cap);
+  if (cudaMemsetAsync(L.d_fb_count, 0, 4, stream) != cudaSuccess) return TESSA_ERR_CUDA;
   uint32_t grid = L.num_tiles < (uint32_t)L.sm_count ? L.num_tiles : (uint32_t)L.sm_count;
-  leaf::leaf_topk_sq8_kernel<<<grid, leaf::kThreads, smem, stream>>>(ta, tb, prm);
-  if (cudaGetLastError() != cudaSuccess) return TESSA_ERR_CUDA;
+  int rc;
+  if (L.k <= 2)
+    rc = launch_main<2>(ta, tb, prm, smem, grid, stream);
+  else if (L.k <= 4)
+    rc = launch_main<4>(ta, tb, prm, smem, grid, stream);
+  else if (L.k <= 8)
+    rc = launch_main<8>(ta, tb, prm, smem, grid, stream);
+  else if (L.k <= 16)
+    rc = launch_main<16>(ta, tb, prm, smem, grid, stream);
+  else
+    rc = launch_main<32>(ta, tb, prm, smem, grid, stream);
+  if (rc != TESSA_OK) return rc;
   // Exact recomputation of the rows whose result depends on insertion order.
-  uint32_t fb_smem = 8u * L.padded_dim;  // one code row per warp
-  leaf::leaf_fallback_kernel<<<(unsigned)L.sm_count, 256, fb_smem, stream>>>(L.leaf_codes, L.padded_dim, prm);
+  uint32_t fb_smem = L.padded_dim + leaf::kFbBlock * 12u;
+  leaf::leaf_fallback_kernel<<<(unsigned)L.sm_count * 4u, leaf::kFbThreads, fb_smem, stream>>>(L.leaf_codes,
+                                                                                            L.padded_dim, prm);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 
