@@ -48,7 +48,7 @@
 //   warps 2..5  epilogue: thread t owns TMEM lane (leaf row) t; per 32
 //               columns it computes the exact reference distances, builds a
 //               bit mask of the ones below the row's bound (one funnel shift
-//               per column), stashes the distances in shared memory and then
+//               per column, four independent chains), stashes the distances in shared memory and then
 //               pops the marked columns into the log and the sorted array.
 //   warp 6      column metadata (scale, norm, global id) of each chunk into a
 //               4-slot shared-memory ring, so the epilogue warps never wait
@@ -181,15 +181,68 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // per slot.
 template <int KS>
 __device__ __forceinline__ void topk_insert2(float (&s)[KS], float x, float y) {
-  float n[KS];
+  // In place, ascending: slot t reads slots t+1 and t+2 before they change.
 #pragma unroll
   for (int t = 0; t < KS; ++t) {
-    float s1 = (t + 1 < KS) ? s[t + 1] : -INFINITY;
-    float s2 = (t + 2 < KS) ? s[t + 2] : -INFINITY;
-    n[t] = fmax3(s2, fminf(s1, y), fminf(s[t], x));
+    const float s1 = (t + 1 < KS) ? s[t + 1] : -INFINITY;
+    const float s2 = (t + 2 < KS) ? s[t + 2] : -INFINITY;
+    s[t] = fmax3(s2, fminf(s1, y), fminf(s[t], x));
+  }
+}
+
+// Bitonic sort of 32 register values, ascending (all indices compile-time).
+__device__ __forceinline__ void sort32_asc(float (&x)[32]) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const float a = x[i], b = x[j];
+          const bool up = (i & size) == 0;
+          x[i] = up ? fminf(a, b) : fmaxf(a, b);
+          x[j] = up ? fmaxf(a, b) : fminf(a, b);
+        }
+      }
+    }
+  }
+}
+
+// Merge 32 candidates (sorted ascending in x) into the sorted array s
+// (descending, KS <= 32 slots): min(s[t], x[t]) holds the KS smallest of both
+// as a bitonic sequence, which the half-cleaner stages sort descending.
+template <int KS>
+__device__ __forceinline__ void topk_merge32(float (&s)[KS], const float (&x)[32]) {
+  float m[KS];
+#pragma unroll
+  for (int t = 0; t < KS; ++t) m[t] = fminf(s[t], x[t]);
+#pragma unroll
+  for (int stride = KS >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+    for (int i = 0; i < KS; ++i) {
+      const int j = i ^ stride;
+      if (j > i) {
+        const float a = m[i], b = m[j];
+        m[i] = fmaxf(a, b);
+        m[j] = fminf(a, b);
+      }
+    }
   }
 #pragma unroll
-  for (int t = 0; t < KS; ++t) s[t] = n[t];
+  for (int t = 0; t < KS; ++t) s[t] = m[t];
+}
+
+// Take the next two marked columns (bit 31 - column, highest first) out of
+// `mask`; a missing one gets h = false and a harmless in-range index.
+__device__ __forceinline__ void next_pair(uint32_t& mask, bool& h0, uint32_t& c0, bool& h1, uint32_t& c1) {
+  h0 = mask != 0u;
+  c0 = h0 ? __clz(mask) : 0u;
+  mask &= ~(h0 ? (0x80000000u >> c0) : 0u);
+  h1 = mask != 0u;
+  c1 = h1 ? __clz(mask) : 0u;
+  mask &= ~(h1 ? (0x80000000u >> c1) : 0u);
 }
 
 // Keep the log entries of `row` with distance <= thr, in place.  Entries are
@@ -260,62 +313,75 @@ __device__ bool finish_row(const Params& p, uint2* log, uint8_t* perm, uint32_t 
   }
   if (occ != (E >= 64u ? ~0ull : ((1ull << E) - 1ull))) return false;  // not a permutation: give up safely
 
-  uint32_t q = 0;  // output slots written
-  uint32_t i = 0;
-  uint2 vi = E > 0 ? log[perm[0] * kBM + row] : make_uint2(0u, 0u);
-  while (q < k && i < E) {
-    float di = __uint_as_float(vi.x);
-    uint32_t e = i + 1;
-    float prev = di;
-    uint2 ve = make_uint2(0u, 0u);
-    while (e < E) {
-      ve = log[perm[e] * kBM + row];
-      float de = __uint_as_float(ve.x);
-      if (!(fabsf(__fsub_rn(de, prev)) <= kTieEps)) break;
-      prev = de;
-      ++e;
-    }
-    uint32_t len = e - i;
-    // The run holding rank k must end inside the zone: every candidate
-    // outside the zone lies above thr, hence more than eps above the run.
-    if (q + len >= k && e == E && !complete && !(__fsub_rn(thr, prev) > kTieEps)) return false;
-    if (len == 1) {
-      p.out_ids[out + q] = vi.y;
-      p.out_dists[out + q] = di;
-      ++q;
-    } else {
-      // Tournament of the run under the eps/id rule: transitive iff the win
-      // counts are 0..len-1 (then "<" orders the run by wins).
-      if (len > kMaxRun) return false;
-      float rd[kMaxRun];
-      uint32_t rg[kMaxRun];
-      for (uint32_t t = 0; t < len; ++t) {
-        uint2 v = log[perm[i + t] * kBM + row];
-        rd[t] = __uint_as_float(v.x);
-        rg[t] = v.y;
-      }
-      uint32_t wins[kMaxRun];
-      uint32_t seen = 0;
-      for (uint32_t t = 0; t < len; ++t) {
-        uint32_t w = 0;
-        for (uint32_t u = 0; u < len; ++u)
-          if (u != t && stable_better(rd[t], rg[t], rd[u], rg[u])) ++w;
-        wins[t] = w;
-        seen |= 1u << w;
-      }
-      if (seen != (1u << len) - 1u) return false;
-      for (uint32_t rank = 0; rank < len && q < k; ++rank) {
-        uint32_t want = len - 1 - rank;
-        for (uint32_t t = 0; t < len; ++t)
-          if (wins[t] == want) {
-            p.out_ids[out + q] = rg[t];
-            p.out_dists[out + q] = rd[t];
-          }
+  // One pass over the zone in sorted order.  A run (neighbours closer than
+  // eps) is emitted when it closes: runs of one and two directly, longer runs
+  // through the tournament check.
+  uint32_t q = 0;   // output slots written
+  uint32_t rs = 0;  // start of the current run
+  float prev = -INFINITY;
+  uint2 first = make_uint2(0u, 0u), second = make_uint2(0u, 0u);
+  for (uint32_t i = 0; i <= E && q < k; ++i) {
+    const bool end = i == E;
+    const uint2 vi = end ? make_uint2(0x7f800000u, 0u) : log[perm[i] * kBM + row];
+    const float di = __uint_as_float(vi.x);
+    const bool close = !end && i > 0 && fabsf(__fsub_rn(di, prev)) <= kTieEps;
+    if (i > 0 && !close) {
+      const uint32_t len = i - rs;  // run [rs, i) is complete
+      // The run holding rank k must end inside the zone: every candidate
+      // outside the zone lies above thr, hence more than eps above the run.
+      if (q + len >= k && end && !complete && !(__fsub_rn(thr, prev) > kTieEps)) return false;
+      if (len == 1) {
+        p.out_ids[out + q] = first.y;
+        p.out_dists[out + q] = __uint_as_float(first.x);
         ++q;
+      } else if (len == 2) {
+        // Two candidates: the eps/id rule orders them (trivially transitive).
+        const bool sw = stable_better(__uint_as_float(second.x), second.y, __uint_as_float(first.x), first.y);
+        const uint2 lo = sw ? second : first, hi = sw ? first : second;
+        p.out_ids[out + q] = lo.y;
+        p.out_dists[out + q] = __uint_as_float(lo.x);
+        ++q;
+        if (q < k) {
+          p.out_ids[out + q] = hi.y;
+          p.out_dists[out + q] = __uint_as_float(hi.x);
+          ++q;
+        }
+      } else {
+        // Tournament of the run under the eps/id rule: transitive iff the win
+        // counts are 0..len-1 (then "<" orders the run by wins).
+        if (len > kMaxRun) return false;
+        float rd[kMaxRun];
+        uint32_t rg[kMaxRun];
+        for (uint32_t t = 0; t < len; ++t) {
+          uint2 v = log[perm[rs + t] * kBM + row];
+          rd[t] = __uint_as_float(v.x);
+          rg[t] = v.y;
+        }
+        uint32_t wins[kMaxRun];
+        uint32_t seen = 0;
+        for (uint32_t t = 0; t < len; ++t) {
+          uint32_t w = 0;
+          for (uint32_t u = 0; u < len; ++u)
+            if (u != t && stable_better(rd[t], rg[t], rd[u], rg[u])) ++w;
+          wins[t] = w;
+          seen |= 1u << w;
+        }
+        if (seen != (1u << len) - 1u) return false;
+        for (uint32_t rank = 0; rank < len && q < k; ++rank) {
+          uint32_t want = len - 1 - rank;
+          for (uint32_t t = 0; t < len; ++t)
+            if (wins[t] == want) {
+              p.out_ids[out + q] = rg[t];
+              p.out_dists[out + q] = rd[t];
+            }
+          ++q;
+        }
       }
+      rs = i;
     }
-    i = e;
-    vi = ve;
+    if (i == rs) first = vi;
+    if (i == rs + 1) second = vi;
+    prev = di;
   }
   for (; q < k; ++q) {
     p.out_ids[out + q] = 0xffffffffu;
@@ -469,22 +535,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        // All member ids first, then all dependent loads, then the stores.
+        uint32_t lid[kBN / 32];
 #pragma unroll
         for (uint32_t u = 0; u < kBN / 32; ++u) {
           uint32_t col = c * kBN + u * 32 + lane;
-          float2 sn = make_float2(0.f, INFINITY);  // past the leaf: distance +inf
-          uint32_t g = 0xffffffffu;
-          if (col < cnt) {
-            uint32_t lid = __ldg(p.members + start + col);
-            if (lid < p.resident_rows) {
-              sn = make_float2(__ldg(p.scales + lid), __ldg(p.norms + lid));
-              g = __ldg(p.global_ids + lid);
-            } else {
-              atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
-            }
+          lid[u] = col < cnt ? __ldg(p.members + start + col) : 0xffffffffu;
+        }
+        float2 sn[kBN / 32];
+        uint32_t gv[kBN / 32];
+#pragma unroll
+        for (uint32_t u = 0; u < kBN / 32; ++u) {
+          sn[u] = make_float2(0.f, INFINITY);  // past the leaf: distance +inf
+          gv[u] = 0xffffffffu;
+          if (lid[u] < p.resident_rows) {
+            sn[u] = make_float2(__ldg(p.scales + lid[u]), __ldg(p.norms + lid[u]));
+            gv[u] = __ldg(p.global_ids + lid[u]);
+          } else if (lid[u] != 0xffffffffu) {
+            atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
           }
-          s.meta_sn[slot * kBN + u * 32 + lane] = sn;
-          s.meta_g[slot * kBN + u * 32 + lane] = g;
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kBN / 32; ++u) {
+          s.meta_sn[slot * kBN + u * 32 + lane] = sn[u];
+          s.meta_g[slot * kBN + u * 32 + lane] = gv[u];
         }
         mbar_arrive(&s.m_full[slot]);
       }
@@ -548,7 +622,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Exact reference distances; bit (31 - cc) of mask = column cc is
           // below the bound (the sign of d - thr, shifted in).
           float dc[32];
-          uint32_t mask = 0;
+          // Four independent 8-column chains keep the mask off the critical path.
+          uint32_t mq[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
           for (uint32_t cc = 0; cc < kGroup; cc += 2) {
             float4 m = msn[(g * kGroup + cc) >> 1];
@@ -563,43 +638,100 @@ __global__ void __launch_bounds__(kThreads, 1)
             float d1 = __fmaf_rn(-2.0f, u1, nn1);
             dc[cc] = d0;
             dc[cc + 1] = d1;
-            mask = __funnelshift_l(__float_as_uint(__fsub_rn(d0, thr)), mask, 1);
-            mask = __funnelshift_l(__float_as_uint(__fsub_rn(d1, thr)), mask, 1);
+            uint32_t& w = mq[cc >> 3];
+            w = __funnelshift_l(__float_as_uint(__fsub_rn(d0, thr)), w, 1);
+            w = __funnelshift_l(__float_as_uint(__fsub_rn(d1, thr)), w, 1);
           }
+          // Bit (31 - cc) of mask: column cc is below the bound (the sign of
+          // d - thr, shifted in).
+          uint32_t mask = (mq[0] << 24) | (mq[1] << 16) | (mq[2] << 8) | mq[3];
           float4* st = reinterpret_cast<float4*>(stash);
 #pragma unroll
           for (uint32_t q = 0; q < kGroup / 4; ++q)
             st[q] = make_float4(dc[4 * q], dc[4 * q + 1], dc[4 * q + 2], dc[4 * q + 3]);
           if (c == c_self && g == quad) mask &= ~(0x80000000u >> lane);  // the row itself
-          if (__any_sync(0xffffffffu, nlog + __popc(mask) > cap)) nlog = log_compact(s.log, row_in_tile, nlog, thr);
           const uint32_t* gg = mg + g * kGroup;
-          // Two candidates per step.  Both are logged if within the bound;
-          // the pair insertion is a no-op for values above the k-th smallest.
-#pragma unroll 1
-          while (mask) {
-            uint32_t c0 = __clz(mask);
-            mask ^= 0x80000000u >> c0;
-            uint32_t c1 = mask ? __clz(mask) : c0;
-            mask ^= mask ? (0x80000000u >> c1) : 0u;
-            float d0 = stash[c0], d1 = stash[c1];
-            uint32_t g0 = gg[c0], g1 = gg[c1];
-            d0 = d0 > 0.0f ? d0 : 0.0f;  // reference clamp (CB:8999-9001)
-            const bool two = c1 != c0;
-            d1 = two ? (d1 > 0.0f ? d1 : 0.0f) : INFINITY;
-            bool ok0 = d0 <= thr, ok1 = two && d1 <= thr;
-            if (nlog + 2u > cap) {  // rare: make room, or give the row to the fallback
-              nlog = log_compact(s.log, row_in_tile, nlog, thr);
-              if (nlog + 2u > cap) {
-                ovf = true;
-                ok0 = ok1 = false;
+          if (KS >= 16 && __reduce_max_sync(0xffffffffu, __popc(mask)) >= 8u) {
+            // Dense group (early in a row, most columns pass): sort all 32
+            // candidates and merge them into the sorted array at once, then
+            // log the ones within the new bound.
+            float x[32];
+#pragma unroll
+            for (uint32_t cc = 0; cc < kGroup; ++cc) {
+              dc[cc] = dc[cc] > 0.0f ? dc[cc] : 0.0f;  // reference clamp d <= 0 -> +0 (CB:8999-9001)
+              x[cc] = ((mask >> (31u - cc)) & 1u) ? dc[cc] : INFINITY;
+            }
+            sort32_asc(x);
+            topk_merge32<KS>(sk, x);
+            thr = __fadd_rn(sk[0], kMargin);
+            if (__any_sync(0xffffffffu, nlog + __popc(mask) > cap)) nlog = log_compact(s.log, row_in_tile, nlog, thr);
+            const uint4* gg4 = reinterpret_cast<const uint4*>(gg);
+#pragma unroll
+            for (uint32_t q4 = 0; q4 < kGroup / 4; ++q4) {
+              const uint4 gq = gg4[q4];
+              const uint32_t gv[4] = {gq.x, gq.y, gq.z, gq.w};
+#pragma unroll
+              for (uint32_t u = 0; u < 4; ++u) {
+                const uint32_t cc = 4 * q4 + u;
+                const bool ok = ((mask >> (31u - cc)) & 1u) && dc[cc] <= thr;
+                const bool w = ok && nlog < cap;
+                if (w) s.log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(dc[cc]), gv[u]);
+                nlog += w ? 1u : 0u;
+                ovf |= ok && !w;
               }
             }
-            if (ok0) s.log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(d0), g0);
-            nlog += ok0 ? 1u : 0u;
-            if (ok1) s.log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(d1), g1);
-            nlog += ok1 ? 1u : 0u;
-            topk_insert2<KS>(sk, fminf(d0, d1), fmaxf(d0, d1));
-            thr = __fadd_rn(sk[0], kMargin);
+            __syncwarp();
+            continue;
+          }
+          // Two candidates per step, the same number of steps in every lane
+          // (no divergence).  Both are logged if within the bound; the pair
+          // insertion is a no-op for values above the k-th smallest.  The
+          // next pair's shared-memory loads are issued before the current
+          // pair is inserted, so their latency hides behind the insertion.
+          const uint32_t steps = (__reduce_max_sync(0xffffffffu, __popc(mask)) + 1u) >> 1;
+          bool h0, h1;
+          uint32_t c0, c1;
+          next_pair(mask, h0, c0, h1, c1);
+          float a0 = stash[c0], a1 = stash[c1];
+          uint32_t g0 = gg[c0], g1 = gg[c1];
+          for (uint32_t it = 0; it < steps;) {
+            // Log room for a batch of steps (<= 2 appends each), so the
+            // steps themselves carry no capacity check.  Compacts rarely; a
+            // row that still cannot fit goes to the exact fallback.
+            uint32_t room = (cap - nlog) >> 1;
+            if (__any_sync(0xffffffffu, room < steps - it)) {
+              nlog = log_compact(s.log, row_in_tile, nlog, thr);
+              room = (cap - nlog) >> 1;
+            }
+            uint32_t batch = min(steps - it, __reduce_min_sync(0xffffffffu, room));
+            batch = batch > 0u ? batch : 1u;
+            const uint32_t end = it + batch;
+#pragma unroll 1
+            for (; it < end; ++it) {
+              bool nh0, nh1;
+              uint32_t nc0, nc1;
+              next_pair(mask, nh0, nc0, nh1, nc1);
+              const float na0 = stash[nc0], na1 = stash[nc1];
+              const uint32_t ng0 = gg[nc0], ng1 = gg[nc1];
+              const float d0 = h0 ? (a0 > 0.0f ? a0 : 0.0f) : INFINITY;  // reference clamp d <= 0 -> +0 (CB:8999-9001)
+              const float d1 = h1 ? (a1 > 0.0f ? a1 : 0.0f) : INFINITY;
+              const bool ok0 = h0 && d0 <= thr, ok1 = h1 && d1 <= thr;
+              const bool w0 = ok0 && nlog < cap;
+              const uint32_t e1 = nlog + (w0 ? 1u : 0u);
+              const bool w1 = ok1 && e1 < cap;
+              if (w0) s.log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(d0), g0);
+              if (w1) s.log[e1 * kBM + row_in_tile] = make_uint2(__float_as_uint(d1), g1);
+              nlog = e1 + (w1 ? 1u : 0u);
+              ovf |= (ok0 && !w0) || (ok1 && !w1);
+              topk_insert2<KS>(sk, fminf(d0, d1), fmaxf(d0, d1));
+              thr = __fadd_rn(sk[0], kMargin);
+              h0 = nh0;
+              h1 = nh1;
+              a0 = na0;
+              a1 = na1;
+              g0 = ng0;
+              g1 = ng1;
+            }
           }
           __syncwarp();
         }
