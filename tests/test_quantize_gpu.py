@@ -5,7 +5,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("rows,dim", [(2, 3), (257, 100), (1000, 768), (64, 1024)])
+@pytest.mark.parametrize("rows,dim", [(2, 3), (257, 100), (1000, 768), (64, 1024), (400_000, 8)])
 def test_quantize_matches_cpu_bits(oracle, rows, dim):
     import torch
     from shear_b200 import ops
