@@ -190,50 +190,6 @@ __device__ __forceinline__ void topk_insert2(float (&s)[KS], float x, float y) {
   }
 }
 
-// Bitonic sort of 32 register values, ascending (all indices compile-time).
-__device__ __forceinline__ void sort32_asc(float (&x)[32]) {
-#pragma unroll
-  for (int size = 2; size <= 32; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const float a = x[i], b = x[j];
-          const bool up = (i & size) == 0;
-          x[i] = up ? fminf(a, b) : fmaxf(a, b);
-          x[j] = up ? fmaxf(a, b) : fminf(a, b);
-        }
-      }
-    }
-  }
-}
-
-// Merge 32 candidates (sorted ascending in x) into the sorted array s
-// (descending, KS <= 32 slots): min(s[t], x[t]) holds the KS smallest of both
-// as a bitonic sequence, which the half-cleaner stages sort descending.
-template <int KS>
-__device__ __forceinline__ void topk_merge32(float (&s)[KS], const float (&x)[32]) {
-  float m[KS];
-#pragma unroll
-  for (int t = 0; t < KS; ++t) m[t] = fminf(s[t], x[t]);
-#pragma unroll
-  for (int stride = KS >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-    for (int i = 0; i < KS; ++i) {
-      const int j = i ^ stride;
-      if (j > i) {
-        const float a = m[i], b = m[j];
-        m[i] = fmaxf(a, b);
-        m[j] = fminf(a, b);
-      }
-    }
-  }
-#pragma unroll
-  for (int t = 0; t < KS; ++t) s[t] = m[t];
-}
-
 // Take the next two marked columns (bit 31 - column, highest first) out of
 // `mask`; a missing one gets h = false and a harmless in-range index.
 __device__ __forceinline__ void next_pair(uint32_t& mask, bool& h0, uint32_t& c0, bool& h1, uint32_t& c1) {
@@ -651,38 +607,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             st[q] = make_float4(dc[4 * q], dc[4 * q + 1], dc[4 * q + 2], dc[4 * q + 3]);
           if (c == c_self && g == quad) mask &= ~(0x80000000u >> lane);  // the row itself
           const uint32_t* gg = mg + g * kGroup;
-          if (KS >= 16 && __reduce_max_sync(0xffffffffu, __popc(mask)) >= 8u) {
-            // Dense group (early in a row, most columns pass): sort all 32
-            // candidates and merge them into the sorted array at once, then
-            // log the ones within the new bound.
-            float x[32];
-#pragma unroll
-            for (uint32_t cc = 0; cc < kGroup; ++cc) {
-              dc[cc] = dc[cc] > 0.0f ? dc[cc] : 0.0f;  // reference clamp d <= 0 -> +0 (CB:8999-9001)
-              x[cc] = ((mask >> (31u - cc)) & 1u) ? dc[cc] : INFINITY;
-            }
-            sort32_asc(x);
-            topk_merge32<KS>(sk, x);
-            thr = __fadd_rn(sk[0], kMargin);
-            if (__any_sync(0xffffffffu, nlog + __popc(mask) > cap)) nlog = log_compact(s.log, row_in_tile, nlog, thr);
-            const uint4* gg4 = reinterpret_cast<const uint4*>(gg);
-#pragma unroll
-            for (uint32_t q4 = 0; q4 < kGroup / 4; ++q4) {
-              const uint4 gq = gg4[q4];
-              const uint32_t gv[4] = {gq.x, gq.y, gq.z, gq.w};
-#pragma unroll
-              for (uint32_t u = 0; u < 4; ++u) {
-                const uint32_t cc = 4 * q4 + u;
-                const bool ok = ((mask >> (31u - cc)) & 1u) && dc[cc] <= thr;
-                const bool w = ok && nlog < cap;
-                if (w) s.log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(dc[cc]), gv[u]);
-                nlog += w ? 1u : 0u;
-                ovf |= ok && !w;
-              }
-            }
-            __syncwarp();
-            continue;
-          }
           // Two candidates per step, the same number of steps in every lane
           // (no divergence).  Both are logged if within the bound; the pair
           // insertion is a no-op for values above the k-th smallest.  The

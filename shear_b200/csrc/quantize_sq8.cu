@@ -27,7 +27,6 @@ __global__ void __launch_bounds__(kThreads)
                              float* __restrict__ norms, uint32_t* err_word) {
   __shared__ float tile[kWarps][32][33];
   __shared__ float wscale[kWarps][32];
-  __shared__ uint32_t wzero[kWarps];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint64_t nblk = (rows + 31) / 32;
   for (uint64_t blk = blockIdx.x * (uint64_t)kWarps + warp; blk < nblk; blk += (uint64_t)gridDim.x * kWarps) {
