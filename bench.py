@@ -395,7 +395,7 @@ def run_ours(a):
     cpu = None
     if not a.no_cpu_baseline and world == 1:
         from oracle import oracle as O
-        max_leaves = max(O.num_threads(), 1) * 4
+        max_leaves = max(O.num_threads(), 1) * 32  # ~10 s of OpenMP work; the time limit ends it
         host = host_sample(torch, w, min(a.leaves, max_leaves), a)
         v, thr, nl, dt = cpu_leaf_sample(O, host, a, a.cpu_seconds, min(a.leaves, max_leaves))
         cpu = {"value": v, "unit": "vectors/s", "cores": thr, "kind": "port",

@@ -146,6 +146,13 @@ TESSA_API int tessa_leaf_topk_sq8(tessa_ctx* ctx, const tessa_leaf_args* args, v
  * process_quantized_subtree_l2_compact_topk (CB:3693-3884) binds. */
 TESSA_API int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* args);
 
+/* Batch size (bytes of codes) of the host-buffer call's copy/compute pipeline,
+ * used when leaf_members is the identity and the leaves are in ascending,
+ * disjoint row order: batch b's upload, leaf kernel and download overlap
+ * those of its neighbours.  0 restores the default (128 MiB).  A library
+ * tuning knob with no reference counterpart; results do not depend on it. */
+TESSA_API int tessa_set_host_batch_bytes(tessa_ctx* ctx, uint64_t bytes);
+
 /* Rows of the context's last leaf call whose lists depended on insertion order
  * (eps-tie chains) and were recomputed with the exact sequential rule -- the
  * counterpart of the reference's leaf_exact_fallback_rows counter

@@ -108,6 +108,7 @@ SIGNATURES = [
     ("tessa_leaf_topk_sq8_host", ctypes.c_int, [c_vp, ctypes.POINTER(LeafArgs)]),
     ("tessa_leaf_topk_sq8_noalloc", ctypes.c_int, [ctypes.POINTER(LeafArgs), c_vp]),
     ("tessa_leaf_last_fallback_rows", ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint64)]),
+    ("tessa_set_host_batch_bytes", ctypes.c_int, [c_vp, ctypes.c_uint64]),
     ("tessa_assign", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(AssignArgs), c_vp]),
     ("tessa_replay_session_create", ctypes.c_int,
      [ctypes.c_int, ctypes.POINTER(PreparedReplay), ctypes.POINTER(c_vp)]),

@@ -46,6 +46,8 @@ int fail(int code, const char* fmt, ...) {
   } while (0)
 
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // bounded device waits: 2 s
+constexpr uint64_t kDefaultHostBatchBytes = 128ull << 20;  // codes per batch of the host-buffer pipeline
+constexpr uint64_t kMaxHostBatches = 64;
 
 // Grow-only device buffer.
 struct DevBuf {
@@ -215,6 +217,12 @@ struct tessa_ctx {
   DevBuf h_codes, h_scales, h_norms, h_gids, h_members, h_ids, h_dists, h_x;
   uint64_t timeout_ns = kDefaultTimeoutNs;
   uint64_t last_fallback_rows = 0;  // rows of the last leaf call recomputed by the exact fallback
+  // batched host-buffer pipeline: copy-in and copy-out streams, per-batch
+  // events and fallback-row counters (created on first use)
+  cudaStream_t stream_in = nullptr, stream_out = nullptr;
+  std::vector<cudaEvent_t> ev_in, ev_done;
+  DevBuf fb_counts;
+  uint64_t host_batch_bytes = kDefaultHostBatchBytes;
 };
 
 namespace {
@@ -236,9 +244,38 @@ int clear_err(tessa_ctx* ctx, cudaStream_t st) {
   return TESSA_OK;
 }
 
+// Blocked scans: the inner loops have no early exit, so they vectorise.
 bool members_identity(const uint32_t* m, uint64_t n) {
-  for (uint64_t i = 0; i < n; ++i)
-    if (m[i] != (uint32_t)i) return false;
+  for (uint64_t b = 0; b < n; b += 4096) {
+    const uint64_t e = n - b < 4096 ? n : b + 4096;
+    uint32_t diff = 0;
+    for (uint64_t i = b; i < e; ++i) diff |= m[i] ^ (uint32_t)i;
+    if (diff) return false;
+  }
+  return true;
+}
+
+// Index of the first entry >= bound, or n.
+uint64_t first_at_or_above(const uint32_t* m, uint64_t n, uint64_t bound) {
+  if (bound > 0xffffffffull) return n;
+  for (uint64_t b = 0; b < n; b += 4096) {
+    const uint64_t e = n - b < 4096 ? n : b + 4096;
+    uint32_t mx = 0;
+    for (uint64_t i = b; i < e; ++i) mx = m[i] > mx ? m[i] : mx;
+    if (mx >= bound)
+      for (uint64_t i = b; i < e; ++i)
+        if (m[i] >= bound) return i;
+  }
+  return n;
+}
+
+// Leaves in ascending start order with disjoint row ranges.
+bool leaves_ordered(const uint64_t* starts, const uint64_t* sizes, uint64_t n) {
+  uint64_t end = 0;
+  for (uint64_t l = 0; l < n; ++l) {
+    if (starts[l] < end) return false;
+    end = starts[l] + sizes[l];
+  }
   return true;
 }
 
@@ -259,6 +296,39 @@ int validate_leaf(const tessa_leaf_args* a) {
 }
 
 // Leaf op on device pointers (layout arrays on the host).
+// Launches the leaf kernel (and its exact fallback) over tiles
+// [tile0, tile0 + ntiles) of the current leaf plan on `st`, without waiting.
+// The fallback-row count of this launch lands in *d_fb_count.
+int leaf_launch_tiles(tessa_ctx* ctx, const tessa_leaf_args* a, const int8_t* lc, uint32_t tile0, uint32_t ntiles,
+                      uint32_t* d_fb_count, cudaStream_t st) {
+  if (ntiles == 0) return TESSA_OK;
+  LeafLaunch L;
+  L.leaf_codes = lc;
+  L.leaf_rows = a->leaf_rows;
+  L.padded_dim = a->padded_dim;
+  L.scales = a->scales;
+  L.norms = a->norms;
+  L.global_ids = a->global_ids;
+  L.members = a->leaf_members;
+  L.d_leaf_starts = ctx->leaf_plan.d_starts.as<uint64_t>();
+  L.d_leaf_sizes = ctx->leaf_plan.d_sizes.as<uint32_t>();
+  L.d_tiles = ctx->leaf_plan.d_tiles.as<uint2>() + tile0;
+  L.num_tiles = ntiles;
+  L.k = a->k;
+  L.out_ids = a->topk_ids;
+  L.out_dists = a->topk_dists;
+  L.d_err = ctx->d_err.as<uint32_t>();
+  L.d_fb_count = d_fb_count;
+  L.d_fb_list = reinterpret_cast<uint2*>(ctx->fallback.as<uint8_t>() + 16);
+  L.fb_capacity = (uint32_t)a->leaf_rows;
+  L.resident_rows = a->resident_rows;
+  L.timeout_ns = ctx->timeout_ns;
+  L.sm_count = ctx->sm_count;
+  int r = launch_leaf_topk_sq8(L, st);
+  if (r != TESSA_OK) return fail(r, "leaf kernel launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return TESSA_OK;
+}
+
 int leaf_device(tessa_ctx* ctx, const tessa_leaf_args* a, cudaStream_t st) {
   TRY(ctx->leaf_plan.build(a->leaf_starts, a->leaf_sizes, a->leaf_count, a->leaf_rows, st));
   if (ctx->leaf_plan.num_tiles == 0) return TESSA_OK;
@@ -270,36 +340,125 @@ int leaf_device(tessa_ctx* ctx, const tessa_leaf_args* a, cudaStream_t st) {
     lc = ctx->gather.as<int8_t>();
   }
   TRY(clear_err(ctx, st));
-  LeafLaunch L;
-  L.leaf_codes = lc;
-  L.leaf_rows = a->leaf_rows;
-  L.padded_dim = a->padded_dim;
-  L.scales = a->scales;
-  L.norms = a->norms;
-  L.global_ids = a->global_ids;
-  L.members = a->leaf_members;
-  L.d_leaf_starts = ctx->leaf_plan.d_starts.as<uint64_t>();
-  L.d_leaf_sizes = ctx->leaf_plan.d_sizes.as<uint32_t>();
-  L.d_tiles = ctx->leaf_plan.d_tiles.as<uint2>();
-  L.num_tiles = ctx->leaf_plan.num_tiles;
-  L.k = a->k;
-  L.out_ids = a->topk_ids;
-  L.out_dists = a->topk_dists;
-  L.d_err = ctx->d_err.as<uint32_t>();
   TRY(ctx->fallback.ensure(16 + (size_t)a->leaf_rows * 8));
-  L.d_fb_count = ctx->fallback.as<uint32_t>();
-  L.d_fb_list = reinterpret_cast<uint2*>(ctx->fallback.as<uint8_t>() + 16);
-  L.fb_capacity = (uint32_t)a->leaf_rows;
-  L.resident_rows = a->resident_rows;
-  L.timeout_ns = ctx->timeout_ns;
-  L.sm_count = ctx->sm_count;
-  int r = launch_leaf_topk_sq8(L, st);
-  if (r != TESSA_OK) return fail(r, "leaf kernel launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  uint32_t* d_fb = ctx->fallback.as<uint32_t>();
+  TRY(leaf_launch_tiles(ctx, a, lc, 0, ctx->leaf_plan.num_tiles, d_fb, st));
   uint32_t fb = 0;
-  CUDA_TRY(cudaMemcpyAsync(&fb, L.d_fb_count, 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaMemcpyAsync(&fb, d_fb, 4, cudaMemcpyDeviceToHost, st));
   uint32_t bits = 0;
   TRY(read_err(ctx, st, &bits));
   ctx->last_fallback_rows = fb;
+  return map_device_error(bits);
+}
+
+// Host-buffer leaf call when the members are the identity and the leaves are
+// ordered and disjoint (the layout a contiguous subtree build produces): the
+// member rows split into batches of whole leaves, and batch b's upload (copy
+// stream), leaf kernel (compute stream) and download (second copy stream)
+// overlap the neighbouring batches', so the call approaches the slowest of
+// the three instead of their sum.  Only rows [0, leaf_rows) travel: identity
+// members reference no other resident row.
+int leaf_host_pipelined(tessa_ctx* ctx, const tessa_leaf_args* a) {
+  const uint64_t M = a->leaf_rows, P = a->padded_dim, K = a->k;
+  cudaStream_t st = ctx->stream;
+  if (!ctx->stream_in) CUDA_TRY(cudaStreamCreateWithFlags(&ctx->stream_in, cudaStreamNonBlocking));
+  if (!ctx->stream_out) CUDA_TRY(cudaStreamCreateWithFlags(&ctx->stream_out, cudaStreamNonBlocking));
+  TRY(ctx->h_codes.ensure(M * P + 16));
+  TRY(ctx->h_scales.ensure(M * 4 + 4));
+  TRY(ctx->h_norms.ensure(M * 4 + 4));
+  TRY(ctx->h_gids.ensure(M * 4 + 4));
+  TRY(ctx->h_members.ensure(M * 4 + 4));
+  TRY(ctx->h_ids.ensure(M * K * 4 + 4));
+  TRY(ctx->h_dists.ensure(M * K * 4 + 4));
+  TRY(ctx->fallback.ensure(16 + M * 8));
+  TRY(ctx->leaf_plan.build(a->leaf_starts, a->leaf_sizes, a->leaf_count, M, st));
+
+  struct Batch {
+    uint64_t r0, r1;
+    uint32_t t0, nt;
+  };
+  std::vector<Batch> batches;
+  const uint64_t per_batch = ctx->host_batch_bytes / P;
+  const uint64_t min_rows = (M + kMaxHostBatches - 1) / kMaxHostBatches;
+  const uint64_t target = per_batch > min_rows ? per_batch : (min_rows ? min_rows : 1);
+  uint64_t r0 = 0;
+  uint32_t t = 0, t0 = 0;
+  for (uint64_t l = 0; l < a->leaf_count; ++l) {
+    t += (uint32_t)((a->leaf_sizes[l] + 127) / 128);
+    const uint64_t end = a->leaf_starts[l] + a->leaf_sizes[l];
+    const bool last = l + 1 == a->leaf_count;
+    if (last || end - r0 >= target) {
+      batches.push_back({r0, last ? M : end, t0, t - t0});
+      r0 = end;
+      t0 = t;
+    }
+  }
+  const size_t nb = batches.size();
+  while (ctx->ev_in.size() < nb) {
+    cudaEvent_t e;
+    CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    ctx->ev_in.push_back(e);
+  }
+  while (ctx->ev_done.size() < nb) {
+    cudaEvent_t e;
+    CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    ctx->ev_done.push_back(e);
+  }
+  TRY(ctx->fb_counts.ensure(nb * 4));
+
+  tessa_leaf_args d = *a;
+  d.codes = ctx->h_codes.as<int8_t>();
+  d.scales = ctx->h_scales.as<float>();
+  d.norms = ctx->h_norms.as<float>();
+  d.global_ids = ctx->h_gids.as<uint32_t>();
+  d.leaf_members = ctx->h_members.as<uint32_t>();
+  d.topk_ids = ctx->h_ids.as<uint32_t>();
+  d.topk_dists = ctx->h_dists.as<float>();
+  d.leaf_ordered_codes = d.codes;
+  d.resident_rows = M;
+
+  auto issue = [&]() -> int {
+    TRY(clear_err(ctx, st));
+    CUDA_TRY(cudaMemsetAsync(ctx->fb_counts.ptr, 0, nb * 4, st));
+    for (size_t b = 0; b < nb; ++b) {
+      const Batch& B = batches[b];
+      const uint64_t n = B.r1 - B.r0;
+      cudaStream_t si = ctx->stream_in, so = ctx->stream_out;
+      CUDA_TRY(cudaMemcpyAsync(ctx->h_codes.as<int8_t>() + B.r0 * P, a->codes + B.r0 * P, n * P,
+                               cudaMemcpyHostToDevice, si));
+      CUDA_TRY(cudaMemcpyAsync(ctx->h_scales.as<float>() + B.r0, a->scales + B.r0, n * 4, cudaMemcpyHostToDevice, si));
+      CUDA_TRY(cudaMemcpyAsync(ctx->h_norms.as<float>() + B.r0, a->norms + B.r0, n * 4, cudaMemcpyHostToDevice, si));
+      CUDA_TRY(cudaMemcpyAsync(ctx->h_gids.as<uint32_t>() + B.r0, a->global_ids + B.r0, n * 4,
+                               cudaMemcpyHostToDevice, si));
+      CUDA_TRY(cudaMemcpyAsync(ctx->h_members.as<uint32_t>() + B.r0, a->leaf_members + B.r0, n * 4,
+                               cudaMemcpyHostToDevice, si));
+      CUDA_TRY(cudaEventRecord(ctx->ev_in[b], si));
+      CUDA_TRY(cudaStreamWaitEvent(st, ctx->ev_in[b], 0));
+      TRY(leaf_launch_tiles(ctx, &d, d.codes, B.t0, B.nt, ctx->fb_counts.as<uint32_t>() + b, st));
+      CUDA_TRY(cudaEventRecord(ctx->ev_done[b], st));
+      CUDA_TRY(cudaStreamWaitEvent(so, ctx->ev_done[b], 0));
+      CUDA_TRY(cudaMemcpyAsync(a->topk_ids + B.r0 * K, ctx->h_ids.as<uint32_t>() + B.r0 * K, n * K * 4,
+                               cudaMemcpyDeviceToHost, so));
+      CUDA_TRY(cudaMemcpyAsync(a->topk_dists + B.r0 * K, ctx->h_dists.as<float>() + B.r0 * K, n * K * 4,
+                               cudaMemcpyDeviceToHost, so));
+    }
+    return TESSA_OK;
+  };
+  const int r = issue();
+  // drain every stream before reporting, on success and failure alike
+  const cudaError_t e_in = cudaStreamSynchronize(ctx->stream_in);
+  const cudaError_t e_st = cudaStreamSynchronize(st);
+  const cudaError_t e_out = cudaStreamSynchronize(ctx->stream_out);
+  if (r != TESSA_OK) return r;
+  for (cudaError_t e : {e_in, e_st, e_out})
+    if (e != cudaSuccess) return fail(TESSA_ERR_CUDA, "leaf pipeline: %s", cudaGetErrorString(e));
+  std::vector<uint32_t> fb(nb);
+  CUDA_TRY(cudaMemcpyAsync(fb.data(), ctx->fb_counts.ptr, nb * 4, cudaMemcpyDeviceToHost, st));
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  uint64_t total = 0;
+  for (uint32_t c : fb) total += c;
+  ctx->last_fallback_rows = total;
   return map_device_error(bits);
 }
 
@@ -408,8 +567,15 @@ void tessa_destroy(tessa_ctx* ctx) {
   ctx->leaf_plan.release();
   ctx->assign_plan.release();
   DevBuf* bufs[] = {&ctx->h_codes, &ctx->h_scales, &ctx->h_norms, &ctx->h_gids, &ctx->h_members,
-                    &ctx->h_ids, &ctx->h_dists, &ctx->h_x};
+                    &ctx->h_ids, &ctx->h_dists, &ctx->h_x, &ctx->fb_counts};
   for (DevBuf* b : bufs) b->release();
+  for (cudaStream_t s : {ctx->stream_in, ctx->stream_out})
+    if (s) {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  for (cudaEvent_t e : ctx->ev_in) cudaEventDestroy(e);
+  for (cudaEvent_t e : ctx->ev_done) cudaEventDestroy(e);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -468,16 +634,26 @@ int tessa_leaf_topk_sq8(tessa_ctx* ctx, const tessa_leaf_args* args, void* strea
   return leaf_device(ctx, args, (cudaStream_t)stream);
 }
 
+int tessa_set_host_batch_bytes(tessa_ctx* ctx, uint64_t bytes) {
+  if (!ctx) return fail(TESSA_ERR_INVALID_ARG, "null context");
+  ctx->host_batch_bytes = bytes ? bytes : kDefaultHostBatchBytes;
+  return TESSA_OK;
+}
+
 int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* a) {
   TRY(bind(ctx));
   TRY(validate_leaf(a));
-  for (uint64_t i = 0; i < a->leaf_rows; ++i)
-    if (a->leaf_members[i] >= a->resident_rows)
-      return fail(TESSA_ERR_BAD_ROW, "leaf member %llu = %u outside %llu resident rows", (unsigned long long)i,
-                  a->leaf_members[i], (unsigned long long)a->resident_rows);
-  cudaStream_t st = ctx->stream;
   const uint64_t R = a->resident_rows, M = a->leaf_rows, P = a->padded_dim;
-  bool ident = (M <= R) && members_identity(a->leaf_members, M);
+  const bool ident = (M <= R) && members_identity(a->leaf_members, M);
+  if (!ident) {
+    uint64_t i = first_at_or_above(a->leaf_members, M, R);
+    if (i < M)
+      return fail(TESSA_ERR_BAD_ROW, "leaf member %llu = %u outside %llu resident rows", (unsigned long long)i,
+                  a->leaf_members[i], (unsigned long long)R);
+  }
+  if (ident && a->leaf_count && leaves_ordered(a->leaf_starts, a->leaf_sizes, a->leaf_count))
+    return leaf_host_pipelined(ctx, a);
+  cudaStream_t st = ctx->stream;
   TRY(ctx->h_codes.ensure(R * P + 16));
   TRY(ctx->h_scales.ensure(R * 4 + 4));
   TRY(ctx->h_norms.ensure(R * 4 + 4));

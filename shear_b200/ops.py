@@ -160,11 +160,14 @@ def leaf_topk_sq8(codes, scales, norms, global_ids, leaf_members, leaf_starts, l
 
 
 def leaf_topk_sq8_host(codes, scales, norms, global_ids, leaf_members, leaf_starts, leaf_sizes, k: int,
-                       device: int = 0, out=None):
+                       device: int = 0, out=None, batch_bytes: int | None = None):
     """Host-buffer form: numpy arrays in, numpy (ids uint32, dists f32) out.
 
     Pinned host arrays (e.g. ``torch.empty(..., pin_memory=True).numpy()``)
-    make the copies inside the call run at full link speed.
+    make the copies inside the call run at full link speed.  With identity
+    members and ordered, disjoint leaves the call pipelines upload, kernel and
+    download in batches of ``batch_bytes`` bytes of codes (None keeps the
+    context's setting; 0 restores the 128 MiB default).
     """
     codes = np.ascontiguousarray(codes, dtype=np.int8)
     scales = np.ascontiguousarray(scales, dtype=np.float32)
@@ -183,8 +186,16 @@ def leaf_topk_sq8_host(codes, scales, norms, global_ids, leaf_members, leaf_star
                    k=k, leaf_members=members.ctypes.data, leaf_starts=starts.ctypes.data,
                    leaf_sizes=sizes.ctypes.data, leaf_count=starts.shape[0], leaf_rows=members.shape[0],
                    topk_ids=ids.ctypes.data, topk_dists=dists.ctypes.data, leaf_ordered_codes=None)
+    if batch_bytes is not None:
+        set_host_batch_bytes(batch_bytes, device=device)
     C.check(C.load().tessa_leaf_topk_sq8_host(context(device).handle, ctypes.byref(a)))
     return ids, dists
+
+
+def set_host_batch_bytes(batch_bytes: int, ctx: Context | None = None, device: int = 0) -> None:
+    """Bytes of codes per batch of the host-buffer pipeline (0 = default 128 MiB)."""
+    ctx = ctx or context(device)
+    C.check(C.load().tessa_set_host_batch_bytes(ctx.handle, int(batch_bytes)))
 
 
 def leaf_last_fallback_rows(ctx: Context | None = None, device: int = 0) -> int:

@@ -71,6 +71,62 @@ def test_leaf_host_api_matches_oracle(oracle):
     _assert_same(got, oracle_leaf(oracle, c, 32))
 
 
+def _host_run(c, k, batch_bytes=None):
+    from shear_b200 import ops
+    try:
+        return ops.leaf_topk_sq8_host(c["codes"], c["scales"], c["norms"], c["gids"], c["members"], c["starts"],
+                                      c["sizes"], k, batch_bytes=batch_bytes)
+    finally:
+        ops.set_host_batch_bytes(0)
+
+
+@pytest.mark.parametrize("k", [2, 9, 32])
+def test_leaf_host_pipeline_batches_match_oracle(oracle, k):
+    # identity members + ordered leaves take the batched upload/kernel/download
+    # pipeline; ~256 rows of codes per batch gives many batches of whole leaves
+    c = make_leaf_batch(oracle, [300, 129, 512, 77, 1000, 2, 640, 128], 768, seed=31 + k, dup=True)
+    want = oracle_leaf(oracle, c, k)
+    _assert_same(_host_run(c, k, batch_bytes=256 * 768), want)
+    _assert_same(_host_run(c, k, batch_bytes=1), want)
+    _assert_same(_host_run(c, k), want)
+
+
+def test_leaf_host_pipeline_with_gaps_between_leaves(oracle):
+    # rows outside every leaf are not compared (no leaf writes them)
+    c = make_leaf_batch(oracle, [850], 256, seed=8)
+    c["starts"] = np.array([5, 300, 700], np.uint64)
+    c["sizes"] = np.array([200, 390, 100], np.uint64)
+    k = 6
+    wi, wd = oracle_leaf(oracle, c, k)
+    gi, gd = _host_run(c, k, batch_bytes=150 * 256)
+    rows = np.concatenate([np.arange(int(s), int(s + n)) for s, n in zip(c["starts"], c["sizes"])])
+    slots = (rows[:, None] * k + np.arange(k)[None, :]).ravel()
+    _assert_same((gi[slots], gd[slots]), (wi[slots], wd[slots]))
+
+
+def test_leaf_host_unordered_leaves_take_serial_path(oracle):
+    c = make_leaf_batch(oracle, [200, 300, 100], 128, seed=4)
+    c["starts"] = np.array([500, 0, 200], np.uint64)
+    c["sizes"] = np.array([100, 200, 300], np.uint64)
+    _assert_same(_host_run(c, 5, batch_bytes=64 * 128), oracle_leaf(oracle, c, 5))
+
+
+def test_leaf_host_pipeline_sums_fallback_rows(oracle):
+    from shear_b200 import ops
+    rng = np.random.default_rng(78)
+    def formula(rows, dim):
+        base = rng.standard_normal(dim).astype(np.float32)
+        x = base[None, :] + rng.standard_normal((rows, dim)).astype(np.float32) * np.float32(2e-3)
+        return x / np.linalg.norm(x, axis=1, keepdims=True)
+    c = make_leaf_batch(oracle, [700, 300, 500], 128, seed=3, formula=formula)
+    _device_run(c, 8)
+    want_fb = ops.leaf_last_fallback_rows()
+    assert want_fb > 0
+    got = _host_run(c, 8, batch_bytes=128 * 300)
+    assert ops.leaf_last_fallback_rows() == want_fb
+    _assert_same(got, oracle_leaf(oracle, c, 8))
+
+
 def test_leaf_duplicate_local_ids_are_all_skipped(oracle):
     # CB:9569-9650 skips every column whose local id equals the row's
     c = make_leaf_batch(oracle, [40], 64, seed=9)
