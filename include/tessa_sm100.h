@@ -217,6 +217,47 @@ typedef struct tessa_assign_args {
  * arrays, which are HOST pointers (the library uploads them). */
 TESSA_API int tessa_assign(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* args, void* stream);
 
+/* ------------------------------------------------------------ global D0 --- */
+
+/* Global-D0 SQ8 staging, the compute-backend trait method
+ * quantize_sq8_and_assign_global_d0 (trait CB:3828-3837; CUDA implementation
+ * CB:24281-24760 with kernels CB:17955-18112, 18114, 18446; CPU reference
+ * quantize_sq8_and_assign_global_d0_reference, P/dco_sq_int8.rs:1929-2070,
+ * called from P/rbc_partition.rs:8429).  Quantizes a batch of raw rows to SQ8
+ * (CPU quantizer bits, P/dco_sq_int8.rs:1331-1466) and assigns every row to
+ * its fanout_top nearest global D0 leaders by SQ8 distance (CB:8987-9002
+ * rounding), ordered by the stable eps/id rule on (distance, leader id)
+ * (P/mod.rs:417-428).  Output fragment (row, slot) = (child_ids, point_ids)
+ * at row * fanout_top + slot: the leader INDEX (0..leader_count) and the
+ * row's global id, best leader first -- the reference's D0AssignmentFragment
+ * list (P/dco_sq_int8.rs:2055-2060) as two arrays. */
+typedef struct tessa_d0_args {
+  const float* raw_vectors;     /* rows x dim f32, row-major */
+  const uint32_t* global_ids;   /* rows */
+  uint64_t rows;
+  uint32_t dim;                 /* padded_dim = ceil(dim / 16) * 16 */
+  uint32_t fanout_top;          /* 1 .. min(32, leader_count) */
+  const uint32_t* leader_ids;   /* leader_count global D0 leader ids (tie order) */
+  const float* leader_vectors;  /* leader_count x dim f32; used when leader_codes is NULL */
+  const int8_t* leader_codes;   /* optional SQ8 leader payload, leader_count x padded_dim */
+  const float* leader_scales;   /* with leader_codes: leader_count */
+  const float* leader_norms;    /* with leader_codes: leader_count */
+  uint32_t leader_count;
+  int8_t* codes;                /* out: rows x padded_dim */
+  float* scales;                /* out: rows */
+  float* norms;                 /* out: rows */
+  uint32_t* child_ids;          /* out: rows x fanout_top leader indices */
+  uint32_t* point_ids;          /* out: rows x fanout_top (= global_ids[row]) */
+  float* dists;                 /* optional out: rows x fanout_top SQ8 distances (NULL = not written) */
+} tessa_d0_args;
+
+/* Device-pointer form: every array is a device pointer except leader_ids,
+ * which may be either (it is read on the host to build the tie keys). */
+TESSA_API int tessa_quantize_sq8_assign_d0(tessa_ctx* ctx, const tessa_d0_args* args, void* stream);
+/* Host-pointer form: every array is a host pointer; the call uploads, runs
+ * and downloads (the form the trait method binds). */
+TESSA_API int tessa_quantize_sq8_assign_d0_host(tessa_ctx* ctx, const tessa_d0_args* args);
+
 /* ------------------------------------------------------- replay session --- */
 
 /* TessaPreparedReplay (P/tessa_replay.rs:1052-1074) as host arrays. */

@@ -61,6 +61,10 @@ def _declare(L):
                                        u64, u32, _p(np.uint32), _p(np.uint64), _p(np.uint64), u64,
                                        u32, u32, u32, _p(np.uint32), _p(np.float32)]
     L.oracle_hash64.restype = u64
+    L.oracle_d0_assign_sq8.restype = ctypes.c_int
+    L.oracle_d0_assign_sq8.argtypes = [_p(np.int8), _p(np.float32), _p(np.float32), u64, u32, _p(np.int8),
+                                       _p(np.float32), _p(np.float32), _p(np.uint32), u32, u32,
+                                       _p(np.uint32), _p(np.float32)]
     L.oracle_hash64.argtypes = [u64]
     L.oracle_assignment_tie_key.restype = u64
     L.oracle_assignment_tie_key.argtypes = [u32, u32]
@@ -128,6 +132,49 @@ def leaf_topk_sq8(codes, scales, norms, global_ids, leaf_members, leaf_offsets, 
     if rc != 0:
         raise ValueError(f"oracle leaf top-k failed (code {rc})")
     return ids, dists
+
+
+def d0_assign(raw_vectors, global_ids, leader_ids, leader_vectors, fanout_top, leader_payload=None):
+    """P/dco_sq_int8.rs:1929-2070 quantize_sq8_and_assign_global_d0_reference.
+
+    Returns dict(codes, scales, norms, child_ids [rows, fanout] (leader
+    indices, best first), point_ids [rows, fanout], dists [rows, fanout]).
+    leader_payload = (codes, scales, norms) replaces quantizing leader_vectors.
+    Raises ValueError with the reference's messages on invalid requests.
+    """
+    raw = np.ascontiguousarray(raw_vectors, dtype=np.float32)
+    gids = np.ascontiguousarray(global_ids, dtype=np.uint32)
+    lids = np.ascontiguousarray(leader_ids, dtype=np.uint32)
+    rows, leaders = gids.shape[0], lids.shape[0]
+    if rows == 0:
+        raise ValueError("SQ GPU-D0 staging requires at least one input row")
+    dim = raw.shape[1] if raw.ndim == 2 else (raw.size // rows if rows else 0)
+    if dim == 0:
+        raise ValueError("SQ GPU-D0 staging requires dim > 0")
+    if leaders == 0:
+        raise ValueError("SQ GPU-D0 staging requires at least one global D0 leader")
+    if fanout_top == 0 or fanout_top > leaders or fanout_top > 32:
+        raise ValueError(f"SQ GPU-D0 staging fanout must be in 1..=min(32, leaders), got fanout={fanout_top} "
+                         f"leaders={leaders}")
+    raw = raw.reshape(rows, dim)
+    codes, scales, norms = quantize_sq8(raw)
+    if leader_payload is None:
+        lcodes, lscales, lnorms = quantize_sq8(np.ascontiguousarray(leader_vectors, np.float32).reshape(leaders, dim))
+    else:
+        lcodes, lscales, lnorms = (np.ascontiguousarray(leader_payload[0], np.int8),
+                                   np.ascontiguousarray(leader_payload[1], np.float32),
+                                   np.ascontiguousarray(leader_payload[2], np.float32))
+        if lcodes.shape != (leaders, codes.shape[1]):
+            raise ValueError("SQ GPU-D0 staging leader payload shape mismatch")
+    child = np.zeros(rows * fanout_top, dtype=np.uint32)
+    dists = np.zeros(rows * fanout_top, dtype=np.float32)
+    rc = lib().oracle_d0_assign_sq8(codes.reshape(-1), scales, norms, rows, codes.shape[1], lcodes.reshape(-1),
+                                    lscales, lnorms, lids, leaders, fanout_top, child, dists)
+    if rc != 0:
+        raise ValueError(f"oracle D0 assignment failed (code {rc})")
+    return dict(codes=codes, scales=scales, norms=norms, child_ids=child.reshape(rows, fanout_top),
+                point_ids=np.repeat(gids, fanout_top).reshape(rows, fanout_top),
+                dists=dists.reshape(rows, fanout_top))
 
 
 def assign(mode, x, norms, codes, scales, global_ids, members, leaders, task_member_offsets,

@@ -232,6 +232,64 @@ int oracle_leaf_topk_sq8(const int8_t* codes, const float* scales, const float* 
     return ORACLE_OK;
 }
 
+/* ------------------------------------------------------ global D0 --- */
+
+/*
+ * P/dco_sq_int8.rs:1929-2070 quantize_sq8_and_assign_global_d0_reference, the
+ * assignment half (the caller quantizes rows and leaders with
+ * oracle_quantize_sq8, P/dco_sq_int8.rs:1994-2035): for every row the SQ8
+ * distance to every leader (sq_int8_approx_l2, P/dco_sq_int8.rs:2950-2965 =
+ * oracle_sq8_l2_from_dot), the candidates ordered by stable_distance_order on
+ * (distance, leader id) (P/mod.rs:417-428), the first fanout leader INDICES
+ * kept, best first (P/dco_sq_int8.rs:2037-2061).
+ *
+ * The reference orders all candidates with sort_unstable_by under the eps/id
+ * rule.  Restated as bounded sequential insertion in ascending leader index
+ * under the same rule (insert_topk): where the rule orders the row's
+ * candidates consistently the two agree; where eps-tie chains make it
+ * inconsistent the sort's result depends on its internal comparison order,
+ * and the sequential form is the one defined here (the same rule as the leaf
+ * path).  A leader id repeated within eps keeps the earlier index first.
+ */
+static inline void insert_topk_idx(float d, uint32_t id, uint32_t idx, uint32_t k, float* bd,
+                                   uint32_t* bi, uint32_t* bx) {
+    if (!better(d, id, bd[k - 1], bi[k - 1])) return;
+    uint32_t pos = k - 1;
+    while (pos > 0 && better(d, id, bd[pos - 1], bi[pos - 1])) {
+        bd[pos] = bd[pos - 1];
+        bi[pos] = bi[pos - 1];
+        bx[pos] = bx[pos - 1];
+        --pos;
+    }
+    bd[pos] = d;
+    bi[pos] = id;
+    bx[pos] = idx;
+}
+
+int oracle_d0_assign_sq8(const int8_t* codes, const float* scales, const float* norms, uint64_t rows,
+                         uint32_t padded_dim, const int8_t* leader_codes, const float* leader_scales,
+                         const float* leader_norms, const uint32_t* leader_ids, uint32_t leaders,
+                         uint32_t fanout, uint32_t* child_ids, float* dists) {
+    if (fanout == 0 || fanout > MAX_K || fanout > leaders) return ORACLE_ERR_ARG;
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t r = 0; r < (int64_t)rows; ++r) {
+        float bd[MAX_K];
+        uint32_t bi[MAX_K], bx[MAX_K];
+        for (uint32_t s = 0; s < fanout; ++s) { bd[s] = EMPTY_DIST; bi[s] = EMPTY_ID; bx[s] = EMPTY_ID; }
+        const int8_t* rc = codes + (uint64_t)r * padded_dim;
+        for (uint32_t j = 0; j < leaders; ++j) {
+            int32_t dot = oracle_sq8_dot(rc, leader_codes + (uint64_t)j * padded_dim, padded_dim);
+            float d = oracle_sq8_l2_from_dot(dot, scales[r], norms[r], leader_scales[j], leader_norms[j]);
+            insert_topk_idx(d, leader_ids[j], j, fanout, bd, bi, bx);
+        }
+        for (uint32_t s = 0; s < fanout; ++s) {
+            child_ids[(uint64_t)r * fanout + s] = bx[s];
+            if (dists) dists[(uint64_t)r * fanout + s] = bd[s];
+        }
+    }
+    return ORACLE_OK;
+}
+
 /* --------------------------------------------------------- assignment --- */
 
 /* CB:5983-5989 gpu_persistent_hash64 (splitmix64 finaliser). */

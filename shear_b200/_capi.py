@@ -68,6 +68,16 @@ class AssignArgs(ctypes.Structure):
     ]
 
 
+class D0Args(ctypes.Structure):
+    _fields_ = [
+        ("raw_vectors", c_vp), ("global_ids", c_vp), ("rows", ctypes.c_uint64), ("dim", ctypes.c_uint32),
+        ("fanout_top", ctypes.c_uint32), ("leader_ids", c_vp), ("leader_vectors", c_vp),
+        ("leader_codes", c_vp), ("leader_scales", c_vp), ("leader_norms", c_vp),
+        ("leader_count", ctypes.c_uint32), ("codes", c_vp), ("scales", c_vp), ("norms", c_vp),
+        ("child_ids", c_vp), ("point_ids", c_vp), ("dists", c_vp),
+    ]
+
+
 class PreparedReplay(ctypes.Structure):
     _fields_ = [
         ("dim", ctypes.c_uint32), ("padded_dim", ctypes.c_uint32), ("resident_rows", ctypes.c_uint64),
@@ -110,6 +120,8 @@ SIGNATURES = [
     ("tessa_leaf_last_fallback_rows", ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint64)]),
     ("tessa_set_host_batch_bytes", ctypes.c_int, [c_vp, ctypes.c_uint64]),
     ("tessa_assign", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(AssignArgs), c_vp]),
+    ("tessa_quantize_sq8_assign_d0", ctypes.c_int, [c_vp, ctypes.POINTER(D0Args), c_vp]),
+    ("tessa_quantize_sq8_assign_d0_host", ctypes.c_int, [c_vp, ctypes.POINTER(D0Args)]),
     ("tessa_replay_session_create", ctypes.c_int,
      [ctypes.c_int, ctypes.POINTER(PreparedReplay), ctypes.POINTER(c_vp)]),
     ("tessa_replay_run_mode", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(ModeResult)]),

@@ -4,10 +4,12 @@
 // CB:34597-35305).  No exception or abort crosses the ABI: every entry point
 // returns TESSA_OK or a negative TESSA_ERR_* code and records a message for
 // tessa_last_error_message().
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <numeric>
 #include <string>
 #include <vector>
 
@@ -223,6 +225,10 @@ struct tessa_ctx {
   std::vector<cudaEvent_t> ev_in, ev_done;
   DevBuf fb_counts;
   uint64_t host_batch_bytes = kDefaultHostBatchBytes;
+  // global-D0 staging: leader payload, tie keys, key -> leader, top-k keys,
+  // and the host form's extra staging
+  DevBuf d0_lcodes, d0_lscales, d0_lnorms, d0_keys, d0_k2l, d0_okeys, d0_dists, d0_lvec, d0_lids, d0_child,
+      d0_point;
 };
 
 namespace {
@@ -462,6 +468,114 @@ int leaf_host_pipelined(tessa_ctx* ctx, const tessa_leaf_args* a) {
   return map_device_error(bits);
 }
 
+// ------------------------------------------------------------- global D0
+
+int validate_d0(const tessa_d0_args* a) {
+  if (!a) return fail(TESSA_ERR_INVALID_ARG, "null D0 args");
+  // P/dco_sq_int8.rs:1932-1960 (messages as the reference's)
+  if (a->rows == 0) return fail(TESSA_ERR_INVALID_ARG, "SQ GPU-D0 staging requires at least one input row");
+  if (a->dim == 0) return fail(TESSA_ERR_INVALID_ARG, "SQ GPU-D0 staging requires dim > 0");
+  if (a->leader_count == 0)
+    return fail(TESSA_ERR_INVALID_ARG, "SQ GPU-D0 staging requires at least one global D0 leader");
+  if (a->fanout_top == 0 || a->fanout_top > a->leader_count || a->fanout_top > 32)
+    return fail(TESSA_ERR_INVALID_ARG,
+                "SQ GPU-D0 staging fanout must be in 1..=min(32, leaders), got fanout=%u leaders=%u", a->fanout_top,
+                a->leader_count);
+  if (!a->raw_vectors || !a->global_ids || !a->leader_ids || !a->codes || !a->scales || !a->norms ||
+      !a->child_ids || !a->point_ids)
+    return fail(TESSA_ERR_INVALID_ARG, "null D0 data pointer");
+  if (!a->leader_codes && !a->leader_vectors)
+    return fail(TESSA_ERR_INVALID_ARG, "D0 leaders need leader_vectors or a leader payload");
+  if (a->leader_codes && (!a->leader_scales || !a->leader_norms))
+    return fail(TESSA_ERR_INVALID_ARG, "D0 leader payload without scales or norms");
+  const uint64_t P = ((uint64_t)a->dim + 15) / 16 * 16;
+  if (P > TESSA_MAX_PADDED_DIM || leaf_num_bstages((uint32_t)P) == 0)
+    return fail(TESSA_ERR_UNSUPPORTED, "padded_dim=%llu above the supported %d", (unsigned long long)P,
+                TESSA_MAX_PADDED_DIM);
+  if (a->rows > kMaxRectRows) return fail(TESSA_ERR_UNSUPPORTED, "more than %llu D0 rows in one call",
+                                          (unsigned long long)kMaxRectRows);
+  return TESSA_OK;
+}
+
+// Tie keys of the leaders: key[j] = rank of (leader_ids[j], j) in
+// lexicographic order.  "key_a < key_b" orders two leaders exactly as their
+// ids do and breaks equal ids by index (the earlier leader first, as the
+// sequential reading of the reference's stable order does), so the keys are
+// distinct and the eps/id rule on keys is the rule on ids.
+void d0_tie_keys(const uint32_t* ids, uint32_t n, std::vector<uint32_t>& key, std::vector<uint32_t>& key_to_leader) {
+  key_to_leader.resize(n);
+  std::iota(key_to_leader.begin(), key_to_leader.end(), 0u);
+  std::stable_sort(key_to_leader.begin(), key_to_leader.end(),
+                   [ids](uint32_t a, uint32_t b) { return ids[a] < ids[b]; });
+  key.resize(n);
+  for (uint32_t r = 0; r < n; ++r) key[key_to_leader[r]] = r;
+}
+
+// Device-pointer D0 staging; h_leader_ids is a host copy of the leader ids.
+int d0_device(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_ids, cudaStream_t st) {
+  const uint64_t rows = a->rows;
+  const uint32_t dim = a->dim, L = a->leader_count, f = a->fanout_top;
+  const uint32_t P = (dim + 15u) / 16u * 16u;
+  std::vector<uint32_t> key, k2l;
+  d0_tie_keys(h_leader_ids, L, key, k2l);
+  TRY(ctx->d0_keys.ensure((size_t)L * 4));
+  TRY(ctx->d0_k2l.ensure((size_t)L * 4));
+  TRY(ctx->d0_okeys.ensure(rows * f * 4));
+  TRY(ctx->fallback.ensure(16 + rows * 8));
+  if (!a->dists) TRY(ctx->d0_dists.ensure(rows * f * 4));
+  CUDA_TRY(cudaMemcpyAsync(ctx->d0_keys.ptr, key.data(), (size_t)L * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(ctx->d0_k2l.ptr, k2l.data(), (size_t)L * 4, cudaMemcpyHostToDevice, st));
+  TRY(clear_err(ctx, st));
+  const int8_t* lc = a->leader_codes;
+  const float* ls = a->leader_scales;
+  const float* ln = a->leader_norms;
+  if (!lc) {
+    TRY(ctx->d0_lcodes.ensure((size_t)L * P));
+    TRY(ctx->d0_lscales.ensure((size_t)L * 4));
+    TRY(ctx->d0_lnorms.ensure((size_t)L * 4));
+    TRY(launch_quantize_sq8(a->leader_vectors, L, dim, P, 8, ctx->d0_lcodes.as<int8_t>(), ctx->d0_lscales.as<float>(),
+                            ctx->d0_lnorms.as<float>(), ctx->d_err.as<uint32_t>(), st));
+    lc = ctx->d0_lcodes.as<int8_t>();
+    ls = ctx->d0_lscales.as<float>();
+    ln = ctx->d0_lnorms.as<float>();
+  }
+  TRY(launch_quantize_sq8(a->raw_vectors, rows, dim, P, 8, a->codes, a->scales, a->norms, ctx->d_err.as<uint32_t>(),
+                          st));
+  RectLaunch R;
+  R.row_codes = a->codes;
+  R.rows = rows;
+  R.padded_dim = P;
+  R.row_scales = a->scales;
+  R.row_norms = a->norms;
+  R.col_codes = lc;
+  R.cols = L;
+  R.col_scales = ls;
+  R.col_norms = ln;
+  R.col_keys = ctx->d0_keys.as<uint32_t>();
+  R.k = f;
+  R.out_keys = ctx->d0_okeys.as<uint32_t>();
+  R.out_dists = a->dists ? a->dists : ctx->d0_dists.as<float>();
+  R.d_err = ctx->d_err.as<uint32_t>();
+  R.d_fb_count = ctx->fallback.as<uint32_t>();
+  R.d_fb_list = reinterpret_cast<uint2*>(ctx->fallback.as<uint8_t>() + 16);
+  R.fb_capacity = (uint32_t)(rows < 0xffffffffull ? rows : 0xffffffffull);
+  R.timeout_ns = ctx->timeout_ns;
+  R.sm_count = ctx->sm_count;
+  int r = launch_rect_topk_sq8(R, st);
+  if (r != TESSA_OK) return fail(r, "D0 assignment launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  r = launch_d0_fragments(R.out_keys, ctx->d0_k2l.as<uint32_t>(), a->global_ids, rows, f, L, a->child_ids,
+                          a->point_ids, ctx->d_err.as<uint32_t>(), ctx->sm_count, st);
+  if (r != TESSA_OK) return fail(r, "D0 fragment launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  uint32_t fb = 0;
+  CUDA_TRY(cudaMemcpyAsync(&fb, R.d_fb_count, 4, cudaMemcpyDeviceToHost, st));
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  ctx->last_fallback_rows = fb;
+  if (bits & TESSA_DEVERR_NONFINITE)
+    return fail(TESSA_ERR_NONFINITE, "SQ GPU-D0 staging: non-finite input or distance (0x%x)", bits);
+  return map_device_error(bits);
+}
+
 int assign_device(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* a, cudaStream_t st) {
   if (!a) return fail(TESSA_ERR_INVALID_ARG, "null assignment args");
   if (source != TESSA_ASSIGN_FP32 && source != TESSA_ASSIGN_SQ8)
@@ -567,7 +681,9 @@ void tessa_destroy(tessa_ctx* ctx) {
   ctx->leaf_plan.release();
   ctx->assign_plan.release();
   DevBuf* bufs[] = {&ctx->h_codes, &ctx->h_scales, &ctx->h_norms, &ctx->h_gids, &ctx->h_members,
-                    &ctx->h_ids, &ctx->h_dists, &ctx->h_x, &ctx->fb_counts};
+                    &ctx->h_ids, &ctx->h_dists, &ctx->h_x, &ctx->fb_counts, &ctx->d0_lcodes,
+                    &ctx->d0_lscales, &ctx->d0_lnorms, &ctx->d0_keys, &ctx->d0_k2l, &ctx->d0_okeys,
+                    &ctx->d0_dists, &ctx->d0_lvec, &ctx->d0_lids, &ctx->d0_child, &ctx->d0_point};
   for (DevBuf* b : bufs) b->release();
   for (cudaStream_t s : {ctx->stream_in, ctx->stream_out})
     if (s) {
@@ -682,6 +798,75 @@ int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* a) {
     CUDA_TRY(cudaMemcpyAsync(a->topk_ids, ctx->h_ids.ptr, M * a->k * 4, cudaMemcpyDeviceToHost, st));
     CUDA_TRY(cudaMemcpyAsync(a->topk_dists, ctx->h_dists.ptr, M * a->k * 4, cudaMemcpyDeviceToHost, st));
   }
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return TESSA_OK;
+}
+
+int tessa_quantize_sq8_assign_d0(tessa_ctx* ctx, const tessa_d0_args* a, void* stream) {
+  TRY(bind(ctx));
+  TRY(validate_d0(a));
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaPointerAttributes attr;
+  CUDA_TRY(cudaPointerGetAttributes(&attr, a->leader_ids));
+  if (attr.type != cudaMemoryTypeDevice) return d0_device(ctx, a, a->leader_ids, st);
+  std::vector<uint32_t> ids(a->leader_count);
+  CUDA_TRY(cudaMemcpyAsync(ids.data(), a->leader_ids, ids.size() * 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return d0_device(ctx, a, ids.data(), st);
+}
+
+int tessa_quantize_sq8_assign_d0_host(tessa_ctx* ctx, const tessa_d0_args* a) {
+  TRY(bind(ctx));
+  TRY(validate_d0(a));
+  cudaStream_t st = ctx->stream;
+  const uint64_t rows = a->rows, L = a->leader_count, f = a->fanout_top, dim = a->dim;
+  const uint64_t P = (dim + 15) / 16 * 16;
+  TRY(ctx->h_x.ensure(rows * dim * 4));
+  TRY(ctx->h_gids.ensure(rows * 4));
+  TRY(ctx->h_codes.ensure(rows * P));
+  TRY(ctx->h_scales.ensure(rows * 4));
+  TRY(ctx->h_norms.ensure(rows * 4));
+  TRY(ctx->d0_child.ensure(rows * f * 4));
+  TRY(ctx->d0_point.ensure(rows * f * 4));
+  TRY(ctx->h_dists.ensure(rows * f * 4));
+  tessa_d0_args d = *a;
+  CUDA_TRY(cudaMemcpyAsync(ctx->h_x.ptr, a->raw_vectors, rows * dim * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(ctx->h_gids.ptr, a->global_ids, rows * 4, cudaMemcpyHostToDevice, st));
+  if (a->leader_codes) {
+    TRY(ctx->d0_lcodes.ensure(L * P));
+    TRY(ctx->d0_lscales.ensure(L * 4));
+    TRY(ctx->d0_lnorms.ensure(L * 4));
+    CUDA_TRY(cudaMemcpyAsync(ctx->d0_lcodes.ptr, a->leader_codes, L * P, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(ctx->d0_lscales.ptr, a->leader_scales, L * 4, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(ctx->d0_lnorms.ptr, a->leader_norms, L * 4, cudaMemcpyHostToDevice, st));
+    d.leader_codes = ctx->d0_lcodes.as<int8_t>();
+    d.leader_scales = ctx->d0_lscales.as<float>();
+    d.leader_norms = ctx->d0_lnorms.as<float>();
+    d.leader_vectors = nullptr;
+  } else {
+    TRY(ctx->d0_lvec.ensure(L * dim * 4));
+    CUDA_TRY(cudaMemcpyAsync(ctx->d0_lvec.ptr, a->leader_vectors, L * dim * 4, cudaMemcpyHostToDevice, st));
+    d.leader_vectors = ctx->d0_lvec.as<float>();
+  }
+  d.raw_vectors = ctx->h_x.as<float>();
+  d.global_ids = ctx->h_gids.as<uint32_t>();
+  d.codes = ctx->h_codes.as<int8_t>();
+  d.scales = ctx->h_scales.as<float>();
+  d.norms = ctx->h_norms.as<float>();
+  d.child_ids = ctx->d0_child.as<uint32_t>();
+  d.point_ids = ctx->d0_point.as<uint32_t>();
+  d.dists = ctx->h_dists.as<float>();
+  const int r = d0_device(ctx, &d, a->leader_ids, st);
+  if (r != TESSA_OK) {
+    cudaStreamSynchronize(st);
+    return r;
+  }
+  CUDA_TRY(cudaMemcpyAsync(a->codes, d.codes, rows * P, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaMemcpyAsync(a->scales, d.scales, rows * 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaMemcpyAsync(a->norms, d.norms, rows * 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaMemcpyAsync(a->child_ids, d.child_ids, rows * f * 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaMemcpyAsync(a->point_ids, d.point_ids, rows * f * 4, cudaMemcpyDeviceToHost, st));
+  if (a->dists) CUDA_TRY(cudaMemcpyAsync(a->dists, d.dists, rows * f * 4, cudaMemcpyDeviceToHost, st));
   CUDA_TRY(cudaStreamSynchronize(st));
   return TESSA_OK;
 }

@@ -33,7 +33,39 @@ struct LeafLaunch {
 // Largest leaf the leaf kernel accepts (member positions are kept in 16 bits).
 constexpr uint64_t kMaxLeafRows = 65535;
 
+// Rectangular form of the leaf kernel: each row of a row matrix against every
+// row (column) of a second matrix, per-row bounded top-k under the same
+// eps/id rule, the column's tie key as the id (global-D0 assignment).
+struct RectLaunch {
+  const int8_t* row_codes;    // rows x padded_dim
+  uint64_t rows;
+  uint32_t padded_dim;
+  const float* row_scales;
+  const float* row_norms;
+  const int8_t* col_codes;    // cols x padded_dim
+  uint32_t cols;
+  const float* col_scales;
+  const float* col_norms;
+  const uint32_t* col_keys;   // distinct tie keys; output ids are these keys
+  uint32_t k;
+  uint32_t* out_keys;         // rows x k
+  float* out_dists;           // rows x k
+  uint32_t* d_err;
+  uint32_t* d_fb_count;
+  uint2* d_fb_list;           // capacity fb_capacity (>= rows suffices)
+  uint32_t fb_capacity;
+  uint64_t timeout_ns;
+  int sm_count;
+};
+
+// Row tiles are indexed in 32 bits.
+constexpr uint64_t kMaxRectRows = 0xffffff00ull;
+
 int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream);
+int launch_rect_topk_sq8(const RectLaunch& R, cudaStream_t stream);
+int launch_d0_fragments(const uint32_t* keys, const uint32_t* key_to_leader, const uint32_t* global_ids, uint64_t rows,
+                        uint32_t fanout, uint32_t leaders, uint32_t* child_ids, uint32_t* point_ids, uint32_t* d_err,
+                        int sm_count, cudaStream_t stream);
 int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes, int8_t* dst,
                        int sm_count, cudaStream_t stream);
 int leaf_num_bstages(uint32_t padded_dim);

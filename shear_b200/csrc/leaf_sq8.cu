@@ -54,6 +54,13 @@
 //               4-slot shared-memory ring, so the epilogue warps never wait
 //               on each other.
 // The distance matrix never leaves the SM.
+//
+// Rectangular mode (template flag RECT, the global-D0 assignment of
+// quantize_sq8_and_assign_global_d0, P/dco_sq_int8.rs:1929-2070): the same
+// pipeline with A = 128-row tiles of a row matrix and B = every row of a
+// separate leader matrix, no self exclusion, and the leader's tie key (the
+// rank of (leader id, leader index)) in place of the global id.  The zone
+// argument above carries over unchanged: only the candidate set differs.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -107,6 +114,14 @@ struct Params {
   uint2* fb_list;               // (leaf, row) entries, capacity fb_capacity
   uint32_t fb_capacity;
   uint64_t timeout_ns;
+  // rectangular mode only: rows [0, nrows) of the A matrix against columns
+  // [0, ncols) of col_codes with per-column scale, norm and tie key
+  uint32_t nrows;
+  uint32_t ncols;
+  const int8_t* col_codes;
+  const float* col_scales;
+  const float* col_norms;
+  const uint32_t* col_keys;
 };
 
 struct Smem {
@@ -346,7 +361,25 @@ __device__ bool finish_row(const Params& p, uint2* log, uint8_t* perm, uint32_t 
   return true;
 }
 
-template <int KS>
+// Work item `tile`: (leaf, first row) from the tile table, or in rectangular
+// mode (0, 128 * tile) over the whole row matrix.
+template <bool RECT>
+__device__ __forceinline__ void tile_span(const Params& p, uint32_t tile, uint2& t, uint64_t& start, uint32_t& rows,
+                                          uint32_t& cols) {
+  if constexpr (RECT) {
+    t = make_uint2(0u, tile * kBM);
+    start = 0;
+    rows = p.nrows;
+    cols = p.ncols;
+  } else {
+    t = p.tiles[tile];
+    start = p.leaf_starts[t.x];
+    rows = p.leaf_sizes[t.x];
+    cols = rows;
+  }
+}
+
+template <int KS, bool RECT>
 __global__ void __launch_bounds__(kThreads, 1)
     leaf_topk_sq8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          const Params p) {
@@ -394,14 +427,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t bstage = 0, bphase = 0, a_iter = 0;
       for (uint32_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++a_iter) {
-        uint2 t = p.tiles[tile];
-        uint64_t start = p.leaf_starts[t.x];
-        uint32_t cnt = p.leaf_sizes[t.x];
+        uint2 t;
+        uint64_t start;
+        uint32_t cnt, ncol;
+        tile_span<RECT>(p, tile, t, start, cnt, ncol);
+        const uint64_t bstart = RECT ? 0 : start;
         if (!mbar_wait(s.a_empty, (a_iter & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns)) break;
         mbar_arrive_expect_tx(s.a_full, p.num_slabs * kASlabBytes);
         for (uint32_t sl = 0; sl < p.num_slabs; ++sl)
           tma_load_2d(&tmap_a, s.a + sl * kASlabBytes, s.a_full, (int32_t)(sl * kSlab), (int32_t)(start + t.y));
-        uint32_t nchunks = (cnt + kBN - 1) / kBN;
+        uint32_t nchunks = (ncol + kBN - 1) / kBN;
         bool ok = true;
         for (uint32_t c = 0; c < nchunks && ok; ++c) {
           for (uint32_t sl = 0; sl < p.num_slabs; ++sl) {
@@ -411,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             mbar_arrive_expect_tx(&s.b_full[bstage], kBStageBytes);
             tma_load_2d(&tmap_b, s.b + bstage * kBStageBytes, &s.b_full[bstage], (int32_t)(sl * kSlab),
-                        (int32_t)(start + c * kBN));
+                        (int32_t)(bstart + c * kBN));
             if (++bstage == p.num_bstages) {
               bstage = 0;
               bphase ^= 1u;
@@ -430,11 +465,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t bstage = 0, bphase = 0, acc = 0, a_iter = 0;
       bool ok = true;
       for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++a_iter) {
-        uint2 t = p.tiles[tile];
-        uint32_t cnt = p.leaf_sizes[t.x];
+        uint2 t;
+        uint64_t start;
+        uint32_t cnt, ncol;
+        tile_span<RECT>(p, tile, t, start, cnt, ncol);
         if (!mbar_wait(s.a_full, a_iter & 1u, abort_flag, p.err_word, p.timeout_ns)) break;
         tc_fence_after();
-        uint32_t nchunks = (cnt + kBN - 1) / kBN;
+        uint32_t nchunks = (ncol + kBN - 1) / kBN;
         for (uint32_t c = 0; c < nchunks && ok; ++c, ++acc) {
           uint32_t buf = acc % kAccBufs, use = acc / kAccBufs;
           if (!mbar_wait(&s.t_empty[buf], (use & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns)) {
@@ -479,10 +516,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t seq = 0;
     bool ok = true;
     for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-      uint2 t = p.tiles[tile];
-      uint64_t start = p.leaf_starts[t.x];
-      uint32_t cnt = p.leaf_sizes[t.x];
-      uint32_t nchunks = (cnt + kBN - 1) / kBN;
+      uint2 t;
+      uint64_t start;
+      uint32_t cnt, ncol;
+      tile_span<RECT>(p, tile, t, start, cnt, ncol);
+      uint32_t nchunks = (ncol + kBN - 1) / kBN;
       for (uint32_t c = 0; c < nchunks; ++c, ++seq) {
         uint32_t slot = seq % kMetaSlots, use = seq / kMetaSlots;
         bool w = true;
@@ -491,24 +529,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        // All member ids first, then all dependent loads, then the stores.
-        uint32_t lid[kBN / 32];
-#pragma unroll
-        for (uint32_t u = 0; u < kBN / 32; ++u) {
-          uint32_t col = c * kBN + u * 32 + lane;
-          lid[u] = col < cnt ? __ldg(p.members + start + col) : 0xffffffffu;
-        }
         float2 sn[kBN / 32];
         uint32_t gv[kBN / 32];
+        if constexpr (RECT) {
 #pragma unroll
-        for (uint32_t u = 0; u < kBN / 32; ++u) {
-          sn[u] = make_float2(0.f, INFINITY);  // past the leaf: distance +inf
-          gv[u] = 0xffffffffu;
-          if (lid[u] < p.resident_rows) {
-            sn[u] = make_float2(__ldg(p.scales + lid[u]), __ldg(p.norms + lid[u]));
-            gv[u] = __ldg(p.global_ids + lid[u]);
-          } else if (lid[u] != 0xffffffffu) {
-            atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+          for (uint32_t u = 0; u < kBN / 32; ++u) {
+            uint32_t col = c * kBN + u * 32 + lane;
+            sn[u] = make_float2(0.f, INFINITY);  // past the last column: distance +inf
+            gv[u] = 0xffffffffu;
+            if (col < ncol) {
+              sn[u] = make_float2(__ldg(p.col_scales + col), __ldg(p.col_norms + col));
+              gv[u] = __ldg(p.col_keys + col);
+            }
+          }
+        } else {
+          // All member ids first, then all dependent loads, then the stores.
+          uint32_t lid[kBN / 32];
+#pragma unroll
+          for (uint32_t u = 0; u < kBN / 32; ++u) {
+            uint32_t col = c * kBN + u * 32 + lane;
+            lid[u] = col < cnt ? __ldg(p.members + start + col) : 0xffffffffu;
+          }
+#pragma unroll
+          for (uint32_t u = 0; u < kBN / 32; ++u) {
+            sn[u] = make_float2(0.f, INFINITY);  // past the leaf: distance +inf
+            gv[u] = 0xffffffffu;
+            if (lid[u] < p.resident_rows) {
+              sn[u] = make_float2(__ldg(p.scales + lid[u]), __ldg(p.norms + lid[u]));
+              gv[u] = __ldg(p.global_ids + lid[u]);
+            } else if (lid[u] != 0xffffffffu) {
+              atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+            }
           }
         }
 #pragma unroll
@@ -529,22 +580,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc = 0, seq = 0;
     bool stop = false;
     for (uint32_t tile = blockIdx.x; tile < p.num_tiles && !stop; tile += gridDim.x) {
-      uint2 t = p.tiles[tile];
-      uint64_t start = p.leaf_starts[t.x];
-      uint32_t cnt = p.leaf_sizes[t.x];
+      uint2 t;
+      uint64_t start;
+      uint32_t cnt, ncol;
+      tile_span<RECT>(p, tile, t, start, cnt, ncol);
       uint32_t row = t.y + row_in_tile;
       bool valid = row < cnt;
       uint32_t gid_i = 0xfffffffeu;
       float s_i = 0.f, n_i = 0.f;
       if (valid) {
-        uint32_t lid_i = __ldg(p.members + start + row);
+        uint32_t lid_i = RECT ? row : __ldg(p.members + start + row);
         if (lid_i >= p.resident_rows) {
           atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
           valid = false;
         } else {
           s_i = __ldg(p.scales + lid_i);
           n_i = __ldg(p.norms + lid_i);
-          gid_i = __ldg(p.global_ids + lid_i);
+          if constexpr (!RECT) gid_i = __ldg(p.global_ids + lid_i);
         }
       }
       float sk[KS];
@@ -553,8 +605,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float thr = valid ? INFINITY : -INFINITY;  // theta + margin
       uint32_t nlog = 0;
       bool ovf = false;
-      const uint32_t nchunks = (cnt + kBN - 1) / kBN;
-      const uint32_t c_self = t.y / kBN;  // the row's own column: chunk c_self, group quad, lane `lane`
+      const uint32_t nchunks = (ncol + kBN - 1) / kBN;
+      const uint32_t c_self = RECT ? 0xffffffffu : t.y / kBN;  // rectangular mode: no self column  // the row's own column: chunk c_self, group quad, lane `lane`
       for (uint32_t c = 0; c < nchunks; ++c, ++acc, ++seq) {
         const uint32_t mslot = seq % kMetaSlots;
         const float4* msn = reinterpret_cast<const float4*>(s.meta_sn + mslot * kBN);
@@ -702,6 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr uint32_t kFbThreads = 256;
 constexpr uint32_t kFbBlock = 2048;  // columns per shared-memory block
 
+template <bool RECT>
 __global__ void __launch_bounds__(kFbThreads) leaf_fallback_kernel(const int8_t* __restrict__ leaf_codes,
                                                                     uint32_t padded_dim, const Params p) {
   extern __shared__ int4 fb_smem[];
@@ -716,11 +769,12 @@ __global__ void __launch_bounds__(kFbThreads) leaf_fallback_kernel(const int8_t*
   const uint32_t k = p.k;
   for (uint32_t item = blockIdx.x; item < n; item += gridDim.x) {
     uint2 e = p.fb_list[item];
-    uint64_t start = p.leaf_starts[e.x];
-    uint32_t cnt = p.leaf_sizes[e.x];
-    uint32_t row = e.y;
-    uint32_t lid_i = p.members[start + row];
-    float s_i = p.scales[lid_i], n_i = p.norms[lid_i];
+    const uint64_t start = RECT ? 0 : p.leaf_starts[e.x];
+    const uint32_t cnt = RECT ? p.ncols : p.leaf_sizes[e.x];
+    const uint32_t row = e.y;
+    const uint32_t lid_row = RECT ? row : p.members[start + row];
+    const uint32_t lid_i = RECT ? 0xffffffffu : lid_row;  // the column to skip (none in rectangular mode)
+    float s_i = p.scales[lid_row], n_i = p.norms[lid_row];
     const int4* rc = reinterpret_cast<const int4*>(leaf_codes + (start + row) * padded_dim);
     for (uint32_t w = threadIdx.x; w < words; w += kFbThreads) rowbuf[w] = rc[w];
     float bd = 3.402823466e+38F;  // warp 0: slot `lane` of the list
@@ -729,11 +783,13 @@ __global__ void __launch_bounds__(kFbThreads) leaf_fallback_kernel(const int8_t*
       uint32_t bn = cnt - b0 < kFbBlock ? cnt - b0 : kFbBlock;
       __syncthreads();
       for (uint32_t c = threadIdx.x; c < bn; c += kFbThreads) {
-        uint32_t lj = p.members[start + b0 + c];
+        uint32_t lj = RECT ? b0 + c : p.members[start + b0 + c];
         float dj = INFINITY;
         uint32_t gj = 0xffffffffu;
-        if (lj < p.resident_rows) {
-          const int4* cc = reinterpret_cast<const int4*>(leaf_codes + (start + b0 + c) * padded_dim);
+        if (RECT || lj < p.resident_rows) {
+          const int8_t* cbase = RECT ? p.col_codes + (uint64_t)lj * padded_dim
+                                     : leaf_codes + (start + b0 + c) * padded_dim;
+          const int4* cc = reinterpret_cast<const int4*>(cbase);
           int dot = 0;
           for (uint32_t w = 0; w < words; ++w) {
             int4 x = rowbuf[w], y = cc[w];
@@ -742,8 +798,13 @@ __global__ void __launch_bounds__(kFbThreads) leaf_fallback_kernel(const int8_t*
             dot = __dp4a(x.z, y.z, dot);
             dot = __dp4a(x.w, y.w, dot);
           }
-          dj = sq8_l2_from_dot(dot, s_i, n_i, p.scales[lj], p.norms[lj]);
-          gj = p.global_ids[lj];
+          if constexpr (RECT) {
+            dj = sq8_l2_from_dot(dot, s_i, n_i, p.col_scales[lj], p.col_norms[lj]);
+            gj = p.col_keys[lj];
+          } else {
+            dj = sq8_l2_from_dot(dot, s_i, n_i, p.scales[lj], p.norms[lj]);
+            gj = p.global_ids[lj];
+          }
         } else {
           lj = lid_i;  // flagged by the main kernel; never a candidate
         }
@@ -877,13 +938,45 @@ int leaf_num_bstages(uint32_t padded_dim) {
   return leaf_plan(padded_dim, 32, &st, &cap) ? (int)st : 0;
 }
 
-template <int KS>
+template <int KS, bool RECT>
 static int launch_main(const CUtensorMap& ta, const CUtensorMap& tb, const leaf::Params& prm, uint32_t smem,
                        uint32_t grid, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(leaf::leaf_topk_sq8_kernel<KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(leaf::leaf_topk_sq8_kernel<KS, RECT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return TESSA_ERR_CUDA;
-  leaf::leaf_topk_sq8_kernel<KS><<<grid, leaf::kThreads, smem, stream>>>(ta, tb, prm);
+  leaf::leaf_topk_sq8_kernel<KS, RECT><<<grid, leaf::kThreads, smem, stream>>>(ta, tb, prm);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+// Main kernel (k-specialised) plus the exact fallback over the rows it lists.
+template <bool RECT>
+static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, leaf::Params& prm, const int8_t* a_codes,
+                       uint32_t padded_dim, int sm_count, cudaStream_t stream) {
+  uint32_t nst = 0, log_cap = 0;
+  if (!leaf_plan(padded_dim, prm.k, &nst, &log_cap)) return TESSA_ERR_UNSUPPORTED;
+  const uint32_t slabs = (padded_dim + leaf::kSlab - 1) / leaf::kSlab;
+  prm.num_slabs = slabs;
+  prm.num_bstages = nst;
+  prm.log_cap = log_cap;
+  const uint32_t smem = leaf::smem_bytes(slabs, nst, log_cap);
+  if (cudaMemsetAsync(prm.fb_count, 0, 4, stream) != cudaSuccess) return TESSA_ERR_CUDA;
+  const uint32_t grid = prm.num_tiles < (uint32_t)sm_count ? prm.num_tiles : (uint32_t)sm_count;
+  int rc;
+  if (prm.k <= 2)
+    rc = launch_main<2, RECT>(ta, tb, prm, smem, grid, stream);
+  else if (prm.k <= 4)
+    rc = launch_main<4, RECT>(ta, tb, prm, smem, grid, stream);
+  else if (prm.k <= 8)
+    rc = launch_main<8, RECT>(ta, tb, prm, smem, grid, stream);
+  else if (prm.k <= 16)
+    rc = launch_main<16, RECT>(ta, tb, prm, smem, grid, stream);
+  else
+    rc = launch_main<32, RECT>(ta, tb, prm, smem, grid, stream);
+  if (rc != TESSA_OK) return rc;
+  // Exact recomputation of the rows whose result depends on insertion order.
+  const uint32_t fb_smem = padded_dim + leaf::kFbBlock * 12u;
+  leaf::leaf_fallback_kernel<RECT><<<(unsigned)sm_count * 4u, leaf::kFbThreads, fb_smem, stream>>>(a_codes, padded_dim,
+                                                                                                  prm);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 
@@ -891,13 +984,10 @@ static int launch_main(const CUtensorMap& ta, const CUtensorMap& tb, const leaf:
 int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
   if (L.num_tiles == 0) return TESSA_OK;
   if (L.k == 0 || L.k > 32) return TESSA_ERR_INVALID_ARG;
-  uint32_t nst = 0, log_cap = 0;
-  if (!leaf_plan(L.padded_dim, L.k, &nst, &log_cap)) return TESSA_ERR_UNSUPPORTED;
-  uint32_t slabs = (L.padded_dim + leaf::kSlab - 1) / leaf::kSlab;
   CUtensorMap ta, tb;
   if (make_code_tmap(&ta, L.leaf_codes, L.leaf_rows, L.padded_dim, leaf::kBM) != 0) return TESSA_ERR_CUDA;
   if (make_code_tmap(&tb, L.leaf_codes, L.leaf_rows, L.padded_dim, leaf::kBN) != 0) return TESSA_ERR_CUDA;
-  leaf::Params prm;
+  leaf::Params prm = {};
   prm.scales = L.scales;
   prm.norms = L.norms;
   prm.global_ids = L.global_ids;
@@ -906,10 +996,7 @@ int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
   prm.leaf_sizes = L.d_leaf_sizes;
   prm.tiles = L.d_tiles;
   prm.num_tiles = L.num_tiles;
-  prm.num_slabs = slabs;
-  prm.num_bstages = nst;
   prm.k = L.k;
-  prm.log_cap = log_cap;
   prm.resident_rows = L.resident_rows;
   prm.out_ids = L.out_ids;
   prm.out_dists = L.out_dists;
@@ -918,25 +1005,66 @@ int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
   prm.fb_list = L.d_fb_list;
   prm.fb_capacity = L.fb_capacity;
   prm.timeout_ns = L.timeout_ns;
-  uint32_t smem = leaf::smem_bytes(slabs, nst, log_cap);
-  if (cudaMemsetAsync(L.d_fb_count, 0, 4, stream) != cudaSuccess) return TESSA_ERR_CUDA;
-  uint32_t grid = L.num_tiles < (uint32_t)L.sm_count ? L.num_tiles : (uint32_t)L.sm_count;
-  int rc;
-  if (L.k <= 2)
-    rc = launch_main<2>(ta, tb, prm, smem, grid, stream);
-  else if (L.k <= 4)
-    rc = launch_main<4>(ta, tb, prm, smem, grid, stream);
-  else if (L.k <= 8)
-    rc = launch_main<8>(ta, tb, prm, smem, grid, stream);
-  else if (L.k <= 16)
-    rc = launch_main<16>(ta, tb, prm, smem, grid, stream);
-  else
-    rc = launch_main<32>(ta, tb, prm, smem, grid, stream);
-  if (rc != TESSA_OK) return rc;
-  // Exact recomputation of the rows whose result depends on insertion order.
-  uint32_t fb_smem = L.padded_dim + leaf::kFbBlock * 12u;
-  leaf::leaf_fallback_kernel<<<(unsigned)L.sm_count * 4u, leaf::kFbThreads, fb_smem, stream>>>(L.leaf_codes,
-                                                                                            L.padded_dim, prm);
+  return launch_pair<false>(ta, tb, prm, L.leaf_codes, L.padded_dim, L.sm_count, stream);
+}
+
+int launch_rect_topk_sq8(const RectLaunch& R, cudaStream_t stream) {
+  if (R.rows == 0 || R.cols == 0) return TESSA_OK;
+  if (R.k == 0 || R.k > 32 || R.rows > kMaxRectRows) return TESSA_ERR_INVALID_ARG;
+  CUtensorMap ta, tb;
+  if (make_code_tmap(&ta, R.row_codes, R.rows, R.padded_dim, leaf::kBM) != 0) return TESSA_ERR_CUDA;
+  if (make_code_tmap(&tb, R.col_codes, R.cols, R.padded_dim, leaf::kBN) != 0) return TESSA_ERR_CUDA;
+  leaf::Params prm = {};
+  prm.scales = R.row_scales;
+  prm.norms = R.row_norms;
+  prm.num_tiles = (uint32_t)((R.rows + leaf::kBM - 1) / leaf::kBM);
+  prm.k = R.k;
+  prm.resident_rows = R.rows;
+  prm.out_ids = R.out_keys;
+  prm.out_dists = R.out_dists;
+  prm.err_word = R.d_err;
+  prm.fb_count = R.d_fb_count;
+  prm.fb_list = R.d_fb_list;
+  prm.fb_capacity = R.fb_capacity;
+  prm.timeout_ns = R.timeout_ns;
+  prm.nrows = (uint32_t)R.rows;
+  prm.ncols = R.cols;
+  prm.col_codes = R.col_codes;
+  prm.col_scales = R.col_scales;
+  prm.col_norms = R.col_norms;
+  prm.col_keys = R.col_keys;
+  return launch_pair<true>(ta, tb, prm, R.row_codes, R.padded_dim, R.sm_count, stream);
+}
+
+// Rectangular-mode epilogue of the global-D0 assignment: key -> leader index
+// and the row's global id beside every slot.
+__global__ void d0_fragments_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ key_to_leader,
+                                    const uint32_t* __restrict__ global_ids, uint64_t rows, uint32_t fanout,
+                                    uint32_t leaders, uint32_t* __restrict__ child_ids,
+                                    uint32_t* __restrict__ point_ids, uint32_t* __restrict__ err) {
+  const uint64_t n = rows * fanout;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t key = keys[i];
+    uint32_t child = 0xffffffffu;
+    if (key < leaders)
+      child = key_to_leader[key];
+    else
+      atomicOr(err, TESSA_DEVERR_NONFINITE);  // fanout <= leaders: only a non-finite distance leaves a slot empty
+    child_ids[i] = child;
+    point_ids[i] = global_ids[i / fanout];
+  }
+}
+
+int launch_d0_fragments(const uint32_t* keys, const uint32_t* key_to_leader, const uint32_t* global_ids, uint64_t rows,
+                        uint32_t fanout, uint32_t leaders, uint32_t* child_ids, uint32_t* point_ids, uint32_t* d_err,
+                        int sm_count, cudaStream_t stream) {
+  const uint64_t n = rows * fanout;
+  if (n == 0) return TESSA_OK;
+  uint64_t blocks = (n + 255) / 256;
+  const uint64_t cap = (uint64_t)sm_count * 8u;
+  if (blocks > cap) blocks = cap;
+  d0_fragments_kernel<<<(unsigned)blocks, 256, 0, stream>>>(keys, key_to_leader, global_ids, rows, fanout, leaders,
+                                                           child_ids, point_ids, d_err);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 

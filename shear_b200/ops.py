@@ -240,3 +240,128 @@ def assign(source: int, *, x=None, raw_norms=None, codes=None, scales=None, sq8_
                      out_ids=ids.data_ptr(), out_dists=dists.data_ptr())
     C.check(C.load().tessa_assign(ctx.handle, int(source), ctypes.byref(a), _stream_ptr(torch, dev)))
     return ids, dists
+
+
+# ------------------------------------------------------------- global D0
+
+class D0Result:
+    """SqGpuD0QuantizeAssignResult (P/dco_sq_int8.rs:1929-2070): the SQ8 matrix
+    of the batch and its D0 assignment fragments.
+
+    codes [rows, padded_dim] int8, scales / norms [rows] f32, child_ids
+    [rows, fanout] leader indices (best first), point_ids [rows, fanout]
+    (the row's global id), dists [rows, fanout] SQ8 distances.
+    """
+
+    def __init__(self, codes, scales, norms, child_ids, point_ids, dists, dim):
+        self.codes, self.scales, self.norms = codes, scales, norms
+        self.child_ids, self.point_ids, self.dists = child_ids, point_ids, dists
+        self.rows = int(codes.shape[0])
+        self.dim = int(dim)
+        self.padded_dim = int(codes.shape[1])
+
+    def fragments(self):
+        """[(child_id, point_id), ...] in the reference's order (row-major, best first)."""
+        c = np.asarray(self.child_ids).reshape(-1)
+        p = np.asarray(self.point_ids).reshape(-1)
+        return list(zip(c.tolist(), p.tolist()))
+
+
+def _d0_leaders(leader_count, dim, leader_vectors, leader_payload):
+    if leader_payload is None:
+        if leader_vectors is None:
+            raise ValueError("global D0 leaders need leader vectors or a leader payload")
+        return leader_vectors, None, None, None
+    codes, scales, norms = leader_payload
+    pd = padded_dim(dim)
+    if tuple(codes.shape) != (leader_count, pd) or scales.shape[0] != leader_count or norms.shape[0] != leader_count:
+        raise ValueError(f"SQ GPU-D0 staging leader payload shape mismatch: codes {tuple(codes.shape)} "
+                         f"expected ({leader_count}, {pd})")
+    return None, codes, scales, norms
+
+
+def quantize_sq8_and_assign_global_d0(raw_vectors, global_ids, global_d0_leader_ids, global_d0_leader_vectors,
+                                      fanout_top: int, leader_payload=None, device: int = 0) -> D0Result:
+    """Host form of the trait method quantize_sq8_and_assign_global_d0
+    (compute_backend.rs:3828-3837; CUDA implementation :24281-24760; CPU
+    reference P/dco_sq_int8.rs:1929-2070): numpy in, numpy out.
+
+    raw_vectors [rows, dim] f32; global_ids [rows]; global_d0_leader_ids
+    [leaders]; global_d0_leader_vectors [leaders, dim] f32 (ignored when
+    leader_payload = (codes, scales, norms) is given).
+    """
+    raw = np.ascontiguousarray(raw_vectors, dtype=np.float32)
+    gids = np.ascontiguousarray(global_ids, dtype=np.uint32)
+    lids = np.ascontiguousarray(global_d0_leader_ids, dtype=np.uint32)
+    rows, leaders = gids.shape[0], lids.shape[0]
+    if raw.ndim != 2:
+        raw = raw.reshape(rows, -1) if rows else raw.reshape(0, 0)
+    dim = raw.shape[1] if raw.ndim == 2 else 0
+    if raw.shape[0] != rows:
+        raise ValueError(f"SQ GPU-D0 staging raw vector shape mismatch: rows={rows} values={raw.size}")
+    lv, lc, ls, ln = _d0_leaders(leaders, dim, global_d0_leader_vectors, leader_payload)
+    if lv is not None:
+        lv = np.ascontiguousarray(lv, dtype=np.float32)
+        if lv.size != leaders * dim:
+            raise ValueError(f"SQ GPU-D0 staging leader vector shape mismatch: leaders={leaders} dim={dim} "
+                             f"values={lv.size}")
+    else:
+        lc = np.ascontiguousarray(lc, dtype=np.int8)
+        ls = np.ascontiguousarray(ls, dtype=np.float32)
+        ln = np.ascontiguousarray(ln, dtype=np.float32)
+    f = int(fanout_top)
+    pd = padded_dim(dim) if dim > 0 else 0
+    codes = np.zeros((rows, pd), dtype=np.int8)
+    scales = np.zeros(rows, dtype=np.float32)
+    norms = np.zeros(rows, dtype=np.float32)
+    n = rows * max(f, 0)
+    child = np.zeros(n, dtype=np.uint32)
+    point = np.zeros(n, dtype=np.uint32)
+    dists = np.zeros(n, dtype=np.float32)
+    a = C.D0Args(raw_vectors=raw.ctypes.data, global_ids=gids.ctypes.data, rows=rows, dim=dim, fanout_top=f,
+                 leader_ids=lids.ctypes.data, leader_vectors=_np_ptr(lv).value, leader_codes=_np_ptr(lc).value,
+                 leader_scales=_np_ptr(ls).value, leader_norms=_np_ptr(ln).value, leader_count=leaders,
+                 codes=codes.ctypes.data, scales=scales.ctypes.data, norms=norms.ctypes.data,
+                 child_ids=child.ctypes.data, point_ids=point.ctypes.data, dists=dists.ctypes.data)
+    C.check(C.load().tessa_quantize_sq8_assign_d0_host(context(device).handle, ctypes.byref(a)))
+    shape = (rows, f)
+    return D0Result(codes, scales, norms, child.reshape(shape), point.reshape(shape), dists.reshape(shape), dim)
+
+
+def quantize_sq8_assign_d0(x, global_ids, leader_ids, fanout_top: int, leader_vectors=None, leader_payload=None,
+                           ctx: Context | None = None) -> D0Result:
+    """Device form: CUDA tensors in (x [rows, dim] f32, global_ids / leader_ids
+    int32 bit patterns of uint32, leader_vectors [leaders, dim] f32 or
+    leader_payload (codes, scales, norms)), CUDA tensors out, on the tensors'
+    current stream."""
+    import torch
+
+    if not x.is_cuda or x.dtype != torch.float32 or x.dim() != 2:
+        raise ValueError("x must be a 2-D float32 CUDA tensor")
+    x = x.contiguous()
+    rows, dim = x.shape
+    dev = x.device.index
+    ctx = ctx or context(dev)
+    leaders = int(leader_ids.numel())
+    lv, lc, ls, ln = _d0_leaders(leaders, dim, leader_vectors, leader_payload)
+    f = int(fanout_top)
+    pd = padded_dim(dim)
+    codes = torch.empty((rows, pd), dtype=torch.int8, device=x.device)
+    scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+    norms = torch.empty(rows, dtype=torch.float32, device=x.device)
+    n = rows * max(f, 0)
+    child = torch.empty(n, dtype=torch.int32, device=x.device)
+    point = torch.empty(n, dtype=torch.int32, device=x.device)
+    dists = torch.empty(n, dtype=torch.float32, device=x.device)
+    c = lambda t: t.contiguous() if t is not None else None
+    lv, lc, ls, ln = c(lv), c(lc), c(ls), c(ln)
+    gid = global_ids.contiguous()
+    lid = leader_ids.contiguous()
+    a = C.D0Args(raw_vectors=x.data_ptr(), global_ids=gid.data_ptr(), rows=rows, dim=dim, fanout_top=f,
+                 leader_ids=lid.data_ptr(), leader_vectors=_ptr(lv).value, leader_codes=_ptr(lc).value,
+                 leader_scales=_ptr(ls).value, leader_norms=_ptr(ln).value, leader_count=leaders,
+                 codes=codes.data_ptr(), scales=scales.data_ptr(), norms=norms.data_ptr(),
+                 child_ids=child.data_ptr(), point_ids=point.data_ptr(), dists=dists.data_ptr())
+    C.check(C.load().tessa_quantize_sq8_assign_d0(ctx.handle, ctypes.byref(a), _stream_ptr(torch, dev)))
+    shape = (rows, f)
+    return D0Result(codes, scales, norms, child.view(shape), point.view(shape), dists.view(shape), dim)

@@ -219,3 +219,53 @@ def test_oracle_assignment_fp32_matches_transliteration(oracle):
         for r in range(2):
             assert sids[p * 2 + r] == gids[best[r][2]]
             assert sd[p * 2 + r] == best[r][0]
+
+
+# ------------------------------------------------------------- global D0
+
+def test_d0_reference_assigns_by_sq_distance_with_stable_ties(oracle):
+    # P/dco_sq_int8.rs:3422-3453 sq_gpu_d0_reference_assigns_by_sq_distance_with_stable_ties
+    leaders = np.array([[1.0, 0.0], [-1.0, 0.0]], np.float32)
+    payload = oracle.quantize_sq8(leaders)
+    r = oracle.d0_assign(np.array([[0.0, 0.0], [1.0, 0.0]], np.float32), [0, 1], [5, 3], leaders, 1,
+                         leader_payload=payload)
+    frags = list(zip(r["child_ids"].ravel().tolist(), r["point_ids"].ravel().tolist()))
+    assert frags == [(1, 0), (0, 1)]
+    assert r["codes"].shape == (2, 16)
+
+
+@pytest.mark.parametrize("fanout", [1, 6, 17, 32])
+def test_d0_oracle_matches_sorting_reference_on_compute_backend_fixture(oracle, fanout):
+    # compute_backend.rs:43857-43940 fixture (duplicate leader, row equal to a leader)
+    from d0cases import reference_fixture_43857, py_d0_sort
+    raw, gids, lids, lv = reference_fixture_43857()
+    r = oracle.d0_assign(raw, gids, lids, lv, fanout)
+    lc, ls, ln = oracle.quantize_sq8(lv)
+    want = py_d0_sort(r["codes"], r["scales"], r["norms"], lc, ls, ln, lids, fanout)
+    assert np.array_equal(r["child_ids"], want)
+    assert np.array_equal(r["point_ids"], np.repeat(gids, fanout).reshape(-1, fanout))
+    # leader 1 (id 100) ties leader 0 (id 90000) exactly: the smaller id wins
+    assert r["child_ids"][0, 0] == 1
+
+
+@pytest.mark.parametrize("rows,dim,leaders,fanout,seed", [(40, 24, 19, 3, 1), (25, 100, 64, 8, 2),
+                                                           (30, 16, 5, 5, 3)])
+def test_d0_oracle_matches_sorting_reference_on_random_rows(oracle, rows, dim, leaders, fanout, seed):
+    from d0cases import random_case, py_d0_sort
+    raw, gids, lids, lv = random_case(rows, dim, leaders, seed)
+    r = oracle.d0_assign(raw, gids, lids, lv, fanout)
+    lc, ls, ln = oracle.quantize_sq8(lv)
+    assert np.array_equal(r["child_ids"], py_d0_sort(r["codes"], r["scales"], r["norms"], lc, ls, ln, lids,
+                                                      fanout))
+
+
+def test_d0_oracle_rejects_invalid_requests(oracle):
+    # P/dco_sq_int8.rs:1932-1960
+    lv = np.ones((2, 4), np.float32)
+    with pytest.raises(ValueError, match="at least one input row"):
+        oracle.d0_assign(np.zeros((0, 4), np.float32), [], [1, 2], lv, 1)
+    with pytest.raises(ValueError, match="at least one global D0 leader"):
+        oracle.d0_assign(np.ones((1, 4), np.float32), [0], [], np.zeros((0, 4), np.float32), 1)
+    for f in (0, 3):
+        with pytest.raises(ValueError, match="fanout must be in"):
+            oracle.d0_assign(np.ones((1, 4), np.float32), [0], [1, 2], lv, f)
