@@ -54,6 +54,11 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["leaf", "d0"], default="leaf",
+                    help="leaf = the north-star leaf replay (default); d0 = global-D0 SQ8 staging")
+    ap.add_argument("--d0-rows", type=int, default=1 << 20, help="D0: raw rows per GPU per step")
+    ap.add_argument("--d0-leaders", type=int, default=1000, help="D0: global leaders (params.rs max_leaders)")
+    ap.add_argument("--d0-fanout", type=int, default=10, help="D0: fanout_top (params.rs default)")
     return ap.parse_args()
 
 
@@ -422,8 +427,216 @@ def run_ours(a):
     return 0
 
 
+# ----------------------------------------------------------------- global D0
+
+def d0_desc(a):
+    return {
+        "workload": f"global-D0 SQ8 staging (quantize_sq8_and_assign_global_d0): {a.d0_rows} raw rows x "
+                    f"{a.dim}-d f32 per GPU, {a.d0_leaders} leaders, fanout {a.d0_fanout}",
+        "rows": a.d0_rows, "dim": a.dim, "leaders": a.d0_leaders, "fanout": a.d0_fanout,
+        "l2": "inputs larger than L2 (raw rows %.1f GB per GPU); no flush" % (a.d0_rows * a.dim * 4 / 1e9),
+    }
+
+
+def make_d0_workload(torch, dev, a, seed):
+    """Unit-normal rows on the device; leaders are rows of the batch (the
+    reference samples its root leaders from the data)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.empty((a.d0_rows, a.dim), dtype=torch.float32, device=dev)
+    chunk = 1 << 18
+    for r0 in range(0, a.d0_rows, chunk):
+        r1 = min(a.d0_rows, r0 + chunk)
+        y = torch.randn((r1 - r0, a.dim), generator=g, device=dev, dtype=torch.float32)
+        x[r0:r1] = y / torch.linalg.vector_norm(y, dim=1, keepdim=True)
+    pick = torch.randperm(a.d0_rows, generator=g, device=dev)[:a.d0_leaders]
+    gids = (torch.arange(a.d0_rows, device=dev, dtype=torch.int64) + seed * a.d0_rows).to(torch.int32)
+    lv = x[pick].contiguous()
+    lids = gids[pick].contiguous()
+    torch.cuda.synchronize(dev)
+    return x, gids, lids, lv
+
+
+def run_d0_reference(a):
+    """CPU restatement of quantize_sq8_and_assign_global_d0_reference (oracle port), rank 0 only."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    threads = O.num_threads()
+    rng = np.random.default_rng(0)
+    rows = max(threads, 1) * 512
+    x = rng.standard_normal((rows, a.dim)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    pick = rng.permutation(rows)[:a.d0_leaders]
+    gids = np.arange(rows, dtype=np.uint32)
+    times = []
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        O.d0_assign(x, gids, gids[pick], x[pick], a.d0_fanout)
+        dt = time.perf_counter() - t0
+        if i >= a.warmup:
+            times.append(dt)
+    mean = float(np.mean(times))
+    value = rows / mean
+    line = {
+        "impl": "reference", "metric": "D0 staging rows/sec", "value": value, "unit": "rows/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": mean * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: N(0,1) rows, L2-normalised (seed 0)", "config": d0_desc(a),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows per step ({rows / a.d0_rows:.2%} of the per-GPU batch)"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's quantize + D0 assignment restated in C (oracle/tessa_oracle.c), OpenMP",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_d0(a):
+    import torch
+
+    from shear_b200 import ops
+
+    world, rank, local = dist_env()
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = ops.context(dev.index)
+    x, gids, lids, lv = make_d0_workload(torch, dev, a, seed=1 + rank)
+    rows, f, L = a.d0_rows, a.d0_fanout, a.d0_leaders
+    pd = ops.padded_dim(a.dim)
+    out = (torch.empty((rows, pd), dtype=torch.int8, device=dev), torch.empty(rows, device=dev),
+           torch.empty(rows, device=dev), torch.empty(rows * f, dtype=torch.int32, device=dev),
+           torch.empty(rows * f, dtype=torch.int32, device=dev), torch.empty(rows * f, device=dev))
+    assign_ms = []
+
+    def step(record=False):
+        ops.quantize_sq8_assign_d0(x, gids, lids, f, leader_vectors=lv, ctx=ctx, out=out)
+        if record:
+            assign_ms.append(ops.d0_last_profile(ctx)["assign_ms"])
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(a.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(dev.index) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for _ in range(a.steps):
+            step(record=True)
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    total_s = t_start.elapsed_time(t_end) / 1e3
+    kern_s = float(np.mean(assign_ms)) / 1e3
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([total_s, kern_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_s, kern_s = float(tt[0]), float(tt[1])
+    per_step = total_s / a.steps
+    value = world * rows / per_step
+    ops_per_step = 2.0 * rows * L * pd
+
+    e2e = None
+    if not a.no_e2e and a.e2e_steps > 0:
+        pin = lambda t: t.cpu().pin_memory()
+        hx, hg, hl, hv = pin(x), pin(gids), pin(lids), pin(lv)
+        hout = tuple(torch.empty(t.shape, dtype=t.dtype).pin_memory().numpy() for t in out)
+        hout = (hout[0], hout[1], hout[2], hout[3].view(np.uint32), hout[4].view(np.uint32), hout[5])
+        args = (hx.numpy(), hg.numpy().view(np.uint32), hl.numpy().view(np.uint32), hv.numpy(), f)
+        ops.quantize_sq8_and_assign_global_d0(*args, device=dev.index, out=hout)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(a.e2e_steps):
+            ops.quantize_sq8_and_assign_global_d0(*args, device=dev.index, out=hout)
+        e2e_s = (time.perf_counter() - t0) / a.e2e_steps
+        if world > 1:
+            import torch.distributed as dist
+            tt = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_s = float(tt[0])
+        h2d = hx.numel() * 4 + hg.numel() * 4 + hl.numel() * 4 + hv.numel() * 4
+        d2h = rows * pd + rows * 8 + rows * f * 12
+        e2e = {"value": world * rows / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3,
+               "timing": "wall clock around the synchronous host-buffer C-ABI call, pinned host memory"}
+        del hx, hg, hl, hv, hout
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    int8_peak = int8_peak_tops(torch, dev)
+    achieved = ops_per_step / kern_s / 1e12
+    peak, src = (int8_peak, "measured in-run: cuBLAS int8 burst (torch._int_mm 8192^3)") if int8_peak else \
+        (NOMINAL_INT8_TOPS, "nominal B200 dense int8 4.5 POPS (no measured int8 peak)")
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
+                "traffic": None, "peak_source": src, "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
+                "kernel": f"tessa::leaf::leaf_topk_sq8_kernel<{next(v for v in (2, 4, 8, 16, 32) if f <= v)}, true>",
+                "algorithmic_ops_per_launch": ops_per_step, "kernel_ms": kern_s * 1e3}
+
+    cpu = None
+    if not a.no_cpu_baseline and world == 1:
+        from oracle import oracle as O
+        hx = x[: min(rows, 1 << 17)].cpu().numpy()
+        hg = gids[: hx.shape[0]].cpu().numpy().view(np.uint32)
+        hl, hv = lids.cpu().numpy().view(np.uint32), lv.cpu().numpy()
+        done, t0, chunk = 0, time.perf_counter(), max(O.num_threads(), 1) * 256
+        while done < hx.shape[0]:
+            O.d0_assign(hx[done:done + chunk], hg[done:done + chunk], hl, hv, f)
+            done += min(chunk, hx.shape[0] - done)
+            if time.perf_counter() - t0 >= a.cpu_seconds:
+                break
+        dt = time.perf_counter() - t0
+        cpu = {"value": done / dt, "unit": "rows/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"{done} of {rows} rows in {dt:.1f} s (quantize + assign), oracle/tessa_oracle.c OpenMP"}
+
+    line = {
+        "metric": "D0 staging rows/sec", "value": value, "unit": "rows/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: N(0,1) rows, L2-normalised, leaders drawn from the rows (seed 1+rank)",
+        "config": dict(d0_desc(a), parallelism=f"row-sharded x{world} (independent, no collective)"),
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": 5 * a.steps,  # leader quantize, row quantize, assignment, fallback, fragments
+        "clocks": clk.summary(),
+        "profile_last_step": ops.d0_last_profile(ctx),
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse_args()
+    if a.workload == "d0":
+        return run_d0_reference(a) if a.impl == "reference" else run_d0(a)
     if a.impl == "reference":
         return run_reference(a)
     return run_ours(a)

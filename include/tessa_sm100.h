@@ -251,6 +251,24 @@ typedef struct tessa_d0_args {
   float* dists;                 /* optional out: rows x fanout_top SQ8 distances (NULL = not written) */
 } tessa_d0_args;
 
+/* Phase times of the context's last D0 call, from CUDA events on its stream --
+ * the device-side fields of the reference's SqGpuD0StagingProfile
+ * (P/dco_sq_int8.rs:411-436: gpu_quantize_wall, leader_quantize_wall,
+ * d0_assign_distance_kernel_wall, d0_assign_merge_kernel_wall). */
+typedef struct tessa_d0_profile {
+  double leader_quantize_ms;    /* 0 when a leader payload was given */
+  double quantize_ms;           /* rows -> SQ8 */
+  double assign_ms;             /* rectangular top-k kernel + its exact fallback */
+  double fragment_ms;           /* tie key -> leader index, point ids */
+  uint64_t rows;
+  uint64_t fallback_rows;       /* rows recomputed by the exact sequential rule */
+  uint32_t leaders;
+  uint32_t fanout;
+  uint32_t padded_dim;
+} tessa_d0_profile;
+
+TESSA_API int tessa_d0_last_profile(const tessa_ctx* ctx, tessa_d0_profile* out);
+
 /* Device-pointer form: every array is a device pointer except leader_ids,
  * which may be either (it is read on the host to build the tie keys). */
 TESSA_API int tessa_quantize_sq8_assign_d0(tessa_ctx* ctx, const tessa_d0_args* args, void* stream);

@@ -78,6 +78,14 @@ class D0Args(ctypes.Structure):
     ]
 
 
+class D0Profile(ctypes.Structure):
+    _fields_ = [
+        ("leader_quantize_ms", ctypes.c_double), ("quantize_ms", ctypes.c_double), ("assign_ms", ctypes.c_double),
+        ("fragment_ms", ctypes.c_double), ("rows", ctypes.c_uint64), ("fallback_rows", ctypes.c_uint64),
+        ("leaders", ctypes.c_uint32), ("fanout", ctypes.c_uint32), ("padded_dim", ctypes.c_uint32),
+    ]
+
+
 class PreparedReplay(ctypes.Structure):
     _fields_ = [
         ("dim", ctypes.c_uint32), ("padded_dim", ctypes.c_uint32), ("resident_rows", ctypes.c_uint64),
@@ -122,6 +130,7 @@ SIGNATURES = [
     ("tessa_assign", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(AssignArgs), c_vp]),
     ("tessa_quantize_sq8_assign_d0", ctypes.c_int, [c_vp, ctypes.POINTER(D0Args), c_vp]),
     ("tessa_quantize_sq8_assign_d0_host", ctypes.c_int, [c_vp, ctypes.POINTER(D0Args)]),
+    ("tessa_d0_last_profile", ctypes.c_int, [c_vp, ctypes.POINTER(D0Profile)]),
     ("tessa_replay_session_create", ctypes.c_int,
      [ctypes.c_int, ctypes.POINTER(PreparedReplay), ctypes.POINTER(c_vp)]),
     ("tessa_replay_run_mode", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(ModeResult)]),

@@ -229,6 +229,8 @@ struct tessa_ctx {
   // and the host form's extra staging
   DevBuf d0_lcodes, d0_lscales, d0_lnorms, d0_keys, d0_k2l, d0_okeys, d0_dists, d0_lvec, d0_lids, d0_child,
       d0_point;
+  cudaEvent_t d0_ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // phase boundaries of a D0 call
+  tessa_d0_profile d0_prof = {};
 };
 
 namespace {
@@ -523,9 +525,12 @@ int d0_device(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_i
   TRY(ctx->d0_okeys.ensure(rows * f * 4));
   TRY(ctx->fallback.ensure(16 + rows * 8));
   if (!a->dists) TRY(ctx->d0_dists.ensure(rows * f * 4));
+  for (cudaEvent_t& e : ctx->d0_ev)
+    if (!e) CUDA_TRY(cudaEventCreate(&e));
   CUDA_TRY(cudaMemcpyAsync(ctx->d0_keys.ptr, key.data(), (size_t)L * 4, cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaMemcpyAsync(ctx->d0_k2l.ptr, k2l.data(), (size_t)L * 4, cudaMemcpyHostToDevice, st));
   TRY(clear_err(ctx, st));
+  CUDA_TRY(cudaEventRecord(ctx->d0_ev[0], st));
   const int8_t* lc = a->leader_codes;
   const float* ls = a->leader_scales;
   const float* ln = a->leader_norms;
@@ -539,8 +544,10 @@ int d0_device(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_i
     ls = ctx->d0_lscales.as<float>();
     ln = ctx->d0_lnorms.as<float>();
   }
+  CUDA_TRY(cudaEventRecord(ctx->d0_ev[1], st));
   TRY(launch_quantize_sq8(a->raw_vectors, rows, dim, P, 8, a->codes, a->scales, a->norms, ctx->d_err.as<uint32_t>(),
                           st));
+  CUDA_TRY(cudaEventRecord(ctx->d0_ev[2], st));
   RectLaunch R;
   R.row_codes = a->codes;
   R.rows = rows;
@@ -563,14 +570,28 @@ int d0_device(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_i
   R.sm_count = ctx->sm_count;
   int r = launch_rect_topk_sq8(R, st);
   if (r != TESSA_OK) return fail(r, "D0 assignment launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  CUDA_TRY(cudaEventRecord(ctx->d0_ev[3], st));
   r = launch_d0_fragments(R.out_keys, ctx->d0_k2l.as<uint32_t>(), a->global_ids, rows, f, L, a->child_ids,
                           a->point_ids, ctx->d_err.as<uint32_t>(), ctx->sm_count, st);
   if (r != TESSA_OK) return fail(r, "D0 fragment launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  CUDA_TRY(cudaEventRecord(ctx->d0_ev[4], st));
   uint32_t fb = 0;
   CUDA_TRY(cudaMemcpyAsync(&fb, R.d_fb_count, 4, cudaMemcpyDeviceToHost, st));
   uint32_t bits = 0;
   TRY(read_err(ctx, st, &bits));
   ctx->last_fallback_rows = fb;
+  float ms[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < 4; ++i) CUDA_TRY(cudaEventElapsedTime(&ms[i], ctx->d0_ev[i], ctx->d0_ev[i + 1]));
+  tessa_d0_profile& pr = ctx->d0_prof;
+  pr.leader_quantize_ms = a->leader_codes ? 0.0 : ms[0];
+  pr.quantize_ms = ms[1];
+  pr.assign_ms = ms[2];
+  pr.fragment_ms = ms[3];
+  pr.rows = rows;
+  pr.fallback_rows = fb;
+  pr.leaders = L;
+  pr.fanout = f;
+  pr.padded_dim = P;
   if (bits & TESSA_DEVERR_NONFINITE)
     return fail(TESSA_ERR_NONFINITE, "SQ GPU-D0 staging: non-finite input or distance (0x%x)", bits);
   return map_device_error(bits);
@@ -690,6 +711,8 @@ void tessa_destroy(tessa_ctx* ctx) {
       cudaStreamSynchronize(s);
       cudaStreamDestroy(s);
     }
+  for (cudaEvent_t e : ctx->d0_ev)
+    if (e) cudaEventDestroy(e);
   for (cudaEvent_t e : ctx->ev_in) cudaEventDestroy(e);
   for (cudaEvent_t e : ctx->ev_done) cudaEventDestroy(e);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -799,6 +822,12 @@ int tessa_leaf_topk_sq8_host(tessa_ctx* ctx, const tessa_leaf_args* a) {
     CUDA_TRY(cudaMemcpyAsync(a->topk_dists, ctx->h_dists.ptr, M * a->k * 4, cudaMemcpyDeviceToHost, st));
   }
   CUDA_TRY(cudaStreamSynchronize(st));
+  return TESSA_OK;
+}
+
+int tessa_d0_last_profile(const tessa_ctx* ctx, tessa_d0_profile* out) {
+  if (!ctx || !out) return fail(TESSA_ERR_INVALID_ARG, "null argument");
+  *out = ctx->d0_prof;
   return TESSA_OK;
 }
 

@@ -109,6 +109,16 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, void* smem_d
       : "memory");
 }
 
+// 1-D bulk copy from global memory into this CTA's shared memory (no
+// multicast); both addresses 16-byte aligned, `bytes` a multiple of 16;
+// completion is signalled on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // ------------------------------------------------------------- tcgen05 ---
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {

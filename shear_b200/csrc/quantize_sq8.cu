@@ -11,6 +11,9 @@
 #include "kernels.h"
 
 namespace tessa {
+
+constexpr uint64_t kQuantTimeoutNs = 2000000000ull;  // bounded pipeline waits: 2 s
+
 namespace quant {
 
 constexpr uint32_t kWarps = 4;
@@ -90,6 +93,221 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ------------------------------------------------------------ tiled path
+//
+// One persistent CTA per SM streams tiles of TR consecutive rows of x through
+// NBUF shared-memory buffers with plain bulk copies (cp.async.bulk, one per
+// row, into a padded row pitch), so every element is read from HBM once:
+//   warp 0       producer: refills a buffer when its consumers release it;
+//   warps 1..2   norms, alternate tiles: lane r walks row r front to back in
+//                the reference's sequential order (the pitch makes the lanes'
+//                float4 reads conflict-free);
+//   warps 3..18  per-row max |x| (order-free), scale, and codes, coalesced.
+// The norms and the codes read the same shared-memory tile.
+constexpr uint32_t kNormWarps = 2;
+constexpr uint32_t kQWarps = 16;          // code warps
+constexpr uint32_t kTWarps = 1 + kNormWarps + kQWarps;
+constexpr uint32_t kTThreads = kTWarps * 32;
+constexpr uint32_t kTMaxBufs = 4;
+constexpr uint32_t kTSmemBudget = 220u * 1024u;
+
+struct TiledPlan {
+  uint32_t tr;          // rows per tile (32, 16 or 8)
+  uint32_t nbuf;        // tile buffers
+  uint32_t pitch;       // bytes per staged row (16-byte multiple, odd in 16-byte units)
+};
+
+__host__ __device__ inline uint32_t tiled_pitch(uint32_t dim) {
+  uint32_t units = dim / 4u + 1u;  // dim % 4 == 0: dim*4 bytes + at least one 16-byte pad unit
+  if ((units & 1u) == 0u) ++units;
+  return units * 16u;
+}
+
+// max(a, |b|) propagating NaN (PTX max.NaN): a non-finite element leaves a
+// non-finite row maximum, so one test per row replaces one per element.
+__device__ __forceinline__ float max_abs_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(fabsf(b)));
+  return r;
+}
+
+// Code of v for a row with scale sc and r = fl(1/sc) (sc normal, r finite):
+// the reference's clamp(round_half_away(fl(v / sc))).  With q = fl(v * r),
+// |q - fl(v/sc)| < 2^-22 |q| (three roundings of relative size <= 2^-24), so
+// where q lies more than 2^-20 |q| from every half-integer, fl(v/sc) lies on
+// the same side of all of them and round_half_away(q) is the answer; q - t and
+// f - 0.5 are exact there.  Inside that band the exactly rounded quotient
+// decides (a few in 10^5 elements).
+__device__ __forceinline__ int sq8_code(float v, float sc, float r, float max_code) {
+  const float q = __fmul_rn(v, r);
+  const float t = truncf(q);
+  const float f = fabsf(__fsub_rn(q, t));
+  float n = f >= 0.5f ? __fadd_rn(t, copysignf(1.0f, q)) : t;
+  if (fabsf(__fsub_rn(f, 0.5f)) <= __fmul_rn(fabsf(q), 0x1p-20f)) n = roundf(__fdiv_rn(v, sc));
+  n = fminf(fmaxf(n, -max_code), max_code);
+  return (int)n;
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return ((uint32_t)a & 0xffu) | (((uint32_t)b & 0xffu) << 8) | (((uint32_t)c & 0xffu) << 16) |
+         ((uint32_t)d << 24);
+}
+
+__global__ void __launch_bounds__(kTThreads, 1)
+    sq8_quantize_tiled_kernel(const float* __restrict__ x, uint64_t rows, uint32_t dim, uint32_t padded,
+                              float max_code, TiledPlan plan, int8_t* __restrict__ codes,
+                              float* __restrict__ scales, float* __restrict__ norms, uint32_t* err_word,
+                              uint64_t timeout_ns) {
+  extern __shared__ __align__(128) uint8_t qsm[];
+  const uint32_t TR = plan.tr, NB = plan.nbuf, pitch = plan.pitch;
+  uint64_t* full = reinterpret_cast<uint64_t*>(qsm);
+  uint64_t* empty = full + kTMaxBufs;
+  uint32_t* abort_flag_p = reinterpret_cast<uint32_t*>(empty + kTMaxBufs);
+  uint8_t* tiles = qsm + 128;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  volatile uint32_t* abort_flag = abort_flag_p;
+  if (threadIdx.x == 0) {
+    for (uint32_t b = 0; b < NB; ++b) {
+      mbar_init(&full[b], 1);
+      mbar_init(&empty[b], 1 + kQWarps);  // the tile's norm warp + every code warp
+    }
+    *abort_flag_p = 0u;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint64_t ntiles = (rows + TR - 1) / TR;
+  const uint32_t row_bytes = dim * 4u;
+
+  if (warp == 0) {
+    uint32_t it = 0;
+    int32_t last_use[kTMaxBufs] = {-1, -1, -1, -1};
+    for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const uint32_t b = it % NB, use = it / NB;
+      const uint64_t r0 = t * TR;
+      const uint32_t nr = rows - r0 < TR ? (uint32_t)(rows - r0) : TR;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&empty[b], (use & 1u) ^ 1u, abort_flag, err_word, timeout_ns);
+      if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0u) break;
+      if (lane == 0) mbar_arrive_expect_tx(&full[b], nr * row_bytes);
+      __syncwarp();
+      uint8_t* dst = tiles + (size_t)b * TR * pitch;
+      for (uint32_t i = lane; i < nr; i += 32)
+        bulk_load(dst + i * pitch, x + (r0 + i) * dim, row_bytes, &full[b]);
+      last_use[b] = (int32_t)use;
+    }
+    // Copies still in flight (consumers that gave up) land before the CTA exits.
+    if (lane == 0) {
+      uint32_t no_abort = 0u;
+      for (uint32_t b = 0; b < NB; ++b)
+        if (last_use[b] >= 0) mbar_wait(&full[b], (uint32_t)last_use[b] & 1u, &no_abort, err_word, timeout_ns);
+    }
+  } else if (warp <= kNormWarps) {
+    const uint32_t nw = warp - 1;
+    uint32_t it = 0;
+    for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      if (it % kNormWarps != nw) continue;
+      const uint32_t b = it % NB, use = it / NB;
+      const uint64_t r0 = t * TR;
+      const uint32_t nr = rows - r0 < TR ? (uint32_t)(rows - r0) : TR;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&full[b], use & 1u, abort_flag, err_word, timeout_ns);
+      if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0u) break;
+      if (lane < nr) {
+        const float4* rowp = reinterpret_cast<const float4*>(tiles + ((size_t)b * TR + lane) * pitch);
+        float norm = 0.0f;
+        const uint32_t n4 = dim / 4u;
+#pragma unroll 4
+        for (uint32_t q = 0; q < n4; ++q) {
+          const float4 v = rowp[q];
+          norm = __fadd_rn(norm, __fmul_rn(v.x, v.x));
+          norm = __fadd_rn(norm, __fmul_rn(v.y, v.y));
+          norm = __fadd_rn(norm, __fmul_rn(v.z, v.z));
+          norm = __fadd_rn(norm, __fmul_rn(v.w, v.w));
+        }
+        norms[r0 + lane] = norm;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[b]);
+    }
+  } else {
+    const uint32_t qw = warp - 1 - kNormWarps;
+    uint32_t it = 0;
+    for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const uint32_t b = it % NB, use = it / NB;
+      const uint64_t r0 = t * TR;
+      const uint32_t nr = rows - r0 < TR ? (uint32_t)(rows - r0) : TR;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&full[b], use & 1u, abort_flag, err_word, timeout_ns);
+      if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0u) break;
+      for (uint32_t i = qw; i < nr; i += kQWarps) {
+        const float* rowp = reinterpret_cast<const float*>(tiles + ((size_t)b * TR + i) * pitch);
+        float m = 0.0f;
+        for (uint32_t c = lane * 4u; c < dim; c += 128u) {
+          const float4 v = *reinterpret_cast<const float4*>(rowp + c);
+          m = max_abs_nan(max_abs_nan(m, v.x), v.y);
+          m = max_abs_nan(max_abs_nan(m, v.z), v.w);
+        }
+#pragma unroll
+        for (uint32_t o = 16; o > 0; o >>= 1) {
+          const float other = __shfl_xor_sync(0xffffffffu, m, o);
+          asm("max.NaN.f32 %0, %0, %1;" : "+f"(m) : "f"(other));
+        }
+        const bool bad = !(m <= 3.402823466e+38F);  // NaN or inf somewhere in the row
+        const bool zero = m == 0.0f;
+        const float sc = zero ? 1.0f : __fdiv_rn(m, max_code);
+        const float r = __frcp_rn(sc);
+        const bool exact = !(fabsf(sc) >= 1.17549435e-38F) || !(fabsf(r) <= 3.402823466e+38F);
+        if (lane == 0) {
+          scales[r0 + i] = sc;
+          if (bad) atomicOr(err_word, TESSA_DEVERR_NONFINITE);
+        }
+        int8_t* orow = codes + (r0 + i) * padded;
+        for (uint32_t c = lane * 4u; c < padded; c += 128u) {
+          uint32_t w = 0;
+          if (!zero && c < dim) {  // dim % 4 == 0: all four columns are inside the row
+            const float4 v = *reinterpret_cast<const float4*>(rowp + c);
+            if (!exact) {
+              w = pack4(sq8_code(v.x, sc, r, max_code), sq8_code(v.y, sc, r, max_code),
+                        sq8_code(v.z, sc, r, max_code), sq8_code(v.w, sc, r, max_code));
+            } else {
+              const float vv[4] = {v.x, v.y, v.z, v.w};
+              int cq[4];
+#pragma unroll
+              for (uint32_t u = 0; u < 4; ++u)
+                cq[u] = (int)fminf(fmaxf(roundf(__fdiv_rn(vv[u], sc)), -max_code), max_code);
+              w = pack4(cq[0], cq[1], cq[2], cq[3]);
+            }
+          }
+          if ((padded & 3u) == 0u) {
+            *reinterpret_cast<uint32_t*>(orow + c) = w;
+          } else {
+            for (uint32_t u = 0; u < 4 && c + u < padded; ++u) orow[c + u] = (int8_t)((w >> (u * 8u)) & 0xffu);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[b]);
+    }
+  }
+}
+
+// Rows per tile and buffer count for the tiled path, or false if it does not apply.
+static bool tiled_plan(const float* x, uint32_t dim, TiledPlan* plan) {
+  if (dim == 0 || dim % 4u != 0u || (reinterpret_cast<uintptr_t>(x) & 15u) != 0u) return false;
+  const uint32_t pitch = tiled_pitch(dim);
+  for (uint32_t tr : {32u, 16u, 8u}) {
+    uint32_t nb = kTSmemBudget / (tr * pitch);
+    if (nb > kTMaxBufs) nb = kTMaxBufs;
+    if (nb >= 2) {
+      plan->tr = tr;
+      plan->nbuf = nb;
+      plan->pitch = pitch;
+      return true;
+    }
+  }
+  return false;
+}
+
 }  // namespace quant
 
 int launch_quantize_sq8(const float* x, uint64_t rows, uint32_t dim, uint32_t padded, uint32_t bits, int8_t* codes,
@@ -99,6 +317,18 @@ int launch_quantize_sq8(const float* x, uint64_t rows, uint32_t dim, uint32_t pa
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  quant::TiledPlan plan;
+  if (quant::tiled_plan(x, dim, &plan)) {
+    const uint32_t smem = 128u + plan.nbuf * plan.tr * plan.pitch;
+    if (cudaFuncSetAttribute(quant::sq8_quantize_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return TESSA_ERR_CUDA;
+    const uint64_t ntiles = (rows + plan.tr - 1) / plan.tr;
+    const uint32_t grid = ntiles < (uint64_t)sms ? (uint32_t)ntiles : (uint32_t)sms;
+    quant::sq8_quantize_tiled_kernel<<<grid, quant::kTThreads, smem, stream>>>(
+        x, rows, dim, padded, max_code, plan, codes, scales, norms, d_err, kQuantTimeoutNs);
+    return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+  }
   uint64_t blocks = ((rows + 31) / 32 + quant::kWarps - 1) / quant::kWarps;
   uint64_t cap = (uint64_t)sms * 16u;
   if (blocks > cap) blocks = cap;

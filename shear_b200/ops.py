@@ -267,6 +267,14 @@ class D0Result:
         return list(zip(c.tolist(), p.tolist()))
 
 
+def d0_last_profile(ctx: Context | None = None, device: int = 0) -> dict:
+    """Event-timed phases of the context's last D0 call (SqGpuD0StagingProfile's device walls)."""
+    ctx = ctx or context(device)
+    p = C.D0Profile()
+    C.check(C.load().tessa_d0_last_profile(ctx.handle, ctypes.byref(p)))
+    return {n: getattr(p, n) for n, _ in C.D0Profile._fields_}
+
+
 def _d0_leaders(leader_count, dim, leader_vectors, leader_payload):
     if leader_payload is None:
         if leader_vectors is None:
@@ -281,14 +289,15 @@ def _d0_leaders(leader_count, dim, leader_vectors, leader_payload):
 
 
 def quantize_sq8_and_assign_global_d0(raw_vectors, global_ids, global_d0_leader_ids, global_d0_leader_vectors,
-                                      fanout_top: int, leader_payload=None, device: int = 0) -> D0Result:
+                                      fanout_top: int, leader_payload=None, device: int = 0, out=None) -> D0Result:
     """Host form of the trait method quantize_sq8_and_assign_global_d0
     (compute_backend.rs:3828-3837; CUDA implementation :24281-24760; CPU
     reference P/dco_sq_int8.rs:1929-2070): numpy in, numpy out.
 
     raw_vectors [rows, dim] f32; global_ids [rows]; global_d0_leader_ids
     [leaders]; global_d0_leader_vectors [leaders, dim] f32 (ignored when
-    leader_payload = (codes, scales, norms) is given).
+    leader_payload = (codes, scales, norms) is given).  out = (codes, scales,
+    norms, child_ids, point_ids, dists) preallocated numpy arrays (e.g. pinned).
     """
     raw = np.ascontiguousarray(raw_vectors, dtype=np.float32)
     gids = np.ascontiguousarray(global_ids, dtype=np.uint32)
@@ -311,13 +320,20 @@ def quantize_sq8_and_assign_global_d0(raw_vectors, global_ids, global_d0_leader_
         ln = np.ascontiguousarray(ln, dtype=np.float32)
     f = int(fanout_top)
     pd = padded_dim(dim) if dim > 0 else 0
-    codes = np.zeros((rows, pd), dtype=np.int8)
-    scales = np.zeros(rows, dtype=np.float32)
-    norms = np.zeros(rows, dtype=np.float32)
     n = rows * max(f, 0)
-    child = np.zeros(n, dtype=np.uint32)
-    point = np.zeros(n, dtype=np.uint32)
-    dists = np.zeros(n, dtype=np.float32)
+    if out is None:
+        codes = np.zeros((rows, pd), dtype=np.int8)
+        scales = np.zeros(rows, dtype=np.float32)
+        norms = np.zeros(rows, dtype=np.float32)
+        child = np.zeros(n, dtype=np.uint32)
+        point = np.zeros(n, dtype=np.uint32)
+        dists = np.zeros(n, dtype=np.float32)
+    else:
+        codes, scales, norms, child, point, dists = out
+        if codes.size != rows * pd or scales.size != rows or norms.size != rows or child.size != n or \
+                point.size != n or dists.size != n:
+            raise ValueError("D0 output buffers have the wrong sizes")
+        codes = codes.reshape(rows, pd)
     a = C.D0Args(raw_vectors=raw.ctypes.data, global_ids=gids.ctypes.data, rows=rows, dim=dim, fanout_top=f,
                  leader_ids=lids.ctypes.data, leader_vectors=_np_ptr(lv).value, leader_codes=_np_ptr(lc).value,
                  leader_scales=_np_ptr(ls).value, leader_norms=_np_ptr(ln).value, leader_count=leaders,
@@ -329,11 +345,12 @@ def quantize_sq8_and_assign_global_d0(raw_vectors, global_ids, global_d0_leader_
 
 
 def quantize_sq8_assign_d0(x, global_ids, leader_ids, fanout_top: int, leader_vectors=None, leader_payload=None,
-                           ctx: Context | None = None) -> D0Result:
+                           ctx: Context | None = None, out=None) -> D0Result:
     """Device form: CUDA tensors in (x [rows, dim] f32, global_ids / leader_ids
     int32 bit patterns of uint32, leader_vectors [leaders, dim] f32 or
     leader_payload (codes, scales, norms)), CUDA tensors out, on the tensors'
-    current stream."""
+    current stream.  out = (codes, scales, norms, child_ids, point_ids, dists)
+    preallocated CUDA tensors."""
     import torch
 
     if not x.is_cuda or x.dtype != torch.float32 or x.dim() != 2:
@@ -346,13 +363,22 @@ def quantize_sq8_assign_d0(x, global_ids, leader_ids, fanout_top: int, leader_ve
     lv, lc, ls, ln = _d0_leaders(leaders, dim, leader_vectors, leader_payload)
     f = int(fanout_top)
     pd = padded_dim(dim)
-    codes = torch.empty((rows, pd), dtype=torch.int8, device=x.device)
-    scales = torch.empty(rows, dtype=torch.float32, device=x.device)
-    norms = torch.empty(rows, dtype=torch.float32, device=x.device)
     n = rows * max(f, 0)
-    child = torch.empty(n, dtype=torch.int32, device=x.device)
-    point = torch.empty(n, dtype=torch.int32, device=x.device)
-    dists = torch.empty(n, dtype=torch.float32, device=x.device)
+    if out is None:
+        codes = torch.empty((rows, pd), dtype=torch.int8, device=x.device)
+        scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+        norms = torch.empty(rows, dtype=torch.float32, device=x.device)
+        child = torch.empty(n, dtype=torch.int32, device=x.device)
+        point = torch.empty(n, dtype=torch.int32, device=x.device)
+        dists = torch.empty(n, dtype=torch.float32, device=x.device)
+    else:
+        codes, scales, norms, child, point, dists = out
+        if codes.numel() != rows * pd or scales.numel() != rows or norms.numel() != rows or \
+                child.numel() != n or point.numel() != n or dists.numel() != n:
+            raise ValueError("D0 output tensors have the wrong sizes")
+        if not all(t.is_contiguous() and t.is_cuda for t in out):
+            raise ValueError("D0 output tensors must be contiguous CUDA tensors")
+        codes = codes.view(rows, pd)
     c = lambda t: t.contiguous() if t is not None else None
     lv, lc, ls, ln = c(lv), c(lc), c(ls), c(ln)
     gid = global_ids.contiguous()
