@@ -99,20 +99,24 @@ __global__ void __launch_bounds__(kThreads)
 // NBUF shared-memory buffers with plain bulk copies (cp.async.bulk, one per
 // row, into a padded row pitch), so every element is read from HBM once:
 //   warp 0       producer: refills a buffer when its consumers release it;
-//   warps 1..2   norms, alternate tiles: lane r walks row r front to back in
+//   warps 1..4   norms, buffers in turn: lane r walks row r front to back in
 //                the reference's sequential order (the pitch makes the lanes'
 //                float4 reads conflict-free);
-//   warps 3..18  per-row max |x| (order-free), scale, and codes, coalesced.
+//   warps 5..20  per-row max |x| (order-free), scale, and codes, coalesced.
+// Tiles are kept small (<= 56 KiB) so that three or more are in flight per SM
+// while one is consumed: HBM latency x the per-SM share of bandwidth.
 // The norms and the codes read the same shared-memory tile.
-constexpr uint32_t kNormWarps = 2;
+constexpr uint32_t kNormWarps = 4;
 constexpr uint32_t kQWarps = 16;          // code warps
 constexpr uint32_t kTWarps = 1 + kNormWarps + kQWarps;
 constexpr uint32_t kTThreads = kTWarps * 32;
-constexpr uint32_t kTMaxBufs = 4;
+constexpr uint32_t kTMaxBufs = 8;
+constexpr uint32_t kTHeader = 256;       // barriers and the abort flag
 constexpr uint32_t kTSmemBudget = 220u * 1024u;
+constexpr uint32_t kTTileTarget = 56u * 1024u;  // small tiles: several in flight per SM
 
 struct TiledPlan {
-  uint32_t tr;          // rows per tile (32, 16 or 8)
+  uint32_t tr;          // rows per tile (32, 16, 8 or 4)
   uint32_t nbuf;        // tile buffers
   uint32_t pitch;       // bytes per staged row (16-byte multiple, odd in 16-byte units)
 };
@@ -133,24 +137,37 @@ __device__ __forceinline__ float max_abs_nan(float a, float b) {
 
 // Code of v for a row with scale sc and r = fl(1/sc) (sc normal, r finite):
 // the reference's clamp(round_half_away(fl(v / sc))).  With q = fl(v * r),
-// |q - fl(v/sc)| < 2^-22 |q| (three roundings of relative size <= 2^-24), so
-// where q lies more than 2^-20 |q| from every half-integer, fl(v/sc) lies on
-// the same side of all of them and round_half_away(q) is the answer; q - t and
-// f - 0.5 are exact there.  Inside that band the exactly rounded quotient
-// decides (a few in 10^5 elements).
-__device__ __forceinline__ int sq8_code(float v, float sc, float r, float max_code) {
+// |q - fl(v/sc)| < 2^-22 |q| (three roundings of relative size <= 2^-24).  If
+// q lies more than 2^-19 |q| from every half-integer, fl(v/sc) lies on the same
+// side of all of them and is no tie, so rint(q) (nearest, ties to even) is the
+// answer; e = q - rint(q) is exact, and the distance to the nearest
+// half-integer is 0.5 - |e|.  `near` reports the band where the exactly
+// rounded quotient must decide instead.  No clamp is needed here:
+// |v| <= max|x| gives |q| <= max_code * (1 + 4 * 2^-24) < max_code + 0.5.
+__device__ __forceinline__ int sq8_code_fast(float v, float r, bool& near) {
   const float q = __fmul_rn(v, r);
-  const float t = truncf(q);
-  const float f = fabsf(__fsub_rn(q, t));
-  float n = f >= 0.5f ? __fadd_rn(t, copysignf(1.0f, q)) : t;
-  if (fabsf(__fsub_rn(f, 0.5f)) <= __fmul_rn(fabsf(q), 0x1p-20f)) n = roundf(__fdiv_rn(v, sc));
-  n = fminf(fmaxf(n, -max_code), max_code);
+  const float n = rintf(q);
+  const float e = __fsub_rn(q, n);
+  near = __fmaf_rn(fabsf(q), 0x1p-19f, fabsf(e)) >= 0.5f;
   return (int)n;
 }
 
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d);
+
+// Exact codes of four elements (IEEE quotient, then round half away from zero).
+__device__ __noinline__ uint32_t sq8_codes4_exact(float a, float b, float c, float d, float sc, float max_code) {
+  const float vv[4] = {a, b, c, d};
+  int cq[4];
+#pragma unroll
+  for (uint32_t u = 0; u < 4; ++u) cq[u] = (int)fminf(fmaxf(roundf(__fdiv_rn(vv[u], sc)), -max_code), max_code);
+  return pack4(cq[0], cq[1], cq[2], cq[3]);
+}
+
+// Low bytes of a, b, c, d as one little-endian word.
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  return ((uint32_t)a & 0xffu) | (((uint32_t)b & 0xffu) << 8) | (((uint32_t)c & 0xffu) << 16) |
-         ((uint32_t)d << 24);
+  const uint32_t lo = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040u);
+  const uint32_t hi = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040u);
+  return __byte_perm(lo, hi, 0x5410u);
 }
 
 __global__ void __launch_bounds__(kTThreads, 1)
@@ -163,7 +180,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(qsm);
   uint64_t* empty = full + kTMaxBufs;
   uint32_t* abort_flag_p = reinterpret_cast<uint32_t*>(empty + kTMaxBufs);
-  uint8_t* tiles = qsm + 128;
+  uint8_t* tiles = qsm + kTHeader;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   volatile uint32_t* abort_flag = abort_flag_p;
   if (threadIdx.x == 0) {
@@ -180,7 +197,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
 
   if (warp == 0) {
     uint32_t it = 0;
-    int32_t last_use[kTMaxBufs] = {-1, -1, -1, -1};
+    int32_t last_use[kTMaxBufs];
+#pragma unroll
+    for (uint32_t b = 0; b < kTMaxBufs; ++b) last_use[b] = -1;
     for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const uint32_t b = it % NB, use = it / NB;
       const uint64_t r0 = t * TR;
@@ -202,10 +221,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
         if (last_use[b] >= 0) mbar_wait(&full[b], (uint32_t)last_use[b] & 1u, &no_abort, err_word, timeout_ns);
     }
   } else if (warp <= kNormWarps) {
+    // A norm warp owns whole buffers (b % kNormWarps == nw), so it observes
+    // every phase of the full barriers it waits on: a waiter that skipped a
+    // phase could take an older phase of the same parity for the current one.
     const uint32_t nw = warp - 1;
     uint32_t it = 0;
     for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-      if (it % kNormWarps != nw) continue;
+      if ((it % NB) % kNormWarps != nw) continue;
       const uint32_t b = it % NB, use = it / NB;
       const uint64_t r0 = t * TR;
       const uint32_t nr = rows - r0 < TR ? (uint32_t)(rows - r0) : TR;
@@ -266,17 +288,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
           uint32_t w = 0;
           if (!zero && c < dim) {  // dim % 4 == 0: all four columns are inside the row
             const float4 v = *reinterpret_cast<const float4*>(rowp + c);
-            if (!exact) {
-              w = pack4(sq8_code(v.x, sc, r, max_code), sq8_code(v.y, sc, r, max_code),
-                        sq8_code(v.z, sc, r, max_code), sq8_code(v.w, sc, r, max_code));
-            } else {
-              const float vv[4] = {v.x, v.y, v.z, v.w};
-              int cq[4];
-#pragma unroll
-              for (uint32_t u = 0; u < 4; ++u)
-                cq[u] = (int)fminf(fmaxf(roundf(__fdiv_rn(vv[u], sc)), -max_code), max_code);
-              w = pack4(cq[0], cq[1], cq[2], cq[3]);
-            }
+            bool n0, n1, n2, n3;
+            const int c0 = sq8_code_fast(v.x, r, n0), c1 = sq8_code_fast(v.y, r, n1);
+            const int c2 = sq8_code_fast(v.z, r, n2), c3 = sq8_code_fast(v.w, r, n3);
+            if (exact || n0 || n1 || n2 || n3)
+              w = sq8_codes4_exact(v.x, v.y, v.z, v.w, sc, max_code);
+            else
+              w = pack4(c0, c1, c2, c3);
           }
           if ((padded & 3u) == 0u) {
             *reinterpret_cast<uint32_t*>(orow + c) = w;
@@ -295,17 +313,15 @@ __global__ void __launch_bounds__(kTThreads, 1)
 static bool tiled_plan(const float* x, uint32_t dim, TiledPlan* plan) {
   if (dim == 0 || dim % 4u != 0u || (reinterpret_cast<uintptr_t>(x) & 15u) != 0u) return false;
   const uint32_t pitch = tiled_pitch(dim);
-  for (uint32_t tr : {32u, 16u, 8u}) {
-    uint32_t nb = kTSmemBudget / (tr * pitch);
-    if (nb > kTMaxBufs) nb = kTMaxBufs;
-    if (nb >= 2) {
-      plan->tr = tr;
-      plan->nbuf = nb;
-      plan->pitch = pitch;
-      return true;
-    }
-  }
-  return false;
+  uint32_t tr = 32u;
+  while (tr > 4u && tr * pitch > kTTileTarget) tr >>= 1;
+  uint32_t nb = kTSmemBudget / (tr * pitch);
+  if (nb > kTMaxBufs) nb = kTMaxBufs;
+  if (nb < 2) return false;
+  plan->tr = tr;
+  plan->nbuf = nb;
+  plan->pitch = pitch;
+  return true;
 }
 
 }  // namespace quant
@@ -319,7 +335,7 @@ int launch_quantize_sq8(const float* x, uint64_t rows, uint32_t dim, uint32_t pa
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   quant::TiledPlan plan;
   if (quant::tiled_plan(x, dim, &plan)) {
-    const uint32_t smem = 128u + plan.nbuf * plan.tr * plan.pitch;
+    const uint32_t smem = quant::kTHeader + plan.nbuf * plan.tr * plan.pitch;
     if (cudaFuncSetAttribute(quant::sq8_quantize_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return TESSA_ERR_CUDA;

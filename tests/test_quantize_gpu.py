@@ -6,7 +6,10 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("rows,dim", [(2, 3), (257, 100), (1000, 768), (64, 1024), (400_000, 8), (3, 2000),
-                                      (1001, 4), (77, 12), (50_000, 768), (300, 4096), (33, 36)])
+                                      (1001, 4), (77, 12), (50_000, 768), (300, 4096), (33, 36),
+                                      # enough rows that every CTA reuses its buffers (3, 4, 6 and 8 of them)
+                                      (40_000, 1024), (3_000, 4096), (30_000, 2000), (200_000, 128),
+                                      (100_000, 100), (60_000, 512)])
 def test_quantize_matches_cpu_bits(oracle, rows, dim):
     import torch
     from shear_b200 import ops
