@@ -556,6 +556,7 @@ def run_d0(a):
     per_step = total_s / a.steps
     value = world * rows / per_step
     ops_per_step = 2.0 * rows * L * pd
+    prof = ops.d0_last_profile(ctx)  # phases of the last timed step (before the host-buffer calls)
 
     e2e = None
     if not a.no_e2e and a.e2e_steps > 0:
@@ -623,7 +624,7 @@ def run_d0(a):
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": 5 * a.steps,  # leader quantize, row quantize, assignment, fallback, fragments
         "clocks": clk.summary(),
-        "profile_last_step": ops.d0_last_profile(ctx),
+        "profile_last_step": prof,
     }
     print(json.dumps(line), flush=True)
     if world > 1:

@@ -513,41 +513,48 @@ void d0_tie_keys(const uint32_t* ids, uint32_t n, std::vector<uint32_t>& key, st
   for (uint32_t r = 0; r < n; ++r) key[key_to_leader[r]] = r;
 }
 
-// Device-pointer D0 staging; h_leader_ids is a host copy of the leader ids.
-int d0_device(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_ids, cudaStream_t st) {
-  const uint64_t rows = a->rows;
-  const uint32_t dim = a->dim, L = a->leader_count, f = a->fanout_top;
+// Leader side of a D0 call: tie keys to the device, leaders quantized unless a
+// payload is given.  Sets the leader code / scale / norm pointers to use.
+int d0_prepare(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_ids, cudaStream_t st,
+               const int8_t** lc, const float** ls, const float** ln) {
+  const uint32_t dim = a->dim, L = a->leader_count;
   const uint32_t P = (dim + 15u) / 16u * 16u;
   std::vector<uint32_t> key, k2l;
   d0_tie_keys(h_leader_ids, L, key, k2l);
   TRY(ctx->d0_keys.ensure((size_t)L * 4));
   TRY(ctx->d0_k2l.ensure((size_t)L * 4));
-  TRY(ctx->d0_okeys.ensure(rows * f * 4));
-  TRY(ctx->fallback.ensure(16 + rows * 8));
-  if (!a->dists) TRY(ctx->d0_dists.ensure(rows * f * 4));
-  for (cudaEvent_t& e : ctx->d0_ev)
-    if (!e) CUDA_TRY(cudaEventCreate(&e));
   CUDA_TRY(cudaMemcpyAsync(ctx->d0_keys.ptr, key.data(), (size_t)L * 4, cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaMemcpyAsync(ctx->d0_k2l.ptr, k2l.data(), (size_t)L * 4, cudaMemcpyHostToDevice, st));
-  TRY(clear_err(ctx, st));
-  CUDA_TRY(cudaEventRecord(ctx->d0_ev[0], st));
-  const int8_t* lc = a->leader_codes;
-  const float* ls = a->leader_scales;
-  const float* ln = a->leader_norms;
-  if (!lc) {
+  *lc = a->leader_codes;
+  *ls = a->leader_scales;
+  *ln = a->leader_norms;
+  if (!*lc) {
     TRY(ctx->d0_lcodes.ensure((size_t)L * P));
     TRY(ctx->d0_lscales.ensure((size_t)L * 4));
     TRY(ctx->d0_lnorms.ensure((size_t)L * 4));
     TRY(launch_quantize_sq8(a->leader_vectors, L, dim, P, 8, ctx->d0_lcodes.as<int8_t>(), ctx->d0_lscales.as<float>(),
                             ctx->d0_lnorms.as<float>(), ctx->d_err.as<uint32_t>(), st));
-    lc = ctx->d0_lcodes.as<int8_t>();
-    ls = ctx->d0_lscales.as<float>();
-    ln = ctx->d0_lnorms.as<float>();
+    *lc = ctx->d0_lcodes.as<int8_t>();
+    *ls = ctx->d0_lscales.as<float>();
+    *ln = ctx->d0_lnorms.as<float>();
   }
-  CUDA_TRY(cudaEventRecord(ctx->d0_ev[1], st));
+  // The pageable key vectors must be consumed before they go out of scope.
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return TESSA_OK;
+}
+
+// Row side of a D0 call over a->rows rows (all pointers of `a` already at the
+// batch's first row): quantize, assign (top-fanout keys into okeys / dists),
+// fragments.  ev, if given, receives three events: after quantize, after
+// assignment, after fragments.  Does not wait.
+int d0_rows(tessa_ctx* ctx, const tessa_d0_args* a, const int8_t* lc, const float* ls, const float* ln,
+            uint32_t* okeys, float* dists, uint32_t* d_fb_count, cudaStream_t st, cudaEvent_t* ev) {
+  const uint64_t rows = a->rows;
+  const uint32_t dim = a->dim, L = a->leader_count, f = a->fanout_top;
+  const uint32_t P = (dim + 15u) / 16u * 16u;
   TRY(launch_quantize_sq8(a->raw_vectors, rows, dim, P, 8, a->codes, a->scales, a->norms, ctx->d_err.as<uint32_t>(),
                           st));
-  CUDA_TRY(cudaEventRecord(ctx->d0_ev[2], st));
+  if (ev) CUDA_TRY(cudaEventRecord(ev[0], st));
   RectLaunch R;
   R.row_codes = a->codes;
   R.rows = rows;
@@ -560,23 +567,51 @@ int d0_device(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_i
   R.col_norms = ln;
   R.col_keys = ctx->d0_keys.as<uint32_t>();
   R.k = f;
-  R.out_keys = ctx->d0_okeys.as<uint32_t>();
-  R.out_dists = a->dists ? a->dists : ctx->d0_dists.as<float>();
+  R.out_keys = okeys;
+  R.out_dists = dists;
   R.d_err = ctx->d_err.as<uint32_t>();
-  R.d_fb_count = ctx->fallback.as<uint32_t>();
+  R.d_fb_count = d_fb_count;
   R.d_fb_list = reinterpret_cast<uint2*>(ctx->fallback.as<uint8_t>() + 16);
   R.fb_capacity = (uint32_t)(rows < 0xffffffffull ? rows : 0xffffffffull);
   R.timeout_ns = ctx->timeout_ns;
   R.sm_count = ctx->sm_count;
   int r = launch_rect_topk_sq8(R, st);
   if (r != TESSA_OK) return fail(r, "D0 assignment launch failed: %s", cudaGetErrorString(cudaGetLastError()));
-  CUDA_TRY(cudaEventRecord(ctx->d0_ev[3], st));
-  r = launch_d0_fragments(R.out_keys, ctx->d0_k2l.as<uint32_t>(), a->global_ids, rows, f, L, a->child_ids,
-                          a->point_ids, ctx->d_err.as<uint32_t>(), ctx->sm_count, st);
+  if (ev) CUDA_TRY(cudaEventRecord(ev[1], st));
+  r = launch_d0_fragments(okeys, ctx->d0_k2l.as<uint32_t>(), a->global_ids, rows, f, L, a->child_ids, a->point_ids,
+                          ctx->d_err.as<uint32_t>(), ctx->sm_count, st);
   if (r != TESSA_OK) return fail(r, "D0 fragment launch failed: %s", cudaGetErrorString(cudaGetLastError()));
-  CUDA_TRY(cudaEventRecord(ctx->d0_ev[4], st));
+  if (ev) CUDA_TRY(cudaEventRecord(ev[2], st));
+  return TESSA_OK;
+}
+
+int d0_status(uint32_t bits) {
+  if (bits & TESSA_DEVERR_NONFINITE)
+    return fail(TESSA_ERR_NONFINITE, "SQ GPU-D0 staging: non-finite input or distance (0x%x)", bits);
+  return map_device_error(bits);
+}
+
+// Device-pointer D0 staging; h_leader_ids is a host copy of the leader ids.
+int d0_device(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_ids, cudaStream_t st) {
+  const uint64_t rows = a->rows;
+  const uint32_t L = a->leader_count, f = a->fanout_top;
+  TRY(ctx->d0_okeys.ensure(rows * f * 4));
+  TRY(ctx->fallback.ensure(16 + rows * 8));
+  if (!a->dists) TRY(ctx->d0_dists.ensure(rows * f * 4));
+  for (cudaEvent_t& e : ctx->d0_ev)
+    if (!e) CUDA_TRY(cudaEventCreate(&e));
+  TRY(clear_err(ctx, st));
+  CUDA_TRY(cudaEventRecord(ctx->d0_ev[0], st));
+  const int8_t* lc;
+  const float* ls;
+  const float* ln;
+  TRY(d0_prepare(ctx, a, h_leader_ids, st, &lc, &ls, &ln));
+  CUDA_TRY(cudaEventRecord(ctx->d0_ev[1], st));
+  uint32_t* d_fb = ctx->fallback.as<uint32_t>();
+  TRY(d0_rows(ctx, a, lc, ls, ln, ctx->d0_okeys.as<uint32_t>(), a->dists ? a->dists : ctx->d0_dists.as<float>(),
+              d_fb, st, &ctx->d0_ev[2]));
   uint32_t fb = 0;
-  CUDA_TRY(cudaMemcpyAsync(&fb, R.d_fb_count, 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaMemcpyAsync(&fb, d_fb, 4, cudaMemcpyDeviceToHost, st));
   uint32_t bits = 0;
   TRY(read_err(ctx, st, &bits));
   ctx->last_fallback_rows = fb;
@@ -591,10 +626,8 @@ int d0_device(tessa_ctx* ctx, const tessa_d0_args* a, const uint32_t* h_leader_i
   pr.fallback_rows = fb;
   pr.leaders = L;
   pr.fanout = f;
-  pr.padded_dim = P;
-  if (bits & TESSA_DEVERR_NONFINITE)
-    return fail(TESSA_ERR_NONFINITE, "SQ GPU-D0 staging: non-finite input or distance (0x%x)", bits);
-  return map_device_error(bits);
+  pr.padded_dim = (a->dim + 15u) / 16u * 16u;
+  return d0_status(bits);
 }
 
 int assign_device(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* a, cudaStream_t st) {
@@ -844,12 +877,18 @@ int tessa_quantize_sq8_assign_d0(tessa_ctx* ctx, const tessa_d0_args* a, void* s
   return d0_device(ctx, a, ids.data(), st);
 }
 
+// Host-buffer D0 staging.  Leaders are prepared once; the rows then go in
+// batches of about host_batch_bytes of f32 whose upload (copy stream), device
+// work (compute stream) and download (second copy stream) overlap those of the
+// neighbouring batches, ordered by events.
 int tessa_quantize_sq8_assign_d0_host(tessa_ctx* ctx, const tessa_d0_args* a) {
   TRY(bind(ctx));
   TRY(validate_d0(a));
   cudaStream_t st = ctx->stream;
   const uint64_t rows = a->rows, L = a->leader_count, f = a->fanout_top, dim = a->dim;
   const uint64_t P = (dim + 15) / 16 * 16;
+  if (!ctx->stream_in) CUDA_TRY(cudaStreamCreateWithFlags(&ctx->stream_in, cudaStreamNonBlocking));
+  if (!ctx->stream_out) CUDA_TRY(cudaStreamCreateWithFlags(&ctx->stream_out, cudaStreamNonBlocking));
   TRY(ctx->h_x.ensure(rows * dim * 4));
   TRY(ctx->h_gids.ensure(rows * 4));
   TRY(ctx->h_codes.ensure(rows * P));
@@ -858,9 +897,9 @@ int tessa_quantize_sq8_assign_d0_host(tessa_ctx* ctx, const tessa_d0_args* a) {
   TRY(ctx->d0_child.ensure(rows * f * 4));
   TRY(ctx->d0_point.ensure(rows * f * 4));
   TRY(ctx->h_dists.ensure(rows * f * 4));
+  TRY(ctx->d0_okeys.ensure(rows * f * 4));
+  TRY(ctx->fallback.ensure(16 + rows * 8));
   tessa_d0_args d = *a;
-  CUDA_TRY(cudaMemcpyAsync(ctx->h_x.ptr, a->raw_vectors, rows * dim * 4, cudaMemcpyHostToDevice, st));
-  CUDA_TRY(cudaMemcpyAsync(ctx->h_gids.ptr, a->global_ids, rows * 4, cudaMemcpyHostToDevice, st));
   if (a->leader_codes) {
     TRY(ctx->d0_lcodes.ensure(L * P));
     TRY(ctx->d0_lscales.ensure(L * 4));
@@ -877,27 +916,84 @@ int tessa_quantize_sq8_assign_d0_host(tessa_ctx* ctx, const tessa_d0_args* a) {
     CUDA_TRY(cudaMemcpyAsync(ctx->d0_lvec.ptr, a->leader_vectors, L * dim * 4, cudaMemcpyHostToDevice, st));
     d.leader_vectors = ctx->d0_lvec.as<float>();
   }
-  d.raw_vectors = ctx->h_x.as<float>();
-  d.global_ids = ctx->h_gids.as<uint32_t>();
-  d.codes = ctx->h_codes.as<int8_t>();
-  d.scales = ctx->h_scales.as<float>();
-  d.norms = ctx->h_norms.as<float>();
-  d.child_ids = ctx->d0_child.as<uint32_t>();
-  d.point_ids = ctx->d0_point.as<uint32_t>();
-  d.dists = ctx->h_dists.as<float>();
-  const int r = d0_device(ctx, &d, a->leader_ids, st);
-  if (r != TESSA_OK) {
-    cudaStreamSynchronize(st);
-    return r;
+  TRY(clear_err(ctx, st));
+  const int8_t* lc;
+  const float* ls;
+  const float* ln;
+  TRY(d0_prepare(ctx, &d, a->leader_ids, st, &lc, &ls, &ln));
+
+  const uint64_t per_batch = ctx->host_batch_bytes / (dim * 4);
+  const uint64_t min_rows = (rows + kMaxHostBatches - 1) / kMaxHostBatches;
+  const uint64_t brows = per_batch > min_rows ? per_batch : (min_rows ? min_rows : 1);
+  const size_t nb = (size_t)((rows + brows - 1) / brows);
+  while (ctx->ev_in.size() < nb) {
+    cudaEvent_t e;
+    CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    ctx->ev_in.push_back(e);
   }
-  CUDA_TRY(cudaMemcpyAsync(a->codes, d.codes, rows * P, cudaMemcpyDeviceToHost, st));
-  CUDA_TRY(cudaMemcpyAsync(a->scales, d.scales, rows * 4, cudaMemcpyDeviceToHost, st));
-  CUDA_TRY(cudaMemcpyAsync(a->norms, d.norms, rows * 4, cudaMemcpyDeviceToHost, st));
-  CUDA_TRY(cudaMemcpyAsync(a->child_ids, d.child_ids, rows * f * 4, cudaMemcpyDeviceToHost, st));
-  CUDA_TRY(cudaMemcpyAsync(a->point_ids, d.point_ids, rows * f * 4, cudaMemcpyDeviceToHost, st));
-  if (a->dists) CUDA_TRY(cudaMemcpyAsync(a->dists, d.dists, rows * f * 4, cudaMemcpyDeviceToHost, st));
-  CUDA_TRY(cudaStreamSynchronize(st));
-  return TESSA_OK;
+  while (ctx->ev_done.size() < nb) {
+    cudaEvent_t e;
+    CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    ctx->ev_done.push_back(e);
+  }
+  TRY(ctx->fb_counts.ensure(nb * 4));
+  CUDA_TRY(cudaMemsetAsync(ctx->fb_counts.ptr, 0, nb * 4, st));
+
+  auto issue = [&]() -> int {
+    for (size_t b = 0; b < nb; ++b) {
+      const uint64_t r0 = b * brows, n = rows - r0 < brows ? rows - r0 : brows;
+      cudaStream_t si = ctx->stream_in, so = ctx->stream_out;
+      tessa_d0_args v = d;
+      v.rows = n;
+      v.raw_vectors = ctx->h_x.as<float>() + r0 * dim;
+      v.global_ids = ctx->h_gids.as<uint32_t>() + r0;
+      v.codes = ctx->h_codes.as<int8_t>() + r0 * P;
+      v.scales = ctx->h_scales.as<float>() + r0;
+      v.norms = ctx->h_norms.as<float>() + r0;
+      v.child_ids = ctx->d0_child.as<uint32_t>() + r0 * f;
+      v.point_ids = ctx->d0_point.as<uint32_t>() + r0 * f;
+      v.dists = ctx->h_dists.as<float>() + r0 * f;
+      CUDA_TRY(cudaMemcpyAsync(const_cast<float*>(v.raw_vectors), a->raw_vectors + r0 * dim, n * dim * 4,
+                               cudaMemcpyHostToDevice, si));
+      CUDA_TRY(cudaMemcpyAsync(const_cast<uint32_t*>(v.global_ids), a->global_ids + r0, n * 4,
+                               cudaMemcpyHostToDevice, si));
+      CUDA_TRY(cudaEventRecord(ctx->ev_in[b], si));
+      CUDA_TRY(cudaStreamWaitEvent(st, ctx->ev_in[b], 0));
+      TRY(d0_rows(ctx, &v, lc, ls, ln, ctx->d0_okeys.as<uint32_t>() + r0 * f, v.dists,
+                  ctx->fb_counts.as<uint32_t>() + b, st, nullptr));
+      CUDA_TRY(cudaEventRecord(ctx->ev_done[b], st));
+      CUDA_TRY(cudaStreamWaitEvent(so, ctx->ev_done[b], 0));
+      CUDA_TRY(cudaMemcpyAsync(a->codes + r0 * P, v.codes, n * P, cudaMemcpyDeviceToHost, so));
+      CUDA_TRY(cudaMemcpyAsync(a->scales + r0, v.scales, n * 4, cudaMemcpyDeviceToHost, so));
+      CUDA_TRY(cudaMemcpyAsync(a->norms + r0, v.norms, n * 4, cudaMemcpyDeviceToHost, so));
+      CUDA_TRY(cudaMemcpyAsync(a->child_ids + r0 * f, v.child_ids, n * f * 4, cudaMemcpyDeviceToHost, so));
+      CUDA_TRY(cudaMemcpyAsync(a->point_ids + r0 * f, v.point_ids, n * f * 4, cudaMemcpyDeviceToHost, so));
+      if (a->dists) CUDA_TRY(cudaMemcpyAsync(a->dists + r0 * f, v.dists, n * f * 4, cudaMemcpyDeviceToHost, so));
+    }
+    return TESSA_OK;
+  };
+  const int r = issue();
+  const cudaError_t e_in = cudaStreamSynchronize(ctx->stream_in);
+  const cudaError_t e_st = cudaStreamSynchronize(st);
+  const cudaError_t e_out = cudaStreamSynchronize(ctx->stream_out);
+  if (r != TESSA_OK) return r;
+  for (cudaError_t e : {e_in, e_st, e_out})
+    if (e != cudaSuccess) return fail(TESSA_ERR_CUDA, "D0 pipeline: %s", cudaGetErrorString(e));
+  std::vector<uint32_t> fb(nb);
+  CUDA_TRY(cudaMemcpyAsync(fb.data(), ctx->fb_counts.ptr, nb * 4, cudaMemcpyDeviceToHost, st));
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  uint64_t total = 0;
+  for (uint32_t c : fb) total += c;
+  ctx->last_fallback_rows = total;
+  tessa_d0_profile& pr = ctx->d0_prof;
+  pr = tessa_d0_profile{};  // phases overlap across batches: no per-phase times
+  pr.rows = rows;
+  pr.fallback_rows = total;
+  pr.leaders = (uint32_t)L;
+  pr.fanout = (uint32_t)f;
+  pr.padded_dim = (uint32_t)P;
+  return d0_status(bits);
 }
 
 int tessa_assign(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* args, void* stream) {

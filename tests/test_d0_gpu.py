@@ -121,3 +121,22 @@ def test_d0_rejects_invalid_requests():
     # the context stays usable after an error
     got = ops.quantize_sq8_and_assign_global_d0(np.ones((1, 4), np.float32), [9], [1, 2], lv, 2)
     assert got.fragments() == [(0, 9), (1, 9)]
+
+
+def test_d0_host_pipeline_batches(oracle):
+    # ~256 rows of f32 per batch: the host call uploads, assigns and downloads
+    # in a dozen overlapping batches; results equal the single-call oracle.
+    from shear_b200 import ops, TessaError
+    raw, gids, lids, lv = random_case(3000, 64, 150, seed=21, near_dup_leaders=20)
+    want = oracle.d0_assign(raw, gids, lids, lv, 7)
+    try:
+        ops.set_host_batch_bytes(256 * 64 * 4)
+        got = ops.quantize_sq8_and_assign_global_d0(raw, gids, lids, lv, 7)
+        _same(got, want)
+        bad = raw.copy()
+        bad[1700, 5] = np.inf
+        with pytest.raises(TessaError, match="NONFINITE"):
+            ops.quantize_sq8_and_assign_global_d0(bad, gids, lids, lv, 7)
+        _same(ops.quantize_sq8_and_assign_global_d0(raw, gids, lids, lv, 7), want)
+    finally:
+        ops.set_host_batch_bytes(0)
