@@ -276,6 +276,42 @@ TESSA_API int tessa_quantize_sq8_assign_d0(tessa_ctx* ctx, const tessa_d0_args* 
  * and downloads (the form the trait method binds). */
 TESSA_API int tessa_quantize_sq8_assign_d0_host(tessa_ctx* ctx, const tessa_d0_args* args);
 
+/* ------------------------------------------------------ candidate edges --- */
+
+/* Largest sketch width / hash bit count (compute_hash asserts m_bits <= 16,
+ * P/hash_prune.rs:2239-2241). */
+#define TESSA_MAX_HASH_BITS 16
+
+/* Per-point sketches for the HashPrune reducer: sketches[i*m + h] = the f32
+ * sum over axes in order of x[i][a] * hyperplanes[h][a], one rounding per
+ * multiply and per add -- fill_sketch_row (P/hash_prune.rs:2208-2232) as
+ * compute_sketches_from_store calls it (:2155-2194).  The hyperplanes (m x dim,
+ * from generate_hyperplanes, :2196-2206) are an input.  Device pointers. */
+TESSA_API int tessa_sketch_rows(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t dim, const float* hyperplanes,
+                                uint32_t m, float* sketches, void* stream);
+
+/* Both personalised-residual hashes of every (row, rank) slot of a leaf
+ * batch, for the edge flush of flush_compact_topk_batch_into_edges
+ * (P/leaf_build.rs:1749-1808): with i = point_ids[row], j = topk_ids[row*k +
+ * rank], hash_fwd = compute_hash(sketch_i, sketch_j) and hash_rev =
+ * compute_hash(sketch_j, sketch_i) (P/hash_prune.rs:2239-2251: bit b set iff
+ * sketch_c[b] - sketch_p[b] >= 0).  Sketch rows are indexed by global point id
+ * (the reference's SketchStore), sketch_width floats apart; slots whose id is
+ * 0xffffffff get 0.  Device pointers. */
+TESSA_API int tessa_edge_hashes(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids, uint64_t rows,
+                                uint32_t k, const float* sketches, uint64_t sketch_rows, uint32_t sketch_width,
+                                uint32_t m_bits, uint16_t* hash_fwd, uint16_t* hash_rev, void* stream);
+
+/* Host-side edge expansion of a leaf batch in the reference's order
+ * (P/leaf_build.rs:1749-1808): for each row, each rank with a valid id and a
+ * finite distance, the edge (i -> j, hash_fwd, d) then (j -> i, hash_rev, d).
+ * Host pointers; no device work.  With edge_p == NULL (or a capacity below the
+ * count) only *edge_count is set; `threads` host threads (0 = 1). */
+TESSA_API int tessa_expand_edges(const uint32_t* point_ids, const uint32_t* topk_ids, const float* topk_dists,
+                                 const uint16_t* hash_fwd, const uint16_t* hash_rev, uint64_t rows, uint32_t k,
+                                 uint32_t threads, uint32_t* edge_p, uint32_t* edge_c, uint16_t* edge_hash,
+                                 float* edge_dist, uint64_t capacity, uint64_t* edge_count);
+
 /* ------------------------------------------------------- replay session --- */
 
 /* TessaPreparedReplay (P/tessa_replay.rs:1052-1074) as host arrays. */

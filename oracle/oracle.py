@@ -65,6 +65,13 @@ def _declare(L):
     L.oracle_d0_assign_sq8.argtypes = [_p(np.int8), _p(np.float32), _p(np.float32), u64, u32, _p(np.int8),
                                        _p(np.float32), _p(np.float32), _p(np.uint32), u32, u32,
                                        _p(np.uint32), _p(np.float32)]
+    L.oracle_sketch_rows.restype = None
+    L.oracle_sketch_rows.argtypes = [_p(np.float32), u64, u32, _p(np.float32), u32, _p(np.float32)]
+    L.oracle_compute_hash.restype = u32
+    L.oracle_compute_hash.argtypes = [_p(np.float32), _p(np.float32), u32]
+    L.oracle_flush_edges.restype = u64
+    L.oracle_flush_edges.argtypes = [_p(np.uint32), _p(np.uint32), _p(np.float32), u64, u32, _p(np.float32), u32, u32,
+                                     _p(np.uint32), _p(np.uint32), _p(np.uint16), _p(np.float32), u64]
     L.oracle_hash64.argtypes = [u64]
     L.oracle_assignment_tie_key.restype = u64
     L.oracle_assignment_tie_key.argtypes = [u32, u32]
@@ -175,6 +182,39 @@ def d0_assign(raw_vectors, global_ids, leader_ids, leader_vectors, fanout_top, l
     return dict(codes=codes, scales=scales, norms=norms, child_ids=child.reshape(rows, fanout_top),
                 point_ids=np.repeat(gids, fanout_top).reshape(rows, fanout_top),
                 dists=dists.reshape(rows, fanout_top))
+
+
+def sketch_rows(x, planes):
+    """P/hash_prune.rs:2208-2232 fill_sketch_row for every row -> [rows, m] f32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    planes = np.ascontiguousarray(planes, dtype=np.float32)
+    rows, dim = x.shape
+    m = planes.shape[0]
+    out = np.zeros((rows, m), np.float32)
+    lib().oracle_sketch_rows(x.reshape(-1), rows, dim, planes.reshape(-1), m, out.reshape(-1))
+    return out
+
+
+def compute_hash(sketch_p, sketch_c, m_bits: int) -> int:
+    """P/hash_prune.rs:2239-2251."""
+    return int(lib().oracle_compute_hash(np.ascontiguousarray(sketch_p, np.float32),
+                                         np.ascontiguousarray(sketch_c, np.float32), m_bits))
+
+
+def flush_edges(point_ids, topk_ids, topk_dists, k, sketches, m_bits):
+    """P/leaf_build.rs:1749-1808: (p, c, hash, dist) edge arrays in the reference's order."""
+    pid = np.ascontiguousarray(point_ids, np.uint32)
+    ids = np.ascontiguousarray(topk_ids, np.uint32).reshape(-1)
+    ds = np.ascontiguousarray(topk_dists, np.float32).reshape(-1)
+    sk = np.ascontiguousarray(sketches, np.float32)
+    rows = pid.shape[0]
+    z = np.zeros(0, np.uint32)
+    n = int(lib().oracle_flush_edges(pid, ids, ds, rows, k, sk.reshape(-1), sk.shape[1], m_bits, z, z,
+                                     np.zeros(0, np.uint16), np.zeros(0, np.float32), 0))
+    p, c = np.zeros(n, np.uint32), np.zeros(n, np.uint32)
+    h, d = np.zeros(n, np.uint16), np.zeros(n, np.float32)
+    lib().oracle_flush_edges(pid, ids, ds, rows, k, sk.reshape(-1), sk.shape[1], m_bits, p, c, h, d, n)
+    return p, c, h, d
 
 
 def assign(mode, x, norms, codes, scales, global_ids, members, leaders, task_member_offsets,

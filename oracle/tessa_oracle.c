@@ -290,6 +290,72 @@ int oracle_d0_assign_sq8(const int8_t* codes, const float* scales, const float* 
     return ORACLE_OK;
 }
 
+/* ------------------------------------------------ candidate edges --- */
+
+/*
+ * P/hash_prune.rs:2208-2232 fill_sketch_row: out[i*m + h] = sum over axes in
+ * order of x[i][a] * planes[h][a], f32, `acc += a * b` (one rounding each).
+ */
+void oracle_sketch_rows(const float* x, uint64_t rows, uint32_t dim, const float* planes, uint32_t m,
+                        float* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)rows; ++i) {
+        const float* xi = x + (uint64_t)i * dim;
+        for (uint32_t h = 0; h < m; ++h) {
+            const float* ph = planes + (uint64_t)h * dim;
+            float acc = 0.0f;
+            for (uint32_t a = 0; a < dim; ++a) {
+                float prod = xi[a] * ph[a];
+                acc = acc + prod;
+            }
+            out[(uint64_t)i * m + h] = acc;
+        }
+    }
+}
+
+/* P/hash_prune.rs:2239-2251 compute_hash: bit b = (c[b] - p[b] >= 0). */
+uint32_t oracle_compute_hash(const float* sketch_p, const float* sketch_c, uint32_t m_bits) {
+    uint32_t h = 0;
+    for (uint32_t b = 0; b < m_bits; ++b) {
+        float diff = sketch_c[b] - sketch_p[b];
+        if (diff >= 0.0f) h |= 1u << b;
+    }
+    return h;
+}
+
+/*
+ * P/leaf_build.rs:1749-1808 (flush_compact_topk_batch_into_edges without
+ * evidence annotation or lune pruning): for each row i and rank r whose id j
+ * is not u32::MAX and whose distance d is finite, the edge
+ * (point_ids[i] -> j, compute_hash(s_i, s_j), d) then (j -> point_ids[i],
+ * compute_hash(s_j, s_i), d).  Sketch rows are indexed by global point id.
+ * Returns the edge count (edges written only if it fits `capacity`).
+ */
+uint64_t oracle_flush_edges(const uint32_t* point_ids, const uint32_t* topk_ids, const float* topk_dists,
+                            uint64_t rows, uint32_t k, const float* sketches, uint32_t width,
+                            uint32_t m_bits, uint32_t* out_p, uint32_t* out_c, uint16_t* out_hash,
+                            float* out_dist, uint64_t capacity) {
+    uint64_t e = 0;
+    for (uint64_t i = 0; i < rows; ++i) {
+        uint32_t pi = point_ids[i];
+        const float* si = sketches + (uint64_t)pi * width;
+        for (uint32_t r = 0; r < k; ++r) {
+            uint32_t j = topk_ids[i * k + r];
+            float d = topk_dists[i * k + r];
+            if (j == EMPTY_ID || !isfinite(d)) continue;
+            const float* sj = sketches + (uint64_t)j * width;
+            if (e + 2 <= capacity) {
+                out_p[e] = pi; out_c[e] = j; out_hash[e] = (uint16_t)oracle_compute_hash(si, sj, m_bits);
+                out_dist[e] = d;
+                out_p[e + 1] = j; out_c[e + 1] = pi;
+                out_hash[e + 1] = (uint16_t)oracle_compute_hash(sj, si, m_bits); out_dist[e + 1] = d;
+            }
+            e += 2;
+        }
+    }
+    return e;
+}
+
 /* --------------------------------------------------------- assignment --- */
 
 /* CB:5983-5989 gpu_persistent_hash64 (splitmix64 finaliser). */

@@ -27,6 +27,7 @@ ERRORS = {
 MAX_LEAF_K = 32
 MAX_RH = 4
 MAX_PADDED_DIM = 1024
+MAX_HASH_BITS = 16
 NOALLOC_SCRATCH_BYTES = 64 << 20
 ASSIGN_FP32 = 0
 ASSIGN_SQ8 = 2
@@ -131,6 +132,14 @@ SIGNATURES = [
     ("tessa_quantize_sq8_assign_d0", ctypes.c_int, [c_vp, ctypes.POINTER(D0Args), c_vp]),
     ("tessa_quantize_sq8_assign_d0_host", ctypes.c_int, [c_vp, ctypes.POINTER(D0Args)]),
     ("tessa_d0_last_profile", ctypes.c_int, [c_vp, ctypes.POINTER(D0Profile)]),
+    ("tessa_sketch_rows", ctypes.c_int,
+     [c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, c_vp, ctypes.c_uint32, c_vp, c_vp]),
+    ("tessa_edge_hashes", ctypes.c_int,
+     [c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32,
+      c_vp, c_vp, c_vp]),
+    ("tessa_expand_edges", ctypes.c_int,
+     [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp,
+      ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     ("tessa_replay_session_create", ctypes.c_int,
      [ctypes.c_int, ctypes.POINTER(PreparedReplay), ctypes.POINTER(c_vp)]),
     ("tessa_replay_run_mode", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(ModeResult)]),

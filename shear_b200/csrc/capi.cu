@@ -996,6 +996,55 @@ int tessa_quantize_sq8_assign_d0_host(tessa_ctx* ctx, const tessa_d0_args* a) {
   return d0_status(bits);
 }
 
+int tessa_sketch_rows(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t dim, const float* hyperplanes,
+                      uint32_t m, float* sketches, void* stream) {
+  TRY(bind(ctx));
+  if (m == 0 || m > TESSA_MAX_HASH_BITS)
+    return fail(TESSA_ERR_INVALID_ARG, "sketch width m=%u outside 1..%d", m, TESSA_MAX_HASH_BITS);
+  if (dim == 0) return fail(TESSA_ERR_INVALID_ARG, "sketches require dim > 0");
+  if (rows && (!x || !hyperplanes || !sketches)) return fail(TESSA_ERR_INVALID_ARG, "null pointer");
+  const int r = launch_sketch_rows(x, rows, dim, hyperplanes, m, sketches, ctx->sm_count, (cudaStream_t)stream);
+  if (r != TESSA_OK) return fail(r, "sketch launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return TESSA_OK;
+}
+
+int tessa_edge_hashes(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids, uint64_t rows, uint32_t k,
+                      const float* sketches, uint64_t sketch_rows, uint32_t sketch_width, uint32_t m_bits,
+                      uint16_t* hash_fwd, uint16_t* hash_rev, void* stream) {
+  TRY(bind(ctx));
+  if (m_bits == 0 || m_bits > TESSA_MAX_HASH_BITS || m_bits > sketch_width)
+    return fail(TESSA_ERR_INVALID_ARG, "m_bits=%u outside 1..min(%d, sketch width %u)", m_bits, TESSA_MAX_HASH_BITS,
+                sketch_width);
+  if (rows && k && (!point_ids || !topk_ids || !sketches || !hash_fwd || !hash_rev))
+    return fail(TESSA_ERR_INVALID_ARG, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  TRY(clear_err(ctx, st));
+  const int r = launch_edge_hashes(point_ids, topk_ids, rows, k, sketches, sketch_rows, sketch_width, m_bits,
+                                   hash_fwd, hash_rev, ctx->d_err.as<uint32_t>(), ctx->sm_count, st);
+  if (r != TESSA_OK) return fail(r, "edge hash launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  if (bits & TESSA_DEVERR_BAD_ROW) return fail(TESSA_ERR_BAD_ROW, "leaf slot or row id outside the sketch store");
+  return map_device_error(bits);
+}
+
+int tessa_expand_edges(const uint32_t* point_ids, const uint32_t* topk_ids, const float* topk_dists,
+                       const uint16_t* hash_fwd, const uint16_t* hash_rev, uint64_t rows, uint32_t k, uint32_t threads,
+                       uint32_t* edge_p, uint32_t* edge_c, uint16_t* edge_hash, float* edge_dist, uint64_t capacity,
+                       uint64_t* edge_count) {
+  if (!edge_count) return fail(TESSA_ERR_INVALID_ARG, "null edge_count");
+  *edge_count = 0;
+  if (rows && k && (!point_ids || !topk_ids || !topk_dists || !hash_fwd || !hash_rev))
+    return fail(TESSA_ERR_INVALID_ARG, "null input pointer");
+  if (edge_p && (!edge_c || !edge_hash || !edge_dist)) return fail(TESSA_ERR_INVALID_ARG, "null output pointer");
+  *edge_count = expand_edges_host(point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, rows, k, edge_p, edge_c,
+                                  edge_hash, edge_dist, capacity, threads);
+  if (edge_p && *edge_count > capacity)
+    return fail(TESSA_ERR_INVALID_ARG, "edge capacity %llu below the %llu edges", (unsigned long long)capacity,
+                (unsigned long long)*edge_count);
+  return TESSA_OK;
+}
+
 int tessa_assign(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* args, void* stream) {
   TRY(bind(ctx));
   return assign_device(ctx, source, args, (cudaStream_t)stream);

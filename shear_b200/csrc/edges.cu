@@ -1,0 +1,189 @@
+// Candidate edges of the leaf lists for the host reducer (HashPrune / TierLift):
+// per-point sketches, the two personalised-residual hashes of every leaf slot,
+// and the forward / reverse edge expansion in the reference's order.
+//
+// Reference (wbh1765091327/SHEAR, P = shear-core/src/algorithm/pipnn/):
+//   * sketch of point i, hyperplane h = sum over axes in order of x[a] * H[h][a]
+//     in f32, one rounding per multiply and per add (`acc += a * b`,
+//     P/hash_prune.rs:2208-2232 fill_sketch_row; the hyperplanes come from
+//     generate_hyperplanes, :2196-2206, and are an input here);
+//   * compute_hash(p, c): bit b = (sketch_c[b] - sketch_p[b] >= 0)
+//     (P/hash_prune.rs:2239-2251);
+//   * per leaf row i and rank r with j = topk_ids[i*k+r] != u32::MAX and a
+//     finite distance d: edge (i -> j, compute_hash(s_i, s_j), d), then
+//     (j -> i, compute_hash(s_j, s_i), d)  (P/leaf_build.rs:1749-1808).
+//
+// B200 split: the GPU computes the sketches (HBM-bound, one pass over the
+// rows) and the two 16-bit hashes of every leaf slot right after the leaf
+// kernel (4 bytes per slot next to the 8 bytes of ids and distances the host
+// receives anyway); the host then expands edges with no sketch gathers.
+#include <algorithm>
+#include <cmath>
+#include <thread>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tessa {
+namespace edges {
+
+constexpr uint32_t kSkWarps = 8;
+constexpr uint32_t kSkThreads = kSkWarps * 32;
+constexpr uint32_t kMaxPlanes = 16;
+
+// One warp per 32 rows: 32 x 32 slabs of x go through shared memory with
+// coalesced loads (lane = column); then lane r walks row r's slab in axis
+// order and advances its m sequential sums (m independent chains).
+__global__ void __launch_bounds__(kSkThreads)
+    sketch_rows_kernel(const float* __restrict__ x, uint64_t rows, uint32_t dim, const float* __restrict__ planes,
+                       uint32_t m, float* __restrict__ out) {
+  __shared__ float tile[kSkWarps][32][33];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint64_t nblk = (rows + 31) / 32;
+  for (uint64_t blk = blockIdx.x * (uint64_t)kSkWarps + warp; blk < nblk; blk += (uint64_t)gridDim.x * kSkWarps) {
+    const uint64_t r0 = blk * 32;
+    const uint32_t nr = rows - r0 < 32 ? (uint32_t)(rows - r0) : 32u;
+    float acc[kMaxPlanes];
+#pragma unroll
+    for (uint32_t h = 0; h < kMaxPlanes; ++h) acc[h] = 0.0f;
+    for (uint32_t c0 = 0; c0 < dim; c0 += 32) {
+      const uint32_t nc = dim - c0 < 32 ? dim - c0 : 32u;
+      if (lane < nc) {
+#pragma unroll 8
+        for (uint32_t i = 0; i < 32; ++i) tile[warp][i][lane] = i < nr ? __ldg(x + (r0 + i) * dim + c0 + lane) : 0.0f;
+      }
+      __syncwarp();
+      for (uint32_t j = 0; j < nc; ++j) {
+        const float v = tile[warp][lane][j];
+        const float* hp = planes + c0 + j;
+#pragma unroll
+        for (uint32_t h = 0; h < kMaxPlanes; ++h)
+          if (h < m) acc[h] = __fadd_rn(acc[h], __fmul_rn(v, __ldg(hp + (uint64_t)h * dim)));
+      }
+      __syncwarp();
+    }
+    if (lane < nr) {
+      float* o = out + (r0 + lane) * m;
+#pragma unroll
+      for (uint32_t h = 0; h < kMaxPlanes; ++h)
+        if (h < m) o[h] = acc[h];
+    }
+  }
+}
+
+// Both hashes of every (row, rank) slot of a leaf batch.  Slots without a
+// candidate (id 0xffffffff) get 0; ids outside the sketch store are flagged.
+__global__ void edge_hashes_kernel(const uint32_t* __restrict__ point_ids, const uint32_t* __restrict__ topk_ids,
+                                   uint64_t rows, uint32_t k, const float* __restrict__ sketches,
+                                   uint64_t sketch_rows, uint32_t width, uint32_t m_bits,
+                                   uint16_t* __restrict__ hash_fwd, uint16_t* __restrict__ hash_rev,
+                                   uint32_t* __restrict__ err) {
+  const uint64_t n = rows * k;
+  for (uint64_t s = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; s < n; s += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t i = point_ids[s / k];
+    const uint32_t j = topk_ids[s];
+    uint32_t hf = 0, hr = 0;
+    if (j != 0xffffffffu) {
+      if (i >= sketch_rows || j >= sketch_rows) {
+        atomicOr(err, TESSA_DEVERR_BAD_ROW);
+      } else {
+        const float* si = sketches + (uint64_t)i * width;
+        const float* sj = sketches + (uint64_t)j * width;
+        for (uint32_t b = 0; b < m_bits; ++b) {
+          const float a = __ldg(si + b), c = __ldg(sj + b);
+          hf |= (__fsub_rn(c, a) >= 0.0f ? 1u : 0u) << b;
+          hr |= (__fsub_rn(a, c) >= 0.0f ? 1u : 0u) << b;
+        }
+      }
+    }
+    hash_fwd[s] = (uint16_t)hf;
+    hash_rev[s] = (uint16_t)hr;
+  }
+}
+
+}  // namespace edges
+
+int launch_sketch_rows(const float* x, uint64_t rows, uint32_t dim, const float* planes, uint32_t m, float* out,
+                       int sm_count, cudaStream_t stream) {
+  if (rows == 0) return TESSA_OK;
+  if (m == 0 || m > edges::kMaxPlanes) return TESSA_ERR_INVALID_ARG;
+  uint64_t blocks = ((rows + 31) / 32 + edges::kSkWarps - 1) / edges::kSkWarps;
+  const uint64_t cap = (uint64_t)sm_count * 8u;
+  if (blocks > cap) blocks = cap;
+  edges::sketch_rows_kernel<<<(unsigned)blocks, edges::kSkThreads, 0, stream>>>(x, rows, dim, planes, m, out);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+int launch_edge_hashes(const uint32_t* point_ids, const uint32_t* topk_ids, uint64_t rows, uint32_t k,
+                       const float* sketches, uint64_t sketch_rows, uint32_t width, uint32_t m_bits,
+                       uint16_t* hash_fwd, uint16_t* hash_rev, uint32_t* d_err, int sm_count, cudaStream_t stream) {
+  const uint64_t n = rows * k;
+  if (n == 0) return TESSA_OK;
+  uint64_t blocks = (n + 255) / 256;
+  const uint64_t cap = (uint64_t)sm_count * 16u;
+  if (blocks > cap) blocks = cap;
+  edges::edge_hashes_kernel<<<(unsigned)blocks, 256, 0, stream>>>(point_ids, topk_ids, rows, k, sketches, sketch_rows,
+                                                                  width, m_bits, hash_fwd, hash_rev, d_err);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+// Host expansion: rows split into contiguous chunks over `threads` host
+// threads; each chunk counts its edges, an exclusive scan places the chunks,
+// and each writes its edges in row / rank order, so the output order is the
+// reference's sequential one.
+uint64_t expand_edges_host(const uint32_t* point_ids, const uint32_t* topk_ids, const float* topk_dists,
+                           const uint16_t* hash_fwd, const uint16_t* hash_rev, uint64_t rows, uint32_t k,
+                           uint32_t* out_p, uint32_t* out_c, uint16_t* out_hash, float* out_dist, uint64_t capacity,
+                           uint32_t threads) {
+  auto valid = [&](uint64_t s) {
+    const uint32_t j = topk_ids[s];
+    const float d = topk_dists[s];
+    return j != 0xffffffffu && std::isfinite(d);
+  };
+  if (threads == 0) threads = 1;
+  const uint64_t chunk_rows = std::max<uint64_t>(1, (rows + threads - 1) / threads);
+  const uint32_t nchunks = (uint32_t)((rows + chunk_rows - 1) / chunk_rows);
+  std::vector<uint64_t> count(nchunks + 1, 0);
+  auto run = [&](auto&& body) {
+    std::vector<std::thread> pool;
+    for (uint32_t c = 1; c < nchunks; ++c) pool.emplace_back(body, c);
+    if (nchunks > 0) body(0u);
+    for (auto& t : pool) t.join();
+  };
+  run([&](uint32_t c) {
+    const uint64_t r0 = c * chunk_rows, r1 = std::min(rows, r0 + chunk_rows);
+    uint64_t n = 0;
+    for (uint64_t s = r0 * k; s < r1 * k; ++s) n += valid(s) ? 2u : 0u;
+    count[c + 1] = n;
+  });
+  for (uint32_t c = 0; c < nchunks; ++c) count[c + 1] += count[c];
+  const uint64_t total = count[nchunks];
+  if (total > capacity || !out_p) return total;
+  run([&](uint32_t c) {
+    const uint64_t r0 = c * chunk_rows, r1 = std::min(rows, r0 + chunk_rows);
+    uint64_t e = count[c];
+    for (uint64_t i = r0; i < r1; ++i) {
+      const uint32_t pi = point_ids[i];
+      for (uint32_t r = 0; r < k; ++r) {
+        const uint64_t s = i * k + r;
+        if (!valid(s)) continue;
+        const uint32_t j = topk_ids[s];
+        const float d = topk_dists[s];
+        out_p[e] = pi;
+        out_c[e] = j;
+        out_hash[e] = hash_fwd[s];
+        out_dist[e] = d;
+        ++e;
+        out_p[e] = j;
+        out_c[e] = pi;
+        out_hash[e] = hash_rev[s];
+        out_dist[e] = d;
+        ++e;
+      }
+    }
+  });
+  return total;
+}
+
+}  // namespace tessa

@@ -66,6 +66,17 @@ int launch_rect_topk_sq8(const RectLaunch& R, cudaStream_t stream);
 int launch_d0_fragments(const uint32_t* keys, const uint32_t* key_to_leader, const uint32_t* global_ids, uint64_t rows,
                         uint32_t fanout, uint32_t leaders, uint32_t* child_ids, uint32_t* point_ids, uint32_t* d_err,
                         int sm_count, cudaStream_t stream);
+int launch_sketch_rows(const float* x, uint64_t rows, uint32_t dim, const float* planes, uint32_t m, float* out,
+                       int sm_count, cudaStream_t stream);
+int launch_edge_hashes(const uint32_t* point_ids, const uint32_t* topk_ids, uint64_t rows, uint32_t k,
+                       const float* sketches, uint64_t sketch_rows, uint32_t width, uint32_t m_bits,
+                       uint16_t* hash_fwd, uint16_t* hash_rev, uint32_t* d_err, int sm_count, cudaStream_t stream);
+// Returns the edge count; writes the edges only if out_p is non-null and the
+// count fits `capacity`.
+uint64_t expand_edges_host(const uint32_t* point_ids, const uint32_t* topk_ids, const float* topk_dists,
+                           const uint16_t* hash_fwd, const uint16_t* hash_rev, uint64_t rows, uint32_t k,
+                           uint32_t* out_p, uint32_t* out_c, uint16_t* out_hash, float* out_dist, uint64_t capacity,
+                           uint32_t threads);
 int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes, int8_t* dst,
                        int sm_count, cudaStream_t stream);
 int leaf_num_bstages(uint32_t padded_dim);

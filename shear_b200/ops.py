@@ -391,3 +391,66 @@ def quantize_sq8_assign_d0(x, global_ids, leader_ids, fanout_top: int, leader_ve
     C.check(C.load().tessa_quantize_sq8_assign_d0(ctx.handle, ctypes.byref(a), _stream_ptr(torch, dev)))
     shape = (rows, f)
     return D0Result(codes, scales, norms, child.view(shape), point.view(shape), dists.view(shape), dim)
+
+
+# ------------------------------------------------------- candidate edges
+
+def sketch_rows(x, hyperplanes, ctx: Context | None = None, out=None):
+    """Per-point sketches (fill_sketch_row, hash_prune.rs:2208-2232) on the GPU.
+
+    x: CUDA f32 [rows, dim]; hyperplanes: CUDA f32 [m, dim] (m <= 16).
+    Returns CUDA f32 [rows, m], bit-exact with the reference's sequential sums.
+    """
+    import torch
+
+    x = x.contiguous()
+    planes = hyperplanes.contiguous()
+    rows, dim = x.shape
+    m = planes.shape[0]
+    ctx = ctx or context(x.device.index)
+    if out is None:
+        out = torch.empty((rows, m), dtype=torch.float32, device=x.device)
+    C.check(C.load().tessa_sketch_rows(ctx.handle, _ptr(x), rows, dim, _ptr(planes), m, _ptr(out),
+                                       _stream_ptr(torch, x.device.index)))
+    return out
+
+
+def edge_hashes(point_ids, topk_ids, k: int, sketches, m_bits: int, ctx: Context | None = None, out=None):
+    """Forward / reverse hashes of every leaf slot (int32-bit CUDA tensors in,
+    (hash_fwd, hash_rev) int16-bit CUDA tensors of rows * k out).  Sketch rows
+    are indexed by global point id."""
+    import torch
+
+    rows = int(point_ids.numel())
+    ctx = ctx or context(point_ids.device.index)
+    if out is None:
+        out = (torch.empty(rows * k, dtype=torch.int16, device=point_ids.device),
+               torch.empty(rows * k, dtype=torch.int16, device=point_ids.device))
+    sk = sketches.contiguous()
+    C.check(C.load().tessa_edge_hashes(ctx.handle, _ptr(point_ids.contiguous()), _ptr(topk_ids.contiguous()), rows, k,
+                                       _ptr(sk), sk.shape[0], sk.shape[1], m_bits, _ptr(out[0]), _ptr(out[1]),
+                                       _stream_ptr(torch, point_ids.device.index)))
+    return out
+
+
+def expand_edges(point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, k: int, threads: int = 0):
+    """Host edge expansion in the reference's order (numpy in / out):
+    returns (p uint32, c uint32, hash uint16, dist f32)."""
+    import os
+    pid = np.ascontiguousarray(point_ids, np.uint32)
+    ids = np.ascontiguousarray(topk_ids).view(np.uint32).reshape(-1)
+    ds = np.ascontiguousarray(topk_dists, np.float32).reshape(-1)
+    hf = np.ascontiguousarray(hash_fwd).view(np.uint16).reshape(-1)
+    hr = np.ascontiguousarray(hash_rev).view(np.uint16).reshape(-1)
+    rows = pid.shape[0]
+    if ids.shape[0] != rows * k or ds.shape[0] != rows * k or hf.shape[0] != rows * k or hr.shape[0] != rows * k:
+        raise ValueError("edge inputs must hold rows * k slots")
+    threads = threads or min(32, os.cpu_count() or 1)
+    n = ctypes.c_uint64()
+    lib = C.load()
+    args = (_np_ptr(pid), _np_ptr(ids), _np_ptr(ds), _np_ptr(hf), _np_ptr(hr), rows, k, threads)
+    C.check(lib.tessa_expand_edges(*args, None, None, None, None, 0, ctypes.byref(n)))
+    p, c = np.empty(n.value, np.uint32), np.empty(n.value, np.uint32)
+    h, d = np.empty(n.value, np.uint16), np.empty(n.value, np.float32)
+    C.check(lib.tessa_expand_edges(*args, _np_ptr(p), _np_ptr(c), _np_ptr(h), _np_ptr(d), n.value, ctypes.byref(n)))
+    return p, c, h, d

@@ -269,3 +269,68 @@ def test_d0_oracle_rejects_invalid_requests(oracle):
     for f in (0, 3):
         with pytest.raises(ValueError, match="fanout must be in"):
             oracle.d0_assign(np.ones((1, 4), np.float32), [0], [1, 2], lv, f)
+
+
+# ------------------------------------------------------------ candidate edges
+
+def _test_sketches(num_points, width):
+    # P/leaf_build.rs:2900-2908 build_test_sketches: point * 0.1 + bit (f32)
+    return np.array([[np.float32(p) * np.float32(0.1) + np.float32(b) for b in range(width)]
+                     for p in range(num_points)], np.float32)
+
+
+def test_flush_edges_reference_fixture(oracle):
+    # P/leaf_build.rs:3126-3137 fixture, 12-bit hashes: every valid slot gives
+    # (i -> j, hash(s_i, s_j)) then (j -> i, hash(s_j, s_i)); the (30, u32::MAX,
+    # inf) slot is skipped.
+    sk = _test_sketches(31, 12)
+    p, c, h, d = oracle.flush_edges([10, 20, 30], [20, 30, 30, 10, 20, 0xFFFFFFFF],
+                                    [1.0, 2.0, 1.5, 1.0, 1.5, np.inf], 2, sk, 12)
+    assert list(zip(p.tolist(), c.tolist())) == [(10, 20), (20, 10), (10, 30), (30, 10), (20, 30), (30, 20),
+                                                 (20, 10), (10, 20), (30, 20), (20, 30)]
+    assert d.tolist() == [1.0, 1.0, 2.0, 2.0, 1.5, 1.5, 1.0, 1.0, 1.5, 1.5]
+    # higher point ids have larger sketches in every bit: forward to a larger id = all ones
+    assert h.tolist() == [0xFFF, 0, 0xFFF, 0, 0xFFF, 0, 0, 0xFFF, 0, 0xFFF]
+
+
+def test_compute_hash_and_sketch_transliteration(oracle):
+    rng = np.random.default_rng(4)
+    a = rng.standard_normal(16).astype(np.float32)
+    b = a.copy()
+    b[3] = a[3] + np.float32(1e-3)
+    b[5] = np.nextafter(a[5], np.float32(-np.inf), dtype=np.float32)
+    want = sum(1 << i for i in range(16) if np.float32(b[i] - a[i]) >= 0)
+    assert oracle.compute_hash(a, b, 16) == want
+    assert oracle.compute_hash(a, b, 4) == want & 0xF
+    x = rng.standard_normal((5, 37)).astype(np.float32)
+    planes = rng.uniform(-1, 1, (12, 37)).astype(np.float32)
+    got = oracle.sketch_rows(x, planes)
+    for i in range(5):
+        for hh in range(12):
+            acc = np.float32(0)
+            for ax in range(37):
+                acc = np.float32(acc + np.float32(x[i, ax] * planes[hh, ax]))
+            assert got[i, hh].view(np.uint32) == acc.view(np.uint32)
+
+
+def test_library_expand_edges_matches_oracle_flush(oracle):
+    # host-only entry point of the library (no device work)
+    from shear_b200 import ops
+    rng = np.random.default_rng(9)
+    rows, k, n = 300, 7, 1000
+    sk = rng.standard_normal((n, 12)).astype(np.float32)
+    pid = rng.permutation(n)[:rows].astype(np.uint32)
+    ids = rng.integers(0, n, rows * k).astype(np.uint32)
+    ds = rng.uniform(0, 2, rows * k).astype(np.float32)
+    ids[::11] = 0xFFFFFFFF
+    ds[5::13] = np.inf
+    ds[7::17] = np.nan
+    hf = np.array([oracle.compute_hash(sk[pid[s // k]], sk[ids[s]], 12) if ids[s] != 0xFFFFFFFF else 0
+                   for s in range(rows * k)], np.uint16)
+    hr = np.array([oracle.compute_hash(sk[ids[s]], sk[pid[s // k]], 12) if ids[s] != 0xFFFFFFFF else 0
+                   for s in range(rows * k)], np.uint16)
+    want = oracle.flush_edges(pid, ids, ds, k, sk, 12)
+    for threads in (1, 3, 8):
+        got = ops.expand_edges(pid, ids, ds, hf, hr, k, threads=threads)
+        for g, w in zip(got, want):
+            assert np.array_equal(g.view(np.uint8), w.view(np.uint8))
