@@ -54,8 +54,10 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["leaf", "d0"], default="leaf",
-                    help="leaf = the north-star leaf replay (default); d0 = global-D0 SQ8 staging")
+    ap.add_argument("--workload", choices=["leaf", "d0", "edges"], default="leaf",
+                    help="leaf = the north-star leaf replay (default); d0 = global-D0 SQ8 staging; "
+                         "edges = candidate-edge hashes + host expansion of the leaf lists")
+    ap.add_argument("--hash-bits", type=int, default=12, help="edges: m_hash_bits (params.rs default 12)")
     ap.add_argument("--d0-rows", type=int, default=1 << 20, help="D0: raw rows per GPU per step")
     ap.add_argument("--d0-leaders", type=int, default=1000, help="D0: global leaders (params.rs max_leaders)")
     ap.add_argument("--d0-fanout", type=int, default=10, help="D0: fanout_top (params.rs default)")
@@ -634,8 +636,265 @@ def run_d0(a):
     return 0
 
 
+# ----------------------------------------------------------------- candidate edges
+
+def edges_desc(a):
+    return {
+        "workload": f"candidate edges of the leaf lists (flush_compact_topk_batch_into_edges): {a.leaves} leaves x "
+                    f"{a.leaf_rows} rows, top-{a.k}, {a.hash_bits}-bit sketch hashes, both directions",
+        "leaves": a.leaves, "leaf_rows": a.leaf_rows, "k": a.k, "hash_bits": a.hash_bits,
+        "l2": "slot arrays larger than L2 (%.1f GB of ids); no flush" % (a.leaves * a.leaf_rows * a.k * 4 / 1e9),
+    }
+
+
+def edges_inputs(torch, dev, a, seed):
+    """Leaf lists of the config-2 workload (one leaf-kernel run) and a sketch
+    store over every global id (unit-normal sketches; sketch values do not
+    change the hash cost)."""
+    from shear_b200 import ops
+
+    w = make_workload(torch, dev, a, seed)
+    rows = a.leaves * a.leaf_rows
+    ids = torch.empty(rows * a.k, dtype=torch.int32, device=dev)
+    dists = torch.empty(rows * a.k, dtype=torch.float32, device=dev)
+    ops.leaf_topk_sq8(w["codes"], w["scales"], w["norms"], w["gids"], w["members"], w["starts"], w["sizes"], a.k,
+                      leaf_ordered_codes=w["codes"], out=(ids, dists))
+    point_ids = w["gids"]  # members are the identity: leaf row r holds global id gids[r]
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 7)
+    sketches = torch.randn((rows, a.hash_bits), generator=g, device=dev, dtype=torch.float32)
+    layout = (w["starts"], w["sizes"])
+    del w
+    torch.cuda.synchronize(dev)
+    return point_ids, ids, dists, sketches, layout
+
+
+def run_edges_reference(a):
+    """The reference's flush (hash from sketches + edge expansion) restated in C, rank 0 only."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as O
+
+    threads = O.num_threads()
+    rng = np.random.default_rng(0)
+    per_step = max(threads, 1) * 4  # leaves per step
+    rows = per_step * a.leaf_rows
+    n_points = rows
+    sk = rng.standard_normal((n_points, a.hash_bits)).astype(np.float32)
+    pid = rng.permutation(n_points).astype(np.uint32)
+    ids = rng.integers(0, n_points, rows * a.k).astype(np.uint32)
+    ds = rng.uniform(0, 2, rows * a.k).astype(np.float32)
+
+    def one(l):
+        lo, hi = l * a.leaf_rows, (l + 1) * a.leaf_rows
+        return O.flush_edges(pid[lo:hi], ids[lo * a.k:hi * a.k], ds[lo * a.k:hi * a.k], a.k, sk, a.hash_bits)[0].size
+
+    times = []
+    with ThreadPoolExecutor(max_workers=max(threads, 1)) as ex:
+        for i in range(a.warmup + a.steps):
+            t0 = time.perf_counter()
+            n_edges = sum(ex.map(one, range(per_step)))
+            dt = time.perf_counter() - t0
+            if i >= a.warmup:
+                times.append(dt)
+    mean = float(np.mean(times))
+    value = n_edges / mean
+    line = {
+        "impl": "reference", "metric": "candidate edges/sec", "value": value, "unit": "edges/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": mean * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: random leaf lists and unit-normal sketches (seed 0)", "config": edges_desc(a),
+        "cpu_baseline": {"value": value, "unit": "edges/s", "cores": threads, "kind": "port",
+                         "sample": f"{per_step} leaves x {a.leaf_rows} rows x {a.k} slots per step"},
+        "e2e": {"value": value, "unit": "edges/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference flush restated in C (oracle/tessa_oracle.c), one host thread per leaf batch",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_edges(a):
+    import torch
+
+    from shear_b200 import ops
+
+    world, rank, local = dist_env()
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = ops.context(dev.index)
+    point_ids, ids, dists, sketches, layout = edges_inputs(torch, dev, a, seed=1234 + rank)
+    rows = a.leaves * a.leaf_rows
+    slots = rows * a.k
+    hf = torch.empty(slots, dtype=torch.int16, device=dev)
+    hr = torch.empty(slots, dtype=torch.int16, device=dev)
+    n_valid = int((ids != -1).sum())
+
+    def step():
+        ops.edge_hashes(point_ids, ids, a.k, sketches, a.hash_bits, *layout, ctx=ctx, out=(hf, hr))
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(a.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    with ClockSampler(dev.index) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for s_, e_ in evs:
+            s_.record(stream)
+            step()
+            e_.record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    total_s = t_start.elapsed_time(t_end) / 1e3
+    kern_s = float(np.mean([s_.elapsed_time(e_) for s_, e_ in evs])) / 1e3
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([total_s, kern_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_s, kern_s = float(tt[0]), float(tt[1])
+    per_step = total_s / a.steps
+    value = world * 2 * n_valid / per_step
+
+    # sketch kernel on 1M x 768 f32 rows (fill_sketch_row for the store)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    xs = torch.randn((1 << 20, a.dim), generator=g, device=dev)
+    planes = torch.rand((a.hash_bits, a.dim), generator=g, device=dev) * 2 - 1
+    sk_out = torch.empty((1 << 20, a.hash_bits), device=dev)
+    for _ in range(3):
+        ops.sketch_rows(xs, planes, ctx=ctx, out=sk_out)
+    torch.cuda.synchronize(dev)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(5):
+        ops.sketch_rows(xs, planes, ctx=ctx, out=sk_out)
+    s1.record(stream)
+    torch.cuda.synchronize(dev)
+    sketch_ms = s0.elapsed_time(s1) / 5
+    del xs, sk_out
+
+    e2e = None
+    if not a.no_e2e and a.e2e_steps > 0:
+        h_pid = point_ids.cpu().numpy().view(np.uint32)
+        h_ids = torch.empty(slots, dtype=torch.int32).pin_memory()
+        h_d = torch.empty(slots, dtype=torch.float32).pin_memory()
+        h_hf = torch.empty(slots, dtype=torch.int16).pin_memory()
+        h_hr = torch.empty(slots, dtype=torch.int16).pin_memory()
+
+        def e2e_step():
+            step()
+            h_ids.copy_(ids, non_blocking=True)
+            h_d.copy_(dists, non_blocking=True)
+            h_hf.copy_(hf, non_blocking=True)
+            h_hr.copy_(hr, non_blocking=True)
+            torch.cuda.synchronize(dev)
+            return ops.expand_edges(h_pid, h_ids.numpy(), h_d.numpy(), h_hf.numpy(), h_hr.numpy(), a.k)
+
+        e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(a.e2e_steps):
+            out = e2e_step()
+        e2e_s = (time.perf_counter() - t0) / a.e2e_steps
+        assert out[0].shape[0] == 2 * n_valid
+        del out
+        if world > 1:
+            import torch.distributed as dist
+            tt = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_s = float(tt[0])
+        e2e = {"value": world * 2 * n_valid / e2e_s, "unit": "edges/s", "h2d_bytes_per_step": 0,
+               "d2h_bytes_per_step": int(slots * 12), "ms_per_step": e2e_s * 1e3,
+               "timing": "wall clock: hash kernel, D2H of ids, distances and both hashes into pinned memory, "
+                         "host expansion into edge arrays (all host threads)"}
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    peaks = measured_peaks()
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    # algorithmic bytes per launch: ids in, both hashes out, each row's point id
+    # and every global id's sketch once
+    alg_bytes = slots * 4 + slots * 4 + rows * 4 + rows * a.hash_bits * 4
+    achieved = alg_bytes / kern_s / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": None, "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks.get("hbm_gbs") else "fallback",
+                "kernel": "tessa::edges::leaf_edge_hashes_kernel", "algorithmic_bytes_per_launch": alg_bytes,
+                "kernel_ms": kern_s * 1e3}
+
+    cpu = None
+    if not a.no_cpu_baseline and world == 1:
+        from concurrent.futures import ThreadPoolExecutor
+
+        from oracle import oracle as O
+        threads = O.num_threads()
+        nl = min(a.leaves, max(threads, 1) * 16)
+        h_sk = sketches.cpu().numpy()
+        h_pid = point_ids[: nl * a.leaf_rows].cpu().numpy().view(np.uint32)
+        h_ids = ids[: nl * a.leaf_rows * a.k].cpu().numpy().view(np.uint32)
+        h_d = dists[: nl * a.leaf_rows * a.k].cpu().numpy()
+
+        def one(l):
+            lo, hi = l * a.leaf_rows, (l + 1) * a.leaf_rows
+            return O.flush_edges(h_pid[lo:hi], h_ids[lo * a.k:hi * a.k], h_d[lo * a.k:hi * a.k], a.k, h_sk,
+                                 a.hash_bits)[0].size
+
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=max(threads, 1)) as ex:
+            n_e = sum(ex.map(one, range(nl)))
+        dt = time.perf_counter() - t0
+        cpu = {"value": n_e / dt, "unit": "edges/s", "cores": threads, "kind": "port",
+               "sample": f"{nl} of {a.leaves} leaves in {dt:.1f} s (hash from sketches + expansion), "
+                         f"oracle/tessa_oracle.c, one thread per leaf"}
+
+    line = {
+        "metric": "candidate edges/sec", "value": value, "unit": "edges/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: config-2 leaf lists from the leaf kernel, unit-normal sketches (seed 1234+rank)",
+        "config": dict(edges_desc(a), parallelism=f"leaf-sharded x{world} (independent, no collective)"),
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": a.steps, "clocks": clk.summary(),
+        "edges_per_step": 2 * n_valid, "sketch_rows_per_sec": (1 << 20) / (sketch_ms / 1e3),
+        "sketch_ms_1Mx768": sketch_ms,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse_args()
+    if a.workload == "edges":
+        return run_edges_reference(a) if a.impl == "reference" else run_edges(a)
     if a.workload == "d0":
         return run_d0_reference(a) if a.impl == "reference" else run_d0(a)
     if a.impl == "reference":

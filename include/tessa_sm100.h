@@ -290,17 +290,25 @@ TESSA_API int tessa_quantize_sq8_assign_d0_host(tessa_ctx* ctx, const tessa_d0_a
 TESSA_API int tessa_sketch_rows(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t dim, const float* hyperplanes,
                                 uint32_t m, float* sketches, void* stream);
 
-/* Both personalised-residual hashes of every (row, rank) slot of a leaf
- * batch, for the edge flush of flush_compact_topk_batch_into_edges
+/* Both personalised-residual hashes of every (row, rank) slot of a batch of
+ * leaves, for the edge flush of flush_compact_topk_batch_into_edges
  * (P/leaf_build.rs:1749-1808): with i = point_ids[row], j = topk_ids[row*k +
  * rank], hash_fwd = compute_hash(sketch_i, sketch_j) and hash_rev =
  * compute_hash(sketch_j, sketch_i) (P/hash_prune.rs:2239-2251: bit b set iff
  * sketch_c[b] - sketch_p[b] >= 0).  Sketch rows are indexed by global point id
  * (the reference's SketchStore), sketch_width floats apart; slots whose id is
- * 0xffffffff get 0.  Device pointers. */
+ * 0xffffffff get 0.  point_ids, topk_ids, sketches and the outputs are device
+ * pointers.  leaf_starts / leaf_sizes (HOST arrays, leaf_count entries) give
+ * the leaves as row ranges, each one CompactTopKBatch: the leaf's sketches are
+ * then staged once in shared memory, and a candidate that is not a member of
+ * its leaf is TESSA_ERR_BAD_TASK as in the reference (P/leaf_build.rs:
+ * 1771-1777).  With leaf_count == 0 (or leaves too large to stage) every
+ * candidate's sketch is read from the store directly, without that check. */
 TESSA_API int tessa_edge_hashes(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids, uint64_t rows,
-                                uint32_t k, const float* sketches, uint64_t sketch_rows, uint32_t sketch_width,
-                                uint32_t m_bits, uint16_t* hash_fwd, uint16_t* hash_rev, void* stream);
+                                uint32_t k, const uint64_t* leaf_starts, const uint64_t* leaf_sizes,
+                                uint64_t leaf_count, const float* sketches, uint64_t sketch_rows,
+                                uint32_t sketch_width, uint32_t m_bits, uint16_t* hash_fwd, uint16_t* hash_rev,
+                                void* stream);
 
 /* Host-side edge expansion of a leaf batch in the reference's order
  * (P/leaf_build.rs:1749-1808): for each row, each rank with a valid id and a

@@ -229,6 +229,7 @@ struct tessa_ctx {
   // and the host form's extra staging
   DevBuf d0_lcodes, d0_lscales, d0_lnorms, d0_keys, d0_k2l, d0_okeys, d0_dists, d0_lvec, d0_lids, d0_child,
       d0_point;
+  DevBuf e_starts, e_sizes;  // leaf layout of an edge-hash call
   cudaEvent_t d0_ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // phase boundaries of a D0 call
   tessa_d0_profile d0_prof = {};
 };
@@ -737,7 +738,8 @@ void tessa_destroy(tessa_ctx* ctx) {
   DevBuf* bufs[] = {&ctx->h_codes, &ctx->h_scales, &ctx->h_norms, &ctx->h_gids, &ctx->h_members,
                     &ctx->h_ids, &ctx->h_dists, &ctx->h_x, &ctx->fb_counts, &ctx->d0_lcodes,
                     &ctx->d0_lscales, &ctx->d0_lnorms, &ctx->d0_keys, &ctx->d0_k2l, &ctx->d0_okeys,
-                    &ctx->d0_dists, &ctx->d0_lvec, &ctx->d0_lids, &ctx->d0_child, &ctx->d0_point};
+                    &ctx->d0_dists, &ctx->d0_lvec, &ctx->d0_lids, &ctx->d0_child, &ctx->d0_point,
+                    &ctx->e_starts, &ctx->e_sizes};
   for (DevBuf* b : bufs) b->release();
   for (cudaStream_t s : {ctx->stream_in, ctx->stream_out})
     if (s) {
@@ -1009,6 +1011,7 @@ int tessa_sketch_rows(tessa_ctx* ctx, const float* x, uint64_t rows, uint32_t di
 }
 
 int tessa_edge_hashes(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids, uint64_t rows, uint32_t k,
+                      const uint64_t* leaf_starts, const uint64_t* leaf_sizes, uint64_t leaf_count,
                       const float* sketches, uint64_t sketch_rows, uint32_t sketch_width, uint32_t m_bits,
                       uint16_t* hash_fwd, uint16_t* hash_rev, void* stream) {
   TRY(bind(ctx));
@@ -1017,14 +1020,40 @@ int tessa_edge_hashes(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t*
                 sketch_width);
   if (rows && k && (!point_ids || !topk_ids || !sketches || !hash_fwd || !hash_rev))
     return fail(TESSA_ERR_INVALID_ARG, "null pointer");
+  if (leaf_count && (!leaf_starts || !leaf_sizes)) return fail(TESSA_ERR_INVALID_ARG, "null leaf layout");
+  uint64_t max_rows = 0;
+  for (uint64_t l = 0; l < leaf_count; ++l) {
+    if (leaf_starts[l] > rows || leaf_sizes[l] > rows - leaf_starts[l])
+      return fail(TESSA_ERR_INVALID_ARG, "leaf %llu [start %llu, size %llu] outside %llu rows", (unsigned long long)l,
+                  (unsigned long long)leaf_starts[l], (unsigned long long)leaf_sizes[l], (unsigned long long)rows);
+    max_rows = std::max(max_rows, leaf_sizes[l]);
+  }
   cudaStream_t st = (cudaStream_t)stream;
   TRY(clear_err(ctx, st));
-  const int r = launch_edge_hashes(point_ids, topk_ids, rows, k, sketches, sketch_rows, sketch_width, m_bits,
-                                   hash_fwd, hash_rev, ctx->d_err.as<uint32_t>(), ctx->sm_count, st);
+  uint32_t log2cap = 0;
+  const bool staged = leaf_count > 0 && leaf_count <= 0xffffffffull && max_rows <= 0xffffffull &&
+                      leaf_edge_smem((uint32_t)max_rows, m_bits, &log2cap) <= kLeafEdgeSmemMax;
+  int r;
+  if (staged) {
+    std::vector<uint32_t> sz32(leaf_count);
+    for (uint64_t l = 0; l < leaf_count; ++l) sz32[l] = (uint32_t)leaf_sizes[l];
+    TRY(ctx->e_starts.ensure(leaf_count * 8));
+    TRY(ctx->e_sizes.ensure(leaf_count * 4));
+    CUDA_TRY(cudaMemcpyAsync(ctx->e_starts.ptr, leaf_starts, leaf_count * 8, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(ctx->e_sizes.ptr, sz32.data(), leaf_count * 4, cudaMemcpyHostToDevice, st));
+    r = launch_leaf_edge_hashes(point_ids, topk_ids, ctx->e_starts.as<uint64_t>(), ctx->e_sizes.as<uint32_t>(),
+                                (uint32_t)leaf_count, (uint32_t)max_rows, k, sketches, sketch_rows, sketch_width,
+                                m_bits, hash_fwd, hash_rev, ctx->d_err.as<uint32_t>(), ctx->sm_count, st);
+  } else {
+    r = launch_edge_hashes(point_ids, topk_ids, rows, k, sketches, sketch_rows, sketch_width, m_bits, hash_fwd,
+                           hash_rev, ctx->d_err.as<uint32_t>(), ctx->sm_count, st);
+  }
   if (r != TESSA_OK) return fail(r, "edge hash launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   uint32_t bits = 0;
-  TRY(read_err(ctx, st, &bits));
+  TRY(read_err(ctx, st, &bits));  // synchronises: the pageable size vector outlives the copy
   if (bits & TESSA_DEVERR_BAD_ROW) return fail(TESSA_ERR_BAD_ROW, "leaf slot or row id outside the sketch store");
+  if (bits & TESSA_DEVERR_BAD_TASK)
+    return fail(TESSA_ERR_BAD_TASK, "a leaf slot references a point outside its leaf");
   return map_device_error(bits);
 }
 

@@ -74,6 +74,10 @@ __global__ void __launch_bounds__(kSkThreads)
 
 // Both hashes of every (row, rank) slot of a leaf batch.  Slots without a
 // candidate (id 0xffffffff) get 0; ids outside the sketch store are flagged.
+// Thread = (row, rank) with rank fastest, so a warp covers whole rows and the
+// row's sketch comes from L1; sketches with a width that is a multiple of 4
+// load as float4.
+template <bool VEC>
 __global__ void edge_hashes_kernel(const uint32_t* __restrict__ point_ids, const uint32_t* __restrict__ topk_ids,
                                    uint64_t rows, uint32_t k, const float* __restrict__ sketches,
                                    uint64_t sketch_rows, uint32_t width, uint32_t m_bits,
@@ -81,24 +85,163 @@ __global__ void edge_hashes_kernel(const uint32_t* __restrict__ point_ids, const
                                    uint32_t* __restrict__ err) {
   const uint64_t n = rows * k;
   for (uint64_t s = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; s < n; s += (uint64_t)gridDim.x * blockDim.x) {
-    const uint32_t i = point_ids[s / k];
-    const uint32_t j = topk_ids[s];
+    const uint64_t row = n <= 0xffffffffull ? (uint64_t)((uint32_t)s / k) : s / k;
+    const uint32_t i = __ldg(point_ids + row);
+    const uint32_t j = __ldg(topk_ids + s);
     uint32_t hf = 0, hr = 0;
     if (j != 0xffffffffu) {
       if (i >= sketch_rows || j >= sketch_rows) {
         atomicOr(err, TESSA_DEVERR_BAD_ROW);
       } else {
+        float a[16], c[16];
         const float* si = sketches + (uint64_t)i * width;
         const float* sj = sketches + (uint64_t)j * width;
-        for (uint32_t b = 0; b < m_bits; ++b) {
-          const float a = __ldg(si + b), c = __ldg(sj + b);
-          hf |= (__fsub_rn(c, a) >= 0.0f ? 1u : 0u) << b;
-          hr |= (__fsub_rn(a, c) >= 0.0f ? 1u : 0u) << b;
+        if constexpr (VEC) {
+#pragma unroll
+          for (uint32_t q = 0; q < 4; ++q)
+            if (4 * q < m_bits) {
+              const float4 u = __ldg(reinterpret_cast<const float4*>(si) + q);
+              const float4 v = __ldg(reinterpret_cast<const float4*>(sj) + q);
+              a[4 * q] = u.x; a[4 * q + 1] = u.y; a[4 * q + 2] = u.z; a[4 * q + 3] = u.w;
+              c[4 * q] = v.x; c[4 * q + 1] = v.y; c[4 * q + 2] = v.z; c[4 * q + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+          for (uint32_t b = 0; b < 16; ++b)
+            if (b < m_bits) {
+              a[b] = __ldg(si + b);
+              c[b] = __ldg(sj + b);
+            }
         }
+#pragma unroll
+        for (uint32_t b = 0; b < 16; ++b)
+          if (b < m_bits) {
+            hf |= (__fsub_rn(c[b], a[b]) >= 0.0f ? 1u : 0u) << b;
+            hr |= (__fsub_rn(a[b], c[b]) >= 0.0f ? 1u : 0u) << b;
+          }
       }
     }
     hash_fwd[s] = (uint16_t)hf;
     hash_rev[s] = (uint16_t)hr;
+  }
+}
+
+// Per-leaf form (one CTA per leaf, as the reference flushes one leaf batch at
+// a time): the leaf's sketches are gathered once into shared memory in leaf
+// order and a shared-memory open-addressing table maps global id -> leaf row,
+// so each slot reads its two sketches from shared memory instead of gathering
+// the candidate's row from the store.  A candidate that is not a member of its
+// leaf is an error, as in the reference (P/leaf_build.rs:1771-1777).
+constexpr uint32_t kLeafThreads = 512;
+constexpr uint32_t kUnroll = 8;  // slots per thread per pass
+constexpr uint32_t kEmptyKey = 0xffffffffu;
+
+__device__ __forceinline__ uint32_t table_slot(uint32_t key, uint32_t log2cap) {
+  return (key * 0x9E3779B1u) >> (32u - log2cap);
+}
+
+__global__ void __launch_bounds__(kLeafThreads)
+    leaf_edge_hashes_kernel(const uint32_t* __restrict__ point_ids, const uint32_t* __restrict__ topk_ids,
+                            const uint64_t* __restrict__ leaf_starts, const uint32_t* __restrict__ leaf_sizes,
+                            uint32_t leaf_count, uint32_t k, const float* __restrict__ sketches,
+                            uint64_t sketch_rows, uint32_t width, uint32_t m_bits, uint32_t log2cap,
+                            uint16_t* __restrict__ hash_fwd, uint16_t* __restrict__ hash_rev,
+                            uint32_t* __restrict__ err) {
+  extern __shared__ __align__(16) uint8_t esm[];
+  const uint32_t cap = 1u << log2cap;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(esm);
+  uint32_t* vals = keys + cap;
+  float4* sk = reinterpret_cast<float4*>(vals + cap);  // [rows][m4]: m_bits floats, zero padded
+  const uint32_t m4 = (m_bits + 3u) / 4u;
+  for (uint32_t leaf = blockIdx.x; leaf < leaf_count; leaf += gridDim.x) {
+    const uint64_t base = leaf_starts[leaf];
+    const uint32_t n = leaf_sizes[leaf];
+    for (uint32_t t = threadIdx.x; t < cap; t += blockDim.x) keys[t] = kEmptyKey;
+    __syncthreads();
+    for (uint32_t r = threadIdx.x; r < n; r += blockDim.x) {
+      const uint32_t g = __ldg(point_ids + base + r);
+      if (g >= sketch_rows || g == kEmptyKey) {
+        atomicOr(err, TESSA_DEVERR_BAD_ROW);
+        for (uint32_t q = 0; q < m4; ++q) sk[r * m4 + q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        continue;
+      }
+      const float* src = sketches + (uint64_t)g * width;
+      float v[16];
+#pragma unroll
+      for (uint32_t b = 0; b < 16; ++b) v[b] = b < m_bits ? __ldg(src + b) : 0.0f;  // all loads before the stores
+#pragma unroll
+      for (uint32_t q = 0; q < 4; ++q)
+        if (q < m4) sk[r * m4 + q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      // First insert of a global id wins; a repeated id has the same sketch.
+      // (the table is at most half full, so a free slot lies within cap probes)
+      uint32_t t = table_slot(g, log2cap);
+      for (uint32_t probe = 0; probe < cap; ++probe) {
+        const uint32_t prev = atomicCAS(keys + t, kEmptyKey, g);
+        if (prev == kEmptyKey) {
+          vals[t] = r;
+          break;
+        }
+        if (prev == g) break;
+        t = (t + 1u) & (cap - 1u);
+      }
+    }
+    __syncthreads();
+    // The leaf's slots are contiguous (rows base .. base+n, k each): a thread
+    // takes kUnroll of them per pass with all id loads issued first, so a pass
+    // keeps kUnroll loads per thread in flight.
+    const uint32_t nslots = n * k;
+    const uint64_t o0 = base * k;
+    for (uint32_t s0 = threadIdx.x; s0 < nslots; s0 += blockDim.x * kUnroll) {
+      uint32_t jj[kUnroll];
+#pragma unroll
+      for (uint32_t u = 0; u < kUnroll; ++u) {
+        const uint32_t s = s0 + u * blockDim.x;
+        jj[u] = s < nslots ? __ldg(topk_ids + o0 + s) : kEmptyKey;
+      }
+#pragma unroll 1
+      for (uint32_t u = 0; u < kUnroll; ++u) {
+      const uint32_t s = s0 + u * blockDim.x;
+      if (s >= nslots) break;
+      const uint32_t r = s / k;
+      const uint64_t o = o0 + s;
+      const uint32_t j = jj[u];
+      uint32_t hf = 0, hr = 0;
+      if (j != kEmptyKey) {
+        uint32_t t = table_slot(j, log2cap), p = kEmptyKey;
+        // at most cap probes: the table is at most half full, so an empty slot ends a miss
+        for (uint32_t probe = 0; probe < cap; ++probe) {
+          const uint32_t key = keys[t];
+          if (key == j) {
+            p = vals[t];
+            break;
+          }
+          if (key == kEmptyKey) break;
+          t = (t + 1u) & (cap - 1u);
+        }
+        if (p == kEmptyKey) {
+          atomicOr(err, TESSA_DEVERR_BAD_TASK);  // candidate outside its leaf
+        } else {
+          float a[16], c[16];
+#pragma unroll
+          for (uint32_t q = 0; q < 4; ++q)
+            if (q < m4) {
+              const float4 u = sk[r * m4 + q], w = sk[p * m4 + q];
+              a[4 * q] = u.x; a[4 * q + 1] = u.y; a[4 * q + 2] = u.z; a[4 * q + 3] = u.w;
+              c[4 * q] = w.x; c[4 * q + 1] = w.y; c[4 * q + 2] = w.z; c[4 * q + 3] = w.w;
+            }
+#pragma unroll
+          for (uint32_t b = 0; b < 16; ++b)
+            if (b < m_bits) {
+              hf |= (__fsub_rn(c[b], a[b]) >= 0.0f ? 1u : 0u) << b;
+              hr |= (__fsub_rn(a[b], c[b]) >= 0.0f ? 1u : 0u) << b;
+            }
+        }
+      }
+      hash_fwd[o] = (uint16_t)hf;
+      hash_rev[o] = (uint16_t)hr;
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -123,8 +266,46 @@ int launch_edge_hashes(const uint32_t* point_ids, const uint32_t* topk_ids, uint
   uint64_t blocks = (n + 255) / 256;
   const uint64_t cap = (uint64_t)sm_count * 16u;
   if (blocks > cap) blocks = cap;
-  edges::edge_hashes_kernel<<<(unsigned)blocks, 256, 0, stream>>>(point_ids, topk_ids, rows, k, sketches, sketch_rows,
-                                                                  width, m_bits, hash_fwd, hash_rev, d_err);
+  // float4 loads need 16-byte aligned sketch rows; they may read up to 3
+  // floats past m_bits, inside the row because width >= round_up(m_bits, 4).
+  const bool vec = width % 4u == 0u && (reinterpret_cast<uintptr_t>(sketches) & 15u) == 0u;
+  if (vec)
+    edges::edge_hashes_kernel<true><<<(unsigned)blocks, 256, 0, stream>>>(point_ids, topk_ids, rows, k, sketches,
+                                                                        sketch_rows, width, m_bits, hash_fwd, hash_rev,
+                                                                        d_err);
+  else
+    edges::edge_hashes_kernel<false><<<(unsigned)blocks, 256, 0, stream>>>(point_ids, topk_ids, rows, k, sketches,
+                                                                         sketch_rows, width, m_bits, hash_fwd,
+                                                                         hash_rev, d_err);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+// Shared memory of the per-leaf form for leaves of up to max_rows rows.
+uint32_t leaf_edge_smem(uint32_t max_rows, uint32_t m_bits, uint32_t* log2cap) {
+  uint32_t l = 1;
+  while ((1u << l) < 2u * max_rows) ++l;
+  *log2cap = l;
+  return (1u << l) * 8u + max_rows * ((m_bits + 3u) / 4u) * 16u;
+}
+
+int launch_leaf_edge_hashes(const uint32_t* point_ids, const uint32_t* topk_ids, const uint64_t* d_leaf_starts,
+                            const uint32_t* d_leaf_sizes, uint32_t leaf_count, uint32_t max_rows, uint32_t k,
+                            const float* sketches, uint64_t sketch_rows, uint32_t width, uint32_t m_bits,
+                            uint16_t* hash_fwd, uint16_t* hash_rev, uint32_t* d_err, int sm_count,
+                            cudaStream_t stream) {
+  if (leaf_count == 0 || k == 0) return TESSA_OK;
+  uint32_t log2cap = 0;
+  const uint32_t smem = leaf_edge_smem(max_rows, m_bits, &log2cap);
+  if (smem > kLeafEdgeSmemMax) return TESSA_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(edges::leaf_edge_hashes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return TESSA_ERR_CUDA;
+  const uint32_t per_sm = std::max<uint32_t>(1u, 220u * 1024u / std::max<uint32_t>(smem, 1u));
+  const uint64_t cap = (uint64_t)sm_count * std::min<uint32_t>(per_sm, 4u);
+  const uint32_t grid = (uint32_t)std::min<uint64_t>(leaf_count, cap);
+  edges::leaf_edge_hashes_kernel<<<grid, edges::kLeafThreads, smem, stream>>>(
+      point_ids, topk_ids, d_leaf_starts, d_leaf_sizes, leaf_count, k, sketches, sketch_rows, width, m_bits, log2cap,
+      hash_fwd, hash_rev, d_err);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 

@@ -71,6 +71,15 @@ int launch_sketch_rows(const float* x, uint64_t rows, uint32_t dim, const float*
 int launch_edge_hashes(const uint32_t* point_ids, const uint32_t* topk_ids, uint64_t rows, uint32_t k,
                        const float* sketches, uint64_t sketch_rows, uint32_t width, uint32_t m_bits,
                        uint16_t* hash_fwd, uint16_t* hash_rev, uint32_t* d_err, int sm_count, cudaStream_t stream);
+// Per-leaf hashes (leaf layout on the device); TESSA_ERR_UNSUPPORTED if the
+// largest leaf's sketches and id table exceed kLeafEdgeSmemMax.
+constexpr uint32_t kLeafEdgeSmemMax = 200u * 1024u;
+uint32_t leaf_edge_smem(uint32_t max_rows, uint32_t m_bits, uint32_t* log2cap);
+int launch_leaf_edge_hashes(const uint32_t* point_ids, const uint32_t* topk_ids, const uint64_t* d_leaf_starts,
+                            const uint32_t* d_leaf_sizes, uint32_t leaf_count, uint32_t max_rows, uint32_t k,
+                            const float* sketches, uint64_t sketch_rows, uint32_t width, uint32_t m_bits,
+                            uint16_t* hash_fwd, uint16_t* hash_rev, uint32_t* d_err, int sm_count,
+                            cudaStream_t stream);
 // Returns the edge count; writes the edges only if out_p is non-null and the
 // count fits `capacity`.
 uint64_t expand_edges_host(const uint32_t* point_ids, const uint32_t* topk_ids, const float* topk_dists,

@@ -415,10 +415,13 @@ def sketch_rows(x, hyperplanes, ctx: Context | None = None, out=None):
     return out
 
 
-def edge_hashes(point_ids, topk_ids, k: int, sketches, m_bits: int, ctx: Context | None = None, out=None):
+def edge_hashes(point_ids, topk_ids, k: int, sketches, m_bits: int, leaf_starts=None, leaf_sizes=None,
+                ctx: Context | None = None, out=None):
     """Forward / reverse hashes of every leaf slot (int32-bit CUDA tensors in,
     (hash_fwd, hash_rev) int16-bit CUDA tensors of rows * k out).  Sketch rows
-    are indexed by global point id."""
+    are indexed by global point id.  With the leaf layout (host sequences)
+    each leaf's sketches are staged once in shared memory and candidates must
+    be members of their leaf."""
     import torch
 
     rows = int(point_ids.numel())
@@ -427,8 +430,13 @@ def edge_hashes(point_ids, topk_ids, k: int, sketches, m_bits: int, ctx: Context
         out = (torch.empty(rows * k, dtype=torch.int16, device=point_ids.device),
                torch.empty(rows * k, dtype=torch.int16, device=point_ids.device))
     sk = sketches.contiguous()
+    if leaf_starts is None:
+        starts = sizes = np.zeros(0, np.uint64)
+    else:
+        starts, sizes = _layout(leaf_starts, leaf_sizes)
     C.check(C.load().tessa_edge_hashes(ctx.handle, _ptr(point_ids.contiguous()), _ptr(topk_ids.contiguous()), rows, k,
-                                       _ptr(sk), sk.shape[0], sk.shape[1], m_bits, _ptr(out[0]), _ptr(out[1]),
+                                       _np_ptr(starts), _np_ptr(sizes), starts.shape[0], _ptr(sk), sk.shape[0],
+                                       sk.shape[1], m_bits, _ptr(out[0]), _ptr(out[1]),
                                        _stream_ptr(torch, point_ids.device.index)))
     return out
 
