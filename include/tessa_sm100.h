@@ -320,6 +320,19 @@ TESSA_API int tessa_expand_edges(const uint32_t* point_ids, const uint32_t* topk
                                  uint32_t threads, uint32_t* edge_p, uint32_t* edge_c, uint16_t* edge_hash,
                                  float* edge_dist, uint64_t capacity, uint64_t* edge_count);
 
+/* -------------------------------------------------------------- capture --- */
+
+/* Membership digests of leaf tasks for the TESSA capture sampler: for leaf l
+ * (rows leaf_starts[l] .. + leaf_sizes[l] of `ids`, HOST layout arrays) the
+ * wrapping sum of mix(id) and the xor of rotl(mix(id), id & 63) over its
+ * member ids, mix = the splitmix64 finaliser of id + 0x9e3779b97f4a7c15
+ * (P/tessa_capture.rs:274-293, the digest every task hash covers).  With
+ * global_ids non-NULL the member id is global_ids[ids[i]].  ids, global_ids
+ * and the outputs (leaf_count u64 each) are device pointers. */
+TESSA_API int tessa_membership_digests(tessa_ctx* ctx, const uint32_t* ids, const uint32_t* global_ids,
+                                       const uint64_t* leaf_starts, const uint64_t* leaf_sizes, uint64_t leaf_count,
+                                       uint64_t* out_sum, uint64_t* out_xor, void* stream);
+
 /* ------------------------------------------------------- replay session --- */
 
 /* TessaPreparedReplay (P/tessa_replay.rs:1052-1074) as host arrays. */

@@ -1074,6 +1074,25 @@ int tessa_expand_edges(const uint32_t* point_ids, const uint32_t* topk_ids, cons
   return TESSA_OK;
 }
 
+int tessa_membership_digests(tessa_ctx* ctx, const uint32_t* ids, const uint32_t* global_ids,
+                             const uint64_t* leaf_starts, const uint64_t* leaf_sizes, uint64_t leaf_count,
+                             uint64_t* out_sum, uint64_t* out_xor, void* stream) {
+  TRY(bind(ctx));
+  if (leaf_count == 0) return TESSA_OK;
+  if (!ids || !leaf_starts || !leaf_sizes || !out_sum || !out_xor) return fail(TESSA_ERR_INVALID_ARG, "null pointer");
+  if (leaf_count > 0xffffffffull) return fail(TESSA_ERR_UNSUPPORTED, "more than 2^32 leaves");
+  cudaStream_t st = (cudaStream_t)stream;
+  TRY(ctx->e_starts.ensure(leaf_count * 8));
+  TRY(ctx->e_sizes.ensure(leaf_count * 8));
+  CUDA_TRY(cudaMemcpyAsync(ctx->e_starts.ptr, leaf_starts, leaf_count * 8, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(ctx->e_sizes.ptr, leaf_sizes, leaf_count * 8, cudaMemcpyHostToDevice, st));
+  const int r = launch_membership_digests(ids, global_ids, ctx->e_starts.as<uint64_t>(), ctx->e_sizes.as<uint64_t>(),
+                                          (uint32_t)leaf_count, out_sum, out_xor, ctx->sm_count, st);
+  if (r != TESSA_OK) return fail(r, "digest launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return TESSA_OK;
+}
+
 int tessa_assign(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* args, void* stream) {
   TRY(bind(ctx));
   return assign_device(ctx, source, args, (cudaStream_t)stream);

@@ -86,6 +86,9 @@ uint64_t expand_edges_host(const uint32_t* point_ids, const uint32_t* topk_ids, 
                            const uint16_t* hash_fwd, const uint16_t* hash_rev, uint64_t rows, uint32_t k,
                            uint32_t* out_p, uint32_t* out_c, uint16_t* out_hash, float* out_dist, uint64_t capacity,
                            uint32_t threads);
+int launch_membership_digests(const uint32_t* ids, const uint32_t* global_ids, const uint64_t* d_leaf_starts,
+                              const uint64_t* d_leaf_sizes, uint32_t leaf_count, uint64_t* out_sum,
+                              uint64_t* out_xor, int sm_count, cudaStream_t stream);
 int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes, int8_t* dst,
                        int sm_count, cudaStream_t stream);
 int leaf_num_bstages(uint32_t padded_dim);

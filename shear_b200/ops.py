@@ -462,3 +462,23 @@ def expand_edges(point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, k: int, th
     h, d = np.empty(n.value, np.uint16), np.empty(n.value, np.float32)
     C.check(lib.tessa_expand_edges(*args, _np_ptr(p), _np_ptr(c), _np_ptr(h), _np_ptr(d), n.value, ctypes.byref(n)))
     return p, c, h, d
+
+
+# ---------------------------------------------------------------- capture
+
+def membership_digests(ids, leaf_starts, leaf_sizes, global_ids=None, ctx: Context | None = None):
+    """Per-leaf (count, sum, xor) membership digests of device member arrays
+    (int32-bit CUDA tensors; member id = global_ids[ids[i]] when given) ->
+    numpy uint64 [leaves, 3], the input of TessaCaptureSampler.observe_leaf_digests."""
+    import torch
+
+    starts, sizes = _layout(leaf_starts, leaf_sizes)
+    ctx = ctx or context(ids.device.index)
+    n = starts.shape[0]
+    out = torch.empty((2, max(n, 1)), dtype=torch.int64, device=ids.device)
+    gid = global_ids.contiguous() if global_ids is not None else None
+    C.check(C.load().tessa_membership_digests(ctx.handle, _ptr(ids.contiguous()), _ptr(gid), _np_ptr(starts),
+                                              _np_ptr(sizes), n, _ptr(out[0]), _ptr(out[1]),
+                                              _stream_ptr(torch, ids.device.index)))
+    d = out[:, :n].cpu().numpy().view(np.uint64)
+    return np.stack([sizes.astype(np.uint64), d[0], d[1]], axis=1)
