@@ -109,8 +109,8 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, void* smem_d
       : "memory");
 }
 
-// 1-D bulk copy from global memory into this CTA's shared memory (no
-// multicast); both addresses 16-byte aligned, `bytes` a multiple of 16;
+// 1-D bulk copy from global memory into this CTA's own shared memory only;
+// both addresses 16-byte aligned, `bytes` a multiple of 16;
 // completion is signalled on `bar` as transaction bytes.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
