@@ -333,6 +333,19 @@ TESSA_API int tessa_membership_digests(tessa_ctx* ctx, const uint32_t* ids, cons
                                        const uint64_t* leaf_starts, const uint64_t* leaf_sizes, uint64_t leaf_count,
                                        uint64_t* out_sum, uint64_t* out_xor, void* stream);
 
+/* ------------------------------------------------------- graph search --- */
+
+/* Greedy search for recall runs (apps/search_shear_index/src/main.rs
+ * search_one_with_stats :1007-1085, l2_distance :1639-1644): per query, the k
+ * nearest ids found with list size l (l_eff = max(l, k + 1)) starting at
+ * `start`, over a graph given as CSR (offsets[n + 1], neighbors); exact f32
+ * squared L2 summed in axis order.  HOST pointers; `threads` host threads
+ * (0 = 1).  Slots beyond the found results are 0xffffffff.  *comparisons
+ * (optional) receives the distance evaluations. */
+TESSA_API int tessa_graph_search(const float* data, uint64_t n, uint32_t dim, const uint64_t* offsets,
+                                 const uint32_t* neighbors, uint32_t start, const float* queries, uint64_t nq,
+                                 uint32_t k, uint32_t l, uint32_t threads, uint32_t* out_ids, uint64_t* comparisons);
+
 /* ------------------------------------------------------- replay session --- */
 
 /* TessaPreparedReplay (P/tessa_replay.rs:1052-1074) as host arrays. */

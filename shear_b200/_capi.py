@@ -138,6 +138,9 @@ SIGNATURES = [
      [c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint64, c_vp, ctypes.c_uint64,
       ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp]),
     ("tessa_membership_digests", ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, c_vp, c_vp, c_vp]),
+    ("tessa_graph_search", ctypes.c_int,
+     [c_vp, ctypes.c_uint64, ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint64, ctypes.c_uint32,
+      ctypes.c_uint32, ctypes.c_uint32, c_vp, ctypes.POINTER(ctypes.c_uint64)]),
     ("tessa_expand_edges", ctypes.c_int,
      [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp,
       ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),

@@ -1093,6 +1093,22 @@ int tessa_membership_digests(tessa_ctx* ctx, const uint32_t* ids, const uint32_t
   return TESSA_OK;
 }
 
+int tessa_graph_search(const float* data, uint64_t n, uint32_t dim, const uint64_t* offsets,
+                       const uint32_t* neighbors, uint32_t start, const float* queries, uint64_t nq, uint32_t k,
+                       uint32_t l, uint32_t threads, uint32_t* out_ids, uint64_t* comparisons) {
+  if (nq == 0) return TESSA_OK;
+  if (!data || !offsets || !queries || !out_ids || (offsets[n] && !neighbors))
+    return fail(TESSA_ERR_INVALID_ARG, "null pointer");
+  if (n == 0 || dim == 0 || k == 0) return fail(TESSA_ERR_INVALID_ARG, "graph search needs n, dim and k > 0");
+  if (start >= n) return fail(TESSA_ERR_INVALID_ARG, "start node %u outside %llu points", start, (unsigned long long)n);
+  for (uint64_t v = 0; v < n; ++v)
+    if (offsets[v] > offsets[v + 1]) return fail(TESSA_ERR_INVALID_ARG, "graph offsets decrease at node %llu",
+                                                 (unsigned long long)v);
+  const uint64_t c = graph_search_host(data, n, dim, offsets, neighbors, start, queries, nq, k, l, threads, out_ids);
+  if (comparisons) *comparisons = c;
+  return TESSA_OK;
+}
+
 int tessa_assign(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* args, void* stream) {
   TRY(bind(ctx));
   return assign_device(ctx, source, args, (cudaStream_t)stream);

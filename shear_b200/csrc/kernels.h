@@ -89,6 +89,11 @@ uint64_t expand_edges_host(const uint32_t* point_ids, const uint32_t* topk_ids, 
 int launch_membership_digests(const uint32_t* ids, const uint32_t* global_ids, const uint64_t* d_leaf_starts,
                               const uint64_t* d_leaf_sizes, uint32_t leaf_count, uint64_t* out_sum,
                               uint64_t* out_xor, int sm_count, cudaStream_t stream);
+// Greedy search of nq queries over a CSR graph (host threads); returns the
+// number of distance evaluations.
+uint64_t graph_search_host(const float* data, uint64_t n, uint32_t dim, const uint64_t* offsets,
+                           const uint32_t* neighbors, uint32_t start, const float* queries, uint64_t nq, uint32_t k,
+                           uint32_t l, uint32_t threads, uint32_t* out_ids);
 int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes, int8_t* dst,
                        int sm_count, cudaStream_t stream);
 int leaf_num_bstages(uint32_t padded_dim);
