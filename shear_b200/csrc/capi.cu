@@ -1032,6 +1032,7 @@ int tessa_edge_hashes(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t*
   TRY(clear_err(ctx, st));
   uint32_t log2cap = 0;
   const bool staged = leaf_count > 0 && leaf_count <= 0xffffffffull && max_rows <= 0xffffffull &&
+                      max_rows * k <= 0xffffffffull &&  // slot indices within a leaf are 32-bit
                       leaf_edge_smem((uint32_t)max_rows, m_bits, &log2cap) <= kLeafEdgeSmemMax;
   int r;
   if (staged) {

@@ -28,17 +28,21 @@
 namespace tessa {
 namespace edges {
 
-constexpr uint32_t kSkWarps = 8;
+constexpr uint32_t kSkWarps = 4;
 constexpr uint32_t kSkThreads = kSkWarps * 32;
 constexpr uint32_t kMaxPlanes = 16;
 
 // One warp per 32 rows: 32 x 32 slabs of x go through shared memory with
-// coalesced loads (lane = column); then lane r walks row r's slab in axis
-// order and advances its m sequential sums (m independent chains).
+// coalesced loads (lane = column), and the matching 32 columns of the m
+// hyperplanes are staged beside them (column-major, 16 floats per column, so
+// a lane reads four planes with one broadcast float4 load); then lane r walks
+// row r's slab in axis order and advances its m sequential sums (m
+// independent chains).
 __global__ void __launch_bounds__(kSkThreads)
     sketch_rows_kernel(const float* __restrict__ x, uint64_t rows, uint32_t dim, const float* __restrict__ planes,
                        uint32_t m, float* __restrict__ out) {
   __shared__ float tile[kSkWarps][32][33];
+  __shared__ __align__(16) float ptile[kSkWarps][32][kMaxPlanes];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint64_t nblk = (rows + 31) / 32;
   for (uint64_t blk = blockIdx.x * (uint64_t)kSkWarps + warp; blk < nblk; blk += (uint64_t)gridDim.x * kSkWarps) {
@@ -52,14 +56,24 @@ __global__ void __launch_bounds__(kSkThreads)
       if (lane < nc) {
 #pragma unroll 8
         for (uint32_t i = 0; i < 32; ++i) tile[warp][i][lane] = i < nr ? __ldg(x + (r0 + i) * dim + c0 + lane) : 0.0f;
+#pragma unroll
+        for (uint32_t h = 0; h < kMaxPlanes; ++h)
+          ptile[warp][lane][h] = h < m ? __ldg(planes + (uint64_t)h * dim + c0 + lane) : 0.0f;
       }
       __syncwarp();
       for (uint32_t j = 0; j < nc; ++j) {
         const float v = tile[warp][lane][j];
-        const float* hp = planes + c0 + j;
+        const float4* pj = reinterpret_cast<const float4*>(&ptile[warp][j][0]);
 #pragma unroll
-        for (uint32_t h = 0; h < kMaxPlanes; ++h)
-          if (h < m) acc[h] = __fadd_rn(acc[h], __fmul_rn(v, __ldg(hp + (uint64_t)h * dim)));
+        for (uint32_t q = 0; q < kMaxPlanes / 4; ++q) {
+          if (4 * q < m) {
+            const float4 w = pj[q];
+            acc[4 * q] = __fadd_rn(acc[4 * q], __fmul_rn(v, w.x));
+            acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], __fmul_rn(v, w.y));
+            acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], __fmul_rn(v, w.z));
+            acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], __fmul_rn(v, w.w));
+          }
+        }
       }
       __syncwarp();
     }
@@ -252,7 +266,7 @@ int launch_sketch_rows(const float* x, uint64_t rows, uint32_t dim, const float*
   if (rows == 0) return TESSA_OK;
   if (m == 0 || m > edges::kMaxPlanes) return TESSA_ERR_INVALID_ARG;
   uint64_t blocks = ((rows + 31) / 32 + edges::kSkWarps - 1) / edges::kSkWarps;
-  const uint64_t cap = (uint64_t)sm_count * 8u;
+  const uint64_t cap = (uint64_t)sm_count * 16u;
   if (blocks > cap) blocks = cap;
   edges::sketch_rows_kernel<<<(unsigned)blocks, edges::kSkThreads, 0, stream>>>(x, rows, dim, planes, m, out);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;

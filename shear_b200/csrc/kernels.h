@@ -30,7 +30,8 @@ struct LeafLaunch {
   int sm_count;
 };
 
-// Largest leaf the leaf kernel accepts (member positions are kept in 16 bits).
+// Largest leaf the leaf kernel accepts (a validated cap above the reference's
+// leaf sizes).
 constexpr uint64_t kMaxLeafRows = 65535;
 
 // Rectangular form of the leaf kernel: each row of a row matrix against every
