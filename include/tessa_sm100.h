@@ -41,7 +41,9 @@
 extern "C" {
 #endif
 
-#define TESSA_ABI_VERSION 1
+/* 1: leaf, quantize, assignment, replay; 2: + host pipeline knob, global D0, candidate
+ * edges, capture digests, graph search (additive). */
+#define TESSA_ABI_VERSION 2
 
 #define TESSA_OK 0
 #define TESSA_ERR_INVALID_ARG (-1)  /* malformed sizes, null pointers, k out of range */

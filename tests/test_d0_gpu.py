@@ -55,6 +55,7 @@ CASES = [
     (2000, 768, 1000, 6, 0),
     (513, 256, 300, 16, 40),
     (400, 64, 64, 32, 64),
+    (300, 64, 32, 32, 0),     # fanout equal to the leader count
 ]
 
 

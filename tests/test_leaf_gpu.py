@@ -185,6 +185,24 @@ def test_leaf_config2_shape_sample(oracle):
     _assert_same(_device_run(c, 32), oracle_leaf(oracle, c, 32))
 
 
+def test_leaf_large_single_leaf(oracle):
+    # one leaf four times the reference's largest staged leaf (2048 rows)
+    c = make_leaf_batch(oracle, [8192], 128, seed=8192, dup=True)
+    _assert_same(_device_run(c, 32), oracle_leaf(oracle, c, 32))
+
+
+def test_leaf_empty_batch_is_a_no_op():
+    import torch
+    from shear_b200 import ops
+    dev = torch.device("cuda:0")
+    codes = torch.zeros((4, 16), dtype=torch.int8, device=dev)
+    f = torch.zeros(4, device=dev)
+    g = torch.zeros(4, dtype=torch.int32, device=dev)
+    ids, dists = ops.leaf_topk_sq8(codes, f, f, g, g[:0], np.zeros(0, np.uint64), np.zeros(0, np.uint64), 4)
+    torch.cuda.synchronize()
+    assert ids.numel() == 0 and dists.numel() == 0
+
+
 def test_leaf_rejects_bad_arguments(oracle):
     from shear_b200 import ops, TessaError
     c = make_leaf_batch(oracle, [10], 32, seed=1)
