@@ -54,10 +54,13 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["leaf", "d0", "edges"], default="leaf",
+    ap.add_argument("--workload", choices=["leaf", "d0", "edges", "assign"], default="leaf",
                     help="leaf = the north-star leaf replay (default); d0 = global-D0 SQ8 staging; "
                          "edges = candidate-edge hashes + host expansion of the leaf lists")
     ap.add_argument("--hash-bits", type=int, default=12, help="edges: m_hash_bits (params.rs default 12)")
+    ap.add_argument("--assign-leaders", type=int, default=16, help="assign: leaders per task (replay contract)")
+    ap.add_argument("--assign-rh", type=int, default=2, help="assign: r_h (replay contract)")
+    ap.add_argument("--assign-fp32", action="store_true", help="assign: raw f32 rows (mode A0) instead of SQ8")
     ap.add_argument("--d0-rows", type=int, default=1 << 20, help="D0: raw rows per GPU per step")
     ap.add_argument("--d0-leaders", type=int, default=1000, help="D0: global leaders (params.rs max_leaders)")
     ap.add_argument("--d0-fanout", type=int, default=10, help="D0: fanout_top (params.rs default)")
@@ -891,8 +894,188 @@ def run_edges(a):
     return 0
 
 
+# ----------------------------------------------------------------- assignment
+
+def assign_desc(a):
+    src = "fp32 rows (A0)" if a.assign_fp32 else "SQ8 codes"
+    return {
+        "workload": f"TESSA assignment replay: {a.leaves} tasks x {a.leaf_rows} member rows, {a.dim}-d {src}, "
+                    f"{a.assign_leaders} leaders per task, r_h = {a.assign_rh}",
+        "tasks": a.leaves, "task_rows": a.leaf_rows, "dim": a.dim, "leaders": a.assign_leaders, "r_h": a.assign_rh,
+        "source": src, "l2": "member rows larger than L2; no flush",
+    }
+
+
+def assign_tasks(a, rng):
+    """Contiguous tasks of leaf_rows members; each task's leaders are members of it."""
+    n = a.leaves * a.leaf_rows
+    moff = (np.arange(a.leaves, dtype=np.uint64) * a.leaf_rows).astype(np.uint32)
+    mcnt = np.full(a.leaves, a.leaf_rows, np.uint32)
+    pick = np.stack([rng.choice(a.leaf_rows, a.assign_leaders, replace=False) for _ in range(a.leaves)])
+    leaders = (pick + moff[:, None]).astype(np.uint32).reshape(-1)
+    loff = (np.arange(a.leaves, dtype=np.uint64) * a.assign_leaders).astype(np.uint32)
+    lcnt = np.full(a.leaves, a.assign_leaders, np.uint32)
+    rh = np.full(a.leaves, a.assign_rh, np.uint32)
+    outoff = (moff.astype(np.uint64) * a.assign_rh).astype(np.uint64)
+    return n, leaders, moff, mcnt, loff, lcnt, rh, outoff
+
+
+def run_assign_reference(a):
+    """The reference's assignment replay restated in C (oracle port) on a task sample, rank 0 only."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(0)
+    b = argparse.Namespace(**vars(a))
+    b.leaves = max(O.num_threads(), 1) * 2
+    n, leaders, moff, mcnt, loff, lcnt, rh, outoff = assign_tasks(b, rng)
+    x = rng.standard_normal((n, a.dim)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    codes, scales, qn = O.quantize_sq8(x)
+    norms = O.raw_norms(x) if a.assign_fp32 else qn
+    mode = 0 if a.assign_fp32 else 3
+    gids = np.arange(n, dtype=np.uint32)
+    members = np.arange(n, dtype=np.uint32)
+    times = []
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        O.assign(mode, x, norms, codes, scales, gids, members, leaders, moff, mcnt, loff, lcnt, rh, outoff,
+                 n * a.assign_rh)
+        dt = time.perf_counter() - t0
+        if i >= a.warmup:
+            times.append(dt)
+    mean = float(np.mean(times))
+    value = n / mean
+    line = {
+        "impl": "reference", "metric": "assignment rows/sec", "value": value, "unit": "rows/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if a.assign_fp32 else "int8",
+        "data": "synthetic: N(0,1) rows, L2-normalised (seed 0)", "config": assign_desc(a),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": O.num_threads(), "kind": "port",
+                         "sample": f"{b.leaves} tasks x {a.leaf_rows} rows per step"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "assignment replay restated in C (oracle/tessa_oracle.c), sequential per task",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_assign(a):
+    import torch
+
+    from shear_b200 import _capi as CA, ops
+
+    world, rank, local = dist_env()
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = ops.context(dev.index)
+    rng = np.random.default_rng(1 + rank)
+    n, leaders, moff, mcnt, loff, lcnt, rh, outoff = assign_tasks(a, rng)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3 + rank)
+    x = torch.empty((n, a.dim), dtype=torch.float32, device=dev)
+    for r0 in range(0, n, 1 << 20):
+        y = torch.randn((min(n, r0 + (1 << 20)) - r0, a.dim), generator=g, device=dev)
+        x[r0:r0 + y.shape[0]] = y / torch.linalg.vector_norm(y, dim=1, keepdim=True)
+    codes, scales, qn = ops.quantize_sq8(x)
+    raw_norms = (x * x).sum(1) if a.assign_fp32 else None
+    if not a.assign_fp32:
+        del x
+        x = None
+    gids = torch.arange(n, dtype=torch.int32, device=dev)
+    members = gids
+    lead = torch.from_numpy(leaders.view(np.int32)).to(dev)
+    torch.cuda.synchronize(dev)
+    src = CA.ASSIGN_FP32 if a.assign_fp32 else CA.ASSIGN_SQ8
+
+    def step():
+        if a.assign_fp32:
+            return ops.assign(src, x=x, raw_norms=raw_norms, global_ids=gids, members=members, leaders=lead,
+                              task_member_offsets=moff, task_member_counts=mcnt, task_leader_offsets=loff,
+                              task_leader_counts=lcnt, task_rh=rh, task_output_offsets=outoff,
+                              output_len=n * a.assign_rh, ctx=ctx)
+        return ops.assign(src, codes=codes, scales=scales, sq8_norms=qn, global_ids=gids, members=members,
+                          leaders=lead, task_member_offsets=moff, task_member_counts=mcnt, task_leader_offsets=loff,
+                          task_leader_counts=lcnt, task_rh=rh, task_output_offsets=outoff,
+                          output_len=n * a.assign_rh, ctx=ctx)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(a.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(dev.index) as clk:
+        t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0e.record(stream)
+        for _ in range(a.steps):
+            step()
+        t1e.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    total_s = t0e.elapsed_time(t1e) / 1e3
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([total_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_s = float(tt[0])
+    per_step = total_s / a.steps
+    value = world * n / per_step
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+    peaks = measured_peaks()
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    row_bytes = a.dim * 4 + 4 if a.assign_fp32 else codes.shape[1] + 8
+    # algorithmic bytes: every member row (and its norm / scale) once, leaders
+    # once per task, the outputs (id + distance per r_h slot)
+    alg = n * row_bytes + a.leaves * a.assign_leaders * row_bytes + n * a.assign_rh * 8
+    achieved = alg / per_step / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": None,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks.get("hbm_gbs") else "fallback",
+                "kernel": f"tessa::assign::assign_kernel<{'false' if a.assign_fp32 else 'true'}>",
+                "algorithmic_bytes_per_launch": alg, "kernel_ms": per_step * 1e3,
+                "note": "per-step time includes the host-side task table build and one host sync"}
+    line = {
+        "metric": "assignment rows/sec", "value": value, "unit": "rows/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32" if a.assign_fp32 else "int8",
+        "data": "synthetic: N(0,1) rows, L2-normalised; leaders drawn from each task's members (seed 1+rank)",
+        "config": dict(assign_desc(a), parallelism=f"task-sharded x{world} (independent, no collective)"),
+        "roofline": roofline, "cpu_baseline": None, "e2e": None, "gpu_launches": a.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse_args()
+    if a.workload == "assign":
+        return run_assign_reference(a) if a.impl == "reference" else run_assign(a)
     if a.workload == "edges":
         return run_edges_reference(a) if a.impl == "reference" else run_edges(a)
     if a.workload == "d0":

@@ -81,6 +81,10 @@ TESSA_API const char* tessa_last_error_message(void);
 TESSA_API int tessa_create(int device, tessa_ctx** out);
 TESSA_API void tessa_destroy(tessa_ctx* ctx);
 TESSA_API int tessa_ctx_device(const tessa_ctx* ctx);
+/* Device bytes the context currently holds in scratch and staging buffers
+ * (grow-only; freed by tessa_destroy) -- the quantity the task former's
+ * admission model bounds. */
+TESSA_API int tessa_ctx_device_bytes(const tessa_ctx* ctx, uint64_t* bytes);
 
 /* ------------------------------------------------------- SQ8 quantizer --- */
 

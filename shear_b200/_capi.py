@@ -118,6 +118,7 @@ SIGNATURES = [
     ("tessa_create", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(c_vp)]),
     ("tessa_destroy", None, [c_vp]),
     ("tessa_ctx_device", ctypes.c_int, [c_vp]),
+    ("tessa_ctx_device_bytes", ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint64)]),
     ("tessa_quantize_sq8", ctypes.c_int,
      [c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp,
       c_vp]),

@@ -21,9 +21,11 @@
 //              rounding per operation.
 //
 // Layout: one CTA = 128 member rows of one task, one thread per row; leaders
-// are streamed through shared memory in groups of 32 leaders x one K tile, and
-// each thread keeps 32 independent partial dots in registers (axis order per
-// dot is preserved, so the FP32 sums stay bit-exact).
+// are streamed through shared memory in groups of LG = 8, 16 or 32 leaders
+// (the smallest that holds the largest task) x one K tile, each thread keeps
+// LG independent partial dots in registers, member rows load 16 bytes at a
+// time and leader tiles are read with broadcast 16-byte shared loads (axis
+// order per dot is preserved, so the FP32 sums stay bit-exact).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -32,8 +34,8 @@ namespace assign {
 
 constexpr uint32_t kRows = 128;     // member rows per CTA
 constexpr uint32_t kLeaders = 32;   // leaders per register group
-constexpr uint32_t kAxF = 32;       // FP32 axes per K tile
-constexpr uint32_t kAxQ = 64;       // SQ8 bytes per K tile
+constexpr uint32_t kAxF = 64;       // FP32 axes per K tile
+constexpr uint32_t kAxQ = 256;      // SQ8 bytes per K tile
 
 
 __device__ __forceinline__ uint64_t hash64(uint64_t v) {
@@ -90,13 +92,15 @@ __device__ __forceinline__ void insert4(float d, uint32_t point, uint32_t leader
     }
 }
 
-template <bool SQ8>
+template <bool SQ8, int LG>
 __global__ void __launch_bounds__(kRows) assign_kernel(const Params p) {
-  __shared__ __align__(16) float lt_f[kLeaders][kAxF];
-  __shared__ __align__(16) int lt_q[kLeaders][kAxQ / 4];
-  __shared__ uint32_t l_ids[kLeaders];
-  __shared__ float l_norm[kLeaders];
-  __shared__ float l_scale[kLeaders];
+  // Leader tiles: LG leaders x one K tile, read by every thread with
+  // broadcast 16-byte loads.
+  __shared__ __align__(16) float lt_f[SQ8 ? 1 : LG][SQ8 ? 4 : kAxF];
+  __shared__ __align__(16) int lt_q[SQ8 ? LG : 1][SQ8 ? kAxQ / 4 : 4];
+  __shared__ uint32_t l_ids[LG];
+  __shared__ float l_norm[LG];
+  __shared__ float l_scale[LG];
 
   if (blockIdx.x >= p.num_work) return;
   uint2 w = p.work[blockIdx.x];
@@ -113,6 +117,8 @@ __global__ void __launch_bounds__(kRows) assign_kernel(const Params p) {
   const float* norms = SQ8 ? p.sq8_norms : p.raw_norms;
   float n_p = valid ? norms[point] : 0.f;
   float s_p = (SQ8 && valid) ? p.scales[point] : 0.f;
+  // f32 rows load as float4 when every row starts 16-byte aligned
+  const bool vec_rows = (p.dim & 3u) == 0u && (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0u;
 
   float bd[4];
   uint32_t bs[4], bl[4];
@@ -123,10 +129,10 @@ __global__ void __launch_bounds__(kRows) assign_kernel(const Params p) {
     bl[j] = 0xffffffffu;
   }
 
-  for (uint32_t lg = 0; lg < nl; lg += kLeaders) {
-    uint32_t gl = nl - lg < kLeaders ? nl - lg : kLeaders;
+  for (uint32_t lg = 0; lg < nl; lg += LG) {
+    uint32_t gl = nl - lg < (uint32_t)LG ? nl - lg : (uint32_t)LG;
     __syncthreads();
-    if (threadIdx.x < kLeaders) {
+    if (threadIdx.x < (uint32_t)LG) {
       uint32_t lid = 0xffffffffu;
       float ln = 0.f, ls = 0.f;
       if (threadIdx.x < gl) {
@@ -143,57 +149,83 @@ __global__ void __launch_bounds__(kRows) assign_kernel(const Params p) {
       l_norm[threadIdx.x] = ln;
       l_scale[threadIdx.x] = ls;
     }
-    float accf[kLeaders];
-    int acci[kLeaders];
+    float accf[LG];
+    int acci[LG];
 #pragma unroll
-    for (int l = 0; l < (int)kLeaders; ++l) {
+    for (int l = 0; l < LG; ++l) {
       accf[l] = 0.0f;
       acci[l] = 0;
     }
-    if (!SQ8) {
+    if constexpr (!SQ8) {
       for (uint32_t a0 = 0; a0 < p.dim; a0 += kAxF) {
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < kLeaders * kAxF; i += kRows) {
+        for (uint32_t i = threadIdx.x; i < (uint32_t)LG * kAxF; i += kRows) {
           uint32_t l = i / kAxF, a = i % kAxF;
           uint32_t lid = l_ids[l];
           lt_f[l][a] = (lid != 0xffffffffu && a0 + a < p.dim) ? p.x[(uint64_t)lid * p.dim + a0 + a] : 0.0f;
         }
         __syncthreads();
-        uint32_t na = p.dim - a0 < kAxF ? p.dim - a0 : kAxF;
+        const uint32_t na = p.dim - a0 < kAxF ? p.dim - a0 : kAxF;
         const float* xr = p.x + (uint64_t)point * p.dim + a0;
-        for (uint32_t a = 0; a < na; ++a) {
-          float xv = valid ? __ldg(xr + a) : 0.0f;
+        // Axes strictly in order for every leader: rn(rn(x*y) + acc).
+        uint32_t a = 0;
+        if (vec_rows) {
+          for (; a + 4 <= na; a += 4) {
+            const float4 xv = valid ? __ldg(reinterpret_cast<const float4*>(xr + a)) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int l = 0; l < (int)kLeaders; ++l) accf[l] = __fadd_rn(accf[l], __fmul_rn(xv, lt_f[l][a]));
+            for (int l = 0; l < LG; ++l) {
+              const float4 yv = *reinterpret_cast<const float4*>(&lt_f[l][a]);
+              float t = accf[l];
+              t = __fadd_rn(t, __fmul_rn(xv.x, yv.x));
+              t = __fadd_rn(t, __fmul_rn(xv.y, yv.y));
+              t = __fadd_rn(t, __fmul_rn(xv.z, yv.z));
+              accf[l] = __fadd_rn(t, __fmul_rn(xv.w, yv.w));
+            }
+          }
+        }
+        for (; a < na; ++a) {
+          const float xv = valid ? __ldg(xr + a) : 0.0f;
+#pragma unroll
+          for (int l = 0; l < LG; ++l) accf[l] = __fadd_rn(accf[l], __fmul_rn(xv, lt_f[l][a]));
         }
       }
     } else {
+      // codes rows are padded_dim bytes, a multiple of 16: int4 loads
       for (uint32_t a0 = 0; a0 < p.padded_dim; a0 += kAxQ) {
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < kLeaders * (kAxQ / 4); i += kRows) {
-          uint32_t l = i / (kAxQ / 4), q = i % (kAxQ / 4);
+        for (uint32_t i = threadIdx.x; i < (uint32_t)LG * (kAxQ / 16); i += kRows) {
+          uint32_t l = i / (kAxQ / 16), c = i % (kAxQ / 16);
           uint32_t lid = l_ids[l];
-          int v = 0;
-          if (lid != 0xffffffffu && a0 + q * 4 < p.padded_dim)
-            v = *reinterpret_cast<const int*>(p.codes + (uint64_t)lid * p.padded_dim + a0 + q * 4);
-          lt_q[l][q] = v;
+          int4 v = make_int4(0, 0, 0, 0);
+          if (lid != 0xffffffffu && a0 + c * 16 < p.padded_dim)
+            v = *reinterpret_cast<const int4*>(p.codes + (uint64_t)lid * p.padded_dim + a0 + c * 16);
+          *reinterpret_cast<int4*>(&lt_q[l][c * 4]) = v;
         }
         __syncthreads();
-        uint32_t nq = (p.padded_dim - a0 < kAxQ ? p.padded_dim - a0 : kAxQ) / 4;
-        const int* cr = reinterpret_cast<const int*>(p.codes + (uint64_t)point * p.padded_dim + a0);
-        for (uint32_t q = 0; q < nq; ++q) {
-          int cv = valid ? __ldg(cr + q) : 0;
+        const uint32_t nc = (p.padded_dim - a0 < kAxQ ? p.padded_dim - a0 : kAxQ) / 16;
+        const int4* cr = reinterpret_cast<const int4*>(p.codes + (uint64_t)point * p.padded_dim + a0);
+        for (uint32_t c = 0; c < nc; ++c) {
+          const int4 cv = valid ? __ldg(cr + c) : make_int4(0, 0, 0, 0);
 #pragma unroll
-          for (int l = 0; l < (int)kLeaders; ++l) acci[l] = __dp4a(cv, lt_q[l][q], acci[l]);
+          for (int l = 0; l < LG; ++l) {
+            const int4 lv = *reinterpret_cast<const int4*>(&lt_q[l][c * 4]);
+            int t = acci[l];
+            t = __dp4a(cv.x, lv.x, t);
+            t = __dp4a(cv.y, lv.y, t);
+            t = __dp4a(cv.z, lv.z, t);
+            acci[l] = __dp4a(cv.w, lv.w, t);
+          }
         }
       }
     }
     if (valid) {
-      for (uint32_t l = 0; l < gl; ++l) {
+#pragma unroll
+      for (int l = 0; l < LG; ++l) {
+        if ((uint32_t)l >= gl) break;
         uint32_t lid = l_ids[l];
         if (lid == 0xffffffffu) continue;
         float d;
-        if (!SQ8) {
+        if constexpr (!SQ8) {
           d = __fadd_rn(__fadd_rn(n_p, l_norm[l]), __fmul_rn(-2.0f, accf[l]));
         } else {
           float nn = __fadd_rn(n_p, l_norm[l]);
@@ -224,12 +256,23 @@ __global__ void __launch_bounds__(kRows) assign_kernel(const Params p) {
 }  // namespace assign
 
 
-int launch_assign(const assign::Params& prm, bool sq8, cudaStream_t stream) {
+template <bool SQ8>
+static void launch_lg(const assign::Params& prm, uint32_t max_leaders, cudaStream_t stream) {
+  if (max_leaders <= 8)
+    assign::assign_kernel<SQ8, 8><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+  else if (max_leaders <= 16)
+    assign::assign_kernel<SQ8, 16><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+  else
+    assign::assign_kernel<SQ8, 32><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+}
+
+// max_leaders: the largest leader count of any task (picks the register group).
+int launch_assign(const assign::Params& prm, bool sq8, uint32_t max_leaders, cudaStream_t stream) {
   if (prm.num_work == 0) return TESSA_OK;
   if (sq8)
-    assign::assign_kernel<true><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+    launch_lg<true>(prm, max_leaders, stream);
   else
-    assign::assign_kernel<false><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+    launch_lg<false>(prm, max_leaders, stream);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 

@@ -153,11 +153,35 @@ struct AssignPlan {
   DevBuf d_moff, d_mcnt, d_loff, d_lcnt, d_rh, d_out, d_work;
   uint32_t num_work = 0;
   uint32_t task_count = 0;
+  uint32_t max_leaders = 0;  // largest leader count of any task
+  // host copy of the task arrays the device tables were built from: a call
+  // with the same tasks (replay sweeps) reuses them without an upload
+  std::vector<uint32_t> key32;
+  std::vector<uint64_t> key64;
+  uint64_t key_member_rows = 0, out_len_cached = 0;
+  bool valid = false;
+
+  bool same_tasks(const tessa_assign_args& a) const {
+    const size_t n = a.task_count;
+    if (!valid || n != task_count || a.member_rows != key_member_rows || key32.size() != 5 * n) return false;
+    const uint32_t* cols[5] = {a.task_member_offsets, a.task_member_counts, a.task_leader_offsets,
+                               a.task_leader_counts, a.task_rh};
+    for (int c = 0; c < 5; ++c)
+      if (n && memcmp(cols[c], key32.data() + c * n, n * 4) != 0) return false;
+    return n == 0 || memcmp(a.task_output_offsets, key64.data(), n * 8) == 0;
+  }
 
   int build(const tessa_assign_args& a, uint64_t* output_len, cudaStream_t st) {
+    if (same_tasks(a)) {
+      *output_len = out_len_cached;
+      return TESSA_OK;
+    }
+    valid = false;
     std::vector<uint2> work;
     uint64_t out_len = 0;
+    max_leaders = 0;
     for (uint32_t t = 0; t < a.task_count; ++t) {
+      max_leaders = std::max(max_leaders, a.task_leader_counts[t]);
       if (a.task_rh[t] == 0 || a.task_rh[t] > TESSA_MAX_RH || a.task_leader_counts[t] < a.task_rh[t])
         return fail(TESSA_ERR_INVALID_ARG, "assignment task %u has invalid r_h=%u for %u leaders", t, a.task_rh[t],
                     a.task_leader_counts[t]);
@@ -189,9 +213,19 @@ struct AssignPlan {
     CUDA_TRY(cudaStreamSynchronize(st));
     num_work = (uint32_t)work.size();
     task_count = a.task_count;
+    key32.resize(5 * n);
+    key64.assign(a.task_output_offsets, a.task_output_offsets + n);
+    const uint32_t* cols[5] = {a.task_member_offsets, a.task_member_counts, a.task_leader_offsets,
+                               a.task_leader_counts, a.task_rh};
+    for (int c = 0; c < 5; ++c)
+      if (n) memcpy(key32.data() + c * n, cols[c], n * 4);
+    key_member_rows = a.member_rows;
+    out_len_cached = out_len;
+    valid = true;
     return TESSA_OK;
   }
   void release() {
+    valid = false;
     d_moff.release();
     d_mcnt.release();
     d_loff.release();
@@ -637,6 +671,8 @@ int assign_device(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* a, c
     return fail(TESSA_ERR_INVALID_ARG, "unknown assignment source %u", source);
   if (source == TESSA_ASSIGN_SQ8 && (a->padded_dim == 0 || a->padded_dim % 16 != 0))
     return fail(TESSA_ERR_INVALID_ARG, "padded_dim=%u must be a positive multiple of 16", a->padded_dim);
+  if (source == TESSA_ASSIGN_SQ8 && (reinterpret_cast<uintptr_t>(a->codes) & 15u) != 0u)
+    return fail(TESSA_ERR_INVALID_ARG, "SQ8 codes must start on a 16-byte boundary");
   if (a->task_count && (!a->task_member_offsets || !a->task_member_counts || !a->task_leader_offsets ||
                         !a->task_leader_counts || !a->task_rh || !a->task_output_offsets))
     return fail(TESSA_ERR_INVALID_ARG, "null task array");
@@ -668,7 +704,7 @@ int assign_device(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* a, c
   p.out_ids = a->out_ids;
   p.out_dists = a->out_dists;
   p.err_word = ctx->d_err.as<uint32_t>();
-  TRY(launch_assign(p, source == TESSA_ASSIGN_SQ8, st));
+  TRY(launch_assign(p, source == TESSA_ASSIGN_SQ8, ctx->assign_plan.max_leaders, st));
   uint32_t bits = 0;
   TRY(read_err(ctx, st, &bits));
   return map_device_error(bits);
@@ -755,6 +791,22 @@ void tessa_destroy(tessa_ctx* ctx) {
 }
 
 int tessa_ctx_device(const tessa_ctx* ctx) { return ctx ? ctx->device : -1; }
+
+int tessa_ctx_device_bytes(const tessa_ctx* ctx, uint64_t* bytes) {
+  if (!ctx || !bytes) return fail(TESSA_ERR_INVALID_ARG, "null argument");
+  const DevBuf* bufs[] = {&ctx->d_err, &ctx->gather, &ctx->fallback, &ctx->leaf_plan.d_starts,
+                          &ctx->leaf_plan.d_sizes, &ctx->leaf_plan.d_tiles, &ctx->assign_plan.d_moff,
+                          &ctx->assign_plan.d_mcnt, &ctx->assign_plan.d_loff, &ctx->assign_plan.d_lcnt,
+                          &ctx->assign_plan.d_rh, &ctx->assign_plan.d_out, &ctx->assign_plan.d_work, &ctx->h_codes,
+                          &ctx->h_scales, &ctx->h_norms, &ctx->h_gids, &ctx->h_members, &ctx->h_ids, &ctx->h_dists,
+                          &ctx->h_x, &ctx->fb_counts, &ctx->d0_lcodes, &ctx->d0_lscales, &ctx->d0_lnorms,
+                          &ctx->d0_keys, &ctx->d0_k2l, &ctx->d0_okeys, &ctx->d0_dists, &ctx->d0_lvec, &ctx->d0_lids,
+                          &ctx->d0_child, &ctx->d0_point, &ctx->e_starts, &ctx->e_sizes};
+  uint64_t n = 0;
+  for (const DevBuf* b : bufs) n += b->bytes;
+  *bytes = n;
+  return TESSA_OK;
+}
 
 int tessa_leaf_last_fallback_rows(const tessa_ctx* ctx, uint64_t* rows) {
   if (!ctx || !rows) return fail(TESSA_ERR_INVALID_ARG, "null argument");

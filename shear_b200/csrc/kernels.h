@@ -129,7 +129,7 @@ struct Params {
 };
 }  // namespace assign
 
-int launch_assign(const assign::Params& prm, bool sq8, cudaStream_t stream);
+int launch_assign(const assign::Params& prm, bool sq8, uint32_t max_leaders, cudaStream_t stream);
 
 // Records `code` and `message` as the calling thread's last error (returned by
 // tessa_last_error_message); returns `code`.
