@@ -247,6 +247,7 @@ struct tessa_ctx {
   DevBuf d_err;         // one uint32 error word
   DevBuf gather;        // leaf-ordered codes scratch
   DevBuf fallback;      // exact-fallback row list: count + (leaf, row) entries
+  DevBuf dump;          // column-split leaf kernel: per-row zone dump
   LeafPlan leaf_plan;
   AssignPlan assign_plan;
   // staging for host-buffer entry points
@@ -342,10 +343,19 @@ int validate_leaf(const tessa_leaf_args* a) {
 // Launches the leaf kernel (and its exact fallback) over tiles
 // [tile0, tile0 + ntiles) of the current leaf plan on `st`, without waiting.
 // The fallback-row count of this launch lands in *d_fb_count.
+// Rows [row0, row0 + nrows) of the leaf-ordered space hold every leaf of the
+// launch (the range of the column-split kernel's zone dump).
 int leaf_launch_tiles(tessa_ctx* ctx, const tessa_leaf_args* a, const int8_t* lc, uint32_t tile0, uint32_t ntiles,
-                      uint32_t* d_fb_count, cudaStream_t st) {
+                      uint32_t* d_fb_count, cudaStream_t st, uint64_t row0, uint64_t nrows) {
   if (ntiles == 0) return TESSA_OK;
   LeafLaunch L;
+  uint32_t ring = 0, log_cap = 0;
+  if (nrows && leaf_split_plan(a->padded_dim, a->k, &ring, &log_cap)) {
+    TRY(ctx->dump.ensure(leaf_dump_bytes(nrows, a->k)));
+    L.d_dump = ctx->dump.ptr;
+    L.dump_row0 = row0;
+    L.dump_rows = nrows;
+  }
   L.leaf_codes = lc;
   L.leaf_rows = a->leaf_rows;
   L.padded_dim = a->padded_dim;
@@ -385,7 +395,7 @@ int leaf_device(tessa_ctx* ctx, const tessa_leaf_args* a, cudaStream_t st) {
   TRY(clear_err(ctx, st));
   TRY(ctx->fallback.ensure(16 + (size_t)a->leaf_rows * 8));
   uint32_t* d_fb = ctx->fallback.as<uint32_t>();
-  TRY(leaf_launch_tiles(ctx, a, lc, 0, ctx->leaf_plan.num_tiles, d_fb, st));
+  TRY(leaf_launch_tiles(ctx, a, lc, 0, ctx->leaf_plan.num_tiles, d_fb, st, 0, a->leaf_rows));
   uint32_t fb = 0;
   CUDA_TRY(cudaMemcpyAsync(&fb, d_fb, 4, cudaMemcpyDeviceToHost, st));
   uint32_t bits = 0;
@@ -448,6 +458,14 @@ int leaf_host_pipelined(tessa_ctx* ctx, const tessa_leaf_args* a) {
     ctx->ev_done.push_back(e);
   }
   TRY(ctx->fb_counts.ensure(nb * 4));
+  {
+    // size the zone dump for the largest batch before any copy is queued
+    uint64_t max_rows = 0;
+    for (const Batch& B : batches) max_rows = B.r1 - B.r0 > max_rows ? B.r1 - B.r0 : max_rows;
+    uint32_t ring = 0, log_cap = 0;
+    if (max_rows && leaf_split_plan((uint32_t)P, (uint32_t)K, &ring, &log_cap))
+      TRY(ctx->dump.ensure(leaf_dump_bytes(max_rows, (uint32_t)K)));
+  }
 
   tessa_leaf_args d = *a;
   d.codes = ctx->h_codes.as<int8_t>();
@@ -477,7 +495,7 @@ int leaf_host_pipelined(tessa_ctx* ctx, const tessa_leaf_args* a) {
                                cudaMemcpyHostToDevice, si));
       CUDA_TRY(cudaEventRecord(ctx->ev_in[b], si));
       CUDA_TRY(cudaStreamWaitEvent(st, ctx->ev_in[b], 0));
-      TRY(leaf_launch_tiles(ctx, &d, d.codes, B.t0, B.nt, ctx->fb_counts.as<uint32_t>() + b, st));
+      TRY(leaf_launch_tiles(ctx, &d, d.codes, B.t0, B.nt, ctx->fb_counts.as<uint32_t>() + b, st, B.r0, B.r1 - B.r0));
       CUDA_TRY(cudaEventRecord(ctx->ev_done[b], st));
       CUDA_TRY(cudaStreamWaitEvent(so, ctx->ev_done[b], 0));
       CUDA_TRY(cudaMemcpyAsync(a->topk_ids + B.r0 * K, ctx->h_ids.as<uint32_t>() + B.r0 * K, n * K * 4,
@@ -769,6 +787,7 @@ void tessa_destroy(tessa_ctx* ctx) {
   ctx->d_err.release();
   ctx->gather.release();
   ctx->fallback.release();
+  ctx->dump.release();
   ctx->leaf_plan.release();
   ctx->assign_plan.release();
   DevBuf* bufs[] = {&ctx->h_codes, &ctx->h_scales, &ctx->h_norms, &ctx->h_gids, &ctx->h_members,
@@ -794,7 +813,7 @@ int tessa_ctx_device(const tessa_ctx* ctx) { return ctx ? ctx->device : -1; }
 
 int tessa_ctx_device_bytes(const tessa_ctx* ctx, uint64_t* bytes) {
   if (!ctx || !bytes) return fail(TESSA_ERR_INVALID_ARG, "null argument");
-  const DevBuf* bufs[] = {&ctx->d_err, &ctx->gather, &ctx->fallback, &ctx->leaf_plan.d_starts,
+  const DevBuf* bufs[] = {&ctx->d_err, &ctx->gather, &ctx->fallback, &ctx->dump, &ctx->leaf_plan.d_starts,
                           &ctx->leaf_plan.d_sizes, &ctx->leaf_plan.d_tiles, &ctx->assign_plan.d_moff,
                           &ctx->assign_plan.d_mcnt, &ctx->assign_plan.d_loff, &ctx->assign_plan.d_lcnt,
                           &ctx->assign_plan.d_rh, &ctx->assign_plan.d_out, &ctx->assign_plan.d_work, &ctx->h_codes,

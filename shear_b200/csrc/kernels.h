@@ -28,7 +28,19 @@ struct LeafLaunch {
   uint64_t resident_rows;     // bound for member ids
   uint64_t timeout_ns;
   int sm_count;
+  // Column-split kernel (padded_dim <= 1024): per-row zone dump for rows
+  // [dump_row0, dump_row0 + dump_rows) of the leaf-ordered row space,
+  // leaf_dump_bytes(dump_rows, k) bytes at d_dump.  Null: the four-warp kernel.
+  void* d_dump = nullptr;
+  uint64_t dump_row0 = 0;
+  uint64_t dump_rows = 0;
 };
+
+// Column-split leaf kernel: shared-memory plan (false: not supported for this
+// padded_dim / k) and the dump scratch it needs for `rows` leaf rows.
+bool leaf_split_plan(uint32_t padded_dim, uint32_t k, uint32_t* ring, uint32_t* log_cap);
+uint64_t leaf_dump_bytes(uint64_t rows, uint32_t k);
+uint32_t leaf_dump_entries(uint32_t k);
 
 // Largest leaf the leaf kernel accepts (a validated cap above the reference's
 // leaf sizes).

@@ -1,0 +1,930 @@
+// SQ8 leaf all-pairs evaluation with fused per-row bounded top-k, column-split
+// epilogue (sm_100a, padded_dim <= 1024).
+//
+// Same result as leaf_topk_sq8_kernel (leaf_sq8.cu): candidates of row r are
+// the other members of its leaf, distance = gpu_persistent_sq_int8_l2_from_dot
+// (CB = shear-core/src/algorithm/pipnn/compute_backend.rs, CB:8987-9002), the
+// k best under the eps/id rule of gpu_persistent_insert_topk_candidate_fp32
+// (CB:7229-7259) in ascending member order (CB:9569-9650), derived without
+// sequential insertion by the zone argument in leaf_sq8.cu: per row, every
+// candidate within kMargin of the k-th smallest distance is collected, sorted
+// and checked for order independence; rows that fail go to the exact fallback.
+//
+// Why a second kernel: in the four-warp form one epilogue warp per SM
+// sub-partition computes distances, maintains the per-row bound and finishes
+// the rows, and it is latency-bound (one warp cannot hide its own dependency
+// chains).  Here two warps share every TMEM lane quadrant and split each
+// 128-column chunk: warp half h takes the 32-column groups h and h + 2 with
+// its own sorted bound and candidate log.  Shared memory for the second set of logs
+// comes from keeping the A tile (the 128 rows of the tile) in tensor memory
+// instead of shared memory: the MMA reads A from TMEM (tcgen05.mma with an
+// A tensor-memory operand), B streams through shared memory as before.
+//
+// Per-row bound of a half: min(own k-th smallest, max(own j-th, other j-th))
+// with j = ceil(k/2): at least j + j >= k candidates of the row lie at or
+// below max(own j-th, other j-th), so both terms bound the row's k-th
+// smallest from above.  The halves publish their j-th smallest after every
+// column group (tagged with the tile, so a value of a previous tile is never
+// used).  A candidate is logged while it is within kMargin of the bound.  At
+// the end of a tile the halves exchange their sorted arrays and both merge
+// them into the row's k smallest distances (theta = the k-th); each half
+// compacts its log to [0, theta + kMargin] (its part of the zone) and writes
+// it to a per-row dump in global memory, half 0 adds the merged k smallest.
+// leaf_finish_kernel then ranks each row's zone against those k values (as
+// leaf_sq8.cu's finish does), verifies it and writes the k results (or lists
+// the row for the exact fallback), with enough warps per SM to hide latency.
+// The next tile's A is written to TMEM before a tile's rows are wrapped up,
+// so the MMA runs ahead meanwhile.
+//
+// Roles (352 threads, one persistent CTA per SM):
+//   warp 0      TMA producer: a ring of 16 KiB stages carrying, per tile, the
+//               A slabs (128 rows x 128 bytes of K) and then the B slabs of
+//               every 128-column chunk;
+//   warp 1      TMEM owner (512 columns: A tile at [0, padded_dim/4), two
+//               128-column accumulators at [256, 512)) and MMA issuer;
+//   warps 2..9  epilogue; warp w reads TMEM lane quadrant w % 4, half
+//               (w - 2) / 4; at the start of a tile all eight copy the A slabs
+//               from the ring into TMEM (each a quadrant x 64 bytes of K);
+//   warp 10     column metadata ring (scale, norm, global id per column).
+#include "common.cuh"
+#include "kernels.h"
+#include "leaf_common.cuh"
+
+namespace tessa {
+namespace leaf {
+namespace split {
+
+constexpr uint32_t kThreads = 352;
+constexpr uint32_t kEpiWarps = 8;
+constexpr uint32_t kMetaWarp = 10;
+constexpr uint32_t kAccBufs = 2;
+constexpr uint32_t kAccCol = 256;  // first accumulator column
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kMaxSlabs = 8;  // padded_dim <= 1024: A tile <= 256 TMEM columns
+constexpr uint32_t kMaxRing = 8;
+constexpr uint32_t kStageBytes = kBM * kSlab;  // 16 KiB (A and B slabs alike)
+constexpr uint32_t kMetaBytes = kMetaSlots * kBN * 12u;
+constexpr uint32_t kStashBytes = kEpiWarps * 32u * kStashStride * 4u;
+constexpr uint32_t kPubBytes = 2u * kBM * 8u;
+constexpr uint32_t kBarBytes = 512u;
+constexpr uint32_t kFinThreads = 128;
+
+static_assert(kBM == kBN, "A and B slabs share the ring and the tensor map");
+
+struct Smem {
+  uint8_t* ring;
+  float2* meta_sn;
+  uint32_t* meta_g;
+  float* stash;     // [8 warps][32 lanes][kStashStride]
+  uint64_t* pub;    // [2 halves][kBM] (tile tag << 32 | bound bits)
+  uint2* log;       // [2 halves][log_cap][kBM]
+  uint64_t* b_full;
+  uint64_t* b_empty;
+  uint64_t* t_full;
+  uint64_t* t_empty;
+  uint64_t* m_full;
+  uint64_t* m_empty;
+  uint64_t* a_tm_full;  // A tile of the current tile written to TMEM
+  uint64_t* a_rd;       // [kMaxRing] all epilogue warps have read the A slab in this stage
+  uint64_t* pair;       // [4] two warps of a lane quadrant
+  uint64_t* mma_done;
+  uint32_t* tmem_slot;
+  uint32_t* abort_flag;
+};
+
+__host__ __device__ inline uint32_t smem_bytes(uint32_t ring, uint32_t log_cap) {
+  return 1024u + ring * kStageBytes + kMetaBytes + kStashBytes + kPubBytes + 2u * log_cap * kBM * kLogEntryBytes +
+         kBarBytes;
+}
+
+__device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t ring, uint32_t log_cap) {
+  uintptr_t base = (reinterpret_cast<uintptr_t>(raw) + 1023u) & ~uintptr_t(1023u);
+  uint8_t* p = reinterpret_cast<uint8_t*>(base);
+  Smem s;
+  s.ring = p;
+  p += ring * kStageBytes;
+  s.meta_sn = reinterpret_cast<float2*>(p);
+  p += kMetaSlots * kBN * 8u;
+  s.meta_g = reinterpret_cast<uint32_t*>(p);
+  p += kMetaSlots * kBN * 4u;
+  s.stash = reinterpret_cast<float*>(p);
+  p += kStashBytes;
+  s.pub = reinterpret_cast<uint64_t*>(p);
+  p += kPubBytes;
+  s.log = reinterpret_cast<uint2*>(p);
+  p += 2u * log_cap * kBM * kLogEntryBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(p);
+  s.b_full = bars;
+  s.b_empty = s.b_full + kMaxRing;
+  s.t_full = s.b_empty + kMaxRing;
+  s.t_empty = s.t_full + kAccBufs;
+  s.m_full = s.t_empty + kAccBufs;
+  s.m_empty = s.m_full + kMetaSlots;
+  s.a_tm_full = s.m_empty + kMetaSlots;
+  s.a_rd = s.a_tm_full + 1;
+  s.pair = s.a_rd + kMaxRing;
+  s.mma_done = s.pair + 4;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.mma_done + 1);
+  s.abort_flag = s.tmem_slot + 1;
+  return s;
+}
+
+// Both warps of a lane quadrant meet; false if the wait timed out or the CTA
+// aborted.  `phase` counts the meetings of this pair.
+__device__ __forceinline__ bool pair_meet(uint64_t* bar, uint32_t& phase, uint32_t lane,
+                                          volatile uint32_t* abort_flag, const Params& p) {
+  __syncwarp();
+  bool ok = true;
+  if (lane == 0) {
+    mbar_arrive(bar);
+    ok = mbar_wait(bar, phase & 1u, abort_flag, p.err_word, p.timeout_ns);
+  }
+  ++phase;
+  return __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0u;
+}
+
+// Epilogue warp: copy this lane's row of the A tile (whose first ring item is
+// `rpos`) into TMEM: 16-byte pieces 4*half..4*half+3 of every A slab (128B
+// swizzle: piece j of row r sits at j ^ (r & 7)).  Each ring stage is
+// released as soon as all eight warps have read it (one read barrier per
+// stage: a warp can arrive on a stage's barrier again only after the stage
+// was released and refilled).  Then arrive on a_tm_full.  False on a timed
+// out or aborted wait.
+__device__ __forceinline__ bool load_a_tile(const Smem& s, const Params& p, uint32_t rpos, uint32_t ew,
+                                            uint32_t half, uint32_t row_in_tile, uint32_t lane, uint32_t lane_base,
+                                            uint32_t tmem_base, uint32_t& arp, volatile uint32_t* abort_flag) {
+  const uint32_t nst = p.num_bstages;
+  for (uint32_t sl = 0; sl < p.num_slabs; ++sl) {
+    const uint32_t it = rpos + sl, st = it % nst, ph = (it / nst) & 1u;
+    const bool ok = mbar_wait(&s.b_full[st], ph, abort_flag, p.err_word, p.timeout_ns);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const uint8_t* rowp = s.ring + st * kStageBytes + row_in_tile * kSlab;
+    uint32_t r[16];
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u) {
+      const uint32_t j = half * 4u + u;
+      const uint4 v = *reinterpret_cast<const uint4*>(rowp + ((j ^ (row_in_tile & 7u)) << 4));
+      r[4 * u] = v.x;
+      r[4 * u + 1] = v.y;
+      r[4 * u + 2] = v.z;
+      r[4 * u + 3] = v.w;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s.a_rd[st]);
+    tmem_st_32x32b_x16(tmem_base + lane_base + sl * (kSlab / 4u) + half * 16u, r);
+    if (ew == 0) {
+      bool rd = true;
+      if (lane == 0) {
+        rd = mbar_wait(&s.a_rd[st], (arp >> st) & 1u, abort_flag, p.err_word, p.timeout_ns);
+        if (rd) mbar_arrive(&s.b_empty[st]);
+      }
+      arp ^= 1u << st;  // completed phases of each stage's read barrier, mod 2
+      if (__shfl_sync(0xffffffffu, rd ? 1u : 0u, 0) == 0u) return false;
+    }
+  }
+  tmem_st_wait();
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(s.a_tm_full);
+  return true;
+}
+
+template <int KS>
+__global__ void __launch_bounds__(kThreads, 1)
+    leaf_topk_split_kernel(const __grid_constant__ CUtensorMap tmap, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem s = carve(smem_raw, p.num_bstages, p.log_cap);
+  const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+  volatile uint32_t* abort_flag = s.abort_flag;
+  const uint32_t nst = p.num_bstages;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < nst; ++i) {
+      mbar_init(&s.b_full[i], 1);
+      mbar_init(&s.b_empty[i], 1);
+    }
+    for (uint32_t i = 0; i < kAccBufs; ++i) {
+      mbar_init(&s.t_full[i], 1);
+      mbar_init(&s.t_empty[i], kEpiWarps);
+    }
+    for (uint32_t i = 0; i < kMetaSlots; ++i) {
+      mbar_init(&s.m_full[i], 32);
+      mbar_init(&s.m_empty[i], kEpiWarps);
+    }
+    mbar_init(s.a_tm_full, kEpiWarps);
+    for (uint32_t i = 0; i < nst; ++i) mbar_init(&s.a_rd[i], kEpiWarps);
+    for (uint32_t i = 0; i < 4; ++i) mbar_init(&s.pair[i], 2);
+    mbar_init(s.mma_done, 1);
+    *s.abort_flag = 0u;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp >= 2 && warp < 2 + kEpiWarps) s.pub[((warp - 2) >> 2) * kBM + (warp & 3u) * 32u + lane] = 0ull;
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap);
+  if (warp == 1) {
+    tmem_alloc(s.tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s.tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        uint2 t;
+        uint64_t start;
+        uint32_t cnt, ncol;
+        tile_span<false>(p, tile, t, start, cnt, ncol);
+        const uint32_t nchunks = (ncol + kBN - 1) / kBN;
+        // A slabs of the tile's rows, then B slabs chunk by chunk.
+        for (uint32_t item = 0; item < p.num_slabs * (1u + nchunks) && ok; ++item) {
+          const uint32_t sl = item % p.num_slabs;
+          const uint32_t c = item / p.num_slabs;  // 0 = A, c >= 1: chunk c - 1
+          if (!mbar_wait(&s.b_empty[stage], phase ^ 1u, abort_flag, p.err_word, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.b_full[stage], kStageBytes);
+          const int32_t y = c == 0 ? (int32_t)(start + t.y) : (int32_t)(start + (uint64_t)(c - 1) * kBN);
+          tma_load_2d(&tmap, s.ring + stage * kStageBytes, &s.b_full[stage], (int32_t)(sl * kSlab), y);
+          if (++stage == nst) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(kBM, kBN);
+      const uint32_t ring_base = smem_u32(s.ring);
+      uint32_t stage = 0, phase = 0, acc = 0, a_iter = 0;
+      bool ok = true;
+      for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++a_iter) {
+        uint2 t;
+        uint64_t start;
+        uint32_t cnt, ncol;
+        tile_span<false>(p, tile, t, start, cnt, ncol);
+        const uint32_t nchunks = (ncol + kBN - 1) / kBN;
+        // The A items of the ring belong to the epilogue warps.
+        for (uint32_t sl = 0; sl < p.num_slabs; ++sl)
+          if (++stage == nst) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        if (!mbar_wait(s.a_tm_full, a_iter & 1u, abort_flag, p.err_word, p.timeout_ns)) break;
+        tc_fence_after();
+        for (uint32_t c = 0; c < nchunks && ok; ++c, ++acc) {
+          const uint32_t buf = acc % kAccBufs, use = acc / kAccBufs;
+          if (!mbar_wait(&s.t_empty[buf], (use & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tmem_d = tmem_base + kAccCol + buf * kBN;
+          for (uint32_t sl = 0; sl < p.num_slabs; ++sl) {
+            if (!mbar_wait(&s.b_full[stage], phase, abort_flag, p.err_word, p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t b_addr = ring_base + stage * kStageBytes;
+#pragma unroll
+            for (uint32_t kk = 0; kk < kSlab / kMmaK; ++kk)
+              mma_i8_ts(tmem_d, tmem_base + sl * (kSlab / 4u) + kk * (kMmaK / 4u), smem_desc_sw128(b_addr + kk * kMmaK),
+                        idesc, (sl | kk) != 0u ? 1u : 0u);
+            mma_commit(&s.b_empty[stage]);
+            if (++stage == nst) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (ok) mma_commit(&s.t_full[buf]);
+        }
+      }
+      // Every issued MMA must have landed before TMEM is released.
+      mma_commit(s.mma_done);
+      uint32_t dummy_abort = 0u;
+      mbar_wait(s.mma_done, 0u, &dummy_abort, p.err_word, p.timeout_ns);
+    }
+  } else if (warp == kMetaWarp) {
+    // ------------------------------------------------------ column metadata
+    uint32_t seq = 0;
+    bool ok = true;
+    for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      uint2 t;
+      uint64_t start;
+      uint32_t cnt, ncol;
+      tile_span<false>(p, tile, t, start, cnt, ncol);
+      const uint32_t nchunks = (ncol + kBN - 1) / kBN;
+      for (uint32_t c = 0; c < nchunks; ++c, ++seq) {
+        const uint32_t slot = seq % kMetaSlots, use = seq / kMetaSlots;
+        bool w = true;
+        if (lane == 0) w = mbar_wait(&s.m_empty[slot], (use & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns);
+        if (__shfl_sync(0xffffffffu, w ? 1u : 0u, 0) == 0u) {
+          ok = false;
+          break;
+        }
+        uint32_t lid[kBN / 32];
+#pragma unroll
+        for (uint32_t u = 0; u < kBN / 32; ++u) {
+          const uint32_t col = c * kBN + u * 32 + lane;
+          lid[u] = col < cnt ? __ldg(p.members + start + col) : 0xffffffffu;
+        }
+        float2 sn[kBN / 32];
+        uint32_t gv[kBN / 32];
+#pragma unroll
+        for (uint32_t u = 0; u < kBN / 32; ++u) {
+          sn[u] = make_float2(0.f, INFINITY);  // past the leaf: distance +inf
+          gv[u] = 0xffffffffu;
+          if (lid[u] < p.resident_rows) {
+            sn[u] = make_float2(__ldg(p.scales + lid[u]), __ldg(p.norms + lid[u]));
+            gv[u] = __ldg(p.global_ids + lid[u]);
+          } else if (lid[u] != 0xffffffffu) {
+            atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+          }
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kBN / 32; ++u) {
+          s.meta_sn[slot * kBN + u * 32 + lane] = sn[u];
+          s.meta_g[slot * kBN + u * 32 + lane] = gv[u];
+        }
+        mbar_arrive(&s.m_full[slot]);
+      }
+    }
+  } else if (warp < 2 + kEpiWarps) {
+    // ------------------------------------------------------ epilogue
+    const uint32_t ew = warp - 2;        // 0..7
+    const uint32_t quad = warp & 3u;     // TMEM lane quadrant this warp may access
+    const uint32_t half = ew >> 2;       // column groups half, half + 2
+    const uint32_t row_in_tile = quad * 32u + lane;
+    const uint32_t lane_base = (quad * 32u) << 16;
+    float* stash = s.stash + (ew * 32u + lane) * kStashStride;
+    const float* ostash = s.stash + ((ew ^ 4u) * 32u + lane) * kStashStride;  // the other half's
+    uint2* log = s.log + half * p.log_cap * kBM;
+    volatile uint64_t* my_pub = s.pub + half * kBM + row_in_tile;
+    volatile uint64_t* other_pub = s.pub + (half ^ 1u) * kBM + row_in_tile;
+    const uint32_t cap = p.log_cap;
+    const uint32_t k = p.k;
+    const uint32_t jt = k >> 1;  // sk[jt] is the ceil(k/2)-th smallest
+    uint32_t acc = 0, seq = 0, rpos = 0, tseq = 0, pair_phase = 0, arp = 0;
+    bool stop = false;
+    uint32_t tile = blockIdx.x;
+    if (tile < p.num_tiles) {
+      uint2 t;
+      uint64_t start;
+      uint32_t cnt, ncol;
+      tile_span<false>(p, tile, t, start, cnt, ncol);
+      stop = !load_a_tile(s, p, rpos, ew, half, row_in_tile, lane, lane_base, tmem_base, arp, abort_flag);
+      rpos += p.num_slabs * (1u + (ncol + kBN - 1) / kBN);
+    }
+    for (; tile < p.num_tiles && !stop; tile += gridDim.x, ++tseq) {
+      uint2 t;
+      uint64_t start;
+      uint32_t cnt, ncol;
+      tile_span<false>(p, tile, t, start, cnt, ncol);
+      const uint32_t nchunks = (ncol + kBN - 1) / kBN;
+      const uint32_t row = t.y + row_in_tile;
+      bool valid = row < cnt;
+      float s_i = 0.f, n_i = 0.f;
+      if (valid) {
+        const uint32_t lid_i = __ldg(p.members + start + row);
+        if (lid_i >= p.resident_rows) {
+          atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+          valid = false;
+        } else {
+          s_i = __ldg(p.scales + lid_i);
+          n_i = __ldg(p.norms + lid_i);
+        }
+      }
+      // sk: the k smallest distances of this half, descending (sk[0] = the
+      // k-th smallest); slots [k, KS) hold -inf sentinels.
+      float sk[KS];
+#pragma unroll
+      for (int q = 0; q < KS; ++q) sk[q] = (uint32_t)q < k ? INFINITY : -INFINITY;
+      float xb = INFINITY;  // max(own, other) ceil(k/2)-th smallest at the last exchange
+      float ob = INFINITY;  // the other half's ceil(k/2)-th smallest, as last published
+      float thr = valid ? INFINITY : -INFINITY;
+      uint32_t nlog = 0;
+      bool ovf = false;
+      const uint32_t c_self = t.y / kBN;  // the row's own column: chunk c_self, group quad, lane `lane`
+      const uint64_t tag = (uint64_t)(tseq + 1u) << 32;
+      for (uint32_t c = 0; c < nchunks; ++c, ++acc, ++seq) {
+        const uint32_t mslot = seq % kMetaSlots;
+        const float4* msn = reinterpret_cast<const float4*>(s.meta_sn + mslot * kBN);
+        const uint32_t* mg = s.meta_g + mslot * kBN;
+        const uint32_t buf = acc % kAccBufs, use = acc / kAccBufs;
+        bool ok = true;
+        if (lane == 0) {
+          ok = mbar_wait(&s.m_full[mslot], (seq / kMetaSlots) & 1u, abort_flag, p.err_word, p.timeout_ns) &&
+               mbar_wait(&s.t_full[buf], use & 1u, abort_flag, p.err_word, p.timeout_ns);
+        }
+        if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0u) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (uint32_t gg = 0; gg < 2; ++gg) {
+          const uint32_t g = gg * 2u + half;  // groups interleaved: both halves see the leaf's first columns
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_base + kAccCol + buf * kBN + g * kGroup, v);
+          tmem_ld_wait();
+          // Exact reference distances; bit (31 - cc) of mask = column cc is
+          // below the bound (the sign of d - thr, shifted in), four chains.
+          float dc[32];
+          uint32_t mq[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+          for (uint32_t cc = 0; cc < kGroup; cc += 2) {
+            const float4 m = msn[(g * kGroup + cc) >> 1];
+            const float t0 = __fmul_rn(s_i, m.x);
+            const float t1 = __fmul_rn(s_i, m.z);
+            const float u0 = __fmul_rn(t0, __int2float_rn((int)v[cc]));
+            const float u1 = __fmul_rn(t1, __int2float_rn((int)v[cc + 1]));
+            const float nn0 = __fadd_rn(n_i, m.y);
+            const float nn1 = __fadd_rn(n_i, m.w);
+            // rn(nn + rn(-2*u)) == fma(-2, u, nn): -2*u is exact.
+            const float d0 = __fmaf_rn(-2.0f, u0, nn0);
+            const float d1 = __fmaf_rn(-2.0f, u1, nn1);
+            dc[cc] = d0;
+            dc[cc + 1] = d1;
+            uint32_t& w = mq[cc >> 3];
+            w = __funnelshift_l(__float_as_uint(__fsub_rn(d0, thr)), w, 1);
+            w = __funnelshift_l(__float_as_uint(__fsub_rn(d1, thr)), w, 1);
+          }
+          uint32_t mask = (mq[0] << 24) | (mq[1] << 16) | (mq[2] << 8) | mq[3];
+          float4* st4 = reinterpret_cast<float4*>(stash);
+#pragma unroll
+          for (uint32_t q = 0; q < kGroup / 4; ++q)
+            st4[q] = make_float4(dc[4 * q], dc[4 * q + 1], dc[4 * q + 2], dc[4 * q + 3]);
+          if (c == c_self && g == quad) mask &= ~(0x80000000u >> lane);  // the row itself
+          const uint32_t* gq = mg + g * kGroup;
+          // Two candidates per step, the same number of steps in every lane;
+          // the next pair's loads are issued before the current insertion.
+          const uint32_t steps = (__reduce_max_sync(0xffffffffu, __popc(mask)) + 1u) >> 1;
+          bool h0, h1;
+          uint32_t c0, c1;
+          next_pair(mask, h0, c0, h1, c1);
+          float a0 = stash[c0], a1 = stash[c1];
+          uint32_t g0 = gq[c0], g1 = gq[c1];
+          for (uint32_t it = 0; it < steps;) {
+            uint32_t room = (cap - nlog) >> 1;
+            if (__any_sync(0xffffffffu, room < steps - it)) {
+              nlog = log_compact(log, row_in_tile, nlog, thr);
+              room = (cap - nlog) >> 1;
+            }
+            uint32_t batch = min(steps - it, __reduce_min_sync(0xffffffffu, room));
+            batch = batch > 0u ? batch : 1u;
+            const uint32_t end = it + batch;
+#pragma unroll 1
+            for (; it < end; ++it) {
+              bool nh0, nh1;
+              uint32_t nc0, nc1;
+              next_pair(mask, nh0, nc0, nh1, nc1);
+              const float na0 = stash[nc0], na1 = stash[nc1];
+              const uint32_t ng0 = gq[nc0], ng1 = gq[nc1];
+              const float d0 = h0 ? (a0 > 0.0f ? a0 : 0.0f) : INFINITY;  // reference clamp d <= 0 -> +0 (CB:8999-9001)
+              const float d1 = h1 ? (a1 > 0.0f ? a1 : 0.0f) : INFINITY;
+              const bool ok0 = h0 && d0 <= thr, ok1 = h1 && d1 <= thr;
+              const bool w0 = ok0 && nlog < cap;
+              const uint32_t e1 = nlog + (w0 ? 1u : 0u);
+              const bool w1 = ok1 && e1 < cap;
+              if (w0) log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(d0), g0);
+              if (w1) log[e1 * kBM + row_in_tile] = make_uint2(__float_as_uint(d1), g1);
+              nlog = e1 + (w1 ? 1u : 0u);
+              ovf |= (ok0 && !w0) || (ok1 && !w1);
+              topk_insert2<KS>(sk, fminf(d0, d1), fmaxf(d0, d1));
+              if (valid) thr = __fadd_rn(fminf(sk[0], xb), kMargin);
+              h0 = nh0;
+              h1 = nh1;
+              a0 = na0;
+              a1 = na1;
+              g0 = ng0;
+              g1 = ng1;
+            }
+          }
+          // Exchange ceil(k/2)-th smallest distances with the other half.
+          float own_j = sk[KS / 2];  // k == KS (the usual case): a fixed slot
+          if (k != (uint32_t)KS) {
+#pragma unroll
+            for (int q = 0; q < KS; ++q)
+              if ((uint32_t)q == jt) own_j = sk[q];
+          }
+          *my_pub = tag | __float_as_uint(own_j);
+          const uint64_t o = *other_pub;
+          if ((o & 0xffffffff00000000ull) == tag) ob = fminf(ob, __uint_as_float((uint32_t)o));
+          xb = fmaxf(own_j, ob);
+          if (valid) thr = __fadd_rn(fminf(sk[0], xb), kMargin);
+          __syncwarp();
+        }
+        if (stop) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&s.t_empty[buf]);
+          mbar_arrive(&s.m_empty[mslot]);
+        }
+      }
+      if (stop) break;
+
+      // ---- the next tile's A first: the MMA starts on it while this tile's
+      // rows are wrapped up (all MMAs of this tile have completed).
+      const uint32_t next = tile + gridDim.x;
+      if (next < p.num_tiles) {
+        uint2 tn;
+        uint64_t sn;
+        uint32_t cn, nn;
+        tile_span<false>(p, next, tn, sn, cn, nn);
+        if (!load_a_tile(s, p, rpos, ew, half, row_in_tile, lane, lane_base, tmem_base, arp, abort_flag)) {
+          stop = true;
+          break;
+        }
+        rpos += p.num_slabs * (1u + (nn + kBN - 1) / kBN);
+      }
+
+      // ---- tile end: the row's k smallest distances from both sorted arrays
+#pragma unroll
+      for (int q = 0; q < KS; ++q) stash[q] = sk[q];
+      if (!pair_meet(&s.pair[quad], pair_phase, lane, abort_flag, p)) {
+        stop = true;
+        break;
+      }
+      if (k == (uint32_t)KS) {
+        // sk descending, the other's reversed ascending: their element-wise
+        // minimum is the KS smallest of both, a bitonic sequence; half-cleaners
+        // sort it descending.
+#pragma unroll
+        for (int q = 0; q < KS; ++q) sk[q] = fminf(sk[q], ostash[KS - 1 - q]);
+#pragma unroll
+        for (int dd = KS / 2; dd >= 1; dd >>= 1)
+#pragma unroll
+          for (int q = 0; q < KS; ++q)
+            if ((q & dd) == 0) {
+              const float a = sk[q], b = sk[q + dd];
+              sk[q] = fmaxf(a, b);
+              sk[q + dd] = fminf(a, b);
+            }
+      } else {
+        for (uint32_t q = 0; q < k; q += 2) {
+          const float x = ostash[q], y = q + 1u < k ? ostash[q + 1u] : INFINITY;
+          topk_insert2<KS>(sk, fminf(x, y), fmaxf(x, y));
+        }
+      }
+      // sk: the row's k smallest, descending; sk[0] = theta
+      if (!pair_meet(&s.pair[quad], pair_phase, lane, abort_flag, p)) {
+        stop = true;
+        break;
+      }
+      if (valid) {
+        const uint32_t E = log_compact(log, row_in_tile, nlog, __fadd_rn(sk[0], kMargin));
+        const uint64_t rd = start + row - p.dump_row0;
+        if (rd < p.dump_rows) {
+          const bool fits = !ovf && E <= p.dump_d;
+          if (fits)
+            for (uint32_t e = 0; e < E; ++e)
+              p.dump[(uint64_t)(half ? p.dump_d - 1u - e : e) * p.dump_rows + rd] = log[e * kBM + row_in_tile];
+          p.dump_cnt[2u * rd + half] = fits ? (uint8_t)E : (uint8_t)0xFFu;
+          if (half == 0) {
+            // the sorted k smallest for the finishing kernel's ranks (32 slots, -inf padded)
+#pragma unroll
+            for (int q = 0; q < 32; q += 4)
+              p.dump_m[(uint64_t)(q / 4) * p.dump_rows + rd] =
+                  make_float4(q < KS ? sk[q] : -INFINITY, q + 1 < KS ? sk[q + 1] : -INFINITY,
+                              q + 2 < KS ? sk[q + 2] : -INFINITY, q + 3 < KS ? sk[q + 3] : -INFINITY);
+          }
+        } else {
+          atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
+        }
+      }
+      __syncwarp();
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Output slots of one row, written four at a time (16-byte stores) when the
+// row's slots are 16-byte aligned.
+struct RowWriter {
+  uint32_t* ids;
+  float* dists;
+  bool vec;
+  uint32_t bi[4];
+  float bd[4];
+  __device__ __forceinline__ void put(uint32_t q, uint32_t id, float d) {
+    if (!vec) {
+      ids[q] = id;
+      dists[q] = d;
+      return;
+    }
+    const uint32_t w = q & 3u;
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u)
+      if (u == w) {
+        bi[u] = id;
+        bd[u] = d;
+      }
+    if (w == 3u) {
+      *reinterpret_cast<uint4*>(ids + q - 3u) = make_uint4(bi[0], bi[1], bi[2], bi[3]);
+      *reinterpret_cast<float4*>(dists + q - 3u) = make_float4(bd[0], bd[1], bd[2], bd[3]);
+    }
+  }
+  // q = slots written so far; flush a partial group of four
+  __device__ __forceinline__ void flush(uint32_t q) {
+    if (!vec) return;
+#pragma unroll
+    for (uint32_t u = 0; u < 3; ++u)
+      if (u < (q & 3u)) {
+        ids[(q & ~3u) + u] = bi[u];
+        dists[(q & ~3u) + u] = bd[u];
+      }
+  }
+};
+
+// Finish the rows of one tile per block (thread = row), as leaf_sq8.cu's
+// finish does: the row's zone (both halves' dumps) is ranked against the
+// row's k smallest distances (m, descending, -inf padded to 32; theta = m[0]):
+// an entry at or below theta ranks by the number of smaller values in m,
+// equal distances take consecutive ranks in dump order, entries in the
+// margin follow ordered by distance.  The sorted zone is then verified run by
+// run and the k results written, or the row is listed for the exact fallback.
+// A zone entry with the row's own global id (a repeated member) sends the row
+// to the fallback.
+__global__ void __launch_bounds__(kFinThreads) leaf_finish_kernel(const Params p) {
+  extern __shared__ uint32_t fin_smem[];
+  const uint32_t D = p.dump_d;
+  float* zd = reinterpret_cast<float*>(fin_smem);        // [D][128]
+  uint32_t* zg = fin_smem + D * kFinThreads;             // [D][128]
+  uint8_t* perm = reinterpret_cast<uint8_t*>(zg + D * kFinThreads);  // [D][128]
+  const uint32_t tid = threadIdx.x;
+  const uint32_t k = p.k;
+  for (uint32_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    const uint2 t = p.tiles[tile];
+    const uint64_t start = p.leaf_starts[t.x];
+    const uint32_t cnt = p.leaf_sizes[t.x];
+    const uint32_t row = t.y + tid;
+    if (row >= cnt) continue;
+    const uint64_t rd = start + row - p.dump_row0;
+    if (rd >= p.dump_rows) continue;  // reported by the main kernel
+    const uint32_t lid_i = p.members[start + row];
+    if (lid_i >= p.resident_rows) continue;  // reported by the main kernel
+    const uint32_t gid_i = p.global_ids[lid_i];
+    const uint32_t e0 = p.dump_cnt[2u * rd], e1 = p.dump_cnt[2u * rd + 1u];
+    bool ok = e0 != 0xFFu && e1 != 0xFFu && e0 + e1 <= D;
+    if (ok) {
+      const uint32_t E = e0 + e1;
+      float m[32];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 v = p.dump_m[(uint64_t)q * p.dump_rows + rd];
+        m[4 * q] = v.x;
+        m[4 * q + 1] = v.y;
+        m[4 * q + 2] = v.z;
+        m[4 * q + 3] = v.w;
+      }
+      const float theta = m[0];
+      const bool complete = !(theta < INFINITY);
+      const float thr = __fadd_rn(theta, kMargin);
+      uint32_t n_inner = 0;
+      for (uint32_t e = 0; e < e0; ++e) {
+        const uint2 v = p.dump[(uint64_t)e * p.dump_rows + rd];
+        zd[e * kFinThreads + tid] = __uint_as_float(v.x);
+        zg[e * kFinThreads + tid] = v.y;
+        n_inner += __uint_as_float(v.x) <= theta ? 1u : 0u;
+        ok &= v.y != gid_i;
+      }
+      for (uint32_t e = 0; e < e1; ++e) {
+        const uint2 v = p.dump[(uint64_t)(D - 1u - e) * p.dump_rows + rd];
+        zd[(e0 + e) * kFinThreads + tid] = __uint_as_float(v.x);
+        zg[(e0 + e) * kFinThreads + tid] = v.y;
+        n_inner += __uint_as_float(v.x) <= theta ? 1u : 0u;
+        ok &= v.y != gid_i;
+      }
+      uint64_t occ = 0;
+      for (uint32_t e = 0; ok && e < E; ++e) {
+        const float d = zd[e * kFinThreads + tid];
+        uint32_t r;
+        if (d <= theta) {
+          uint32_t r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+#pragma unroll
+          for (int q = 0; q < 32; q += 4) {
+            r0 += m[q] < d ? 1u : 0u;
+            r1 += m[q + 1] < d ? 1u : 0u;
+            r2 += m[q + 2] < d ? 1u : 0u;
+            r3 += m[q + 3] < d ? 1u : 0u;
+          }
+          r = (r0 + r1) + (r2 + r3) - (32u - k);  // minus the -inf padding
+        } else {
+          r = n_inner;
+          for (uint32_t f = 0; f < E; ++f) {
+            const float df = zd[f * kFinThreads + tid];
+            r += (df > theta && (df < d || (df == d && f < e))) ? 1u : 0u;
+          }
+        }
+        while (r < 63u && ((occ >> r) & 1ull)) ++r;
+        occ |= 1ull << r;
+        if (r < D) perm[r * kFinThreads + tid] = (uint8_t)e;
+      }
+      ok &= occ == (E >= 64u ? ~0ull : ((1ull << E) - 1ull));  // a permutation, else give up safely
+      const uint32_t Z = E;
+      const uint64_t out = (start + row) * (uint64_t)k;
+      RowWriter wr;
+      wr.ids = p.out_ids + out;
+      wr.dists = p.out_dists + out;
+      wr.vec = (k & 3u) == 0u && ((reinterpret_cast<uintptr_t>(wr.ids) | reinterpret_cast<uintptr_t>(wr.dists)) & 15u) == 0u;
+      // One pass in sorted order; a run (neighbours closer than eps) is
+      // emitted when it closes: runs of one and two directly, longer runs
+      // through the tournament check.
+      uint32_t q = 0, rs = 0;
+      float prev = -INFINITY;
+      uint2 first = make_uint2(0u, 0u), second = make_uint2(0u, 0u);
+      for (uint32_t i = 0; ok && i <= Z && q < k; ++i) {
+        const bool end = i == Z;
+        uint2 vi = make_uint2(0x7f800000u, 0u);
+        if (!end) {
+          const uint32_t e = perm[i * kFinThreads + tid];
+          vi = make_uint2(__float_as_uint(zd[e * kFinThreads + tid]), zg[e * kFinThreads + tid]);
+        }
+        const float di = __uint_as_float(vi.x);
+        const bool close = !end && i > 0 && fabsf(__fsub_rn(di, prev)) <= kTieEps;
+        if (i > 0 && !close) {
+          const uint32_t len = i - rs;  // run [rs, i) is complete
+          // The run holding rank k must end inside the zone: every candidate
+          // outside the zone lies above thr, hence more than eps above the run.
+          if (q + len >= k && end && !complete && !(__fsub_rn(thr, prev) > kTieEps)) {
+            ok = false;
+            break;
+          }
+          if (len == 1) {
+            wr.put(q, first.y, __uint_as_float(first.x));
+            ++q;
+          } else if (len == 2) {
+            const bool sw = stable_better(__uint_as_float(second.x), second.y, __uint_as_float(first.x), first.y);
+            const uint2 lo = sw ? second : first, hi = sw ? first : second;
+            wr.put(q, lo.y, __uint_as_float(lo.x));
+            ++q;
+            if (q < k) {
+              wr.put(q, hi.y, __uint_as_float(hi.x));
+              ++q;
+            }
+          } else {
+            // Tournament of the run under the eps/id rule: transitive iff the
+            // win counts are 0..len-1 (then "<" orders the run by wins).
+            if (len > kMaxRun) {
+              ok = false;
+              break;
+            }
+            float rdist[kMaxRun];
+            uint32_t rg[kMaxRun];
+            for (uint32_t u = 0; u < len; ++u) {
+              const uint32_t e = perm[(rs + u) * kFinThreads + tid];
+              rdist[u] = zd[e * kFinThreads + tid];
+              rg[u] = zg[e * kFinThreads + tid];
+            }
+            uint32_t wins[kMaxRun];
+            uint32_t seen = 0;
+            for (uint32_t u = 0; u < len; ++u) {
+              uint32_t w = 0;
+              for (uint32_t x = 0; x < len; ++x)
+                if (x != u && stable_better(rdist[u], rg[u], rdist[x], rg[x])) ++w;
+              wins[u] = w;
+              seen |= 1u << w;
+            }
+            if (seen != (1u << len) - 1u) {
+              ok = false;
+              break;
+            }
+            for (uint32_t rank = 0; rank < len && q < k; ++rank) {
+              const uint32_t want = len - 1 - rank;
+              for (uint32_t u = 0; u < len; ++u)
+                if (wins[u] == want) wr.put(q, rg[u], rdist[u]);
+              ++q;
+            }
+          }
+          rs = i;
+        }
+        if (i == rs) first = vi;
+        if (i == rs + 1) second = vi;
+        prev = di;
+      }
+      if (ok) {
+        for (; q < k; ++q) wr.put(q, 0xffffffffu, 3.402823466e+38F);
+        wr.flush(q);
+      }
+    }
+    if (!ok) {
+      const uint32_t slot = atomicAdd(p.fb_count, 1u);
+      if (slot < p.fb_capacity)
+        p.fb_list[slot] = make_uint2(t.x, row);
+      else
+        atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
+    }
+  }
+}
+
+}  // namespace split
+}  // namespace leaf
+
+// ---------------------------------------------------------------- host side
+
+// Ring stages and log entries per row and half for the column-split kernel:
+// the deepest ring (<= 8 stages) that leaves a log of max(k + 24, 34) entries
+// per half (a half logs up to 32 candidates of its first group before the
+// halves first exchange bounds; room above the zone keeps compactions rare,
+// which measured worth more than ring depth: 4 stages with 58 entries beat 6
+// with 42 at k = 32), else 4 stages with at least max(k + 4, 34).  False if
+// neither fits or padded_dim > 1024.
+bool leaf_split_plan(uint32_t padded_dim, uint32_t k, uint32_t* ring, uint32_t* log_cap) {
+  const uint32_t slabs = (padded_dim + leaf::kSlab - 1) / leaf::kSlab;
+  if (slabs == 0 || slabs > leaf::split::kMaxSlabs || k == 0 || k > 32) return false;
+  auto cap_for = [&](uint32_t st) -> uint32_t {
+    const uint32_t used = leaf::split::smem_bytes(st, 0);
+    if (used >= leaf::kSmemLimit) return 0;
+    const uint32_t c = (leaf::kSmemLimit - used) / (2u * leaf::kBM * leaf::kLogEntryBytes);
+    return c < leaf::kMaxLogCap ? c : leaf::kMaxLogCap;
+  };
+  for (uint32_t st = leaf::split::kMaxRing; st >= 4; --st) {
+    const uint32_t c = cap_for(st);
+    if (c >= k + 24 && c >= 34) {
+      *ring = st;
+      *log_cap = c;
+      return true;
+    }
+  }
+  const uint32_t c = cap_for(4);
+  if (c >= k + 4 && c >= 34) {
+    *ring = 4;
+    *log_cap = c;
+    return true;
+  }
+  return false;
+}
+
+// Zone entries dumped per row (both halves together); rows with a larger zone
+// go to the exact fallback.  48 holds the k = 32 zone with room for ties.
+uint32_t leaf_dump_entries(uint32_t) { return 48u; }
+
+// Per row: the zone entries (8 bytes each), the merged k smallest (32 floats)
+// and two entry counts.
+uint64_t leaf_dump_bytes(uint64_t rows, uint32_t k) {
+  return rows * ((uint64_t)leaf_dump_entries(k) * 8u + 128u + 2u);
+}
+
+template <int KS>
+static int launch_split_main(const CUtensorMap& tm, const leaf::Params& prm, uint32_t smem, uint32_t grid,
+                             cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(leaf::split::leaf_topk_split_kernel<KS>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return TESSA_ERR_CUDA;
+  leaf::split::leaf_topk_split_kernel<KS><<<grid, leaf::split::kThreads, smem, stream>>>(tm, prm);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+// Column-split main kernel, finishing kernel (the exact fallback follows in
+// the caller).  prm must carry the dump buffers; fb_count is cleared here.
+int launch_leaf_split(const CUtensorMap& tm, leaf::Params& prm, uint32_t padded_dim, int sm_count,
+                      cudaStream_t stream) {
+  uint32_t ring = 0, log_cap = 0;
+  if (!leaf_split_plan(padded_dim, prm.k, &ring, &log_cap)) return TESSA_ERR_UNSUPPORTED;
+  prm.num_slabs = (padded_dim + leaf::kSlab - 1) / leaf::kSlab;
+  prm.num_bstages = ring;
+  prm.log_cap = log_cap;
+  prm.dump_d = leaf_dump_entries(prm.k);
+  const uint32_t smem = leaf::split::smem_bytes(ring, log_cap);
+  const uint32_t grid = prm.num_tiles < (uint32_t)sm_count ? prm.num_tiles : (uint32_t)sm_count;
+  int rc;
+  if (prm.k <= 2)
+    rc = launch_split_main<2>(tm, prm, smem, grid, stream);
+  else if (prm.k <= 4)
+    rc = launch_split_main<4>(tm, prm, smem, grid, stream);
+  else if (prm.k <= 8)
+    rc = launch_split_main<8>(tm, prm, smem, grid, stream);
+  else if (prm.k <= 16)
+    rc = launch_split_main<16>(tm, prm, smem, grid, stream);
+  else
+    rc = launch_split_main<32>(tm, prm, smem, grid, stream);
+  if (rc != TESSA_OK) return rc;
+  const uint32_t fin_smem = prm.dump_d * leaf::split::kFinThreads * 9u;
+  const uint32_t fin_grid = prm.num_tiles < (uint32_t)sm_count * 8u ? prm.num_tiles : (uint32_t)sm_count * 8u;
+  if (fin_smem > 48u * 1024u &&
+      cudaFuncSetAttribute(leaf::split::leaf_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)fin_smem) != cudaSuccess)
+    return TESSA_ERR_CUDA;
+  leaf::split::leaf_finish_kernel<<<fin_grid, leaf::split::kFinThreads, fin_smem, stream>>>(prm);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+}  // namespace tessa

@@ -63,66 +63,23 @@
 // argument above carries over unchanged: only the candidate set differs.
 #include "common.cuh"
 #include "kernels.h"
+#include "leaf_common.cuh"
 
 namespace tessa {
 namespace leaf {
 
-constexpr uint32_t kBM = 128;          // rows per tile (TMEM lanes)
-constexpr uint32_t kBN = 128;          // columns per chunk (MMA N)
-constexpr uint32_t kSlab = 128;        // K bytes per TMA box (one 128B swizzle atom)
-constexpr uint32_t kMmaK = 32;         // K per tcgen05.mma kind::i8
 constexpr uint32_t kThreads = 224;     // TMA, MMA, 4 epilogue warps, metadata warp
 constexpr uint32_t kEpiWarps = 4;
 constexpr uint32_t kMetaWarp = 6;
-constexpr uint32_t kMetaSlots = 4;      // chunk metadata ring
 constexpr uint32_t kAccBufs = 4;
 constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 512
 constexpr uint32_t kASlabBytes = kBM * kSlab;   // 16 KiB
 constexpr uint32_t kBStageBytes = kBN * kSlab;  // 16 KiB
-constexpr uint32_t kGroup = 32;                 // columns per tcgen05.ld
 constexpr uint32_t kGroups = kBN / kGroup;
 constexpr uint32_t kMaxBStages = 8;
-constexpr uint32_t kStashStride = 36;           // floats per lane (16B aligned, conflict-free STS.128)
 constexpr uint32_t kMetaBytes = kMetaSlots * kBN * 12u;  // ring of (scale, norm) + global id
 constexpr uint32_t kStashBytes = 4u * 32u * kStashStride * 4u;
-constexpr uint32_t kLogEntryBytes = 8u;         // (distance bits, global id)
-constexpr uint32_t kMaxLogCap = 64;             // entries per row; ranks fit a 64-bit occupancy mask
 constexpr uint32_t kBarBytes = 512u;
-constexpr uint32_t kSmemLimit = 232448u;  // 227 KiB opt-in per block
-constexpr float kTieEps = 2.0e-5f;
-constexpr float kMargin = 4.0f * kTieEps;  // zone = [0, theta + kMargin]
-constexpr uint32_t kMaxRun = 8;            // longest eps-run checked by tournament
-
-struct Params {
-  const float* scales;
-  const float* norms;
-  const uint32_t* global_ids;
-  const uint32_t* members;      // leaf-ordered local ids
-  const uint64_t* leaf_starts;
-  const uint32_t* leaf_sizes;
-  const uint2* tiles;           // (leaf, first row of tile)
-  uint32_t num_tiles;
-  uint32_t num_slabs;
-  uint32_t num_bstages;
-  uint32_t k;
-  uint32_t log_cap;             // log entries per row (<= kMaxLogCap)
-  uint64_t resident_rows;
-  uint32_t* out_ids;
-  float* out_dists;
-  uint32_t* err_word;
-  uint32_t* fb_count;           // rows handed to the exact fallback
-  uint2* fb_list;               // (leaf, row) entries, capacity fb_capacity
-  uint32_t fb_capacity;
-  uint64_t timeout_ns;
-  // rectangular mode only: rows [0, nrows) of the A matrix against columns
-  // [0, ncols) of col_codes with per-column scale, norm and tie key
-  uint32_t nrows;
-  uint32_t ncols;
-  const int8_t* col_codes;
-  const float* col_scales;
-  const float* col_norms;
-  const uint32_t* col_keys;
-};
 
 struct Smem {
   uint8_t* a;
@@ -178,62 +135,6 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t num_slabs, uint32_t
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.mma_done + 1);
   s.abort_flag = s.tmem_slot + 1;
   return s;
-}
-
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
-// Sorted array (descending, s[0] = maximum) of the KS smallest values seen.
-// Inserting the pair x <= y keeps the KS smallest of s, x and y:
-//   new[t] = max(s[t+2], min(s[t+1], y), min(s[t], x))
-// (the t-th largest of the merged sequence; s[KS] = s[KS+1] = -inf).  With
-// y = +inf it is the single insertion max(s[t+1], min(s[t], x)); values at or
-// above s[0] leave s unchanged.  Slots [k, KS) hold -inf sentinels that never
-// move, so s[0] is the k-th smallest.  Branch-free: 2 min + 1 three-input max
-// per slot.
-template <int KS>
-__device__ __forceinline__ void topk_insert2(float (&s)[KS], float x, float y) {
-  // In place, ascending: slot t reads slots t+1 and t+2 before they change.
-#pragma unroll
-  for (int t = 0; t < KS; ++t) {
-    const float s1 = (t + 1 < KS) ? s[t + 1] : -INFINITY;
-    const float s2 = (t + 2 < KS) ? s[t + 2] : -INFINITY;
-    s[t] = fmax3(s2, fminf(s1, y), fminf(s[t], x));
-  }
-}
-
-// Take the next two marked columns (bit 31 - column, highest first) out of
-// `mask`; a missing one gets h = false and a harmless in-range index.
-__device__ __forceinline__ void next_pair(uint32_t& mask, bool& h0, uint32_t& c0, bool& h1, uint32_t& c1) {
-  h0 = mask != 0u;
-  c0 = h0 ? __clz(mask) : 0u;
-  mask &= ~(h0 ? (0x80000000u >> c0) : 0u);
-  h1 = mask != 0u;
-  c1 = h1 ? __clz(mask) : 0u;
-  mask &= ~(h1 ? (0x80000000u >> c1) : 0u);
-}
-
-// Keep the log entries of `row` with distance <= thr, in place.  Entries are
-// read eight at a time (all loads before any store of the batch: the write
-// index never passes the read index, so the batch is intact).
-__device__ __forceinline__ uint32_t log_compact(uint2* log, uint32_t row, uint32_t cnt, float thr) {
-  uint32_t j = 0;
-  for (uint32_t e0 = 0; e0 < cnt; e0 += 8) {
-    uint2 v[8];
-#pragma unroll
-    for (uint32_t u = 0; u < 8; ++u) v[u] = (e0 + u < cnt) ? log[(e0 + u) * kBM + row] : make_uint2(0x7f800000u, 0u);
-#pragma unroll
-    for (uint32_t u = 0; u < 8; ++u) {
-      if (e0 + u < cnt && __uint_as_float(v[u].x) <= thr) {
-        log[j * kBM + row] = v[u];
-        ++j;
-      }
-    }
-  }
-  return j;
 }
 
 // Finish one row: sort the zone, verify order independence, write k results.
@@ -359,24 +260,6 @@ __device__ bool finish_row(const Params& p, uint2* log, uint8_t* perm, uint32_t 
     p.out_dists[out + q] = 3.402823466e+38F;
   }
   return true;
-}
-
-// Work item `tile`: (leaf, first row) from the tile table, or in rectangular
-// mode (0, 128 * tile) over the whole row matrix.
-template <bool RECT>
-__device__ __forceinline__ void tile_span(const Params& p, uint32_t tile, uint2& t, uint64_t& start, uint32_t& rows,
-                                          uint32_t& cols) {
-  if constexpr (RECT) {
-    t = make_uint2(0u, tile * kBM);
-    start = 0;
-    rows = p.nrows;
-    cols = p.ncols;
-  } else {
-    t = p.tiles[tile];
-    start = p.leaf_starts[t.x];
-    rows = p.leaf_sizes[t.x];
-    cols = rows;
-  }
 }
 
 template <int KS, bool RECT>
@@ -948,6 +831,19 @@ static int launch_main(const CUtensorMap& ta, const CUtensorMap& tb, const leaf:
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 
+// Exact recomputation of the rows whose result depends on insertion order.
+template <bool RECT>
+static int launch_fallback(const leaf::Params& prm, const int8_t* a_codes, uint32_t padded_dim, int sm_count,
+                           cudaStream_t stream) {
+  const uint32_t fb_smem = padded_dim + leaf::kFbBlock * 12u;
+  leaf::leaf_fallback_kernel<RECT><<<(unsigned)sm_count * 4u, leaf::kFbThreads, fb_smem, stream>>>(a_codes, padded_dim,
+                                                                                                  prm);
+  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+int launch_leaf_split(const CUtensorMap& tm, leaf::Params& prm, uint32_t padded_dim, int sm_count,
+                      cudaStream_t stream);
+
 // Main kernel (k-specialised) plus the exact fallback over the rows it lists.
 template <bool RECT>
 static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, leaf::Params& prm, const int8_t* a_codes,
@@ -973,11 +869,7 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, leaf::Param
   else
     rc = launch_main<32, RECT>(ta, tb, prm, smem, grid, stream);
   if (rc != TESSA_OK) return rc;
-  // Exact recomputation of the rows whose result depends on insertion order.
-  const uint32_t fb_smem = padded_dim + leaf::kFbBlock * 12u;
-  leaf::leaf_fallback_kernel<RECT><<<(unsigned)sm_count * 4u, leaf::kFbThreads, fb_smem, stream>>>(a_codes, padded_dim,
-                                                                                                  prm);
-  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+  return launch_fallback<RECT>(prm, a_codes, padded_dim, sm_count, stream);
 }
 
 // Returns 0, or a TESSA_ERR_* code.
@@ -1005,6 +897,20 @@ int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
   prm.fb_list = L.d_fb_list;
   prm.fb_capacity = L.fb_capacity;
   prm.timeout_ns = L.timeout_ns;
+  uint32_t ring = 0, log_cap = 0;
+  if (L.d_dump && L.dump_rows && leaf_split_plan(L.padded_dim, L.k, &ring, &log_cap)) {
+    // Column-split kernel + finishing kernel + exact fallback.
+    prm.dump_row0 = L.dump_row0;
+    prm.dump_rows = L.dump_rows;
+    prm.dump_d = leaf_dump_entries(L.k);
+    prm.dump = reinterpret_cast<uint2*>(L.d_dump);
+    prm.dump_m = reinterpret_cast<float4*>(prm.dump + (uint64_t)prm.dump_d * L.dump_rows);
+    prm.dump_cnt = reinterpret_cast<uint8_t*>(prm.dump_m + 8u * L.dump_rows);
+    if (cudaMemsetAsync(prm.fb_count, 0, 4, stream) != cudaSuccess) return TESSA_ERR_CUDA;
+    int rc = launch_leaf_split(ta, prm, L.padded_dim, L.sm_count, stream);
+    if (rc != TESSA_OK) return rc;
+    return launch_fallback<false>(prm, L.leaf_codes, L.padded_dim, L.sm_count, stream);
+  }
   return launch_pair<false>(ta, tb, prm, L.leaf_codes, L.padded_dim, L.sm_count, stream);
 }
 

@@ -19,7 +19,8 @@ bounds it) and M = R * f leaf rows:
 * leaf batch: member ids M * 4, leaf-ordered code scratch M * padded_dim when
   members are not contiguous, lists M * k * 8, the exact-fallback row list
   M * 8 + 16, leaf layout and tile table (16 bytes per leaf, 8 per 128-row
-  tile, leaves of at least leaf_min rows);
+  tile, leaves of at least leaf_min rows), and for padded_dim <= 1024 the
+  column-split kernel's per-row zone dump M * (8 * 48 + 128 + 2);
 * assignment: member / leader ids 4 * (R + leaders), outputs R * r_h * 8.
 
 ``library_scratch_bytes`` reports what a context actually holds, and the GPU
@@ -166,8 +167,10 @@ def plan_subtree_admission(rows: int, dim: int, leaf_k: int, max_fanout: int, bu
     resident = rows * (pd + 12) + (rows * dim * 4 if raw_assignment else 0)
     leaves = -(-m // GPU_PERSISTENT_LEAF_MIN) if m else 0
     tiles = leaves + -(-m // 128)
-    leaf = (m * 4 + (0 if leaf_ordered else m * pd) + m * min(leaf_k, 32) * 8 + m * 8 + 16
-            + leaves * 16 + tiles * 8)
+    kk = min(leaf_k, 32)
+    dump = m * (8 * 48 + 128 + 2) if pd <= 1024 else 0
+    leaf = (m * 4 + (0 if leaf_ordered else m * pd) + m * kk * 8 + m * 8 + 16
+            + leaves * 16 + tiles * 8 + dump)
     assign = 4 * (rows + leaders) + rows * r_h * 8
     required = resident + leaf + assign
     ok = leaf_k <= 32 and (budget_bytes is None or rows == 0 or required <= budget_bytes)
