@@ -699,17 +699,14 @@ __global__ void __launch_bounds__(kFinThreads) leaf_finish_kernel(const Params p
       const bool complete = !(theta < INFINITY);
       const float thr = __fadd_rn(theta, kMargin);
       uint32_t n_inner = 0;
-      for (uint32_t e = 0; e < e0; ++e) {
-        const uint2 v = p.dump[(uint64_t)e * p.dump_rows + rd];
+      // Entry e < e0 sits at dump slot e, entry e0 + e at slot D - 1 - e
+      // (half 1 fills the slots from the back); four loads in flight at a time.
+#pragma unroll 4
+      for (uint32_t e = 0; e < E; ++e) {
+        const uint32_t slot = e < e0 ? e : D - 1u - (e - e0);
+        const uint2 v = p.dump[(uint64_t)slot * p.dump_rows + rd];
         zd[e * kFinThreads + tid] = __uint_as_float(v.x);
         zg[e * kFinThreads + tid] = v.y;
-        n_inner += __uint_as_float(v.x) <= theta ? 1u : 0u;
-        ok &= v.y != gid_i;
-      }
-      for (uint32_t e = 0; e < e1; ++e) {
-        const uint2 v = p.dump[(uint64_t)(D - 1u - e) * p.dump_rows + rd];
-        zd[(e0 + e) * kFinThreads + tid] = __uint_as_float(v.x);
-        zg[(e0 + e) * kFinThreads + tid] = v.y;
         n_inner += __uint_as_float(v.x) <= theta ? 1u : 0u;
         ok &= v.y != gid_i;
       }
