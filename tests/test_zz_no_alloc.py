@@ -56,8 +56,12 @@ def _allocating(c, d, k):
 
 def test_noalloc_matches_allocating_entry_point_on_two_calls(oracle):
     # Permuted members force the gather of leaf-ordered codes into the static
-    # scratch; the two batches differ in shape, data and k.
-    for sizes, dim, k, seed in (([300, 257, 129], 768, 32, 41), ([640, 100], 256, 4, 42)):
+    # scratch; the batches differ in shape, data and k.  The allocation-free
+    # call runs the four-warp leaf kernel, the allocating call the
+    # column-split kernel and its finishing kernel: the two must agree bit
+    # for bit.
+    for sizes, dim, k, seed in (([300, 257, 129], 768, 32, 41), ([640, 100], 256, 4, 42),
+                                ([2048, 700], 768, 32, 43), ([500, 129], 1024, 16, 44)):
         c = make_leaf_batch(oracle, sizes, dim, seed=seed, dup=True, permute=True)
         d = _tensors(c)
         want_ids, want_d = _allocating(c, d, k)
