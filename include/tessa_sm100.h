@@ -143,7 +143,11 @@ typedef struct tessa_leaf_args {
  * gpu_persistent_subtree_topk_only's SQ8 executors (CB:16146, CB:9364,
  * CB:10389) as launched by TessaCudaReplaySession::launch_leaf
  * (CB:35026-35152).  Rows without k candidates keep (FLT_MAX, 0xffffffff)
- * in their tail slots. */
+ * in their tail slots.  Device scratch held by the context, grown on demand:
+ * the optional leaf-ordered codes (above), the tile table, the exact-fallback
+ * row list (8 bytes per row) and, for padded_dim <= 1024, a per-row zone dump
+ * of 514 bytes per leaf row (the leaf kernel's candidates near each row's k-th
+ * distance, read back by its finishing kernel). */
 TESSA_API int tessa_leaf_topk_sq8(tessa_ctx* ctx, const tessa_leaf_args* args, void* stream);
 
 /* Host-buffer variant: every pointer of `args` (including leaf_members and the
