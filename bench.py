@@ -1052,7 +1052,8 @@ def run_assign(a):
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": None,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks.get("hbm_gbs") else "fallback",
-                "kernel": f"tessa::assign::assign_kernel<{'false' if a.assign_fp32 else 'true'}>",
+                "kernel": ("tessa::assign::assign_kernel<false, LG> (FP32, SIMT)" if a.assign_fp32
+                           else "tessa::assign::tc::assign_tc_kernel<NB> (SQ8, tcgen05)"),
                 "algorithmic_bytes_per_launch": alg, "kernel_ms": per_step * 1e3,
                 "note": "per-step time includes the host-side task table build and one host sync"}
     line = {

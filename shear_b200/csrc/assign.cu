@@ -267,11 +267,13 @@ static void launch_lg(const assign::Params& prm, uint32_t max_leaders, cudaStrea
 }
 
 // max_leaders: the largest leader count of any task (picks the register group).
-int launch_assign(const assign::Params& prm, bool sq8, uint32_t max_leaders, cudaStream_t stream) {
+int launch_assign(const assign::Params& prm, bool sq8, uint32_t max_leaders, int sm_count, cudaStream_t stream) {
   if (prm.num_work == 0) return TESSA_OK;
-  if (sq8)
+  if (sq8) {
+    const int rc = launch_assign_sq8_tc(prm, max_leaders, sm_count, stream);
+    if (rc != TESSA_ERR_UNSUPPORTED) return rc;
     launch_lg<true>(prm, max_leaders, stream);
-  else
+  } else
     launch_lg<false>(prm, max_leaders, stream);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }

@@ -722,7 +722,8 @@ int assign_device(tessa_ctx* ctx, uint32_t source, const tessa_assign_args* a, c
   p.out_ids = a->out_ids;
   p.out_dists = a->out_dists;
   p.err_word = ctx->d_err.as<uint32_t>();
-  TRY(launch_assign(p, source == TESSA_ASSIGN_SQ8, ctx->assign_plan.max_leaders, st));
+  p.timeout_ns = ctx->timeout_ns;
+  TRY(launch_assign(p, source == TESSA_ASSIGN_SQ8, ctx->assign_plan.max_leaders, ctx->sm_count, st));
   uint32_t bits = 0;
   TRY(read_err(ctx, st, &bits));
   return map_device_error(bits);

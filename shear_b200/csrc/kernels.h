@@ -138,10 +138,15 @@ struct Params {
   uint32_t* out_ids;
   float* out_dists;
   uint32_t* err_word;
+  uint64_t timeout_ns = 2000000000ull;  // bound of every wait in the tensor-core kernel
 };
 }  // namespace assign
 
-int launch_assign(const assign::Params& prm, bool sq8, uint32_t max_leaders, cudaStream_t stream);
+// SQ8 sources go to the tensor-core kernel (assign_tc.cu) when every task has
+// at most 128 leaders, to the SIMT kernel otherwise; FP32 sources to the SIMT
+// kernel.
+int launch_assign(const assign::Params& prm, bool sq8, uint32_t max_leaders, int sm_count, cudaStream_t stream);
+int launch_assign_sq8_tc(const assign::Params& prm, uint32_t max_leaders, int sm_count, cudaStream_t stream);
 
 // Records `code` and `message` as the calling thread's last error (returned by
 // tessa_last_error_message); returns `code`.
