@@ -253,17 +253,193 @@ __global__ void __launch_bounds__(kRows) assign_kernel(const Params p) {
   }
 }
 
+// FP32 rows whose starts are all 16-byte aligned (dim % 4 == 0): member rows
+// and the leader group stream through shared memory in 128-byte K stages
+// (32 axes) with cp.async, two stages in flight.  Eight consecutive threads
+// copy one row's 128 contiguous bytes, so a warp's copy instruction covers
+// four whole row segments; each thread then reads its own row from a padded
+// buffer (conflict-free 16-byte loads) and the leader stage with broadcast
+// loads.  The per-leader sums keep the axis order of assign_kernel:
+// rn(rn(x*y) + acc), axis by axis.
+constexpr uint32_t kStage = 128;          // row bytes per K stage
+constexpr uint32_t kPitch = kStage + 16;  // padded row buffer pitch
+
+__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int LG>
+__global__ void __launch_bounds__(kRows) assign_f32_staged_kernel(const Params p) {
+  extern __shared__ __align__(16) uint8_t stg[];
+  uint8_t* rows_buf = stg;                        // [2][kRows][kPitch]
+  uint8_t* lead_buf = stg + 2u * kRows * kPitch;  // [2][LG][kStage]
+  __shared__ uint32_t l_ids[LG];
+  __shared__ float l_norm[LG];
+  __shared__ uint32_t m_pt[kRows];
+
+  if (blockIdx.x >= p.num_work) return;
+  const uint2 w = p.work[blockIdx.x];
+  const uint32_t task = w.x;
+  const uint32_t moff = p.t_moff[task], mcnt = p.t_mcnt[task];
+  const uint32_t loff = p.t_loff[task], nl = p.t_lcnt[task], rh = p.t_rh[task];
+  const uint32_t tid = threadIdx.x;
+  const uint32_t r = w.y + tid;
+  bool valid = r < mcnt;
+  uint32_t point = valid ? p.members[moff + r] : 0u;
+  if (valid && point >= p.resident_rows) {
+    atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+    valid = false;
+    point = 0u;
+  }
+  m_pt[tid] = valid ? point : 0xffffffffu;
+  const float n_p = valid ? p.raw_norms[point] : 0.f;
+  const uint32_t row_bytes = p.dim * 4u;
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(p.x);
+  const uint32_t nstage = (row_bytes + kStage - 1) / kStage;
+  const uint32_t rows_addr = smem_u32(rows_buf), lead_addr = smem_u32(lead_buf);
+
+  float bd[4];
+  uint32_t bs[4], bl[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    bd[j] = 3.402823466e+38F;
+    bs[j] = 0xffffffffu;
+    bl[j] = 0xffffffffu;
+  }
+
+  auto issue = [&](uint32_t st, uint32_t b) {
+    const uint32_t b0 = st * kStage;
+#pragma unroll
+    for (uint32_t i = tid; i < kRows * (kStage / 16); i += kRows) {
+      const uint32_t row = i / (kStage / 16), c = i % (kStage / 16);
+      const uint32_t pt = m_pt[row];
+      const uint32_t off = b0 + c * 16u;
+      const uint32_t n = (pt != 0xffffffffu && off < row_bytes) ? 16u : 0u;
+      cp_async16(rows_addr + (b * kRows + row) * kPitch + c * 16u, base + (n ? (uint64_t)pt * row_bytes + off : 0u), n);
+    }
+    for (uint32_t i = tid; i < (uint32_t)LG * (kStage / 16); i += kRows) {
+      const uint32_t l = i / (kStage / 16), c = i % (kStage / 16);
+      const uint32_t lid = l_ids[l];
+      const uint32_t off = b0 + c * 16u;
+      const uint32_t n = (lid != 0xffffffffu && off < row_bytes) ? 16u : 0u;
+      cp_async16(lead_addr + (b * LG + l) * kStage + c * 16u, base + (n ? (uint64_t)lid * row_bytes + off : 0u), n);
+    }
+    cp_async_commit();
+  };
+
+  for (uint32_t lg = 0; lg < nl; lg += LG) {
+    const uint32_t gl = nl - lg < (uint32_t)LG ? nl - lg : (uint32_t)LG;
+    __syncthreads();
+    if (tid < (uint32_t)LG) {
+      uint32_t lid = 0xffffffffu;
+      float ln = 0.f;
+      if (tid < gl) {
+        lid = p.leaders[loff + lg + tid];
+        if (lid >= p.resident_rows) {
+          atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+          lid = 0xffffffffu;
+        } else {
+          ln = p.raw_norms[lid];
+        }
+      }
+      l_ids[tid] = lid;
+      l_norm[tid] = ln;
+    }
+    __syncthreads();
+    float accf[LG];
+#pragma unroll
+    for (int l = 0; l < LG; ++l) accf[l] = 0.0f;
+    issue(0, 0);
+    for (uint32_t st = 0; st < nstage; ++st) {
+      const uint32_t b = st & 1u;
+      if (st + 1 < nstage) {
+        issue(st + 1, b ^ 1u);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+      const uint8_t* rsrc = rows_buf + (b * kRows + tid) * kPitch;
+      const uint8_t* lsrc = lead_buf + b * LG * kStage;
+      const uint32_t rem = row_bytes - st * kStage;
+      const uint32_t nchunk = (rem < kStage ? rem : kStage) / 16u;
+      for (uint32_t c = 0; c < nchunk; ++c) {
+        const float4 xv = *reinterpret_cast<const float4*>(rsrc + c * 16u);
+#pragma unroll
+        for (int l = 0; l < LG; ++l) {
+          const float4 yv = *reinterpret_cast<const float4*>(lsrc + l * kStage + c * 16u);
+          float t = accf[l];
+          t = __fadd_rn(t, __fmul_rn(xv.x, yv.x));
+          t = __fadd_rn(t, __fmul_rn(xv.y, yv.y));
+          t = __fadd_rn(t, __fmul_rn(xv.z, yv.z));
+          accf[l] = __fadd_rn(t, __fmul_rn(xv.w, yv.w));
+        }
+      }
+      __syncthreads();  // buffer b is refilled by the next stage's copies
+    }
+    if (valid) {
+#pragma unroll
+      for (int l = 0; l < LG; ++l) {
+        if ((uint32_t)l >= gl) break;
+        const uint32_t lid = l_ids[l];
+        if (lid == 0xffffffffu) continue;
+        float d = __fadd_rn(__fadd_rn(n_p, l_norm[l]), __fmul_rn(-2.0f, accf[l]));
+        if (d <= 0.0f) d = 0.0f;
+        insert4(d, point, lid, lg + l, bd, bs, bl);
+      }
+    }
+  }
+
+  if (!valid) return;
+  const uint64_t out = p.t_out[task] + (uint64_t)r * rh;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if ((uint32_t)j >= rh) break;
+    if (bs[j] >= nl) {
+      atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
+      continue;
+    }
+    p.out_ids[out + j] = p.global_ids[bl[j]];
+    p.out_dists[out + j] = bd[j];
+  }
+}
+
 }  // namespace assign
 
 
+template <int LG>
+static void launch_f32_staged(const assign::Params& prm, cudaStream_t stream) {
+  const uint32_t smem = 2u * assign::kRows * assign::kPitch + 2u * LG * assign::kStage;
+  cudaFuncSetAttribute(assign::assign_f32_staged_kernel<LG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  assign::assign_f32_staged_kernel<LG><<<prm.num_work, assign::kRows, smem, stream>>>(prm);
+}
+
 template <bool SQ8>
 static void launch_lg(const assign::Params& prm, uint32_t max_leaders, cudaStream_t stream) {
-  if (max_leaders <= 8)
-    assign::assign_kernel<SQ8, 8><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
-  else if (max_leaders <= 16)
-    assign::assign_kernel<SQ8, 16><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
-  else
-    assign::assign_kernel<SQ8, 32><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+  // f32 rows stage through shared memory when every row starts 16-byte aligned
+  const bool staged = !SQ8 && (prm.dim & 3u) == 0u && (reinterpret_cast<uintptr_t>(prm.x) & 15u) == 0u;
+  if (max_leaders <= 8) {
+    if (staged)
+      launch_f32_staged<8>(prm, stream);
+    else
+      assign::assign_kernel<SQ8, 8><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+  } else if (max_leaders <= 16) {
+    if (staged)
+      launch_f32_staged<16>(prm, stream);
+    else
+      assign::assign_kernel<SQ8, 16><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+  } else {
+    if (staged)
+      launch_f32_staged<32>(prm, stream);
+    else
+      assign::assign_kernel<SQ8, 32><<<prm.num_work, assign::kRows, 0, stream>>>(prm);
+  }
 }
 
 // max_leaders: the largest leader count of any task (picks the register group).
