@@ -665,35 +665,50 @@ __global__ void __launch_bounds__(kFbThreads) leaf_fallback_kernel(const int8_t*
     for (uint32_t b0 = 0; b0 < cnt; b0 += kFbBlock) {
       uint32_t bn = cnt - b0 < kFbBlock ? cnt - b0 : kFbBlock;
       __syncthreads();
-      for (uint32_t c = threadIdx.x; c < bn; c += kFbThreads) {
-        uint32_t lj = RECT ? b0 + c : p.members[start + b0 + c];
-        float dj = INFINITY;
-        uint32_t gj = 0xffffffffu;
-        if (RECT || lj < p.resident_rows) {
-          const int8_t* cbase = RECT ? p.col_codes + (uint64_t)lj * padded_dim
-                                     : leaf_codes + (start + b0 + c) * padded_dim;
-          const int4* cc = reinterpret_cast<const int4*>(cbase);
-          int dot = 0;
-          for (uint32_t w = 0; w < words; ++w) {
-            int4 x = rowbuf[w], y = cc[w];
-            dot = __dp4a(x.x, y.x, dot);
-            dot = __dp4a(x.y, y.y, dot);
-            dot = __dp4a(x.z, y.z, dot);
-            dot = __dp4a(x.w, y.w, dot);
+      // Eight lanes per column (four columns per warp): each 16-byte load
+      // instruction reads 128 contiguous bytes of every column row it touches.
+      const uint32_t grp = lane >> 3, sub = lane & 7u;
+      for (uint32_t cb = warp * 4u; cb < bn; cb += (kFbThreads / 32u) * 4u) {
+        const uint32_t c = cb + grp;
+        uint32_t lj = 0xffffffffu;
+        bool live = false;
+        int dot = 0;
+        if (c < bn) {
+          lj = RECT ? b0 + c : p.members[start + b0 + c];
+          live = RECT || lj < p.resident_rows;
+          if (live) {
+            const int4* cc = reinterpret_cast<const int4*>(RECT ? p.col_codes + (uint64_t)lj * padded_dim
+                                                                : leaf_codes + (start + b0 + c) * padded_dim);
+            for (uint32_t w = sub; w < words; w += 8u) {
+              const int4 x = rowbuf[w], y = cc[w];
+              dot = __dp4a(x.x, y.x, dot);
+              dot = __dp4a(x.y, y.y, dot);
+              dot = __dp4a(x.z, y.z, dot);
+              dot = __dp4a(x.w, y.w, dot);
+            }
           }
-          if constexpr (RECT) {
-            dj = sq8_l2_from_dot(dot, s_i, n_i, p.col_scales[lj], p.col_norms[lj]);
-            gj = p.col_keys[lj];
-          } else {
-            dj = sq8_l2_from_dot(dot, s_i, n_i, p.scales[lj], p.norms[lj]);
-            gj = p.global_ids[lj];
-          }
-        } else {
-          lj = lid_i;  // flagged by the main kernel; never a candidate
         }
-        bd_s[c] = dj;
-        bg_s[c] = gj;
-        bl_s[c] = lj;
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+        if (c < bn && sub == 0u) {
+          float dj = INFINITY;
+          uint32_t gj = 0xffffffffu;
+          if (live) {
+            if constexpr (RECT) {
+              dj = sq8_l2_from_dot(dot, s_i, n_i, p.col_scales[lj], p.col_norms[lj]);
+              gj = p.col_keys[lj];
+            } else {
+              dj = sq8_l2_from_dot(dot, s_i, n_i, p.scales[lj], p.norms[lj]);
+              gj = p.global_ids[lj];
+            }
+          } else {
+            lj = lid_i;  // flagged by the main kernel; never a candidate
+          }
+          bd_s[c] = dj;
+          bg_s[c] = gj;
+          bl_s[c] = lj;
+        }
       }
       __syncthreads();
       if (warp == 0) {
