@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t row = t.y + row_in_tile;
       bool valid = row < cnt;
       float s_i = 0.f, n_i = 0.f;
+      uint32_t gid_i = 0xfffffffeu;
       if (valid) {
         const uint32_t lid_i = __ldg(p.members + start + row);
         if (lid_i >= p.resident_rows) {
@@ -402,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           s_i = __ldg(p.scales + lid_i);
           n_i = __ldg(p.norms + lid_i);
+          gid_i = __ldg(p.global_ids + lid_i);
         }
       }
       // sk: the k smallest distances of this half, descending (sk[0] = the
@@ -586,10 +588,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t E = log_compact(log, row_in_tile, nlog, __fadd_rn(sk[0], kMargin));
         const uint64_t rd = start + row - p.dump_row0;
         if (rd < p.dump_rows) {
-          const bool fits = !ovf && E <= p.dump_d;
-          if (fits)
-            for (uint32_t e = 0; e < E; ++e)
-              p.dump[(uint64_t)(half ? p.dump_d - 1u - e : e) * p.dump_rows + rd] = log[e * kBM + row_in_tile];
+          // A zone entry with the row's own global id (a repeated member) sends
+          // the row to the exact fallback, as does an overflowing log.
+          bool fits = !ovf && E <= p.dump_d;
+          for (uint32_t e = 0; fits && e < E; ++e) {
+            const uint2 v = log[e * kBM + row_in_tile];
+            fits = v.y != gid_i;
+            p.dump[(uint64_t)(half ? p.dump_d - 1u - e : e) * p.dump_rows + rd] = v;
+          }
           p.dump_cnt[2u * rd + half] = fits ? (uint8_t)E : (uint8_t)0xFFu;
           if (half == 0) {
             // the sorted k smallest for the finishing kernel's ranks (32 slots, -inf padded)
@@ -660,9 +666,9 @@ struct RowWriter {
 // an entry at or below theta ranks by the number of smaller values in m,
 // equal distances take consecutive ranks in dump order, entries in the
 // margin follow ordered by distance.  The sorted zone is then verified run by
-// run and the k results written, or the row is listed for the exact fallback.
-// A zone entry with the row's own global id (a repeated member) sends the row
-// to the fallback.
+// run and the k results written, or the row is listed for the exact fallback
+// (the main kernel marks rows whose zone holds the row's own global id, a
+// repeated member, or whose log overflowed).
 __global__ void __launch_bounds__(kFinThreads) leaf_finish_kernel(const Params p) {
   extern __shared__ uint32_t fin_smem[];
   const uint32_t D = p.dump_d;
@@ -679,9 +685,6 @@ __global__ void __launch_bounds__(kFinThreads) leaf_finish_kernel(const Params p
     if (row >= cnt) continue;
     const uint64_t rd = start + row - p.dump_row0;
     if (rd >= p.dump_rows) continue;  // reported by the main kernel
-    const uint32_t lid_i = p.members[start + row];
-    if (lid_i >= p.resident_rows) continue;  // reported by the main kernel
-    const uint32_t gid_i = p.global_ids[lid_i];
     const uint32_t e0 = p.dump_cnt[2u * rd], e1 = p.dump_cnt[2u * rd + 1u];
     bool ok = e0 != 0xFFu && e1 != 0xFFu && e0 + e1 <= D;
     if (ok) {
@@ -708,7 +711,6 @@ __global__ void __launch_bounds__(kFinThreads) leaf_finish_kernel(const Params p
         zd[e * kFinThreads + tid] = __uint_as_float(v.x);
         zg[e * kFinThreads + tid] = v.y;
         n_inner += __uint_as_float(v.x) <= theta ? 1u : 0u;
-        ok &= v.y != gid_i;
       }
       uint64_t occ = 0;
       for (uint32_t e = 0; ok && e < E; ++e) {
