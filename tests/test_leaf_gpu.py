@@ -179,6 +179,16 @@ def test_leaf_tie_chains_go_through_exact_fallback(oracle):
         assert ops.leaf_last_fallback_rows() > 0
 
 
+@pytest.mark.parametrize("k", [3, 5, 12, 17, 24, 31])
+def test_leaf_k_between_register_widths(oracle, k):
+    # k below its register width (the merge of the two column halves then
+    # inserts the other half's values one pair at a time instead of the
+    # bitonic merge used when k fills the width); ragged leaves and repeated
+    # members
+    c = make_leaf_batch(oracle, [700, 129, 300, 64, 40], 256, seed=100 + k, dup=True, permute=True)
+    _assert_same(_device_run(c, k), oracle_leaf(oracle, c, k))
+
+
 def test_leaf_config2_shape_sample(oracle):
     # 16 leaves of the 4096 x 2048 x 768 k=32 benchmark workload
     from shear_b200 import ops
