@@ -468,6 +468,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             st4[q] = make_float4(dc[4 * q], dc[4 * q + 1], dc[4 * q + 2], dc[4 * q + 3]);
           if (c == c_self && g == quad) mask &= ~(0x80000000u >> lane);  // the row itself
           const uint32_t* gq = mg + g * kGroup;
+          if constexpr (KS == 32) {
+            // A tile's first group (k = 32): the bound is still +inf, so every
+            // marked column is a candidate and is logged; the sorted array is
+            // then simply the 32 sorted distances (bitonic network, about a
+            // third of the pair insertions it replaces).
+            if (c == 0 && gg == 0 && k == 32u) {
+              float v[32];
+#pragma unroll
+              for (uint32_t cc = 0; cc < 32; ++cc) {
+                const bool hit = (mask >> (31u - cc)) & 1u;
+                const float d = dc[cc] > 0.0f ? dc[cc] : 0.0f;  // reference clamp d <= 0 -> +0 (CB:8999-9001)
+                v[cc] = hit ? d : INFINITY;
+                if (hit) {
+                  log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(d), gq[cc]);
+                  ++nlog;
+                }
+              }
+#pragma unroll
+              for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+                for (int stride = size >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) {
+                    const int j = i ^ stride;
+                    if (j > i) {
+                      const float x = v[i], y = v[j];
+                      if ((i & size) == 0) {
+                        v[i] = fminf(x, y);
+                        v[j] = fmaxf(x, y);
+                      } else {
+                        v[i] = fmaxf(x, y);
+                        v[j] = fminf(x, y);
+                      }
+                    }
+                  }
+#pragma unroll
+              for (int q = 0; q < 32; ++q) sk[q] = v[31 - q];  // descending
+              if (valid) thr = __fadd_rn(fminf(sk[0], xb), kMargin);
+              mask = 0u;
+            }
+          }
           // Two candidates per step, the same number of steps in every lane;
           // the next pair's loads are issued before the current insertion.
           const uint32_t steps = (__reduce_max_sync(0xffffffffu, __popc(mask)) + 1u) >> 1;
