@@ -73,7 +73,7 @@ static_assert(kBM == kBN, "A and B slabs share the ring and the tensor map");
 
 struct Smem {
   uint8_t* ring;
-  float2* meta_sn;
+  float* meta_sn;   // [slot][column pair][s_even, s_odd, n_even, n_odd]
   uint32_t* meta_g;
   float* stash;     // [8 warps][32 lanes][kStashStride]
   uint64_t* pub;    // [2 halves][kBM] (tile tag << 32 | bound bits)
@@ -103,7 +103,7 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t ring, uint32_t log_
   Smem s;
   s.ring = p;
   p += ring * kStageBytes;
-  s.meta_sn = reinterpret_cast<float2*>(p);
+  s.meta_sn = reinterpret_cast<float*>(p);
   p += kMetaSlots * kBN * 8u;
   s.meta_g = reinterpret_cast<uint32_t*>(p);
   p += kMetaSlots * kBN * 4u;
@@ -353,7 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (uint32_t u = 0; u < kBN / 32; ++u) {
-          s.meta_sn[slot * kBN + u * 32 + lane] = sn[u];
+          // scales and norms of a column pair side by side: the epilogue
+          // reads both as register pairs for the paired f32 arithmetic
+          float* mp = s.meta_sn + slot * kBN * 2u + ((u * 32u + lane) >> 1) * 4u + (lane & 1u);
+          mp[0] = sn[u].x;
+          mp[2] = sn[u].y;
           s.meta_g[slot * kBN + u * 32 + lane] = gv[u];
         }
         mbar_arrive(&s.m_full[slot]);
@@ -406,6 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           gid_i = __ldg(p.global_ids + lid_i);
         }
       }
+      const uint64_t si2 = f2_pack(s_i, s_i), ni2 = f2_pack(n_i, n_i), m2x2 = f2_pack(-2.0f, -2.0f);
       // sk: the k smallest distances of this half, descending (sk[0] = the
       // k-th smallest); slots [k, KS) hold -inf sentinels.
       float sk[KS];
@@ -420,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t tag = (uint64_t)(tseq + 1u) << 32;
       for (uint32_t c = 0; c < nchunks; ++c, ++acc, ++seq) {
         const uint32_t mslot = seq % kMetaSlots;
-        const float4* msn = reinterpret_cast<const float4*>(s.meta_sn + mslot * kBN);
+        const float4* msn = reinterpret_cast<const float4*>(s.meta_sn + mslot * kBN * 2u);
         const uint32_t* mg = s.meta_g + mslot * kBN;
         const uint32_t buf = acc % kAccBufs, use = acc / kAccBufs;
         bool ok = true;
@@ -441,25 +446,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           // Exact reference distances; bit (31 - cc) of mask = column cc is
           // below the bound (the sign of d - thr, shifted in), four chains.
+          // Two columns per step on register pairs (paired f32 instructions,
+          // each element rounded as the scalar form).
           float dc[32];
           uint32_t mq[4] = {0u, 0u, 0u, 0u};
+          const uint64_t nthr2 = f2_pack(-thr, -thr);
 #pragma unroll
           for (uint32_t cc = 0; cc < kGroup; cc += 2) {
-            const float4 m = msn[(g * kGroup + cc) >> 1];
-            const float t0 = __fmul_rn(s_i, m.x);
-            const float t1 = __fmul_rn(s_i, m.z);
-            const float u0 = __fmul_rn(t0, __int2float_rn((int)v[cc]));
-            const float u1 = __fmul_rn(t1, __int2float_rn((int)v[cc + 1]));
-            const float nn0 = __fadd_rn(n_i, m.y);
-            const float nn1 = __fadd_rn(n_i, m.w);
+            const float4 m = msn[(g * kGroup + cc) >> 1];  // s_c, s_c+1, n_c, n_c+1
+            const uint64_t t = f2_mul(si2, f2_pack(m.x, m.y));
+            const uint64_t u = f2_mul(t, f2_pack(__int2float_rn((int)v[cc]), __int2float_rn((int)v[cc + 1])));
             // rn(nn + rn(-2*u)) == fma(-2, u, nn): -2*u is exact.
-            const float d0 = __fmaf_rn(-2.0f, u0, nn0);
-            const float d1 = __fmaf_rn(-2.0f, u1, nn1);
+            const uint64_t d = f2_fma(m2x2, u, f2_add(ni2, f2_pack(m.z, m.w)));
+            float d0, d1, e0, e1;
+            f2_unpack(d, d0, d1);
+            f2_unpack(f2_add(d, nthr2), e0, e1);  // rn(d - thr)
             dc[cc] = d0;
             dc[cc + 1] = d1;
             uint32_t& w = mq[cc >> 3];
-            w = __funnelshift_l(__float_as_uint(__fsub_rn(d0, thr)), w, 1);
-            w = __funnelshift_l(__float_as_uint(__fsub_rn(d1, thr)), w, 1);
+            w = __funnelshift_l(__float_as_uint(e0), w, 1);
+            w = __funnelshift_l(__float_as_uint(e1), w, 1);
           }
           uint32_t mask = (mq[0] << 24) | (mq[1] << 16) | (mq[2] << 8) | mq[3];
           float4* st4 = reinterpret_cast<float4*>(stash);
