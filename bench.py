@@ -347,6 +347,7 @@ def run_ours(a):
         total_s, kern_s = float(tt[0]), float(tt[1])
     per_step = total_s / a.steps
     value = world * rows / per_step
+    fb_rows = ops.leaf_last_fallback_rows(ctx)  # rows of the last step sent to the exact fallback
     pairs = a.leaves * a.leaf_rows * (a.leaf_rows - 1)
     ops_per_step = 2.0 * a.dim * a.leaf_rows * a.leaf_rows * a.leaves  # int8 MAC*2 incl. the diagonal tile
 
@@ -422,6 +423,7 @@ def run_ours(a):
         "gpu_launches": 3 * a.steps,  # column-split leaf kernel, finishing kernel, exact fallback per step
         "clocks": clk.summary(),
         "leaf_kernel_ms": kern_s * 1e3, "pairs_per_sec": world * pairs / per_step,
+        "fallback_rows_per_step": fb_rows,
         "int8_tops": achieved_tops,
     }
     print(json.dumps(line), flush=True)

@@ -20,16 +20,21 @@
 // instead of shared memory: the MMA reads A from TMEM (tcgen05.mma with an
 // A tensor-memory operand), B streams through shared memory as before.
 //
-// Per-row bound of a half: min(own k-th smallest, max(own j-th, other j-th))
-// with j = ceil(k/2): at least j + j >= k candidates of the row lie at or
-// below max(own j-th, other j-th), so both terms bound the row's k-th
-// smallest from above.  The halves publish their j-th smallest after every
-// column group (tagged with the tile, so a value of a previous tile is never
-// used).  A candidate is logged while it is within kMargin of the bound.  At
-// the end of a tile the halves exchange their sorted arrays and both merge
-// them into the row's k smallest distances (theta = the k-th); each half
-// compacts its log to [0, theta + kMargin] (its part of the zone) and writes
-// it to a per-row dump in global memory, half 0 adds the merged k smallest.
+// Per-row bound of a half: max(own j-th smallest, other j-th smallest) with
+// j = ceil(k/2): at least j + j >= k candidates of the row lie at or below
+// it, so it bounds the row's k-th smallest from above, and each half keeps
+// only its j smallest distances sorted (half the insertion work of keeping k).
+// The halves publish their j-th smallest after every column group (tagged
+// with the tile, so a value of a previous tile is never used; the other's
+// value may be older than the current group, which only loosens the bound,
+// and for the first kMeetGroups groups the two warps meet so it is not).  A
+// candidate is logged while it is within kMargin of the bound.  At the end of
+// a tile each half takes the k smallest distances of its log (every distance
+// at or below the row's k-th smallest was within the bound when it arrived),
+// the halves exchange them and both merge them into the row's k smallest
+// distances (theta = the k-th); each half compacts its log to
+// [0, theta + kMargin] (its part of the zone) and writes it to a per-row dump
+// in global memory, half 0 adds the merged k smallest.
 // leaf_finish_kernel then ranks each row's zone against those k values (as
 // leaf_sq8.cu's finish does), verifies it and writes the k results (or lists
 // the row for the exact fallback), with enough warps per SM to hide latency.
@@ -68,6 +73,7 @@ constexpr uint32_t kStashBytes = kEpiWarps * 32u * kStashStride * 4u;
 constexpr uint32_t kPubBytes = 2u * kBM * 8u;
 constexpr uint32_t kBarBytes = 512u;
 constexpr uint32_t kFinThreads = 128;
+constexpr uint32_t kMeetGroups = 8;  // groups per tile after which the two halves meet
 
 static_assert(kBM == kBN, "A and B slabs share the ring and the tensor map");
 
@@ -377,7 +383,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile uint64_t* other_pub = s.pub + (half ^ 1u) * kBM + row_in_tile;
     const uint32_t cap = p.log_cap;
     const uint32_t k = p.k;
-    const uint32_t jt = k >> 1;  // sk[jt] is the ceil(k/2)-th smallest
+    constexpr int KH = KS / 2;             // slots of the per-half sorted array
+    const uint32_t jk = k - (k >> 1);      // ceil(k/2) <= KH
     uint32_t acc = 0, seq = 0, rpos = 0, tseq = 0, pair_phase = 0, arp = 0;
     bool stop = false;
     uint32_t tile = blockIdx.x;
@@ -411,13 +418,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const uint64_t si2 = f2_pack(s_i, s_i), ni2 = f2_pack(n_i, n_i), m2x2 = f2_pack(-2.0f, -2.0f);
-      // sk: the k smallest distances of this half, descending (sk[0] = the
-      // k-th smallest); slots [k, KS) hold -inf sentinels.
-      float sk[KS];
+      // sk: the j = ceil(k/2) smallest distances of this half, descending
+      // (sk[0] = the j-th smallest); slots [j, KH) hold -inf sentinels.
+      float sk[KH];
 #pragma unroll
-      for (int q = 0; q < KS; ++q) sk[q] = (uint32_t)q < k ? INFINITY : -INFINITY;
-      float xb = INFINITY;  // max(own, other) ceil(k/2)-th smallest at the last exchange
-      float ob = INFINITY;  // the other half's ceil(k/2)-th smallest, as last published
+      for (int q = 0; q < KH; ++q) sk[q] = (uint32_t)q < jk ? INFINITY : -INFINITY;
+      float ob = INFINITY;  // the other half's j-th smallest, as last published
       float thr = valid ? INFINITY : -INFINITY;
       uint32_t nlog = 0;
       bool ovf = false;
@@ -510,8 +516,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                   }
 #pragma unroll
-              for (int q = 0; q < 32; ++q) sk[q] = v[31 - q];  // descending
-              if (valid) thr = __fadd_rn(fminf(sk[0], xb), kMargin);
+              for (int q = 0; q < KH; ++q) sk[q] = v[KH - 1 - q];  // the j smallest, descending
+              if (valid) thr = __fadd_rn(fmaxf(sk[0], ob), kMargin);
               mask = 0u;
             }
           }
@@ -549,8 +555,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (w1) log[e1 * kBM + row_in_tile] = make_uint2(__float_as_uint(d1), g1);
               nlog = e1 + (w1 ? 1u : 0u);
               ovf |= (ok0 && !w0) || (ok1 && !w1);
-              topk_insert2<KS>(sk, fminf(d0, d1), fmaxf(d0, d1));
-              if (valid) thr = __fadd_rn(fminf(sk[0], xb), kMargin);
+              topk_insert2<KH>(sk, fminf(d0, d1), fmaxf(d0, d1));
+              if (valid) thr = __fadd_rn(fmaxf(sk[0], ob), kMargin);
               h0 = nh0;
               h1 = nh1;
               a0 = na0;
@@ -559,18 +565,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               g1 = ng1;
             }
           }
-          // Exchange ceil(k/2)-th smallest distances with the other half.
-          float own_j = sk[KS / 2];  // k == KS (the usual case): a fixed slot
-          if (k != (uint32_t)KS) {
-#pragma unroll
-            for (int q = 0; q < KS; ++q)
-              if ((uint32_t)q == jt) own_j = sk[q];
+          // Publish this half's j-th smallest and take the other half's.  For
+          // the first kMeetGroups groups of a tile the two warps meet after
+          // publishing, so each bound uses the other's value of the same
+          // group while the bounds still fall fast (one a group older there
+          // lets the logs overfill); later the other's latest value is used.
+          *my_pub = tag | __float_as_uint(sk[0]);
+          if (c * 2u + gg < kMeetGroups) {
+            __threadfence_block();
+            if (!pair_meet(&s.pair[quad], pair_phase, lane, abort_flag, p)) {
+              stop = true;
+              break;
+            }
           }
-          *my_pub = tag | __float_as_uint(own_j);
           const uint64_t o = *other_pub;
           if ((o & 0xffffffff00000000ull) == tag) ob = fminf(ob, __uint_as_float((uint32_t)o));
-          xb = fmaxf(own_j, ob);
-          if (valid) thr = __fadd_rn(fminf(sk[0], xb), kMargin);
+          if (valid) thr = __fadd_rn(fmaxf(sk[0], ob), kMargin);
           __syncwarp();
         }
         if (stop) break;
@@ -598,41 +608,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         rpos += p.num_slabs * (1u + (nn + kBN - 1) / kBN);
       }
 
-      // ---- tile end: the row's k smallest distances from both sorted arrays
+      // ---- tile end: this half's k smallest logged distances (every
+      // distance of the row at or below its k-th smallest was within the bound
+      // on arrival and is logged, so the two halves' k smallest hold the
+      // row's), then both halves merged.
+      float mk[KS];
 #pragma unroll
-      for (int q = 0; q < KS; ++q) stash[q] = sk[q];
+      for (int q = 0; q < KS; ++q) mk[q] = (uint32_t)q < k ? INFINITY : -INFINITY;
+      for (uint32_t e = 0; e < nlog; e += 2u) {
+        const float x = __uint_as_float(log[e * kBM + row_in_tile].x);
+        const float y = e + 1u < nlog ? __uint_as_float(log[(e + 1u) * kBM + row_in_tile].x) : INFINITY;
+        topk_insert2<KS>(mk, fminf(x, y), fmaxf(x, y));
+      }
+#pragma unroll
+      for (int q = 0; q < KS; ++q) stash[q] = mk[q];
       if (!pair_meet(&s.pair[quad], pair_phase, lane, abort_flag, p)) {
         stop = true;
         break;
       }
       if (k == (uint32_t)KS) {
-        // sk descending, the other's reversed ascending: their element-wise
+        // mk descending, the other's reversed ascending: their element-wise
         // minimum is the KS smallest of both, a bitonic sequence; half-cleaners
         // sort it descending.
 #pragma unroll
-        for (int q = 0; q < KS; ++q) sk[q] = fminf(sk[q], ostash[KS - 1 - q]);
+        for (int q = 0; q < KS; ++q) mk[q] = fminf(mk[q], ostash[KS - 1 - q]);
 #pragma unroll
         for (int dd = KS / 2; dd >= 1; dd >>= 1)
 #pragma unroll
           for (int q = 0; q < KS; ++q)
             if ((q & dd) == 0) {
-              const float a = sk[q], b = sk[q + dd];
-              sk[q] = fmaxf(a, b);
-              sk[q + dd] = fminf(a, b);
+              const float a = mk[q], b = mk[q + dd];
+              mk[q] = fmaxf(a, b);
+              mk[q + dd] = fminf(a, b);
             }
       } else {
         for (uint32_t q = 0; q < k; q += 2) {
           const float x = ostash[q], y = q + 1u < k ? ostash[q + 1u] : INFINITY;
-          topk_insert2<KS>(sk, fminf(x, y), fmaxf(x, y));
+          topk_insert2<KS>(mk, fminf(x, y), fmaxf(x, y));
         }
       }
-      // sk: the row's k smallest, descending; sk[0] = theta
+      // mk: the row's k smallest, descending; mk[0] = theta
       if (!pair_meet(&s.pair[quad], pair_phase, lane, abort_flag, p)) {
         stop = true;
         break;
       }
       if (valid) {
-        const uint32_t E = log_compact(log, row_in_tile, nlog, __fadd_rn(sk[0], kMargin));
+        const uint32_t E = log_compact(log, row_in_tile, nlog, __fadd_rn(mk[0], kMargin));
         const uint64_t rd = start + row - p.dump_row0;
         if (rd < p.dump_rows) {
           // A zone entry with the row's own global id (a repeated member) sends
@@ -649,8 +670,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int q = 0; q < 32; q += 4)
               p.dump_m[(uint64_t)(q / 4) * p.dump_rows + rd] =
-                  make_float4(q < KS ? sk[q] : -INFINITY, q + 1 < KS ? sk[q + 1] : -INFINITY,
-                              q + 2 < KS ? sk[q + 2] : -INFINITY, q + 3 < KS ? sk[q + 3] : -INFINITY);
+                  make_float4(q < KS ? mk[q] : -INFINITY, q + 1 < KS ? mk[q + 1] : -INFINITY,
+                              q + 2 < KS ? mk[q + 2] : -INFINITY, q + 3 < KS ? mk[q + 3] : -INFINITY);
           }
         } else {
           atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
