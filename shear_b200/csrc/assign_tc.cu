@@ -8,20 +8,30 @@
 // slots as (global id, distance).  Only the dots move to the tensor cores:
 // they are exact int32 sums either way, so the results are bit-identical.
 //
-// Per work item (128 member rows of one task):
-//   * the member rows and the task's leader rows are gathered by id, one
-//     128-byte K slab at a time, with cp.async straight into the 128-byte
-//     swizzled K-major layout tcgen05.mma reads (piece j of row r at
-//     j ^ (r & 7)), eight threads per row so copies are whole 128-byte
-//     segments; two slab buffers, so the next slab's copies are in flight
-//     while the current slab's MMAs run;
-//   * one thread issues tcgen05.mma.kind::i8, M = 128 rows, N = NB leader slots
-//     (the launch's leader count rounded up to 16), K = 32, int32 accumulators
-//     in TMEM; tcgen05.commit frees each slab buffer;
-//   * warp w reads TMEM lanes 32w..32w+31 (its 32 rows' dots) with tcgen05.ld
-//     and runs the distance and the insertion per row.
-// The CTA is persistent over work items and keeps its TMEM columns; the next
-// item's metadata loads overlap the current item's copies.
+// The work is a stream of items (128 member rows of one task); the member and
+// leader rows are gathered by id, so the kernel is a pipelined gather feeding
+// tcgen05.mma.  Warp-specialised, persistent, two CTAs per SM:
+//   warps 0-3  producers: walk the items, load each item's metadata chain
+//              (work entry -> task -> member and leader ids -> norms, scales,
+//              global ids) into a metadata slot, and copy the rows one
+//              128-byte K slab at a time into a ring of shared-memory stages,
+//              already in the 128-byte swizzled K-major layout the MMA reads
+//              (piece j of row r at j ^ (r & 7)).  Thread t copies piece t & 7
+//              of rows (t >> 3) + 16u, from row pointers computed once per
+//              item; cp.async.mbarrier.arrive hands the completion of a
+//              thread's copies to the stage's barrier, so a producer never
+//              waits for its own copies and every stage of the ring can be in
+//              flight, across item boundaries;
+//   warp 8     TMEM owner and MMA issuer: tcgen05.mma.kind::i8, M = 128 rows,
+//              N = NB leader slots (the launch's leader count rounded up to 16),
+//              K = 32, into one of two accumulator buffers; tcgen05.commit
+//              frees each stage and, after an item's last slab, hands the
+//              buffer to the epilogue;
+//   warps 4-7  epilogue: warp 4 + q reads TMEM lanes 32q..32q+31 (its rows'
+//              dots) and runs the distance and the insertion per row, while
+//              the MMA fills the other buffer.
+// Every wait is bounded; a timed-out or aborted wait raises the CTA's abort
+// flag and the error word, and all roles then leave their loops.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -30,18 +40,31 @@ namespace assign {
 namespace tc {
 
 constexpr uint32_t kRowsTc = 128;  // member rows per work item (MMA M = TMEM lanes)
-constexpr uint32_t kThreadsTc = 128;
 constexpr uint32_t kSlabTc = 128;  // K bytes per slab (one 128-byte swizzle atom)
 constexpr uint32_t kMmaKTc = 32;
 constexpr uint32_t kASlabTc = kRowsTc * kSlabTc;  // 16 KiB
-constexpr uint32_t kCtasPerSm = 5;
 constexpr uint32_t kMaxNB = 128;  // leader slots per MMA (task leader counts above use the SIMT kernel)
+constexpr uint32_t kProdThreads = 128;  // warps 0-3
+constexpr uint32_t kAccBufs = 4;        // accumulator buffers = metadata slots = epilogue groups
+constexpr uint32_t kEpiWarp0 = 4;       // warps 4-19: epilogue group g = warps 4 + 4g .. 7 + 4g
+constexpr uint32_t kMmaWarp = 4 + 4 * kAccBufs;
+constexpr uint32_t kThreadsTc = (kMmaWarp + 1) * 32;
+constexpr uint32_t kSmemPerCta = 232448u;  // one CTA per SM
 
-__host__ __device__ constexpr uint32_t tmem_cols_for(uint32_t nb) { return nb <= 32 ? 32 : (nb <= 64 ? 64 : 128); }
-
-__host__ __device__ constexpr uint32_t smem_bytes_tc(uint32_t nb) {
-  return 1024u + 2u * (kASlabTc + nb * kSlabTc) + 256u;
-}
+template <uint32_t NB>
+struct Geom {
+  static constexpr uint32_t kStage = kASlabTc + NB * kSlabTc;  // A slab then B slab, multiples of 1 KiB
+  // metadata slot: per row point/norm/scale, per leader slot id/gid/norm/scale, item fields
+  static constexpr uint32_t kMeta = kRowsTc * 12u + NB * 16u + 32u;
+  static constexpr uint32_t kMetaSlots = kAccBufs;
+  static constexpr uint32_t kBars = 256u;
+  static constexpr uint32_t kFixed = 1024u + kMetaSlots * kMeta + kBars;
+  static constexpr uint32_t kStages = (kSmemPerCta - kFixed) / kStage < 8u ? (kSmemPerCta - kFixed) / kStage : 8u;
+  static constexpr uint32_t kSmem = 1024u + kStages * kStage + kMetaSlots * kMeta + kBars;
+  static constexpr uint32_t kTmemCols = kAccBufs * NB <= 64u ? 64u : (kAccBufs * NB <= 128u ? 128u : (kAccBufs * NB <= 256u ? 256u : 512u));
+  static_assert(kStages >= 3, "ring too shallow");
+  static_assert(kSmem <= kSmemPerCta, "shared memory");
+};
 
 __device__ __forceinline__ uint64_t hash64(uint64_t v) {
   v ^= v >> 30;
@@ -55,9 +78,17 @@ __device__ __forceinline__ uint64_t tie_key(uint32_t point, uint32_t leader) {
   return hash64((((uint64_t)point) << 32) ^ (uint64_t)leader ^ 0x9e3779b97f4a7c15ull);
 }
 
-// CB:6524-6578 with slots = 4 (as assign.cu's insert4).
-__device__ __forceinline__ void insert4(float d, uint32_t point, uint32_t leader, uint32_t slot, float (&bd)[4],
-                                        uint32_t (&bs)[4], uint32_t (&bl)[4]) {
+struct Top4 {
+  float d[4];
+  uint32_t s[4], l[4];
+};
+
+// CB:6524-6578 with slots = 4 (as assign.cu's insert4).  Out of line: it is
+// only reached for a candidate within the 2e-5 tie window of a held slot.
+__device__ __noinline__ Top4 insert4_ties(Top4 t, float d, uint32_t point, uint32_t leader, uint32_t slot) {
+  float (&bd)[4] = t.d;
+  uint32_t (&bs)[4] = t.s;
+  uint32_t (&bl)[4] = t.l;
   bool better = d < bd[3];
   uint64_t ck = 0;
   bool ck_ready = false;
@@ -67,7 +98,7 @@ __device__ __forceinline__ void insert4(float d, uint32_t point, uint32_t leader
     const uint64_t fk = tie_key(point, bl[3]);
     better = ck < fk || (ck == fk && leader < bl[3]);
   }
-  if (!better) return;
+  if (!better) return t;
   int pos = 3;
 #pragma unroll
   for (int j = 3; j >= 1; --j) {
@@ -94,17 +125,60 @@ __device__ __forceinline__ void insert4(float d, uint32_t point, uint32_t leader
       bs[j] = slot;
       bl[j] = leader;
     }
+  return t;
 }
+
+// The same insertion.  A candidate more than 2e-5 from every held slot
+// compares by distance alone against each of them (no tie key is consulted),
+// so it is placed by a short branch-free network; otherwise the full rule runs.
+__device__ __forceinline__ void insert4(float d, uint32_t point, uint32_t leader, uint32_t slot, float (&bd)[4],
+                                        uint32_t (&bs)[4], uint32_t (&bl)[4]) {
+  const bool near = fabsf(__fsub_rn(d, bd[0])) <= 2.0e-5f || fabsf(__fsub_rn(d, bd[1])) <= 2.0e-5f ||
+                    fabsf(__fsub_rn(d, bd[2])) <= 2.0e-5f || fabsf(__fsub_rn(d, bd[3])) <= 2.0e-5f;
+  if (near) {
+    Top4 t;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      t.d[k] = bd[k];
+      t.s[k] = bs[k];
+      t.l[k] = bl[k];
+    }
+    t = insert4_ties(t, d, point, leader, slot);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      bd[k] = t.d[k];
+      bs[k] = t.s[k];
+      bl[k] = t.l[k];
+    }
+    return;
+  }
+  if (!(d < bd[3])) return;
+  const bool c0 = d < bd[0], c1 = d < bd[1], c2 = d < bd[2];
+  bd[3] = c2 ? bd[2] : d;
+  bs[3] = c2 ? bs[2] : slot;
+  bl[3] = c2 ? bl[2] : leader;
+  bd[2] = c1 ? bd[1] : (c2 ? d : bd[2]);
+  bs[2] = c1 ? bs[1] : (c2 ? slot : bs[2]);
+  bl[2] = c1 ? bl[1] : (c2 ? leader : bl[2]);
+  bd[1] = c0 ? bd[0] : (c1 ? d : bd[1]);
+  bs[1] = c0 ? bs[0] : (c1 ? slot : bs[1]);
+  bl[1] = c0 ? bl[0] : (c1 ? leader : bl[1]);
+  bd[0] = c0 ? d : bd[0];
+  bs[0] = c0 ? slot : bs[0];
+  bl[0] = c0 ? leader : bl[0];
+}
+
 
 __device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Arrive on `bar` once every cp.async this thread issued before has landed
+// (the arrival is part of the barrier's expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // 32 lanes x 16 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -116,285 +190,314 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
-// Per-thread metadata of one work item: its task, the thread's member row and
-// (thread t < NB) leader slot t.
-struct ItemMeta {
-  uint32_t task, r, moff, mcnt, loff, nl, rh;
-  uint32_t point, lid, lg;
-  bool valid;
-  float n_p, s_p, ln, ls;
+template <uint32_t NB>
+struct MetaSlot {
+  uint32_t pt[kRowsTc];  // member row of each tile row (0xffffffff: none)
+  float np[kRowsTc];
+  float sp[kRowsTc];
+  uint32_t lid[NB];      // leader row of each slot (0xffffffff: none)
+  uint32_t lg[NB];
+  float ln[NB];
+  float ls[NB];
+  uint32_t task, rh, nl, r0;
+  uint64_t tout;
+  uint32_t pad[2];
 };
 
-// One level of the item's load chain (steps 0..3 in order).
+// One item's producer-side metadata: the task, this thread's metadata row and
+// leader slot, and the member and leader rows it copies.  Loaded as a chain of
+// dependent loads (steps 0..3), so the next item's chain is walked one step
+// per slab while the current item's slabs are issued.
 template <uint32_t NB>
-__device__ __forceinline__ void meta_step(const Params& p, uint32_t item, uint32_t step, ItemMeta& m, uint32_t tid) {
+struct ProdMeta {
+  uint32_t task, r0, moff, mcnt, loff, nl, rh;
+  uint64_t tout;
+  uint32_t pt, lid, lg;
+  float np, sp, ln, ls;
+  uint32_t crow[8];       // member rows (t >> 3) + 16u of the item (0xffffffff: none)
+  uint32_t lrow[NB / 16];  // leader rows (t >> 3) + 16v of the task
+};
+
+template <uint32_t NB>
+__device__ __forceinline__ void prod_step(const Params& p, uint32_t item, uint32_t step, ProdMeta<NB>& m,
+                                          uint32_t t) {
+  constexpr uint32_t kNone = 0xffffffffu;
+  const uint32_t row0 = t >> 3;
   if (step == 0) {
     const uint2 w = p.work[item];
     m.task = w.x;
-    m.r = w.y + tid;
+    m.r0 = w.y;
   } else if (step == 1) {
     m.moff = p.t_moff[m.task];
     m.mcnt = p.t_mcnt[m.task];
     m.loff = p.t_loff[m.task];
     m.nl = p.t_lcnt[m.task];
     m.rh = p.t_rh[m.task];
+    m.tout = p.t_out[m.task];
   } else if (step == 2) {
-    m.valid = m.r < m.mcnt;
-    m.point = m.valid ? p.members[m.moff + m.r] : 0u;
-    m.lid = (tid < NB && tid < m.nl) ? p.leaders[m.loff + tid] : 0xffffffffu;
+    const uint32_t r = m.r0 + t;
+    m.pt = r < m.mcnt ? p.members[m.moff + r] : kNone;
+    m.lid = (t < NB && t < m.nl) ? p.leaders[m.loff + t] : kNone;
+#pragma unroll
+    for (uint32_t u = 0; u < 8; ++u) {
+      const uint32_t rr = m.r0 + row0 + 16u * u;
+      m.crow[u] = rr < m.mcnt ? p.members[m.moff + rr] : kNone;
+    }
+#pragma unroll
+    for (uint32_t v = 0; v < NB / 16; ++v) {
+      const uint32_t lr = row0 + 16u * v;
+      m.lrow[v] = lr < m.nl ? p.leaders[m.loff + lr] : kNone;
+    }
   } else {
-    if (m.valid && m.point >= p.resident_rows) {
+    // Ids at or past resident_rows are reported (each row and leader slot by
+    // the thread that owns its metadata) and dropped.
+    if (m.pt != kNone && m.pt >= p.resident_rows) {
       atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
-      m.valid = false;
-      m.point = 0u;
+      m.pt = kNone;
     }
-    m.n_p = m.valid ? p.sq8_norms[m.point] : 0.f;
-    m.s_p = m.valid ? p.scales[m.point] : 0.f;
-    m.ln = 0.f;
-    m.ls = 0.f;
-    m.lg = 0u;
-    if (m.lid != 0xffffffffu) {
-      if (m.lid >= p.resident_rows) {
-        atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
-        m.lid = 0xffffffffu;
-      } else {
-        m.ln = p.sq8_norms[m.lid];
-        m.ls = p.scales[m.lid];
-        m.lg = p.global_ids[m.lid];
-      }
+    if (m.lid != kNone && m.lid >= p.resident_rows) {
+      atomicOr(p.err_word, TESSA_DEVERR_BAD_ROW);
+      m.lid = kNone;
     }
+#pragma unroll
+    for (uint32_t u = 0; u < 8; ++u)
+      if (m.crow[u] >= p.resident_rows) m.crow[u] = kNone;
+#pragma unroll
+    for (uint32_t v = 0; v < NB / 16; ++v)
+      if (m.lrow[v] >= p.resident_rows) m.lrow[v] = kNone;
+    m.np = m.pt != kNone ? p.sq8_norms[m.pt] : 0.f;
+    m.sp = m.pt != kNone ? p.scales[m.pt] : 0.f;
+    m.ln = m.lid != kNone ? p.sq8_norms[m.lid] : 0.f;
+    m.ls = m.lid != kNone ? p.scales[m.lid] : 0.f;
+    m.lg = m.lid != kNone ? p.global_ids[m.lid] : 0u;
   }
 }
 
 template <uint32_t NB>
-__global__ void __launch_bounds__(kThreadsTc) assign_tc_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p) {
+  using G = Geom<NB>;
+  static_assert(sizeof(MetaSlot<NB>) == G::kMeta, "metadata slot size");
+  constexpr uint32_t S = G::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
-  uint8_t* a_buf = base;                              // [2][128 rows][128 B]
-  uint8_t* b_buf = base + 2u * kASlabTc;              // [2][NB rows][128 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(b_buf + 2u * NB * kSlabTc);
-  uint64_t* mma_bar = bars;                           // [2] slab buffer b's MMAs done
-  uint64_t* done_bar = bars + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  uint8_t* ring = base;
+  MetaSlot<NB>* meta = reinterpret_cast<MetaSlot<NB>*>(ring + S * G::kStage);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(meta) + G::kMetaSlots * G::kMeta);
+  uint64_t* full = bars;                 // [S] stage copies landed (128 producer arrivals)
+  uint64_t* empty = bars + 8;            // [S] stage read by its MMAs
+  uint64_t* acc_full = bars + 16;        // [kAccBufs] buffer's item complete
+  uint64_t* acc_empty = bars + 20;       // [kAccBufs] buffer and metadata slot released by the epilogue
+  uint64_t* meta_full = bars + 24;       // [kAccBufs] metadata slot written
+  uint64_t* done_bar = bars + 28;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 29);
   uint32_t* abort_word = tmem_slot + 1;
-  // leader slots of the current and the next item (double-buffered)
-  __shared__ uint32_t l_ids[2][NB];
-  __shared__ float l_norm[2][NB];
-  __shared__ float l_scale[2][NB];
-  __shared__ uint32_t l_gid[2][NB];
-  __shared__ uint32_t m_pt[2][kRowsTc];  // member row of each tile row (0xffffffff: none)
-
-  const uint32_t tid = threadIdx.x, warp = tid >> 5;
-  constexpr uint32_t kCols = tmem_cols_for(NB);
   volatile uint32_t* abort_flag = abort_word;
+
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
   if (tid == 0) {
-    mbar_init(&mma_bar[0], 1);
-    mbar_init(&mma_bar[1], 1);
+    for (uint32_t i = 0; i < S; ++i) {
+      mbar_init(&full[i], kProdThreads);
+      mbar_init(&empty[i], 1);
+    }
+    for (uint32_t i = 0; i < kAccBufs; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+      mbar_init(&meta_full[i], kProdThreads);
+    }
     mbar_init(done_bar, 1);
     *abort_word = 0u;
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, kCols);
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, G::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t idesc = idesc_i8(kRowsTc, NB);
   const uint32_t pd = p.padded_dim;
   const uint32_t nslab = (pd + kSlabTc - 1) / kSlabTc;
-  const uint32_t a_addr0 = smem_u32(a_buf), b_addr0 = smem_u32(b_buf);
-  uint32_t ph0 = 0, ph1 = 0;  // next phase parity of mma_bar[0], mma_bar[1]
-  bool stop = false;
+  const uint32_t ring0 = smem_u32(ring);
 
-  // Item metadata is a chain of dependent loads (work entry -> task table ->
-  // member and leader ids -> norms and scales); the next item's chain is
-  // walked one level per slab, just before the slab waits for its copies.
-  ItemMeta cur, nxt;
-  uint32_t par = 0;  // leader-slot buffer of the current item
-  auto put_leaders = [&](const ItemMeta& m, uint32_t q) {
-    m_pt[q][tid] = m.valid ? m.point : 0xffffffffu;
-    if (tid < NB) {
-      l_ids[q][tid] = m.lid;
-      l_norm[q][tid] = m.ln;
-      l_scale[q][tid] = m.ls;
-      l_gid[q][tid] = m.lg;
-    }
-  };
-  // Slab s of the member rows and leader rows of slot buffer q into slab
-  // buffer b.  Eight consecutive threads copy one row's 128 contiguous bytes,
-  // so a warp's copy instruction covers four whole rows.
-  auto stage = [&](uint32_t q, uint32_t s, uint32_t b) {
-    const uint32_t k0 = s * kSlabTc;
-#pragma unroll
-    for (uint32_t i = tid; i < kRowsTc * (kSlabTc / 16); i += kThreadsTc) {
-      const uint32_t row = i / (kSlabTc / 16), j = i % (kSlabTc / 16);
-      const uint32_t pt = m_pt[q][row];
-      const uint32_t off = k0 + j * 16u;
-      const uint32_t n = (pt != 0xffffffffu && off < pd) ? 16u : 0u;
-      cp_async16(a_addr0 + b * kASlabTc + row * kSlabTc + ((j ^ (row & 7u)) << 4),
-                 p.codes + (n ? (uint64_t)pt * pd + off : 0u), n);
-    }
-    const uint32_t bdst = b_addr0 + b * NB * kSlabTc;
-    for (uint32_t i = tid; i < NB * (kSlabTc / 16); i += kThreadsTc) {
-      const uint32_t l = i / (kSlabTc / 16), j = i % (kSlabTc / 16);
-      const uint32_t lid = l_ids[q][l];
-      const uint32_t off = k0 + j * 16u;
-      const uint32_t n = (lid != 0xffffffffu && off < pd) ? 16u : 0u;
-      cp_async16(bdst + l * kSlabTc + ((j ^ (l & 7u)) << 4), p.codes + (n ? (uint64_t)lid * pd + off : 0u), n);
-    }
-    cp_async_commit();
-  };
-  auto wait_buf = [&](uint32_t b) -> bool {
+  if (warp < kEpiWarp0) {
+    // ------------------------------------------------------------ producers
+    const uint32_t t = tid;
+    const uint32_t piece = t & 7u, row0 = t >> 3;
+    const uint32_t swz = (piece ^ (row0 & 7u)) << 4;  // row & 7 == row0 & 7 for rows row0 + 16u
+    uint32_t gs = 0;  // slabs issued by this thread
     bool ok = true;
-    if (b == 0) {
-      ok = mbar_wait(&mma_bar[0], ph0, abort_flag, p.err_word, p.timeout_ns);
-      ph0 ^= 1u;
-    } else {
-      ok = mbar_wait(&mma_bar[1], ph1, abort_flag, p.err_word, p.timeout_ns);
-      ph1 ^= 1u;
-    }
-    return ok;
-  };
-
-  uint32_t item = blockIdx.x;
-  if (item < p.num_work) {
-    for (uint32_t step = 0; step < 4; ++step) meta_step<NB>(p, item, step, cur, tid);
-    put_leaders(cur, 0);
-    __syncthreads();
-    stage(0, 0, 0);
-  }
-  for (; item < p.num_work && !stop; item += gridDim.x) {
-    const uint32_t next = item + gridDim.x;
-    const bool has_next = next < p.num_work;
-    const uint32_t task = cur.task, nl = cur.nl, rh = cur.rh, r = cur.r, point = cur.point;
-    const bool valid = cur.valid;
-    const float n_p = cur.n_p, s_p = cur.s_p;
-
-    // Slab 0 is already in flight (issued before the previous item's epilogue).
-    bool pend0 = false, pend1 = false;  // buffer b has MMAs not yet waited for
-    for (uint32_t s = 0; s < nslab; ++s) {
-      const uint32_t b = s & 1u;
-      if (s + 1 < nslab) {
-        // the buffer of slab s + 1 was read by slab s - 1's MMAs
-        if (b == 0 && pend1) {
-          stop |= !wait_buf(1);
-          pend1 = false;
-        } else if (b == 1 && pend0) {
-          stop |= !wait_buf(0);
-          pend0 = false;
+    ProdMeta<NB> cur, nxt;
+    if (blockIdx.x < p.num_work)
+      for (uint32_t step = 0; step < 4; ++step) prod_step<NB>(p, blockIdx.x, step, cur, t);
+    for (uint32_t item = blockIdx.x, li = 0; ok && item < p.num_work; item += gridDim.x, ++li) {
+      const uint32_t a = li % kAccBufs;
+      const uint32_t next = item + gridDim.x;
+      const bool has_next = next < p.num_work;
+      // the metadata slot is free once the epilogue released item li - kAccBufs
+      if (!mbar_wait(&acc_empty[a], ((li / kAccBufs) & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      MetaSlot<NB>& m = meta[a];
+      m.pt[t] = cur.pt;
+      m.np[t] = cur.np;
+      m.sp[t] = cur.sp;
+      if (t < NB) {
+        m.lid[t] = cur.lid;
+        m.lg[t] = cur.lg;
+        m.ln[t] = cur.ln;
+        m.ls[t] = cur.ls;
+      }
+      if (t == 0) {
+        m.task = cur.task;
+        m.rh = cur.rh;
+        m.nl = cur.nl;
+        m.r0 = cur.r0;
+        m.tout = cur.tout;
+      }
+      mbar_arrive(&meta_full[a]);
+      for (uint32_t sl = 0; sl < nslab; ++sl) {
+        if (has_next && sl < 4) prod_step<NB>(p, next, sl, nxt, t);
+        const uint32_t st = gs % S;
+        if (!mbar_wait(&empty[st], ((gs / S) & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns)) {
+          ok = false;
+          break;
         }
-        stage(par, s + 1, b ^ 1u);
-        if (has_next && s < 4) meta_step<NB>(p, next, s, nxt, tid);
-        cp_async_wait<1>();
-      } else {
-        if (has_next && s < 4) meta_step<NB>(p, next, s, nxt, tid);
-        cp_async_wait<0>();
-      }
-      fence_proxy_async_smem();  // the copies were generic-proxy writes; the MMA reads through the async proxy
-      __syncthreads();
-      if (tid == 0 && !stop) {
-        tc_fence_after();
-        const uint32_t aa = a_addr0 + b * kASlabTc, ba = b_addr0 + b * NB * kSlabTc;
+        const uint32_t off = sl * kSlabTc + piece * 16u;
+        const uint32_t n = off < pd ? 16u : 0u;
+        const uint32_t adst = ring0 + st * G::kStage + row0 * kSlabTc + swz;
 #pragma unroll
-        for (uint32_t kk = 0; kk < kSlabTc / kMmaKTc; ++kk)
-          mma_i8_ss(tmem_base, smem_desc_sw128(aa + kk * kMmaKTc), smem_desc_sw128(ba + kk * kMmaKTc), idesc,
-                    (s | kk) != 0u ? 1u : 0u);
-        mma_commit(&mma_bar[b]);
-      }
-      if (b == 0)
-        pend0 = true;
-      else
-        pend1 = true;
-    }
-    if (has_next)
-      for (uint32_t step = nslab; step < 4; ++step) meta_step<NB>(p, next, step, nxt, tid);
-    // both buffers' last commits (the later one covers every MMA of the item)
-    if (pend0) stop |= !wait_buf(0);
-    if (pend1) stop |= !wait_buf(1);
-    stop = __syncthreads_or(stop ? 1 : 0) != 0;
-    if (stop) break;
-    // Both slab buffers are free: the next item's leader slots and first slab
-    // go out now, so their copies overlap this item's epilogue.
-    if (has_next) {
-      put_leaders(nxt, par ^ 1u);
-      __syncthreads();
-      stage(par ^ 1u, 0, 0);
-    }
-    tc_fence_after();
-
-    float bd[4];
-    uint32_t bs[4], bl[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      bd[j] = 3.402823466e+38F;
-      bs[j] = 0xffffffffu;
-      bl[j] = 0xffffffffu;
-    }
-#pragma unroll 1
-    for (uint32_t c0 = 0; c0 < NB; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld_32x32b_x16(tmem_base + ((warp * 32u) << 16) + c0, v);
-      tmem_ld_wait();
-      if (valid) {
-#pragma unroll
-        for (uint32_t j = 0; j < 16; ++j) {
-          const uint32_t l = c0 + j;
-          if (l >= nl) break;
-          const uint32_t lid = l_ids[par][l];
-          if (lid == 0xffffffffu) continue;
-          const float nn = __fadd_rn(n_p, l_norm[par][l]);
-          const float t = __fmul_rn(__fmul_rn(2.0f, s_p), l_scale[par][l]);
-          const float df = __int2float_rn((int)v[j]);
-          float d = p.fused ? __fmaf_rn(-t, df, nn) : __fsub_rn(nn, __fmul_rn(t, df));
-          if (d <= 0.0f) d = 0.0f;
-          insert4(d, point, lid, l, bd, bs, bl);
+        for (uint32_t u = 0; u < 8; ++u) {
+          const uint32_t nu = cur.crow[u] != 0xffffffffu ? n : 0u;
+          cp_async16(adst + u * 16u * kSlabTc, nu ? p.codes + (uint64_t)cur.crow[u] * pd + off : p.codes, nu);
         }
+        const uint32_t bdst = ring0 + st * G::kStage + kASlabTc + row0 * kSlabTc + swz;
+#pragma unroll
+        for (uint32_t v = 0; v < NB / 16u; ++v) {
+          const uint32_t nv = cur.lrow[v] != 0xffffffffu ? n : 0u;
+          cp_async16(bdst + v * 16u * kSlabTc, nv ? p.codes + (uint64_t)cur.lrow[v] * pd + off : p.codes, nv);
+        }
+        cp_async_mbar_arrive(&full[st]);
+        ++gs;
       }
+      if (has_next)
+        for (uint32_t step = nslab; step < 4; ++step) prod_step<NB>(p, next, step, nxt, t);
+      cur = nxt;
     }
-    if (valid) {
-      const uint64_t out = p.t_out[task] + (uint64_t)r * rh;
+    cp_async_wait_all();  // nothing in flight when the CTA leaves
+  } else if (warp < kMmaWarp) {
+    // ------------------------------------------------------------ epilogue
+    // group a takes items a, a + kAccBufs, ... of this CTA (accumulator buffer
+    // and metadata slot a); warp 4 + 4a + q reads TMEM lane quadrant q.
+    const uint32_t a = (warp - kEpiWarp0) >> 2, q = warp & 3u;
+    const uint32_t row = q * 32u + lane;
+    for (uint32_t item = blockIdx.x + a * gridDim.x, li = a; item < p.num_work;
+         item += kAccBufs * gridDim.x, li += kAccBufs) {
+      const uint32_t ph = (li / kAccBufs) & 1u;
+      bool ok = true;
+      if (lane == 0)
+        ok = mbar_wait(&meta_full[a], ph, abort_flag, p.err_word, p.timeout_ns) &&
+             mbar_wait(&acc_full[a], ph, abort_flag, p.err_word, p.timeout_ns);
+      if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0u) break;
+      tc_fence_after();
+      const MetaSlot<NB>& m = meta[a];
+      const uint32_t point = m.pt[row], nl = m.nl, rh = m.rh;
+      const bool valid = point != 0xffffffffu;
+      const float n_p = m.np[row], s_p = m.sp[row];
+      float bd[4];
+      uint32_t bs[4], bl[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if ((uint32_t)j >= rh) break;
-        if (bs[j] >= nl) {
-          atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
-          continue;
+        bd[j] = 3.402823466e+38F;
+        bs[j] = 0xffffffffu;
+        bl[j] = 0xffffffffu;
+      }
+#pragma unroll 1
+      for (uint32_t c0 = 0; c0 < NB; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(tmem_base + ((q * 32u) << 16) + a * NB + c0, v);
+        tmem_ld_wait();
+        if (valid) {
+#pragma unroll
+          for (uint32_t j = 0; j < 16; ++j) {
+            const uint32_t l = c0 + j;
+            const uint32_t lid = l < nl ? m.lid[l] : 0xffffffffu;
+            const float nn = __fadd_rn(n_p, m.ln[l]);
+            const float tt = __fmul_rn(__fmul_rn(2.0f, s_p), m.ls[l]);
+            const float df = __int2float_rn((int)v[j]);
+            float d = p.fused ? __fmaf_rn(-tt, df, nn) : __fsub_rn(nn, __fmul_rn(tt, df));
+            if (d <= 0.0f) d = 0.0f;
+            if (lid != 0xffffffffu) insert4(d, point, lid, l, bd, bs, bl);
+          }
         }
-        p.out_ids[out + j] = l_gid[par][bs[j]];
-        p.out_dists[out + j] = bd[j];
+      }
+      if (valid) {
+        const uint64_t out = m.tout + (uint64_t)(m.r0 + row) * rh;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if ((uint32_t)j >= rh) break;
+          if (bs[j] >= nl) {
+            atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
+            continue;
+          }
+          p.out_ids[out + j] = m.lg[bs[j]];
+          p.out_dists[out + j] = bd[j];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  } else if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = idesc_i8(kRowsTc, NB);
+    uint32_t gs = 0;
+    bool ok = true;
+    for (uint32_t item = blockIdx.x, li = 0; ok && item < p.num_work; item += gridDim.x, ++li) {
+      const uint32_t a = li % kAccBufs;
+      if (!mbar_wait(&acc_empty[a], ((li / kAccBufs) & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns)) break;
+      tc_fence_after();
+      for (uint32_t sl = 0; sl < nslab; ++sl, ++gs) {
+        const uint32_t st = gs % S;
+        if (!mbar_wait(&full[st], (gs / S) & 1u, abort_flag, p.err_word, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        // the stage's copies have landed: the barrier completes only after
+        // every producer's cp.async writes are done
+        tc_fence_after();
+        const uint32_t aa = ring0 + st * G::kStage, ba = aa + kASlabTc;
+#pragma unroll
+        for (uint32_t kk = 0; kk < kSlabTc / kMmaKTc; ++kk)
+          mma_i8_ss(tmem_base + a * NB, smem_desc_sw128(aa + kk * kMmaKTc), smem_desc_sw128(ba + kk * kMmaKTc),
+                    idesc, (sl | kk) != 0u ? 1u : 0u);
+        mma_commit(&empty[st]);
+        if (sl + 1 == nslab) mma_commit(&acc_full[a]);
       }
     }
-    tc_fence_before();
-    __syncthreads();  // all TMEM reads and slot reads done before the next item's MMAs and slot writes
-    cur = nxt;
-    par ^= 1u;
-  }
-
-  cp_async_wait<0>();  // no copy in flight past this point (an aborted item may have left some)
-  // Every issued MMA must have landed before TMEM is released.
-  if (tid == 0) {
+    // every issued MMA has landed before TMEM is released
     mma_commit(done_bar);
     uint32_t dummy_abort = 0u;
     mbar_wait(done_bar, 0u, &dummy_abort, p.err_word, p.timeout_ns);
   }
+
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kCols);
+    tmem_dealloc(tmem_base, G::kTmemCols);
   }
 }
 
 template <uint32_t NB>
 static int launch_nb(const Params& prm, int sm_count, cudaStream_t stream) {
-  const uint32_t smem = smem_bytes_tc(NB);
+  const uint32_t smem = Geom<NB>::kSmem;
   if (cudaFuncSetAttribute(assign_tc_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return TESSA_ERR_CUDA;
-  const uint32_t cap = (uint32_t)sm_count * kCtasPerSm;
+  const uint32_t cap = (uint32_t)sm_count;  // one CTA per SM
   const uint32_t grid = prm.num_work < cap ? prm.num_work : cap;
   assign_tc_kernel<NB><<<grid, kThreadsTc, smem, stream>>>(prm);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;

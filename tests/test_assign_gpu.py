@@ -60,3 +60,45 @@ def test_assignment_fp32_and_sq8_match_oracle(oracle, dim):
     same = ops.as_u32(ids) == ui
     assert same.mean() > 0.99
     assert np.allclose(d.cpu().numpy()[same], ud[same], rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("leaders,dim", [(16, 768), (16, 128), (32, 768), (60, 256), (128, 784)])
+def test_sq8_assignment_many_items_per_cta(oracle, leaders, dim):
+    """Enough 128-row work items that every CTA of the persistent tensor-core
+    kernel takes several (ring wrap-around, both accumulator buffers, slabs
+    pending across item boundaries), with ragged member counts, one leader
+    width per launch (16, 32, 64 and 128 leader slots) and a K tail
+    (784 = 6 slabs + 16 bytes)."""
+    import torch
+    from shear_b200 import ops
+    from shear_b200._capi import ASSIGN_SQ8
+    rng = np.random.default_rng(1000 + leaders + dim)
+    rows = 6000
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    codes, scales, qn = oracle.quantize_sq8(x)
+    gids = rng.permutation(10 * rows)[:rows].astype(np.uint32)
+    ntasks = 420
+    moff, mcnt, loff, lcnt, rh, out = [], [], [], [], [], []
+    members, lead = [], []
+    o = 0
+    for t in range(ntasks):
+        m = int(rng.integers(1, 400))
+        r = int(rng.integers(1, 5))
+        moff.append(len(members)); mcnt.append(m)
+        loff.append(len(lead)); lcnt.append(leaders)
+        rh.append(r); out.append(o)
+        members += rng.integers(0, rows, m).tolist()
+        lead += rng.choice(rows, leaders, replace=False).tolist()
+        o += m * r
+    members = np.array(members, np.uint32)
+    lead = np.array(lead, np.uint32)
+    out = np.array(out, np.uint64)
+    dv = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    ids, d = ops.assign(ASSIGN_SQ8, codes=dv(codes), scales=dv(scales), sq8_norms=dv(qn),
+                        global_ids=dv(gids.view(np.int32)), members=dv(members.view(np.int32)),
+                        leaders=dv(lead.view(np.int32)), task_member_offsets=moff, task_member_counts=mcnt,
+                        task_leader_offsets=loff, task_leader_counts=lcnt, task_rh=rh, task_output_offsets=out,
+                        output_len=o)
+    wi, wd = oracle.assign(3, x, qn, codes, scales, gids, members, lead, moff, mcnt, loff, lcnt, rh, out, o)
+    assert np.array_equal(ops.as_u32(ids), wi)
+    assert np.array_equal(d.cpu().numpy().view(np.uint32), wd.view(np.uint32))
