@@ -612,6 +612,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // distance of the row at or below its k-th smallest was within the bound
       // on arrival and is logged, so the two halves' k smallest hold the
       // row's), then both halves merged.
+      // The log first drops what lies above the final bound (at or above the
+      // row's k-th smallest plus the margin), so fewer entries are inserted.
+      nlog = log_compact(log, row_in_tile, nlog, thr);
       float mk[KS];
 #pragma unroll
       for (int q = 0; q < KS; ++q) mk[q] = (uint32_t)q < k ? INFINITY : -INFINITY;

@@ -102,3 +102,53 @@ def test_sq8_assignment_many_items_per_cta(oracle, leaders, dim):
     wi, wd = oracle.assign(3, x, qn, codes, scales, gids, members, lead, moff, mcnt, loff, lcnt, rh, out, o)
     assert np.array_equal(ops.as_u32(ids), wi)
     assert np.array_equal(d.cpu().numpy().view(np.uint32), wd.view(np.uint32))
+
+
+@pytest.mark.parametrize("leaders", [16, 60])
+def test_sq8_assignment_exact_leader_ties(oracle, leaders):
+    """Every row has an identical twin and the tasks' leaders include both
+    twins, so many candidates tie exactly (and within 2e-5) with a held slot:
+    the insertion must take the reference's hash-tie rule (CB:6524-6578) for
+    those and the plain distance order elsewhere."""
+    import torch
+    from shear_b200 import ops
+    from shear_b200._capi import ASSIGN_SQ8
+    rng = np.random.default_rng(77 + leaders)
+    rows, dim = 4000, 128
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    x[1::2] = x[0::2]
+    codes, scales, qn = oracle.quantize_sq8(x)
+    gids = rng.permutation(10 * rows)[:rows].astype(np.uint32)
+    ntasks = 300
+    moff, mcnt, loff, lcnt, rh, out = [], [], [], [], [], []
+    members, lead = [], []
+    o = 0
+    for t in range(ntasks):
+        m = int(rng.integers(1, 300))
+        moff.append(len(members)); mcnt.append(m)
+        loff.append(len(lead)); lcnt.append(leaders)
+        r = 4
+        rh.append(r); out.append(o)
+        members += rng.integers(0, rows, m).tolist()
+        base = rng.choice(rows // 2, leaders // 2, replace=False) * 2
+        lead += np.stack([base, base + 1], 1).reshape(-1).tolist()
+        o += m * r
+    members = np.array(members, np.uint32)
+    lead = np.array(lead, np.uint32)
+    out = np.array(out, np.uint64)
+    dv = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    ids, d = ops.assign(ASSIGN_SQ8, codes=dv(codes), scales=dv(scales), sq8_norms=dv(qn),
+                        global_ids=dv(gids.view(np.int32)), members=dv(members.view(np.int32)),
+                        leaders=dv(lead.view(np.int32)), task_member_offsets=moff, task_member_counts=mcnt,
+                        task_leader_offsets=loff, task_leader_counts=lcnt, task_rh=rh, task_output_offsets=out,
+                        output_len=o)
+    wi, wd = oracle.assign(3, x, qn, codes, scales, gids, members, lead, moff, mcnt, loff, lcnt, rh, out, o)
+    assert np.array_equal(ops.as_u32(ids), wi)
+    assert np.array_equal(d.cpu().numpy().view(np.uint32), wd.view(np.uint32))
+    # the twins really tie: a row's two best slots are almost always the two
+    # copies of its nearest leader, ordered by the tie key
+    got = ops.as_u32(ids).reshape(-1, 4)
+    twin_of = dict(zip(gids[0::2].tolist(), gids[1::2].tolist()))
+    twin_of.update(zip(gids[1::2].tolist(), gids[0::2].tolist()))
+    pairs = np.array([twin_of.get(a) == b for a, b in got[:, :2].tolist()])
+    assert pairs.mean() > 0.9
