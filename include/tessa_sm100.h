@@ -146,8 +146,9 @@ typedef struct tessa_leaf_args {
  * in their tail slots.  Device scratch held by the context, grown on demand:
  * the optional leaf-ordered codes (above), the tile table, the exact-fallback
  * row list (8 bytes per row) and, for padded_dim <= 1024, a per-row zone dump
- * of 514 bytes per leaf row (the leaf kernel's candidates near each row's k-th
- * distance, read back by its finishing kernel). */
+ * of 8 * min(k + 7, 48) rounded down to even, plus 130, bytes per leaf row (434
+ * at k = 32: the leaf kernel's candidates near each row's k-th distance, read
+ * back by its finishing kernel). */
 TESSA_API int tessa_leaf_topk_sq8(tessa_ctx* ctx, const tessa_leaf_args* args, void* stream);
 
 /* Host-buffer variant: every pointer of `args` (including leaf_members and the

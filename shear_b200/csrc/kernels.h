@@ -40,6 +40,7 @@ struct LeafLaunch {
 // padded_dim / k) and the dump scratch it needs for `rows` leaf rows.
 bool leaf_split_plan(uint32_t padded_dim, uint32_t k, uint32_t* ring, uint32_t* log_cap);
 uint64_t leaf_dump_bytes(uint64_t rows, uint32_t k);
+uint64_t leaf_dump_m_offset(uint64_t rows, uint32_t k);
 uint32_t leaf_dump_entries(uint32_t k);
 
 // Largest leaf the leaf kernel accepts (a validated cap above the reference's

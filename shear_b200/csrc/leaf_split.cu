@@ -944,13 +944,23 @@ bool leaf_split_plan(uint32_t padded_dim, uint32_t k, uint32_t* ring, uint32_t* 
 }
 
 // Zone entries dumped per row (both halves together); rows with a larger zone
-// go to the exact fallback.  48 holds the k = 32 zone with room for ties.
-uint32_t leaf_dump_entries(uint32_t) { return 48u; }
+// go to the exact fallback.  About k + 6 holds the zone (the k smallest and
+// the few within the margin above the k-th) with room for ties, and keeps the
+// finishing kernel's staging (9 bytes per entry and row, 128 rows per block)
+// small enough for five blocks per SM at k = 32.  Even, so the entry region
+// (8 bytes per entry and row) ends on a 16-byte boundary.
+uint32_t leaf_dump_entries(uint32_t k) { return (k + 7u < 48u ? k + 7u : 48u) & ~1u; }
+
+// Byte offset of the merged k smallest (float4 rows) in the dump buffer: the
+// entry region rounded up to 16 bytes.
+uint64_t leaf_dump_m_offset(uint64_t rows, uint32_t k) {
+  return ((uint64_t)leaf_dump_entries(k) * 8u * rows + 15u) & ~uint64_t(15u);
+}
 
 // Per row: the zone entries (8 bytes each), the merged k smallest (32 floats)
 // and two entry counts.
 uint64_t leaf_dump_bytes(uint64_t rows, uint32_t k) {
-  return rows * ((uint64_t)leaf_dump_entries(k) * 8u + 128u + 2u);
+  return leaf_dump_m_offset(rows, k) + rows * (128u + 2u);
 }
 
 template <int KS>

@@ -919,7 +919,7 @@ int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
     prm.dump_rows = L.dump_rows;
     prm.dump_d = leaf_dump_entries(L.k);
     prm.dump = reinterpret_cast<uint2*>(L.d_dump);
-    prm.dump_m = reinterpret_cast<float4*>(prm.dump + (uint64_t)prm.dump_d * L.dump_rows);
+    prm.dump_m = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(L.d_dump) + leaf_dump_m_offset(L.dump_rows, L.k));
     prm.dump_cnt = reinterpret_cast<uint8_t*>(prm.dump_m + 8u * L.dump_rows);
     if (cudaMemsetAsync(prm.fb_count, 0, 4, stream) != cudaSuccess) return TESSA_ERR_CUDA;
     int rc = launch_leaf_split(ta, prm, L.padded_dim, L.sm_count, stream);

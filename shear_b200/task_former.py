@@ -20,7 +20,8 @@ bounds it) and M = R * f leaf rows:
   members are not contiguous, lists M * k * 8, the exact-fallback row list
   M * 8 + 16, leaf layout and tile table (16 bytes per leaf, 8 per 128-row
   tile, leaves of at least leaf_min rows), and for padded_dim <= 1024 the
-  column-split kernel's per-row zone dump M * (8 * 48 + 128 + 2);
+  column-split kernel's per-row zone dump M * (8 * D + 128 + 2) with
+  D = min(k + 7, 48) rounded down to even (38 at k = 32);
 * assignment: member / leader ids 4 * (R + leaders), outputs R * r_h * 8.
 
 ``library_scratch_bytes`` reports what a context actually holds, and the GPU
@@ -168,7 +169,8 @@ def plan_subtree_admission(rows: int, dim: int, leaf_k: int, max_fanout: int, bu
     leaves = -(-m // GPU_PERSISTENT_LEAF_MIN) if m else 0
     tiles = leaves + -(-m // 128)
     kk = min(leaf_k, 32)
-    dump = m * (8 * 48 + 128 + 2) if pd <= 1024 else 0
+    zone = min(kk + 7, 48) & ~1
+    dump = m * (8 * zone + 128 + 2) + 16 if pd <= 1024 else 0
     leaf = (m * 4 + (0 if leaf_ordered else m * pd) + m * kk * 8 + m * 8 + 16
             + leaves * 16 + tiles * 8 + dump)
     assign = 4 * (rows + leaders) + rows * r_h * 8

@@ -67,19 +67,21 @@ def test_admission_binary_search_finds_the_boundary():
 def test_b200_root_plan_for_the_35m_config():
     # The reference's resident-budget test (P/d0_capacity.rs:383-431) finds
     # capacity pressure for Wiki35M under its persistent-kernel queue model.
-    # This library's footprint is about 4.7 KB per row at fanout 3 (codes,
-    # leaf batch with the column-split kernel's zone dump, assignment), so a
-    # 24 GiB workspace admits ~5.4M-row subtrees and capacity binds (78 root
-    # leaders); at 32 GiB ~7.3M rows fit and the quality floor (64) binds.
+    # This library's footprint is about 3.8 KB per row at fanout 3 and leaf
+    # k = 2 (codes, leaf batch with the column-split kernel's zone dump,
+    # assignment): the 35M config's 24 GiB workspace admits ~6.8M-row subtrees,
+    # where the quality floor (64 root leaders) binds; a 16 GiB workspace
+    # admits ~4.6M rows and capacity binds (93 root leaders).
     cfg = tf.D0CapacityConfig()
     c_gpu = tf.find_max_admissible_rows(768, 2, 3, 24 * (1 << 30))
     p = tf.plan_root_leaders(35_000_000, 6, tf.compute_thresholds(c_gpu, cfg), cfg)
-    assert 5_000_000 < c_gpu < 6_000_000
-    assert p.k_capacity > cfg.quality_min_root_leaders and p.root_leader_source == "capacity"
-    big = tf.find_max_admissible_rows(768, 2, 3, 32 * (1 << 30))
-    q = tf.plan_root_leaders(35_000_000, 6, tf.compute_thresholds(big, cfg), cfg)
-    assert q.k_capacity < cfg.quality_min_root_leaders
-    assert (q.k_initial, q.root_leader_source) == (64, "quality_floor")
+    assert 6_000_000 < c_gpu < 7_500_000
+    assert p.k_capacity < cfg.quality_min_root_leaders
+    assert (p.k_initial, p.root_leader_source) == (64, "quality_floor")
+    small = tf.find_max_admissible_rows(768, 2, 3, 16 * (1 << 30))
+    q = tf.plan_root_leaders(35_000_000, 6, tf.compute_thresholds(small, cfg), cfg)
+    assert 4_000_000 < small < 5_000_000
+    assert q.k_capacity > cfg.quality_min_root_leaders and q.root_leader_source == "capacity"
 
 
 @pytest.mark.gpu
