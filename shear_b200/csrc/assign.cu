@@ -371,14 +371,20 @@ __global__ void __launch_bounds__(kRows) assign_f32_staged_kernel(const Params p
       const uint32_t nchunk = (rem < kStage ? rem : kStage) / 16u;
       for (uint32_t c = 0; c < nchunk; ++c) {
         const float4 xv = *reinterpret_cast<const float4*>(rsrc + c * 16u);
+        const uint64_t x01 = f2_pack(xv.x, xv.y), x23 = f2_pack(xv.z, xv.w);
 #pragma unroll
         for (int l = 0; l < LG; ++l) {
           const float4 yv = *reinterpret_cast<const float4*>(lsrc + l * kStage + c * 16u);
+          // products of two adjacent axes per paired instruction (each rounded
+          // as __fmul_rn), then the sums strictly in axis order
+          float p0, p1, p2, p3;
+          f2_unpack(f2_mul(x01, f2_pack(yv.x, yv.y)), p0, p1);
+          f2_unpack(f2_mul(x23, f2_pack(yv.z, yv.w)), p2, p3);
           float t = accf[l];
-          t = __fadd_rn(t, __fmul_rn(xv.x, yv.x));
-          t = __fadd_rn(t, __fmul_rn(xv.y, yv.y));
-          t = __fadd_rn(t, __fmul_rn(xv.z, yv.z));
-          accf[l] = __fadd_rn(t, __fmul_rn(xv.w, yv.w));
+          t = __fadd_rn(t, p0);
+          t = __fadd_rn(t, p1);
+          t = __fadd_rn(t, p2);
+          accf[l] = __fadd_rn(t, p3);
         }
       }
       __syncthreads();  // buffer b is refilled by the next stage's copies
