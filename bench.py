@@ -26,7 +26,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import re
 import subprocess
 import sys
 import time
@@ -38,6 +37,9 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 NOMINAL_INT8_TOPS = 4500.0  # B200 dense int8, nominal
+# The leaf workload measures leaf-operator rows (vectors) per second of the
+# config-2 replay, not a whole build; the build is --workload build.
+LEAF_METRIC = "leaf-replay vectors/sec (config 2 leaf operator)"
 
 
 def parse_args():
@@ -200,15 +202,22 @@ def int8_peak_tops(torch, dev):
         return None
 
 
-def ncu_traffic_per_launch():
-    """DRAM bytes per leaf-kernel launch from the committed ncu summary, if present."""
-    path = os.path.join(ROOT, "profiles", "leaf_topk_sq8_config2.md")
-    try:
-        txt = open(path).read()
-    except OSError:
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
-    return float(m.group(1)) if m else None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one config-2
+# leaf step, from one ncu capture of the three leaf kernels (one launch each)
+# on 256 leaves of the same shape (inputs 4x the L2), scaled by 4096/256 leaves:
+#   python bench.py --leaves 256 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline &&
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum \
+#       --clock-control none -k regex:"leaf_topk_split|leaf_finish|leaf_fallback" -s 3 -c 3 \
+#       python bench.py --leaves 256 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline
+LEAF_STEP_TRAFFIC = {"leaf_topk_split_kernel": 8.65e9, "leaf_finish_kernel": 4.28e9, "leaf_fallback_kernel": None}
+
+
+def host_oracle():
+    """The CPU restatement (test infrastructure) with every host core: torchrun
+    sets OMP_NUM_THREADS=1 in each rank, which would leave it one thread."""
+    from oracle import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)
+    return O
 
 
 # ----------------------------------------------------------------- CPU legs
@@ -235,6 +244,36 @@ def cpu_leaf_sample(oracle_mod, host, a, seconds, max_leaves):
     return done_rows / dt, threads, leaves, dt
 
 
+def reference_gpu_leaf(torch, w, a, sample_leaves=128):
+    """The reference's own leaf kernel (gpu_persistent_subtree_topk_only, s8-WMMA
+    filter, staged column tasks, launched as its replay session launches it) on
+    the first `sample_leaves` leaves of the same workload, same B200, after our
+    timed region; per-step time extrapolated by leaf count (the kernel is a
+    persistent queue of independent leaf tasks)."""
+    try:
+        from oracle import refkernel as RK
+    except Exception:
+        return None
+    if not RK.available():
+        return None
+    n = min(sample_leaves, a.leaves)
+    host = host_sample(torch, w, n, a)
+    rows = n * a.leaf_rows
+    members = np.arange(rows, dtype=np.uint32)
+    starts = np.arange(n, dtype=np.uint64) * np.uint64(a.leaf_rows)
+    sizes = np.full(n, a.leaf_rows, np.uint64)
+    try:
+        _, _, counters, ms = RK.leaf_replay(host["codes"], host["scales"], host["norms"], host["gids"], members,
+                                            starts, sizes, a.k, 2)
+    except Exception as e:  # noqa: BLE001 - reported, not fatal to our arm
+        return {"error": str(e)}
+    step_ms = ms * a.leaves / n
+    return {"kernel": "reference gpu_persistent_subtree_topk_only, SQ8 s8-WMMA filter (replay mode A3)",
+            "value": a.leaves * a.leaf_rows / (step_ms / 1e3), "unit": "vectors/s",
+            "ms_per_step": step_ms, "sample": f"{n} of {a.leaves} leaves in one launch ({ms:.1f} ms), "
+                                              f"scaled by leaf count", "safety_gate": RK.leaf_safety_gate(counters, 2)}
+
+
 def host_sample(torch, w, leaves, a):
     rows = leaves * a.leaf_rows
     return dict(codes=w["codes"][:rows].cpu().numpy(), scales=w["scales"][:rows].cpu().numpy(),
@@ -246,7 +285,7 @@ def run_reference(a):
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    from oracle import oracle as O
+    O = host_oracle()
 
     threads = O.num_threads()
     rng = np.random.default_rng(0)
@@ -270,7 +309,7 @@ def run_reference(a):
     value = rows / mean
     sample = f"{per_step} leaves x {a.leaf_rows} rows per step ({per_step / a.leaves:.4%} of the workload)"
     line = {
-        "impl": "reference", "metric": "build vectors/sec", "value": value, "unit": "vectors/s",
+        "impl": "reference", "metric": LEAF_METRIC, "value": value, "unit": "vectors/s",
         "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": mean * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic: N(0,1) rows, L2-normalised, SQ8 per-row int8 (seed 0)",
@@ -394,7 +433,7 @@ def run_ours(a):
         (NOMINAL_INT8_TOPS, "nominal B200 dense int8 4.5 POPS (no measured int8 peak)")
     # The committed ncu figure is for the full config-2 launch only.
     full_cfg = (a.leaves, a.leaf_rows, a.dim, a.k) == (4096, 2048, 768, 32)
-    traffic = ncu_traffic_per_launch() if full_cfg else None
+    traffic = sum(v for v in LEAF_STEP_TRAFFIC.values() if v) if full_cfg else None
     roofline = {"bound": "tensor", "achieved": achieved_tops, "peak": peak, "unit": "TOP/s",
                 "frac": achieved_tops / peak, "traffic": traffic, "peak_source": src,
                 "frac_of_nominal_4500": achieved_tops / NOMINAL_INT8_TOPS,
@@ -405,7 +444,7 @@ def run_ours(a):
 
     cpu = None
     if not a.no_cpu_baseline and world == 1:
-        from oracle import oracle as O
+        O = host_oracle()
         max_leaves = max(O.num_threads(), 1) * 32  # ~10 s of OpenMP work; the time limit ends it
         host = host_sample(torch, w, min(a.leaves, max_leaves), a)
         v, thr, nl, dt = cpu_leaf_sample(O, host, a, a.cpu_seconds, min(a.leaves, max_leaves))
@@ -413,8 +452,10 @@ def run_ours(a):
                "sample": f"{nl} of {a.leaves} leaves ({nl * a.leaf_rows} rows) in {dt:.1f} s, "
                          f"oracle/tessa_oracle.c OpenMP"}
 
+    ref_gpu = reference_gpu_leaf(torch, w, a) if world == 1 else None
+
     line = {
-        "metric": "build vectors/sec", "value": value, "unit": "vectors/s", "n_gpus": world,
+        "metric": LEAF_METRIC, "value": value, "unit": "vectors/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic: N(0,1) rows, L2-normalised, SQ8 per-row int8 (seed 1234+rank)",
@@ -469,7 +510,7 @@ def run_d0_reference(a):
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    from oracle import oracle as O
+    O = host_oracle()
 
     threads = O.num_threads()
     rng = np.random.default_rng(0)
@@ -608,7 +649,7 @@ def run_d0(a):
 
     cpu = None
     if not a.no_cpu_baseline and world == 1:
-        from oracle import oracle as O
+        O = host_oracle()
         hx = x[: min(rows, 1 << 17)].cpu().numpy()
         hg = gids[: hx.shape[0]].cpu().numpy().view(np.uint32)
         hl, hv = lids.cpu().numpy().view(np.uint32), lv.cpu().numpy()
@@ -681,7 +722,7 @@ def run_edges_reference(a):
         return 0
     from concurrent.futures import ThreadPoolExecutor
 
-    from oracle import oracle as O
+    O = host_oracle()
 
     threads = O.num_threads()
     rng = np.random.default_rng(0)
@@ -856,7 +897,7 @@ def run_edges(a):
     if not a.no_cpu_baseline and world == 1:
         from concurrent.futures import ThreadPoolExecutor
 
-        from oracle import oracle as O
+        O = host_oracle()
         threads = O.num_threads()
         nl = min(a.leaves, max(threads, 1) * 16)
         h_sk = sketches.cpu().numpy()
@@ -927,7 +968,7 @@ def run_assign_reference(a):
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    from oracle import oracle as O
+    O = host_oracle()
 
     rng = np.random.default_rng(0)
     b = argparse.Namespace(**vars(a))
