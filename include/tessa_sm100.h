@@ -42,8 +42,8 @@ extern "C" {
 #endif
 
 /* 1: leaf, quantize, assignment, replay; 2: + host pipeline knob, global D0, candidate
- * edges, capture digests, graph search (additive). */
-#define TESSA_ABI_VERSION 2
+ * edges, capture digests, graph search (additive); 3: + subtree partition (additive). */
+#define TESSA_ABI_VERSION 3
 
 #define TESSA_OK 0
 #define TESSA_ERR_INVALID_ARG (-1)  /* malformed sizes, null pointers, k out of range */
@@ -55,6 +55,8 @@ extern "C" {
 #define TESSA_ERR_NONFINITE (-7)    /* non-finite input to the SQ8 quantizer */
 #define TESSA_ERR_NO_DEVICE (-8)    /* no sm_100 device / extension not usable */
 #define TESSA_ERR_BAD_TASK (-9)     /* malformed task descriptor seen on the device */
+#define TESSA_ERR_PARTITION (-10)   /* the subtree partition cannot finish: a node above leaf_max at max_depth
+                                       (GPU_PERSISTENT_OVERSIZED_TERMINAL_NODE, CB:4849) or output capacity */
 
 /* Largest leaf k (CB:4890 GPU_PERSISTENT_LEAF_DCO_MAX_SURVIVORS). */
 #define TESSA_MAX_LEAF_K 32
@@ -397,6 +399,69 @@ typedef struct tessa_prepared_replay {
 #define TESSA_MODE_A3_SQ8_WMMA_BATCH8 3u
 #define TESSA_MODE_SQ8_DP4A_BATCH8 4u
 #define TESSA_MODE_SQ8_WMMA_BATCH1 5u
+
+/* ------------------------------------------------ subtree partition --- */
+
+/* One batch of D1+ subtree tasks (GpuSubtreePartitionRequest, CB:1818-1826,
+ * one per child run) for the recursive leader partition of the reference's
+ * persistent kernel gpu_persistent_subtree_topk (CB:16336-17381).  Task t has
+ * the resident rows task_members[task_offsets[t] .. + task_counts[t]),
+ * ascending; inside a task rows are named by position (the reference's
+ * subtree-local resident ids), which the leader sampler and the assignment tie
+ * key hash.  Parameters are the persistent plan's (CB:1309-1340 with
+ * PiPNNParams defaults, P/params.rs:3342-3368): leaf_max = max(256, c_max),
+ * leaf_min 64, max_depth 10, max_leaders min(params.max_leaders, 128),
+ * fanout_second 3 (root fanout, at most 4), root_depth = request.depth,
+ * small_node_limit 4096, psamp_fraction 0.001; task_seeds as
+ * gpu_queue_root_seed (CB:1597-1603).
+ *
+ * Result: leaves of at most leaf_max rows, written as resident ids into
+ * leaf_rows (device) at leaf_starts[l] with leaf_sizes[l] rows from task
+ * leaf_tasks[l] (host arrays).  Rows of a leaf ascend.  leaf_rows_capacity of
+ * fanout_second * member_rows always suffices (the extent used may contain
+ * gaps); leaf_capacity of the same bound too.  Leaves come in round order: all
+ * leaves emitted by the nodes of one level, node by node, before the next.
+ * The reference scatters rows into children with atomics (CB:15615-15626),
+ * so its child order and deeper leaders vary from run to run; this call uses
+ * the sequential order (rows ascending), which is deterministic. */
+typedef struct tessa_subtree_args {
+  const int8_t* codes;         /* device, resident_rows x padded_dim SQ8 codes */
+  const float* scales;         /* device */
+  const float* sq8_norms;      /* device */
+  uint64_t resident_rows;
+  uint32_t padded_dim;
+  const uint32_t* task_members;  /* device */
+  uint64_t member_rows;          /* entries of task_members */
+  const uint64_t* task_offsets;  /* host, task_count */
+  const uint32_t* task_counts;   /* host */
+  const uint64_t* task_seeds;    /* host */
+  uint32_t task_count;
+  uint32_t leaf_max, leaf_min, max_depth, max_leaders, fanout_second, root_depth, small_node_limit;
+  float psamp_fraction;
+  uint32_t* leaf_rows;           /* device, leaf_rows_capacity entries */
+  uint64_t leaf_rows_capacity;
+  uint64_t* leaf_starts;         /* host, leaf_capacity entries */
+  uint32_t* leaf_sizes;          /* host */
+  uint32_t* leaf_tasks;          /* host, may be NULL */
+  uint64_t leaf_capacity;
+} tessa_subtree_args;
+
+typedef struct tessa_subtree_result {
+  uint64_t leaf_count;
+  uint64_t leaf_rows_used;       /* extent of leaf_rows written */
+  uint32_t rounds;               /* levels (plus retry rounds) */
+  uint32_t large_assignments;    /* node assignments on the tensor cores */
+  uint32_t retries;              /* large-node leader resamples (CB:15416-15478) */
+  uint32_t balanced;             /* balanced even/odd fallbacks (CB:15480-15504) */
+  uint32_t small_nodes;          /* subtree roots split on the small path */
+} tessa_subtree_result;
+
+/* The partition of one batch of subtree tasks (synchronous on `stream`).
+ * Replaces the partition workers of gpu_persistent_subtree_topk behind
+ * PiPNNComputeBackend::process_quantized_subtree_l2_compact_topk (CB:3693-3884);
+ * the leaves then go to tessa_leaf_topk_sq8. */
+TESSA_API int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* args, tessa_subtree_result* result,
+                                      void* stream);
 
 /* TessaCudaModeResult (P/tessa_replay.rs:190-200); caller-owned host buffers
  * of assignment_output_len and leaf_rows*leaf_k entries.  leaf_* may be NULL

@@ -82,6 +82,13 @@ def _declare(L):
                                 _p(np.uint32), _p(np.uint64), u32, _p(np.uint32), _p(np.float32)]
     L.oracle_num_threads.restype = ctypes.c_int
     L.oracle_set_num_threads.argtypes = [ctypes.c_int]
+    L.oracle_adaptive_psamp.restype = f32
+    L.oracle_adaptive_psamp.argtypes = [f32, u32, u32]
+    L.oracle_subtree_partition.restype = i64
+    L.oracle_subtree_partition.argtypes = [_p(np.int8), _p(np.float32), _p(np.float32), u32, _p(np.uint32),
+                                           _p(np.uint64), _p(np.uint32), _p(np.uint64), u32, _p(np.uint32), f32,
+                                           _p(np.uint32), u64, _p(np.uint64), _p(np.uint32), _p(np.uint32), u64,
+                                           _p(np.uint64)]
 
 
 def padded_dim(dim: int, k_align: int = 16) -> int:
@@ -252,3 +259,48 @@ def num_threads() -> int:
 
 def set_num_threads(n: int) -> None:
     lib().oracle_set_num_threads(int(n))
+
+
+# ------------------------------------------------------------ subtree partition
+
+SUBTREE_ERRORS = {-10: "oversized terminal node", -11: "leader overflow", -12: "fanout over 4",
+                  -13: "node row overflow", -14: "output capacity", -15: "out of memory", -1: "bad argument"}
+
+
+def subtree_params(leaf_max=2048, leaf_min=64, max_depth=10, max_leaders=1000, fanout_second=3, root_depth=1,
+                   small_node_limit=4096):
+    """Persistent-subtree plan values (CB:1309-1340 with PiPNNParams defaults, P/params.rs:3342-3368):
+    leaf_max = max(256, c_max), leaf_min 64, small_node_limit 4096, max_leaders capped at 128."""
+    return np.array([leaf_max, leaf_min, max_depth, max_leaders, fanout_second, root_depth, small_node_limit],
+                    np.uint32)
+
+
+def subtree_partition(codes, scales, norms, members, task_offsets, task_counts, task_seeds, params=None,
+                      psamp=0.001):
+    """Recursive leader partition of subtree tasks into leaves (CB:16336-17381, sequential
+    canonical order).  Returns (leaf_rows u32 resident ids, leaf_starts u64, leaf_sizes u32,
+    leaf_tasks u32, stats {rounds, large_assignments, retries, balanced, small_nodes})."""
+    codes = np.ascontiguousarray(codes, np.int8)
+    members = np.ascontiguousarray(members, np.uint32)
+    toff = np.ascontiguousarray(task_offsets, np.uint64)
+    tcnt = np.ascontiguousarray(task_counts, np.uint32)
+    tseed = np.ascontiguousarray(task_seeds, np.uint64)
+    prm = subtree_params() if params is None else np.ascontiguousarray(params, np.uint32)
+    total = int(tcnt.sum())
+    cap_rows = 4 * total + 16
+    rows = np.zeros(cap_rows, np.uint32)
+    starts = np.zeros(cap_rows, np.uint64)
+    sizes = np.zeros(cap_rows, np.uint32)
+    tasks = np.zeros(cap_rows, np.uint32)
+    stats = np.zeros(5, np.uint64)
+    n = lib().oracle_subtree_partition(codes.reshape(-1), np.ascontiguousarray(scales, np.float32),
+                                       np.ascontiguousarray(norms, np.float32), codes.shape[1], members, toff, tcnt,
+                                       tseed, tcnt.size, prm, psamp, rows, cap_rows, starts, sizes, tasks,
+                                       cap_rows, stats)
+    if n < 0:
+        raise ValueError(f"oracle subtree partition failed: {SUBTREE_ERRORS.get(int(n), n)}")
+    n = int(n)
+    used = int(starts[n - 1] + sizes[n - 1]) if n else 0
+    keys = ["rounds", "large_assignments", "retries", "balanced", "small_nodes"]
+    return rows[:used].copy(), starts[:n].copy(), sizes[:n].copy(), tasks[:n].copy(), \
+        dict(zip(keys, (int(v) for v in stats)))

@@ -513,3 +513,478 @@ void oracle_set_num_threads(int n) {
     (void)n;
 #endif
 }
+
+/* ------------------------------------------ subtree partition (D1+) --- */
+
+/*
+ * The recursive leader partition of one or more subtree tasks, as the
+ * reference's persistent kernel gpu_persistent_subtree_topk runs it
+ * (CB:16336-17381), restated sequentially.  A task is a list of resident rows
+ * (ascending); inside it rows are named by their position (the reference's
+ * subtree-local resident ids), which the leader sampler and the assignment tie
+ * key hash.  Two node paths:
+ *   small (process_node, CB:12648-13048): nodes of at most leaf_max rows that
+ *     still split because they are a subtree root with fanout_second > 1 and
+ *     n * fanout_second <= small_node_limit -- hash bottom-k leaders, up to six
+ *     attempts, children below leaf_min merged;
+ *   large (stage_large_node + process_large_task_cta, CB:12456-12646 and
+ *     CB:15047-15727): every other node above leaf_max -- leaders at evenly
+ *     spaced positions, retries with the span sampler (CB:5991-6017), a
+ *     balanced even/odd split when no retry is left.
+ * Children of at most leaf_max rows are leaves; larger ones are queued one
+ * level deeper with seed ^ child * 0x94d049bb133111eb ^ (len << 23).
+ *
+ * Order.  The reference scatters a large node's rows into its children with
+ * atomicAdd (CB:15615-15626), so child row order -- and with it the positional
+ * leaders of deeper nodes -- differs from run to run.  The canonical order here
+ * is the sequential one: rows in ascending position, fanout slots in rank order
+ * (the same order the small path's sort gives).  Rows of every node therefore
+ * stay ascending.  The work is organised in rounds (every queued node once per
+ * round; a node that retries is queued again with its next attempt), the order
+ * in which the GPU driver runs it, so leaves come out in the same order.
+ *
+ * Arithmetic: SQ8 assignment distance in the contracted form (CB:14676-14678),
+ * the hash-tie insertion over local_fanout slots (CB:6524-6578), leader count
+ * round(psamp * n) formed as fmaf(psamp, n, 0.5f) (nvcc contracts
+ * CB:12761 / CB:12566 the same way).
+ */
+#define SUBTREE_ERR_OVERSIZED (-10)   /* GPU_PERSISTENT_OVERSIZED_TERMINAL_NODE */
+#define SUBTREE_ERR_LEADERS (-11)     /* GPU_PERSISTENT_LEADER_OVERFLOW */
+#define SUBTREE_ERR_FANOUT (-12)      /* GPU_PERSISTENT_FANOUT_OVER_32 */
+#define SUBTREE_ERR_ROWS (-13)        /* GPU_PERSISTENT_QUEUE_ROW_OVERFLOW */
+#define SUBTREE_ERR_CAPACITY (-14)    /* output capacity exceeded */
+#define SUBTREE_ERR_NOMEM (-15)
+
+/* CB:7044-7075 gpu_persistent_adaptive_psamp_fraction */
+float oracle_adaptive_psamp(float base, uint32_t n, uint32_t depth) {
+    float f = base;
+    if (n >= 20000000u) f *= 0.05f;
+    else if (n >= 10000000u) f *= 0.1f;
+    else if (n >= 5000000u) f *= 0.2f;
+    else if (n >= 1000000u) f *= 0.4f;
+    else if (n >= 100000u) f *= 0.7f;
+    if (depth > 4u) f *= 0.35f;
+    else if (depth > 2u) f *= 0.5f;
+    else if (depth > 0u) f *= 0.8f;
+    if (f < 0.00005f) f = 0.00005f;
+    if (f > 0.1f) f = 0.1f;
+    return f;
+}
+
+/* CB:7082-7101 gpu_persistent_meaningful_split */
+static int meaningful_split(uint32_t parent, uint32_t max_child, uint32_t terminal) {
+    if (parent <= terminal || max_child <= terminal) return 1;
+    if (max_child >= parent) return 0;
+    uint32_t min_shrink = parent >> 5;
+    if (min_shrink < 32u) min_shrink = 32u;
+    if (min_shrink >= parent) min_shrink = 1u;
+    return max_child + min_shrink <= parent;
+}
+
+static uint32_t leader_count(float psamp, uint32_t n, uint32_t max_leaders) {
+    uint32_t b = (uint32_t)fmaf(psamp, (float)n, 0.5f);
+    if (b < 2u) b = 2u;
+    if (b > max_leaders) b = max_leaders;
+    return b;
+}
+
+typedef struct {
+    uint32_t task, off, n, depth, attempt, num;
+    uint64_t seed;
+} st_node;
+
+typedef struct {
+    const int8_t* codes;
+    const float* scales;
+    const float* norms;
+    uint32_t pd;
+    const uint32_t* members;   /* resident rows of all tasks */
+    const uint64_t* task_off;
+    /* parameters */
+    uint32_t leaf_max, leaf_min, max_depth, max_leaders, fanout_second, root_depth, small_limit;
+    float psamp;
+    /* outputs */
+    uint32_t* leaf_rows;
+    uint64_t leaf_rows_cap, leaf_rows_len;
+    uint64_t* leaf_starts;
+    uint32_t* leaf_sizes;
+    uint32_t* leaf_tasks;
+    uint64_t leaf_cap, leaf_len;
+} st_ctx;
+
+typedef struct {
+    uint32_t* rows;
+    uint64_t len, cap;
+    st_node* nodes;
+    uint64_t n, ncap;
+} st_round;
+
+static int st_queue(st_round* r, st_node nd, const uint32_t* rows) {
+    if (r->n == r->ncap) {
+        uint64_t ncap = r->ncap * 2 + 16;
+        st_node* a = (st_node*)realloc(r->nodes, ncap * sizeof(st_node));
+        if (!a) return SUBTREE_ERR_NOMEM;
+        r->nodes = a;
+        r->ncap = ncap;
+    }
+    if (r->len + nd.n > r->cap) {
+        uint64_t cap = (r->cap + nd.n) * 2;
+        uint32_t* b = (uint32_t*)realloc(r->rows, cap * sizeof(uint32_t));
+        if (!b) return SUBTREE_ERR_NOMEM;
+        r->rows = b;
+        r->cap = cap;
+    }
+    nd.off = (uint32_t)r->len;
+    memcpy(r->rows + r->len, rows, sizeof(uint32_t) * nd.n);
+    r->len += nd.n;
+    r->nodes[r->n++] = nd;
+    return ORACLE_OK;
+}
+
+static int st_emit_leaf(st_ctx* c, uint32_t task, const uint32_t* local, uint32_t n) {
+    if (c->leaf_len >= c->leaf_cap || c->leaf_rows_len + n > c->leaf_rows_cap) return SUBTREE_ERR_CAPACITY;
+    const uint32_t* tm = c->members + c->task_off[task];
+    for (uint32_t i = 0; i < n; ++i) c->leaf_rows[c->leaf_rows_len + i] = tm[local[i]];
+    c->leaf_starts[c->leaf_len] = c->leaf_rows_len;
+    c->leaf_sizes[c->leaf_len] = n;
+    c->leaf_tasks[c->leaf_len] = task;
+    c->leaf_len++;
+    c->leaf_rows_len += n;
+    return ORACLE_OK;
+}
+
+/* Best local_fanout leader slots of one row (tie ids are local ids). */
+static void st_assign_row(const st_ctx* c, uint32_t task, uint32_t point, const uint32_t* leaders,
+                          uint32_t num, uint32_t lf, uint32_t* out_slots) {
+    const uint32_t* tm = c->members + c->task_off[task];
+    float bd[4];
+    uint32_t bs[4], bl[4];
+    for (int s = 0; s < 4; ++s) { bd[s] = EMPTY_DIST; bs[s] = EMPTY_ID; bl[s] = EMPTY_ID; }
+    uint32_t rp = tm[point];
+    for (uint32_t slot = 0; slot < num; ++slot) {
+        uint32_t rl = tm[leaders[slot]];
+        float d = assign_dist(3, NULL, c->norms, c->codes, c->scales, 0, c->pd, rp, rl);
+        assign_insert(d, point, leaders[slot], slot, lf, bd, bs, bl);
+    }
+    for (uint32_t k = 0; k < lf; ++k) out_slots[k] = bs[k];
+}
+
+/* merge two ascending lists into out (ascending, duplicates dropped) */
+static uint32_t merge_unique(const uint32_t* a, uint32_t na, const uint32_t* b, uint32_t nb, uint32_t* out) {
+    uint32_t i = 0, j = 0, o = 0;
+    while (i < na || j < nb) {
+        uint32_t v;
+        if (j >= nb || (i < na && a[i] <= b[j])) v = a[i++];
+        else v = b[j++];
+        if (o == 0 || out[o - 1] != v) out[o++] = v;
+    }
+    return o;
+}
+
+static uint64_t child_seed(uint64_t seed, uint32_t child, uint32_t len) {
+    return seed ^ ((uint64_t)child * 0x94d049bb133111ebull) ^ (((uint64_t)len) << 23);
+}
+
+/* process_node (CB:12648-13048) for a node that splits on the small path. */
+static int st_small(st_ctx* c, const st_node* nd, const uint32_t* rows, st_round* next) {
+    uint32_t n = nd->n;
+    uint32_t depth = nd->depth;
+    uint32_t rd = depth >= c->root_depth ? depth - c->root_depth : 0u;
+    uint32_t terminal = c->leaf_max;
+    if (depth >= c->max_depth) return SUBTREE_ERR_OVERSIZED;
+    uint32_t max_leaders = c->max_leaders < n ? c->max_leaders : n;
+    if (max_leaders < 2u) max_leaders = 2u;
+    if (max_leaders > 128u) return SUBTREE_ERR_LEADERS;
+    uint32_t base = leader_count(oracle_adaptive_psamp(c->psamp, n, depth), n, max_leaders);
+    uint32_t requested = rd == 0u ? c->fanout_second : 1u;
+    if (requested < 1u) requested = 1u;
+    if (requested > 4u) return SUBTREE_ERR_FANOUT;
+    uint32_t leaders[128], counts[128], starts[128], writes[128];
+    uint32_t child_off[129], child_cnt[129];
+    uint32_t* slots = (uint32_t*)malloc(sizeof(uint32_t) * 4u * n);
+    uint32_t* clustered = (uint32_t*)malloc(sizeof(uint32_t) * 4096u);
+    uint32_t* merged = (uint32_t*)malloc(sizeof(uint32_t) * 4096u);
+    uint32_t* small = (uint32_t*)malloc(sizeof(uint32_t) * 4096u);
+    uint32_t* tmp = (uint32_t*)malloc(sizeof(uint32_t) * 8192u);
+    int rc = ORACLE_OK, ok = 0;
+    uint32_t nchild = 0;
+    if (!slots || !clustered || !merged || !small || !tmp) { rc = SUBTREE_ERR_NOMEM; goto done; }
+    for (uint32_t attempt = 0; attempt < 6u; ++attempt) {
+        uint32_t num = base << attempt;
+        if (num > max_leaders || (base << attempt) >> attempt != base) num = max_leaders;
+        uint64_t scores[128];
+        for (uint32_t s = 0; s < num; ++s) { leaders[s] = 0xffffffffu; scores[s] = ~0ull; }
+        for (uint32_t i = 0; i < n; ++i) {
+            uint32_t point = rows[i];
+            uint64_t key = oracle_hash64(nd->seed ^ ((uint64_t)attempt * 0xbf58476d1ce4e5b9ull) ^
+                                         (((uint64_t)depth) << 19) ^ (((uint64_t)i) << 7) ^
+                                         (((uint64_t)point) << 31));
+            uint32_t ins = num;
+            for (uint32_t p = 0; p < num; ++p)
+                if (key < scores[p] || (key == scores[p] && point < leaders[p])) { ins = p; break; }
+            if (ins < num) {
+                for (uint32_t p = num - 1; p > ins; --p) { scores[p] = scores[p - 1]; leaders[p] = leaders[p - 1]; }
+                scores[ins] = key;
+                leaders[ins] = point;
+            }
+        }
+        uint32_t lf = requested < num ? requested : num;
+        for (uint32_t s = 0; s < num; ++s) counts[s] = 0;
+        for (uint32_t i = 0; i < n; ++i) {
+            st_assign_row(c, nd->task, rows[i], leaders, num, lf, slots + (uint64_t)i * lf);
+            for (uint32_t k = 0; k < lf; ++k) {
+                uint32_t s = slots[(uint64_t)i * lf + k];
+                if (s >= num) { rc = SUBTREE_ERR_ROWS; goto done; }
+                counts[s]++;
+            }
+        }
+        uint32_t running = 0;
+        for (uint32_t s = 0; s < num; ++s) { starts[s] = running; writes[s] = running; running += counts[s]; }
+        if (running > 4096u) { rc = SUBTREE_ERR_ROWS; goto done; }
+        for (uint32_t i = 0; i < n; ++i)
+            for (uint32_t k = 0; k < lf; ++k) clustered[writes[slots[(uint64_t)i * lf + k]]++] = rows[i];
+        nchild = 0;
+        uint32_t merged_rows = 0, small_len = 0, max_child = 0;
+        for (uint32_t s = 0; s < num; ++s) {
+            uint32_t cnt = counts[s];
+            if (cnt == 0) continue;
+            const uint32_t* seg = clustered + starts[s];  /* ascending, distinct */
+            if (cnt < c->leaf_min) {
+                uint32_t m = merge_unique(small, small_len, seg, cnt, tmp);
+                memcpy(small, tmp, sizeof(uint32_t) * m);
+                small_len = m;
+                if (small_len >= c->leaf_min) {
+                    memcpy(merged + merged_rows, small, sizeof(uint32_t) * small_len);
+                    child_off[nchild] = merged_rows;
+                    child_cnt[nchild] = small_len;
+                    merged_rows += small_len;
+                    if (small_len > max_child) max_child = small_len;
+                    nchild++;
+                    small_len = 0;
+                }
+            } else {
+                child_off[nchild] = merged_rows;
+                child_cnt[nchild] = cnt;
+                memcpy(merged + merged_rows, seg, sizeof(uint32_t) * cnt);
+                merged_rows += cnt;
+                if (cnt > max_child) max_child = cnt;
+                nchild++;
+            }
+        }
+        if (small_len > 0 && nchild > 0) {
+            uint32_t last = nchild - 1;
+            if (child_cnt[last] + small_len <= terminal) {
+                uint32_t m = merge_unique(merged + child_off[last], child_cnt[last], small, small_len, tmp);
+                memcpy(merged + child_off[last], tmp, sizeof(uint32_t) * m);
+                merged_rows = child_off[last] + m;
+                child_cnt[last] = m;
+                if (m > max_child) max_child = m;
+                small_len = 0;
+            }
+        }
+        if (small_len > 0) {
+            memcpy(merged + merged_rows, small, sizeof(uint32_t) * small_len);
+            child_off[nchild] = merged_rows;
+            child_cnt[nchild] = small_len;
+            merged_rows += small_len;
+            if (small_len > max_child) max_child = small_len;
+            nchild++;
+        }
+        if (nchild > 1 && meaningful_split(n, max_child, terminal)) { ok = 1; break; }
+        if (num >= max_leaders) break;
+    }
+    if (!ok) {
+        if (n > terminal) { rc = SUBTREE_ERR_OVERSIZED; goto done; }
+        rc = st_emit_leaf(c, nd->task, rows, n);
+        goto done;
+    }
+    for (uint32_t ci = 0; ci < nchild && rc == ORACLE_OK; ++ci) {
+        uint32_t len = child_cnt[ci];
+        const uint32_t* cr = merged + child_off[ci];
+        if (len == 0) continue;
+        if (len <= terminal) {
+            rc = st_emit_leaf(c, nd->task, cr, len);
+        } else if (depth + 1u >= c->max_depth) {
+            rc = SUBTREE_ERR_OVERSIZED;
+        } else {
+            st_node ch = {nd->task, 0u, len, depth + 1u, 0u, 0u, child_seed(nd->seed, ci, len)};
+            rc = st_queue(next, ch, cr);
+        }
+    }
+done:
+    free(slots); free(clustered); free(merged); free(small); free(tmp);
+    return rc;
+}
+
+/* gpu_persistent_sample_large_retry_leaders (CB:5991-6017) */
+static void st_retry_leaders(const uint32_t* rows, uint32_t n, uint32_t num, uint64_t seed, uint32_t attempt,
+                             uint32_t* leaders) {
+    for (uint32_t s = 0; s < num; ++s) {
+        uint32_t b = (uint32_t)(((uint64_t)s * n) / num);
+        uint32_t e = (uint32_t)(((uint64_t)(s + 1u) * n) / num);
+        if (e <= b) e = b + 1u;
+        uint32_t span = e - b;
+        uint64_t key = oracle_hash64(seed ^ ((uint64_t)attempt * 0xd6e8feb86659fd93ull) ^
+                                     ((uint64_t)s * 0x9e3779b97f4a7c15ull));
+        leaders[s] = rows[b + (uint32_t)(key % span)];
+    }
+}
+
+/*
+ * Partition the tasks into leaves.  params = {leaf_max, leaf_min, max_depth,
+ * max_leaders, fanout_second, root_depth, small_node_limit}; task t has rows
+ * members[task_offsets[t] .. + task_counts[t]) (ascending resident ids) and
+ * seed task_seeds[t].  Leaves are written as resident ids in round order;
+ * returns the leaf count or a negative error.  out_stats (may be NULL) gets
+ * {rounds, large-node assignments, retries, balanced splits, small nodes}.
+ */
+int64_t oracle_subtree_partition(const int8_t* codes, const float* scales, const float* norms,
+                                 uint32_t padded_dim, const uint32_t* members, const uint64_t* task_offsets,
+                                 const uint32_t* task_counts, const uint64_t* task_seeds, uint32_t task_count,
+                                 const uint32_t* params, float psamp, uint32_t* leaf_rows, uint64_t leaf_rows_cap,
+                                 uint64_t* leaf_starts, uint32_t* leaf_sizes, uint32_t* leaf_tasks,
+                                 uint64_t leaf_cap, uint64_t* out_stats) {
+    st_ctx c;
+    memset(&c, 0, sizeof c);
+    c.codes = codes; c.scales = scales; c.norms = norms; c.pd = padded_dim;
+    c.members = members; c.task_off = task_offsets;
+    c.leaf_max = params[0]; c.leaf_min = params[1]; c.max_depth = params[2];
+    c.max_leaders = params[3] < 128u ? params[3] : 128u;
+    c.fanout_second = params[4]; c.root_depth = params[5]; c.small_limit = params[6];
+    c.psamp = psamp;
+    c.leaf_rows = leaf_rows; c.leaf_rows_cap = leaf_rows_cap;
+    c.leaf_starts = leaf_starts; c.leaf_sizes = leaf_sizes; c.leaf_tasks = leaf_tasks; c.leaf_cap = leaf_cap;
+    if (c.leaf_max == 0 || c.leaf_min == 0 || c.leaf_max > c.small_limit) return ORACLE_ERR_ARG;
+    uint64_t stats[5] = {0, 0, 0, 0, 0};
+    uint64_t cur_len = 0, cur_cap = 16, nn = 0;
+    for (uint32_t t = 0; t < task_count; ++t) cur_cap += task_counts[t];
+    uint32_t* cur = (uint32_t*)malloc(cur_cap * sizeof(uint32_t));
+    st_node* nodes = (st_node*)malloc((task_count + 16) * sizeof(st_node));
+    int rc = ORACLE_OK;
+    if (!cur || !nodes) { free(cur); free(nodes); return SUBTREE_ERR_NOMEM; }
+    for (uint32_t t = 0; t < task_count; ++t) {
+        if (task_counts[t] == 0) continue;
+        st_node r = {t, (uint32_t)cur_len, task_counts[t], c.root_depth, 0u, 0u, task_seeds[t]};
+        for (uint32_t i = 0; i < task_counts[t]; ++i) cur[cur_len + i] = i;
+        cur_len += task_counts[t];
+        nodes[nn++] = r;
+    }
+    uint32_t* slots = NULL;
+    uint64_t slots_cap = 0;
+    while (nn > 0 && rc == ORACLE_OK) {
+        stats[0]++;
+        st_round next = {NULL, 0, 0, NULL, 0, 0};
+        for (uint64_t q = 0; q < nn && rc == ORACLE_OK; ++q) {
+            st_node nd = nodes[q];
+            const uint32_t* rows = cur + nd.off;
+            uint32_t n = nd.n;
+            uint32_t rd = nd.depth >= c.root_depth ? nd.depth - c.root_depth : 0u;
+            int probe = rd == 0u && c.fanout_second > 1u && n > 1u;
+            int probe_over = probe && (uint64_t)n * c.fanout_second > c.small_limit;
+            if (n <= c.leaf_max && !probe_over) {
+                if (!probe) { rc = st_emit_leaf(&c, nd.task, rows, n); continue; }
+                stats[4]++;
+                rc = st_small(&c, &nd, rows, &next);
+                continue;
+            }
+            /* large path: stage_large_node (CB:12456-12646) */
+            if (nd.depth >= c.max_depth) { rc = SUBTREE_ERR_OVERSIZED; break; }
+            uint32_t retry_max = n < 2u ? 2u : n;
+            if (retry_max > 128u) retry_max = 128u;
+            uint32_t max_leaders = c.max_leaders < retry_max ? c.max_leaders : retry_max;
+            if (max_leaders < 2u) max_leaders = 2u;
+            uint32_t requested = rd == 0u ? c.fanout_second : 1u;
+            if (requested < 1u) requested = 1u;
+            if (requested > 4u) { rc = SUBTREE_ERR_FANOUT; break; }
+            uint32_t base = leader_count(oracle_adaptive_psamp(c.psamp, n, nd.depth), n, max_leaders);
+            uint32_t lf = requested < base ? requested : base;  /* fixed at staging */
+            uint32_t num = nd.attempt == 0u ? base : nd.num;
+            uint32_t leaders[128], counts[128];
+            if (nd.attempt == 0u) {
+                for (uint32_t s = 0; s < num; ++s) {
+                    uint64_t ord = ((uint64_t)s * n) / num;
+                    if (ord >= n) ord = n - 1u;
+                    leaders[s] = rows[ord];
+                }
+            } else {
+                st_retry_leaders(rows, n, num, nd.seed, nd.attempt, leaders);
+            }
+            if (slots_cap < (uint64_t)n * 4u) {
+                free(slots);
+                slots_cap = (uint64_t)n * 4u;
+                slots = (uint32_t*)malloc(slots_cap * sizeof(uint32_t));
+                if (!slots) { rc = SUBTREE_ERR_NOMEM; break; }
+            }
+            stats[1]++;
+            for (uint32_t s = 0; s < num; ++s) counts[s] = 0;
+#pragma omp parallel for schedule(static)
+            for (int64_t i = 0; i < (int64_t)n; ++i)
+                st_assign_row(&c, nd.task, rows[i], leaders, num, lf, slots + (uint64_t)i * lf);
+            for (uint32_t i = 0; i < n; ++i)
+                for (uint32_t k = 0; k < lf; ++k) {
+                    uint32_t s = slots[(uint64_t)i * lf + k];
+                    if (s < num) counts[s]++;
+                }
+            uint32_t nonempty = 0, max_child = 0;
+            for (uint32_t s = 0; s < num; ++s)
+                if (counts[s]) { nonempty++; if (counts[s] > max_child) max_child = counts[s]; }
+            int split = nonempty > 1u && meaningful_split(n, max_child, c.leaf_max);
+            int balanced = 0;
+            if (!split) {
+                if (nd.attempt == 0u || num < retry_max) {
+                    uint32_t next_num = num;
+                    if (nd.attempt > 0u) {
+                        uint32_t dbl = num << 1;
+                        next_num = (dbl > num && dbl < retry_max) ? dbl : retry_max;
+                    }
+                    if (next_num > retry_max) next_num = retry_max;
+                    /* queued again, same rows, next attempt */
+                    st_node again = nd;
+                    again.attempt = nd.attempt + 1u;
+                    again.num = next_num;
+                    rc = st_queue(&next, again, rows);
+                    stats[2]++;
+                    continue;
+                }
+                balanced = 1;
+                stats[3]++;
+            }
+            /* children: slot order (balanced: position parity), rows ascending */
+            uint32_t nchild = balanced ? 2u : num;
+            for (uint32_t ci = 0; ci < nchild && rc == ORACLE_OK; ++ci) {
+                uint32_t len = 0;
+                uint32_t* buf = (uint32_t*)malloc(sizeof(uint32_t) * (n + 1u));
+                if (!buf) { rc = SUBTREE_ERR_NOMEM; break; }
+                for (uint32_t i = 0; i < n; ++i) {
+                    if (balanced) {
+                        if ((i & 1u) == ci) buf[len++] = rows[i];
+                    } else {
+                        for (uint32_t k = 0; k < lf; ++k)
+                            if (slots[(uint64_t)i * lf + k] == ci) { buf[len++] = rows[i]; break; }
+                    }
+                }
+                if (len == 0) { free(buf); continue; }
+                if (len <= c.leaf_max) {
+                    rc = st_emit_leaf(&c, nd.task, buf, len);
+                } else if (nd.depth + 1u >= c.max_depth) {
+                    rc = SUBTREE_ERR_OVERSIZED;
+                } else {
+                    st_node ch = {nd.task, 0u, len, nd.depth + 1u, 0u, 0u, child_seed(nd.seed, ci, len)};
+                    rc = st_queue(&next, ch, buf);
+                }
+                free(buf);
+            }
+        }
+        free(cur);
+        free(nodes);
+        cur = next.rows;
+        cur_len = next.len;
+        nodes = next.nodes;
+        nn = next.n;
+    }
+    free(cur);
+    free(nodes);
+    free(slots);
+    if (out_stats) memcpy(out_stats, stats, sizeof stats);
+    return rc == ORACLE_OK ? (int64_t)c.leaf_len : (int64_t)rc;
+}

@@ -23,6 +23,7 @@ ERRORS = {
     -7: "TESSA_ERR_NONFINITE",
     -8: "TESSA_ERR_NO_DEVICE",
     -9: "TESSA_ERR_BAD_TASK",
+    -10: "TESSA_ERR_PARTITION",
 }
 MAX_LEAF_K = 32
 MAX_RH = 4
@@ -110,6 +111,27 @@ class ModeResult(ctypes.Structure):
     ]
 
 
+class SubtreeArgs(ctypes.Structure):
+    _fields_ = [
+        ("codes", c_vp), ("scales", c_vp), ("sq8_norms", c_vp), ("resident_rows", ctypes.c_uint64),
+        ("padded_dim", ctypes.c_uint32), ("task_members", c_vp), ("member_rows", ctypes.c_uint64),
+        ("task_offsets", c_vp), ("task_counts", c_vp), ("task_seeds", c_vp), ("task_count", ctypes.c_uint32),
+        ("leaf_max", ctypes.c_uint32), ("leaf_min", ctypes.c_uint32), ("max_depth", ctypes.c_uint32),
+        ("max_leaders", ctypes.c_uint32), ("fanout_second", ctypes.c_uint32), ("root_depth", ctypes.c_uint32),
+        ("small_node_limit", ctypes.c_uint32), ("psamp_fraction", ctypes.c_float),
+        ("leaf_rows", c_vp), ("leaf_rows_capacity", ctypes.c_uint64), ("leaf_starts", c_vp),
+        ("leaf_sizes", c_vp), ("leaf_tasks", c_vp), ("leaf_capacity", ctypes.c_uint64),
+    ]
+
+
+class SubtreeResult(ctypes.Structure):
+    _fields_ = [
+        ("leaf_count", ctypes.c_uint64), ("leaf_rows_used", ctypes.c_uint64), ("rounds", ctypes.c_uint32),
+        ("large_assignments", ctypes.c_uint32), ("retries", ctypes.c_uint32), ("balanced", ctypes.c_uint32),
+        ("small_nodes", ctypes.c_uint32),
+    ]
+
+
 # (name, restype, argtypes) for every entry point of include/tessa_sm100.h
 SIGNATURES = [
     ("tessa_abi_version", ctypes.c_int, []),
@@ -149,6 +171,8 @@ SIGNATURES = [
      [ctypes.c_int, ctypes.POINTER(PreparedReplay), ctypes.POINTER(c_vp)]),
     ("tessa_replay_run_mode", ctypes.c_int, [c_vp, ctypes.c_uint32, ctypes.POINTER(ModeResult)]),
     ("tessa_replay_session_destroy", None, [c_vp]),
+    ("tessa_subtree_partition", ctypes.c_int,
+     [c_vp, ctypes.POINTER(SubtreeArgs), ctypes.POINTER(SubtreeResult), c_vp]),
 ]
 
 _lib = None

@@ -168,6 +168,57 @@ __device__ __forceinline__ void insert4(float d, uint32_t point, uint32_t leader
   bl[0] = c0 ? leader : bl[0];
 }
 
+// CB:6524-6578 with a list of n <= 4 slots (the subtree partition keeps
+// local_fanout slots, CB:6618-6698): the candidate is tested against slot
+// n - 1 first, then moved up while it beats the slot above.
+__device__ __forceinline__ void insertn(float d, uint32_t point, uint32_t leader, uint32_t slot, uint32_t n,
+                                        float (&bd)[4], uint32_t (&bs)[4], uint32_t (&bl)[4]) {
+  const uint32_t last = n - 1u;
+  float dl = bd[0];
+  uint32_t ll = bl[0];
+#pragma unroll
+  for (uint32_t j = 1; j < 4; ++j)
+    if (j == last) {
+      dl = bd[j];
+      ll = bl[j];
+    }
+  bool better = d < dl;
+  uint64_t ck = 0;
+  bool ck_ready = false;
+  if (fabsf(__fsub_rn(d, dl)) <= 2.0e-5f) {
+    ck = tie_key(point, leader);
+    ck_ready = true;
+    const uint64_t fk = tie_key(point, ll);
+    better = ck < fk || (ck == fk && leader < ll);
+  }
+  if (!better) return;
+  uint32_t pos = last;
+#pragma unroll
+  for (uint32_t j = 3; j >= 1; --j) {
+    if (j > last || pos != j) continue;
+    bool before = d < bd[j - 1];
+    if (fabsf(__fsub_rn(d, bd[j - 1])) <= 2.0e-5f) {
+      if (!ck_ready) {
+        ck = tie_key(point, leader);
+        ck_ready = true;
+      }
+      const uint64_t pk = tie_key(point, bl[j - 1]);
+      before = ck < pk || (ck == pk && leader < bl[j - 1]);
+    }
+    if (!before) continue;
+    bd[j] = bd[j - 1];
+    bs[j] = bs[j - 1];
+    bl[j] = bl[j - 1];
+    pos = j - 1;
+  }
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j)
+    if (j == pos) {
+      bd[j] = d;
+      bs[j] = slot;
+      bl[j] = leader;
+    }
+}
 
 __device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
@@ -269,11 +320,14 @@ __device__ __forceinline__ void prod_step(const Params& p, uint32_t item, uint32
     m.sp = m.pt != kNone ? p.scales[m.pt] : 0.f;
     m.ln = m.lid != kNone ? p.sq8_norms[m.lid] : 0.f;
     m.ls = m.lid != kNone ? p.scales[m.lid] : 0.f;
-    m.lg = m.lid != kNone ? p.global_ids[m.lid] : 0u;
+    m.lg = (m.lid != kNone && !p.out_slots) ? p.global_ids[m.lid] : 0u;
+    // slot mode: the insertion hashes subtree-local ids
+    if (p.member_tie && m.pt != kNone) m.pt = p.member_tie[m.moff + m.r0 + t];
+    if (p.leader_tie && m.lid != kNone) m.lid = p.leader_tie[m.loff + t];
   }
 }
 
-template <uint32_t NB>
+template <uint32_t NB, bool SLOTS>
 __global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p) {
   using G = Geom<NB>;
   static_assert(sizeof(MetaSlot<NB>) == G::kMeta, "metadata slot size");
@@ -428,7 +482,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p
             const float df = __int2float_rn((int)v[j]);
             float d = p.fused ? __fmaf_rn(-tt, df, nn) : __fsub_rn(nn, __fmul_rn(tt, df));
             if (d <= 0.0f) d = 0.0f;
-            if (lid != 0xffffffffu) insert4(d, point, lid, l, bd, bs, bl);
+            if (lid != 0xffffffffu) {
+              if constexpr (SLOTS)
+                insertn(d, point, lid, l, rh, bd, bs, bl);
+              else
+                insert4(d, point, lid, l, bd, bs, bl);
+            }
           }
         }
       }
@@ -441,8 +500,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p
             atomicOr(p.err_word, TESSA_DEVERR_BAD_TASK);
             continue;
           }
-          p.out_ids[out + j] = m.lg[bs[j]];
-          p.out_dists[out + j] = bd[j];
+          if constexpr (SLOTS) {
+            p.out_slots[out + j] = bs[j];
+            if (p.out_dists) p.out_dists[out + j] = bd[j];
+          } else {
+            p.out_ids[out + j] = m.lg[bs[j]];
+            p.out_dists[out + j] = bd[j];
+          }
         }
       }
       tc_fence_before();
@@ -491,16 +555,22 @@ __global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p
   }
 }
 
-template <uint32_t NB>
-static int launch_nb(const Params& prm, int sm_count, cudaStream_t stream) {
+template <uint32_t NB, bool SLOTS>
+static int launch_nb_mode(const Params& prm, int sm_count, cudaStream_t stream) {
   const uint32_t smem = Geom<NB>::kSmem;
-  if (cudaFuncSetAttribute(assign_tc_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (cudaFuncSetAttribute(assign_tc_kernel<NB, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return TESSA_ERR_CUDA;
   const uint32_t cap = (uint32_t)sm_count;  // one CTA per SM
   const uint32_t grid = prm.num_work < cap ? prm.num_work : cap;
-  assign_tc_kernel<NB><<<grid, kThreadsTc, smem, stream>>>(prm);
+  assign_tc_kernel<NB, SLOTS><<<grid, kThreadsTc, smem, stream>>>(prm);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+}
+
+template <uint32_t NB>
+static int launch_nb(const Params& prm, int sm_count, cudaStream_t stream) {
+  return prm.out_slots ? launch_nb_mode<NB, true>(prm, sm_count, stream)
+                       : launch_nb_mode<NB, false>(prm, sm_count, stream);
 }
 
 }  // namespace tc

@@ -267,6 +267,7 @@ struct tessa_ctx {
   DevBuf e_starts, e_sizes;  // leaf layout of an edge-hash call
   cudaEvent_t d0_ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // phase boundaries of a D0 call
   tessa_d0_profile d0_prof = {};
+  SubtreeState* subtree = nullptr;  // subtree partition scratch (created on first use)
 };
 
 namespace {
@@ -747,6 +748,7 @@ const char* tessa_strerror(int code) {
     case TESSA_ERR_NONFINITE: return "non-finite input";
     case TESSA_ERR_NO_DEVICE: return "no usable sm_100 device";
     case TESSA_ERR_BAD_TASK: return "malformed task descriptor";
+    case TESSA_ERR_PARTITION: return "subtree partition cannot finish";
     default: return "unknown error";
   }
 }
@@ -797,6 +799,8 @@ void tessa_destroy(tessa_ctx* ctx) {
                     &ctx->d0_dists, &ctx->d0_lvec, &ctx->d0_lids, &ctx->d0_child, &ctx->d0_point,
                     &ctx->e_starts, &ctx->e_sizes};
   for (DevBuf* b : bufs) b->release();
+  subtree_state_free(ctx->subtree);
+  ctx->subtree = nullptr;
   for (cudaStream_t s : {ctx->stream_in, ctx->stream_out})
     if (s) {
       cudaStreamSynchronize(s);
@@ -1399,3 +1403,56 @@ void tessa_replay_session_destroy(tessa_replay_session* s) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------ subtree partition
+
+int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* a, tessa_subtree_result* result, void* stream) {
+  TRY(bind(ctx));
+  if (!a || !result) return fail(TESSA_ERR_INVALID_ARG, "null subtree arguments");
+  if (a->padded_dim == 0 || a->padded_dim % 16 != 0)
+    return fail(TESSA_ERR_INVALID_ARG, "padded_dim=%u must be a positive multiple of 16", a->padded_dim);
+  if (a->task_count && (!a->task_offsets || !a->task_counts || !a->task_seeds || !a->task_members))
+    return fail(TESSA_ERR_INVALID_ARG, "null task arrays");
+  if (!a->codes || !a->scales || !a->sq8_norms || !a->leaf_rows || !a->leaf_starts || !a->leaf_sizes)
+    return fail(TESSA_ERR_INVALID_ARG, "null data or output pointer");
+  if (a->leaf_max == 0 || a->leaf_min == 0 || a->max_depth == 0 || a->max_leaders < 2)
+    return fail(TESSA_ERR_INVALID_ARG, "leaf_max, leaf_min, max_depth must be positive and max_leaders >= 2");
+  if (a->fanout_second == 0 || a->fanout_second > TESSA_MAX_RH)
+    return fail(TESSA_ERR_INVALID_ARG, "fanout_second=%u outside 1..4 (GPU_PERSISTENT_FANOUT_OVER_32)",
+                a->fanout_second);
+  if (a->small_node_limit > 4096 || a->small_node_limit < 2)
+    return fail(TESSA_ERR_UNSUPPORTED, "small_node_limit=%u outside 2..4096", a->small_node_limit);
+  if (a->leaf_max > a->small_node_limit)
+    return fail(TESSA_ERR_UNSUPPORTED, "leaf_max=%u above small_node_limit=%u (GPU_PERSISTENT_QUEUE_ROW_OVERFLOW)",
+                a->leaf_max, a->small_node_limit);
+  if (!(a->psamp_fraction > 0.0f) || !(a->psamp_fraction <= 1.0f))
+    return fail(TESSA_ERR_INVALID_ARG, "psamp_fraction outside (0, 1]");
+  if (a->resident_rows > 0xffffffffull) return fail(TESSA_ERR_UNSUPPORTED, "resident rows beyond 2^32");
+  if ((uint64_t)a->fanout_second * a->member_rows >= 0xfffffff0ull)
+    return fail(TESSA_ERR_UNSUPPORTED, "fanout_second * member_rows beyond 2^32");
+  uint64_t total = 0;
+  for (uint32_t t = 0; t < a->task_count; ++t) {
+    if (a->task_offsets[t] + a->task_counts[t] > a->member_rows)
+      return fail(TESSA_ERR_INVALID_ARG, "subtree task %u rows outside task_members", t);
+    total += a->task_counts[t];
+  }
+  (void)total;
+  if (!ctx->subtree) {
+    ctx->subtree = subtree_state_new();
+    if (!ctx->subtree) return fail(TESSA_ERR_OOM, "subtree state allocation failed");
+  }
+  cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+  TRY(clear_err(ctx, st));
+  SubtreeStats stats{};
+  const int rc = subtree_partition(ctx->subtree, *a, &stats, ctx->d_err.as<uint32_t>(), ctx->sm_count,
+                                   ctx->timeout_ns, st);
+  if (rc != TESSA_OK) return rc;
+  result->leaf_count = stats.leaf_count;
+  result->leaf_rows_used = stats.leaf_rows_used;
+  result->rounds = stats.rounds;
+  result->large_assignments = stats.large_assignments;
+  result->retries = stats.retries;
+  result->balanced = stats.balanced;
+  result->small_nodes = stats.small_nodes;
+  return TESSA_OK;
+}

@@ -4,6 +4,8 @@
 #include <stdint.h>
 #include <cuda_runtime.h>
 
+#include "../../include/tessa_sm100.h"
+
 namespace tessa {
 
 struct LeafLaunch {
@@ -140,6 +142,15 @@ struct Params {
   float* out_dists;
   uint32_t* err_word;
   uint64_t timeout_ns = 2000000000ull;  // bound of every wait in the tensor-core kernel
+  // Slot mode (the subtree partition, SQ8 tensor-core kernel only): when
+  // out_slots is set, each row keeps a list of t_rh[task] slots (not four),
+  // the insertion's tie keys hash member_tie / leader_tie (parallel to
+  // members / leaders: subtree-local ids) instead of the resident rows, and
+  // the result is the leader slot index per rank in out_slots (out_dists is
+  // written when non-null, out_ids is not used).
+  const uint32_t* member_tie = nullptr;
+  const uint32_t* leader_tie = nullptr;
+  uint32_t* out_slots = nullptr;
 };
 }  // namespace assign
 
@@ -148,6 +159,17 @@ struct Params {
 // kernel.
 int launch_assign(const assign::Params& prm, bool sq8, uint32_t max_leaders, int sm_count, cudaStream_t stream);
 int launch_assign_sq8_tc(const assign::Params& prm, uint32_t max_leaders, int sm_count, cudaStream_t stream);
+
+// Recursive subtree partition (subtree.cu); scratch owned by the context.
+struct SubtreeState;
+SubtreeState* subtree_state_new();
+void subtree_state_free(SubtreeState* s);
+struct SubtreeStats {
+  uint64_t leaf_count, leaf_rows_used;
+  uint32_t rounds, large_assignments, retries, balanced, small_nodes;
+};
+int subtree_partition(SubtreeState* s, const tessa_subtree_args& a, SubtreeStats* stats, uint32_t* d_err,
+                      int sm_count, uint64_t timeout_ns, cudaStream_t stream);
 
 // Records `code` and `message` as the calling thread's last error (returned by
 // tessa_last_error_message); returns `code`.

@@ -482,3 +482,72 @@ def membership_digests(ids, leaf_starts, leaf_sizes, global_ids=None, ctx: Conte
                                               _stream_ptr(torch, ids.device.index)))
     d = out[:, :n].cpu().numpy().view(np.uint64)
     return np.stack([sizes.astype(np.uint64), d[0], d[1]], axis=1)
+
+
+# -------------------------------------------------------- subtree partition
+
+class SubtreeParams:
+    """Persistent-subtree plan values (CB:1309-1340 with the PiPNNParams
+    defaults of P/params.rs:3342-3368): leaf_max = max(256, c_max), leaf_min 64,
+    max_depth 10, max_leaders min(1000, 128), fanout_second 3, root_depth 1
+    (D1+ tasks), small_node_limit 4096, psamp_fraction 0.001."""
+
+    def __init__(self, c_max=2048, leaf_min=64, max_depth=10, max_leaders=1000, fanout_second=3, root_depth=1,
+                 small_node_limit=4096, psamp_fraction=0.001):
+        self.leaf_max = max(256, int(c_max))
+        self.leaf_min = int(leaf_min)
+        self.max_depth = int(max_depth)
+        self.max_leaders = min(int(max_leaders), 128)
+        self.fanout_second = int(fanout_second)
+        self.root_depth = int(root_depth)
+        self.small_node_limit = int(small_node_limit)
+        self.psamp_fraction = float(psamp_fraction)
+
+    def as_array(self):
+        return np.array([self.leaf_max, self.leaf_min, self.max_depth, self.max_leaders, self.fanout_second,
+                         self.root_depth, self.small_node_limit], np.uint32)
+
+
+def subtree_root_seed(random_seed: int, depth: int, rows: int, parent_points: int, min_recurse_size: int) -> int:
+    """gpu_queue_root_seed (CB:1597-1603)."""
+    def rotl(v, r):
+        v &= (1 << 64) - 1
+        return ((v << r) | (v >> (64 - r))) & ((1 << 64) - 1)
+    return (random_seed ^ ((depth * 0x9E3779B97F4A7C15) & ((1 << 64) - 1)) ^ rotl(rows, 17)
+            ^ rotl(parent_points, 7) ^ rotl(min_recurse_size, 29)) & ((1 << 64) - 1)
+
+
+def subtree_partition(codes, scales, norms, task_members, task_offsets, task_counts, task_seeds,
+                      params: SubtreeParams | None = None, ctx: Context | None = None):
+    """tessa_subtree_partition on device tensors (codes/scales/norms/task_members);
+    task arrays are host sequences.  Returns (leaf_rows device int32 tensor of the
+    used extent, leaf_starts u64, leaf_sizes u32, leaf_tasks u32, stats dict)."""
+    import torch
+
+    prm = params or SubtreeParams()
+    dev = codes.device.index
+    ctx = ctx or context(dev)
+    toff = np.ascontiguousarray(task_offsets, np.uint64)
+    tcnt = np.ascontiguousarray(task_counts, np.uint32)
+    tseed = np.ascontiguousarray(task_seeds, np.uint64)
+    member_rows = int(task_members.numel())
+    cap = max(prm.fanout_second, 1) * member_rows + 16
+    leaf_rows = torch.empty(cap, dtype=torch.int32, device=codes.device)
+    starts = np.zeros(cap, np.uint64)
+    sizes = np.zeros(cap, np.uint32)
+    tasks = np.zeros(cap, np.uint32)
+    a = C.SubtreeArgs(codes=codes.data_ptr(), scales=scales.data_ptr(), sq8_norms=norms.data_ptr(),
+                      resident_rows=codes.shape[0], padded_dim=codes.shape[1], task_members=task_members.data_ptr(),
+                      member_rows=member_rows, task_offsets=toff.ctypes.data, task_counts=tcnt.ctypes.data,
+                      task_seeds=tseed.ctypes.data, task_count=tcnt.size, leaf_max=prm.leaf_max,
+                      leaf_min=prm.leaf_min, max_depth=prm.max_depth, max_leaders=prm.max_leaders,
+                      fanout_second=prm.fanout_second, root_depth=prm.root_depth,
+                      small_node_limit=prm.small_node_limit, psamp_fraction=prm.psamp_fraction,
+                      leaf_rows=leaf_rows.data_ptr(), leaf_rows_capacity=cap, leaf_starts=starts.ctypes.data,
+                      leaf_sizes=sizes.ctypes.data, leaf_tasks=tasks.ctypes.data, leaf_capacity=cap)
+    r = C.SubtreeResult()
+    C.check(C.load().tessa_subtree_partition(ctx.handle, ctypes.byref(a), ctypes.byref(r), _stream_ptr(torch, dev)))
+    n = int(r.leaf_count)
+    stats = {f: int(getattr(r, f)) for f in ("rounds", "large_assignments", "retries", "balanced", "small_nodes",
+                                             "leaf_rows_used")}
+    return leaf_rows[:int(r.leaf_rows_used)], starts[:n].copy(), sizes[:n].copy(), tasks[:n].copy(), stats
