@@ -463,6 +463,33 @@ typedef struct tessa_subtree_result {
 TESSA_API int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* args, tessa_subtree_result* result,
                                       void* stream);
 
+/* ---------------------------------------------------- host reduction --- */
+
+/* HashPrune reservoirs on the host (HashPruneReservoir,
+ * P/hash_prune.rs:269-1452), the CPU-side reduction SHEAR feeds its leaf
+ * candidate records into.  One reservoir of at most l_max slots per point
+ * (l_max <= 255; PiPNNParams l_max 64); `threads` host threads (0 = 1).
+ * Host pointers throughout.  A reducer is not thread-safe. */
+typedef struct tessa_reducer tessa_reducer;
+TESSA_API int tessa_reducer_create(uint64_t num_points, uint32_t l_max, uint32_t threads, tessa_reducer** out);
+/* One CompactTopKBatch (P/leaf_build.rs:271-290) flushed as
+ * flush_compact_topk_batch_into_edges forms its edges (P/leaf_build.rs:
+ * 1749-1808): for row i and rank r with id j != 0xffffffff and a finite
+ * distance d, (point_ids[i] -> j, hash_fwd, d) then (j -> point_ids[i],
+ * hash_rev, d), each inserted with insert_inner (P/hash_prune.rs:1326-1452).
+ * Ids at or above num_points are TESSA_ERR_BAD_ROW. */
+TESSA_API int tessa_reducer_add(tessa_reducer* reducer, const uint32_t* point_ids, const uint32_t* topk_ids,
+                                const float* topk_dists, const uint16_t* hash_fwd, const uint16_t* hash_rev,
+                                uint64_t rows, uint32_t k);
+/* Final neighbour lists, each point's slot targets in hash order (the
+ * resident emit with backfill off, P/mod.rs:2437-2478), as CSR: offsets
+ * (num_points + 1 entries) and neighbors (capacity entries; NULL to size). */
+TESSA_API int tessa_reducer_finish(const tessa_reducer* reducer, uint64_t* offsets, uint32_t* neighbors,
+                                   uint64_t capacity, uint64_t* count);
+/* Edges inserted so far (forward and reverse). */
+TESSA_API int tessa_reducer_edges(const tessa_reducer* reducer, uint64_t* edges);
+TESSA_API void tessa_reducer_destroy(tessa_reducer* reducer);
+
 /* TessaCudaModeResult (P/tessa_replay.rs:190-200); caller-owned host buffers
  * of assignment_output_len and leaf_rows*leaf_k entries.  leaf_* may be NULL
  * for modes that replay no leaf tasks. */

@@ -551,3 +551,55 @@ def subtree_partition(codes, scales, norms, task_members, task_offsets, task_cou
     stats = {f: int(getattr(r, f)) for f in ("rounds", "large_assignments", "retries", "balanced", "small_nodes",
                                              "leaf_rows_used")}
     return leaf_rows[:int(r.leaf_rows_used)], starts[:n].copy(), sizes[:n].copy(), tasks[:n].copy(), stats
+
+
+# ---------------------------------------------------------- host reduction
+
+class Reducer:
+    """HashPrune reservoirs on the host (tessa_reducer_*): add leaf batches
+    (numpy arrays), then finish() -> CSR (offsets u64 [n+1], neighbors u32)."""
+
+    def __init__(self, num_points: int, l_max: int = 64, threads: int = 0):
+        import os
+        self.handle = ctypes.c_void_p()
+        self.lib = C.load()
+        threads = threads or min(64, os.cpu_count() or 1)
+        C.check(self.lib.tessa_reducer_create(num_points, l_max, threads, ctypes.byref(self.handle)))
+        self.num_points = num_points
+
+    def add(self, point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, k: int):
+        pid = np.ascontiguousarray(point_ids).view(np.uint32).reshape(-1)
+        ids = np.ascontiguousarray(topk_ids).view(np.uint32).reshape(-1)
+        ds = np.ascontiguousarray(topk_dists, np.float32).reshape(-1)
+        hf = np.ascontiguousarray(hash_fwd).view(np.uint16).reshape(-1)
+        hr = np.ascontiguousarray(hash_rev).view(np.uint16).reshape(-1)
+        rows = pid.shape[0]
+        if ids.shape[0] != rows * k or ds.shape[0] != rows * k or hf.shape[0] != rows * k or hr.shape[0] != rows * k:
+            raise ValueError("reducer inputs must hold rows * k slots")
+        C.check(self.lib.tessa_reducer_add(self.handle, _np_ptr(pid), _np_ptr(ids), _np_ptr(ds), _np_ptr(hf),
+                                           _np_ptr(hr), rows, k))
+
+    def edges(self) -> int:
+        n = ctypes.c_uint64()
+        C.check(self.lib.tessa_reducer_edges(self.handle, ctypes.byref(n)))
+        return int(n.value)
+
+    def finish(self):
+        offsets = np.zeros(self.num_points + 1, np.uint64)
+        n = ctypes.c_uint64()
+        C.check(self.lib.tessa_reducer_finish(self.handle, _np_ptr(offsets), None, 0, ctypes.byref(n)))
+        nb = np.zeros(max(int(n.value), 1), np.uint32)
+        C.check(self.lib.tessa_reducer_finish(self.handle, _np_ptr(offsets), _np_ptr(nb), nb.shape[0],
+                                              ctypes.byref(n)))
+        return offsets, nb[:int(n.value)]
+
+    def close(self):
+        if self.handle:
+            self.lib.tessa_reducer_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
