@@ -82,6 +82,9 @@ def _declare(L):
                                 _p(np.uint32), _p(np.uint64), u32, _p(np.uint32), _p(np.float32)]
     L.oracle_num_threads.restype = ctypes.c_int
     L.oracle_set_num_threads.argtypes = [ctypes.c_int]
+    L.oracle_slot_hashes.restype = None
+    L.oracle_slot_hashes.argtypes = [_p(np.uint32), _p(np.uint32), u64, u32, _p(np.float32), u32, u32,
+                                     _p(np.uint16), _p(np.uint16)]
     L.oracle_adaptive_psamp.restype = f32
     L.oracle_adaptive_psamp.argtypes = [f32, u32, u32]
     L.oracle_subtree_partition.restype = i64
@@ -304,3 +307,14 @@ def subtree_partition(codes, scales, norms, members, task_offsets, task_counts, 
     keys = ["rounds", "large_assignments", "retries", "balanced", "small_nodes"]
     return rows[:used].copy(), starts[:n].copy(), sizes[:n].copy(), tasks[:n].copy(), \
         dict(zip(keys, (int(v) for v in stats)))
+
+
+def slot_hashes(point_ids, topk_ids, k, sketches, m_bits):
+    """(hash_fwd, hash_rev) uint16 of every leaf slot (P/leaf_build.rs:1749-1808)."""
+    pid = np.ascontiguousarray(point_ids, np.uint32)
+    ids = np.ascontiguousarray(topk_ids).view(np.uint32).reshape(-1)
+    sk = np.ascontiguousarray(sketches, np.float32)
+    hf = np.zeros(ids.size, np.uint16)
+    hr = np.zeros(ids.size, np.uint16)
+    lib().oracle_slot_hashes(pid, ids, pid.size, k, sk.reshape(-1), sk.shape[1], m_bits, hf, hr)
+    return hf, hr

@@ -356,6 +356,29 @@ uint64_t oracle_flush_edges(const uint32_t* point_ids, const uint32_t* topk_ids,
     return e;
 }
 
+/*
+ * Both hashes of every (row, rank) slot (the inputs flush_compact_topk_batch_into_edges
+ * computes per edge, P/leaf_build.rs:1749-1808): hash_fwd = compute_hash(s_i, s_j),
+ * hash_rev = compute_hash(s_j, s_i), i = point_ids[row], j = topk_ids[row*k+rank];
+ * 0 for empty slots.
+ */
+void oracle_slot_hashes(const uint32_t* point_ids, const uint32_t* topk_ids, uint64_t rows, uint32_t k,
+                        const float* sketches, uint32_t width, uint32_t m_bits, uint16_t* hash_fwd,
+                        uint16_t* hash_rev) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)rows; ++i) {
+        const float* si = sketches + (uint64_t)point_ids[i] * width;
+        for (uint32_t r = 0; r < k; ++r) {
+            uint64_t s = (uint64_t)i * k + r;
+            uint32_t j = topk_ids[s];
+            if (j == EMPTY_ID) { hash_fwd[s] = 0; hash_rev[s] = 0; continue; }
+            const float* sj = sketches + (uint64_t)j * width;
+            hash_fwd[s] = (uint16_t)oracle_compute_hash(si, sj, m_bits);
+            hash_rev[s] = (uint16_t)oracle_compute_hash(sj, si, m_bits);
+        }
+    }
+}
+
 /* --------------------------------------------------------- assignment --- */
 
 /* CB:5983-5989 gpu_persistent_hash64 (splitmix64 finaliser). */

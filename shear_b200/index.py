@@ -1,0 +1,214 @@
+"""GPU-subtree index build on one B200: the construction path of
+``build_shear_index`` (apps/build_shear_index) with SHEAR's gpu-subtree
+partitioner, on libtessa_sm100.so.
+
+Reference flow (shear-core/src/algorithm/pipnn/, Rust):
+  D0 preflight (rbc_partition.rs:7332): root leaders, every point assigned to
+    its fanout_top nearest (quantize_sq8_and_assign_global_d0,
+    compute_backend.rs:3828-3837), one child run per root leader;
+  D1+ producer (rbc_partition.rs:9602, :13247): each child run is a subtree
+    task, partitioned recursively and evaluated leaf by leaf by the persistent
+    kernel (compute_backend.rs:16336-17381) into CompactTopKBatch records;
+  host reduction: records flushed into candidate edges with sketch hashes
+    (leaf_build.rs:1604-1829) and reduced by HashPrune reservoirs
+    (hash_prune.rs:1243-1452); the reservoirs are the graph
+    (mod.rs:2437-2478), entry point the first point of the largest child run
+    (rbc_partition.rs:4940-4962).
+
+Here: D0 = tessa_quantize_sq8_assign_d0 (rectangular tcgen05 kernel), child
+runs grouped on the device, all subtree tasks partitioned in one
+tessa_subtree_partition call, leaves through tessa_leaf_topk_sq8, hashes
+through tessa_sketch_rows / tessa_edge_hashes, records copied to pinned host
+memory and reduced by the host reducer (tessa_reducer_*).
+
+Two inputs the reference draws from Rust's StdRng (rand 0.9, ChaCha12),
+which cannot be reproduced outside Rust, come from seeded numpy generators
+here: the root leader sample and the sketch hyperplanes
+(generate_hyperplanes, hash_prune.rs:2196-2206).  Everything after them is
+deterministic and restated exactly.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import ops
+from . import task_former as TF
+
+
+@dataclass
+class BuildParams:
+    """The PiPNNParams fields this path reads (P/params.rs:3342-3490 defaults)."""
+    c_max: int = 2048
+    leaf_knn: int = 2
+    l_max: int = 64
+    m_hash_bits: int = 12
+    fanout_top: int = 10
+    fanout_second: int = 3
+    max_leaders: int = 1000
+    max_depth: int = 10
+    psamp_fraction: float = 0.001
+    random_seed: int = 42
+    root_leaders: int | None = None        # None: the D0 capacity plan decides
+    workspace_bytes: int | None = None     # None: 90% of the device
+    reducer_threads: int = 0
+
+    def adaptive_c_max(self, n: int) -> int:
+        """P/params.rs:3005-3015."""
+        return self.c_max * 2 if n >= 5_000_000 else self.c_max
+
+
+@dataclass
+class BuildResult:
+    offsets: np.ndarray                    # CSR of the graph: uint64 [n + 1]
+    neighbors: np.ndarray                  # uint32
+    entry_point: int
+    timings: dict = field(default_factory=dict)
+    stats: dict = field(default_factory=dict)
+
+    def degree_stats(self):
+        deg = np.diff(self.offsets.astype(np.int64))
+        return {"mean": float(deg.mean()), "max": int(deg.max()), "min": int(deg.min())}
+
+
+def root_leader_count(n: int, dim: int, p: BuildParams, device_bytes: int | None) -> tuple[int, dict]:
+    """D0 capacity plan (P/d0_capacity.rs:55-257, restated in task_former): the
+    largest admissible subtree for the workspace, its thresholds, and the root
+    leader count for n points at fanout_top."""
+    if p.root_leaders is not None:
+        return int(p.root_leaders), {"source": "fixed"}
+    cfg = TF.D0CapacityConfig()
+    budget = p.workspace_bytes if p.workspace_bytes is not None else (
+        TF.b200_workspace_budget(device_bytes) if device_bytes else None)
+    c_gpu = TF.find_max_admissible_rows(dim, p.leaf_knn, p.fanout_second, budget) if budget else n * p.fanout_top
+    thr = TF.compute_thresholds(max(c_gpu, 1), cfg)
+    plan = TF.plan_root_leaders(n, p.fanout_top, thr, cfg)
+    count = min(plan.k_initial, p.max_leaders, n)
+    return int(count), {"source": plan.root_leader_source, "c_gpu": int(c_gpu), "k_capacity": int(plan.k_capacity)}
+
+
+def sample_root_leaders(n: int, count: int, seed: int) -> np.ndarray:
+    """Root leader rows (ascending); a seeded stand-in for the reference's
+    StdRng sample (rbc_partition.rs:18041-18058)."""
+    rng = np.random.default_rng(seed)
+    return np.sort(rng.choice(n, size=count, replace=False)).astype(np.uint32)
+
+
+def hyperplanes(m: int, dim: int, seed: int) -> np.ndarray:
+    """m x dim N(0,1) hyperplanes (generate_hyperplanes, hash_prune.rs:2196-2206;
+    seeded numpy stand-in for StdRng)."""
+    rng = np.random.default_rng(seed ^ 0x5EED)
+    return rng.standard_normal((m, dim)).astype(np.float32)
+
+
+def child_seed_args(p: BuildParams, n: int):
+    """gpu_queue_root_seed inputs (compute_backend.rs:1597-1603) of a D1 task:
+    depth 1, parent_points = n, min_recurse_size = 2 * adaptive_c_max
+    (rbc_partition.rs:7375-7376)."""
+    return 1, n, 2 * p.adaptive_c_max(n)
+
+
+def group_child_runs(child_ids, num_leaders: int):
+    """D0 fragments -> child runs: for leader j the rows that chose it, ascending
+    (the order in which the D0 pass appends rows to child runs).  child_ids is
+    a CUDA int32 tensor [n, fanout]; returns (members CUDA int32, counts,
+    offsets) with the counts / offsets on the host."""
+    import torch
+
+    n, f = child_ids.shape
+    keys = child_ids.reshape(-1).to(torch.int64)
+    order = torch.argsort(keys, stable=True)
+    members = (order // f).to(torch.int32)
+    counts = torch.bincount(keys, minlength=num_leaders).cpu().numpy().astype(np.uint32)
+    offsets = np.concatenate([[0], np.cumsum(counts, dtype=np.uint64)[:-1]]).astype(np.uint64)
+    return members, counts, offsets
+
+
+def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> BuildResult:
+    """Build the graph of x (numpy f32 [n, dim] on the host -- copied to the
+    device inside -- or a CUDA f32 tensor already resident)."""
+    import torch
+
+    p = p or BuildParams()
+    dev = torch.device("cuda", device)
+    ctx = ctx or ops.context(device)
+    timings = {}
+    sync = lambda: torch.cuda.synchronize(dev)
+    t_all = time.perf_counter()
+    if isinstance(x, np.ndarray):
+        xh = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+        xd = xh.pin_memory().to(dev, non_blocking=True) if xh.numel() else xh.to(dev)
+    else:
+        xd = x.contiguous()
+    n, dim = xd.shape
+    sync()
+    timings["upload_s"] = time.perf_counter() - t_all
+
+    # ---- D0: SQ8 codes of every row and its fanout_top root leaders
+    t = time.perf_counter()
+    props = torch.cuda.get_device_properties(dev)
+    k0, plan = root_leader_count(n, dim, p, props.total_memory)
+    fanout = min(p.fanout_top, k0)
+    leaders = sample_root_leaders(n, k0, p.random_seed)
+    lid = torch.from_numpy(leaders.view(np.int32)).to(dev)
+    gids = torch.arange(n, dtype=torch.int32, device=dev)
+    d0 = ops.quantize_sq8_assign_d0(xd, gids, lid, fanout, leader_vectors=xd[lid.long()], ctx=ctx)
+    members, counts, offsets = group_child_runs(d0.child_ids, k0)
+    sync()
+    timings["d0_s"] = time.perf_counter() - t
+
+    # ---- subtree partition of every child run
+    t = time.perf_counter()
+    depth, parent, min_rec = child_seed_args(p, n)
+    seeds = np.array([ops.subtree_root_seed(p.random_seed, depth, int(c), parent, min_rec) for c in counts],
+                     np.uint64)
+    sp = ops.SubtreeParams(c_max=p.adaptive_c_max(n), max_depth=p.max_depth, max_leaders=p.max_leaders,
+                           fanout_second=p.fanout_second, root_depth=depth, psamp_fraction=p.psamp_fraction)
+    leaf_rows, starts, sizes, tasks, pst = ops.subtree_partition(d0.codes, d0.scales, d0.norms, members, offsets,
+                                                                 counts, seeds, sp, ctx=ctx)
+    sync()
+    timings["partition_s"] = time.perf_counter() - t
+
+    # ---- leaf top-k and edge hashes
+    t = time.perf_counter()
+    k = max(1, min(p.leaf_knn, 32))
+    rows = int(leaf_rows.numel())
+    ids = torch.full((rows * k,), -1, dtype=torch.int32, device=dev)
+    dists = torch.full((rows * k,), float("inf"), dtype=torch.float32, device=dev)
+    ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, gids, leaf_rows, starts, sizes, k, out=(ids, dists), ctx=ctx)
+    planes = torch.from_numpy(hyperplanes(p.m_hash_bits, dim, p.random_seed)).to(dev)
+    sketches = ops.sketch_rows(xd, planes, ctx=ctx)
+    hf, hr = ops.edge_hashes(leaf_rows, ids, k, sketches, p.m_hash_bits, starts, sizes, ctx=ctx)
+    sync()
+    timings["leaf_s"] = time.perf_counter() - t
+
+    # ---- candidate records to pinned host memory, host reduction
+    t = time.perf_counter()
+    def pin(v):
+        h = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
+        h.copy_(v, non_blocking=True)
+        return h
+    h_rows, h_ids, h_d, h_hf, h_hr = (pin(leaf_rows), pin(ids), pin(dists), pin(hf), pin(hr))
+    sync()
+    timings["d2h_s"] = time.perf_counter() - t
+    t = time.perf_counter()
+    red = ops.Reducer(n, p.l_max, p.reducer_threads)
+    red.add(h_rows.numpy(), h_ids.numpy(), h_d.numpy(), h_hf.numpy(), h_hr.numpy(), k)
+    offs, nb = red.finish()
+    edges = red.edges()
+    red.close()
+    timings["reduce_s"] = time.perf_counter() - t
+    timings["total_s"] = time.perf_counter() - t_all
+
+    # entry point: first row of the largest child run (last one among equals)
+    big = int(len(counts) - 1 - np.argmax(counts[::-1]))
+    entry = int(members[int(offsets[big])].item()) if counts[big] else 0
+    stats = dict(points=n, dim=dim, root_leaders=k0, root_plan=plan, fanout_top=fanout,
+                 child_rows=int(counts.sum()), leaves=int(sizes.size), leaf_rows=int(sizes.sum()),
+                 leaf_rows_mean=float(sizes.mean()) if sizes.size else 0.0, leaf_k=k, edges=edges,
+                 leaf_pairs=int((sizes.astype(np.int64) * (sizes.astype(np.int64) - 1)).sum()),
+                 leaf_ops=int(2 * d0.codes.shape[1] * (sizes.astype(np.int64) ** 2).sum()),
+                 partition=pst)
+    return BuildResult(offs, nb, entry, timings, stats)
