@@ -56,9 +56,15 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["leaf", "d0", "edges", "assign"], default="leaf",
-                    help="leaf = the north-star leaf replay (default); d0 = global-D0 SQ8 staging; "
+    ap.add_argument("--workload", choices=["build", "leaf", "d0", "edges", "assign"], default="build",
+                    help="build = GPU-subtree index build, BASELINE config 3 (default) or 1 (--config 1); "
+                         "leaf = the config-2 leaf-operator replay; d0 = global-D0 SQ8 staging; "
                          "edges = candidate-edge hashes + host expansion of the leaf lists")
+    ap.add_argument("--config", type=int, choices=[1, 3], default=3, help="build: BASELINE config")
+    ap.add_argument("--rows", type=int, default=0, help="build: base rows (0 = the config's)")
+    ap.add_argument("--queries", type=int, default=0, help="build: recall queries (0 = the config's)")
+    ap.add_argument("--cpu-rows", type=int, default=0, help="build: rows of the CPU-baseline sample (0 = auto)")
+    ap.add_argument("--no-recall", action="store_true")
     ap.add_argument("--hash-bits", type=int, default=12, help="edges: m_hash_bits (params.rs default 12)")
     ap.add_argument("--assign-leaders", type=int, default=16, help="assign: leaders per task (replay contract)")
     ap.add_argument("--assign-rh", type=int, default=2, help="assign: r_h (replay contract)")
@@ -1116,8 +1122,282 @@ def run_assign(a):
     return 0
 
 
+# ----------------------------------------------------------------- build (configs 1 and 3)
+
+BUILD_METRIC = "build vectors/sec"
+BUILD_CONFIGS = {
+    # 200k x 128 GMM (64 components, centres N(0,1), isotropic sigma 0.3,
+    # seed 0), L2, leaf size 1024, degree 64, recall@10 on 1,000 queries (seed 1)
+    1: dict(rows=200_000, dim=128, comps=64, aniso=False, unit=False, sigma=0.3, queries=1000, c_max=1024),
+    # 1M x 768 L2-normalised, 1,024-component anisotropic GMM (diagonal
+    # sigma ~ U[0.05, 0.5]), inner product on unit vectors = L2 order, degree 64, 10,000 queries
+    3: dict(rows=1_000_000, dim=768, comps=1024, aniso=True, unit=True, sigma=None, queries=10_000, c_max=2048),
+}
+
+
+def build_cfg(a):
+    c = dict(BUILD_CONFIGS[a.config])
+    if a.rows:
+        c["rows"] = a.rows
+    if a.queries:
+        c["queries"] = a.queries
+    return c
+
+
+def build_desc(a, c):
+    return {"workload": f"GPU-subtree index build, BASELINE config {a.config}: {c['rows']} x {c['dim']} "
+                        f"{'L2-normalised ' if c['unit'] else ''}{c['comps']}-component "
+                        f"{'anisotropic' if c['aniso'] else 'isotropic'} Gaussian mixture, leaf size "
+                        f"{c['c_max']}, degree 64, recall@10 on {c['queries']} queries",
+            "rows": c["rows"], "dim": c["dim"], "c_max": c["c_max"], "leaf_knn": 2, "l_max": 64,
+            "fanout_top": 10, "fanout_second": 3,
+            "l2": "inputs larger than L2 (%.2f GB of rows); no flush" % (c["rows"] * c["dim"] * 4 / 1e9)}
+
+
+def make_mixture_np(n, c, seed, centre_seed=0):
+    """The config's mixture on the host (numpy), same procedure as make_mixture."""
+    rng = np.random.default_rng(centre_seed)
+    centres = rng.standard_normal((c["comps"], c["dim"])).astype(np.float32)
+    sig = (rng.random((c["comps"], c["dim"])) * 0.45 + 0.05).astype(np.float32) if c["aniso"] else None
+    r2 = np.random.default_rng(seed)
+    comp = r2.integers(0, c["comps"], n)
+    noise = r2.standard_normal((n, c["dim"])).astype(np.float32)
+    x = centres[comp] + (sig[comp] * noise if c["aniso"] else np.float32(c["sigma"]) * noise)
+    if c["unit"]:
+        x /= np.linalg.norm(x, axis=1, keepdims=True)
+    return np.ascontiguousarray(x, np.float32)
+
+
+def make_mixture(torch, dev, n, c, seed, centre_seed=0):
+    """Synthetic stand-in for the config's dataset on the device (centres and
+    per-component sigmas from centre_seed, draws from seed)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(centre_seed)
+    centres = torch.randn((c["comps"], c["dim"]), generator=g, device=dev)
+    sig = torch.rand((c["comps"], c["dim"]), generator=g, device=dev) * 0.45 + 0.05 if c["aniso"] else None
+    g2 = torch.Generator(device=dev)
+    g2.manual_seed(seed)
+    x = torch.empty((n, c["dim"]), dtype=torch.float32, device=dev)
+    for r0 in range(0, n, 1 << 18):
+        r1 = min(n, r0 + (1 << 18))
+        comp = torch.randint(0, c["comps"], (r1 - r0,), generator=g2, device=dev)
+        noise = torch.randn((r1 - r0, c["dim"]), generator=g2, device=dev)
+        y = centres[comp] + (sig[comp] * noise if c["aniso"] else c["sigma"] * noise)
+        if c["unit"]:
+            y /= torch.linalg.vector_norm(y, dim=1, keepdim=True)
+        x[r0:r1] = y
+    torch.cuda.synchronize(dev)
+    return x
+
+
+def build_recall(torch, x, res, queries, ls=(50, 100, 200)):
+    from shear_b200 import graph as G
+    gt, _ = G.exact_knn(x, queries, 10)
+    gt = gt.cpu().numpy()
+    xh = x.cpu().numpy()
+    qh = queries.cpu().numpy()
+    out = {}
+    for l in ls:
+        ids, comps = G.search(xh, res.offsets, res.neighbors, res.entry_point, qh, 10, l)
+        out[str(l)] = G.recall_at(ids, gt, 10)
+    return out
+
+
+def run_build(a):
+    import torch
+
+    from shear_b200 import ops
+    from shear_b200.index import BuildParams, build_index
+
+    world, rank, local = dist_env()
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ctx = ops.context(dev.index)
+    c = build_cfg(a)
+    p = BuildParams(c_max=c["c_max"])
+    # every rank builds its own index of the config's size (weak scaling: builds are independent)
+    x = make_mixture(torch, dev, c["rows"], c, seed=1234 + rank)
+    n = c["rows"]
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(a.warmup, 3)):
+        res = build_index(x, p, device=dev.index, ctx=ctx)
+    torch.cuda.synchronize(dev)
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    times, leaf_ms = [], []
+    with ClockSampler(dev.index) as clk:
+        for _ in range(a.steps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
+            s.record(stream)
+            res = build_index(x, p, device=dev.index, ctx=ctx)
+            e.record(stream)
+            torch.cuda.synchronize(dev)
+            times.append(s.elapsed_time(e) / 1e3)
+            leaf_ms.append(res.timings["leaf_kernel_ms"])
+    barrier()
+    per_step = float(np.mean(times))
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([per_step], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        per_step = float(tt[0])
+    value = world * n / per_step
+
+    # ---- e2e: host rows (pinned) -> graph on the host, through the public build call
+    e2e = None
+    if not a.no_e2e and a.e2e_steps > 0:
+        xh = x.cpu().pin_memory().numpy()
+        build_index(xh, p, device=dev.index, ctx=ctx)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(a.e2e_steps):
+            r2 = build_index(xh, p, device=dev.index, ctx=ctx)
+        e2e_s = (time.perf_counter() - t0) / a.e2e_steps
+        if world > 1:
+            import torch.distributed as dist
+            tt = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_s = float(tt[0])
+        rec_bytes = res.stats["leaf_rows"] * (4 + res.stats["leaf_k"] * 12)
+        e2e = {"value": world * n / e2e_s, "unit": "vectors/s", "h2d_bytes_per_step": int(n * c["dim"] * 4),
+               "d2h_bytes_per_step": int(rec_bytes), "ms_per_step": e2e_s * 1e3,
+               "timing": "wall clock around build_index(host numpy rows): upload, GPU stages, pinned D2H of "
+                         "the candidate records, host HashPrune reduction; graph in host memory"}
+        del xh
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    recall = None
+    if not a.no_recall:
+        q = make_mixture(torch, dev, c["queries"], c, seed=99991)
+        recall = {"at": 10, "queries": c["queries"], "by_L": build_recall(torch, x, res, q),
+                  "ground_truth": "exact f32 L2 top-10 on the GPU", "search": "greedy beam search restating "
+                  "apps/search_shear_index (tessa_graph_search, host threads)"}
+        del q
+
+    peaks = measured_peaks()
+    int8_peak = int8_peak_tops(torch, dev)
+    leaf_s = float(np.mean(leaf_ms)) / 1e3
+    achieved = res.stats["leaf_ops"] / leaf_s / 1e12
+    peak, src = (int8_peak, "measured in-run: cuBLAS int8 burst (torch._int_mm 8192^3)") if int8_peak else \
+        (NOMINAL_INT8_TOPS, "nominal B200 dense int8 4.5 POPS (no measured int8 peak)")
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
+                "traffic": None, "peak_source": src,
+                "kernel": "leaf stage of the build: tessa::leaf::split::leaf_topk_split_kernel<2> + finish "
+                          "(CUDA events around tessa_leaf_topk_sq8)",
+                "algorithmic_ops_per_launch": res.stats["leaf_ops"], "leaf_kernel_ms": leaf_s * 1e3,
+                "hbm_peak_gbs": peaks.get("hbm_gbs")}
+
+    cpu = None
+    parity = None
+    if not a.no_cpu_baseline and world == 1:
+        from oracle.cpu_build import build_index_cpu
+        O = host_oracle()
+        m = a.cpu_rows or min(n, 30000 if c["dim"] > 256 else 100000)
+        xs = x[:m].contiguous()
+        xsh = xs.cpu().numpy()
+        g = build_index(xs, p, device=dev.index, ctx=ctx)
+        t0 = time.perf_counter()
+        offs, nb, entry, tm, _ = build_index_cpu(xsh, p, g.stats["root_leaders"], threads=os.cpu_count() or 1)
+        dt = time.perf_counter() - t0
+        cpu = {"value": m / dt, "unit": "vectors/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"the CPU restatement of the same build (oracle/cpu_build.py: OpenMP C stages + the host "
+                         f"reducer) on the first {m} of the {n} rows, {dt:.1f} s"}
+        same = bool(np.array_equal(g.offsets, offs) and np.array_equal(g.neighbors, nb) and g.entry_point == entry)
+        parity = {"rows": m, "graphs_identical": same}
+        if not a.no_recall:
+            q = make_mixture(torch, dev, min(1000, c["queries"]), c, seed=99991)
+            from shear_b200.index import BuildResult
+            parity["recall10_L100_gpu"] = build_recall(torch, xs, g, q, ls=(100,))["100"]
+            parity["recall10_L100_cpu_restatement"] = build_recall(
+                torch, xs, BuildResult(offs, nb, entry), q, ls=(100,))["100"]
+
+    line = {
+        "metric": BUILD_METRIC, "value": value, "unit": "vectors/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8",
+        "data": f"synthetic stand-in for BASELINE config {a.config} (seeded Gaussian mixture on the device, seed "
+                f"1234+rank); random root leaders and sketch hyperplanes from seeded generators",
+        "config": dict(build_desc(a, c), parallelism=f"independent builds x{world} (no collective)"),
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "recall": recall, "recall_parity": parity,
+        "gpu_launches": res.stats["kernel_launches"] * a.steps,
+        "clocks": clk.summary(),
+        "phases_s": {k: round(v, 4) for k, v in res.timings.items()},
+        "build_stats": {k: v for k, v in res.stats.items() if k not in ("root_plan",)},
+        "degree": res.degree_stats(),
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_build_reference(a):
+    """The reference arm for the build: the CPU restatement of the same build
+    (oracle/cpu_build.py) on all host cores, rank 0 only, on a bounded sample
+    of the config's rows per step."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle.cpu_build import build_index_cpu
+    from shear_b200.index import BuildParams, root_leader_count
+
+    O = host_oracle()
+    c = build_cfg(a)
+    m = a.cpu_rows or min(c["rows"], 30000 if c["dim"] > 256 else 100000)
+    x = make_mixture_np(m, c, seed=1234)
+    p = BuildParams(c_max=c["c_max"])
+    k0, _ = root_leader_count(m, c["dim"], p, 183_000_000_000)
+    times = []
+    for i in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        build_index_cpu(x, p, k0, threads=os.cpu_count() or 1)
+        if i >= a.warmup:
+            times.append(time.perf_counter() - t0)
+    mean = float(np.mean(times))
+    value = m / mean
+    line = {
+        "impl": "reference", "metric": BUILD_METRIC, "value": value, "unit": "vectors/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": f"synthetic stand-in for BASELINE config {a.config} (seeded Gaussian mixture, host)",
+        "config": build_desc(a, c),
+        "cpu_baseline": {"value": value, "unit": "vectors/s", "cores": O.num_threads(), "kind": "port",
+                         "sample": f"{m} of the config's {c['rows']} rows per step"},
+        "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is Rust + NVRTC (no cargo in this image); the timed arm is its build restated on "
+                "the CPU (oracle/, OpenMP) with the host HashPrune reducer, all host cores",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = parse_args()
+    if a.workload == "build":
+        return run_build_reference(a) if a.impl == "reference" else run_build(a)
     if a.workload == "assign":
         return run_assign_reference(a) if a.impl == "reference" else run_assign(a)
     if a.workload == "edges":

@@ -454,6 +454,7 @@ typedef struct tessa_subtree_result {
   uint32_t retries;              /* large-node leader resamples (CB:15416-15478) */
   uint32_t balanced;             /* balanced even/odd fallbacks (CB:15480-15504) */
   uint32_t small_nodes;          /* subtree roots split on the small path */
+  uint32_t kernel_launches;      /* kernels this call launched */
 } tessa_subtree_result;
 
 /* The partition of one batch of subtree tasks (synchronous on `stream`).

@@ -1454,5 +1454,6 @@ int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* a, tessa_s
   result->retries = stats.retries;
   result->balanced = stats.balanced;
   result->small_nodes = stats.small_nodes;
+  result->kernel_launches = stats.launches;
   return TESSA_OK;
 }

@@ -602,6 +602,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       ST_CUDA(cudaMemcpyAsync(S->nodes.ptr, d.data(), d.size() * sizeof(NodeDesc), cudaMemcpyHostToDevice, st));
       iota_kernel<<<(unsigned)d.size(), 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->cur.as<uint32_t>());
       ST_CUDA(cudaGetLastError());
+      stats->launches++;
     }
   }
 
@@ -730,6 +731,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       prm.out_slots = S->slots.as<uint32_t>();
       int rc = launch_assign_sq8_tc(prm, nb_max, sm_count, st);
       if (rc != TESSA_OK) return set_last_error(rc, "subtree assignment launch failed");
+      stats->launches += 3;  // prepare, assignment, count
       count_kernel<<<(unsigned)L, 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->slots.as<uint32_t>(),
                                                 S->counts.as<uint32_t>());
       ST_CUDA(cudaGetLastError());
@@ -851,6 +853,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
                                                          a.task_members, S->task_off.as<uint64_t>(),
                                                          S->next.as<uint32_t>(), a.leaf_rows);
       ST_CUDA(cudaGetLastError());
+      stats->launches++;
     }
     if (!sm.empty()) {
       ST_ALLOC(S->small_nodes, sm.size() * sizeof(NodeDesc));
@@ -876,6 +879,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       sp.err = d_err;
       small_kernel<<<(unsigned)sm.size(), 256, small_smem, st>>>(sp);
       ST_CUDA(cudaGetLastError());
+      stats->launches++;
       std::vector<uint32_t> tab(sm.size() * kTab);
       ST_CUDA(cudaMemcpyAsync(tab.data(), S->tables.ptr, tab.size() * 4, cudaMemcpyDeviceToHost, st));
       uint32_t bits = 0;

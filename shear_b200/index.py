@@ -48,7 +48,11 @@ class BuildParams:
     fanout_top: int = 10
     fanout_second: int = 3
     max_leaders: int = 1000
-    max_depth: int = 10
+    # PiPNNParams.max_depth is 10; the recursion on these child runs needs up to
+    # ~12 levels (the meaningful-split rule, CB:7082-7101, accepts splits that
+    # peel off 1/32 of a node).  The cap only decides when the partition gives
+    # up -- every split it allows is the same -- so the build uses 24.
+    max_depth: int = 24
     psamp_fraction: float = 0.001
     random_seed: int = 42
     root_leaders: int | None = None        # None: the D0 capacity plan decides
@@ -177,12 +181,17 @@ def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> B
     rows = int(leaf_rows.numel())
     ids = torch.full((rows * k,), -1, dtype=torch.int32, device=dev)
     dists = torch.full((rows * k,), float("inf"), dtype=torch.float32, device=dev)
+    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    ev[0].record()
     ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, gids, leaf_rows, starts, sizes, k, out=(ids, dists), ctx=ctx)
+    ev[1].record()
     planes = torch.from_numpy(hyperplanes(p.m_hash_bits, dim, p.random_seed)).to(dev)
     sketches = ops.sketch_rows(xd, planes, ctx=ctx)
     hf, hr = ops.edge_hashes(leaf_rows, ids, k, sketches, p.m_hash_bits, starts, sizes, ctx=ctx)
     sync()
     timings["leaf_s"] = time.perf_counter() - t
+    timings["leaf_kernel_ms"] = ev[0].elapsed_time(ev[1])
+    leaf_fallback = ops.leaf_last_fallback_rows(ctx)
 
     # ---- candidate records to pinned host memory, host reduction
     t = time.perf_counter()
@@ -210,5 +219,8 @@ def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> B
                  leaf_rows_mean=float(sizes.mean()) if sizes.size else 0.0, leaf_k=k, edges=edges,
                  leaf_pairs=int((sizes.astype(np.int64) * (sizes.astype(np.int64) - 1)).sum()),
                  leaf_ops=int(2 * d0.codes.shape[1] * (sizes.astype(np.int64) ** 2).sum()),
-                 partition=pst)
+                 leaf_fallback_rows=int(leaf_fallback), partition=pst,
+                 # quantize + D0 rectangular kernel + its exact fallback + fragments; partition;
+                 # gather + column-split leaf kernel + finish + fallback; sketches; edge hashes
+                 kernel_launches=4 + pst["kernel_launches"] + 4 + 2)
     return BuildResult(offs, nb, entry, timings, stats)

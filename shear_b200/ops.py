@@ -549,7 +549,7 @@ def subtree_partition(codes, scales, norms, task_members, task_offsets, task_cou
     C.check(C.load().tessa_subtree_partition(ctx.handle, ctypes.byref(a), ctypes.byref(r), _stream_ptr(torch, dev)))
     n = int(r.leaf_count)
     stats = {f: int(getattr(r, f)) for f in ("rounds", "large_assignments", "retries", "balanced", "small_nodes",
-                                             "leaf_rows_used")}
+                                             "leaf_rows_used", "kernel_launches")}
     return leaf_rows[:int(r.leaf_rows_used)], starts[:n].copy(), sizes[:n].copy(), tasks[:n].copy(), stats
 
 
