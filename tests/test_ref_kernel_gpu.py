@@ -7,9 +7,10 @@ TessaCudaReplaySession launches them (CB:34841-35230).  Where the reference is
 deterministic its output must equal ours bit for bit.  Leaves above 512 rows
 take the reference's staged path, whose per-row lock-order merge
 (CB:7261-7309) is not deterministic from run to run; there every row where
-the reference and this library differ must be explained by an eps-tie chain
-(|d_i - d_j| <= 2e-5 links, P/mod.rs:74), and the difference rate must stay
-within the reference's own run-to-run variation.
+the reference and this library differ may differ only near its k-th slot,
+where eps-tie chains (|d_i - d_j| <= 2e-5, P/mod.rs:74) make the list depend
+on insertion order, and the difference rate must stay within the
+reference's own run-to-run variation.
 """
 import numpy as np
 import pytest
@@ -49,21 +50,19 @@ def _diff_rows(a, b, k):
     return np.nonzero(m.any(axis=1))[0]
 
 
-def eps_chain_explains(ref_ids, ref_d, our_ids, our_d):
-    """True when every slot where two lists of one row differ lies on one eps-tie
-    chain of their union: sorted by distance, the differing entries span a
-    range whose consecutive gaps are all <= eps.  Insertion under the eps/id
-    rule can only reorder or swap entries linked that way."""
-    ref = list(zip(ref_d.tolist(), ref_ids.tolist()))
-    ours = list(zip(our_d.tolist(), our_ids.tolist()))
-    differing = {p for i, p in enumerate(ref) if ours[i] != p} | {p for i, p in enumerate(ours) if ref[i] != p}
-    if not differing:
-        return True
-    union = sorted(set(ref) | set(ours))
-    lo = min(d for d, _ in differing)
-    hi = max(d for d, _ in differing)
-    span = [d for d, _ in union if lo <= d <= hi]
-    return all(b - a <= EPS * 1.0001 for a, b in zip(span, span[1:]))
+def tail_difference_only(ref_ids, ref_d, our_ids, our_d, margin=8 * EPS):
+    """True when two lists of one row agree on every slot whose distance lies
+    more than `margin` below the row's k-th distance (the smaller of the two
+    lists' last entries).  Under the eps/id rule the insertion order can only
+    change which candidates of an eps-tie chain end near the k-th slot (a chain
+    may run through candidates that were evicted and appear in neither list),
+    never the clearly closer ones."""
+    kth = min(float(ref_d[-1]), float(our_d[-1]))
+    for i in range(len(ref_d)):
+        if ref_ids[i] != our_ids[i] or ref_d[i] != our_d[i]:
+            if min(float(ref_d[i]), float(our_d[i])) < kth - margin:
+                return False
+    return True
 
 
 def _formula_607(rows, dim):
@@ -115,7 +114,7 @@ def test_leaf_lists_equal_reference_kernels(oracle, name, sizes, dim, k, formula
         assert bad.size == 0, f"{label}: {bad.size} rows differ from the reference kernel, first {bad[:5]}"
 
 
-def test_config2_leaves_differ_from_reference_only_on_eps_tie_chains(oracle):
+def test_config2_leaves_differ_from_reference_only_near_the_kth_slot(oracle):
     # 32 leaves of config 2 (2048 rows, 768-d, k = 32): the reference stages
     # them into 128-column tasks merged in lock-arrival order.
     k = 32
@@ -124,13 +123,17 @@ def test_config2_leaves_differ_from_reference_only_on_eps_tie_chains(oracle):
     runs = [_ref(c, k, 2) for _ in range(3)]
     own_variation = max(_diff_rows(runs[0], r, k).size for r in runs[1:])
     rows = c["members"].size
+    # calibration: the reference's own runs differ only in such tails
+    for r in _diff_rows(runs[0], runs[1], k):
+        s = slice(int(r) * k, int(r) * k + k)
+        assert tail_difference_only(runs[0][0][s], runs[0][1][s], runs[1][0][s], runs[1][1][s])
     for ref in runs:
         bad = _diff_rows(ours, ref, k)
         # the same order of magnitude as the reference's own run-to-run changes
         assert bad.size <= max(3 * own_variation, 16) and bad.size <= rows // 1000, (bad.size, own_variation)
         for r in bad:
             s = slice(int(r) * k, int(r) * k + k)
-            assert eps_chain_explains(ref[0][s], ref[1][s], ours[0][s], ours[1][s]), f"row {r} not an eps-tie chain"
+            assert tail_difference_only(ref[0][s], ref[1][s], ours[0][s], ours[1][s]), f"row {r} differs inside"
 
 
 def _assign_case(oracle, seed):
