@@ -1273,11 +1273,11 @@ def run_build(a):
             tt = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             e2e_s = float(tt[0])
-        rec_bytes = res.stats["leaf_rows"] * (4 + res.stats["leaf_k"] * 12)
         e2e = {"value": world * n / e2e_s, "unit": "vectors/s", "h2d_bytes_per_step": int(n * c["dim"] * 4),
-               "d2h_bytes_per_step": int(rec_bytes), "ms_per_step": e2e_s * 1e3,
+               "d2h_bytes_per_step": int(r2.stats["d2h_bytes"]), "ms_per_step": e2e_s * 1e3,
                "timing": "wall clock around build_index(host numpy rows): upload, GPU stages, pinned D2H of "
-                         "the candidate records, host HashPrune reduction; graph in host memory"}
+                         "the candidate records grouped by reservoir, host HashPrune reduction; graph in host "
+                         "memory"}
         del xh
 
     if rank != 0:

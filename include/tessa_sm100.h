@@ -466,6 +466,29 @@ TESSA_API int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* 
 
 /* ---------------------------------------------------- host reduction --- */
 
+/* One candidate edge of a reservoir: the target point, the SQ8 distance and
+ * the personalised-residual hash (hash_prune.rs:2239-2251). */
+typedef struct tessa_edge {
+  uint32_t target;
+  float dist;
+  uint16_t hash;
+  uint16_t reserved;
+} tessa_edge;
+
+/* Candidate records of a leaf batch grouped by reservoir on the device: the
+ * edges of flush_compact_topk_batch_into_edges (P/leaf_build.rs:1749-1808; for
+ * row i and rank r with id j != 0xffffffff and a finite distance d,
+ * (point_ids[i] -> j, hash_fwd, d) and (j -> point_ids[i], hash_rev, d)) laid
+ * out so that point p's edges are edges[offsets[p] .. offsets[p+1]).  All
+ * pointers are device pointers; offsets has num_points + 1 entries, edges
+ * edge_capacity >= 2 * rows * k.  The order of a point's edges within its
+ * group is unspecified (the reservoir does not depend on it).  Ids at or above
+ * num_points are TESSA_ERR_BAD_ROW.  Synchronous on `stream`. */
+TESSA_API int tessa_group_edges(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids,
+                                const float* topk_dists, const uint16_t* hash_fwd, const uint16_t* hash_rev,
+                                uint64_t rows, uint32_t k, uint64_t num_points, uint64_t* offsets, tessa_edge* edges,
+                                uint64_t edge_capacity, void* stream);
+
 /* HashPrune reservoirs on the host (HashPruneReservoir,
  * P/hash_prune.rs:269-1452), the CPU-side reduction SHEAR feeds its leaf
  * candidate records into.  One reservoir of at most l_max slots per point
@@ -482,6 +505,10 @@ TESSA_API int tessa_reducer_create(uint64_t num_points, uint32_t l_max, uint32_t
 TESSA_API int tessa_reducer_add(tessa_reducer* reducer, const uint32_t* point_ids, const uint32_t* topk_ids,
                                 const float* topk_dists, const uint16_t* hash_fwd, const uint16_t* hash_rev,
                                 uint64_t rows, uint32_t k);
+/* Edges already grouped by reservoir (host copies of tessa_group_edges'
+ * outputs: offsets has num_points + 1 entries): each reservoir takes its
+ * group; the result equals tessa_reducer_add on the same records. */
+TESSA_API int tessa_reducer_add_grouped(tessa_reducer* reducer, const uint64_t* offsets, const tessa_edge* edges);
 /* Final neighbour lists, each point's slot targets in hash order (the
  * resident emit with backfill off, P/mod.rs:2437-2478), as CSR: offsets
  * (num_points + 1 entries) and neighbors (capacity entries; NULL to size). */

@@ -177,6 +177,10 @@ SIGNATURES = [
     ("tessa_reducer_add", ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32]),
     ("tessa_reducer_finish", ctypes.c_int, [c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     ("tessa_reducer_edges", ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint64)]),
+    ("tessa_reducer_add_grouped", ctypes.c_int, [c_vp, c_vp, c_vp]),
+    ("tessa_group_edges", ctypes.c_int,
+     [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, c_vp, c_vp,
+      ctypes.c_uint64, c_vp]),
     ("tessa_reducer_destroy", None, [c_vp]),
 ]
 

@@ -268,6 +268,7 @@ struct tessa_ctx {
   cudaEvent_t d0_ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // phase boundaries of a D0 call
   tessa_d0_profile d0_prof = {};
   SubtreeState* subtree = nullptr;  // subtree partition scratch (created on first use)
+  DevBuf g_cursor, g_temp;          // record grouping: per-point cursors, scan scratch
 };
 
 namespace {
@@ -801,6 +802,8 @@ void tessa_destroy(tessa_ctx* ctx) {
   for (DevBuf* b : bufs) b->release();
   subtree_state_free(ctx->subtree);
   ctx->subtree = nullptr;
+  ctx->g_cursor.release();
+  ctx->g_temp.release();
   for (cudaStream_t s : {ctx->stream_in, ctx->stream_out})
     if (s) {
       cudaStreamSynchronize(s);
@@ -1456,4 +1459,33 @@ int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* a, tessa_s
   result->small_nodes = stats.small_nodes;
   result->kernel_launches = stats.launches;
   return TESSA_OK;
+}
+
+// ----------------------------------------------------- record grouping
+
+int tessa_group_edges(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids, const float* topk_dists,
+                      const uint16_t* hash_fwd, const uint16_t* hash_rev, uint64_t rows, uint32_t k,
+                      uint64_t num_points, uint64_t* offsets, tessa_edge* edges, uint64_t edge_capacity,
+                      void* stream) {
+  TRY(bind(ctx));
+  if (!offsets || (rows && (!point_ids || !topk_ids || !topk_dists || !hash_fwd || !hash_rev || !edges)))
+    return fail(TESSA_ERR_INVALID_ARG, "null record or output pointer");
+  if (k == 0 || k > TESSA_MAX_LEAF_K) return fail(TESSA_ERR_INVALID_ARG, "k=%u outside 1..%d", k, TESSA_MAX_LEAF_K);
+  if (num_points == 0 || num_points > 0xffffffffull) return fail(TESSA_ERR_INVALID_ARG, "num_points outside 1..2^32");
+  if (edge_capacity < 2 * rows * (uint64_t)k)
+    return fail(TESSA_ERR_INVALID_ARG, "edge_capacity %llu below 2 * rows * k = %llu",
+                (unsigned long long)edge_capacity, (unsigned long long)(2 * rows * (uint64_t)k));
+  cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+  TRY(ctx->g_cursor.ensure(num_points * 8));
+  size_t need = group_edges_temp_bytes(num_points);
+  TRY(ctx->g_temp.ensure(need + 256));
+  TRY(clear_err(ctx, st));
+  GroupEdgesCall g{point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, rows, k, num_points, offsets,
+                   ctx->g_cursor.as<uint64_t>(), edges, ctx->g_temp.ptr, ctx->g_temp.bytes, &need,
+                   ctx->d_err.as<uint32_t>(), ctx->sm_count};
+  const int rc = group_edges(g, st);
+  if (rc != TESSA_OK) return fail(rc, "edge grouping failed (%s)", cudaGetErrorString(cudaGetLastError()));
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  return map_device_error(bits);
 }

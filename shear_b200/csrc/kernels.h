@@ -171,6 +171,28 @@ struct SubtreeStats {
 int subtree_partition(SubtreeState* s, const tessa_subtree_args& a, SubtreeStats* stats, uint32_t* d_err,
                       int sm_count, uint64_t timeout_ns, cudaStream_t stream);
 
+// Candidate records grouped by reservoir (records.cu).
+struct GroupEdgesCall {
+  const uint32_t* point_ids;
+  const uint32_t* topk_ids;
+  const float* topk_dists;
+  const uint16_t* hash_fwd;
+  const uint16_t* hash_rev;
+  uint64_t rows;
+  uint32_t k;
+  uint64_t num_points;
+  uint64_t* offsets;      // num_points + 1
+  uint64_t* cursor;       // num_points scratch
+  tessa_edge* edges;      // capacity >= 2 * rows * k
+  void* temp;             // scan scratch
+  size_t temp_bytes;
+  size_t* temp_needed;
+  uint32_t* d_err;
+  int sm_count;
+};
+int group_edges(const GroupEdgesCall& g, cudaStream_t stream);
+size_t group_edges_temp_bytes(uint64_t num_points);
+
 // Records `code` and `message` as the calling thread's last error (returned by
 // tessa_last_error_message); returns `code`.
 int set_last_error(int code, const char* message);

@@ -2,25 +2,35 @@
 //
 // SHEAR keeps this stage on the CPU: leaf top-k records are flushed into
 // per-point reservoirs (HashPruneReservoir, shear-core/src/algorithm/pipnn/
-// hash_prune.rs:269-1420) and each point's final neighbours are the
+// hash_prune.rs:269-1452) and each point's final neighbours are the
 // reservoir's slots (into_finalized_slots_with_backfill with the default
 // backfill off, :1946-1964, emitted by emit_resident_reservoirs_serial,
-// mod.rs:2437-2478).  This file restates that reservoir for the build: a
-// reservoir holds at most l_max slots (target, hash, dist) sorted by hash;
-// a candidate whose hash is present replaces that slot when it is better;
-// otherwise it is inserted while there is room, else it replaces the
-// farthest slot when better (insert_inner, :1326-1452).  "Better" is the
-// total order (dist via total_cmp, target, hash) (:2094-2130).
+// mod.rs:2437-2478).  A reservoir holds at most l_max slots (target, hash,
+// dist) sorted by hash; insert_inner (:1326-1452) replaces a slot whose hash
+// matches when the candidate is better, inserts while there is room, and
+// otherwise replaces the farthest slot when the candidate is better.  "Better"
+// is the total order (dist via total_cmp, target, hash) (:2094-2130).
+//
+// The slots that sequence of inserts leaves behind do not depend on the
+// insertion order: they are the l_max best (in that order) of the per-hash
+// minima of every candidate offered.  (A per-hash minimum among the l_max best
+// is never rejected -- that needs l_max better slots of other hashes -- and
+// never evicted; nothing else can stay.)  The reducer therefore applies a
+// batch at once: edges are grouped by source point with counting sorts, and
+// each reservoir merges its new candidates in one pass -- per-hash minimum
+// through a table indexed by hash, the l_max best by partial selection, the
+// survivors sorted by hash -- touching its slots once instead of once per
+// candidate.  The result equals the reference's online inserts (tested
+// against a line-by-line restatement of insert_inner).
 //
 // Edges come from leaf batches exactly as flush_compact_topk_batch_into_edges
 // forms them (P/leaf_build.rs:1749-1808): for row i and rank r with a valid id
 // j and a finite distance d, (i -> j, hash_fwd, d) then (j -> i, hash_rev, d).
-// Batches are distributed over host threads by source point (point % T), so
-// every reservoir is owned by one thread; the reservoir's final content does
-// not depend on the insertion order, so the result is deterministic.
+// Source point p belongs to host thread p & (T - 1) (T a power of two).
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <memory>
 #include <new>
 #include <thread>
 #include <vector>
@@ -35,8 +45,7 @@ struct tessa_reducer {
   std::vector<uint16_t> hash;
   std::vector<float> dist;
   std::vector<uint8_t> len;      // slots used (l_max <= 255)
-  std::vector<uint8_t> far;      // index of the farthest slot
-  uint64_t edges = 0;            // edges inserted so far
+  uint64_t edges = 0;            // edges offered so far
 };
 
 namespace {
@@ -44,105 +53,79 @@ namespace {
 struct Edge {
   uint32_t src, dst;
   float dist;
-  uint16_t hash;
+  uint32_t hash;
 };
 
-inline int total_cmp_f32(float a, float b) {
-  // f32::total_cmp: order of the sign-flipped bit patterns
-  int32_t ia, ib;
-  memcpy(&ia, &a, 4);
-  memcpy(&ib, &b, 4);
-  ia ^= (int32_t)((uint32_t)(ia >> 31) >> 1);
-  ib ^= (int32_t)((uint32_t)(ib >> 31) >> 1);
-  return ia < ib ? -1 : (ia > ib ? 1 : 0);
+inline uint32_t total_key(float d) {
+  // f32::total_cmp order as an unsigned key
+  uint32_t u;
+  memcpy(&u, &d, 4);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// hashprune_candidate_total_order (hash_prune.rs:2094-2106): < 0 when (d1, t1, h1) comes first
-inline int cand_order(uint32_t t1, uint16_t h1, float d1, uint32_t t2, uint16_t h2, float d2) {
-  int c = total_cmp_f32(d1, d2);
-  if (c) return c;
-  if (t1 != t2) return t1 < t2 ? -1 : 1;
-  if (h1 != h2) return h1 < h2 ? -1 : 1;
-  return 0;
+struct Cand {
+  uint32_t dkey, target, hash;
+  float dist;
+};
+
+// hashprune_candidate_total_order (hash_prune.rs:2094-2106)
+inline bool cand_less(const Cand& a, const Cand& b) {
+  if (a.dkey != b.dkey) return a.dkey < b.dkey;
+  if (a.target != b.target) return a.target < b.target;
+  return a.hash < b.hash;
 }
 
-void recompute_far(const uint32_t* t, const uint16_t* h, const float* d, uint32_t n, uint8_t* far) {
-  uint32_t idx = 0;
-  for (uint32_t i = 1; i < n; ++i)
-    if (cand_order(t[i], h[i], d[i], t[idx], h[idx], d[idx]) > 0) idx = i;
-  *far = (uint8_t)idx;
+struct Scratch {
+  std::vector<uint32_t> stamp;   // per hash: batch stamp of the entry
+  std::vector<uint32_t> where;   // per hash: index into cand
+  std::vector<Cand> cand;
+  std::vector<uint32_t> count;   // counting sort by local source
+  std::unique_ptr<Edge[]> sorted;  // not value-initialised
+  uint64_t sorted_cap = 0;
+  uint32_t cur = 0;
+  Scratch() : stamp(1u << 16, 0), where(1u << 16, 0) {}
+};
+
+void offer(Scratch& S, uint32_t target, uint32_t hash, float dist) {
+  const Cand c{total_key(dist), target, hash, dist};
+  if (S.stamp[hash] != S.cur) {
+    S.stamp[hash] = S.cur;
+    S.where[hash] = (uint32_t)S.cand.size();
+    S.cand.push_back(c);
+  } else if (cand_less(c, S.cand[S.where[hash]])) {
+    S.cand[S.where[hash]] = c;
+  }
 }
 
-// insert_inner (hash_prune.rs:1326-1452) on one reservoir.
-void insert(tessa_reducer* R, uint64_t p, uint32_t tgt, uint16_t hs, float ds) {
+inline uint32_t edge_target(const Edge& e) { return e.dst; }
+inline uint32_t edge_target(const tessa_edge& e) { return e.target; }
+
+// Merge the edges of one source into its reservoir.
+template <class E>
+void merge(tessa_reducer* R, Scratch& S, uint64_t p, const E* e, size_t n) {
   const uint32_t L = R->l_max;
   uint32_t* t = R->target.data() + p * L;
   uint16_t* h = R->hash.data() + p * L;
   float* d = R->dist.data() + p * L;
-  uint32_t n = R->len[p];
-  uint8_t* far = &R->far[p];
-  // binary search by hash
-  uint32_t lo = 0, hi = n;
-  while (lo < hi) {
-    const uint32_t mid = (lo + hi) >> 1;
-    if (h[mid] < hs) lo = mid + 1;
-    else hi = mid;
+  if (++S.cur == 0) {  // stamps wrapped: clear them
+    std::fill(S.stamp.begin(), S.stamp.end(), 0u);
+    S.cur = 1;
   }
-  if (lo < n && h[lo] == hs) {
-    if (cand_order(tgt, hs, ds, t[lo], h[lo], d[lo]) < 0) {
-      t[lo] = tgt;
-      d[lo] = ds;
-      if (lo == *far) recompute_far(t, h, d, n, far);
-    }
-    return;
+  S.cand.clear();
+  for (uint32_t i = 0; i < R->len[p]; ++i) offer(S, t[i], h[i], d[i]);
+  for (size_t i = 0; i < n; ++i) offer(S, edge_target(e[i]), e[i].hash, e[i].dist);
+  auto& c = S.cand;
+  if (c.size() > L) {
+    std::nth_element(c.begin(), c.begin() + L, c.end(), cand_less);
+    c.resize(L);
   }
-  if (n < L) {
-    for (uint32_t i = n; i > lo; --i) {
-      t[i] = t[i - 1];
-      h[i] = h[i - 1];
-      d[i] = d[i - 1];
-    }
-    t[lo] = tgt;
-    h[lo] = hs;
-    d[lo] = ds;
-    R->len[p] = (uint8_t)(n + 1);
-    if (n == 0) {
-      *far = 0;
-    } else {
-      uint32_t fi = *far;
-      if (lo <= fi) fi++;
-      if (cand_order(t[lo], h[lo], d[lo], t[fi], h[fi], d[fi]) > 0) fi = lo;
-      *far = (uint8_t)fi;
-    }
-    return;
+  std::sort(c.begin(), c.end(), [](const Cand& a, const Cand& b) { return a.hash < b.hash; });
+  for (size_t i = 0; i < c.size(); ++i) {
+    t[i] = c[i].target;
+    h[i] = (uint16_t)c[i].hash;
+    d[i] = c[i].dist;
   }
-  const uint32_t fi = *far;
-  if (cand_order(tgt, hs, ds, t[fi], h[fi], d[fi]) >= 0) return;
-  // replace the farthest slot and move it to its hash position
-  uint32_t pos = fi;
-  if (fi > 0 && h[fi - 1] > hs) {
-    uint32_t tp = 0;
-    while (tp < fi && h[tp] < hs) ++tp;
-    for (uint32_t i = fi; i > tp; --i) {
-      t[i] = t[i - 1];
-      h[i] = h[i - 1];
-      d[i] = d[i - 1];
-    }
-    pos = tp;
-  } else if (fi + 1 < n && h[fi + 1] < hs) {
-    uint32_t tp = fi + 1;
-    while (tp < n && h[tp] < hs) ++tp;
-    for (uint32_t i = fi; i + 1 < tp; ++i) {
-      t[i] = t[i + 1];
-      h[i] = h[i + 1];
-      d[i] = d[i + 1];
-    }
-    pos = tp - 1;
-  }
-  t[pos] = tgt;
-  h[pos] = hs;
-  d[pos] = ds;
-  recompute_far(t, h, d, n, far);
+  R->len[p] = (uint8_t)c.size();
 }
 
 template <class F>
@@ -173,12 +156,13 @@ TESSA_API int tessa_reducer_create(uint64_t num_points, uint32_t l_max, uint32_t
   try {
     R->points = num_points;
     R->l_max = l_max;
-    R->threads = threads ? threads : 1;
+    uint32_t t = 1;
+    while (t * 2 <= (threads ? threads : 1) && t < 256) t *= 2;
+    R->threads = t;
     R->target.resize(num_points * l_max);
     R->hash.resize(num_points * l_max);
     R->dist.resize(num_points * l_max);
     R->len.assign(num_points, 0);
-    R->far.assign(num_points, 0);
   } catch (...) {
     delete R;
     return tessa::set_last_error(TESSA_ERR_OOM, "reducer reservoirs do not fit in host memory");
@@ -194,13 +178,47 @@ TESSA_API int tessa_reducer_add(tessa_reducer* R, const uint32_t* point_ids, con
   if (rows == 0) return TESSA_OK;
   if (!point_ids || !topk_ids || !topk_dists || !hash_fwd || !hash_rev || k == 0)
     return tessa::set_last_error(TESSA_ERR_INVALID_ARG, "null edge input or k = 0");
-  const uint32_t T = R->threads;
-  // phase 1: form the edges of a row range per thread, bucketed by owner thread
-  std::vector<std::vector<std::vector<Edge>>> buckets(T, std::vector<std::vector<Edge>>(T));
+  const uint32_t T = R->threads, mask = T - 1, shift = (uint32_t)__builtin_ctz(T);
+  const uint64_t P = R->points;
+  // 1. per (row range w, owner thread o) edge counts
+  std::vector<uint64_t> cnt((size_t)T * T, 0);
   std::vector<int> bad(T, 0);
   parallel(T, [&](uint32_t w) {
     const uint64_t r0 = rows * w / T, r1 = rows * (w + 1) / T;
-    auto& mine = buckets[w];
+    uint64_t* c = cnt.data() + (size_t)w * T;
+    for (uint64_t i = r0; i < r1; ++i) {
+      const uint32_t p = point_ids[i];
+      for (uint32_t r = 0; r < k; ++r) {
+        const uint64_t s = i * k + r;
+        const uint32_t j = topk_ids[s];
+        if (j == 0xffffffffu || !std::isfinite(topk_dists[s])) continue;
+        if (p >= P || j >= P) {
+          bad[w] = 1;
+          continue;
+        }
+        c[p & mask]++;
+        c[j & mask]++;
+      }
+    }
+  });
+  for (int b : bad)
+    if (b) return tessa::set_last_error(TESSA_ERR_BAD_ROW, "edge endpoint outside the reducer's points");
+  // 2. owner-major layout: owner o's edges are contiguous
+  std::vector<uint64_t> off((size_t)T * T), base(T + 1, 0);
+  for (uint32_t o = 0; o < T; ++o) {
+    uint64_t run = base[o];
+    for (uint32_t w = 0; w < T; ++w) {
+      off[(size_t)w * T + o] = run;
+      run += cnt[(size_t)w * T + o];
+    }
+    base[o + 1] = run;
+  }
+  const uint64_t total = base[T];
+  std::unique_ptr<Edge[]> edges(new (std::nothrow) Edge[total ? total : 1]);
+  if (!edges) return tessa::set_last_error(TESSA_ERR_OOM, "reducer batch does not fit in host memory");
+  parallel(T, [&](uint32_t w) {
+    const uint64_t r0 = rows * w / T, r1 = rows * (w + 1) / T;
+    uint64_t* o = off.data() + (size_t)w * T;
     for (uint64_t i = r0; i < r1; ++i) {
       const uint32_t p = point_ids[i];
       for (uint32_t r = 0; r < k; ++r) {
@@ -208,25 +226,81 @@ TESSA_API int tessa_reducer_add(tessa_reducer* R, const uint32_t* point_ids, con
         const uint32_t j = topk_ids[s];
         const float d = topk_dists[s];
         if (j == 0xffffffffu || !std::isfinite(d)) continue;
-        if (p >= R->points || j >= R->points) {
-          bad[w] = 1;
-          continue;
-        }
-        mine[p % T].push_back(Edge{p, j, d, hash_fwd[s]});
-        mine[j % T].push_back(Edge{j, p, d, hash_rev[s]});
+        edges[o[p & mask]++] = Edge{p, j, d, hash_fwd[s]};
+        edges[o[j & mask]++] = Edge{j, p, d, hash_rev[s]};
       }
     }
   });
-  for (int b : bad)
-    if (b) return tessa::set_last_error(TESSA_ERR_BAD_ROW, "edge endpoint outside the reducer's points");
-  // phase 2: every thread applies the edges of the points it owns
-  std::vector<uint64_t> counted(T, 0);
-  parallel(T, [&](uint32_t owner) {
-    for (uint32_t w = 0; w < T; ++w)
-      for (const Edge& e : buckets[w][owner]) insert(R, e.src, e.dst, e.hash, e.dist);
-    for (uint32_t w = 0; w < T; ++w) counted[owner] += buckets[w][owner].size();
+  // 3. every owner sorts its edges by source (counting sort) and merges each
+  //    source's edges into its reservoir, sources in ascending order
+  std::vector<int> oom(T, 0);
+  parallel(T, [&](uint32_t o) {
+    static thread_local Scratch S;
+    const uint64_t b = base[o], n = base[o + 1] - b;
+    if (n == 0) return;
+    const uint64_t locals = (P - o + T - 1) >> shift;  // sources p = o + T * li
+    try {
+      S.count.assign(locals + 1, 0);
+      if (S.sorted_cap < n) {
+        S.sorted.reset(new Edge[n]);
+        S.sorted_cap = n;
+      }
+    } catch (...) {
+      oom[o] = 1;
+      return;
+    }
+    const Edge* e = edges.get() + b;
+    uint32_t* cnt_l = S.count.data();
+    for (uint64_t i = 0; i < n; ++i) cnt_l[(e[i].src >> shift) + 1]++;
+    for (uint64_t li = 0; li < locals; ++li) cnt_l[li + 1] += cnt_l[li];
+    Edge* srt = S.sorted.get();
+    for (uint64_t i = 0; i < n; ++i) srt[cnt_l[e[i].src >> shift]++] = e[i];
+    // count[li] is now the end of source li's edges
+    uint64_t lo = 0;
+    for (uint64_t li = 0; li < locals; ++li) {
+      const uint64_t hi = cnt_l[li];
+      if (hi > lo) merge(R, S, o + ((uint64_t)li << shift), srt + lo, hi - lo);
+      lo = hi;
+    }
   });
-  for (uint64_t c : counted) R->edges += c;
+  for (int b : oom)
+    if (b) return tessa::set_last_error(TESSA_ERR_OOM, "reducer scratch does not fit in host memory");
+  R->edges += total;
+  return TESSA_OK;
+}
+
+TESSA_API int tessa_reducer_add_grouped(tessa_reducer* R, const uint64_t* offsets, const tessa_edge* edges) {
+  if (!R || !offsets) return tessa::set_last_error(TESSA_ERR_INVALID_ARG, "null reducer input");
+  const uint64_t P = R->points;
+  if (offsets[0] != 0) return tessa::set_last_error(TESSA_ERR_INVALID_ARG, "grouped offsets must start at 0");
+  for (uint64_t p = 0; p < P; ++p)
+    if (offsets[p + 1] < offsets[p]) return tessa::set_last_error(TESSA_ERR_INVALID_ARG, "grouped offsets decrease");
+  const uint64_t total = offsets[P];
+  if (total && !edges) return tessa::set_last_error(TESSA_ERR_INVALID_ARG, "null edges");
+  const uint32_t T = R->threads;
+  std::vector<int> bad(T, 0);
+  // contiguous point ranges of about equal edge counts
+  parallel(T, [&](uint32_t w) {
+    static thread_local Scratch S;
+    const uint64_t e0 = total * w / T, e1 = total * (w + 1) / T;
+    uint64_t p = std::upper_bound(offsets, offsets + P + 1, e0) - offsets - 1;
+    if (w == 0) p = 0;
+    for (; p < P && offsets[p] < e1; ++p) {
+      if (w > 0 && offsets[p] < e0) continue;  // owned by the previous range
+      const uint64_t a = offsets[p], b = offsets[p + 1];
+      if (b == a) continue;
+      bool ok = true;
+      for (uint64_t i = a; i < b; ++i) ok &= edges[i].target < P;
+      if (!ok) {
+        bad[w] = 1;
+        continue;
+      }
+      merge(R, S, p, edges + a, b - a);
+    }
+  });
+  for (int b : bad)
+    if (b) return tessa::set_last_error(TESSA_ERR_BAD_ROW, "edge target outside the reducer's points");
+  R->edges += total;
   return TESSA_OK;
 }
 

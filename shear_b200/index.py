@@ -18,8 +18,9 @@ Reference flow (shear-core/src/algorithm/pipnn/, Rust):
 Here: D0 = tessa_quantize_sq8_assign_d0 (rectangular tcgen05 kernel), child
 runs grouped on the device, all subtree tasks partitioned in one
 tessa_subtree_partition call, leaves through tessa_leaf_topk_sq8, hashes
-through tessa_sketch_rows / tessa_edge_hashes, records copied to pinned host
-memory and reduced by the host reducer (tessa_reducer_*).
+through tessa_sketch_rows / tessa_edge_hashes, records grouped by reservoir on
+the device (tessa_group_edges), copied to pinned host memory and reduced by
+the host reducer (tessa_reducer_add_grouped).
 
 Two inputs the reference draws from Rust's StdRng (rand 0.9, ChaCha12),
 which cannot be reproduced outside Rust, come from seeded numpy generators
@@ -130,6 +131,30 @@ def group_child_runs(child_ids, num_leaders: int):
     return members, counts, offsets
 
 
+_PINNED: dict = {}
+_GROUPING: dict = {}
+
+
+def _pinned(name, torch, nbytes):
+    """Pinned host staging reused across builds (grown on demand)."""
+    buf = _PINNED.get(name)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(int(nbytes * 1.25) + 64, dtype=torch.uint8, pin_memory=True)
+        _PINNED[name] = buf
+    return buf[:nbytes]
+
+
+def _grouping_buffers(torch, dev, n, cap):
+    """Device outputs of the record grouping, reused across builds."""
+    key = dev.index
+    bufs = _GROUPING.get(key)
+    if bufs is None or bufs[0].numel() < n + 1 or bufs[1].numel() < cap * 12:
+        bufs = (torch.empty(n + 1, dtype=torch.int64, device=dev),
+                torch.empty(max(cap, 1) * 12, dtype=torch.uint8, device=dev))
+        _GROUPING[key] = bufs
+    return bufs[0][:n + 1], bufs[1][:max(cap, 1) * 12]
+
+
 def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> BuildResult:
     """Build the graph of x (numpy f32 [n, dim] on the host -- copied to the
     device inside -- or a CUDA f32 tensor already resident)."""
@@ -193,18 +218,22 @@ def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> B
     timings["leaf_kernel_ms"] = ev[0].elapsed_time(ev[1])
     leaf_fallback = ops.leaf_last_fallback_rows(ctx)
 
-    # ---- candidate records to pinned host memory, host reduction
+    # ---- candidate records grouped by reservoir on the device, pinned D2H,
+    #      host HashPrune reduction
     t = time.perf_counter()
-    def pin(v):
-        h = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
-        h.copy_(v, non_blocking=True)
-        return h
-    h_rows, h_ids, h_d, h_hf, h_hr = (pin(leaf_rows), pin(ids), pin(dists), pin(hf), pin(hr))
+    goff, gedges = ops.group_edges(leaf_rows, ids, dists, hf, hr, k, n, ctx=ctx,
+                                   out=_grouping_buffers(torch, dev, n, 2 * rows * k))
+    total = int(goff[n].item())
+    h_off = _pinned("offsets", torch, (n + 1) * 8)
+    h_edges = _pinned("edges", torch, max(total, 1) * 12)
+    h_off.copy_(goff.view(torch.uint8), non_blocking=True)
+    if total:
+        h_edges[:total * 12].copy_(gedges[:total * 12], non_blocking=True)
     sync()
-    timings["d2h_s"] = time.perf_counter() - t
+    timings["group_d2h_s"] = time.perf_counter() - t
     t = time.perf_counter()
     red = ops.Reducer(n, p.l_max, p.reducer_threads)
-    red.add(h_rows.numpy(), h_ids.numpy(), h_d.numpy(), h_hf.numpy(), h_hr.numpy(), k)
+    red.add_grouped(h_off.numpy().view(np.uint64), h_edges[:total * 12].numpy().view(ops.EDGE_DTYPE))
     offs, nb = red.finish()
     edges = red.edges()
     red.close()
@@ -220,7 +249,9 @@ def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> B
                  leaf_pairs=int((sizes.astype(np.int64) * (sizes.astype(np.int64) - 1)).sum()),
                  leaf_ops=int(2 * d0.codes.shape[1] * (sizes.astype(np.int64) ** 2).sum()),
                  leaf_fallback_rows=int(leaf_fallback), partition=pst,
+                 d2h_bytes=int((n + 1) * 8 + total * 12),
                  # quantize + D0 rectangular kernel + its exact fallback + fragments; partition;
-                 # gather + column-split leaf kernel + finish + fallback; sketches; edge hashes
-                 kernel_launches=4 + pst["kernel_launches"] + 4 + 2)
+                 # gather + column-split leaf kernel + finish + fallback; sketches; edge hashes;
+                 # record grouping (count, scan, scatter)
+                 kernel_launches=4 + pst["kernel_launches"] + 4 + 2 + 3)
     return BuildResult(offs, nb, entry, timings, stats)

@@ -579,6 +579,15 @@ class Reducer:
         C.check(self.lib.tessa_reducer_add(self.handle, _np_ptr(pid), _np_ptr(ids), _np_ptr(ds), _np_ptr(hf),
                                            _np_ptr(hr), rows, k))
 
+    def add_grouped(self, offsets, edges):
+        """Edges grouped by reservoir (host copies of group_edges' outputs:
+        offsets uint64 [n+1], edges as the 12-byte tessa_edge records)."""
+        off = np.ascontiguousarray(offsets, np.uint64)
+        e = np.ascontiguousarray(edges)
+        if off.shape[0] != self.num_points + 1:
+            raise ValueError("offsets must hold num_points + 1 entries")
+        C.check(self.lib.tessa_reducer_add_grouped(self.handle, _np_ptr(off), _np_ptr(e)))
+
     def edges(self) -> int:
         n = ctypes.c_uint64()
         C.check(self.lib.tessa_reducer_edges(self.handle, ctypes.byref(n)))
@@ -603,3 +612,27 @@ class Reducer:
             self.close()
         except Exception:
             pass
+
+
+EDGE_DTYPE = np.dtype([("target", "<u4"), ("dist", "<f4"), ("hash", "<u2"), ("reserved", "<u2")])
+
+
+def group_edges(point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, k: int, num_points: int,
+                ctx: Context | None = None, out=None):
+    """tessa_group_edges on device tensors: (offsets int64 [n+1], edges uint8 [cap * 12])
+    CUDA tensors; point p's edges are edges[offsets[p]:offsets[p+1]] (tessa_edge records)."""
+    import torch
+
+    rows = int(point_ids.numel())
+    dev = point_ids.device
+    ctx = ctx or context(dev.index)
+    cap = 2 * rows * k
+    if out is None:
+        offsets = torch.empty(num_points + 1, dtype=torch.int64, device=dev)
+        edges = torch.empty(max(cap, 1) * 12, dtype=torch.uint8, device=dev)
+    else:
+        offsets, edges = out
+    C.check(C.load().tessa_group_edges(ctx.handle, _ptr(point_ids), _ptr(topk_ids), _ptr(topk_dists),
+                                       _ptr(hash_fwd), _ptr(hash_rev), rows, k, num_points, _ptr(offsets),
+                                       _ptr(edges), cap, _stream_ptr(torch, dev.index)))
+    return offsets, edges

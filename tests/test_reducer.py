@@ -61,3 +61,39 @@ def test_reducer_rejects_out_of_range_ids():
         red.add(np.array([3], np.uint32), np.array([[11]], np.uint32), np.array([[0.5]], np.float32),
                 np.array([[1]], np.uint16), np.array([[2]], np.uint16), 1)
     red.close()
+
+
+def _group_on_host(batch, points):
+    """Edges of one record batch grouped by reservoir (numpy), as tessa_group_edges lays them out."""
+    from shear_b200.ops import EDGE_DTYPE
+    pid, ids, ds, hf, hr, k = batch
+    ids = ids.reshape(-1)
+    ds = ds.reshape(-1)
+    src = np.repeat(pid, k)
+    ok = (ids != 0xFFFFFFFF) & np.isfinite(ds)
+    s1, t1, h1, d1 = src[ok], ids[ok], hf.reshape(-1)[ok], ds[ok]
+    s2, t2, h2 = t1, s1, hr.reshape(-1)[ok]
+    s = np.concatenate([s1, s2])
+    e = np.zeros(s.size, EDGE_DTYPE)
+    e["target"] = np.concatenate([t1, t2])
+    e["dist"] = np.concatenate([d1, d1])
+    e["hash"] = np.concatenate([h1, h2])
+    order = np.argsort(s, kind="stable")
+    offsets = np.concatenate([[0], np.cumsum(np.bincount(s, minlength=points))]).astype(np.uint64)
+    return offsets, e[order]
+
+
+@pytest.mark.parametrize("threads", [1, 4])
+def test_grouped_add_equals_record_add(threads):
+    from shear_b200 import ops
+    rng = np.random.default_rng(12)
+    batches = _batches(rng, 400, 3000, 2, 3, 8, dup_dist=True)
+    a = ops.Reducer(400, 24, threads)
+    b = ops.Reducer(400, 24, threads)
+    for bt in batches:
+        a.add(*bt)
+        b.add_grouped(*_group_on_host(bt, 400))
+    ra, rb = a.finish(), b.finish()
+    a.close()
+    b.close()
+    assert np.array_equal(ra[0], rb[0]) and np.array_equal(ra[1], rb[1])
