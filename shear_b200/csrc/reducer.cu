@@ -63,44 +63,48 @@ inline uint32_t total_key(float d) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// A candidate in hashprune_candidate_total_order (hash_prune.rs:2094-2106):
+// (dist by total_cmp, target) packed into one 64-bit key, hash last.
 struct Cand {
-  uint32_t dkey, target, hash;
+  uint64_t key;
+  uint32_t hash;
   float dist;
 };
 
-// hashprune_candidate_total_order (hash_prune.rs:2094-2106)
 inline bool cand_less(const Cand& a, const Cand& b) {
-  if (a.dkey != b.dkey) return a.dkey < b.dkey;
-  if (a.target != b.target) return a.target < b.target;
-  return a.hash < b.hash;
+  return a.key != b.key ? a.key < b.key : a.hash < b.hash;
 }
 
 struct Scratch {
-  std::vector<uint32_t> stamp;   // per hash: batch stamp of the entry
-  std::vector<uint32_t> where;   // per hash: index into cand
+  // per hash value: stamp of the merge that last touched it and the index of
+  // its candidate; a bitset of the surviving hashes for hash-ordered output
+  std::vector<uint64_t> slot;    // (stamp << 32) | candidate index
+  std::vector<uint64_t> bits;
   std::vector<Cand> cand;
   std::vector<uint32_t> count;   // counting sort by local source
   std::unique_ptr<Edge[]> sorted;  // not value-initialised
   uint64_t sorted_cap = 0;
   uint32_t cur = 0;
-  Scratch() : stamp(1u << 16, 0), where(1u << 16, 0) {}
+  Scratch() : slot(1u << 16, 0), bits((1u << 16) / 64, 0) { cand.reserve(512); }
 };
 
-void offer(Scratch& S, uint32_t target, uint32_t hash, float dist) {
-  const Cand c{total_key(dist), target, hash, dist};
-  if (S.stamp[hash] != S.cur) {
-    S.stamp[hash] = S.cur;
-    S.where[hash] = (uint32_t)S.cand.size();
+inline void offer(Scratch& S, uint32_t target, uint32_t hash, float dist) {
+  const Cand c{((uint64_t)total_key(dist) << 32) | target, hash, dist};
+  const uint64_t sl = S.slot[hash];
+  if ((uint32_t)(sl >> 32) != S.cur) {
+    S.slot[hash] = ((uint64_t)S.cur << 32) | (uint32_t)S.cand.size();
     S.cand.push_back(c);
-  } else if (cand_less(c, S.cand[S.where[hash]])) {
-    S.cand[S.where[hash]] = c;
+  } else {
+    Cand& o = S.cand[(uint32_t)sl];
+    if (cand_less(c, o)) o = c;
   }
 }
 
 inline uint32_t edge_target(const Edge& e) { return e.dst; }
 inline uint32_t edge_target(const tessa_edge& e) { return e.target; }
 
-// Merge the edges of one source into its reservoir.
+// Merge the edges of one source into its reservoir: per-hash minimum of the
+// old slots and the new edges, the l_max best, written back in hash order.
 template <class E>
 void merge(tessa_reducer* R, Scratch& S, uint64_t p, const E* e, size_t n) {
   const uint32_t L = R->l_max;
@@ -108,7 +112,7 @@ void merge(tessa_reducer* R, Scratch& S, uint64_t p, const E* e, size_t n) {
   uint16_t* h = R->hash.data() + p * L;
   float* d = R->dist.data() + p * L;
   if (++S.cur == 0) {  // stamps wrapped: clear them
-    std::fill(S.stamp.begin(), S.stamp.end(), 0u);
+    std::fill(S.slot.begin(), S.slot.end(), 0ull);
     S.cur = 1;
   }
   S.cand.clear();
@@ -119,11 +123,28 @@ void merge(tessa_reducer* R, Scratch& S, uint64_t p, const E* e, size_t n) {
     std::nth_element(c.begin(), c.begin() + L, c.end(), cand_less);
     c.resize(L);
   }
-  std::sort(c.begin(), c.end(), [](const Cand& a, const Cand& b) { return a.hash < b.hash; });
-  for (size_t i = 0; i < c.size(); ++i) {
-    t[i] = c[i].target;
-    h[i] = (uint16_t)c[i].hash;
-    d[i] = c[i].dist;
+  // emit in hash order through the bitset of surviving hashes
+  uint32_t lo_w = 0xffffffffu, hi_w = 0;
+  for (uint32_t i = 0; i < c.size(); ++i) {
+    const uint32_t hv = c[i].hash;
+    S.slot[hv] = ((uint64_t)S.cur << 32) | i;
+    S.bits[hv >> 6] |= 1ull << (hv & 63);
+    lo_w = std::min(lo_w, hv >> 6);
+    hi_w = std::max(hi_w, hv >> 6);
+  }
+  uint32_t out = 0;
+  for (uint32_t w = lo_w; w <= hi_w && out < c.size(); ++w) {
+    uint64_t b = S.bits[w];
+    S.bits[w] = 0;
+    while (b) {
+      const uint32_t hv = (w << 6) | (uint32_t)__builtin_ctzll(b);
+      b &= b - 1;
+      const Cand& x = c[(uint32_t)S.slot[hv]];
+      t[out] = (uint32_t)x.key;
+      h[out] = (uint16_t)x.hash;
+      d[out] = x.dist;
+      ++out;
+    }
   }
   R->len[p] = (uint8_t)c.size();
 }
