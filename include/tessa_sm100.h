@@ -187,7 +187,9 @@ TESSA_API int tessa_leaf_last_fallback_rows(const tessa_ctx* ctx, uint64_t* rows
  * one static device array of TESSA_NOALLOC_SCRATCH_BYTES that every GPU loading
  * the library holds until exit.  Batches needing more scratch are rejected
  * with TESSA_ERR_UNSUPPORTED.  The first call on a device resolves the array's
- * address (make it before any stream capture).  All calls share the array and
+ * address (make it before any stream capture) and keeps it for the process; a
+ * device reset makes it stale, so do not call this again after one.  All calls
+ * share the array and
  * leave their contents in it; calls whose GPU work overlaps race and must be
  * serialised by the caller.  Returns after the work has completed. */
 TESSA_API int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* args, void* stream);
@@ -399,6 +401,25 @@ typedef struct tessa_prepared_replay {
 #define TESSA_MODE_A3_SQ8_WMMA_BATCH8 3u
 #define TESSA_MODE_SQ8_DP4A_BATCH8 4u
 #define TESSA_MODE_SQ8_WMMA_BATCH1 5u
+
+/* ---------------------------------------------------- failure path --- */
+
+/* Limit of every bounded device wait of the context's kernels (default 2 s;
+ * 0 restores it; 10 ms .. 60 s).  A wait that runs out records
+ * TESSA_DEVERR_TIMEOUT, every role of the kernel drains (waiting, under the
+ * same limit, for its copies and MMAs in flight), tensor memory is freed and
+ * the call returns TESSA_ERR_TIMEOUT -- as the reference's watchdog gives up
+ * with a status instead of trapping (CB:5024-5025, CB:5883-5930). */
+TESSA_API int tessa_set_wait_timeout_ns(tessa_ctx* ctx, uint64_t timeout_ns);
+
+/* Self-test of that failure path (no counterpart in the reference): one CTA
+ * waits, through the library's bounded wait, on a shared-memory barrier that
+ * nothing arrives on, while a second warp waits with a much longer limit.  The
+ * first wait gives up after timeout_ns (1 us .. 60 s) and raises the CTA's
+ * abort flag, the second warp leaves at its next check, and the call returns
+ * TESSA_ERR_TIMEOUT with *elapsed_ns (may be NULL) the kernel's own wait time.
+ * The context stays usable.  No copy or MMA is in flight during the probe. */
+TESSA_API int tessa_check_bounded_wait(tessa_ctx* ctx, uint64_t timeout_ns, uint64_t* elapsed_ns, void* stream);
 
 /* ------------------------------------------------ subtree partition --- */
 

@@ -48,6 +48,11 @@ int fail(int code, const char* fmt, ...) {
   } while (0)
 
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // bounded device waits: 2 s
+// A pipeline's drain after a wait gives up waits, under the same limit, for
+// its in-flight copies and MMAs (microseconds); the floor keeps the limit far
+// above that, the ceiling keeps a stuck kernel from holding the GPU long.
+constexpr uint64_t kMinTimeoutNs = 10000000ull;      // 10 ms
+constexpr uint64_t kMaxTimeoutNs = 60000000000ull;   // 60 s
 constexpr uint64_t kDefaultHostBatchBytes = 128ull << 20;  // codes per batch of the host-buffer pipeline
 constexpr uint64_t kMaxHostBatches = 64;
 
@@ -269,6 +274,7 @@ struct tessa_ctx {
   tessa_d0_profile d0_prof = {};
   SubtreeState* subtree = nullptr;  // subtree partition scratch (created on first use)
   DevBuf g_cursor, g_temp;          // record grouping: per-point cursors, scan scratch
+  DevBuf probe;                     // bounded-wait probe: elapsed time
 };
 
 namespace {
@@ -804,6 +810,7 @@ void tessa_destroy(tessa_ctx* ctx) {
   ctx->subtree = nullptr;
   ctx->g_cursor.release();
   ctx->g_temp.release();
+  ctx->probe.release();
   for (cudaStream_t s : {ctx->stream_in, ctx->stream_out})
     if (s) {
       cudaStreamSynchronize(s);
@@ -1487,5 +1494,66 @@ int tessa_group_edges(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t*
   if (rc != TESSA_OK) return fail(rc, "edge grouping failed (%s)", cudaGetErrorString(cudaGetLastError()));
   uint32_t bits = 0;
   TRY(read_err(ctx, st, &bits));
+  return map_device_error(bits);
+}
+
+// --------------------------------------------------- bounded-wait probe
+
+namespace {
+
+// Two waiters on barriers that nothing arrives on: warp 0 with the probe's
+// limit, warp 1 with a limit far beyond it.  Warp 0 gives up first, records
+// the timeout and raises the CTA's abort flag; warp 1 must then leave at its
+// next check instead of running to its own limit -- the way every role of a
+// pipeline drains after one of its waits gives up.
+__global__ void wait_probe_kernel(uint32_t* err_word, uint64_t timeout_ns, unsigned long long* elapsed_ns) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t abort_word;
+  volatile uint32_t* abort_flag = &abort_word;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    abort_word = 0u;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint64_t t0 = global_timer_ns();
+  if (threadIdx.x == 0) mbar_wait(&bars[0], 0u, abort_flag, err_word, timeout_ns);
+  if (threadIdx.x == 32) mbar_wait(&bars[1], 0u, abort_flag, err_word, 20ull * timeout_ns + 2000000000ull);
+  __syncthreads();
+  if (threadIdx.x == 0) *elapsed_ns = global_timer_ns() - t0;
+}
+
+}  // namespace
+
+int tessa_set_wait_timeout_ns(tessa_ctx* ctx, uint64_t timeout_ns) {
+  if (!ctx) return fail(TESSA_ERR_INVALID_ARG, "null context");
+  if (timeout_ns == 0) {
+    ctx->timeout_ns = kDefaultTimeoutNs;
+    return TESSA_OK;
+  }
+  if (timeout_ns < kMinTimeoutNs || timeout_ns > kMaxTimeoutNs)
+    return fail(TESSA_ERR_INVALID_ARG, "wait limit %llu ns outside %llu..%llu ns", (unsigned long long)timeout_ns,
+                (unsigned long long)kMinTimeoutNs, (unsigned long long)kMaxTimeoutNs);
+  ctx->timeout_ns = timeout_ns;
+  return TESSA_OK;
+}
+
+int tessa_check_bounded_wait(tessa_ctx* ctx, uint64_t timeout_ns, uint64_t* elapsed_ns, void* stream) {
+  TRY(bind(ctx));
+  if (timeout_ns < 1000ull || timeout_ns > kMaxTimeoutNs)
+    return fail(TESSA_ERR_INVALID_ARG, "probe limit %llu ns outside 1000..%llu ns", (unsigned long long)timeout_ns,
+                (unsigned long long)kMaxTimeoutNs);
+  cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+  TRY(ctx->probe.ensure(8));
+  TRY(clear_err(ctx, st));
+  wait_probe_kernel<<<1, 64, 0, st>>>(ctx->d_err.as<uint32_t>(), timeout_ns,
+                                       ctx->probe.as<unsigned long long>());
+  CUDA_TRY(cudaGetLastError());
+  uint64_t ns = 0;
+  CUDA_TRY(cudaMemcpyAsync(&ns, ctx->probe.ptr, 8, cudaMemcpyDeviceToHost, st));
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  if (elapsed_ns) *elapsed_ns = ns;
   return map_device_error(bits);
 }

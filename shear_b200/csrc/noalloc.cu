@@ -15,6 +15,9 @@
 // array's symbol as a device address: the first call on each device (with that
 // device current) resolves the real address with cudaGetSymbolAddress and
 // caches it, so that first call should be made before any stream capture.
+// The cached address belongs to the device's primary context: after
+// cudaDeviceReset (or anything else that destroys that context) it is stale,
+// and this entry point must not be called again in that process.
 // All calls share the array and a call leaves its contents behind; calls whose
 // GPU work overlaps (same device, different streams, or different host threads)
 // race on it and must be serialised by the caller.  The call allocates nothing:
@@ -94,6 +97,7 @@ extern "C" int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* a, void* strea
                        !a->topk_ids || !a->topk_dists))
     return err(TESSA_ERR_INVALID_ARG, "null leaf data pointer");
   if (a->leaf_rows > 0x7fffffffull) return err(TESSA_ERR_UNSUPPORTED, "more than 2^31 leaf member rows");
+  if (a->resident_rows > 0xffffffffull) return err(TESSA_ERR_UNSUPPORTED, "more than 2^32 resident rows");
 
   // Tile count and layout checks (no host allocation: one pass over the layout).
   uint64_t num_tiles = 0;
@@ -173,7 +177,7 @@ extern "C" int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* a, void* strea
   if (gather) {
     r = launch_gather_rows(a->codes, a->leaf_members, a->leaf_rows, a->padded_dim,
                            reinterpret_cast<int8_t*>(s + off_codes), sms, st);
-    if (r != TESSA_OK) return err(r, "gather launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    if (r != TESSA_OK) return err(r, "gather kernel launch failed (code %d)", r);
     leaf_codes = reinterpret_cast<const int8_t*>(s + off_codes);
   }
 
@@ -200,7 +204,7 @@ extern "C" int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* a, void* strea
   L.timeout_ns = kTimeoutNs;
   L.sm_count = sms;
   r = launch_leaf_topk_sq8(L, st);
-  if (r != TESSA_OK) return err(r, "leaf kernel launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  if (r != TESSA_OK) return err(r, "leaf kernel launch failed (code %d)", r);
 
   uint32_t bits = 0;
   if ((e = cudaMemcpyAsync(&bits, s + off_err, 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess)
