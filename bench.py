@@ -210,12 +210,15 @@ def int8_peak_tops(torch, dev):
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one config-2
 # leaf step, from one ncu capture of the three leaf kernels (one launch each)
-# on 256 leaves of the same shape (inputs 4x the L2), scaled by 4096/256 leaves:
-#   python bench.py --leaves 256 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline &&
+# on 256 leaves of the same shape (400 MB of codes, 3x the L2), scaled by
+# 4096/256 leaves (the fallback's share scales with its rows, 289 per 256
+# leaves in the capture, 4,471 per step in the bench):
+#   python bench.py --workload leaf --leaves 256 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline &&
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum \
-#       --clock-control none -k regex:"leaf_topk_split|leaf_finish|leaf_fallback" -s 3 -c 3 \
-#       python bench.py --leaves 256 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline
-LEAF_STEP_TRAFFIC = {"leaf_topk_split_kernel": 8.65e9, "leaf_finish_kernel": 4.28e9, "leaf_fallback_kernel": None}
+#       --clock-control none -k regex:"leaf_topk_split|leaf_finish|leaf_fallback" -s 9 -c 3 \
+#       python bench.py --workload leaf --leaves 256 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline
+LEAF_STEP_TRAFFIC = {"leaf_topk_split_kernel": 16 * 647565312, "leaf_finish_kernel": 16 * 335143680,
+                     "leaf_fallback_kernel": 16 * 289767168}
 
 
 def host_oracle():
@@ -1091,6 +1094,68 @@ def run_assign(a):
             dist.barrier()
             dist.destroy_process_group()
         return 0
+    # ---- e2e: the step's rows from pinned host memory, tessa_assign, results back
+    e2e = None
+    if not a.no_e2e and a.e2e_steps > 0 and world == 1:
+        if a.assign_fp32:
+            hx, hn = x.cpu().pin_memory(), raw_norms.cpu().pin_memory()
+            dx, dn = torch.empty_like(x), torch.empty_like(raw_norms)
+            h2d = hx.numel() * 4 + hn.numel() * 4
+        else:
+            hc, hs, hq = codes.cpu().pin_memory(), scales.cpu().pin_memory(), qn.cpu().pin_memory()
+            dc, ds_, dq = torch.empty_like(codes), torch.empty_like(scales), torch.empty_like(qn)
+            h2d = hc.numel() + hs.numel() * 4 + hq.numel() * 4
+        oi = torch.empty(n * a.assign_rh, dtype=torch.int32).pin_memory()
+        od = torch.empty(n * a.assign_rh, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            if a.assign_fp32:
+                dx.copy_(hx, non_blocking=True)
+                dn.copy_(hn, non_blocking=True)
+                ids, dists = ops.assign(src, x=dx, raw_norms=dn, global_ids=gids, members=members, leaders=lead,
+                                        task_member_offsets=moff, task_member_counts=mcnt, task_leader_offsets=loff,
+                                        task_leader_counts=lcnt, task_rh=rh, task_output_offsets=outoff,
+                                        output_len=n * a.assign_rh, ctx=ctx)
+            else:
+                dc.copy_(hc, non_blocking=True)
+                ds_.copy_(hs, non_blocking=True)
+                dq.copy_(hq, non_blocking=True)
+                ids, dists = ops.assign(src, codes=dc, scales=ds_, sq8_norms=dq, global_ids=gids, members=members,
+                                        leaders=lead, task_member_offsets=moff, task_member_counts=mcnt,
+                                        task_leader_offsets=loff, task_leader_counts=lcnt, task_rh=rh,
+                                        task_output_offsets=outoff, output_len=n * a.assign_rh, ctx=ctx)
+            oi.copy_(ids, non_blocking=True)
+            od.copy_(dists, non_blocking=True)
+            torch.cuda.synchronize(dev)
+        e2e_step()
+        t0 = time.perf_counter()
+        for _ in range(a.e2e_steps):
+            e2e_step()
+        e2e_s = (time.perf_counter() - t0) / a.e2e_steps
+        e2e = {"value": n / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(n * a.assign_rh * 8), "ms_per_step": e2e_s * 1e3,
+               "timing": "wall clock: pinned H2D of the rows, tessa_assign, D2H of ids and distances"}
+
+    cpu = None
+    if not a.no_cpu_baseline and world == 1:
+        O = host_oracle()
+        t_take = min(a.leaves, max(O.num_threads(), 1) * 8)
+        sel = slice(0, t_take)
+        rows_s = int(np.sum(mcnt[sel]))
+        xs = (x[:rows_s].cpu().numpy() if a.assign_fp32 else np.zeros((rows_s, 1), np.float32))
+        ns = (raw_norms if a.assign_fp32 else qn)[:rows_s].cpu().numpy()
+        cs, ss = codes[:rows_s].cpu().numpy(), scales[:rows_s].cpu().numpy()
+        g_s = np.arange(rows_s, dtype=np.uint32)
+        lds = leaders[:int(np.sum(lcnt[sel]))]
+        outs = np.asarray(outoff[sel], np.uint64)
+        t0 = time.perf_counter()
+        O.assign(0 if a.assign_fp32 else 3, xs, ns, cs, ss, g_s, g_s, lds, moff[sel], mcnt[sel], loff[sel],
+                 lcnt[sel], rh[sel], outs, rows_s * a.assign_rh)
+        dt = time.perf_counter() - t0
+        cpu = {"value": rows_s / dt, "unit": "rows/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"{t_take} of {a.leaves} tasks ({rows_s} rows) in {dt:.2f} s, oracle/tessa_oracle.c "
+                         f"oracle_assign (OpenMP over rows)"}
+
     peaks = measured_peaks()
     hbm = peaks.get("hbm_gbs") or 6650.0
     row_bytes = a.dim * 4 + 4 if a.assign_fp32 else codes.shape[1] + 8
@@ -1111,7 +1176,7 @@ def run_assign(a):
         "vs_baseline": None, "dtype": "f32" if a.assign_fp32 else "int8",
         "data": "synthetic: N(0,1) rows, L2-normalised; leaders drawn from each task's members (seed 1+rank)",
         "config": dict(assign_desc(a), parallelism=f"task-sharded x{world} (independent, no collective)"),
-        "roofline": roofline, "cpu_baseline": None, "e2e": None, "gpu_launches": a.steps,
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": a.steps,
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -1223,7 +1288,8 @@ def run_build(a):
     dev = torch.device("cuda", torch.cuda.current_device())
     ctx = ops.context(dev.index)
     c = build_cfg(a)
-    p = BuildParams(c_max=c["c_max"])
+    # the host cores are shared by every rank's reducer
+    p = BuildParams(c_max=c["c_max"], reducer_threads=max(1, (os.cpu_count() or 1) // world))
     # every rank builds its own index of the config's size (weak scaling: builds are independent)
     x = make_mixture(torch, dev, c["rows"], c, seed=1234 + rank)
     n = c["rows"]
