@@ -500,11 +500,14 @@ typedef struct tessa_edge {
  * edges of flush_compact_topk_batch_into_edges (P/leaf_build.rs:1749-1808; for
  * row i and rank r with id j != 0xffffffff and a finite distance d,
  * (point_ids[i] -> j, hash_fwd, d) and (j -> point_ids[i], hash_rev, d)) laid
- * out so that point p's edges are edges[offsets[p] .. offsets[p+1]).  All
- * pointers are device pointers; offsets has num_points + 1 entries, edges
- * edge_capacity >= 2 * rows * k.  The order of a point's edges within its
- * group is unspecified (the reservoir does not depend on it).  Ids at or above
- * num_points are TESSA_ERR_BAD_ROW.  Synchronous on `stream`. */
+ * out so that point p's edges are edges[offsets[p] .. offsets[p+1]), ascending
+ * by target.  An edge that repeats another exactly (same source, target, hash
+ * and distance -- overlapping leaves produce every edge many times) is kept
+ * once: a reservoir ignores a repeated candidate, so the reduction's result is
+ * unchanged.  All pointers are device pointers; offsets has num_points + 1
+ * entries, edges edge_capacity >= 2 * rows * k; 2 * rows * k must be below
+ * 2^32.  Ids at or above num_points are TESSA_ERR_BAD_ROW.  Synchronous on
+ * `stream`. */
 TESSA_API int tessa_group_edges(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids,
                                 const float* topk_dists, const uint16_t* hash_fwd, const uint16_t* hash_rev,
                                 uint64_t rows, uint32_t k, uint64_t num_points, uint64_t* offsets, tessa_edge* edges,

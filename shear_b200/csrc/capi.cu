@@ -273,7 +273,7 @@ struct tessa_ctx {
   cudaEvent_t d0_ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // phase boundaries of a D0 call
   tessa_d0_profile d0_prof = {};
   SubtreeState* subtree = nullptr;  // subtree partition scratch (created on first use)
-  DevBuf g_cursor, g_temp;          // record grouping: per-point cursors, scan scratch
+  DevBuf g_temp;                    // record grouping: sort and scan scratch
   DevBuf probe;                     // bounded-wait probe: elapsed time
 };
 
@@ -808,7 +808,6 @@ void tessa_destroy(tessa_ctx* ctx) {
   for (DevBuf* b : bufs) b->release();
   subtree_state_free(ctx->subtree);
   ctx->subtree = nullptr;
-  ctx->g_cursor.release();
   ctx->g_temp.release();
   ctx->probe.release();
   for (cudaStream_t s : {ctx->stream_in, ctx->stream_out})
@@ -1482,16 +1481,17 @@ int tessa_group_edges(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t*
   if (edge_capacity < 2 * rows * (uint64_t)k)
     return fail(TESSA_ERR_INVALID_ARG, "edge_capacity %llu below 2 * rows * k = %llu",
                 (unsigned long long)edge_capacity, (unsigned long long)(2 * rows * (uint64_t)k));
+  const uint64_t m = 2 * rows * (uint64_t)k;
+  if (m >= 0xffffffffull)
+    return fail(TESSA_ERR_UNSUPPORTED, "2 * rows * k = %llu edges in one batch; at most 2^32 - 1 (split the batch)",
+                (unsigned long long)m);
   cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
-  TRY(ctx->g_cursor.ensure(num_points * 8));
-  size_t need = group_edges_temp_bytes(num_points);
-  TRY(ctx->g_temp.ensure(need + 256));
+  TRY(ctx->g_temp.ensure(group_edges_scratch_bytes(m, num_points)));
   TRY(clear_err(ctx, st));
   GroupEdgesCall g{point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, rows, k, num_points, offsets,
-                   ctx->g_cursor.as<uint64_t>(), edges, ctx->g_temp.ptr, ctx->g_temp.bytes, &need,
-                   ctx->d_err.as<uint32_t>(), ctx->sm_count};
+                   edges, ctx->g_temp.ptr, ctx->g_temp.bytes, ctx->d_err.as<uint32_t>(), ctx->sm_count};
   const int rc = group_edges(g, st);
-  if (rc != TESSA_OK) return fail(rc, "edge grouping failed (%s)", cudaGetErrorString(cudaGetLastError()));
+  if (rc != TESSA_OK) return fail(rc, "edge grouping failed (code %d)", rc);
   uint32_t bits = 0;
   TRY(read_err(ctx, st, &bits));
   return map_device_error(bits);

@@ -182,16 +182,14 @@ struct GroupEdgesCall {
   uint32_t k;
   uint64_t num_points;
   uint64_t* offsets;      // num_points + 1
-  uint64_t* cursor;       // num_points scratch
   tessa_edge* edges;      // capacity >= 2 * rows * k
-  void* temp;             // scan scratch
+  void* temp;             // group_edges_scratch_bytes(2 * rows * k, num_points)
   size_t temp_bytes;
-  size_t* temp_needed;
   uint32_t* d_err;
   int sm_count;
 };
 int group_edges(const GroupEdgesCall& g, cudaStream_t stream);
-size_t group_edges_temp_bytes(uint64_t num_points);
+size_t group_edges_scratch_bytes(uint64_t edges, uint64_t num_points);
 
 // Records `code` and `message` as the calling thread's last error (returned by
 // tessa_last_error_message); returns `code`.
