@@ -155,6 +155,89 @@ def _grouping_buffers(torch, dev, n, cap):
     return bufs[0][:n + 1], bufs[1][:max(cap, 1) * 12]
 
 
+def _upload(x, dev, torch):
+    if isinstance(x, np.ndarray):
+        xh = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+        return xh.pin_memory().to(dev, non_blocking=True) if xh.numel() else xh.to(dev)
+    return x.contiguous()
+
+
+def d0_stage(xd, p: BuildParams, ctx):
+    """SQ8 codes of every row, its fanout_top root leaders, and the child runs
+    (rows ascending per leader).  Deterministic: every rank of a multi-GPU
+    build computes the same result."""
+    import torch
+
+    dev = xd.device
+    n, dim = xd.shape
+    props = torch.cuda.get_device_properties(dev)
+    k0, plan = root_leader_count(n, dim, p, props.total_memory)
+    fanout = min(p.fanout_top, k0)
+    leaders = sample_root_leaders(n, k0, p.random_seed)
+    lid = torch.from_numpy(leaders.view(np.int32)).to(dev)
+    gids = torch.arange(n, dtype=torch.int32, device=dev)
+    d0 = ops.quantize_sq8_assign_d0(xd, gids, lid, fanout, leader_vectors=xd[lid.long()], ctx=ctx)
+    members, counts, offsets = group_child_runs(d0.child_ids, k0)
+    depth, parent, min_rec = child_seed_args(p, n)
+    seeds = np.array([ops.subtree_root_seed(p.random_seed, depth, int(c), parent, min_rec) for c in counts],
+                     np.uint64)
+    big = int(len(counts) - 1 - np.argmax(counts[::-1]))
+    entry = int(members[int(offsets[big])].item()) if counts[big] else 0
+    return dict(d0=d0, gids=gids, members=members, counts=counts, offsets=offsets, seeds=seeds, k0=k0,
+                plan=plan, fanout=fanout, depth=depth, entry=entry)
+
+
+def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None):
+    """Subtree partition of the child runs `tasks` (all when None), their
+    leaves' top-k lists and both sketch hashes of every slot, on the device."""
+    import torch
+
+    timings = {} if timings is None else timings
+    dev = xd.device
+    n, dim = xd.shape
+    d0 = st["d0"]
+    sel = np.arange(len(st["counts"])) if tasks is None else np.asarray(tasks, np.int64)
+    t = time.perf_counter()
+    sp = ops.SubtreeParams(c_max=p.adaptive_c_max(n), max_depth=p.max_depth, max_leaders=p.max_leaders,
+                           fanout_second=p.fanout_second, root_depth=st["depth"], psamp_fraction=p.psamp_fraction)
+    leaf_rows, starts, sizes, _, pst = ops.subtree_partition(d0.codes, d0.scales, d0.norms, st["members"],
+                                                             st["offsets"][sel], st["counts"][sel],
+                                                             st["seeds"][sel], sp, ctx=ctx)
+    torch.cuda.synchronize(dev)
+    timings["partition_s"] = time.perf_counter() - t
+    t = time.perf_counter()
+    k = max(1, min(p.leaf_knn, 32))
+    rows = int(leaf_rows.numel())
+    ids = torch.full((rows * k,), -1, dtype=torch.int32, device=dev)
+    dists = torch.full((rows * k,), float("inf"), dtype=torch.float32, device=dev)
+    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    ev[0].record()
+    ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, st["gids"], leaf_rows, starts, sizes, k, out=(ids, dists),
+                      ctx=ctx)
+    ev[1].record()
+    planes = torch.from_numpy(hyperplanes(p.m_hash_bits, dim, p.random_seed)).to(dev)
+    sketches = ops.sketch_rows(xd, planes, ctx=ctx)
+    hf, hr = ops.edge_hashes(leaf_rows, ids, k, sketches, p.m_hash_bits, starts, sizes, ctx=ctx)
+    torch.cuda.synchronize(dev)
+    timings["leaf_s"] = time.perf_counter() - t
+    timings["leaf_kernel_ms"] = ev[0].elapsed_time(ev[1])
+    return dict(leaf_rows=leaf_rows, ids=ids, dists=dists, hf=hf, hr=hr, k=k, starts=starts, sizes=sizes,
+                partition=pst, fallback=ops.leaf_last_fallback_rows(ctx))
+
+
+def group_stage(rec: dict, n: int, ctx):
+    """Distinct candidate edges grouped by reservoir on the device:
+    (offsets int64 [n + 1], edges uint8 [total * 12], total)."""
+    import torch
+
+    dev = rec["ids"].device
+    rows, k = int(rec["leaf_rows"].numel()), rec["k"]
+    goff, gedges = ops.group_edges(rec["leaf_rows"], rec["ids"], rec["dists"], rec["hf"], rec["hr"], k, n, ctx=ctx,
+                                   out=_grouping_buffers(torch, dev, n, 2 * rows * k))
+    total = int(goff[n].item())
+    return goff, gedges[:total * 12], total
+
+
 def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> BuildResult:
     """Build the graph of x (numpy f32 [n, dim] on the host -- copied to the
     device inside -- or a CUDA f32 tensor already resident)."""
@@ -166,69 +249,29 @@ def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> B
     timings = {}
     sync = lambda: torch.cuda.synchronize(dev)
     t_all = time.perf_counter()
-    if isinstance(x, np.ndarray):
-        xh = torch.from_numpy(np.ascontiguousarray(x, np.float32))
-        xd = xh.pin_memory().to(dev, non_blocking=True) if xh.numel() else xh.to(dev)
-    else:
-        xd = x.contiguous()
+    xd = _upload(x, dev, torch)
     n, dim = xd.shape
     sync()
     timings["upload_s"] = time.perf_counter() - t_all
 
     # ---- D0: SQ8 codes of every row and its fanout_top root leaders
     t = time.perf_counter()
-    props = torch.cuda.get_device_properties(dev)
-    k0, plan = root_leader_count(n, dim, p, props.total_memory)
-    fanout = min(p.fanout_top, k0)
-    leaders = sample_root_leaders(n, k0, p.random_seed)
-    lid = torch.from_numpy(leaders.view(np.int32)).to(dev)
-    gids = torch.arange(n, dtype=torch.int32, device=dev)
-    d0 = ops.quantize_sq8_assign_d0(xd, gids, lid, fanout, leader_vectors=xd[lid.long()], ctx=ctx)
-    members, counts, offsets = group_child_runs(d0.child_ids, k0)
+    st = d0_stage(xd, p, ctx)
     sync()
     timings["d0_s"] = time.perf_counter() - t
 
-    # ---- subtree partition of every child run
-    t = time.perf_counter()
-    depth, parent, min_rec = child_seed_args(p, n)
-    seeds = np.array([ops.subtree_root_seed(p.random_seed, depth, int(c), parent, min_rec) for c in counts],
-                     np.uint64)
-    sp = ops.SubtreeParams(c_max=p.adaptive_c_max(n), max_depth=p.max_depth, max_leaders=p.max_leaders,
-                           fanout_second=p.fanout_second, root_depth=depth, psamp_fraction=p.psamp_fraction)
-    leaf_rows, starts, sizes, tasks, pst = ops.subtree_partition(d0.codes, d0.scales, d0.norms, members, offsets,
-                                                                 counts, seeds, sp, ctx=ctx)
-    sync()
-    timings["partition_s"] = time.perf_counter() - t
-
-    # ---- leaf top-k and edge hashes
-    t = time.perf_counter()
-    k = max(1, min(p.leaf_knn, 32))
-    rows = int(leaf_rows.numel())
-    ids = torch.full((rows * k,), -1, dtype=torch.int32, device=dev)
-    dists = torch.full((rows * k,), float("inf"), dtype=torch.float32, device=dev)
-    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-    ev[0].record()
-    ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, gids, leaf_rows, starts, sizes, k, out=(ids, dists), ctx=ctx)
-    ev[1].record()
-    planes = torch.from_numpy(hyperplanes(p.m_hash_bits, dim, p.random_seed)).to(dev)
-    sketches = ops.sketch_rows(xd, planes, ctx=ctx)
-    hf, hr = ops.edge_hashes(leaf_rows, ids, k, sketches, p.m_hash_bits, starts, sizes, ctx=ctx)
-    sync()
-    timings["leaf_s"] = time.perf_counter() - t
-    timings["leaf_kernel_ms"] = ev[0].elapsed_time(ev[1])
-    leaf_fallback = ops.leaf_last_fallback_rows(ctx)
+    # ---- subtree partition of every child run, leaf top-k, edge hashes
+    rec = records_stage(xd, st, p, ctx, timings=timings)
 
     # ---- candidate records grouped by reservoir on the device, pinned D2H,
     #      host HashPrune reduction
     t = time.perf_counter()
-    goff, gedges = ops.group_edges(leaf_rows, ids, dists, hf, hr, k, n, ctx=ctx,
-                                   out=_grouping_buffers(torch, dev, n, 2 * rows * k))
-    total = int(goff[n].item())
+    goff, gedges, total = group_stage(rec, n, ctx)
     h_off = _pinned("offsets", torch, (n + 1) * 8)
     h_edges = _pinned("edges", torch, max(total, 1) * 12)
     h_off.copy_(goff.view(torch.uint8), non_blocking=True)
     if total:
-        h_edges[:total * 12].copy_(gedges[:total * 12], non_blocking=True)
+        h_edges[:total * 12].copy_(gedges, non_blocking=True)
     sync()
     timings["group_d2h_s"] = time.perf_counter() - t
     t = time.perf_counter()
@@ -239,19 +282,20 @@ def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> B
     red.close()
     timings["reduce_s"] = time.perf_counter() - t
     timings["total_s"] = time.perf_counter() - t_all
+    return BuildResult(offs, nb, st["entry"], timings, _stats(st, rec, n, dim, edges, total))
 
-    # entry point: first row of the largest child run (last one among equals)
-    big = int(len(counts) - 1 - np.argmax(counts[::-1]))
-    entry = int(members[int(offsets[big])].item()) if counts[big] else 0
-    stats = dict(points=n, dim=dim, root_leaders=k0, root_plan=plan, fanout_top=fanout,
-                 child_rows=int(counts.sum()), leaves=int(sizes.size), leaf_rows=int(sizes.sum()),
-                 leaf_rows_mean=float(sizes.mean()) if sizes.size else 0.0, leaf_k=k, edges=edges,
-                 leaf_pairs=int((sizes.astype(np.int64) * (sizes.astype(np.int64) - 1)).sum()),
-                 leaf_ops=int(2 * d0.codes.shape[1] * (sizes.astype(np.int64) ** 2).sum()),
-                 leaf_fallback_rows=int(leaf_fallback), partition=pst,
-                 d2h_bytes=int((n + 1) * 8 + total * 12),
-                 # quantize + D0 rectangular kernel + its exact fallback + fragments; partition;
-                 # gather + column-split leaf kernel + finish + fallback; sketches; edge hashes;
-                 # record grouping (count, scan, scatter)
-                 kernel_launches=4 + pst["kernel_launches"] + 4 + 2 + 3)
-    return BuildResult(offs, nb, entry, timings, stats)
+
+def _stats(st, rec, n, dim, edges, total):
+    sizes = rec["sizes"]
+    pst = rec["partition"]
+    return dict(points=n, dim=dim, root_leaders=st["k0"], root_plan=st["plan"], fanout_top=st["fanout"],
+                child_rows=int(st["counts"].sum()), leaves=int(sizes.size), leaf_rows=int(sizes.sum()),
+                leaf_rows_mean=float(sizes.mean()) if sizes.size else 0.0, leaf_k=rec["k"], edges=edges,
+                leaf_pairs=int((sizes.astype(np.int64) * (sizes.astype(np.int64) - 1)).sum()),
+                leaf_ops=int(2 * st["d0"].codes.shape[1] * (sizes.astype(np.int64) ** 2).sum()),
+                leaf_fallback_rows=int(rec["fallback"]), partition=pst,
+                d2h_bytes=int((n + 1) * 8 + total * 12),
+                # quantize + D0 rectangular kernel + its exact fallback + fragments; partition;
+                # gather + column-split leaf kernel + finish + fallback; sketches; edge hashes;
+                # record grouping (keys, mark, emit; the sorts and scans are CUB's)
+                kernel_launches=4 + pst["kernel_launches"] + 4 + 2 + 3)
