@@ -43,7 +43,7 @@ extern "C" {
 
 /* 1: leaf, quantize, assignment, replay; 2: + host pipeline knob, global D0, candidate
  * edges, capture digests, graph search (additive); 3: + subtree partition (additive). */
-#define TESSA_ABI_VERSION 3
+#define TESSA_ABI_VERSION 4
 
 #define TESSA_OK 0
 #define TESSA_ERR_INVALID_ARG (-1)  /* malformed sizes, null pointers, k out of range */
@@ -541,6 +541,38 @@ TESSA_API int tessa_reducer_finish(const tessa_reducer* reducer, uint64_t* offse
 /* Edges inserted so far (forward and reverse). */
 TESSA_API int tessa_reducer_edges(const tessa_reducer* reducer, uint64_t* edges);
 TESSA_API void tessa_reducer_destroy(tessa_reducer* reducer);
+
+/* HashPrune reservoirs built on the device.  The result equals the host
+ * reducer above (and the reference's sequence of insert_inner calls,
+ * P/hash_prune.rs:1326-1452) on the same edges: each source's slots are the
+ * l_max best, in the total order (distance via total_cmp, target, hash) of
+ * P/hash_prune.rs:2094-2130, of the per-hash minima of its edges, written in
+ * hash order.  Outputs (device): out_offsets (num_points + 1 entries) and the
+ * slots as neighbour ids (out_neighbors) and/or full slots (out_slots, which
+ * can be fed back as grouped input); either may be NULL.  slot_capacity >=
+ * min(edges, num_points * l_max) always suffices; *slot_count (host) gets the
+ * slot total, and a capacity below it is TESSA_ERR_INVALID_ARG after the
+ * offsets are written.  l_max in 1..255.  Synchronous on `stream`.
+ *
+ * tessa_reduce_records takes leaf records as tessa_reducer_add does (device
+ * pointers; ids at or above num_points are TESSA_ERR_BAD_ROW; 2 * rows * k
+ * below 2^32).  tessa_reduce_grouped takes `groups` pieces of edges grouped by
+ * source over points 0 .. num_points-1 -- piece g: group_offsets[g] (device,
+ * num_points + 1 entries, not necessarily starting at 0) and group_edges[g]
+ * (device, group_edge_counts[g] edges from group_offsets[g][0] on); the
+ * pointer arrays and counts are host arrays -- such as tessa_group_edges'
+ * output or other reservoirs' out_slots.  Edges with a non-finite distance are
+ * skipped; the sum of the counts must be below 2^32. */
+TESSA_API int tessa_reduce_records(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids,
+                                   const float* topk_dists, const uint16_t* hash_fwd, const uint16_t* hash_rev,
+                                   uint64_t rows, uint32_t k, uint64_t num_points, uint32_t l_max,
+                                   uint64_t* out_offsets, uint32_t* out_neighbors, tessa_edge* out_slots,
+                                   uint64_t slot_capacity, uint64_t* slot_count, void* stream);
+TESSA_API int tessa_reduce_grouped(tessa_ctx* ctx, uint32_t groups, const uint64_t* const* group_offsets,
+                                   const tessa_edge* const* group_edges, const uint64_t* group_edge_counts,
+                                   uint64_t num_points, uint32_t l_max, uint64_t* out_offsets,
+                                   uint32_t* out_neighbors, tessa_edge* out_slots, uint64_t slot_capacity,
+                                   uint64_t* slot_count, void* stream);
 
 /* TessaCudaModeResult (P/tessa_replay.rs:190-200); caller-owned host buffers
  * of assignment_output_len and leaf_rows*leaf_k entries.  leaf_* may be NULL

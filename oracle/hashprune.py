@@ -82,9 +82,10 @@ class Reservoir:
         self._recompute_far()
 
 
-def reduce_leaf_batches(num_points: int, l_max: int, batches):
+def reduce_leaf_batches(num_points: int, l_max: int, batches, slots: bool = False):
     """batches: iterable of (point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, k).
-    Returns the per-point neighbour lists (slot targets in hash order)."""
+    Returns the per-point neighbour lists (slot targets in hash order), or with
+    slots=True the (target, hash, dist) slots themselves."""
     res = [Reservoir(l_max) for _ in range(num_points)]
     for pid, ids, ds, hf, hr, k in batches:
         pid = np.asarray(pid).view(np.uint32)
@@ -100,4 +101,6 @@ def reduce_leaf_batches(num_points: int, l_max: int, batches):
                     continue
                 res[p].insert(j, int(hf[s]), d)
                 res[j].insert(p, int(hr[s]), d)
+    if slots:
+        return [list(r.slots) for r in res]
     return [[t for t, _, _ in r.slots] for r in res]

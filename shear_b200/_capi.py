@@ -184,6 +184,12 @@ SIGNATURES = [
      [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, c_vp, c_vp,
       ctypes.c_uint64, c_vp]),
     ("tessa_reducer_destroy", None, [c_vp]),
+    ("tessa_reduce_records", ctypes.c_int,
+     [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32,
+      c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64), c_vp]),
+    ("tessa_reduce_grouped", ctypes.c_int,
+     [c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, c_vp, c_vp, c_vp,
+      ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64), c_vp]),
 ]
 
 _lib = None

@@ -1497,6 +1497,99 @@ int tessa_group_edges(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t*
   return map_device_error(bits);
 }
 
+// ------------------------------------------------ device reservoirs
+
+namespace {
+
+int reduce_common(tessa_ctx* ctx, ReservoirCall& r, uint64_t* slot_count, void* stream) {
+  if (!r.out_offsets || !slot_count) return fail(TESSA_ERR_INVALID_ARG, "null output offsets or slot count");
+  if (r.l_max == 0 || r.l_max > 255) return fail(TESSA_ERR_INVALID_ARG, "l_max=%u outside 1..255", r.l_max);
+  if (r.num_points == 0 || r.num_points > 0xffffffffull)
+    return fail(TESSA_ERR_INVALID_ARG, "num_points outside 1..2^32");
+  if (r.edges >= 0xffffffffull)
+    return fail(TESSA_ERR_UNSUPPORTED, "%llu edges in one reduction; at most 2^32 - 1 (reduce in pieces and merge "
+                "the reservoirs)", (unsigned long long)r.edges);
+  if (r.capacity && !r.out_neighbors && !r.out_slots)
+    return fail(TESSA_ERR_INVALID_ARG, "slot capacity given without an output array");
+  cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+  TRY(ctx->g_temp.ensure(reservoir_scratch_bytes(r.edges, r.num_points)));
+  TRY(clear_err(ctx, st));
+  r.temp = ctx->g_temp.ptr;
+  r.temp_bytes = ctx->g_temp.bytes;
+  r.d_err = ctx->d_err.as<uint32_t>();
+  r.sm_count = ctx->sm_count;
+  const int rc = reduce_reservoirs(r, st);
+  if (rc != TESSA_OK) return fail(rc, "reservoir reduction failed (code %d)", rc);
+  uint32_t bits = 0;
+  TRY(read_err(ctx, st, &bits));
+  TRY(map_device_error(bits));
+  uint64_t total = 0;
+  if (cudaMemcpyAsync(&total, r.out_offsets + r.num_points, 8, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return fail(TESSA_ERR_CUDA, "reading the slot total failed");
+  *slot_count = total;
+  if (total > r.capacity && (r.out_neighbors || r.out_slots))
+    return fail(TESSA_ERR_INVALID_ARG, "slot capacity %llu below the slot total %llu",
+                (unsigned long long)r.capacity, (unsigned long long)total);
+  return TESSA_OK;
+}
+
+}  // namespace
+
+int tessa_reduce_records(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t* topk_ids, const float* topk_dists,
+                         const uint16_t* hash_fwd, const uint16_t* hash_rev, uint64_t rows, uint32_t k,
+                         uint64_t num_points, uint32_t l_max, uint64_t* out_offsets, uint32_t* out_neighbors,
+                         tessa_edge* out_slots, uint64_t slot_capacity, uint64_t* slot_count, void* stream) {
+  TRY(bind(ctx));
+  if (rows && (!point_ids || !topk_ids || !topk_dists || !hash_fwd || !hash_rev))
+    return fail(TESSA_ERR_INVALID_ARG, "null record pointer");
+  if (k == 0 || k > TESSA_MAX_LEAF_K) return fail(TESSA_ERR_INVALID_ARG, "k=%u outside 1..%d", k, TESSA_MAX_LEAF_K);
+  ReservoirCall r{};
+  r.point_ids = point_ids;
+  r.topk_ids = topk_ids;
+  r.topk_dists = topk_dists;
+  r.hash_fwd = hash_fwd;
+  r.hash_rev = hash_rev;
+  r.rows = rows;
+  r.k = k;
+  r.edges = 2 * rows * (uint64_t)k;
+  r.num_points = num_points;
+  r.l_max = l_max;
+  r.out_offsets = out_offsets;
+  r.out_neighbors = out_neighbors;
+  r.out_slots = out_slots;
+  r.capacity = slot_capacity;
+  return reduce_common(ctx, r, slot_count, stream);
+}
+
+int tessa_reduce_grouped(tessa_ctx* ctx, uint32_t groups, const uint64_t* const* group_offsets,
+                         const tessa_edge* const* group_edges, const uint64_t* group_edge_counts,
+                         uint64_t num_points, uint32_t l_max, uint64_t* out_offsets, uint32_t* out_neighbors,
+                         tessa_edge* out_slots, uint64_t slot_capacity, uint64_t* slot_count, void* stream) {
+  TRY(bind(ctx));
+  if (groups == 0 || !group_offsets || !group_edges || !group_edge_counts)
+    return fail(TESSA_ERR_INVALID_ARG, "no groups, or a null group array");
+  ReservoirCall r{};
+  uint64_t m = 0;
+  for (uint32_t g = 0; g < groups; ++g) {
+    if (!group_offsets[g] || (group_edge_counts[g] && !group_edges[g]))
+      return fail(TESSA_ERR_INVALID_ARG, "group %u: null offsets or edges", g);
+    m += group_edge_counts[g];
+  }
+  r.groups = groups;
+  r.group_offsets = group_offsets;
+  r.group_edges = group_edges;
+  r.group_counts = group_edge_counts;
+  r.edges = m;
+  r.num_points = num_points;
+  r.l_max = l_max;
+  r.out_offsets = out_offsets;
+  r.out_neighbors = out_neighbors;
+  r.out_slots = out_slots;
+  r.capacity = slot_capacity;
+  return reduce_common(ctx, r, slot_count, stream);
+}
+
 // --------------------------------------------------- bounded-wait probe
 
 namespace {

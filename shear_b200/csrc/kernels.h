@@ -191,6 +191,36 @@ struct GroupEdgesCall {
 int group_edges(const GroupEdgesCall& g, cudaStream_t stream);
 size_t group_edges_scratch_bytes(uint64_t edges, uint64_t num_points);
 
+// Device HashPrune reservoirs (reservoirs.cu): leaf records (groups == 0) or
+// edges grouped by source in `groups` CSR pieces -> each source's l_max best
+// per-hash minima in hash order.
+struct ReservoirCall {
+  const uint32_t* point_ids;
+  const uint32_t* topk_ids;
+  const float* topk_dists;
+  const uint16_t* hash_fwd;
+  const uint16_t* hash_rev;
+  uint64_t rows;
+  uint32_t k;
+  uint32_t groups;
+  const uint64_t* const* group_offsets;  // host array of device pointers
+  const tessa_edge* const* group_edges;  // host array of device pointers
+  const uint64_t* group_counts;          // host array
+  uint64_t edges;                        // 2 * rows * k, or the sum of group_counts
+  uint64_t num_points;
+  uint32_t l_max;
+  uint64_t* out_offsets;
+  uint32_t* out_neighbors;
+  tessa_edge* out_slots;
+  uint64_t capacity;
+  void* temp;  // reservoir_scratch_bytes(edges, num_points)
+  size_t temp_bytes;
+  uint32_t* d_err;
+  int sm_count;
+};
+int reduce_reservoirs(const ReservoirCall& r, cudaStream_t stream);
+size_t reservoir_scratch_bytes(uint64_t edges, uint64_t num_points);
+
 // Records `code` and `message` as the calling thread's last error (returned by
 // tessa_last_error_message); returns `code`.
 int set_last_error(int code, const char* message);

@@ -18,9 +18,12 @@ Reference flow (shear-core/src/algorithm/pipnn/, Rust):
 Here: D0 = tessa_quantize_sq8_assign_d0 (rectangular tcgen05 kernel), child
 runs grouped on the device, all subtree tasks partitioned in one
 tessa_subtree_partition call, leaves through tessa_leaf_topk_sq8, hashes
-through tessa_sketch_rows / tessa_edge_hashes, records grouped by reservoir on
-the device (tessa_group_edges), copied to pinned host memory and reduced by
-the host reducer (tessa_reducer_add_grouped).
+through tessa_sketch_rows / tessa_edge_hashes, and the HashPrune reservoirs built on
+the device (tessa_reduce_records); only the graph (CSR) is copied to pinned
+host memory.  The reference's host-side form -- records grouped by reservoir
+on the device (tessa_group_edges), copied to the host and reduced by the host
+reducer (tessa_reducer_add_grouped) -- is BuildParams.reduction = "host"; both
+give the same graph.
 
 Two inputs the reference draws from Rust's StdRng (rand 0.9, ChaCha12),
 which cannot be reproduced outside Rust, come from seeded numpy generators
@@ -59,6 +62,9 @@ class BuildParams:
     root_leaders: int | None = None        # None: the D0 capacity plan decides
     workspace_bytes: int | None = None     # None: 90% of the device
     reducer_threads: int = 0
+    # "device": HashPrune reservoirs built on the GPU (tessa_reduce_records);
+    # "host": records grouped on the GPU, reduced by the host reducer
+    reduction: str = "device"
 
     def adaptive_c_max(self, n: int) -> int:
         """P/params.rs:3005-3015."""
@@ -238,6 +244,39 @@ def group_stage(rec: dict, n: int, ctx):
     return goff, gedges[:total * 12], total
 
 
+def reduce_stage(rec: dict, n: int, p: BuildParams, ctx, neighbors: bool = True, slots: bool = False):
+    """HashPrune reservoirs of the records on the device: (offsets int64
+    [n + 1], neighbors int32 or None, slots uint8 (tessa_edge) or None,
+    slot count).  One reduction takes fewer than 2^32 edges; larger record
+    sets are reduced in row chunks whose reservoirs are merged."""
+    k = rec["k"]
+    args = (rec["leaf_rows"], rec["ids"], rec["dists"], rec["hf"], rec["hr"])
+    rows = int(args[0].numel())
+    chunk = (1 << 31) // (2 * k)
+    if rows <= chunk:
+        return ops.reduce_records(*args, k, n, p.l_max, ctx=ctx, neighbors=neighbors, slots=slots)
+    pieces = []
+    for r0 in range(0, rows, chunk):
+        r1 = min(rows, r0 + chunk)
+        o, _, sl, c = ops.reduce_records(args[0][r0:r1], args[1][r0 * k:r1 * k], args[2][r0 * k:r1 * k],
+                                         args[3][r0 * k:r1 * k], args[4][r0 * k:r1 * k], k, n, p.l_max, ctx=ctx,
+                                         neighbors=False, slots=True)
+        pieces.append((o, sl, c))
+    return ops.reduce_grouped(pieces, n, p.l_max, ctx=ctx, neighbors=neighbors, slots=slots)
+
+
+def graph_to_host(torch, d_off, d_nb, count: int):
+    """CSR from the device into pinned host memory: (offsets uint64, neighbors uint32)."""
+    n1 = int(d_off.numel())
+    h_off = _pinned("g_offsets", torch, n1 * 8)
+    h_nb = _pinned("g_neighbors", torch, max(count, 1) * 4)
+    h_off.copy_(d_off.view(torch.uint8), non_blocking=True)
+    if count:
+        h_nb[:count * 4].copy_(d_nb[:count].view(torch.uint8), non_blocking=True)
+    torch.cuda.current_stream(d_off.device).synchronize()
+    return h_off.numpy().view(np.uint64).copy(), h_nb[:count * 4].numpy().view(np.uint32).copy()
+
+
 def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> BuildResult:
     """Build the graph of x (numpy f32 [n, dim] on the host -- copied to the
     device inside -- or a CUDA f32 tensor already resident)."""
@@ -263,26 +302,45 @@ def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> B
     # ---- subtree partition of every child run, leaf top-k, edge hashes
     rec = records_stage(xd, st, p, ctx, timings=timings)
 
-    # ---- candidate records grouped by reservoir on the device, pinned D2H,
-    #      host HashPrune reduction
-    t = time.perf_counter()
-    goff, gedges, total = group_stage(rec, n, ctx)
-    h_off = _pinned("offsets", torch, (n + 1) * 8)
-    h_edges = _pinned("edges", torch, max(total, 1) * 12)
-    h_off.copy_(goff.view(torch.uint8), non_blocking=True)
-    if total:
-        h_edges[:total * 12].copy_(gedges, non_blocking=True)
-    sync()
-    timings["group_d2h_s"] = time.perf_counter() - t
-    t = time.perf_counter()
-    red = ops.Reducer(n, p.l_max, p.reducer_threads)
-    red.add_grouped(h_off.numpy().view(np.uint64), h_edges[:total * 12].numpy().view(ops.EDGE_DTYPE))
-    offs, nb = red.finish()
-    edges = red.edges()
-    red.close()
-    timings["reduce_s"] = time.perf_counter() - t
+    if p.reduction == "host":
+        # ---- candidate records grouped by reservoir on the device, pinned D2H,
+        #      host HashPrune reduction
+        t = time.perf_counter()
+        goff, gedges, total = group_stage(rec, n, ctx)
+        h_off = _pinned("offsets", torch, (n + 1) * 8)
+        h_edges = _pinned("edges", torch, max(total, 1) * 12)
+        h_off.copy_(goff.view(torch.uint8), non_blocking=True)
+        if total:
+            h_edges[:total * 12].copy_(gedges, non_blocking=True)
+        sync()
+        timings["group_d2h_s"] = time.perf_counter() - t
+        t = time.perf_counter()
+        red = ops.Reducer(n, p.l_max, p.reducer_threads)
+        red.add_grouped(h_off.numpy().view(np.uint64), h_edges[:total * 12].numpy().view(ops.EDGE_DTYPE))
+        offs, nb = red.finish()
+        edges = red.edges()
+        red.close()
+        timings["reduce_s"] = time.perf_counter() - t
+        d2h = (n + 1) * 8 + total * 12
+    elif p.reduction == "device":
+        # ---- HashPrune reservoirs on the device; the graph to pinned host memory
+        t = time.perf_counter()
+        d_off, d_nb, _, count = reduce_stage(rec, n, p, ctx)
+        sync()
+        timings["reduce_s"] = time.perf_counter() - t
+        t = time.perf_counter()
+        offs, nb = graph_to_host(torch, d_off, d_nb, count)
+        timings["d2h_s"] = time.perf_counter() - t
+        edges = None  # not counted on this path (it would cost a pass over the records)
+        total, d2h = 0, (n + 1) * 8 + count * 4
+    else:
+        raise ValueError(f"reduction must be 'device' or 'host', not {p.reduction!r}")
     timings["total_s"] = time.perf_counter() - t_all
-    return BuildResult(offs, nb, st["entry"], timings, _stats(st, rec, n, dim, edges, total))
+    stats = _stats(st, rec, n, dim, edges, total)
+    stats["d2h_bytes"] = int(d2h)
+    stats["reduction"] = p.reduction
+    stats["kernel_launches"] += 3 if p.reduction == "host" else 5
+    return BuildResult(offs, nb, st["entry"], timings, stats)
 
 
 def _stats(st, rec, n, dim, edges, total):
@@ -294,8 +352,8 @@ def _stats(st, rec, n, dim, edges, total):
                 leaf_pairs=int((sizes.astype(np.int64) * (sizes.astype(np.int64) - 1)).sum()),
                 leaf_ops=int(2 * st["d0"].codes.shape[1] * (sizes.astype(np.int64) ** 2).sum()),
                 leaf_fallback_rows=int(rec["fallback"]), partition=pst,
-                d2h_bytes=int((n + 1) * 8 + total * 12),
                 # quantize + D0 rectangular kernel + its exact fallback + fragments; partition;
                 # gather + column-split leaf kernel + finish + fallback; sketches; edge hashes;
-                # record grouping (keys, mark, emit; the sorts and scans are CUB's)
-                kernel_launches=4 + pst["kernel_launches"] + 4 + 2 + 3)
+                # then the reduction's own kernels (host: record grouping's keys, mark, emit;
+                # device: keys, runs, compaction, kept counts, selection; sorts and scans are CUB's)
+                kernel_launches=4 + pst["kernel_launches"] + 4 + 2)

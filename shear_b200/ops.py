@@ -636,3 +636,64 @@ def group_edges(point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, k: int, num
                                        _ptr(hash_fwd), _ptr(hash_rev), rows, k, num_points, _ptr(offsets),
                                        _ptr(edges), cap, _stream_ptr(torch, dev.index)))
     return offsets, edges
+
+
+def _reduce_outputs(torch, dev, num_points, cap, neighbors, slots, out):
+    if out is not None:
+        return out
+    offsets = torch.empty(num_points + 1, dtype=torch.int64, device=dev)
+    nb = torch.empty(max(cap, 1), dtype=torch.int32, device=dev) if neighbors else None
+    sl = torch.empty(max(cap, 1) * 12, dtype=torch.uint8, device=dev) if slots else None
+    return offsets, nb, sl
+
+
+def reduce_records(point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, k: int, num_points: int, l_max: int,
+                   ctx: Context | None = None, neighbors: bool = True, slots: bool = False, out=None):
+    """tessa_reduce_records: HashPrune reservoirs of leaf records on the device.
+
+    Returns (offsets int64 [n+1], neighbors int32 [cap] or None, slots uint8
+    [cap * 12] (tessa_edge) or None, slot_count); point p's slots are
+    [offsets[p], offsets[p+1]), in hash order."""
+    import torch
+
+    rows = int(point_ids.numel())
+    dev = point_ids.device
+    ctx = ctx or context(dev.index)
+    cap = min(2 * rows * k, num_points * l_max)
+    offsets, nb, sl = _reduce_outputs(torch, dev, num_points, cap, neighbors, slots, out)
+    if out is not None:
+        cap = min(nb.numel() if nb is not None else cap, sl.numel() // 12 if sl is not None else cap)
+    count = ctypes.c_uint64()
+    C.check(C.load().tessa_reduce_records(ctx.handle, _ptr(point_ids), _ptr(topk_ids), _ptr(topk_dists),
+                                          _ptr(hash_fwd), _ptr(hash_rev), rows, k, num_points, l_max, _ptr(offsets),
+                                          _ptr(nb) if nb is not None else None,
+                                          _ptr(sl) if sl is not None else None, cap, ctypes.byref(count),
+                                          _stream_ptr(torch, dev.index)))
+    return offsets, nb, sl, int(count.value)
+
+
+def reduce_grouped(pieces, num_points: int, l_max: int, ctx: Context | None = None, neighbors: bool = True,
+                   slots: bool = False, out=None):
+    """tessa_reduce_grouped: merge edges grouped by source -- `pieces` is a
+    list of (offsets int64 [n+1] CUDA tensor, edges uint8 CUDA tensor of
+    tessa_edge records, edge count) -- into reservoirs on the device.  Same
+    returns as reduce_records."""
+    import torch
+
+    dev = pieces[0][0].device
+    ctx = ctx or context(dev.index)
+    g = len(pieces)
+    offs = (ctypes.c_void_p * g)(*[p[0].data_ptr() for p in pieces])
+    eds = (ctypes.c_void_p * g)(*[p[1].data_ptr() if int(p[2]) else None for p in pieces])
+    cnt = (ctypes.c_uint64 * g)(*[int(p[2]) for p in pieces])
+    m = sum(int(p[2]) for p in pieces)
+    cap = min(m, num_points * l_max)
+    offsets, nb, sl = _reduce_outputs(torch, dev, num_points, cap, neighbors, slots, out)
+    if out is not None:
+        cap = min(nb.numel() if nb is not None else cap, sl.numel() // 12 if sl is not None else cap)
+    count = ctypes.c_uint64()
+    C.check(C.load().tessa_reduce_grouped(ctx.handle, g, offs, eds, cnt, num_points, l_max, _ptr(offsets),
+                                          _ptr(nb) if nb is not None else None,
+                                          _ptr(sl) if sl is not None else None, cap, ctypes.byref(count),
+                                          _stream_ptr(torch, dev.index)))
+    return offsets, nb, sl, int(count.value)

@@ -22,12 +22,15 @@ def _recall(x, offsets, nb, entry, queries, l=100):
     return G.recall_at(ids, gt.cpu().numpy(), 10)
 
 
+@pytest.mark.parametrize("reduction", ["device", "host"])
 @pytest.mark.parametrize("n,dim,c_max,fanout_top", [(20000, 128, 1024, 10), (12000, 768, 2048, 4)])
-def test_gpu_build_graph_equals_cpu_restatement(oracle, n, dim, c_max, fanout_top):
+def test_gpu_build_graph_equals_cpu_restatement(oracle, n, dim, c_max, fanout_top, reduction):
+    # device: HashPrune reservoirs on the GPU; host: grouped records reduced by
+    # the host reducer.  The CPU restatement inserts every record on the host.
     from oracle.cpu_build import build_index_cpu
     from shear_b200.index import BuildParams, build_index
     x = clustered_rows(n, dim, 64, seed=n + dim, unit=dim == 768)
-    p = BuildParams(c_max=c_max, fanout_top=fanout_top)
+    p = BuildParams(c_max=c_max, fanout_top=fanout_top, reduction=reduction)
     r = build_index(x, p)
     offs, nb, entry, _, st = build_index_cpu(x, p, r.stats["root_leaders"])
     assert r.stats["leaves"] == st["leaves"] and r.stats["leaf_rows"] == st["leaf_rows"]
