@@ -1273,6 +1273,7 @@ def run_build(a):
 
     from shear_b200 import ops
     from shear_b200.index import BuildParams, build_index
+    from shear_b200.sharded_build import build_index_sharded, row_range
 
     world, rank, local = dist_env()
     if world > 1:
@@ -1288,11 +1289,18 @@ def run_build(a):
     dev = torch.device("cuda", torch.cuda.current_device())
     ctx = ops.context(dev.index)
     c = build_cfg(a)
-    # the host cores are shared by every rank's reducer
     p = BuildParams(c_max=c["c_max"], reducer_threads=max(1, (os.cpu_count() or 1) // world))
-    # every rank builds its own index of the config's size (weak scaling: builds are independent)
-    x = make_mixture(torch, dev, c["rows"], c, seed=1234 + rank)
+    # one dataset of the config's size, split over the ranks (strong scaling): every rank draws the same
+    # mixture (outside the timed region) and keeps its row range
+    x = make_mixture(torch, dev, c["rows"], c, seed=1234)
     n = c["rows"]
+    lo, hi, _ = row_range(n, world, rank)
+    xs = x[lo:hi].contiguous()
+
+    def build(inp):
+        if world == 1:
+            return build_index(inp, p, device=dev.index, ctx=ctx)
+        return build_index_sharded(inp, n, p, device=dev.index, ctx=ctx)
 
     def barrier():
         if world > 1:
@@ -1300,7 +1308,7 @@ def run_build(a):
             dist.barrier()
 
     for _ in range(max(a.warmup, 3)):
-        res = build_index(x, p, device=dev.index, ctx=ctx)
+        res = build(xs)
     torch.cuda.synchronize(dev)
     barrier()
     stream = torch.cuda.current_stream(dev)
@@ -1308,42 +1316,52 @@ def run_build(a):
     with ClockSampler(dev.index) as clk:
         for _ in range(a.steps):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
             torch.cuda.synchronize(dev)
             s.record(stream)
-            res = build_index(x, p, device=dev.index, ctx=ctx)
+            res = build(xs)
             e.record(stream)
             torch.cuda.synchronize(dev)
             times.append(s.elapsed_time(e) / 1e3)
             leaf_ms.append(res.timings["leaf_kernel_ms"])
     barrier()
-    per_step = float(np.mean(times))
-    if world > 1:
+    if world > 1:  # each step's time is its slowest rank's
         import torch.distributed as dist
-        tt = torch.tensor([per_step], device=dev, dtype=torch.float64)
+        tt = torch.tensor(times, device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        per_step = float(tt[0])
-    value = world * n / per_step
+        times = tt.cpu().tolist()
+    per_step = float(np.mean(times))
+    value = n / per_step
 
     # ---- e2e: host rows (pinned) -> graph on the host, through the public build call
     e2e = None
     if not a.no_e2e and a.e2e_steps > 0:
-        xh = x.cpu().pin_memory().numpy()
-        build_index(xh, p, device=dev.index, ctx=ctx)
-        barrier()
-        t0 = time.perf_counter()
+        xh = xs.cpu().pin_memory().numpy()
+        build(xh)
+        e2e_t = []
         for _ in range(a.e2e_steps):
-            r2 = build_index(xh, p, device=dev.index, ctx=ctx)
-        e2e_s = (time.perf_counter() - t0) / a.e2e_steps
+            barrier()
+            t0 = time.perf_counter()
+            r2 = build(xh)
+            e2e_t.append(time.perf_counter() - t0)
+        if world > 1:  # each step's time is its slowest rank's
+            import torch.distributed as dist
+            tt = torch.tensor(e2e_t, device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_t = tt.cpu().tolist()
+        e2e_s = float(np.mean(e2e_t))
+        d2h = torch.tensor([int(r2.stats["d2h_bytes"])], device=dev, dtype=torch.int64)
         if world > 1:
             import torch.distributed as dist
-            tt = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            e2e_s = float(tt[0])
-        e2e = {"value": world * n / e2e_s, "unit": "vectors/s", "h2d_bytes_per_step": int(n * c["dim"] * 4),
-               "d2h_bytes_per_step": int(r2.stats["d2h_bytes"]), "ms_per_step": e2e_s * 1e3,
-               "timing": "wall clock around build_index(host numpy rows): upload, GPU stages, pinned D2H of "
-                         "the candidate records grouped by reservoir, host HashPrune reduction; graph in host "
-                         "memory"}
+            dist.all_reduce(d2h)
+        e2e = {"value": n / e2e_s, "unit": "vectors/s", "h2d_bytes_per_step": int(n * c["dim"] * 4),
+               "d2h_bytes_per_step": int(d2h.item()), "ms_per_step": e2e_s * 1e3,
+               "timing": ("wall clock around build_index(host numpy rows): upload from pinned memory, GPU "
+                          "stages, device HashPrune reservoirs, pinned D2H of the graph" if world == 1 else
+                          "wall clock, slowest rank per step, around build_index_sharded(host numpy row range): "
+                          "each rank uploads its rows from pinned memory; all-gather of D0 rows, partial "
+                          "reservoirs exchanged by owner range, graph gathered on rank 0 and copied to its "
+                          "pinned host memory")}
         del xh
 
     if rank != 0:
@@ -1400,11 +1418,13 @@ def run_build(a):
 
     line = {
         "metric": BUILD_METRIC, "value": value, "unit": "vectors/s", "n_gpus": world, "steps": a.steps,
-        "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8",
         "data": f"synthetic stand-in for BASELINE config {a.config} (seeded Gaussian mixture on the device, seed "
-                f"1234+rank); random root leaders and sketch hyperplanes from seeded generators",
-        "config": dict(build_desc(a, c), parallelism=f"independent builds x{world} (no collective)"),
+                f"1234); random root leaders and sketch hyperplanes from seeded generators",
+        "config": dict(build_desc(a, c), parallelism=(
+            "one GPU" if world == 1 else f"one build over {world} GPUs: row ranges, D0 all-gather, child runs "
+            f"by LPT, partial reservoirs all-to-all by owner range, graph gathered on rank 0 (NCCL)")),
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "recall": recall, "recall_parity": parity,
         "gpu_launches": res.stats["kernel_launches"] * a.steps,
         "clocks": clk.summary(),

@@ -476,6 +476,10 @@ typedef struct tessa_subtree_result {
   uint32_t balanced;             /* balanced even/odd fallbacks (CB:15480-15504) */
   uint32_t small_nodes;          /* subtree roots split on the small path */
   uint32_t kernel_launches;      /* kernels this call launched */
+  float assign_ms;               /* device time of the large-node assignment phases (all rounds) */
+  float scatter_ms;              /* device time of the scatter phases */
+  float small_ms;                /* device time of the small-node path */
+  float wall_ms;                 /* host wall time of the call */
 } tessa_subtree_result;
 
 /* The partition of one batch of subtree tasks (synchronous on `stream`).

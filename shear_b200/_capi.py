@@ -129,6 +129,8 @@ class SubtreeResult(ctypes.Structure):
         ("leaf_count", ctypes.c_uint64), ("leaf_rows_used", ctypes.c_uint64), ("rounds", ctypes.c_uint32),
         ("large_assignments", ctypes.c_uint32), ("retries", ctypes.c_uint32), ("balanced", ctypes.c_uint32),
         ("small_nodes", ctypes.c_uint32), ("kernel_launches", ctypes.c_uint32),
+        ("assign_ms", ctypes.c_float), ("scatter_ms", ctypes.c_float), ("small_ms", ctypes.c_float),
+        ("wall_ms", ctypes.c_float),
     ]
 
 

@@ -1450,7 +1450,7 @@ int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* a, tessa_s
     ctx->subtree = subtree_state_new();
     if (!ctx->subtree) return fail(TESSA_ERR_OOM, "subtree state allocation failed");
   }
-  cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
   TRY(clear_err(ctx, st));
   SubtreeStats stats{};
   const int rc = subtree_partition(ctx->subtree, *a, &stats, ctx->d_err.as<uint32_t>(), ctx->sm_count,
@@ -1464,6 +1464,10 @@ int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* a, tessa_s
   result->balanced = stats.balanced;
   result->small_nodes = stats.small_nodes;
   result->kernel_launches = stats.launches;
+  result->assign_ms = stats.assign_ms;
+  result->scatter_ms = stats.scatter_ms;
+  result->small_ms = stats.small_ms;
+  result->wall_ms = stats.wall_ms;
   return TESSA_OK;
 }
 
@@ -1485,7 +1489,7 @@ int tessa_group_edges(tessa_ctx* ctx, const uint32_t* point_ids, const uint32_t*
   if (m >= 0xffffffffull)
     return fail(TESSA_ERR_UNSUPPORTED, "2 * rows * k = %llu edges in one batch; at most 2^32 - 1 (split the batch)",
                 (unsigned long long)m);
-  cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
   TRY(ctx->g_temp.ensure(group_edges_scratch_bytes(m, num_points)));
   TRY(clear_err(ctx, st));
   GroupEdgesCall g{point_ids, topk_ids, topk_dists, hash_fwd, hash_rev, rows, k, num_points, offsets,
@@ -1511,7 +1515,7 @@ int reduce_common(tessa_ctx* ctx, ReservoirCall& r, uint64_t* slot_count, void* 
                 "the reservoirs)", (unsigned long long)r.edges);
   if (r.capacity && !r.out_neighbors && !r.out_slots)
     return fail(TESSA_ERR_INVALID_ARG, "slot capacity given without an output array");
-  cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
   TRY(ctx->g_temp.ensure(reservoir_scratch_bytes(r.edges, r.num_points)));
   TRY(clear_err(ctx, st));
   r.temp = ctx->g_temp.ptr;
@@ -1637,7 +1641,7 @@ int tessa_check_bounded_wait(tessa_ctx* ctx, uint64_t timeout_ns, uint64_t* elap
   if (timeout_ns < 1000ull || timeout_ns > kMaxTimeoutNs)
     return fail(TESSA_ERR_INVALID_ARG, "probe limit %llu ns outside 1000..%llu ns", (unsigned long long)timeout_ns,
                 (unsigned long long)kMaxTimeoutNs);
-  cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the legacy default stream
   TRY(ctx->probe.ensure(8));
   TRY(clear_err(ctx, st));
   wait_probe_kernel<<<1, 64, 0, st>>>(ctx->d_err.as<uint32_t>(), timeout_ns,

@@ -167,6 +167,7 @@ void subtree_state_free(SubtreeState* s);
 struct SubtreeStats {
   uint64_t leaf_count, leaf_rows_used;
   uint32_t rounds, large_assignments, retries, balanced, small_nodes, launches;
+  float assign_ms, scatter_ms, small_ms, wall_ms;
 };
 int subtree_partition(SubtreeState* s, const tessa_subtree_args& a, SubtreeStats* stats, uint32_t* d_err,
                       int sm_count, uint64_t timeout_ns, cudaStream_t stream);

@@ -25,6 +25,7 @@
 // Nothing here spins: every kernel is straight-line work over its node.
 #include <algorithm>
 #include <cmath>
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -523,6 +524,13 @@ struct Buf {
 struct SubtreeState {
   subtree::Buf cur, next, member_res, slots, leader_local, leader_res, counts, dests, nodes, small_nodes, tables,
       task_off, t_moff, t_mcnt, t_loff, t_lcnt, t_rh, t_out, work;
+  // phase boundaries of a round: assignment, scatter, small path
+  cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  bool events() {
+    for (auto& e : ev)
+      if (!e && cudaEventCreate(&e) != cudaSuccess) return false;
+    return true;
+  }
   void release() {
     subtree::Buf* all[] = {&cur, &next, &member_res, &slots, &leader_local, &leader_res, &counts, &dests, &nodes,
                            &small_nodes, &tables, &task_off, &t_moff, &t_mcnt, &t_loff, &t_lcnt, &t_rh, &t_out,
@@ -535,6 +543,8 @@ SubtreeState* subtree_state_new() { return new (std::nothrow) SubtreeState(); }
 void subtree_state_free(SubtreeState* s) {
   if (!s) return;
   s->release();
+  for (auto& e : s->ev)
+    if (e) cudaEventDestroy(e);
   delete s;
 }
 
@@ -584,6 +594,12 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
   if (a.task_count) ST_CUDA(cudaMemcpyAsync(S->task_off.ptr, a.task_offsets, (size_t)a.task_count * 8,
                                             cudaMemcpyHostToDevice, st));
   *stats = SubtreeStats{};
+  const auto wall0 = std::chrono::steady_clock::now();
+  if (!S->events()) return set_last_error(TESSA_ERR_CUDA, "subtree timing events could not be created");
+  auto elapsed = [&](int a0, int a1) {
+    float ms = 0.f;
+    return cudaEventElapsedTime(&ms, S->ev[a0], S->ev[a1]) == cudaSuccess ? ms : 0.f;
+  };
 
   // round 0: one root node per non-empty task, rows 0..n-1
   std::vector<HNode> nodes;
@@ -700,6 +716,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       ST_CUDA(cudaMemcpyAsync(S->t_rh.ptr, rh.data(), L * 4, cudaMemcpyHostToDevice, st));
       ST_CUDA(cudaMemcpyAsync(S->t_out.ptr, tout.data(), L * 8, cudaMemcpyHostToDevice, st));
       ST_CUDA(cudaMemcpyAsync(S->work.ptr, work.data(), work.size() * 8, cudaMemcpyHostToDevice, st));
+      ST_CUDA(cudaEventRecord(S->ev[0], st));
       prepare_kernel<<<(unsigned)L, 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->cur.as<uint32_t>(), a.task_members,
                                                   S->task_off.as<uint64_t>(), S->member_res.as<uint32_t>(),
                                                   S->leader_local.as<uint32_t>(), S->leader_res.as<uint32_t>());
@@ -735,6 +752,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       count_kernel<<<(unsigned)L, 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->slots.as<uint32_t>(),
                                                 S->counts.as<uint32_t>());
       ST_CUDA(cudaGetLastError());
+      ST_CUDA(cudaEventRecord(S->ev[1], st));
       ST_CUDA(cudaMemcpyAsync(counts.data(), S->counts.ptr, L * kSlots * 4, cudaMemcpyDeviceToHost, st));
       uint32_t bits = 0;
       ST_CUDA(cudaMemcpyAsync(&bits, d_err, 4, cudaMemcpyDeviceToHost, st));
@@ -742,6 +760,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       if (bits) return bits & TESSA_DEVERR_TIMEOUT ? set_last_error(TESSA_ERR_TIMEOUT, "subtree assignment timed out")
                                                    : set_last_error(TESSA_ERR_BAD_TASK, "subtree assignment failed");
       stats->large_assignments += (uint32_t)L;
+      stats->assign_ms += elapsed(0, 1);
     }
 
     // ---- decisions and allocation in node order
@@ -848,11 +867,13 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       ST_ALLOC(S->dests, dests.size() * 8);
       ST_CUDA(cudaMemcpyAsync(S->nodes.ptr, sc.data(), sc.size() * sizeof(NodeDesc), cudaMemcpyHostToDevice, st));
       ST_CUDA(cudaMemcpyAsync(S->dests.ptr, dests.data(), dests.size() * 8, cudaMemcpyHostToDevice, st));
+      ST_CUDA(cudaEventRecord(S->ev[2], st));
       scatter_kernel<<<(unsigned)sc.size(), 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->dests.as<uint64_t>(),
                                                          S->cur.as<uint32_t>(), S->slots.as<uint32_t>(),
                                                          a.task_members, S->task_off.as<uint64_t>(),
                                                          S->next.as<uint32_t>(), a.leaf_rows);
       ST_CUDA(cudaGetLastError());
+      ST_CUDA(cudaEventRecord(S->ev[3], st));
       stats->launches++;
     }
     if (!sm.empty()) {
@@ -877,8 +898,10 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       sp.leaf_rows = a.leaf_rows;
       sp.tables = S->tables.as<uint32_t>();
       sp.err = d_err;
+      ST_CUDA(cudaEventRecord(S->ev[4], st));
       small_kernel<<<(unsigned)sm.size(), 256, small_smem, st>>>(sp);
       ST_CUDA(cudaGetLastError());
+      ST_CUDA(cudaEventRecord(S->ev[5], st));
       stats->launches++;
       std::vector<uint32_t> tab(sm.size() * kTab);
       ST_CUDA(cudaMemcpyAsync(tab.data(), S->tables.ptr, tab.size() * 4, cudaMemcpyDeviceToHost, st));
@@ -897,6 +920,8 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       }
     }
     ST_CUDA(cudaStreamSynchronize(st));
+    if (!sc.empty()) stats->scatter_ms += elapsed(2, 3);
+    if (!sm.empty()) stats->small_ms += elapsed(4, 5);
     std::swap(S->cur, S->next);
     nodes.swap(next_nodes);
   }
@@ -910,6 +935,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
   }
   stats->leaf_count = leaves.size();
   stats->leaf_rows_used = leaf_used;
+  stats->wall_ms = std::chrono::duration<float, std::milli>(std::chrono::steady_clock::now() - wall0).count();
   return TESSA_OK;
 }
 

@@ -170,8 +170,7 @@ def _upload(x, dev, torch):
 
 def d0_stage(xd, p: BuildParams, ctx):
     """SQ8 codes of every row, its fanout_top root leaders, and the child runs
-    (rows ascending per leader).  Deterministic: every rank of a multi-GPU
-    build computes the same result."""
+    (rows ascending per leader), all rows on this device."""
     import torch
 
     dev = xd.device
@@ -183,26 +182,47 @@ def d0_stage(xd, p: BuildParams, ctx):
     lid = torch.from_numpy(leaders.view(np.int32)).to(dev)
     gids = torch.arange(n, dtype=torch.int32, device=dev)
     d0 = ops.quantize_sq8_assign_d0(xd, gids, lid, fanout, leader_vectors=xd[lid.long()], ctx=ctx)
+    st = child_runs_stage(d0, k0, p)
+    st.update(gids=gids, plan=plan, fanout=fanout)
+    return st
+
+
+def child_runs_stage(d0, k0: int, p: BuildParams) -> dict:
+    """Child runs of the D0 assignment (rows ascending per root leader), their
+    subtree seeds and the entry point (first row of the largest run)."""
+    n = d0.rows
     members, counts, offsets = group_child_runs(d0.child_ids, k0)
     depth, parent, min_rec = child_seed_args(p, n)
     seeds = np.array([ops.subtree_root_seed(p.random_seed, depth, int(c), parent, min_rec) for c in counts],
                      np.uint64)
     big = int(len(counts) - 1 - np.argmax(counts[::-1]))
     entry = int(members[int(offsets[big])].item()) if counts[big] else 0
-    return dict(d0=d0, gids=gids, members=members, counts=counts, offsets=offsets, seeds=seeds, k0=k0,
-                plan=plan, fanout=fanout, depth=depth, entry=entry)
+    return dict(d0=d0, members=members, counts=counts, offsets=offsets, seeds=seeds, k0=k0, depth=depth,
+                entry=entry)
 
 
-def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None):
+def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, sketches=None):
     """Subtree partition of the child runs `tasks` (all when None), their
-    leaves' top-k lists and both sketch hashes of every slot, on the device."""
+    leaves' top-k lists and both sketch hashes of every slot, on the device.
+    The sketches of every row are computed from xd unless given."""
     import torch
 
     timings = {} if timings is None else timings
-    dev = xd.device
-    n, dim = xd.shape
     d0 = st["d0"]
+    dev = d0.codes.device
+    n, dim = d0.rows, d0.dim
     sel = np.arange(len(st["counts"])) if tasks is None else np.asarray(tasks, np.int64)
+    sel = sel[st["counts"][sel] > 0]
+    k = max(1, min(p.leaf_knn, 32))
+    if sel.size == 0:  # no work on this device
+        timings.update(partition_s=0.0, leaf_s=0.0, leaf_kernel_ms=0.0)
+        e32 = torch.empty(0, dtype=torch.int32, device=dev)
+        e16 = torch.empty(0, dtype=torch.int16, device=dev)
+        return dict(leaf_rows=e32, ids=e32, dists=torch.empty(0, device=dev), hf=e16, hr=e16, k=k,
+                    starts=np.zeros(0, np.uint64), sizes=np.zeros(0, np.uint64),
+                    partition=dict(rounds=0, large_assignments=0, retries=0, balanced=0, small_nodes=0,
+                                   leaf_rows_used=0, kernel_launches=0),
+                    fallback=0)
     t = time.perf_counter()
     sp = ops.SubtreeParams(c_max=p.adaptive_c_max(n), max_depth=p.max_depth, max_leaders=p.max_leaders,
                            fanout_second=p.fanout_second, root_depth=st["depth"], psamp_fraction=p.psamp_fraction)
@@ -212,7 +232,6 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None):
     torch.cuda.synchronize(dev)
     timings["partition_s"] = time.perf_counter() - t
     t = time.perf_counter()
-    k = max(1, min(p.leaf_knn, 32))
     rows = int(leaf_rows.numel())
     ids = torch.full((rows * k,), -1, dtype=torch.int32, device=dev)
     dists = torch.full((rows * k,), float("inf"), dtype=torch.float32, device=dev)
@@ -221,14 +240,18 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None):
     ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, st["gids"], leaf_rows, starts, sizes, k, out=(ids, dists),
                       ctx=ctx)
     ev[1].record()
-    planes = torch.from_numpy(hyperplanes(p.m_hash_bits, dim, p.random_seed)).to(dev)
-    sketches = ops.sketch_rows(xd, planes, ctx=ctx)
+    if sketches is None:
+        sketches = ops.sketch_rows(xd, sketch_planes(torch, dev, p, dim), ctx=ctx)
     hf, hr = ops.edge_hashes(leaf_rows, ids, k, sketches, p.m_hash_bits, starts, sizes, ctx=ctx)
     torch.cuda.synchronize(dev)
     timings["leaf_s"] = time.perf_counter() - t
     timings["leaf_kernel_ms"] = ev[0].elapsed_time(ev[1])
     return dict(leaf_rows=leaf_rows, ids=ids, dists=dists, hf=hf, hr=hr, k=k, starts=starts, sizes=sizes,
                 partition=pst, fallback=ops.leaf_last_fallback_rows(ctx))
+
+
+def sketch_planes(torch, dev, p: BuildParams, dim: int):
+    return torch.from_numpy(hyperplanes(p.m_hash_bits, dim, p.random_seed)).to(dev)
 
 
 def group_stage(rec: dict, n: int, ctx):
@@ -266,15 +289,16 @@ def reduce_stage(rec: dict, n: int, p: BuildParams, ctx, neighbors: bool = True,
 
 
 def graph_to_host(torch, d_off, d_nb, count: int):
-    """CSR from the device into pinned host memory: (offsets uint64, neighbors uint32)."""
-    n1 = int(d_off.numel())
-    h_off = _pinned("g_offsets", torch, n1 * 8)
-    h_nb = _pinned("g_neighbors", torch, max(count, 1) * 4)
-    h_off.copy_(d_off.view(torch.uint8), non_blocking=True)
+    """CSR from the device into pinned host memory: (offsets uint64, neighbors
+    uint32).  The arrays live in pinned blocks from torch's caching host
+    allocator, released back to it when the result is dropped."""
+    h_off = torch.empty(int(d_off.numel()), dtype=torch.int64, pin_memory=True)
+    h_nb = torch.empty(max(count, 1), dtype=torch.int32, pin_memory=True)
+    h_off.copy_(d_off, non_blocking=True)
     if count:
-        h_nb[:count * 4].copy_(d_nb[:count].view(torch.uint8), non_blocking=True)
+        h_nb[:count].copy_(d_nb[:count], non_blocking=True)
     torch.cuda.current_stream(d_off.device).synchronize()
-    return h_off.numpy().view(np.uint64).copy(), h_nb[:count * 4].numpy().view(np.uint32).copy()
+    return h_off.numpy().view(np.uint64), h_nb[:count].numpy().view(np.uint32)
 
 
 def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> BuildResult:

@@ -54,6 +54,8 @@ def context(device: int = 0) -> Context:
 
 
 def _stream_ptr(torch, device):
+    """torch's current stream as the C ABI's stream argument (its default
+    stream is 0, which the C ABI reads as the legacy default stream)."""
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
@@ -550,6 +552,7 @@ def subtree_partition(codes, scales, norms, task_members, task_offsets, task_cou
     n = int(r.leaf_count)
     stats = {f: int(getattr(r, f)) for f in ("rounds", "large_assignments", "retries", "balanced", "small_nodes",
                                              "leaf_rows_used", "kernel_launches")}
+    stats.update({f: round(float(getattr(r, f)), 3) for f in ("assign_ms", "scatter_ms", "small_ms", "wall_ms")})
     return leaf_rows[:int(r.leaf_rows_used)], starts[:n].copy(), sizes[:n].copy(), tasks[:n].copy(), stats
 
 
