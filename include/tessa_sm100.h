@@ -124,7 +124,8 @@ typedef struct tessa_leaf_args {
   uint32_t padded_dim;          /* multiple of 16, <= TESSA_MAX_PADDED_DIM */
   uint32_t k;                   /* 1 .. TESSA_MAX_LEAF_K */
   /* leaf layout */
-  const uint32_t* leaf_members; /* device pointer, leaf_rows entries */
+  const uint32_t* leaf_members; /* device pointer, leaf_rows entries (entries in no leaf are never
+                                   used; those at or above resident_rows are not read) */
   const uint64_t* leaf_starts;  /* HOST pointer, leaf_count entries */
   const uint64_t* leaf_sizes;   /* HOST pointer, leaf_count entries */
   uint64_t leaf_count;
@@ -480,12 +481,16 @@ typedef struct tessa_subtree_result {
   float scatter_ms;              /* device time of the scatter phases */
   float small_ms;                /* device time of the small-node path */
   float wall_ms;                 /* host wall time of the call */
+  float host_prep_ms;            /* host time building each round's node tables */
+  float host_decide_ms;          /* host time deciding splits and allocating */
+  float sync_wait_ms;            /* host time waiting on the stream */
 } tessa_subtree_result;
 
 /* The partition of one batch of subtree tasks (synchronous on `stream`).
  * Replaces the partition workers of gpu_persistent_subtree_topk behind
  * PiPNNComputeBackend::process_quantized_subtree_l2_compact_topk (CB:3693-3884);
- * the leaves then go to tessa_leaf_topk_sq8. */
+ * the leaves then go to tessa_leaf_topk_sq8.  Entries of leaf_rows that belong
+ * to no leaf (unused reservations of the small-node path) hold 0xffffffff. */
 TESSA_API int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* args, tessa_subtree_result* result,
                                       void* stream);
 

@@ -130,7 +130,8 @@ class SubtreeResult(ctypes.Structure):
         ("large_assignments", ctypes.c_uint32), ("retries", ctypes.c_uint32), ("balanced", ctypes.c_uint32),
         ("small_nodes", ctypes.c_uint32), ("kernel_launches", ctypes.c_uint32),
         ("assign_ms", ctypes.c_float), ("scatter_ms", ctypes.c_float), ("small_ms", ctypes.c_float),
-        ("wall_ms", ctypes.c_float),
+        ("wall_ms", ctypes.c_float), ("host_prep_ms", ctypes.c_float), ("host_decide_ms", ctypes.c_float),
+        ("sync_wait_ms", ctypes.c_float),
     ]
 
 

@@ -396,8 +396,8 @@ int leaf_device(tessa_ctx* ctx, const tessa_leaf_args* a, cudaStream_t st) {
   const int8_t* lc = a->leaf_ordered_codes;
   if (!lc) {
     TRY(ctx->gather.ensure((size_t)a->leaf_rows * a->padded_dim));
-    TRY(launch_gather_rows(a->codes, a->leaf_members, a->leaf_rows, a->padded_dim, ctx->gather.as<int8_t>(),
-                           ctx->sm_count, st));
+    TRY(launch_gather_rows(a->codes, a->leaf_members, a->leaf_rows, a->padded_dim, a->resident_rows,
+                           ctx->gather.as<int8_t>(), ctx->sm_count, st));
     lc = ctx->gather.as<int8_t>();
   }
   TRY(clear_err(ctx, st));
@@ -1468,6 +1468,9 @@ int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* a, tessa_s
   result->scatter_ms = stats.scatter_ms;
   result->small_ms = stats.small_ms;
   result->wall_ms = stats.wall_ms;
+  result->host_prep_ms = stats.host_prep_ms;
+  result->host_decide_ms = stats.host_decide_ms;
+  result->sync_wait_ms = stats.sync_wait_ms;
   return TESSA_OK;
 }
 

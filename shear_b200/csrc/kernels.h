@@ -110,8 +110,8 @@ int launch_membership_digests(const uint32_t* ids, const uint32_t* global_ids, c
 uint64_t graph_search_host(const float* data, uint64_t n, uint32_t dim, const uint64_t* offsets,
                            const uint32_t* neighbors, uint32_t start, const float* queries, uint64_t nq, uint32_t k,
                            uint32_t l, uint32_t threads, uint32_t* out_ids);
-int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes, int8_t* dst,
-                       int sm_count, cudaStream_t stream);
+int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes,
+                       uint64_t resident_rows, int8_t* dst, int sm_count, cudaStream_t stream);
 int leaf_num_bstages(uint32_t padded_dim);
 int launch_quantize_sq8(const float* x, uint64_t rows, uint32_t dim, uint32_t padded, uint32_t bits, int8_t* codes,
                         float* scales, float* norms, uint32_t* d_err, cudaStream_t stream);
@@ -168,6 +168,7 @@ struct SubtreeStats {
   uint64_t leaf_count, leaf_rows_used;
   uint32_t rounds, large_assignments, retries, balanced, small_nodes, launches;
   float assign_ms, scatter_ms, small_ms, wall_ms;
+  float host_prep_ms, host_decide_ms, sync_wait_ms;  // host time: round set-up, decisions, stream waits
 };
 int subtree_partition(SubtreeState* s, const tessa_subtree_args& a, SubtreeStats* stats, uint32_t* d_err,
                       int sm_count, uint64_t timeout_ns, cudaStream_t stream);

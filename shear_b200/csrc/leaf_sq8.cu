@@ -754,15 +754,21 @@ __global__ void __launch_bounds__(kFbThreads) leaf_fallback_kernel(const int8_t*
 }
 
 // Gather code rows into leaf order: dst row p = src row members[p].
+// Leaf-ordered copy of the codes.  An entry outside the resident rows (an
+// arena row that belongs to no leaf, or a bad id the leaf kernel reports
+// itself) gets a zero row instead of a read.
 __global__ void gather_rows_kernel(const int8_t* __restrict__ src, const uint32_t* __restrict__ members,
-                                   uint64_t rows, uint32_t row_bytes, int8_t* __restrict__ dst) {
+                                   uint64_t rows, uint32_t row_bytes, uint64_t resident_rows,
+                                   int8_t* __restrict__ dst) {
   const uint32_t vec = row_bytes / 16u;
   for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < rows * vec;
        idx += (uint64_t)gridDim.x * blockDim.x) {
     uint64_t r = idx / vec;
     uint32_t v = (uint32_t)(idx - r * vec);
-    const uint4* s = reinterpret_cast<const uint4*>(src + (uint64_t)members[r] * row_bytes) + v;
-    reinterpret_cast<uint4*>(dst + r * row_bytes)[v] = *s;
+    const uint32_t m = members[r];
+    uint4 x = make_uint4(0u, 0u, 0u, 0u);
+    if (m < resident_rows) x = reinterpret_cast<const uint4*>(src + (uint64_t)m * row_bytes)[v];
+    reinterpret_cast<uint4*>(dst + r * row_bytes)[v] = x;
   }
 }
 
@@ -989,14 +995,14 @@ int launch_d0_fragments(const uint32_t* keys, const uint32_t* key_to_leader, con
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 
-int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes, int8_t* dst,
-                       int sm_count, cudaStream_t stream) {
+int launch_gather_rows(const int8_t* src, const uint32_t* members, uint64_t rows, uint32_t row_bytes,
+                       uint64_t resident_rows, int8_t* dst, int sm_count, cudaStream_t stream) {
   if (rows == 0) return TESSA_OK;
   uint64_t work = rows * (row_bytes / 16u);
   uint64_t blocks = (work + 255) / 256;
   uint64_t cap = (uint64_t)sm_count * 8u;
   if (blocks > cap) blocks = cap;
-  leaf::gather_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, members, rows, row_bytes, dst);
+  leaf::gather_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, members, rows, row_bytes, resident_rows, dst);
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 

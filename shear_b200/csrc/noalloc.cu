@@ -175,7 +175,7 @@ extern "C" int tessa_leaf_topk_sq8_noalloc(const tessa_leaf_args* a, void* strea
 
   const int8_t* leaf_codes = a->leaf_ordered_codes;
   if (gather) {
-    r = launch_gather_rows(a->codes, a->leaf_members, a->leaf_rows, a->padded_dim,
+    r = launch_gather_rows(a->codes, a->leaf_members, a->leaf_rows, a->padded_dim, a->resident_rows,
                            reinterpret_cast<int8_t*>(s + off_codes), sms, st);
     if (r != TESSA_OK) return err(r, "gather kernel launch failed (code %d)", r);
     leaf_codes = reinterpret_cast<const int8_t*>(s + off_codes);

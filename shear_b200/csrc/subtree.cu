@@ -593,9 +593,16 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
   ST_ALLOC(S->task_off, (size_t)a.task_count * 8 + 8);
   if (a.task_count) ST_CUDA(cudaMemcpyAsync(S->task_off.ptr, a.task_offsets, (size_t)a.task_count * 8,
                                             cudaMemcpyHostToDevice, st));
+  // arena rows that end up in no leaf (the unused part of a small node's
+  // reservation) read as 0xffffffff, never as stale ids
+  if (a.leaf_rows_capacity) ST_CUDA(cudaMemsetAsync(a.leaf_rows, 0xff, (size_t)a.leaf_rows_capacity * 4, st));
   *stats = SubtreeStats{};
   const auto wall0 = std::chrono::steady_clock::now();
   if (!S->events()) return set_last_error(TESSA_ERR_CUDA, "subtree timing events could not be created");
+  using clk = std::chrono::steady_clock;
+  auto ms_since = [](clk::time_point t0) {
+    return std::chrono::duration<float, std::milli>(clk::now() - t0).count();
+  };
   auto elapsed = [&](int a0, int a1) {
     float ms = 0.f;
     return cudaEventElapsedTime(&ms, S->ev[a0], S->ev[a1]) == cudaSuccess ? ms : 0.f;
@@ -640,6 +647,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
 
   while (!nodes.empty()) {
     stats->rounds++;
+    auto t_prep = clk::now();
     // ---- classify
     std::vector<Kind> kind(nodes.size());
     std::vector<uint32_t> large_idx, small_idx;
@@ -716,6 +724,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       ST_CUDA(cudaMemcpyAsync(S->t_rh.ptr, rh.data(), L * 4, cudaMemcpyHostToDevice, st));
       ST_CUDA(cudaMemcpyAsync(S->t_out.ptr, tout.data(), L * 8, cudaMemcpyHostToDevice, st));
       ST_CUDA(cudaMemcpyAsync(S->work.ptr, work.data(), work.size() * 8, cudaMemcpyHostToDevice, st));
+      stats->host_prep_ms += ms_since(t_prep);
       ST_CUDA(cudaEventRecord(S->ev[0], st));
       prepare_kernel<<<(unsigned)L, 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->cur.as<uint32_t>(), a.task_members,
                                                   S->task_off.as<uint64_t>(), S->member_res.as<uint32_t>(),
@@ -756,7 +765,9 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       ST_CUDA(cudaMemcpyAsync(counts.data(), S->counts.ptr, L * kSlots * 4, cudaMemcpyDeviceToHost, st));
       uint32_t bits = 0;
       ST_CUDA(cudaMemcpyAsync(&bits, d_err, 4, cudaMemcpyDeviceToHost, st));
+      const auto t_wait = clk::now();
       ST_CUDA(cudaStreamSynchronize(st));
+      stats->sync_wait_ms += ms_since(t_wait);
       if (bits) return bits & TESSA_DEVERR_TIMEOUT ? set_last_error(TESSA_ERR_TIMEOUT, "subtree assignment timed out")
                                                    : set_last_error(TESSA_ERR_BAD_TASK, "subtree assignment failed");
       stats->large_assignments += (uint32_t)L;
@@ -764,6 +775,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
     }
 
     // ---- decisions and allocation in node order
+    const auto t_decide = clk::now();
     std::vector<HNode> next_nodes;
     uint64_t next_len = 0;
     // scatter plan for leaf-all and large nodes
@@ -861,6 +873,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       dests.insert(dests.end(), dst.begin(), dst.end());
     }
 
+    stats->host_decide_ms += ms_since(t_decide);
     // ---- scatter (leaf-all and large nodes) and the small path
     if (!sc.empty()) {
       ST_ALLOC(S->nodes, sc.size() * sizeof(NodeDesc));
@@ -919,7 +932,9 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
         leaves.insert(leaves.begin() + (ptrdiff_t)sm_leaf_pos[j], ins.begin(), ins.end());
       }
     }
+    const auto t_end = clk::now();
     ST_CUDA(cudaStreamSynchronize(st));
+    stats->sync_wait_ms += ms_since(t_end);
     if (!sc.empty()) stats->scatter_ms += elapsed(2, 3);
     if (!sm.empty()) stats->small_ms += elapsed(4, 5);
     std::swap(S->cur, S->next);

@@ -552,7 +552,8 @@ def subtree_partition(codes, scales, norms, task_members, task_offsets, task_cou
     n = int(r.leaf_count)
     stats = {f: int(getattr(r, f)) for f in ("rounds", "large_assignments", "retries", "balanced", "small_nodes",
                                              "leaf_rows_used", "kernel_launches")}
-    stats.update({f: round(float(getattr(r, f)), 3) for f in ("assign_ms", "scatter_ms", "small_ms", "wall_ms")})
+    stats.update({f: round(float(getattr(r, f)), 3) for f in ("assign_ms", "scatter_ms", "small_ms", "wall_ms",
+                                                          "host_prep_ms", "host_decide_ms", "sync_wait_ms")})
     return leaf_rows[:int(r.leaf_rows_used)], starts[:n].copy(), sizes[:n].copy(), tasks[:n].copy(), stats
 
 
