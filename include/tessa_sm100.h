@@ -55,6 +55,7 @@ extern "C" {
 #define TESSA_ERR_NONFINITE (-7)    /* non-finite input to the SQ8 quantizer */
 #define TESSA_ERR_NO_DEVICE (-8)    /* no sm_100 device / extension not usable */
 #define TESSA_ERR_BAD_TASK (-9)     /* malformed task descriptor seen on the device */
+#define TESSA_ERR_AGAIN (-11)       /* not now: no free submission slot, or the submission is still running */
 #define TESSA_ERR_PARTITION (-10)   /* the subtree partition cannot finish: a node above leaf_max at max_depth
                                        (GPU_PERSISTENT_OVERSIZED_TERMINAL_NODE, CB:4849) or output capacity */
 
@@ -493,6 +494,52 @@ typedef struct tessa_subtree_result {
  * to no leaf (unused reservations of the small-node path) hold 0xffffffff. */
 TESSA_API int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* args, tessa_subtree_result* result,
                                       void* stream);
+
+/* Subtree submissions: submit_owned_quantized_subtree_l2_compact_topk
+ * (CB:3693-3884) with the persistent async D2H ring
+ * (P/persistent_async_d2h.rs:4-80, two slots).  A submission partitions a
+ * batch of subtree tasks (as tessa_subtree_partition; the output fields of
+ * `partition` are ignored -- the slot owns the leaf arena), evaluates every
+ * leaf (as tessa_leaf_topk_sq8 with `global_ids` and `k`), and copies the
+ * CompactTopKBatch (P/leaf_build.rs:271-290) -- the global id of every leaf
+ * row, its k ids and distances -- into the slot's pinned host memory.
+ *
+ * tessa_subtree_submit copies the request's host arrays, records `stream`
+ * (the submission starts after the work queued on it so far) and returns at
+ * once with a ticket; the work runs on a private context of the same device
+ * (its own stream and scratch), in submission order.  The device inputs
+ * (codes, scales, norms, task_members, global_ids) must stay valid until the
+ * ticket is polled.  With both slots leased it returns TESSA_ERR_AGAIN.
+ * tessa_subtree_poll fills `view` once the batch is on the host (wait = 0:
+ * TESSA_ERR_AGAIN while it runs; wait != 0: blocks); a failed submission
+ * returns its error and frees its slot.  The view's arrays stay valid until
+ * tessa_subtree_release(ticket), which frees the slot.  Leaf rows that belong
+ * to no leaf have point id 0xffffffff and k empty slots. */
+typedef struct tessa_subtree_request {
+  tessa_subtree_args partition;
+  const uint32_t* global_ids;    /* device, resident_rows: local id -> point id */
+  uint32_t k;                    /* 1 .. TESSA_MAX_LEAF_K */
+} tessa_subtree_request;
+
+typedef struct tessa_compact_view {
+  uint64_t ticket;
+  uint64_t rows;                 /* leaf rows of the batch */
+  uint32_t k;
+  uint64_t leaf_count;
+  const uint64_t* leaf_starts;   /* host, leaf_count: first row of each leaf */
+  const uint32_t* leaf_sizes;    /* host, leaf_count */
+  const uint32_t* leaf_tasks;    /* host, leaf_count: task index in the request */
+  const uint32_t* point_ids;     /* pinned host, rows */
+  const uint32_t* topk_ids;      /* pinned host, rows * k (0xffffffff: none) */
+  const float* topk_dists;       /* pinned host, rows * k */
+  tessa_subtree_result partition;
+  uint64_t fallback_rows;        /* leaf rows recomputed by the exact sequential kernel */
+} tessa_compact_view;
+
+TESSA_API int tessa_subtree_submit(tessa_ctx* ctx, const tessa_subtree_request* request, uint64_t* ticket,
+                                   void* stream);
+TESSA_API int tessa_subtree_poll(tessa_ctx* ctx, uint64_t ticket, int wait, tessa_compact_view* view);
+TESSA_API int tessa_subtree_release(tessa_ctx* ctx, uint64_t ticket);
 
 /* ---------------------------------------------------- host reduction --- */
 

@@ -24,6 +24,7 @@ ERRORS = {
     -8: "TESSA_ERR_NO_DEVICE",
     -9: "TESSA_ERR_BAD_TASK",
     -10: "TESSA_ERR_PARTITION",
+    -11: "TESSA_ERR_AGAIN",
 }
 MAX_LEAF_K = 32
 MAX_RH = 4
@@ -135,6 +136,19 @@ class SubtreeResult(ctypes.Structure):
     ]
 
 
+class SubtreeRequest(ctypes.Structure):
+    _fields_ = [("partition", SubtreeArgs), ("global_ids", c_vp), ("k", ctypes.c_uint32)]
+
+
+class CompactView(ctypes.Structure):
+    _fields_ = [
+        ("ticket", ctypes.c_uint64), ("rows", ctypes.c_uint64), ("k", ctypes.c_uint32),
+        ("leaf_count", ctypes.c_uint64), ("leaf_starts", c_vp), ("leaf_sizes", c_vp), ("leaf_tasks", c_vp),
+        ("point_ids", c_vp), ("topk_ids", c_vp), ("topk_dists", c_vp), ("partition", SubtreeResult),
+        ("fallback_rows", ctypes.c_uint64),
+    ]
+
+
 # (name, restype, argtypes) for every entry point of include/tessa_sm100.h
 SIGNATURES = [
     ("tessa_abi_version", ctypes.c_int, []),
@@ -187,6 +201,10 @@ SIGNATURES = [
      [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, c_vp, c_vp,
       ctypes.c_uint64, c_vp]),
     ("tessa_reducer_destroy", None, [c_vp]),
+    ("tessa_subtree_submit", ctypes.c_int,
+     [c_vp, ctypes.POINTER(SubtreeRequest), ctypes.POINTER(ctypes.c_uint64), c_vp]),
+    ("tessa_subtree_poll", ctypes.c_int, [c_vp, ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(CompactView)]),
+    ("tessa_subtree_release", ctypes.c_int, [c_vp, ctypes.c_uint64]),
     ("tessa_reduce_records", ctypes.c_int,
      [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32,
       c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64), c_vp]),

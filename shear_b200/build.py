@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(ROOT, "_build", "obj")
 LIB = os.path.join(HERE, "libtessa_sm100.so")
 SOURCES = ["leaf_sq8.cu", "leaf_split.cu", "quantize_sq8.cu", "assign.cu", "assign_tc.cu", "edges.cu", "capture.cu",
-           "graph_search.cu", "subtree.cu", "reducer.cu", "records.cu", "reservoirs.cu", "capi.cu", "noalloc.cu"]
+           "graph_search.cu", "subtree.cu", "reducer.cu", "records.cu", "reservoirs.cu", "submit.cu", "capi.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          f"-I{os.path.join(ROOT, 'include')}"]

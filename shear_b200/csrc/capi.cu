@@ -275,6 +275,7 @@ struct tessa_ctx {
   SubtreeState* subtree = nullptr;  // subtree partition scratch (created on first use)
   DevBuf g_temp;                    // record grouping: sort and scan scratch
   DevBuf probe;                     // bounded-wait probe: elapsed time
+  SubmitRing* ring = nullptr;       // subtree submissions (created on first use)
 };
 
 namespace {
@@ -756,6 +757,7 @@ const char* tessa_strerror(int code) {
     case TESSA_ERR_NO_DEVICE: return "no usable sm_100 device";
     case TESSA_ERR_BAD_TASK: return "malformed task descriptor";
     case TESSA_ERR_PARTITION: return "subtree partition cannot finish";
+    case TESSA_ERR_AGAIN: return "not now (no free slot, or still running)";
     default: return "unknown error";
   }
 }
@@ -792,6 +794,8 @@ int tessa_create(int device, tessa_ctx** out) {
 
 void tessa_destroy(tessa_ctx* ctx) {
   if (!ctx) return;
+  submit_ring_destroy(ctx->ring);  // waits for queued submissions
+  ctx->ring = nullptr;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   ctx->d_err.release();
@@ -1472,6 +1476,34 @@ int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* a, tessa_s
   result->host_decide_ms = stats.host_decide_ms;
   result->sync_wait_ms = stats.sync_wait_ms;
   return TESSA_OK;
+}
+
+// ------------------------------------------------- subtree submissions
+
+int tessa_subtree_submit(tessa_ctx* ctx, const tessa_subtree_request* req, uint64_t* ticket, void* stream) {
+  TRY(bind(ctx));
+  if (!req || !ticket) return fail(TESSA_ERR_INVALID_ARG, "null request or ticket");
+  const tessa_subtree_args& a = req->partition;
+  if (req->k == 0 || req->k > TESSA_MAX_LEAF_K)
+    return fail(TESSA_ERR_INVALID_ARG, "k=%u outside 1..%d", req->k, TESSA_MAX_LEAF_K);
+  if (!req->global_ids || !a.codes || !a.scales || !a.sq8_norms || !a.task_members)
+    return fail(TESSA_ERR_INVALID_ARG, "null device input");
+  if (a.task_count && (!a.task_offsets || !a.task_counts || !a.task_seeds))
+    return fail(TESSA_ERR_INVALID_ARG, "null task array");
+  if (!ctx->ring) TRY(submit_ring_create(ctx->device, &ctx->ring));
+  return submit_ring_submit(ctx->ring, req, ticket, (cudaStream_t)stream);
+}
+
+int tessa_subtree_poll(tessa_ctx* ctx, uint64_t ticket, int wait, tessa_compact_view* view) {
+  if (!ctx || !view) return fail(TESSA_ERR_INVALID_ARG, "null context or view");
+  if (!ctx->ring) return fail(TESSA_ERR_INVALID_ARG, "no submission on this context");
+  return submit_ring_poll(ctx->ring, ticket, wait, view);
+}
+
+int tessa_subtree_release(tessa_ctx* ctx, uint64_t ticket) {
+  if (!ctx) return fail(TESSA_ERR_INVALID_ARG, "null context");
+  if (!ctx->ring) return fail(TESSA_ERR_INVALID_ARG, "no submission on this context");
+  return submit_ring_release(ctx->ring, ticket);
 }
 
 // ----------------------------------------------------- record grouping

@@ -221,6 +221,14 @@ struct ReservoirCall {
   int sm_count;
 };
 int reduce_reservoirs(const ReservoirCall& r, cudaStream_t stream);
+// Subtree submissions (submit.cu): a two-slot ring run by a worker thread on a
+// private context of the same device.
+struct SubmitRing;
+int submit_ring_create(int device, SubmitRing** out);
+void submit_ring_destroy(SubmitRing* ring);
+int submit_ring_submit(SubmitRing* ring, const tessa_subtree_request* req, uint64_t* ticket, cudaStream_t caller);
+int submit_ring_poll(SubmitRing* ring, uint64_t ticket, int wait, tessa_compact_view* view);
+int submit_ring_release(SubmitRing* ring, uint64_t ticket);
 size_t reservoir_scratch_bytes(uint64_t edges, uint64_t num_points);
 
 // Records `code` and `message` as the calling thread's last error (returned by

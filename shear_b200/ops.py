@@ -557,6 +557,71 @@ def subtree_partition(codes, scales, norms, task_members, task_offsets, task_cou
     return leaf_rows[:int(r.leaf_rows_used)], starts[:n].copy(), sizes[:n].copy(), tasks[:n].copy(), stats
 
 
+# ------------------------------------------------------ subtree submissions
+
+_SUBMITTED: dict = {}  # (context handle, ticket) -> the device tensors the submission reads
+
+
+def subtree_submit(codes, scales, norms, global_ids, task_members, task_offsets, task_counts, task_seeds, k: int,
+                   params: SubtreeParams | None = None, ctx: Context | None = None) -> int:
+    """tessa_subtree_submit: partition + leaf top-k of a batch of subtree tasks,
+    queued on the context's submission worker.  Returns the ticket; the device
+    tensors are kept alive here until the ticket is polled."""
+    import torch
+
+    prm = params or SubtreeParams()
+    dev = codes.device.index
+    ctx = ctx or context(dev)
+    toff = np.ascontiguousarray(task_offsets, np.uint64)
+    tcnt = np.ascontiguousarray(task_counts, np.uint32)
+    tseed = np.ascontiguousarray(task_seeds, np.uint64)
+    a = C.SubtreeArgs(codes=codes.data_ptr(), scales=scales.data_ptr(), sq8_norms=norms.data_ptr(),
+                      resident_rows=codes.shape[0], padded_dim=codes.shape[1], task_members=task_members.data_ptr(),
+                      member_rows=int(task_members.numel()), task_offsets=toff.ctypes.data,
+                      task_counts=tcnt.ctypes.data, task_seeds=tseed.ctypes.data, task_count=tcnt.size,
+                      leaf_max=prm.leaf_max, leaf_min=prm.leaf_min, max_depth=prm.max_depth,
+                      max_leaders=prm.max_leaders, fanout_second=prm.fanout_second, root_depth=prm.root_depth,
+                      small_node_limit=prm.small_node_limit, psamp_fraction=prm.psamp_fraction)
+    req = C.SubtreeRequest(partition=a, global_ids=global_ids.data_ptr(), k=int(k))
+    ticket = ctypes.c_uint64()
+    C.check(C.load().tessa_subtree_submit(ctx.handle, ctypes.byref(req), ctypes.byref(ticket),
+                                          _stream_ptr(torch, dev)))
+    _SUBMITTED[(ctx.handle.value, ticket.value)] = (codes, scales, norms, global_ids, task_members)
+    return int(ticket.value)
+
+
+def subtree_poll(ticket: int, wait: bool = True, ctx: Context | None = None, device: int = 0):
+    """tessa_subtree_poll: None while the submission runs (wait=False), else a
+    dict of the CompactTopKBatch as numpy views of the slot's pinned memory
+    (valid until subtree_release) plus the partition stats."""
+    ctx = ctx or context(device)
+    v = C.CompactView()
+    rc = C.load().tessa_subtree_poll(ctx.handle, int(ticket), 1 if wait else 0, ctypes.byref(v))
+    if rc == -11 and not wait:
+        return None
+    _SUBMITTED.pop((ctx.handle.value, int(ticket)), None)
+    C.check(rc)
+    rows, k, nl = int(v.rows), int(v.k), int(v.leaf_count)
+
+    def arr(ptr, n, ct, dt):
+        if n == 0 or not ptr:
+            return np.zeros(0, dt)
+        return np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ct)), shape=(n,)).view(dt)
+    stats = {f: getattr(v.partition, f) for f, _ in C.SubtreeResult._fields_}
+    return dict(ticket=int(v.ticket), rows=rows, k=k, leaf_starts=arr(v.leaf_starts, nl, ctypes.c_uint64, np.uint64),
+                leaf_sizes=arr(v.leaf_sizes, nl, ctypes.c_uint32, np.uint32),
+                leaf_tasks=arr(v.leaf_tasks, nl, ctypes.c_uint32, np.uint32),
+                point_ids=arr(v.point_ids, rows, ctypes.c_uint32, np.uint32),
+                topk_ids=arr(v.topk_ids, rows * k, ctypes.c_uint32, np.uint32),
+                topk_dists=arr(v.topk_dists, rows * k, ctypes.c_float, np.float32),
+                partition=stats, fallback_rows=int(v.fallback_rows))
+
+
+def subtree_release(ticket: int, ctx: Context | None = None, device: int = 0) -> None:
+    ctx = ctx or context(device)
+    C.check(C.load().tessa_subtree_release(ctx.handle, int(ticket)))
+
+
 # ---------------------------------------------------------- host reduction
 
 class Reducer:
