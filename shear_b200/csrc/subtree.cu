@@ -521,11 +521,89 @@ struct Buf {
 
 }  // namespace subtree
 
+// Pinned host memory for one phase's copies: the host tables of a phase are
+// packed here and copied with cudaMemcpyAsync from pinned memory (no driver
+// staging of pageable memory, no host-side wait).  A stage is refilled only
+// after the stream has passed the copies that read it (the round's syncs).
+struct PinnedStage {
+  uint8_t* p = nullptr;
+  size_t cap = 0;
+  std::vector<uint8_t> host;  // bytes collected for the next flush
+  struct Item {
+    void* dst;
+    size_t off, bytes;
+  };
+  std::vector<Item> items;
+  void add(void* dst, const void* src, size_t bytes) {
+    const size_t off = (host.size() + 15) & ~size_t(15);
+    host.resize(off + bytes);
+    if (bytes) memcpy(host.data() + off, src, bytes);
+    items.push_back(Item{dst, off, bytes});
+  }
+  // copies every item to its device destination on `st`
+  cudaError_t flush(cudaStream_t st) {
+    if (host.size() > cap) {
+      cudaError_t e = cudaStreamSynchronize(st);
+      if (e != cudaSuccess) return e;
+      if (p) cudaFreeHost(p);
+      p = nullptr;
+      cap = 0;
+      const size_t want = host.size() + host.size() / 4 + 4096;
+      e = cudaHostAlloc(reinterpret_cast<void**>(&p), want, cudaHostAllocDefault);
+      if (e != cudaSuccess) return e;
+      cap = want;
+    }
+    if (!host.empty()) memcpy(p, host.data(), host.size());
+    for (const Item& it : items) {
+      if (!it.bytes) continue;
+      const cudaError_t e = cudaMemcpyAsync(it.dst, p + it.off, it.bytes, cudaMemcpyHostToDevice, st);
+      if (e != cudaSuccess) return e;
+    }
+    host.clear();
+    items.clear();
+    return cudaSuccess;
+  }
+  void release() {
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+  }
+};
+
+struct PinnedBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  bool ensure(size_t need) {
+    if (need <= cap) return true;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+    if (cudaHostAlloc(&p, need + need / 4 + 64, cudaHostAllocDefault) != cudaSuccess) {
+      p = nullptr;
+      return false;
+    }
+    cap = need + need / 4 + 64;
+    return true;
+  }
+  void release() {
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+  }
+  template <class T>
+  T* as() const {
+    return reinterpret_cast<T*>(p);
+  }
+};
+
 struct SubtreeState {
   subtree::Buf cur, next, member_res, slots, leader_local, leader_res, counts, dests, nodes, small_nodes, tables,
       task_off, t_moff, t_mcnt, t_loff, t_lcnt, t_rh, t_out, work;
   // phase boundaries of a round: assignment, scatter, small path
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  // pinned staging: per-phase host tables, counts and small-node tables back
+  PinnedStage stage_assign, stage_scatter, stage_small;
+  PinnedBuf h_counts, h_tables, h_bits;
   bool events() {
     for (auto& e : ev)
       if (!e && cudaEventCreate(&e) != cudaSuccess) return false;
@@ -536,6 +614,12 @@ struct SubtreeState {
                            &small_nodes, &tables, &task_off, &t_moff, &t_mcnt, &t_loff, &t_lcnt, &t_rh, &t_out,
                            &work};
     for (auto* b : all) b->release();
+    stage_assign.release();
+    stage_scatter.release();
+    stage_small.release();
+    h_counts.release();
+    h_tables.release();
+    h_bits.release();
   }
 };
 
@@ -716,14 +800,18 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       ST_ALLOC(S->t_rh, L * 4);
       ST_ALLOC(S->t_out, L * 8);
       ST_ALLOC(S->work, work.size() * 8);
-      ST_CUDA(cudaMemcpyAsync(S->nodes.ptr, d.data(), L * sizeof(NodeDesc), cudaMemcpyHostToDevice, st));
-      ST_CUDA(cudaMemcpyAsync(S->t_moff.ptr, moff.data(), L * 4, cudaMemcpyHostToDevice, st));
-      ST_CUDA(cudaMemcpyAsync(S->t_mcnt.ptr, mcnt.data(), L * 4, cudaMemcpyHostToDevice, st));
-      ST_CUDA(cudaMemcpyAsync(S->t_loff.ptr, loff.data(), L * 4, cudaMemcpyHostToDevice, st));
-      ST_CUDA(cudaMemcpyAsync(S->t_lcnt.ptr, lcnt.data(), L * 4, cudaMemcpyHostToDevice, st));
-      ST_CUDA(cudaMemcpyAsync(S->t_rh.ptr, rh.data(), L * 4, cudaMemcpyHostToDevice, st));
-      ST_CUDA(cudaMemcpyAsync(S->t_out.ptr, tout.data(), L * 8, cudaMemcpyHostToDevice, st));
-      ST_CUDA(cudaMemcpyAsync(S->work.ptr, work.data(), work.size() * 8, cudaMemcpyHostToDevice, st));
+      {
+        PinnedStage& g = S->stage_assign;
+        g.add(S->nodes.ptr, d.data(), L * sizeof(NodeDesc));
+        g.add(S->t_moff.ptr, moff.data(), L * 4);
+        g.add(S->t_mcnt.ptr, mcnt.data(), L * 4);
+        g.add(S->t_loff.ptr, loff.data(), L * 4);
+        g.add(S->t_lcnt.ptr, lcnt.data(), L * 4);
+        g.add(S->t_rh.ptr, rh.data(), L * 4);
+        g.add(S->t_out.ptr, tout.data(), L * 8);
+        g.add(S->work.ptr, work.data(), work.size() * 8);
+        ST_CUDA(g.flush(st));
+      }
       stats->host_prep_ms += ms_since(t_prep);
       ST_CUDA(cudaEventRecord(S->ev[0], st));
       prepare_kernel<<<(unsigned)L, 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->cur.as<uint32_t>(), a.task_members,
@@ -762,12 +850,15 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
                                                 S->counts.as<uint32_t>());
       ST_CUDA(cudaGetLastError());
       ST_CUDA(cudaEventRecord(S->ev[1], st));
-      ST_CUDA(cudaMemcpyAsync(counts.data(), S->counts.ptr, L * kSlots * 4, cudaMemcpyDeviceToHost, st));
-      uint32_t bits = 0;
-      ST_CUDA(cudaMemcpyAsync(&bits, d_err, 4, cudaMemcpyDeviceToHost, st));
+      if (!S->h_counts.ensure(L * kSlots * 4) || !S->h_bits.ensure(8))
+        return set_last_error(TESSA_ERR_OOM, "subtree pinned staging allocation failed");
+      ST_CUDA(cudaMemcpyAsync(S->h_counts.p, S->counts.ptr, L * kSlots * 4, cudaMemcpyDeviceToHost, st));
+      ST_CUDA(cudaMemcpyAsync(S->h_bits.p, d_err, 4, cudaMemcpyDeviceToHost, st));
       const auto t_wait = clk::now();
       ST_CUDA(cudaStreamSynchronize(st));
       stats->sync_wait_ms += ms_since(t_wait);
+      const uint32_t bits = *S->h_bits.as<uint32_t>();
+      memcpy(counts.data(), S->h_counts.p, L * kSlots * 4);
       if (bits) return bits & TESSA_DEVERR_TIMEOUT ? set_last_error(TESSA_ERR_TIMEOUT, "subtree assignment timed out")
                                                    : set_last_error(TESSA_ERR_BAD_TASK, "subtree assignment failed");
       stats->large_assignments += (uint32_t)L;
@@ -878,8 +969,9 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
     if (!sc.empty()) {
       ST_ALLOC(S->nodes, sc.size() * sizeof(NodeDesc));
       ST_ALLOC(S->dests, dests.size() * 8);
-      ST_CUDA(cudaMemcpyAsync(S->nodes.ptr, sc.data(), sc.size() * sizeof(NodeDesc), cudaMemcpyHostToDevice, st));
-      ST_CUDA(cudaMemcpyAsync(S->dests.ptr, dests.data(), dests.size() * 8, cudaMemcpyHostToDevice, st));
+      S->stage_scatter.add(S->nodes.ptr, sc.data(), sc.size() * sizeof(NodeDesc));
+      S->stage_scatter.add(S->dests.ptr, dests.data(), dests.size() * 8);
+      ST_CUDA(S->stage_scatter.flush(st));
       ST_CUDA(cudaEventRecord(S->ev[2], st));
       scatter_kernel<<<(unsigned)sc.size(), 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->dests.as<uint64_t>(),
                                                          S->cur.as<uint32_t>(), S->slots.as<uint32_t>(),
@@ -892,7 +984,8 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
     if (!sm.empty()) {
       ST_ALLOC(S->small_nodes, sm.size() * sizeof(NodeDesc));
       ST_ALLOC(S->tables, sm.size() * kTab * 4);
-      ST_CUDA(cudaMemcpyAsync(S->small_nodes.ptr, sm.data(), sm.size() * sizeof(NodeDesc), cudaMemcpyHostToDevice, st));
+      S->stage_small.add(S->small_nodes.ptr, sm.data(), sm.size() * sizeof(NodeDesc));
+      ST_CUDA(S->stage_small.flush(st));
       SmallParams sp{};
       sp.nodes = S->small_nodes.as<NodeDesc>();
       sp.cur = S->cur.as<uint32_t>();
@@ -917,10 +1010,13 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       ST_CUDA(cudaEventRecord(S->ev[5], st));
       stats->launches++;
       std::vector<uint32_t> tab(sm.size() * kTab);
-      ST_CUDA(cudaMemcpyAsync(tab.data(), S->tables.ptr, tab.size() * 4, cudaMemcpyDeviceToHost, st));
-      uint32_t bits = 0;
-      ST_CUDA(cudaMemcpyAsync(&bits, d_err, 4, cudaMemcpyDeviceToHost, st));
+      if (!S->h_tables.ensure(tab.size() * 4) || !S->h_bits.ensure(8))
+        return set_last_error(TESSA_ERR_OOM, "subtree pinned staging allocation failed");
+      ST_CUDA(cudaMemcpyAsync(S->h_tables.p, S->tables.ptr, tab.size() * 4, cudaMemcpyDeviceToHost, st));
+      ST_CUDA(cudaMemcpyAsync(S->h_bits.p, d_err, 4, cudaMemcpyDeviceToHost, st));
       ST_CUDA(cudaStreamSynchronize(st));
+      const uint32_t bits = *S->h_bits.as<uint32_t>();
+      memcpy(tab.data(), S->h_tables.p, tab.size() * 4);
       if (bits) return set_last_error(TESSA_ERR_BAD_TASK, "subtree small-node partition failed");
       // insert each small node's leaves at its place in the list (back to front
       // so earlier insertion points stay valid)
