@@ -1467,7 +1467,7 @@ def run_build_reference(a):
     line = {
         "impl": "reference", "metric": BUILD_METRIC, "value": value, "unit": "vectors/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": f"synthetic stand-in for BASELINE config {a.config} (seeded Gaussian mixture, host)",
         "config": build_desc(a, c),
         "cpu_baseline": {"value": value, "unit": "vectors/s", "cores": O.num_threads(), "kind": "port",

@@ -129,10 +129,13 @@ def group_child_runs(child_ids, num_leaders: int):
     import torch
 
     n, f = child_ids.shape
-    keys = child_ids.reshape(-1).to(torch.int64)
+    keys = child_ids.reshape(-1)
+    # the narrowest key type that holds the leader ids: a stable radix sort of
+    # 16-bit keys takes two passes instead of eight
+    keys = keys.to(torch.int16) if num_leaders <= 32767 else keys.to(torch.int64)
     order = torch.argsort(keys, stable=True)
     members = (order // f).to(torch.int32)
-    counts = torch.bincount(keys, minlength=num_leaders).cpu().numpy().astype(np.uint32)
+    counts = torch.bincount(child_ids.reshape(-1), minlength=num_leaders).cpu().numpy().astype(np.uint32)
     offsets = np.concatenate([[0], np.cumsum(counts, dtype=np.uint64)[:-1]]).astype(np.uint64)
     return members, counts, offsets
 
