@@ -775,6 +775,11 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       std::vector<uint32_t> moff(L), mcnt(L), loff(L), lcnt(L), rh(L);
       std::vector<uint64_t> tout(L);
       std::vector<uint2> work;
+      {
+        size_t items = 0;
+        for (size_t j = 0; j < L; ++j) items += (nodes[large_idx[j]].n + 127u) / 128u;
+        work.reserve(items);
+      }
       uint32_t nb_max = 0;
       for (size_t j = 0; j < L; ++j) {
         const HNode& nd = nodes[large_idx[j]];
@@ -872,6 +877,8 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
     // scatter plan for leaf-all and large nodes
     std::vector<NodeDesc> sc;
     std::vector<uint64_t> dests;
+    sc.reserve(nodes.size());
+    dests.reserve(nodes.size() * kSlots);
     // small nodes: reservation and position in the leaf list
     std::vector<NodeDesc> sm;
     std::vector<size_t> sm_leaf_pos;
@@ -920,7 +927,8 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       uint32_t retry_max = nd.n < 2u ? 2u : nd.n;
       if (retry_max > kSlots) retry_max = kSlots;
       NodeDesc plan{nd.off, nd.n, nd.task, nd.num, nd.attempt, nd.lf, nd.depth, kSplit, nd.seed, 0};
-      std::vector<uint64_t> dst(kSlots, 0);
+      uint64_t dst[kSlots];
+      memset(dst, 0, sizeof dst);
       if (!split && (nd.attempt == 0 || nd.num < retry_max)) {
         uint32_t next_num = nd.num;
         if (nd.attempt > 0) {
@@ -961,7 +969,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
         }
       }
       sc.push_back(plan);
-      dests.insert(dests.end(), dst.begin(), dst.end());
+      dests.insert(dests.end(), dst, dst + kSlots);
     }
 
     stats->host_decide_ms += ms_since(t_decide);
