@@ -130,6 +130,13 @@ __device__ __forceinline__ void put(uint64_t dest, uint32_t rank, uint32_t local
 // chunk).  Split: a row's rank in child s is the number of earlier rows of the
 // node assigned to s, from a per-chunk bitmap per slot plus the running count
 // of the chunks before -- the sequential scatter order (ascending position).
+// Assignment work items of large node j: (j, first row) for every 128 rows.
+__global__ void work_kernel(const NodeDesc* nodes, const uint32_t* item_off, uint2* work) {
+  const uint32_t j = blockIdx.x;
+  const uint32_t n = nodes[j].n, base = item_off[j];
+  for (uint32_t i = threadIdx.x; i * 128u < n; i += blockDim.x) work[base + i] = make_uint2(j, i * 128u);
+}
+
 __global__ void __launch_bounds__(256) scatter_kernel(const NodeDesc* nodes, const uint64_t* dests,
                                                       const uint32_t* cur, const uint32_t* slots,
                                                       const uint32_t* task_members, const uint64_t* task_off,
@@ -139,7 +146,7 @@ __global__ void __launch_bounds__(256) scatter_kernel(const NodeDesc* nodes, con
   __shared__ uint32_t tot[kSlots];
   __shared__ uint32_t running[kSlots];
   const NodeDesc nd = nodes[blockIdx.x];
-  const uint64_t* dst = dests + (uint64_t)blockIdx.x * kSlots;
+  const uint64_t* dst = dests + nd.out;  // this node's destinations: 1, 2 or num entries
   const uint32_t* tm = task_members + task_off[nd.task];
   const uint32_t t = threadIdx.x;
   if (nd.mode != kSplit) {
@@ -598,7 +605,7 @@ struct PinnedBuf {
 
 struct SubtreeState {
   subtree::Buf cur, next, member_res, slots, leader_local, leader_res, counts, dests, nodes, small_nodes, tables,
-      task_off, t_moff, t_mcnt, t_loff, t_lcnt, t_rh, t_out, work;
+      task_off, t_moff, t_mcnt, t_loff, t_lcnt, t_rh, t_out, work, item_off;
   // phase boundaries of a round: assignment, scatter, small path
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   // pinned staging: per-phase host tables, counts and small-node tables back
@@ -612,7 +619,7 @@ struct SubtreeState {
   void release() {
     subtree::Buf* all[] = {&cur, &next, &member_res, &slots, &leader_local, &leader_res, &counts, &dests, &nodes,
                            &small_nodes, &tables, &task_off, &t_moff, &t_mcnt, &t_loff, &t_lcnt, &t_rh, &t_out,
-                           &work};
+                           &work, &item_off};
     for (auto* b : all) b->release();
     stage_assign.release();
     stage_scatter.release();
@@ -774,12 +781,10 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       std::vector<NodeDesc> d(L);
       std::vector<uint32_t> moff(L), mcnt(L), loff(L), lcnt(L), rh(L);
       std::vector<uint64_t> tout(L);
-      std::vector<uint2> work;
-      {
-        size_t items = 0;
-        for (size_t j = 0; j < L; ++j) items += (nodes[large_idx[j]].n + 127u) / 128u;
-        work.reserve(items);
-      }
+      // work items (node, first row) are written on the device from each
+      // node's first item index
+      std::vector<uint32_t> item_off(L + 1);
+      uint64_t items = 0;
       uint32_t nb_max = 0;
       for (size_t j = 0; j < L; ++j) {
         const HNode& nd = nodes[large_idx[j]];
@@ -791,7 +796,8 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
         rh[j] = nd.lf;
         tout[j] = (uint64_t)nd.off * 4u;
         nb_max = std::max(nb_max, nd.num);
-        for (uint32_t r0 = 0; r0 < nd.n; r0 += 128) work.push_back(make_uint2((uint32_t)j, r0));
+        item_off[j] = (uint32_t)items;
+        items += (nd.n + 127u) / 128u;
       }
       if (L * kSlots >= 0xffffffffull) return set_last_error(TESSA_ERR_UNSUPPORTED, "too many subtree nodes");
       ST_ALLOC(S->nodes, L * sizeof(NodeDesc));
@@ -804,7 +810,10 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       ST_ALLOC(S->t_lcnt, L * 4);
       ST_ALLOC(S->t_rh, L * 4);
       ST_ALLOC(S->t_out, L * 8);
-      ST_ALLOC(S->work, work.size() * 8);
+      if (items >= 0xffffffffull) return set_last_error(TESSA_ERR_UNSUPPORTED, "too many subtree work items");
+      item_off[L] = (uint32_t)items;
+      ST_ALLOC(S->work, items * 8);
+      ST_ALLOC(S->item_off, (L + 1) * 4);
       {
         PinnedStage& g = S->stage_assign;
         g.add(S->nodes.ptr, d.data(), L * sizeof(NodeDesc));
@@ -814,11 +823,13 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
         g.add(S->t_lcnt.ptr, lcnt.data(), L * 4);
         g.add(S->t_rh.ptr, rh.data(), L * 4);
         g.add(S->t_out.ptr, tout.data(), L * 8);
-        g.add(S->work.ptr, work.data(), work.size() * 8);
+        g.add(S->item_off.ptr, item_off.data(), (L + 1) * 4);
         ST_CUDA(g.flush(st));
       }
       stats->host_prep_ms += ms_since(t_prep);
       ST_CUDA(cudaEventRecord(S->ev[0], st));
+      work_kernel<<<(unsigned)L, 128, 0, st>>>(S->nodes.as<NodeDesc>(), S->item_off.as<uint32_t>(),
+                                               S->work.as<uint2>());
       prepare_kernel<<<(unsigned)L, 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->cur.as<uint32_t>(), a.task_members,
                                                   S->task_off.as<uint64_t>(), S->member_res.as<uint32_t>(),
                                                   S->leader_local.as<uint32_t>(), S->leader_res.as<uint32_t>());
@@ -839,7 +850,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       prm.t_rh = S->t_rh.as<uint32_t>();
       prm.t_out = S->t_out.as<uint64_t>();
       prm.work = S->work.as<uint2>();
-      prm.num_work = (uint32_t)work.size();
+      prm.num_work = (uint32_t)items;
       prm.fused = 1;
       prm.out_ids = nullptr;
       prm.out_dists = nullptr;
@@ -850,7 +861,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       prm.out_slots = S->slots.as<uint32_t>();
       int rc = launch_assign_sq8_tc(prm, nb_max, sm_count, st);
       if (rc != TESSA_OK) return set_last_error(rc, "subtree assignment launch failed");
-      stats->launches += 3;  // prepare, assignment, count
+      stats->launches += 4;  // work items, prepare, assignment, count
       count_kernel<<<(unsigned)L, 256, 0, st>>>(S->nodes.as<NodeDesc>(), S->slots.as<uint32_t>(),
                                                 S->counts.as<uint32_t>());
       ST_CUDA(cudaGetLastError());
@@ -878,7 +889,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
     std::vector<NodeDesc> sc;
     std::vector<uint64_t> dests;
     sc.reserve(nodes.size());
-    dests.reserve(nodes.size() * kSlots);
+    dests.reserve(nodes.size() * 8);
     // small nodes: reservation and position in the leaf list
     std::vector<NodeDesc> sm;
     std::vector<size_t> sm_leaf_pos;
@@ -899,9 +910,8 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
         uint64_t at;
         if (!leaf_alloc(nd.n, &at)) return set_last_error(TESSA_ERR_PARTITION, "subtree leaf_rows capacity exceeded");
         leaves.push_back(LeafEnt{at, nd.n, nd.task});
-        sc.push_back(NodeDesc{nd.off, nd.n, nd.task, 0, 0, 0, nd.depth, kCopyLeaf, nd.seed, 0});
-        dests.resize(sc.size() * kSlots, 0);
-        dests[(sc.size() - 1) * kSlots] = at | kLeafBit;
+        sc.push_back(NodeDesc{nd.off, nd.n, nd.task, 0, 0, 0, nd.depth, kCopyLeaf, nd.seed, dests.size()});
+        dests.push_back(at | kLeafBit);
         continue;
       }
       if (kind[q] == kSmall) {
@@ -926,7 +936,7 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
       const bool split = nonempty > 1u && meaningful_split(nd.n, max_child, a.leaf_max);
       uint32_t retry_max = nd.n < 2u ? 2u : nd.n;
       if (retry_max > kSlots) retry_max = kSlots;
-      NodeDesc plan{nd.off, nd.n, nd.task, nd.num, nd.attempt, nd.lf, nd.depth, kSplit, nd.seed, 0};
+      NodeDesc plan{nd.off, nd.n, nd.task, nd.num, nd.attempt, nd.lf, nd.depth, kSplit, nd.seed, dests.size()};
       uint64_t dst[kSlots];
       memset(dst, 0, sizeof dst);
       if (!split && (nd.attempt == 0 || nd.num < retry_max)) {
@@ -969,7 +979,9 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
         }
       }
       sc.push_back(plan);
-      dests.insert(dests.end(), dst, dst + kSlots);
+      // destinations the scatter reads: one (copy), two (balanced) or one per leader slot
+      const uint32_t ndst = plan.mode == kCopyNext ? 1u : (plan.mode == kBalanced ? 2u : nd.num);
+      dests.insert(dests.end(), dst, dst + ndst);
     }
 
     stats->host_decide_ms += ms_since(t_decide);

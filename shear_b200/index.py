@@ -227,6 +227,15 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, s
                                    leaf_rows_used=0, kernel_launches=0),
                     fallback=0)
     t = time.perf_counter()
+    # the sketches depend only on the rows: computed on a side stream, they
+    # fill the device while the partition's host round loop decides splits
+    side = None
+    if sketches is None:
+        main = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            sketches = ops.sketch_rows(xd, sketch_planes(torch, dev, p, dim), ctx=ctx)
     sp = ops.SubtreeParams(c_max=p.adaptive_c_max(n), max_depth=p.max_depth, max_leaders=p.max_leaders,
                            fanout_second=p.fanout_second, root_depth=st["depth"], psamp_fraction=p.psamp_fraction)
     leaf_rows, starts, sizes, _, pst = ops.subtree_partition(d0.codes, d0.scales, d0.norms, st["members"],
@@ -243,8 +252,9 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, s
     ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, st["gids"], leaf_rows, starts, sizes, k, out=(ids, dists),
                       ctx=ctx)
     ev[1].record()
-    if sketches is None:
-        sketches = ops.sketch_rows(xd, sketch_planes(torch, dev, p, dim), ctx=ctx)
+    if side is not None:
+        torch.cuda.current_stream(dev).wait_stream(side)
+        sketches.record_stream(torch.cuda.current_stream(dev))
     hf, hr = ops.edge_hashes(leaf_rows, ids, k, sketches, p.m_hash_bits, starts, sizes, ctx=ctx)
     torch.cuda.synchronize(dev)
     timings["leaf_s"] = time.perf_counter() - t
