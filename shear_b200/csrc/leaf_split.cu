@@ -175,9 +175,14 @@ __device__ __forceinline__ bool load_a_tile(const Smem& s, const Params& p, uint
       r[4 * u + 2] = v.z;
       r[4 * u + 3] = v.w;
     }
+    // The stage is released to the TMA only after every lane's loads have
+    // delivered: the values go to tensor memory and the store completes
+    // before the warp signals the read (a refill writes the box from row 0
+    // on, so an early release would corrupt the first rows of the slab).
+    tmem_st_32x32b_x16(tmem_base + lane_base + sl * (kSlab / 4u) + half * 16u, r);
+    tmem_st_wait();
     __syncwarp();
     if (lane == 0) mbar_arrive(&s.a_rd[st]);
-    tmem_st_32x32b_x16(tmem_base + lane_base + sl * (kSlab / 4u) + half * 16u, r);
     if (ew == 0) {
       bool rd = true;
       if (lane == 0) {
