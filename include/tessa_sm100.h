@@ -43,7 +43,7 @@ extern "C" {
 
 /* 1: leaf, quantize, assignment, replay; 2: + host pipeline knob, global D0, candidate
  * edges, capture digests, graph search (additive); 3: + subtree partition (additive). */
-#define TESSA_ABI_VERSION 4
+#define TESSA_ABI_VERSION 5
 
 #define TESSA_OK 0
 #define TESSA_ERR_INVALID_ARG (-1)  /* malformed sizes, null pointers, k out of range */
@@ -467,6 +467,12 @@ typedef struct tessa_subtree_args {
   uint32_t* leaf_sizes;          /* host */
   uint32_t* leaf_tasks;          /* host, may be NULL */
   uint64_t leaf_capacity;
+  /* Optional (may be NULL): device output of leaf_rows_capacity x padded_dim
+   * bytes; row p receives the codes of leaf_rows[p] (zeros where the arena
+   * holds no row) -- the leaf-ordered codes tessa_leaf_topk_sq8 takes as
+   * leaf_ordered_codes.  Each round's leaves are copied while the host
+   * decides the next round. */
+  int8_t* leaf_codes;
 } tessa_subtree_args;
 
 typedef struct tessa_subtree_result {

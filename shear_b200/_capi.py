@@ -121,7 +121,7 @@ class SubtreeArgs(ctypes.Structure):
         ("max_leaders", ctypes.c_uint32), ("fanout_second", ctypes.c_uint32), ("root_depth", ctypes.c_uint32),
         ("small_node_limit", ctypes.c_uint32), ("psamp_fraction", ctypes.c_float),
         ("leaf_rows", c_vp), ("leaf_rows_capacity", ctypes.c_uint64), ("leaf_starts", c_vp),
-        ("leaf_sizes", c_vp), ("leaf_tasks", c_vp), ("leaf_capacity", ctypes.c_uint64),
+        ("leaf_sizes", c_vp), ("leaf_tasks", c_vp), ("leaf_capacity", ctypes.c_uint64), ("leaf_codes", c_vp),
     ]
 
 

@@ -154,6 +154,7 @@ int run_job(SubmitRing* R, submit::Slot& S) {
   S.leaf_sizes.assign(cap, 0);
   S.leaf_tasks.assign(cap, 0);
   tessa_subtree_args a = in;
+  a.leaf_codes = nullptr;  // the slot keeps no leaf-ordered copy
   a.task_offsets = S.task_offsets.data();
   a.task_counts = S.task_counts.data();
   a.task_seeds = S.task_seeds.data();

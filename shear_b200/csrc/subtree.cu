@@ -608,6 +608,15 @@ struct SubtreeState {
       task_off, t_moff, t_mcnt, t_loff, t_lcnt, t_rh, t_out, work, item_off;
   // phase boundaries of a round: assignment, scatter, small path
   cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  // leaf-ordered code copies run on a side stream after each round's scatter
+  cudaStream_t side = nullptr;
+  cudaEvent_t round_done = nullptr, side_done = nullptr;
+  bool side_stream() {
+    if (!side && cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking) != cudaSuccess) return false;
+    if (!round_done && cudaEventCreateWithFlags(&round_done, cudaEventDisableTiming) != cudaSuccess) return false;
+    if (!side_done && cudaEventCreateWithFlags(&side_done, cudaEventDisableTiming) != cudaSuccess) return false;
+    return true;
+  }
   // pinned staging: per-phase host tables, counts and small-node tables back
   PinnedStage stage_assign, stage_scatter, stage_small;
   PinnedBuf h_counts, h_tables, h_bits;
@@ -636,6 +645,12 @@ void subtree_state_free(SubtreeState* s) {
   s->release();
   for (auto& e : s->ev)
     if (e) cudaEventDestroy(e);
+  if (s->side) {
+    cudaStreamSynchronize(s->side);
+    cudaStreamDestroy(s->side);
+  }
+  if (s->round_done) cudaEventDestroy(s->round_done);
+  if (s->side_done) cudaEventDestroy(s->side_done);
   delete s;
 }
 
@@ -736,8 +751,20 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
   const uint32_t small_smem = (uint32_t)sizeof(SmallSmem);
   ST_CUDA(cudaFuncSetAttribute(small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)small_smem));
 
+  if (a.leaf_codes && !S->side_stream())
+    return set_last_error(TESSA_ERR_CUDA, "subtree side stream could not be created");
+  // on every way out (errors included) the caller's stream follows the copies
+  struct SideJoin {
+    SubtreeState* S;
+    cudaStream_t st;
+    bool on;
+    ~SideJoin() {
+      if (on && cudaEventRecord(S->side_done, S->side) == cudaSuccess) cudaStreamWaitEvent(st, S->side_done, 0);
+    }
+  } side_join{S, st, a.leaf_codes != nullptr};
   while (!nodes.empty()) {
     stats->rounds++;
+    const uint64_t leaf_round0 = leaf_used;
     auto t_prep = clk::now();
     // ---- classify
     std::vector<Kind> kind(nodes.size());
@@ -1047,6 +1074,16 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
           ins.push_back(LeafEnt{sm[j].out + tb[1 + 2 * cidx], tb[2 + 2 * cidx], sm[j].task});
         leaves.insert(leaves.begin() + (ptrdiff_t)sm_leaf_pos[j], ins.begin(), ins.end());
       }
+    }
+    if (a.leaf_codes && leaf_used > leaf_round0) {
+      // this round's leaves are final: copy their codes while the host decides
+      ST_CUDA(cudaEventRecord(S->round_done, st));
+      ST_CUDA(cudaStreamWaitEvent(S->side, S->round_done, 0));
+      const int grc = launch_gather_rows(a.codes, a.leaf_rows + leaf_round0, leaf_used - leaf_round0, a.padded_dim,
+                                         a.resident_rows, a.leaf_codes + leaf_round0 * a.padded_dim, sm_count,
+                                         S->side);
+      if (grc != TESSA_OK) return set_last_error(grc, "subtree leaf-code copy launch failed");
+      stats->launches++;
     }
     const auto t_end = clk::now();
     ST_CUDA(cudaStreamSynchronize(st));

@@ -238,6 +238,9 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, s
             sketches = ops.sketch_rows(xd, sketch_planes(torch, dev, p, dim), ctx=ctx)
     sp = ops.SubtreeParams(c_max=p.adaptive_c_max(n), max_depth=p.max_depth, max_leaders=p.max_leaders,
                            fanout_second=p.fanout_second, root_depth=st["depth"], psamp_fraction=p.psamp_fraction)
+    # (the partition can also copy the leaf-ordered codes round by round --
+    # leaf_codes -- but on a side stream those copies slow the concurrent
+    # assignment kernels by more than they save the leaf call)
     leaf_rows, starts, sizes, _, pst = ops.subtree_partition(d0.codes, d0.scales, d0.norms, st["members"],
                                                              st["offsets"][sel], st["counts"][sel],
                                                              st["seeds"][sel], sp, ctx=ctx)

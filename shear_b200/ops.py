@@ -510,6 +510,21 @@ class SubtreeParams:
                          self.root_depth, self.small_node_limit], np.uint32)
 
 
+def subtree_leaf_capacity(member_rows: int, params: SubtreeParams | None = None) -> int:
+    """Rows of the leaf arena subtree_partition allocates for member_rows task rows."""
+    prm = params or SubtreeParams()
+    return max(prm.fanout_second, 1) * int(member_rows) + 16
+
+
+def _leaf_codes_ptr(leaf_codes, cap: int, codes):
+    if leaf_codes is None:
+        return None
+    if not leaf_codes.is_cuda or leaf_codes.dtype != codes.dtype or not leaf_codes.is_contiguous() or \
+            leaf_codes.numel() < cap * codes.shape[1]:
+        raise ValueError(f"leaf_codes must be a contiguous int8 CUDA tensor of at least {cap} x {codes.shape[1]}")
+    return leaf_codes.data_ptr()
+
+
 def subtree_root_seed(random_seed: int, depth: int, rows: int, parent_points: int, min_recurse_size: int) -> int:
     """gpu_queue_root_seed (CB:1597-1603)."""
     def rotl(v, r):
@@ -520,7 +535,7 @@ def subtree_root_seed(random_seed: int, depth: int, rows: int, parent_points: in
 
 
 def subtree_partition(codes, scales, norms, task_members, task_offsets, task_counts, task_seeds,
-                      params: SubtreeParams | None = None, ctx: Context | None = None):
+                      params: SubtreeParams | None = None, ctx: Context | None = None, leaf_codes=None):
     """tessa_subtree_partition on device tensors (codes/scales/norms/task_members);
     task arrays are host sequences.  Returns (leaf_rows device int32 tensor of the
     used extent, leaf_starts u64, leaf_sizes u32, leaf_tasks u32, stats dict)."""
@@ -533,7 +548,8 @@ def subtree_partition(codes, scales, norms, task_members, task_offsets, task_cou
     tcnt = np.ascontiguousarray(task_counts, np.uint32)
     tseed = np.ascontiguousarray(task_seeds, np.uint64)
     member_rows = int(task_members.numel())
-    cap = max(prm.fanout_second, 1) * member_rows + 16
+    # every task row lands in at most fanout_second leaves (replication only at the subtree root)
+    cap = subtree_leaf_capacity(int(tcnt.astype(np.uint64).sum()), prm)
     leaf_rows = torch.empty(cap, dtype=torch.int32, device=codes.device)
     starts = np.zeros(cap, np.uint64)
     sizes = np.zeros(cap, np.uint32)
@@ -546,7 +562,8 @@ def subtree_partition(codes, scales, norms, task_members, task_offsets, task_cou
                       fanout_second=prm.fanout_second, root_depth=prm.root_depth,
                       small_node_limit=prm.small_node_limit, psamp_fraction=prm.psamp_fraction,
                       leaf_rows=leaf_rows.data_ptr(), leaf_rows_capacity=cap, leaf_starts=starts.ctypes.data,
-                      leaf_sizes=sizes.ctypes.data, leaf_tasks=tasks.ctypes.data, leaf_capacity=cap)
+                      leaf_sizes=sizes.ctypes.data, leaf_tasks=tasks.ctypes.data, leaf_capacity=cap,
+                      leaf_codes=_leaf_codes_ptr(leaf_codes, cap, codes))
     r = C.SubtreeResult()
     C.check(C.load().tessa_subtree_partition(ctx.handle, ctypes.byref(a), ctypes.byref(r), _stream_ptr(torch, dev)))
     n = int(r.leaf_count)

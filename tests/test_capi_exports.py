@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
 def test_strerror_and_version_without_device():
     from shear_b200 import _capi
     lib = _capi.load()
-    assert lib.tessa_abi_version() == 4
+    assert lib.tessa_abi_version() == 5
     assert lib.tessa_strerror(-10) == b"subtree partition cannot finish"
     assert lib.tessa_strerror(0) == b"ok"
     assert lib.tessa_strerror(-4) == b"device wait timed out"
