@@ -37,5 +37,6 @@ def test_strerror_and_version_without_device():
     lib = _capi.load()
     assert lib.tessa_abi_version() == 5
     assert lib.tessa_strerror(-10) == b"subtree partition cannot finish"
+    assert lib.tessa_strerror(-11) == b"not now (no free slot, or still running)"
     assert lib.tessa_strerror(0) == b"ok"
     assert lib.tessa_strerror(-4) == b"device wait timed out"
