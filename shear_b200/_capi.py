@@ -191,6 +191,7 @@ SIGNATURES = [
     ("tessa_subtree_partition", ctypes.c_int,
      [c_vp, ctypes.POINTER(SubtreeArgs), ctypes.POINTER(SubtreeResult), c_vp]),
     ("tessa_set_wait_timeout_ns", ctypes.c_int, [c_vp, ctypes.c_uint64]),
+    ("tessa_set_leaf_kernel", ctypes.c_int, [c_vp, ctypes.c_uint32]),
     ("tessa_check_bounded_wait", ctypes.c_int, [c_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64), c_vp]),
     ("tessa_reducer_create", ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(c_vp)]),
     ("tessa_reducer_add", ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_uint64, ctypes.c_uint32]),

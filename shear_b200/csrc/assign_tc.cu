@@ -220,6 +220,19 @@ __device__ __forceinline__ void insertn(float d, uint32_t point, uint32_t leader
     }
 }
 
+// Out-of-line insertions for the candidates that pass the reject test below
+// (a small share of them): keeping the tie-aware insertion out of the
+// unrolled leader loop keeps that loop short enough for the instruction cache.
+__device__ __noinline__ Top4 insertn_slow(Top4 t, float d, uint32_t point, uint32_t leader, uint32_t slot,
+                                          uint32_t n) {
+  insertn(d, point, leader, slot, n, t.d, t.s, t.l);
+  return t;
+}
+__device__ __noinline__ Top4 insert4_slow(Top4 t, float d, uint32_t point, uint32_t leader, uint32_t slot) {
+  insert4(d, point, leader, slot, t.d, t.s, t.l);
+  return t;
+}
+
 __device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
                : "memory");
@@ -467,6 +480,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p
         bs[j] = 0xffffffffu;
         bl[j] = 0xffffffffu;
       }
+      // Reject bound: a candidate more than the 2e-5 tie window above it is
+      // neither better than nor tied with any slot the insertion would compare
+      // it to (CB:6524-6578), so it cannot enter.  Slot mode compares with its
+      // last slot first; the four-slot list with every slot (the maximum).
+      float worst = 3.402823466e+38F;
 #pragma unroll 1
       for (uint32_t c0 = 0; c0 < NB; c0 += 16) {
         uint32_t v[16];
@@ -482,11 +500,26 @@ __global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p
             const float df = __int2float_rn((int)v[j]);
             float d = p.fused ? __fmaf_rn(-tt, df, nn) : __fsub_rn(nn, __fmul_rn(tt, df));
             if (d <= 0.0f) d = 0.0f;
-            if (lid != 0xffffffffu) {
+            if (lid != 0xffffffffu && !(__fsub_rn(d, worst) > 2.0e-5f)) {
+              Top4 t;
+#pragma unroll
+              for (int k2 = 0; k2 < 4; ++k2) {
+                t.d[k2] = bd[k2];
+                t.s[k2] = bs[k2];
+                t.l[k2] = bl[k2];
+              }
               if constexpr (SLOTS)
-                insertn(d, point, lid, l, rh, bd, bs, bl);
+                t = insertn_slow(t, d, point, lid, l, rh);
               else
-                insert4(d, point, lid, l, bd, bs, bl);
+                t = insert4_slow(t, d, point, lid, l);
+              worst = SLOTS ? t.d[0] : fmaxf(fmaxf(t.d[0], t.d[1]), fmaxf(t.d[2], t.d[3]));
+#pragma unroll
+              for (int k2 = 0; k2 < 4; ++k2) {
+                bd[k2] = t.d[k2];
+                bs[k2] = t.s[k2];
+                bl[k2] = t.l[k2];
+                if (SLOTS && (uint32_t)k2 + 1u == rh) worst = t.d[k2];
+              }
             }
           }
         }

@@ -102,7 +102,8 @@ struct LeafPlan {
   std::vector<uint64_t> sizes;
   uint64_t leaf_rows = 0;
   uint32_t num_tiles = 0;
-  DevBuf d_starts, d_sizes, d_tiles;
+  uint32_t num_pairs = 0;  // 256-row tile pairs for the two-CTA leaf kernel
+  DevBuf d_starts, d_sizes, d_tiles, d_pairs;
   bool valid = false;
 
   int build(const uint64_t* h_starts, const uint64_t* h_sizes, uint64_t leaf_count, uint64_t rows, cudaStream_t st) {
@@ -112,7 +113,7 @@ struct LeafPlan {
       return TESSA_OK;
     valid = false;
     std::vector<uint32_t> sz32(leaf_count);
-    std::vector<uint2> tiles;
+    std::vector<uint2> tiles, pairs;
     for (uint64_t l = 0; l < leaf_count; ++l) {
       if (h_sizes[l] > 0x7fffffffull || h_starts[l] > rows || h_sizes[l] > rows - h_starts[l])
         return fail(TESSA_ERR_INVALID_ARG, "leaf %llu [start %llu, size %llu] outside %llu member rows",
@@ -125,22 +126,27 @@ struct LeafPlan {
                     (unsigned long long)h_sizes[l], (unsigned long long)kMaxLeafRows);
       sz32[l] = (uint32_t)h_sizes[l];
       for (uint64_t r0 = 0; r0 < h_sizes[l]; r0 += 128) tiles.push_back(make_uint2((uint32_t)l, (uint32_t)r0));
+      for (uint64_t r0 = 0; r0 < h_sizes[l]; r0 += 256) pairs.push_back(make_uint2((uint32_t)l, (uint32_t)r0));
     }
     if (tiles.size() > 0xffffffffull) return fail(TESSA_ERR_UNSUPPORTED, "too many leaf tiles");
     TRY(d_starts.ensure(leaf_count * 8 + 8));
     TRY(d_sizes.ensure(leaf_count * 4 + 4));
     TRY(d_tiles.ensure(tiles.size() * 8 + 8));
+    TRY(d_pairs.ensure(pairs.size() * 8 + 8));
     if (leaf_count) {
       CUDA_TRY(cudaMemcpyAsync(d_starts.ptr, h_starts, leaf_count * 8, cudaMemcpyHostToDevice, st));
       CUDA_TRY(cudaMemcpyAsync(d_sizes.ptr, sz32.data(), leaf_count * 4, cudaMemcpyHostToDevice, st));
     }
     if (!tiles.empty())
       CUDA_TRY(cudaMemcpyAsync(d_tiles.ptr, tiles.data(), tiles.size() * 8, cudaMemcpyHostToDevice, st));
+    if (!pairs.empty())
+      CUDA_TRY(cudaMemcpyAsync(d_pairs.ptr, pairs.data(), pairs.size() * 8, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaStreamSynchronize(st));
     starts.assign(h_starts, h_starts + leaf_count);
     sizes.assign(h_sizes, h_sizes + leaf_count);
     leaf_rows = rows;
     num_tiles = (uint32_t)tiles.size();
+    num_pairs = (uint32_t)pairs.size();
     valid = true;
     return TESSA_OK;
   }
@@ -148,6 +154,7 @@ struct LeafPlan {
     d_starts.release();
     d_sizes.release();
     d_tiles.release();
+    d_pairs.release();
     valid = false;
   }
 };
@@ -276,6 +283,7 @@ struct tessa_ctx {
   DevBuf g_temp;                    // record grouping: sort and scan scratch
   DevBuf probe;                     // bounded-wait probe: elapsed time
   SubmitRing* ring = nullptr;       // subtree submissions (created on first use)
+  uint32_t leaf_kernel = 1;         // 0: column-split kernel on CTA pairs where it applies, 1: one CTA per tile
 };
 
 namespace {
@@ -376,6 +384,10 @@ int leaf_launch_tiles(tessa_ctx* ctx, const tessa_leaf_args* a, const int8_t* lc
   L.d_leaf_sizes = ctx->leaf_plan.d_sizes.as<uint32_t>();
   L.d_tiles = ctx->leaf_plan.d_tiles.as<uint2>() + tile0;
   L.num_tiles = ntiles;
+  if (ctx->leaf_kernel == 0 && tile0 == 0 && ntiles == ctx->leaf_plan.num_tiles && L.d_dump) {
+    L.d_pairs = ctx->leaf_plan.d_pairs.as<uint2>();
+    L.num_pairs = ctx->leaf_plan.num_pairs;
+  }
   L.k = a->k;
   L.out_ids = a->topk_ids;
   L.out_dists = a->topk_dists;
@@ -1657,6 +1669,13 @@ __global__ void wait_probe_kernel(uint32_t* err_word, uint64_t timeout_ns, unsig
 }
 
 }  // namespace
+
+int tessa_set_leaf_kernel(tessa_ctx* ctx, uint32_t mode) {
+  if (!ctx) return fail(TESSA_ERR_INVALID_ARG, "null context");
+  if (mode > 1) return fail(TESSA_ERR_INVALID_ARG, "leaf kernel mode %u outside 0..1", mode);
+  ctx->leaf_kernel = mode;
+  return TESSA_OK;
+}
 
 int tessa_set_wait_timeout_ns(tessa_ctx* ctx, uint64_t timeout_ns) {
   if (!ctx) return fail(TESSA_ERR_INVALID_ARG, "null context");

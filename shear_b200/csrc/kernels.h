@@ -36,6 +36,10 @@ struct LeafLaunch {
   void* d_dump = nullptr;
   uint64_t dump_row0 = 0;
   uint64_t dump_rows = 0;
+  // Column-split kernel on CTA pairs (two SMs share each B chunk): 256-row
+  // tile pairs (leaf, first row); null or zero: one CTA per tile.
+  const uint2* d_pairs = nullptr;
+  uint32_t num_pairs = 0;
 };
 
 // Column-split leaf kernel: shared-memory plan (false: not supported for this

@@ -31,6 +31,8 @@ struct Params {
   const uint32_t* leaf_sizes;
   const uint2* tiles;           // (leaf, first row of tile)
   uint32_t num_tiles;
+  const uint2* pairs;           // column-split kernel on CTA pairs: (leaf, first row of a 256-row pair)
+  uint32_t num_pairs;
   uint32_t num_slabs;
   uint32_t num_bstages;
   uint32_t k;

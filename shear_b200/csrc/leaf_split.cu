@@ -135,6 +135,22 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t ring, uint32_t log_
   return s;
 }
 
+// The work unit of a CTA: a 128-row tile, or in a pair (PAIR) this CTA's
+// half of a 256-row tile pair (rows first + 128 * rank of the pair's leaf).
+template <bool PAIR>
+__device__ __forceinline__ void unit_span(const Params& p, uint32_t unit, uint32_t rank, uint2& t, uint64_t& start,
+                                          uint32_t& rows, uint32_t& cols) {
+  if constexpr (PAIR) {
+    t = p.pairs[unit];
+    t.y += rank * kBM;
+    start = p.leaf_starts[t.x];
+    rows = p.leaf_sizes[t.x];
+    cols = rows;
+  } else {
+    tile_span<false>(p, unit, t, start, rows, cols);
+  }
+}
+
 // Both warps of a lane quadrant meet; false if the wait timed out or the CTA
 // aborted.  `phase` counts the meetings of this pair.
 __device__ __forceinline__ bool pair_meet(uint64_t* bar, uint32_t& phase, uint32_t lane,
@@ -156,9 +172,18 @@ __device__ __forceinline__ bool pair_meet(uint64_t* bar, uint32_t& phase, uint32
 // stage: a warp can arrive on a stage's barrier again only after the stage
 // was released and refilled).  Then arrive on a_tm_full.  False on a timed
 // out or aborted wait.
+//
+// In a pair the stage is released in both CTAs at once, when both have read
+// their A slab: the second CTA's first warp forwards its read barrier to the
+// first CTA's (which counts one more arrival), and the first CTA releases
+// the stage in both.  A CTA's next B half of that stage completes on the
+// first CTA's full barrier, so it may be issued only after that barrier's
+// A phase has completed, which this ordering guarantees.
+template <bool PAIR>
 __device__ __forceinline__ bool load_a_tile(const Smem& s, const Params& p, uint32_t rpos, uint32_t ew,
                                             uint32_t half, uint32_t row_in_tile, uint32_t lane, uint32_t lane_base,
-                                            uint32_t tmem_base, uint32_t& arp, volatile uint32_t* abort_flag) {
+                                            uint32_t tmem_base, uint32_t& arp, uint32_t rank,
+                                            volatile uint32_t* abort_flag) {
   const uint32_t nst = p.num_bstages;
   for (uint32_t sl = 0; sl < p.num_slabs; ++sl) {
     const uint32_t it = rpos + sl, st = it % nst, ph = (it / nst) & 1u;
@@ -186,8 +211,18 @@ __device__ __forceinline__ bool load_a_tile(const Smem& s, const Params& p, uint
     if (ew == 0) {
       bool rd = true;
       if (lane == 0) {
-        rd = mbar_wait(&s.a_rd[st], (arp >> st) & 1u, abort_flag, p.err_word, p.timeout_ns);
-        if (rd) mbar_arrive(&s.b_empty[st]);
+        if constexpr (PAIR) {
+          rd = mbar_wait_cluster(&s.a_rd[st], (arp >> st) & 1u, abort_flag, p.err_word, p.timeout_ns);
+          if (rd && rank != 0u) {
+            mbar_arrive_cluster(mapa_shared(&s.a_rd[st], 0));
+          } else if (rd) {
+            mbar_arrive(&s.b_empty[st]);
+            mbar_arrive_cluster(mapa_shared(&s.b_empty[st], 1));
+          }
+        } else {
+          rd = mbar_wait(&s.a_rd[st], (arp >> st) & 1u, abort_flag, p.err_word, p.timeout_ns);
+          if (rd) mbar_arrive(&s.b_empty[st]);
+        }
       }
       arp ^= 1u << st;  // completed phases of each stage's read barrier, mod 2
       if (__shfl_sync(0xffffffffu, rd ? 1u : 0u, 0) == 0u) return false;
@@ -196,19 +231,31 @@ __device__ __forceinline__ bool load_a_tile(const Smem& s, const Params& p, uint
   tmem_st_wait();
   tc_fence_before();
   __syncwarp();
-  if (lane == 0) mbar_arrive(s.a_tm_full);
+  if (lane == 0) {
+    if constexpr (PAIR)
+      mbar_arrive_cluster(mapa_shared(s.a_tm_full, 0));  // the pair's MMAs wait for both halves of A
+    else
+      mbar_arrive(s.a_tm_full);
+  }
   return true;
 }
 
-template <int KS>
+template <int KS, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
-    leaf_topk_split_kernel(const __grid_constant__ CUtensorMap tmap, const Params p) {
+    leaf_topk_split_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_half,
+                           const Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem s = carve(smem_raw, p.num_bstages, p.log_cap);
   const uint32_t warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
   volatile uint32_t* abort_flag = s.abort_flag;
   const uint32_t nst = p.num_bstages;
+  // Work units: tiles, or tile pairs shared by the two CTAs of a cluster.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const uint32_t unit0 = PAIR ? (blockIdx.x >> 1) : blockIdx.x;
+  const uint32_t ustride = PAIR ? (gridDim.x >> 1) : gridDim.x;
+  const uint32_t num_units = PAIR ? p.num_pairs : p.num_tiles;
+  constexpr uint32_t kPeers = PAIR ? 2u : 1u;
 
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < nst; ++i) {
@@ -217,14 +264,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (uint32_t i = 0; i < kAccBufs; ++i) {
       mbar_init(&s.t_full[i], 1);
-      mbar_init(&s.t_empty[i], kEpiWarps);
+      mbar_init(&s.t_empty[i], kPeers * kEpiWarps);  // a pair: both CTAs' epilogue warps
     }
     for (uint32_t i = 0; i < kMetaSlots; ++i) {
       mbar_init(&s.m_full[i], 32);
       mbar_init(&s.m_empty[i], kEpiWarps);
     }
-    mbar_init(s.a_tm_full, kEpiWarps);
-    for (uint32_t i = 0; i < nst; ++i) mbar_init(&s.a_rd[i], kEpiWarps);
+    mbar_init(s.a_tm_full, kPeers * kEpiWarps);
+    // a pair's first CTA also counts the second CTA's forwarded read
+    for (uint32_t i = 0; i < nst; ++i) mbar_init(&s.a_rd[i], kEpiWarps + (PAIR && rank == 0u ? 1u : 0u));
     for (uint32_t i = 0; i < 4; ++i) mbar_init(&s.pair[i], 2);
     mbar_init(s.mma_done, 1);
     *s.abort_flag = 0u;
@@ -232,13 +280,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
   }
   if (warp >= 2 && warp < 2 + kEpiWarps) s.pub[((warp - 2) >> 2) * kBM + (warp & 3u) * 32u + lane] = 0ull;
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap);
+    if (PAIR) tma_prefetch_desc(&tmap_half);
+  }
   if (warp == 1) {
-    tmem_alloc(s.tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(s.tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(s.tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any arrival on them
   tc_fence_after();
   const uint32_t tmem_base = *s.tmem_slot;
 
@@ -247,23 +304,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (uint32_t tile = unit0; tile < num_units && ok; tile += ustride) {
         uint2 t;
         uint64_t start;
         uint32_t cnt, ncol;
-        tile_span<false>(p, tile, t, start, cnt, ncol);
+        unit_span<PAIR>(p, tile, rank, t, start, cnt, ncol);
         const uint32_t nchunks = (ncol + kBN - 1) / kBN;
         // A slabs of the tile's rows, then B slabs chunk by chunk.
         for (uint32_t item = 0; item < p.num_slabs * (1u + nchunks) && ok; ++item) {
           const uint32_t sl = item % p.num_slabs;
           const uint32_t c = item / p.num_slabs;  // 0 = A, c >= 1: chunk c - 1
-          if (!mbar_wait(&s.b_empty[stage], phase ^ 1u, abort_flag, p.err_word, p.timeout_ns)) {
+          const bool freed = PAIR ? mbar_wait_cluster(&s.b_empty[stage], phase ^ 1u, abort_flag, p.err_word, p.timeout_ns)
+                                  : mbar_wait(&s.b_empty[stage], phase ^ 1u, abort_flag, p.err_word, p.timeout_ns);
+          if (!freed) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&s.b_full[stage], kStageBytes);
-          const int32_t y = c == 0 ? (int32_t)(start + t.y) : (int32_t)(start + (uint64_t)(c - 1) * kBN);
-          tma_load_2d(&tmap, s.ring + stage * kStageBytes, &s.b_full[stage], (int32_t)(sl * kSlab), y);
+          if (PAIR && c != 0) {
+            // B: this CTA's half of the chunk's columns; both halves complete
+            // on the first CTA's barrier, which expects the whole stage
+            const int32_t y = (int32_t)(start + (uint64_t)(c - 1) * kBN + rank * (kBN / 2u));
+            if (rank == 0) {
+              mbar_arrive_expect_tx(&s.b_full[stage], kStageBytes);
+              tma_load_2d(&tmap_half, s.ring + stage * kStageBytes, &s.b_full[stage], (int32_t)(sl * kSlab), y);
+            } else {
+              mbar_arrive(&s.b_full[stage]);  // keeps this CTA's phase count in step
+              tma_load_2d_pair(&tmap_half, s.ring + stage * kStageBytes, mapa_shared(&s.b_full[stage], 0),
+                               (int32_t)(sl * kSlab), y);
+            }
+          } else {
+            mbar_arrive_expect_tx(&s.b_full[stage], kStageBytes);
+            const int32_t y = c == 0 ? (int32_t)(start + t.y) : (int32_t)(start + (uint64_t)(c - 1) * kBN);
+            tma_load_2d(&tmap, s.ring + stage * kStageBytes, &s.b_full[stage], (int32_t)(sl * kSlab), y);
+          }
           if (++stage == nst) {
             stage = 0;
             phase ^= 1u;
@@ -273,16 +346,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_i8(kBM, kBN);
+    if (lane == 0 && PAIR && rank == 1) {
+      // The pair's MMAs are issued by the first CTA; this CTA's tensor memory
+      // and shared memory stay in use until they have all completed.
+      uint32_t dummy_abort = 0u;
+      mbar_wait_cluster(s.mma_done, 0u, &dummy_abort, p.err_word, p.timeout_ns);
+    } else if (lane == 0) {
+      const uint32_t idesc = idesc_i8(PAIR ? 2u * kBM : kBM, kBN);
       const uint32_t ring_base = smem_u32(s.ring);
       uint32_t stage = 0, phase = 0, acc = 0, a_iter = 0;
       bool ok = true;
-      for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++a_iter) {
+      // barriers the pair's MMAs signal in both CTAs (the peer's through its cluster address)
+      auto commit_both = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          mma_commit_pair(mapa_shared(bar, 0));
+          mma_commit_pair(mapa_shared(bar, 1));
+        } else {
+          mma_commit(bar);
+        }
+      };
+      auto wait_peers = [&](uint64_t* bar, uint32_t par) {
+        return PAIR ? mbar_wait_cluster(bar, par, abort_flag, p.err_word, p.timeout_ns)
+                    : mbar_wait(bar, par, abort_flag, p.err_word, p.timeout_ns);
+      };
+      for (uint32_t tile = unit0; tile < num_units && ok; tile += ustride, ++a_iter) {
         uint2 t;
         uint64_t start;
         uint32_t cnt, ncol;
-        tile_span<false>(p, tile, t, start, cnt, ncol);
+        unit_span<PAIR>(p, tile, rank, t, start, cnt, ncol);
         const uint32_t nchunks = (ncol + kBN - 1) / kBN;
         // The A items of the ring belong to the epilogue warps.
         for (uint32_t sl = 0; sl < p.num_slabs; ++sl)
@@ -290,11 +381,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             stage = 0;
             phase ^= 1u;
           }
-        if (!mbar_wait(s.a_tm_full, a_iter & 1u, abort_flag, p.err_word, p.timeout_ns)) break;
+        if (!wait_peers(s.a_tm_full, a_iter & 1u)) break;
         tc_fence_after();
         for (uint32_t c = 0; c < nchunks && ok; ++c, ++acc) {
           const uint32_t buf = acc % kAccBufs, use = acc / kAccBufs;
-          if (!mbar_wait(&s.t_empty[buf], (use & 1u) ^ 1u, abort_flag, p.err_word, p.timeout_ns)) {
+          if (!wait_peers(&s.t_empty[buf], (use & 1u) ^ 1u)) {
             ok = false;
             break;
           }
@@ -308,20 +399,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t b_addr = ring_base + stage * kStageBytes;
 #pragma unroll
-            for (uint32_t kk = 0; kk < kSlab / kMmaK; ++kk)
-              mma_i8_ts(tmem_d, tmem_base + sl * (kSlab / 4u) + kk * (kMmaK / 4u), smem_desc_sw128(b_addr + kk * kMmaK),
-                        idesc, (sl | kk) != 0u ? 1u : 0u);
-            mma_commit(&s.b_empty[stage]);
+            for (uint32_t kk = 0; kk < kSlab / kMmaK; ++kk) {
+              if constexpr (PAIR)
+                mma_i8_ts_pair(tmem_d, tmem_base + sl * (kSlab / 4u) + kk * (kMmaK / 4u),
+                               smem_desc_sw128(b_addr + kk * kMmaK), idesc, (sl | kk) != 0u ? 1u : 0u);
+              else
+                mma_i8_ts(tmem_d, tmem_base + sl * (kSlab / 4u) + kk * (kMmaK / 4u),
+                          smem_desc_sw128(b_addr + kk * kMmaK), idesc, (sl | kk) != 0u ? 1u : 0u);
+            }
+            commit_both(&s.b_empty[stage]);
             if (++stage == nst) {
               stage = 0;
               phase ^= 1u;
             }
           }
-          if (ok) mma_commit(&s.t_full[buf]);
+          if (ok) commit_both(&s.t_full[buf]);
         }
       }
-      // Every issued MMA must have landed before TMEM is released.
-      mma_commit(s.mma_done);
+      // Every issued MMA must have landed before TMEM is released (in both
+      // CTAs of a pair).
+      commit_both(s.mma_done);
       uint32_t dummy_abort = 0u;
       mbar_wait(s.mma_done, 0u, &dummy_abort, p.err_word, p.timeout_ns);
     }
@@ -329,11 +426,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ column metadata
     uint32_t seq = 0;
     bool ok = true;
-    for (uint32_t tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (uint32_t tile = unit0; tile < num_units && ok; tile += ustride) {
       uint2 t;
       uint64_t start;
       uint32_t cnt, ncol;
-      tile_span<false>(p, tile, t, start, cnt, ncol);
+      unit_span<PAIR>(p, tile, rank, t, start, cnt, ncol);
       const uint32_t nchunks = (ncol + kBN - 1) / kBN;
       for (uint32_t c = 0; c < nchunks; ++c, ++seq) {
         const uint32_t slot = seq % kMetaSlots, use = seq / kMetaSlots;
@@ -392,20 +489,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t jk = k - (k >> 1);      // ceil(k/2) <= KH
     uint32_t acc = 0, seq = 0, rpos = 0, tseq = 0, pair_phase = 0, arp = 0;
     bool stop = false;
-    uint32_t tile = blockIdx.x;
-    if (tile < p.num_tiles) {
+    uint32_t tile = unit0;
+    if (tile < num_units) {
       uint2 t;
       uint64_t start;
       uint32_t cnt, ncol;
-      tile_span<false>(p, tile, t, start, cnt, ncol);
-      stop = !load_a_tile(s, p, rpos, ew, half, row_in_tile, lane, lane_base, tmem_base, arp, abort_flag);
+      unit_span<PAIR>(p, tile, rank, t, start, cnt, ncol);
+      stop = !load_a_tile<PAIR>(s, p, rpos, ew, half, row_in_tile, lane, lane_base, tmem_base, arp, rank, abort_flag);
       rpos += p.num_slabs * (1u + (ncol + kBN - 1) / kBN);
     }
-    for (; tile < p.num_tiles && !stop; tile += gridDim.x, ++tseq) {
+    for (; tile < num_units && !stop; tile += ustride, ++tseq) {
       uint2 t;
       uint64_t start;
       uint32_t cnt, ncol;
-      tile_span<false>(p, tile, t, start, cnt, ncol);
+      unit_span<PAIR>(p, tile, rank, t, start, cnt, ncol);
       const uint32_t nchunks = (ncol + kBN - 1) / kBN;
       const uint32_t row = t.y + row_in_tile;
       bool valid = row < cnt;
@@ -442,7 +539,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         if (lane == 0) {
           ok = mbar_wait(&s.m_full[mslot], (seq / kMetaSlots) & 1u, abort_flag, p.err_word, p.timeout_ns) &&
-               mbar_wait(&s.t_full[buf], use & 1u, abort_flag, p.err_word, p.timeout_ns);
+               (PAIR ? mbar_wait_cluster(&s.t_full[buf], use & 1u, abort_flag, p.err_word, p.timeout_ns)
+                     : mbar_wait(&s.t_full[buf], use & 1u, abort_flag, p.err_word, p.timeout_ns));
         }
         if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0u) {
           stop = true;
@@ -592,7 +690,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&s.t_empty[buf]);
+          if constexpr (PAIR)
+            mbar_arrive_cluster(mapa_shared(&s.t_empty[buf], 0));  // the pair's MMA issuer
+          else
+            mbar_arrive(&s.t_empty[buf]);
           mbar_arrive(&s.m_empty[mslot]);
         }
       }
@@ -600,13 +701,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- the next tile's A first: the MMA starts on it while this tile's
       // rows are wrapped up (all MMAs of this tile have completed).
-      const uint32_t next = tile + gridDim.x;
-      if (next < p.num_tiles) {
+      const uint32_t next = tile + ustride;
+      if (next < num_units) {
         uint2 tn;
         uint64_t sn;
         uint32_t cn, nn;
-        tile_span<false>(p, next, tn, sn, cn, nn);
-        if (!load_a_tile(s, p, rpos, ew, half, row_in_tile, lane, lane_base, tmem_base, arp, abort_flag)) {
+        unit_span<PAIR>(p, next, rank, tn, sn, cn, nn);
+        if (!load_a_tile<PAIR>(s, p, rpos, ew, half, row_in_tile, lane, lane_base, tmem_base, arp, rank, abort_flag)) {
           stop = true;
           break;
         }
@@ -692,9 +793,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // neither CTA leaves while the peer may still use its memory
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -969,19 +1074,47 @@ uint64_t leaf_dump_bytes(uint64_t rows, uint32_t k) {
 }
 
 template <int KS>
-static int launch_split_main(const CUtensorMap& tm, const leaf::Params& prm, uint32_t smem, uint32_t grid,
-                             cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(leaf::split::leaf_topk_split_kernel<KS>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return TESSA_ERR_CUDA;
-  leaf::split::leaf_topk_split_kernel<KS><<<grid, leaf::split::kThreads, smem, stream>>>(tm, prm);
-  return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+static int launch_split_main(const CUtensorMap& tm, const CUtensorMap& th, const leaf::Params& prm, uint32_t smem,
+                             int sm_count, bool pair, cudaStream_t stream) {
+  if (!pair) {
+    cudaError_t e = cudaFuncSetAttribute(leaf::split::leaf_topk_split_kernel<KS, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return TESSA_ERR_CUDA;
+    const uint32_t grid = prm.num_tiles < (uint32_t)sm_count ? prm.num_tiles : (uint32_t)sm_count;
+    leaf::split::leaf_topk_split_kernel<KS, false><<<grid, leaf::split::kThreads, smem, stream>>>(tm, th, prm);
+    return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
+  }
+  // CTA pairs: clusters of two, one pair of CTAs per SM pair
+  auto kern = leaf::split::leaf_topk_split_kernel<KS, true>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return TESSA_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(leaf::split::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int max_clusters = 0;
+  cfg.gridDim = dim3((unsigned)(2 * (sm_count / 2)), 1, 1);
+  if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters < 1) {
+    cudaGetLastError();
+    return TESSA_ERR_UNSUPPORTED;
+  }
+  const uint32_t clusters = prm.num_pairs < (uint32_t)max_clusters ? prm.num_pairs : (uint32_t)max_clusters;
+  cfg.gridDim = dim3(2u * clusters, 1, 1);
+  if (cudaLaunchKernelEx(&cfg, kern, tm, th, prm) != cudaSuccess) return TESSA_ERR_CUDA;
+  return TESSA_OK;
 }
 
 // Column-split main kernel, finishing kernel (the exact fallback follows in
 // the caller).  prm must carry the dump buffers; fb_count is cleared here.
-int launch_leaf_split(const CUtensorMap& tm, leaf::Params& prm, uint32_t padded_dim, int sm_count,
-                      cudaStream_t stream) {
+int launch_leaf_split(const CUtensorMap& tm, const CUtensorMap& th, leaf::Params& prm, uint32_t padded_dim,
+                      int sm_count, bool pair, cudaStream_t stream) {
   uint32_t ring = 0, log_cap = 0;
   if (!leaf_split_plan(padded_dim, prm.k, &ring, &log_cap)) return TESSA_ERR_UNSUPPORTED;
   prm.num_slabs = (padded_dim + leaf::kSlab - 1) / leaf::kSlab;
@@ -989,18 +1122,32 @@ int launch_leaf_split(const CUtensorMap& tm, leaf::Params& prm, uint32_t padded_
   prm.log_cap = log_cap;
   prm.dump_d = leaf_dump_entries(prm.k);
   const uint32_t smem = leaf::split::smem_bytes(ring, log_cap);
-  const uint32_t grid = prm.num_tiles < (uint32_t)sm_count ? prm.num_tiles : (uint32_t)sm_count;
+  pair = pair && prm.pairs && prm.num_pairs;
   int rc;
   if (prm.k <= 2)
-    rc = launch_split_main<2>(tm, prm, smem, grid, stream);
+    rc = launch_split_main<2>(tm, th, prm, smem, sm_count, pair, stream);
   else if (prm.k <= 4)
-    rc = launch_split_main<4>(tm, prm, smem, grid, stream);
+    rc = launch_split_main<4>(tm, th, prm, smem, sm_count, pair, stream);
   else if (prm.k <= 8)
-    rc = launch_split_main<8>(tm, prm, smem, grid, stream);
+    rc = launch_split_main<8>(tm, th, prm, smem, sm_count, pair, stream);
   else if (prm.k <= 16)
-    rc = launch_split_main<16>(tm, prm, smem, grid, stream);
+    rc = launch_split_main<16>(tm, th, prm, smem, sm_count, pair, stream);
   else
-    rc = launch_split_main<32>(tm, prm, smem, grid, stream);
+    rc = launch_split_main<32>(tm, th, prm, smem, sm_count, pair, stream);
+  if (rc == TESSA_ERR_UNSUPPORTED && pair) {
+    // no cluster of two could be placed: one CTA per tile
+    pair = false;
+    if (prm.k <= 2)
+      rc = launch_split_main<2>(tm, th, prm, smem, sm_count, false, stream);
+    else if (prm.k <= 4)
+      rc = launch_split_main<4>(tm, th, prm, smem, sm_count, false, stream);
+    else if (prm.k <= 8)
+      rc = launch_split_main<8>(tm, th, prm, smem, sm_count, false, stream);
+    else if (prm.k <= 16)
+      rc = launch_split_main<16>(tm, th, prm, smem, sm_count, false, stream);
+    else
+      rc = launch_split_main<32>(tm, th, prm, smem, sm_count, false, stream);
+  }
   if (rc != TESSA_OK) return rc;
   const uint32_t fin_smem = prm.dump_d * leaf::split::kFinThreads * 9u;
   const uint32_t fin_grid = prm.num_tiles < (uint32_t)sm_count * 8u ? prm.num_tiles : (uint32_t)sm_count * 8u;

@@ -862,8 +862,8 @@ static int launch_fallback(const leaf::Params& prm, const int8_t* a_codes, uint3
   return cudaGetLastError() == cudaSuccess ? TESSA_OK : TESSA_ERR_CUDA;
 }
 
-int launch_leaf_split(const CUtensorMap& tm, leaf::Params& prm, uint32_t padded_dim, int sm_count,
-                      cudaStream_t stream);
+int launch_leaf_split(const CUtensorMap& tm, const CUtensorMap& th, leaf::Params& prm, uint32_t padded_dim,
+                      int sm_count, bool pair, cudaStream_t stream);
 
 // Main kernel (k-specialised) plus the exact fallback over the rows it lists.
 template <bool RECT>
@@ -928,7 +928,13 @@ int launch_leaf_topk_sq8(const LeafLaunch& L, cudaStream_t stream) {
     prm.dump_m = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(L.d_dump) + leaf_dump_m_offset(L.dump_rows, L.k));
     prm.dump_cnt = reinterpret_cast<uint8_t*>(prm.dump_m + 8u * L.dump_rows);
     if (cudaMemsetAsync(prm.fb_count, 0, 4, stream) != cudaSuccess) return TESSA_ERR_CUDA;
-    int rc = launch_leaf_split(ta, prm, L.padded_dim, L.sm_count, stream);
+    const bool pair = L.d_pairs && L.num_pairs;
+    CUtensorMap th = tb;  // B halves of a chunk for CTA pairs
+    if (pair && make_code_tmap(&th, L.leaf_codes, L.leaf_rows, L.padded_dim, leaf::kBN / 2) != 0)
+      return TESSA_ERR_CUDA;
+    prm.pairs = L.d_pairs;
+    prm.num_pairs = L.num_pairs;
+    int rc = launch_leaf_split(ta, th, prm, L.padded_dim, L.sm_count, pair, stream);
     if (rc != TESSA_OK) return rc;
     return launch_fallback<false>(prm, L.leaf_codes, L.padded_dim, L.sm_count, stream);
   }

@@ -200,6 +200,12 @@ def set_host_batch_bytes(batch_bytes: int, ctx: Context | None = None, device: i
     C.check(C.load().tessa_set_host_batch_bytes(ctx.handle, int(batch_bytes)))
 
 
+def set_leaf_kernel(mode: int, ctx: Context | None = None, device: int = 0) -> None:
+    """tessa_set_leaf_kernel: 0 = column-split kernel on CTA pairs (default), 1 = one CTA per tile."""
+    ctx = ctx or context(device)
+    C.check(C.load().tessa_set_leaf_kernel(ctx.handle, int(mode)))
+
+
 def leaf_last_fallback_rows(ctx: Context | None = None, device: int = 0) -> int:
     """Rows of the last leaf call on `ctx` recomputed by the exact sequential fallback."""
     ctx = ctx or context(device)

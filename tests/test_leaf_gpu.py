@@ -232,3 +232,24 @@ def test_leaf_rejects_bad_arguments(oracle):
     big = make_leaf_batch(oracle, [4], 2048, seed=1)
     with pytest.raises(TessaError, match="UNSUPPORTED"):
         _device_run(big, 2)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("sizes,dim,k,seed", [
+    ([300, 129, 1000, 257], 768, 2, 1),      # odd tile counts: the last pair's second CTA holds no rows
+    ([2048, 700, 100, 1500], 768, 32, 2),
+    ([513, 255, 1], 128, 8, 3),
+    ([900, 900, 900], 1024, 16, 4),
+])
+def test_leaf_pair_and_single_cta_kernels_match_oracle(oracle, mode, sizes, dim, k, seed):
+    # mode 0: the column-split kernel on CTA pairs (tcgen05 cta_group::2, each
+    # CTA loading half of every B chunk); mode 1: one CTA per 128-row tile.
+    from shear_b200 import ops
+    c = make_leaf_batch(oracle, sizes, dim, seed=seed, dup=True, permute=True)
+    want = oracle_leaf(oracle, c, k)
+    ops.set_leaf_kernel(mode)
+    try:
+        _assert_same(_device_run(c, k), want)
+        _assert_same(_device_run(c, k, leaf_ordered=True), want)
+    finally:
+        ops.set_leaf_kernel(1)
