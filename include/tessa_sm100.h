@@ -173,13 +173,15 @@ TESSA_API int tessa_set_host_batch_bytes(tessa_ctx* ctx, uint64_t bytes);
  * counterpart of the reference's leaf_exact_fallback_rows counter
  * (P/tessa_replay.rs:155-188; here it is a diagnostic, not an error). */
 TESSA_API int tessa_leaf_last_fallback_rows(const tessa_ctx* ctx, uint64_t* rows);
-/* Which form of the column-split leaf kernel a context uses: 0 (default) --
- * pairs of CTAs on neighbouring SMs (a cluster of two) share each chunk of B
- * columns, one 256-row MMA (tcgen05 cta_group::2) over two 128-row tiles of
- * the same leaf, each CTA loading half of the chunk; 1 -- one CTA per 128-row
- * tile loading the whole chunk.  Both give the same lists bit for bit; the
- * pair form needs whole-batch calls and falls back to the single form when
- * no cluster can be placed. */
+/* Which form of the column-split leaf kernel a context uses: 1 (default) --
+ * one CTA per 128-row tile loading every chunk of B columns; 0 -- pairs of
+ * CTAs on neighbouring SMs (a cluster of two) share each chunk, one 256-row
+ * MMA (tcgen05 cta_group::2) over two 128-row tiles of the same leaf, each
+ * CTA loading half of the chunk.  Both give the same lists bit for bit; the
+ * pair form halves the B traffic but runs its two CTAs in lock step, which
+ * measured slower on epilogue-bound leaves.  It needs whole-batch calls and
+ * falls back to the single form when no cluster can be placed.  Returns
+ * TESSA_ERR_INVALID_ARG for other modes. */
 TESSA_API int tessa_set_leaf_kernel(tessa_ctx* ctx, uint32_t mode);
 
 /* Size of the static device scratch of tessa_leaf_topk_sq8_noalloc (64 MiB). */

@@ -70,6 +70,12 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Sorted array (descending, s[0] = maximum) of the KS smallest values seen.
 // Inserting the pair x <= y keeps the KS smallest of s, x and y:
 //   new[t] = max(s[t+2], min(s[t+1], y), min(s[t], x))

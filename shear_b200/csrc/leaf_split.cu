@@ -553,6 +553,88 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem_base + lane_base + kAccCol + buf * kBN + g * kGroup, v);
           tmem_ld_wait();
+          if (KS == 2 && !(c == c_self && g == quad)) {
+            // k <= 2 (one sorted slot per half), every group but the one
+            // holding the row itself: the group's smallest distance enters
+            // the half's slot before any column is tested, the halves
+            // exchange their slots (meeting for a tile's first groups), and
+            // every column below the tightened bound is logged.  No
+            // per-candidate insertion: the log keeps whatever lies below the
+            // bound, and the bound max(own smallest, other smallest) + margin
+            // is still at or above the row's k-th smallest + margin.
+            const uint32_t* gq = mg + g * kGroup;
+            float dc[32];
+#pragma unroll
+            for (uint32_t cc = 0; cc < kGroup; cc += 2) {
+              const float4 m = msn[(g * kGroup + cc) >> 1];  // s_c, s_c+1, n_c, n_c+1
+              const uint64_t t = f2_mul(si2, f2_pack(m.x, m.y));
+              const uint64_t u = f2_mul(t, f2_pack(__int2float_rn((int)v[cc]), __int2float_rn((int)v[cc + 1])));
+              f2_unpack(f2_fma(m2x2, u, f2_add(ni2, f2_pack(m.z, m.w))), dc[cc], dc[cc + 1]);
+            }
+            float q[11];
+#pragma unroll
+            for (uint32_t i = 0; i < 10; ++i) q[i] = fmin3(dc[3 * i], dc[3 * i + 1], dc[3 * i + 2]);
+            q[10] = fminf(dc[30], dc[31]);
+            const float gm = fmin3(fmin3(q[0], q[1], q[2]), fmin3(q[3], q[4], q[5]),
+                                   fmin3(q[6], q[7], fmin3(q[8], q[9], q[10])));
+            if (valid) sk[0] = fminf(sk[0], gm > 0.0f ? gm : 0.0f);  // reference clamp d <= 0 -> +0 (CB:8999-9001)
+            *my_pub = tag | __float_as_uint(sk[0]);
+            if (c * 2u + gg < kMeetGroups) {
+              __threadfence_block();
+              if (!pair_meet(&s.pair[quad], pair_phase, lane, abort_flag, p)) {
+                stop = true;
+                break;
+              }
+            }
+            const uint64_t o = *other_pub;
+            if ((o & 0xffffffff00000000ull) == tag) ob = fminf(ob, __uint_as_float((uint32_t)o));
+            if (valid) thr = __fadd_rn(fmaxf(sk[0], ob), kMargin);
+            uint32_t mq[4] = {0u, 0u, 0u, 0u};
+            const uint64_t nthr2 = f2_pack(-thr, -thr);
+#pragma unroll
+            for (uint32_t cc = 0; cc < kGroup; cc += 2) {
+              float e0, e1;
+              f2_unpack(f2_add(f2_pack(dc[cc], dc[cc + 1]), nthr2), e0, e1);  // rn(d - thr)
+              uint32_t& w = mq[cc >> 3];
+              w = __funnelshift_l(__float_as_uint(e0), w, 1);
+              w = __funnelshift_l(__float_as_uint(e1), w, 1);
+            }
+            uint32_t mask = (mq[0] << 24) | (mq[1] << 16) | (mq[2] << 8) | mq[3];
+            const uint32_t steps = (__reduce_max_sync(0xffffffffu, __popc(mask)) + 1u) >> 1;
+            if (steps != 0u) {  // the pops read the distances back by column index
+              float4* st4 = reinterpret_cast<float4*>(stash);
+#pragma unroll
+              for (uint32_t q4 = 0; q4 < kGroup / 4; ++q4)
+                st4[q4] = make_float4(dc[4 * q4], dc[4 * q4 + 1], dc[4 * q4 + 2], dc[4 * q4 + 3]);
+            }
+            for (uint32_t it = 0; it < steps;) {
+              uint32_t room = (cap - nlog) >> 1;
+              if (__any_sync(0xffffffffu, room < steps - it)) {
+                nlog = log_compact(log, row_in_tile, nlog, thr);
+                room = (cap - nlog) >> 1;
+              }
+              uint32_t batch = min(steps - it, __reduce_min_sync(0xffffffffu, room));
+              batch = batch > 0u ? batch : 1u;
+              const uint32_t end = it + batch;
+#pragma unroll 1
+              for (; it < end; ++it) {
+                bool h0, h1;
+                uint32_t c0, c1;
+                next_pair(mask, h0, c0, h1, c1);
+                const float a0 = stash[c0], a1 = stash[c1];
+                const uint32_t g0 = gq[c0], g1 = gq[c1];
+                const bool w0 = h0 && nlog < cap;
+                const uint32_t e1 = nlog + (w0 ? 1u : 0u);
+                const bool w1 = h1 && e1 < cap;
+                if (w0) log[nlog * kBM + row_in_tile] = make_uint2(__float_as_uint(a0 > 0.0f ? a0 : 0.0f), g0);
+                if (w1) log[e1 * kBM + row_in_tile] = make_uint2(__float_as_uint(a1 > 0.0f ? a1 : 0.0f), g1);
+                nlog = e1 + (w1 ? 1u : 0u);
+                ovf |= (h0 && !w0) || (h1 && !w1);
+              }
+            }
+            __syncwarp();
+            continue;
+          }
           // Exact reference distances; bit (31 - cc) of mask = column cc is
           // below the bound (the sign of d - thr, shifted in), four chains.
           // Two columns per step on register pairs (paired f32 instructions,
