@@ -73,7 +73,7 @@ constexpr uint32_t kStashBytes = kEpiWarps * 32u * kStashStride * 4u;
 constexpr uint32_t kPubBytes = 2u * kBM * 8u;
 constexpr uint32_t kBarBytes = 512u;
 constexpr uint32_t kFinThreads = 128;
-constexpr uint32_t kMeetGroups = 8;  // groups per tile after which the two halves meet
+constexpr uint32_t kMeetGroups = 8;  // groups per tile after which the two halves meet (k > 2)
 
 static_assert(kBM == kBN, "A and B slabs share the ring and the tensor map");
 
@@ -485,6 +485,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile uint64_t* other_pub = s.pub + (half ^ 1u) * kBM + row_in_tile;
     const uint32_t cap = p.log_cap;
     const uint32_t k = p.k;
+    // Groups per tile after which the halves stop meeting: one for k <= 2
+    // (each group's smallest distance is in the bound before its columns are
+    // tested, so a stale value of the other half costs little).
+    const uint32_t meet_groups = KS == 2 ? 1u : kMeetGroups;
     constexpr int KH = KS / 2;             // slots of the per-half sorted array
     const uint32_t jk = k - (k >> 1);      // ceil(k/2) <= KH
     uint32_t acc = 0, seq = 0, rpos = 0, tseq = 0, pair_phase = 0, arp = 0;
@@ -579,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    fmin3(q[6], q[7], fmin3(q[8], q[9], q[10])));
             if (valid) sk[0] = fminf(sk[0], gm > 0.0f ? gm : 0.0f);  // reference clamp d <= 0 -> +0 (CB:8999-9001)
             *my_pub = tag | __float_as_uint(sk[0]);
-            if (c * 2u + gg < kMeetGroups) {
+            if (c * 2u + gg < meet_groups) {
               __threadfence_block();
               if (!pair_meet(&s.pair[quad], pair_phase, lane, abort_flag, p)) {
                 stop = true;
@@ -756,7 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // group while the bounds still fall fast (one a group older there
           // lets the logs overfill); later the other's latest value is used.
           *my_pub = tag | __float_as_uint(sk[0]);
-          if (c * 2u + gg < kMeetGroups) {
+          if (c * 2u + gg < meet_groups) {
             __threadfence_block();
             if (!pair_meet(&s.pair[quad], pair_phase, lane, abort_flag, p)) {
               stop = true;
