@@ -1312,7 +1312,7 @@ def run_build(a):
     torch.cuda.synchronize(dev)
     barrier()
     stream = torch.cuda.current_stream(dev)
-    times, leaf_ms = [], []
+    times, leaf_ms, step_phases = [], [], []
     with ClockSampler(dev.index) as clk:
         for _ in range(a.steps):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1324,6 +1324,7 @@ def run_build(a):
             torch.cuda.synchronize(dev)
             times.append(s.elapsed_time(e) / 1e3)
             leaf_ms.append(res.timings["leaf_kernel_ms"])
+            step_phases.append({k: round(v, 4) for k, v in res.timings.items() if k.startswith("partition")})
     barrier()
     if world > 1:  # each step's time is its slowest rank's
         import torch.distributed as dist
@@ -1429,6 +1430,8 @@ def run_build(a):
         "gpu_launches": res.stats["kernel_launches"] * a.steps,
         "clocks": clk.summary(),
         "phases_s": {k: round(v, 4) for k, v in res.timings.items()},
+        "step_ms": [round(t * 1e3, 2) for t in times],
+        "step_partition_s": step_phases,
         "build_stats": {k: v for k, v in res.stats.items() if k not in ("root_plan",)},
         "degree": res.degree_stats(),
     }

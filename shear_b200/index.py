@@ -232,19 +232,24 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, s
     side = None
     if sketches is None:
         main = torch.cuda.current_stream(dev)
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(main)
+        side, planes, buf = _sketch_resources(torch, dev, p, n, dim)
+        side.wait_stream(main)  # the previous build's readers of buf are done
         with torch.cuda.stream(side):
-            sketches = ops.sketch_rows(xd, sketch_planes(torch, dev, p, dim), ctx=ctx)
+            sketches = ops.sketch_rows(xd, planes, ctx=ctx, out=buf)
     sp = ops.SubtreeParams(c_max=p.adaptive_c_max(n), max_depth=p.max_depth, max_leaders=p.max_leaders,
                            fanout_second=p.fanout_second, root_depth=st["depth"], psamp_fraction=p.psamp_fraction)
     # (the partition can also copy the leaf-ordered codes round by round --
     # leaf_codes -- but on a side stream those copies slow the concurrent
     # assignment kernels by more than they save the leaf call)
+    t_call = time.perf_counter()
+    timings["partition_setup_s"] = t_call - t
     leaf_rows, starts, sizes, _, pst = ops.subtree_partition(d0.codes, d0.scales, d0.norms, st["members"],
                                                              st["offsets"][sel], st["counts"][sel],
                                                              st["seeds"][sel], sp, ctx=ctx)
+    t_sync = time.perf_counter()
+    timings["partition_call_s"] = t_sync - t_call
     torch.cuda.synchronize(dev)
+    timings["partition_sync_s"] = time.perf_counter() - t_sync
     timings["partition_s"] = time.perf_counter() - t
     t = time.perf_counter()
     rows = int(leaf_rows.numel())
@@ -257,7 +262,6 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, s
     ev[1].record()
     if side is not None:
         torch.cuda.current_stream(dev).wait_stream(side)
-        sketches.record_stream(torch.cuda.current_stream(dev))
     hf, hr = ops.edge_hashes(leaf_rows, ids, k, sketches, p.m_hash_bits, starts, sizes, ctx=ctx)
     torch.cuda.synchronize(dev)
     timings["leaf_s"] = time.perf_counter() - t
@@ -268,6 +272,26 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, s
 
 def sketch_planes(torch, dev, p: BuildParams, dim: int):
     return torch.from_numpy(hyperplanes(p.m_hash_bits, dim, p.random_seed)).to(dev)
+
+
+_SKETCH_RES: dict = {}  # device index -> (side stream, planes key, planes, buffer key, buffer)
+
+
+def _sketch_resources(torch, dev, p: BuildParams, n: int, dim: int):
+    """The side stream, hyperplanes and sketch buffer of a device's builds,
+    kept from build to build: a new stream, a pageable upload of the planes
+    and a fresh buffer per build cost a build up to 30 ms of host time."""
+    r = _SKETCH_RES.get(dev.index)
+    pkey, bkey = (p.m_hash_bits, dim, p.random_seed), (n, p.m_hash_bits)
+    if r is None:
+        r = [torch.cuda.Stream(dev), None, None, None, None]
+        _SKETCH_RES[dev.index] = r
+    if r[1] != pkey:
+        r[1], r[2] = pkey, sketch_planes(torch, dev, p, dim)
+    if r[3] != bkey:
+        r[3], r[4] = bkey, None
+        r[4] = torch.empty((n, p.m_hash_bits), dtype=torch.float32, device=dev)
+    return r[0], r[2], r[4]
 
 
 def group_stage(rec: dict, n: int, ctx):
