@@ -220,17 +220,15 @@ __device__ __forceinline__ void insertn(float d, uint32_t point, uint32_t leader
     }
 }
 
-// Out-of-line insertions for the candidates that pass the reject test below
-// (a small share of them): keeping the tie-aware insertion out of the
-// unrolled leader loop keeps that loop short enough for the instruction cache.
-__device__ __noinline__ Top4 insertn_slow(Top4 t, float d, uint32_t point, uint32_t leader, uint32_t slot,
-                                          uint32_t n) {
-  insertn(d, point, leader, slot, n, t.d, t.s, t.l);
-  return t;
-}
-__device__ __noinline__ Top4 insert4_slow(Top4 t, float d, uint32_t point, uint32_t leader, uint32_t slot) {
-  insert4(d, point, leader, slot, t.d, t.s, t.l);
-  return t;
+// d[j] for a run-time j < 16 (a four-level select tree).
+__device__ __forceinline__ float select16(const float (&d)[16], uint32_t j) {
+  float a8[8], b4[4];
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) a8[i] = (j & 1u) ? d[2 * i + 1] : d[2 * i];
+#pragma unroll
+  for (uint32_t i = 0; i < 4; ++i) b4[i] = (j & 2u) ? a8[2 * i + 1] : a8[2 * i];
+  const float c0 = (j & 4u) ? b4[1] : b4[0], c1 = (j & 4u) ? b4[3] : b4[2];
+  return (j & 8u) ? c1 : c0;
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
@@ -261,8 +259,9 @@ struct MetaSlot {
   float sp[kRowsTc];
   uint32_t lid[NB];      // leader row of each slot (0xffffffff: none)
   uint32_t lg[NB];
-  float ln[NB];
-  float ls[NB];
+  // per leader pair (2i, 2i + 1): norm, norm, scale, scale (one 16-byte load
+  // for two leaders); a missing leader has norm +inf, so its distance is +inf
+  float lnls[2 * NB];
   uint32_t task, rh, nl, r0;
   uint64_t tout;
   uint32_t pad[2];
@@ -331,7 +330,7 @@ __device__ __forceinline__ void prod_step(const Params& p, uint32_t item, uint32
       if (m.lrow[v] >= p.resident_rows) m.lrow[v] = kNone;
     m.np = m.pt != kNone ? p.sq8_norms[m.pt] : 0.f;
     m.sp = m.pt != kNone ? p.scales[m.pt] : 0.f;
-    m.ln = m.lid != kNone ? p.sq8_norms[m.lid] : 0.f;
+    m.ln = m.lid != kNone ? p.sq8_norms[m.lid] : INFINITY;
     m.ls = m.lid != kNone ? p.scales[m.lid] : 0.f;
     m.lg = (m.lid != kNone && !p.out_slots) ? p.global_ids[m.lid] : 0u;
     // slot mode: the insertion hashes subtree-local ids
@@ -413,8 +412,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p
       if (t < NB) {
         m.lid[t] = cur.lid;
         m.lg[t] = cur.lg;
-        m.ln[t] = cur.ln;
-        m.ls[t] = cur.ls;
+        m.lnls[(t >> 1) * 4u + (t & 1u)] = cur.ln;
+        m.lnls[(t >> 1) * 4u + 2u + (t & 1u)] = cur.ls;
       }
       if (t == 0) {
         m.task = cur.task;
@@ -484,42 +483,55 @@ __global__ void __launch_bounds__(kThreadsTc, 1) assign_tc_kernel(const Params p
       // neither better than nor tied with any slot the insertion would compare
       // it to (CB:6524-6578), so it cannot enter.  Slot mode compares with its
       // last slot first; the four-slot list with every slot (the maximum).
+      //
+      // Per 16 leaders: the distances two at a time on register pairs (paired
+      // f32 instructions round each element as the scalar form; -2 s_p l_s is
+      // exact negation of the reference's 2 s_p l_s), and a mask of the
+      // leaders not rejected against the bound at the block's start.  The
+      // bound only falls and clamping only raises a distance, so a leader
+      // outside the mask is rejected in the sequential order too; the masked
+      // ones are taken in ascending slot order and get the exact sequential
+      // test (clamped distance, current bound) before the insertion.
       float worst = 3.402823466e+38F;
+      const float nsp = -2.0f * s_p;
+      const uint64_t np2 = f2_pack(n_p, n_p), nsp2 = f2_pack(nsp, nsp);
+      const float4* lm4 = reinterpret_cast<const float4*>(m.lnls);
 #pragma unroll 1
       for (uint32_t c0 = 0; c0 < NB; c0 += 16) {
         uint32_t v[16];
         tmem_ld_32x32b_x16(tmem_base + ((q * 32u) << 16) + a * NB + c0, v);
         tmem_ld_wait();
         if (valid) {
+          float d[16];
+          uint32_t mask = 0u;
+          const uint64_t nw2 = f2_pack(-worst, -worst);
 #pragma unroll
-          for (uint32_t j = 0; j < 16; ++j) {
+          for (uint32_t j = 0; j < 16; j += 2) {
+            const float4 lm = lm4[(c0 + j) >> 1];  // ln_l, ln_l+1, ls_l, ls_l+1
+            const uint64_t nn = f2_add(np2, f2_pack(lm.x, lm.y));
+            const uint64_t ntt = f2_mul(nsp2, f2_pack(lm.z, lm.w));
+            const uint64_t df = f2_pack(__int2float_rn((int)v[j]), __int2float_rn((int)v[j + 1]));
+            const uint64_t dd = p.fused ? f2_fma(ntt, df, nn) : f2_add(nn, f2_mul(ntt, df));
+            f2_unpack(dd, d[j], d[j + 1]);
+            float r0, r1;
+            f2_unpack(f2_add(dd, nw2), r0, r1);  // rn(d - worst)
+            mask |= (!(r0 > 2.0e-5f) ? 1u : 0u) << j;
+            mask |= (!(r1 > 2.0e-5f) ? 1u : 0u) << (j + 1u);
+          }
+          while (mask != 0u) {
+            const uint32_t j = __ffs(mask) - 1u;
+            mask &= mask - 1u;
             const uint32_t l = c0 + j;
-            const uint32_t lid = l < nl ? m.lid[l] : 0xffffffffu;
-            const float nn = __fadd_rn(n_p, m.ln[l]);
-            const float tt = __fmul_rn(__fmul_rn(2.0f, s_p), m.ls[l]);
-            const float df = __int2float_rn((int)v[j]);
-            float d = p.fused ? __fmaf_rn(-tt, df, nn) : __fsub_rn(nn, __fmul_rn(tt, df));
-            if (d <= 0.0f) d = 0.0f;
-            if (lid != 0xffffffffu && !(__fsub_rn(d, worst) > 2.0e-5f)) {
-              Top4 t;
-#pragma unroll
-              for (int k2 = 0; k2 < 4; ++k2) {
-                t.d[k2] = bd[k2];
-                t.s[k2] = bs[k2];
-                t.l[k2] = bl[k2];
-              }
-              if constexpr (SLOTS)
-                t = insertn_slow(t, d, point, lid, l, rh);
-              else
-                t = insert4_slow(t, d, point, lid, l);
-              worst = SLOTS ? t.d[0] : fmaxf(fmaxf(t.d[0], t.d[1]), fmaxf(t.d[2], t.d[3]));
-#pragma unroll
-              for (int k2 = 0; k2 < 4; ++k2) {
-                bd[k2] = t.d[k2];
-                bs[k2] = t.s[k2];
-                bl[k2] = t.l[k2];
-                if (SLOTS && (uint32_t)k2 + 1u == rh) worst = t.d[k2];
-              }
+            float dj = select16(d, j);
+            if (dj <= 0.0f) dj = 0.0f;
+            const uint32_t lid = m.lid[l];
+            if (lid == 0xffffffffu || __fsub_rn(dj, worst) > 2.0e-5f) continue;
+            if constexpr (SLOTS) {
+              insertn(dj, point, lid, l, rh, bd, bs, bl);
+              worst = rh == 1u ? bd[0] : (rh == 2u ? bd[1] : (rh == 3u ? bd[2] : bd[3]));
+            } else {
+              insert4(dj, point, lid, l, bd, bs, bl);
+              worst = fmaxf(fmaxf(bd[0], bd[1]), fmaxf(bd[2], bd[3]));
             }
           }
         }
