@@ -60,7 +60,7 @@ def parse_args():
                     help="build = GPU-subtree index build, BASELINE config 3 (default) or 1 (--config 1); "
                          "leaf = the config-2 leaf-operator replay; d0 = global-D0 SQ8 staging; "
                          "edges = candidate-edge hashes + host expansion of the leaf lists")
-    ap.add_argument("--config", type=int, choices=[1, 3], default=3, help="build: BASELINE config")
+    ap.add_argument("--config", type=int, choices=[1, 3, 4], default=3, help="build: BASELINE config")
     ap.add_argument("--rows", type=int, default=0, help="build: base rows (0 = the config's)")
     ap.add_argument("--queries", type=int, default=0, help="build: recall queries (0 = the config's)")
     ap.add_argument("--cpu-rows", type=int, default=0, help="build: rows of the CPU-baseline sample (0 = auto)")
@@ -1197,6 +1197,11 @@ BUILD_CONFIGS = {
     # 1M x 768 L2-normalised, 1,024-component anisotropic GMM (diagonal
     # sigma ~ U[0.05, 0.5]), inner product on unit vectors = L2 order, degree 64, 10,000 queries
     3: dict(rows=1_000_000, dim=768, comps=1024, aniso=True, unit=True, sigma=None, queries=10_000, c_max=2048),
+    # 35M x 768, the config-3 family with 4,096 components, 1/2/4/8 GPUs; rows
+    # drawn per 2^18-row chunk from the chunk's own seed, so each rank draws only its row range and every
+    # GPU count builds the same dataset (107.5 GB of f32 rows in all)
+    4: dict(rows=35_000_000, dim=768, comps=4096, aniso=True, unit=True, sigma=None, queries=10_000, c_max=2048,
+            chunked=True),
 }
 
 
@@ -1255,6 +1260,32 @@ def make_mixture(torch, dev, n, c, seed, centre_seed=0):
     return x
 
 
+def make_mixture_range(torch, dev, c, seed, lo, hi, centre_seed=0):
+    """Rows [lo, hi) of the config's mixture drawn chunk by chunk: chunk i
+    (rows i * 2^18 ...) from its own generator (seed, i), so any row range
+    is drawn alone and equals the same rows of the whole set."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(centre_seed)
+    centres = torch.randn((c["comps"], c["dim"]), generator=g, device=dev)
+    sig = torch.rand((c["comps"], c["dim"]), generator=g, device=dev) * 0.45 + 0.05
+    x = torch.empty((hi - lo, c["dim"]), dtype=torch.float32, device=dev)
+    step = 1 << 18
+    for ci in range(lo // step, (hi + step - 1) // step):
+        r0, r1 = ci * step, min(c["rows"], (ci + 1) * step)
+        g2 = torch.Generator(device=dev)
+        g2.manual_seed(seed * 1_000_003 + ci)
+        comp = torch.randint(0, c["comps"], (r1 - r0,), generator=g2, device=dev)
+        noise = torch.randn((r1 - r0, c["dim"]), generator=g2, device=dev)
+        y = centres[comp] + sig[comp] * noise
+        y /= torch.linalg.vector_norm(y, dim=1, keepdim=True)
+        a, b = max(r0, lo), min(r1, hi)
+        if a < b:
+            x[a - lo:b - lo] = y[a - r0:b - r0]
+        del comp, noise, y
+    torch.cuda.synchronize(dev)
+    return x
+
+
 def build_recall(torch, x, res, queries, ls=(50, 100, 200)):
     from shear_b200 import graph as G
     gt, _ = G.exact_knn(x, queries, 10)
@@ -1292,10 +1323,14 @@ def run_build(a):
     p = BuildParams(c_max=c["c_max"], reducer_threads=max(1, (os.cpu_count() or 1) // world))
     # one dataset of the config's size, split over the ranks (strong scaling): every rank draws the same
     # mixture (outside the timed region) and keeps its row range
-    x = make_mixture(torch, dev, c["rows"], c, seed=1234)
     n = c["rows"]
     lo, hi, _ = row_range(n, world, rank)
-    xs = x[lo:hi].contiguous()
+    if c.get("chunked"):  # each rank draws its own range only; the whole set exists on one GPU alone
+        xs = make_mixture_range(torch, dev, c, 1234, lo, hi)
+        x = xs if world == 1 else None
+    else:
+        x = make_mixture(torch, dev, c["rows"], c, seed=1234)
+        xs = x[lo:hi].contiguous()
 
     def build(inp):
         if world == 1:
@@ -1373,7 +1408,7 @@ def run_build(a):
         return 0
 
     recall = None
-    if not a.no_recall:
+    if not a.no_recall and x is not None:
         q = make_mixture(torch, dev, c["queries"], c, seed=99991)
         recall = {"at": 10, "queries": c["queries"], "by_L": build_recall(torch, x, res, q),
                   "ground_truth": "exact f32 L2 top-10 on the GPU", "search": "greedy beam search restating "
@@ -1395,7 +1430,7 @@ def run_build(a):
 
     cpu = None
     parity = None
-    if not a.no_cpu_baseline and world == 1:
+    if not a.no_cpu_baseline and world == 1 and x is not None:
         from oracle.cpu_build import build_index_cpu
         O = host_oracle()
         m = a.cpu_rows or min(n, 30000 if c["dim"] > 256 else 100000)

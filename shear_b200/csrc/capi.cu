@@ -1453,15 +1453,15 @@ int tessa_subtree_partition(tessa_ctx* ctx, const tessa_subtree_args* a, tessa_s
   if (!(a->psamp_fraction > 0.0f) || !(a->psamp_fraction <= 1.0f))
     return fail(TESSA_ERR_INVALID_ARG, "psamp_fraction outside (0, 1]");
   if (a->resident_rows > 0xffffffffull) return fail(TESSA_ERR_UNSUPPORTED, "resident rows beyond 2^32");
-  if ((uint64_t)a->fanout_second * a->member_rows >= 0xfffffff0ull)
-    return fail(TESSA_ERR_UNSUPPORTED, "fanout_second * member_rows beyond 2^32");
   uint64_t total = 0;
   for (uint32_t t = 0; t < a->task_count; ++t) {
     if (a->task_offsets[t] + a->task_counts[t] > a->member_rows)
       return fail(TESSA_ERR_INVALID_ARG, "subtree task %u rows outside task_members", t);
     total += a->task_counts[t];
   }
-  (void)total;
+  // arena positions are 32-bit: the tasks' rows, each in at most fanout_second leaves
+  if ((uint64_t)a->fanout_second * total >= 0xfffffff0ull)
+    return fail(TESSA_ERR_UNSUPPORTED, "fanout_second * task rows beyond 2^32");
   if (!ctx->subtree) {
     ctx->subtree = subtree_state_new();
     if (!ctx->subtree) return fail(TESSA_ERR_OOM, "subtree state allocation failed");

@@ -148,7 +148,9 @@ int run_job(SubmitRing* R, submit::Slot& S) {
   if (cudaStreamWaitEvent(st, S.inputs_ready, 0) != cudaSuccess)
     return set_last_error(TESSA_ERR_CUDA, "submission: waiting for the caller's stream failed");
   const uint32_t fs = in.fanout_second ? in.fanout_second : 1u;
-  const uint64_t cap = (uint64_t)fs * in.member_rows + 16;
+  uint64_t task_rows = 0;  // the leaf arena holds at most fanout_second rows per task row
+  for (uint32_t t = 0; t < in.task_count; ++t) task_rows += S.task_counts[t];
+  const uint64_t cap = (uint64_t)fs * task_rows + 16;
   if (!S.d_rows.ensure(cap * 4)) return set_last_error(TESSA_ERR_OOM, "submission: leaf arena allocation failed");
   S.leaf_starts.assign(cap, 0);
   S.leaf_sizes.assign(cap, 0);

@@ -690,7 +690,11 @@ int subtree_partition(SubtreeState* S, const tessa_subtree_args& a, SubtreeStats
                       uint64_t timeout_ns, cudaStream_t st) {
   using namespace subtree;
   const uint32_t fs = a.fanout_second < 1u ? 1u : a.fanout_second;
-  const uint64_t arena_cap = (uint64_t)fs * a.member_rows + 16;
+  // every task row lands in at most fanout_second arena rows: the scratch is
+  // sized by the tasks' rows, not by the whole member array they index
+  uint64_t task_rows = 0;
+  for (uint32_t t = 0; t < a.task_count; ++t) task_rows += a.task_counts[t];
+  const uint64_t arena_cap = (uint64_t)fs * task_rows + 16;
   const uint32_t max_leaders = a.max_leaders < kSlots ? a.max_leaders : kSlots;
   ST_ALLOC(S->cur, arena_cap * 4);
   ST_ALLOC(S->next, arena_cap * 4);

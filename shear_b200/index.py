@@ -61,6 +61,13 @@ class BuildParams:
     random_seed: int = 42
     root_leaders: int | None = None        # None: the D0 capacity plan decides
     workspace_bytes: int | None = None     # None: 90% of the device
+    # child rows per record batch (partition + leaves + partial reservoirs of a
+    # group of child runs, merged at the end); None: as many as the workspace
+    # left beside the resident rows holds
+    record_batch_rows: int | None = None
+    # leaf rows per leaf call inside a record batch; None: a third of the
+    # batch's budget for the call's leaf-ordered codes and zone dump
+    leaf_call_rows: int | None = None
     reducer_threads: int = 0
     # "device": HashPrune reservoirs built on the GPU (tessa_reduce_records);
     # "host": records grouped on the GPU, reduced by the host reducer
@@ -204,7 +211,92 @@ def child_runs_stage(d0, k0: int, p: BuildParams) -> dict:
                 entry=entry)
 
 
-def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, sketches=None):
+def record_bytes_per_child_row(p: BuildParams, padded_dim: int) -> int:
+    """Device bytes one child row costs a record batch: up to fanout_second
+    leaf rows, each with its leaf-ordered code row, zone dump (at most 48
+    8-byte entries, 32 floats of merged distances), top-k ids, distances and
+    edge hashes, and the reduction's key/value double buffers and run flags
+    for its 2k edges; plus the partition's arena entries."""
+    k = max(1, min(p.leaf_knn, 32))
+    leaf_row = padded_dim + 48 * 8 + 32 * 4 + 2 + 12 * k + 4 + 2 * k * (32 + 8)
+    return p.fanout_second * leaf_row + 64
+
+
+def record_batch_rows(torch, dev, p: BuildParams, n: int, padded_dim: int, x_bytes: int = 0) -> int:
+    """Child rows per record batch: p.record_batch_rows, else the workspace
+    (p.workspace_bytes, or 80% of the device) less what stays resident through
+    the batches -- codes, scales, norms, sketches and child runs of all n rows,
+    the f32 rows if they are on the device -- and a 2 GiB reserve."""
+    if p.record_batch_rows:
+        return int(p.record_batch_rows)
+    total = torch.cuda.get_device_properties(dev).total_memory
+    cap = p.workspace_bytes if p.workspace_bytes is not None else int(0.8 * total)
+    resident = n * (padded_dim + 8 + 4 * p.m_hash_bits + 12 * p.fanout_top) + x_bytes + (2 << 30)
+    return max(1 << 20, (cap - resident) // record_bytes_per_child_row(p, padded_dim))
+
+
+def leaf_call_rows_for(p: BuildParams, padded_dim: int, batch_child_rows: int) -> int:
+    """Leaf rows per leaf call inside a record batch: a third of the batch's
+    budget for the call's leaf-ordered codes and zone dump."""
+    per_row = padded_dim + 48 * 8 + 32 * 4 + 2
+    return max(1 << 20, batch_child_rows * record_bytes_per_child_row(p, padded_dim) // (3 * per_row))
+
+
+def record_batches(counts, tasks, rows_cap: int) -> list:
+    """`tasks` (indices into counts) in order, cut into consecutive groups of
+    at most rows_cap child rows (a larger run forms a group of its own)."""
+    out, cur, acc = [], [], 0
+    for t in tasks:
+        c = int(counts[t])
+        if cur and acc + c > rows_cap:
+            out.append(cur)
+            cur, acc = [], 0
+        cur.append(int(t))
+        acc += c
+    if cur:
+        out.append(cur)
+    return out
+
+
+def batched_reservoirs(xd, st: dict, p: BuildParams, ctx, batches: list, n: int, timings: dict, sketches,
+                       neighbors: bool = True, slots: bool = False, leaf_call_rows=None):
+    """records_stage + partial HashPrune reservoirs per record batch, merged
+    by tessa_reduce_grouped.  Exact: a per-hash minimum among a source's final
+    l_max best is among the best of every part of its edges, so truncating
+    each batch's part to its l_max best per source loses nothing.  Returns
+    (offsets, neighbors, slots, count) as reduce_stage, and a record summary
+    for the statistics."""
+    pieces, sizes, fallback, parts, k = [], [], 0, [], max(1, min(p.leaf_knn, 32))
+    for key in ("partition_s", "leaf_s", "leaf_kernel_ms", "reduce_s"):
+        timings[key] = 0.0
+    import torch
+
+    for b in batches:
+        tb = {}
+        rec = records_stage(xd, st, p, ctx, tasks=b, timings=tb, sketches=sketches, leaf_call_rows=leaf_call_rows)
+        t = time.perf_counter()
+        o, _, sl, c = reduce_stage(rec, n, p, ctx, neighbors=False, slots=True)
+        sl = sl[:c * 12].clone()  # the slots kept, not the buffer sized for every edge
+        tb["reduce_s"] = time.perf_counter() - t
+        pieces.append((o, sl, c))
+        sizes.append(rec["sizes"])
+        fallback += int(rec["fallback"])
+        parts.append(rec["partition"])
+        k = rec["k"]
+        for key in ("partition_s", "leaf_s", "leaf_kernel_ms", "reduce_s"):
+            timings[key] += tb.get(key, 0.0)
+        del rec
+        torch.cuda.empty_cache()  # the next batch's leaf call allocates outside torch's cache
+    t = time.perf_counter()
+    out = ops.reduce_grouped(pieces, n, p.l_max, ctx=ctx, neighbors=neighbors, slots=slots)
+    timings["reduce_s"] += time.perf_counter() - t
+    part = {f: sum(x[f] for x in parts) for f in parts[0]} if parts else {}
+    summary = dict(sizes=np.concatenate(sizes) if sizes else np.zeros(0, np.uint64), fallback=fallback,
+                   partition=part, k=k, batches=len(batches))
+    return out, summary
+
+
+def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, sketches=None, leaf_call_rows=None):
     """Subtree partition of the child runs `tasks` (all when None), their
     leaves' top-k lists and both sketch hashes of every slot, on the device.
     The sketches of every row are computed from xd unless given."""
@@ -257,8 +349,28 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, s
     dists = torch.full((rows * k,), float("inf"), dtype=torch.float32, device=dev)
     ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     ev[0].record()
-    ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, st["gids"], leaf_rows, starts, sizes, k, out=(ids, dists),
-                      ctx=ctx)
+    fallback = 0
+    if not leaf_call_rows or rows <= leaf_call_rows:
+        ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, st["gids"], leaf_rows, starts, sizes, k, out=(ids, dists),
+                          ctx=ctx)
+        fallback = ops.leaf_last_fallback_rows(ctx)
+    else:
+        # whole leaves per call, at most leaf_call_rows rows each (the call's
+        # leaf-ordered codes and zone dump scale with its rows)
+        order = np.argsort(starts, kind="stable")
+        s_ord = starts[order].astype(np.int64)
+        e_ord = np.maximum.accumulate(s_ord + sizes[order].astype(np.int64))
+        i = 0
+        while i < order.size:
+            base = int(s_ord[i])
+            j = max(i + 1, int(np.searchsorted(e_ord, base + leaf_call_rows, side="right")))
+            r1 = int(e_ord[j - 1])
+            sel = order[i:j]
+            ops.leaf_topk_sq8(d0.codes, d0.scales, d0.norms, st["gids"], leaf_rows[base:r1],
+                              (starts[sel] - np.uint64(base)).astype(np.uint64), sizes[sel], k,
+                              out=(ids[base * k:r1 * k], dists[base * k:r1 * k]), ctx=ctx)
+            fallback += ops.leaf_last_fallback_rows(ctx)
+            i = j
     ev[1].record()
     if side is not None:
         torch.cuda.current_stream(dev).wait_stream(side)
@@ -267,7 +379,7 @@ def records_stage(xd, st: dict, p: BuildParams, ctx, tasks=None, timings=None, s
     timings["leaf_s"] = time.perf_counter() - t
     timings["leaf_kernel_ms"] = ev[0].elapsed_time(ev[1])
     return dict(leaf_rows=leaf_rows, ids=ids, dists=dists, hf=hf, hr=hr, k=k, starts=starts, sizes=sizes,
-                partition=pst, fallback=ops.leaf_last_fallback_rows(ctx))
+                partition=pst, fallback=fallback)
 
 
 def sketch_planes(torch, dev, p: BuildParams, dim: int):
@@ -363,7 +475,28 @@ def build_index(x, p: BuildParams | None = None, device: int = 0, ctx=None) -> B
     sync()
     timings["d0_s"] = time.perf_counter() - t
 
-    # ---- subtree partition of every child run, leaf top-k, edge hashes
+    # ---- subtree partition of every child run, leaf top-k, edge hashes; in
+    #      record batches when they do not fit the workspace at once
+    pd = st["d0"].codes.shape[1]
+    live = np.nonzero(st["counts"] > 0)[0]
+    cap_rows = record_batch_rows(torch, dev, p, n, pd, xd.numel() * 4)
+    batches = record_batches(st["counts"], live, cap_rows)
+    if p.reduction == "device" and len(batches) > 1:
+        sk = ops.sketch_rows(xd, sketch_planes(torch, dev, p, dim), ctx=ctx)
+        (d_off, d_nb, _, count), rec = batched_reservoirs(xd, st, p, ctx, batches, n, timings, sk,
+                                                         leaf_call_rows=p.leaf_call_rows or
+                                                         leaf_call_rows_for(p, pd, cap_rows))
+        del sk
+        t = time.perf_counter()
+        offs, nb = graph_to_host(torch, d_off, d_nb, count)
+        timings["d2h_s"] = time.perf_counter() - t
+        timings["total_s"] = time.perf_counter() - t_all
+        stats = _stats(st, rec, n, dim, None, 0)
+        stats.update(d2h_bytes=int((n + 1) * 8 + count * 4), reduction="device", record_batches=len(batches))
+        # D0 and sketches once; per batch the partition's launches, the leaf
+        # call's four, edge hashes and the reduction's five; the merge's five
+        stats["kernel_launches"] = 5 + rec["partition"]["kernel_launches"] + 10 * len(batches) + 5
+        return BuildResult(offs, nb, st["entry"], timings, stats)
     rec = records_stage(xd, st, p, ctx, timings=timings)
 
     if p.reduction == "host":

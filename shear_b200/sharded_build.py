@@ -205,11 +205,21 @@ def build_index_sharded(x_local, n: int, p: IX.BuildParams | None = None, device
     # ---- this rank's child runs: partition, leaves, hashes, partial reservoirs
     shards = plan_lpt([int(c) for c in st["counts"]], world)
     tasks = sorted(shards[rank])
-    rec = IX.records_stage(None, st, p, ctx, tasks=tasks, timings=timings, sketches=sk[:n])
-    t = time.perf_counter()
-    off, _, slots, cnt = IX.reduce_stage(rec, n, p, ctx, neighbors=False, slots=True)
-    sync()
-    timings["reduce_s"] = time.perf_counter() - t
+    live = [t_ for t_ in tasks if st["counts"][t_] > 0]
+    cap_rows = IX.record_batch_rows(torch, dev, p, n, pd, xs.numel() * 4)
+    batches = IX.record_batches(st["counts"], live, cap_rows)
+    if len(batches) > 1:  # the rank's records do not fit the workspace at once
+        (off, _, slots, cnt), rec = IX.batched_reservoirs(None, st, p, ctx, batches, n, timings, sk[:n],
+                                                         neighbors=False, slots=True,
+                                                         leaf_call_rows=p.leaf_call_rows or
+                                                         IX.leaf_call_rows_for(p, pd, cap_rows))
+        sync()
+    else:
+        rec = IX.records_stage(None, st, p, ctx, tasks=tasks, timings=timings, sketches=sk[:n])
+        t = time.perf_counter()
+        off, _, slots, cnt = IX.reduce_stage(rec, n, p, ctx, neighbors=False, slots=True)
+        sync()
+        timings["reduce_s"] = time.perf_counter() - t
 
     # ---- exchange by owner range, merge, gather the graph on rank 0
     t = time.perf_counter()
@@ -229,7 +239,7 @@ def build_index_sharded(x_local, n: int, p: IX.BuildParams | None = None, device
         timings["d2h_s"] = time.perf_counter() - t
     timings["total_s"] = time.perf_counter() - t_all
     stats = IX._stats(st, rec, n, dim, None, 0)
-    stats.update(tasks=len(tasks), task_rows=int(st["counts"][tasks].sum()) if tasks else 0,
+    stats.update(tasks=len(tasks), task_rows=int(st["counts"][tasks].sum()) if tasks else 0, record_batches=len(batches),
                  partial_slots=int(cnt), owned_slots=int(o_cnt), reduction="device",
                  d2h_bytes=int((n + 1) * 8 + nb.size * 4) if nb is not None else 0,
                  # D0 + partition + leaf + hashes of this rank, the local reduction, the owners' merge

@@ -58,3 +58,20 @@ def test_gpu_build_from_device_tensor_equals_host_input(oracle):
     a = build_index(x, p)
     b = build_index(torch.from_numpy(x).cuda(), p)
     assert np.array_equal(a.offsets, b.offsets) and np.array_equal(a.neighbors, b.neighbors)
+
+
+@pytest.mark.parametrize("batch_rows,call_rows", [(30000, None), (70000, None), (70000, 6000)])
+def test_gpu_build_in_record_batches_equals_one_pass(oracle, batch_rows, call_rows):
+    # The child runs split into record batches (partition, leaves and partial
+    # reservoirs per batch, merged at the end; optionally each batch's leaves
+    # in several leaf calls) give the one-pass graph.
+    from shear_b200.index import BuildParams, build_index
+    x = clustered_rows(20000, 128, 64, seed=7)
+    one = build_index(x, BuildParams(c_max=1024))
+    p = BuildParams(c_max=1024, record_batch_rows=batch_rows, leaf_call_rows=call_rows)
+    r = build_index(x, p)
+    assert r.stats["record_batches"] > 1
+    assert r.stats["leaves"] == one.stats["leaves"] and r.stats["leaf_rows"] == one.stats["leaf_rows"]
+    assert r.entry_point == one.entry_point
+    assert np.array_equal(r.offsets, one.offsets)
+    assert np.array_equal(r.neighbors, one.neighbors)

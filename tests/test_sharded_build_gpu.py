@@ -25,7 +25,7 @@ def _rows(n, dim, seed):
     return clustered_rows(n, dim, 48, seed=seed, unit=dim >= 256)
 
 
-def _worker(rank, world, port, n, dim, c_max, out_dir):
+def _worker(rank, world, port, n, dim, c_max, out_dir, batch_rows=None):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     import datetime
@@ -42,7 +42,10 @@ def _worker(rank, world, port, n, dim, c_max, out_dir):
     try:
         x = _rows(n, dim, seed=n + dim)
         lo, hi, _ = row_range(n, world, rank)
-        r = build_index_sharded(np.ascontiguousarray(x[lo:hi]), n, BuildParams(c_max=c_max), device=rank)
+        p = BuildParams(c_max=c_max, record_batch_rows=batch_rows)
+        r = build_index_sharded(np.ascontiguousarray(x[lo:hi]), n, p, device=rank)
+        if batch_rows:
+            assert r.stats["record_batches"] > 1
         if rank == 0:
             np.save(os.path.join(out_dir, "off.npy"), r.offsets)
             np.save(os.path.join(out_dir, "nb.npy"), r.neighbors)
@@ -54,9 +57,9 @@ def _worker(rank, world, port, n, dim, c_max, out_dir):
         dist.destroy_process_group()
 
 
-def _run(tmp_path, world, n, dim, c_max):
+def _run(tmp_path, world, n, dim, c_max, batch_rows=None):
     from shear_b200.index import BuildParams, build_index
-    mp.start_processes(_worker, args=(world, _free_port(), n, dim, c_max, str(tmp_path)), nprocs=world,
+    mp.start_processes(_worker, args=(world, _free_port(), n, dim, c_max, str(tmp_path), batch_rows), nprocs=world,
                        start_method="spawn", join=True)
     want = build_index(_rows(n, dim, seed=n + dim), BuildParams(c_max=c_max))
     assert np.array_equal(np.load(tmp_path / "off.npy"), want.offsets)
@@ -66,6 +69,12 @@ def _run(tmp_path, world, n, dim, c_max):
 
 def test_sharded_build_one_rank_equals_build_index(tmp_path):
     _run(tmp_path, 1, 20000, 128, 1024)
+
+
+def test_sharded_build_one_rank_in_record_batches_equals_build_index(tmp_path):
+    # the rank's child runs in record batches (partial reservoirs merged
+    # before the owner exchange) give the one-pass graph
+    _run(tmp_path, 1, 20000, 128, 1024, batch_rows=40000)
 
 
 @pytest.mark.parametrize("n,dim,c_max", [(30001, 128, 1024), (12000, 768, 2048)])
