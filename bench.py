@@ -1392,6 +1392,7 @@ def run_build(a):
             dist.all_reduce(d2h)
         e2e = {"value": n / e2e_s, "unit": "vectors/s", "h2d_bytes_per_step": int(n * c["dim"] * 4),
                "d2h_bytes_per_step": int(d2h.item()), "ms_per_step": e2e_s * 1e3,
+               "phases_s": {k_: round(v_, 4) for k_, v_ in r2.timings.items()},
                "timing": ("wall clock around build_index(host numpy rows): upload from pinned memory, GPU "
                           "stages, device HashPrune reservoirs, pinned D2H of the graph" if world == 1 else
                           "wall clock, slowest rank per step, around build_index_sharded(host numpy row range): "
