@@ -1374,8 +1374,11 @@ def run_build(a):
     if not a.no_e2e and a.e2e_steps > 0:
         xh = xs.cpu().pin_memory().numpy()
         build(xh)
-        e2e_t = []
+        e2e_t, r2 = [], None
         for _ in range(a.e2e_steps):
+            # the previous result's graph goes back to the pinned cache first (holding it
+            # would make this build allocate new pinned blocks for its graph)
+            r2 = None
             barrier()
             t0 = time.perf_counter()
             r2 = build(xh)
