@@ -323,6 +323,15 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Asynchronous shared-memory -> tensor-memory copy of a 128-row x 32-byte
+// matrix (row m to lane m, its 32 bytes to 8 consecutive 32-bit columns),
+// the source given by a matrix descriptor as for tcgen05.mma.  Issued by one
+// thread; ordered before later tcgen05.mma of the same thread, tracked by
+// tcgen05.commit like an MMA.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

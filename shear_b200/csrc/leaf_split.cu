@@ -38,18 +38,23 @@
 // leaf_finish_kernel then ranks each row's zone against those k values (as
 // leaf_sq8.cu's finish does), verifies it and writes the k results (or lists
 // the row for the exact fallback), with enough warps per SM to hide latency.
-// The next tile's A is written to TMEM before a tile's rows are wrapped up,
-// so the MMA runs ahead meanwhile.
+// The next tile's A is in TMEM before a tile's rows are wrapped up, so the
+// MMA runs ahead meanwhile: one CTA per tile copies it with tcgen05.cp from
+// the MMA thread as soon as the tile's last MMAs have completed; a CTA pair
+// has its epilogue warps write it (tcgen05.st).
 //
 // Roles (352 threads, one persistent CTA per SM):
 //   warp 0      TMA producer: a ring of 16 KiB stages carrying, per tile, the
 //               A slabs (128 rows x 128 bytes of K) and then the B slabs of
 //               every 128-column chunk;
 //   warp 1      TMEM owner (512 columns: A tile at [0, padded_dim/4), two
-//               128-column accumulators at [256, 512)) and MMA issuer;
+//               128-column accumulators at [256, 512)), MMA issuer and, one
+//               CTA per tile, A copier (tcgen05.cp of each A slab from the
+//               ring into TMEM, four 128 x 32-byte copies per slab);
 //   warps 2..9  epilogue; warp w reads TMEM lane quadrant w % 4, half
-//               (w - 2) / 4; at the start of a tile all eight copy the A slabs
-//               from the ring into TMEM (each a quadrant x 64 bytes of K);
+//               (w - 2) / 4; in a CTA pair all eight copy the A slabs at the
+//               start of a tile from the ring into TMEM (each a quadrant x 64
+//               bytes of K);
 //   warp 10     column metadata ring (scale, norm, global id per column).
 #include "common.cuh"
 #include "kernels.h"
@@ -94,6 +99,7 @@ struct Smem {
   uint64_t* a_rd;       // [kMaxRing] all epilogue warps have read the A slab in this stage
   uint64_t* pair;       // [4] two warps of a lane quadrant
   uint64_t* mma_done;
+  uint64_t* a_free;     // all MMAs of the previous tile have completed (A may be overwritten)
   uint32_t* tmem_slot;
   uint32_t* abort_flag;
 };
@@ -130,7 +136,8 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, uint32_t ring, uint32_t log_
   s.a_rd = s.a_tm_full + 1;
   s.pair = s.a_rd + kMaxRing;
   s.mma_done = s.pair + 4;
-  s.tmem_slot = reinterpret_cast<uint32_t*>(s.mma_done + 1);
+  s.a_free = s.mma_done + 1;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.a_free + 1);
   s.abort_flag = s.tmem_slot + 1;
   return s;
 }
@@ -275,6 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (uint32_t i = 0; i < nst; ++i) mbar_init(&s.a_rd[i], kEpiWarps + (PAIR && rank == 0u ? 1u : 0u));
     for (uint32_t i = 0; i < 4; ++i) mbar_init(&s.pair[i], 2);
     mbar_init(s.mma_done, 1);
+    mbar_init(s.a_free, 1);
     *s.abort_flag = 0u;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -375,14 +383,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t cnt, ncol;
         unit_span<PAIR>(p, tile, rank, t, start, cnt, ncol);
         const uint32_t nchunks = (ncol + kBN - 1) / kBN;
-        // The A items of the ring belong to the epilogue warps.
-        for (uint32_t sl = 0; sl < p.num_slabs; ++sl)
-          if (++stage == nst) {
-            stage = 0;
-            phase ^= 1u;
+        if constexpr (PAIR) {
+          // The A items of the ring belong to the epilogue warps.
+          for (uint32_t sl = 0; sl < p.num_slabs; ++sl)
+            if (++stage == nst) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          if (!wait_peers(s.a_tm_full, a_iter & 1u)) break;
+          tc_fence_after();
+        } else {
+          // One CTA: this thread copies the tile's A slabs from the ring into
+          // tensor memory (tcgen05.cp, ordered before the MMAs that read
+          // them), once every MMA of the previous tile, which read the old A,
+          // has completed.  Each stage is released when its copies complete.
+          if (a_iter > 0u) {
+            if (!mbar_wait(s.a_free, (a_iter - 1u) & 1u, abort_flag, p.err_word, p.timeout_ns)) break;
+            tc_fence_after();
           }
-        if (!wait_peers(s.a_tm_full, a_iter & 1u)) break;
-        tc_fence_after();
+          for (uint32_t sl = 0; sl < p.num_slabs && ok; ++sl) {
+            if (!mbar_wait(&s.b_full[stage], phase, abort_flag, p.err_word, p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = ring_base + stage * kStageBytes;
+#pragma unroll
+            for (uint32_t kk = 0; kk < kSlab / kMmaK; ++kk)
+              tmem_cp_128x256b(tmem_base + sl * (kSlab / 4u) + kk * (kMmaK / 4u),
+                               smem_desc_sw128(a_addr + kk * kMmaK));
+            mma_commit(&s.b_empty[stage]);
+            if (++stage == nst) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+        }
         for (uint32_t c = 0; c < nchunks && ok; ++c, ++acc) {
           const uint32_t buf = acc % kAccBufs, use = acc / kAccBufs;
           if (!wait_peers(&s.t_empty[buf], (use & 1u) ^ 1u)) {
@@ -414,6 +451,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (ok) commit_both(&s.t_full[buf]);
+        }
+        if constexpr (!PAIR) {
+          if (ok) mma_commit(s.a_free);
         }
       }
       // Every issued MMA must have landed before TMEM is released (in both
@@ -499,8 +539,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t start;
       uint32_t cnt, ncol;
       unit_span<PAIR>(p, tile, rank, t, start, cnt, ncol);
-      stop = !load_a_tile<PAIR>(s, p, rpos, ew, half, row_in_tile, lane, lane_base, tmem_base, arp, rank, abort_flag);
-      rpos += p.num_slabs * (1u + (ncol + kBN - 1) / kBN);
+      if constexpr (PAIR) {
+        stop = !load_a_tile<PAIR>(s, p, rpos, ew, half, row_in_tile, lane, lane_base, tmem_base, arp, rank,
+                                  abort_flag);
+        rpos += p.num_slabs * (1u + (ncol + kBN - 1) / kBN);
+      }
     }
     for (; tile < num_units && !stop; tile += ustride, ++tseq) {
       uint2 t;
@@ -785,10 +828,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (stop) break;
 
-      // ---- the next tile's A first: the MMA starts on it while this tile's
-      // rows are wrapped up (all MMAs of this tile have completed).
+      // ---- a pair: the next tile's A first, so the MMA starts on it while
+      // this tile's rows are wrapped up (all MMAs of this tile have
+      // completed).  One CTA per tile: the MMA thread copies it.
       const uint32_t next = tile + ustride;
-      if (next < num_units) {
+      if (PAIR && next < num_units) {
         uint2 tn;
         uint64_t sn;
         uint32_t cn, nn;
