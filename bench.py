@@ -220,6 +220,19 @@ def int8_peak_tops(torch, dev):
 LEAF_STEP_TRAFFIC = {"leaf_topk_split_kernel": 16 * 647565312, "leaf_finish_kernel": 16 * 335143680,
                      "leaf_fallback_kernel": 16 * 289767168}
 
+# DRAM bytes of the build's leaf stage per unit, from one ncu capture (one
+# launch of each kernel, in the fourth build) of the same build family at
+# 200k rows (5,348 leaves, 6.0M leaf rows, 1.19e13 int8 ops; the full
+# config-3 build is too large for a multi-metric capture): the main kernel's
+# 10.65 GB per 1.1913e13 ops (its B re-reads grow with the leaves' all-pairs
+# work) and the finishing kernel's 1.07 GB per 6.0M leaf rows.
+#   python bench.py --workload build --config 3 --rows 200000 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline --no-recall &&
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --clock-control none \
+#       -k regex:"leaf_topk_split|leaf_finish" -s 6 -c 2 \
+#       python bench.py --workload build --config 3 --rows 200000 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline --no-recall
+LEAF_BUILD_BYTES_PER_OP = (9711961344 + 942120704) / 11913301266432
+LEAF_BUILD_FINISH_BYTES_PER_ROW = (981619456 + 86723072) / 6000000
+
 
 def host_oracle():
     """The CPU restatement (test infrastructure) with every host core: torchrun
@@ -1425,11 +1438,17 @@ def run_build(a):
     achieved = res.stats["leaf_ops"] / leaf_s / 1e12
     peak, src = (int8_peak, "measured in-run: cuBLAS int8 burst (torch._int_mm 8192^3)") if int8_peak else \
         (NOMINAL_INT8_TOPS, "nominal B200 dense int8 4.5 POPS (no measured int8 peak)")
+    traffic = int(LEAF_BUILD_BYTES_PER_OP * res.stats["leaf_ops"] +
+                  LEAF_BUILD_FINISH_BYTES_PER_ROW * res.stats["leaf_rows"])
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
-                "traffic": None, "peak_source": src,
-                "kernel": "leaf stage of the build: tessa::leaf::split::leaf_topk_split_kernel<2> + finish "
+                "traffic": traffic, "peak_source": src,
+                "traffic_source": "ncu DRAM bytes of the leaf kernels on the 200k-row build of the same family, "
+                                  "scaled by leaf int8 ops (main kernel) and leaf rows (finishing kernel)",
+                "kernel": "leaf stage of the build:tessa::leaf::split::leaf_topk_split_kernel<2> + finish "
                           "(CUDA events around tessa_leaf_topk_sq8)",
                 "algorithmic_ops_per_launch": res.stats["leaf_ops"], "leaf_kernel_ms": leaf_s * 1e3,
+                "hbm_bytes_algorithmic": int(res.stats["leaf_rows"] * ((res.stats["dim"] + 15) // 16 * 16 + 16) +
+                                             res.stats["leaf_rows"] * res.stats["leaf_k"] * 8),
                 "hbm_peak_gbs": peaks.get("hbm_gbs")}
 
     cpu = None
