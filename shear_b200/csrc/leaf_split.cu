@@ -905,9 +905,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           p.dump_cnt[2u * rd + half] = fits ? (uint8_t)E : (uint8_t)0xFFu;
           if (half == 0) {
-            // the sorted k smallest for the finishing kernel's ranks (32 slots, -inf padded)
+            // the sorted k smallest for the finishing kernel's ranks, -inf
+            // padded to a multiple of four: only the first ceil(k / 4) float4
+            // planes are written (and read)
 #pragma unroll
-            for (int q = 0; q < 32; q += 4)
+            for (int q = 0; q < KS; q += 4)
               p.dump_m[(uint64_t)(q / 4) * p.dump_rows + rd] =
                   make_float4(q < KS ? mk[q] : -INFINITY, q + 1 < KS ? mk[q + 1] : -INFINITY,
                               q + 2 < KS ? mk[q + 2] : -INFINITY, q + 3 < KS ? mk[q + 3] : -INFINITY);
@@ -1001,9 +1003,11 @@ __global__ void __launch_bounds__(kFinThreads) leaf_finish_kernel(const Params p
     if (ok) {
       const uint32_t E = e0 + e1;
       float m[32];
+      const uint32_t planes = (k + 3u) / 4u;  // the main kernel writes only these
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const float4 v = p.dump_m[(uint64_t)q * p.dump_rows + rd];
+        const float4 v = (uint32_t)q < planes ? p.dump_m[(uint64_t)q * p.dump_rows + rd]
+                                              : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         m[4 * q] = v.x;
         m[4 * q + 1] = v.y;
         m[4 * q + 2] = v.z;
@@ -1197,7 +1201,7 @@ uint64_t leaf_dump_m_offset(uint64_t rows, uint32_t k) {
   return ((uint64_t)leaf_dump_entries(k) * 8u * rows + 15u) & ~uint64_t(15u);
 }
 
-// Per row: the zone entries (8 bytes each), the merged k smallest (32 floats)
+// Per row: the zone entries (8 bytes each), the merged k smallest (room for 32 floats; the first ceil(k / 4) float4 planes are used)
 // and two entry counts.
 uint64_t leaf_dump_bytes(uint64_t rows, uint32_t k) {
   return leaf_dump_m_offset(rows, k) + rows * (128u + 2u);
