@@ -224,14 +224,15 @@ LEAF_STEP_TRAFFIC = {"leaf_topk_split_kernel": 16 * 647565312, "leaf_finish_kern
 # launch of each kernel, in the fourth build) of the same build family at
 # 200k rows (5,348 leaves, 6.0M leaf rows, 1.19e13 int8 ops; the full
 # config-3 build is too large for a multi-metric capture): the main kernel's
-# 10.65 GB per 1.1913e13 ops (its B re-reads grow with the leaves' all-pairs
-# work) and the finishing kernel's 1.07 GB per 6.0M leaf rows.
+# 9.47 GB per 1.1913e13 ops (its B re-reads grow with the leaves' all-pairs
+# work) and the finishing kernel's 0.38 GB per 6.0M leaf rows (kernels with
+# the A tile copied by tcgen05.cp and ceil(k/4) planes of merged distances).
 #   python bench.py --workload build --config 3 --rows 200000 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline --no-recall &&
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --clock-control none \
 #       -k regex:"leaf_topk_split|leaf_finish" -s 6 -c 2 \
 #       python bench.py --workload build --config 3 --rows 200000 --steps 1 --warmup 3 --no-e2e --no-cpu-baseline --no-recall
-LEAF_BUILD_BYTES_PER_OP = (9711961344 + 942120704) / 11913301266432
-LEAF_BUILD_FINISH_BYTES_PER_ROW = (981619456 + 86723072) / 6000000
+LEAF_BUILD_BYTES_PER_OP = (9198426112 + 274606336) / 11913301266432
+LEAF_BUILD_FINISH_BYTES_PER_ROW = (307059200 + 72790528) / 6000000
 
 
 def host_oracle():
