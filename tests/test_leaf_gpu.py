@@ -55,6 +55,20 @@ def test_leaf_matches_oracle(oracle, sizes, dim, k, dup, permute):
     _assert_same(_device_run(c, k), oracle_leaf(oracle, c, k))
 
 
+@pytest.mark.parametrize("dim,k", [(256, 2), (768, 2), (768, 32), (1024, 2), (512, 9)])
+def test_leaf_many_tiles_per_cta_match_oracle(oracle, dim, k):
+    # More than three times as many 128-row tiles as SMs, of ragged leaves: every
+    # persistent CTA runs several tiles back to back, so each tile's A tile is
+    # copied into tensor memory over the previous tile's once that tile's MMAs
+    # have completed (ring deeper than the A slabs at k = 2, shallower at k = 32).
+    rng = np.random.default_rng(dim * 7 + k)
+    sizes = [int(s) for s in rng.integers(100, 400, size=300)]
+    rows_per_leaf = np.array(sizes)
+    assert int(((rows_per_leaf + 127) // 128).sum()) > 3 * 148
+    c = make_leaf_batch(oracle, sizes, dim, seed=dim + k, dup=True, permute=True)
+    _assert_same(_device_run(c, k), oracle_leaf(oracle, c, k))
+
+
 def test_leaf_ordered_codes_path_matches_gather_path(oracle):
     c = make_leaf_batch(oracle, [300, 200], 256, seed=11, permute=True)
     a = _device_run(c, 8)
