@@ -1018,8 +1018,8 @@ __global__ void __launch_bounds__(kFinThreads) leaf_finish_kernel(const Params p
       const float thr = __fadd_rn(theta, kMargin);
       uint32_t n_inner = 0;
       // Entry e < e0 sits at dump slot e, entry e0 + e at slot D - 1 - e
-      // (half 1 fills the slots from the back); four loads in flight at a time.
-#pragma unroll 4
+      // (half 1 fills the slots from the back); eight loads in flight at a time.
+#pragma unroll 8
       for (uint32_t e = 0; e < E; ++e) {
         const uint32_t slot = e < e0 ? e : D - 1u - (e - e0);
         const uint2 v = p.dump[(uint64_t)slot * p.dump_rows + rd];
